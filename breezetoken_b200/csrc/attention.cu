@@ -1,0 +1,349 @@
+// Split-KV GQA flash-decode with an in-kernel combine.
+//
+// Replaces the reference's tilelang split + combine kernels
+// (breezetoken/kernels/cuda/attention.py:55-366) and matches its torch
+// oracle `_torch_attention` (breezetoken/backends.py:196-215):
+//   out[h] = softmax(q[h] . K[:, h / (heads/kv_heads)] * scale) V
+//
+// Grid (splits, kv_heads, batch); 4 warps per CTA.  A CTA owns one KV head
+// (group) of one sequence and a contiguous slice of positions, and serves all
+// GS = heads/kv_heads query heads of the group, so every K/V byte is read
+// once.  Lane l holds dims [l*DPL, l*DPL + DPL) of the GS queries.  A warp
+// takes PB = 32/GS positions at a time: each lane forms GS*PB partial dot
+// products, a 31-shuffle reduce-scatter leaves score (head l/PB, position
+// l%PB) in lane l, the online softmax runs in base 2 with per-head running
+// max/sum, and P.V accumulates with the probabilities broadcast by shuffle.
+// Warps merge in shared memory; with several splits the last CTA of a group
+// (atomic ticket in the workspace) merges the splits' (max, sum, o) records
+// and re-arms the counter, so no second kernel is needed.
+//
+// Model mode fuses the surrounding ops of the Qwen3.5 attention layer
+// (model/layers.py:55-82 / graph.py:35-64): per-head q/k RMSNorm, partial
+// rotate-half RoPE at the device position, the KV-cache write at that
+// position and the sigmoid output gate.
+#include "attention.cuh"
+#include "errors.h"
+
+namespace bt {
+
+namespace {
+
+constexpr int kAttnWarps = 4;
+constexpr int kAttnThreads = kAttnWarps * 32;
+constexpr float kLog2e = 1.4426950408889634f;
+
+// Sum 32 per-lane values across the warp; lane l returns the total of value l.
+__device__ __forceinline__ float reduce_scatter32(float (&v)[32], int lane) {
+#pragma unroll
+  for (int stage = 16; stage >= 1; stage >>= 1) {
+    const bool upper = (lane & stage) != 0;
+#pragma unroll
+    for (int i = 0; i < stage; ++i) {
+      const float send = upper ? v[i] : v[i + stage];
+      const float keep = upper ? v[i + stage] : v[i];
+      v[i] = keep + __shfl_xor_sync(0xffffffffu, send, stage);
+    }
+  }
+  return v[0];
+}
+
+template <typename KV, int DPL>
+struct KvRow;
+
+template <int DPL>
+struct KvRow<float, DPL> {
+  __device__ static __forceinline__ void load(const void* base, int64_t off, float (&o)[DPL]) {
+    const float4* p = reinterpret_cast<const float4*>(static_cast<const float*>(base) + off);
+#pragma unroll
+    for (int i = 0; i < DPL / 4; ++i) {
+      const float4 t = p[i];
+      o[4 * i] = t.x;
+      o[4 * i + 1] = t.y;
+      o[4 * i + 2] = t.z;
+      o[4 * i + 3] = t.w;
+    }
+  }
+};
+
+template <>
+struct KvRow<__nv_bfloat16, 8> {
+  __device__ static __forceinline__ void load(const void* base, int64_t off, float (&o)[8]) {
+    const uint4 t = *reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(base) + off);
+    o[0] = bf16_lo(t.x); o[1] = bf16_hi(t.x);
+    o[2] = bf16_lo(t.y); o[3] = bf16_hi(t.y);
+    o[4] = bf16_lo(t.z); o[5] = bf16_hi(t.z);
+    o[6] = bf16_lo(t.w); o[7] = bf16_hi(t.w);
+  }
+};
+
+template <>
+struct KvRow<__nv_bfloat16, 4> {
+  __device__ static __forceinline__ void load(const void* base, int64_t off, float (&o)[4]) {
+    const uint2 t = *reinterpret_cast<const uint2*>(static_cast<const __nv_bfloat16*>(base) + off);
+    o[0] = bf16_lo(t.x); o[1] = bf16_hi(t.x);
+    o[2] = bf16_lo(t.y); o[3] = bf16_hi(t.y);
+  }
+};
+
+template <typename KV, int DPL, int GS>
+__global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const __grid_constant__ AttnParams p) {
+  constexpr int DIM = DPL * 32;
+  constexpr int PB = 32 / GS;
+  __shared__ __align__(16) float qs[GS][DIM];
+  __shared__ __align__(16) float kvn[2][DIM];
+  __shared__ float wm[kAttnWarps][GS], wl[kAttnWarps][GS];
+  __shared__ __align__(16) float wacc[kAttnWarps][GS][DIM];
+  __shared__ uint32_t s_ticket;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int split = blockIdx.x, g = blockIdx.y, b = blockIdx.z;
+  pdl_launch_dependents();
+  pdl_wait();
+
+  int L = p.model ? p.pos[b] + 1 : p.lens[b];
+  if (L < 0 || L > p.cap) {
+    if (threadIdx.x == 0) report_status(p.status, BT_ERR_INVALID);
+    L = L < 0 ? 0 : p.cap;
+  }
+  const int chunk = (L + p.splits - 1) / p.splits;
+  const int t0 = min(L, split * chunk), t1 = min(L, t0 + chunk);
+
+  if (!p.model) {
+    for (int i = threadIdx.x; i < GS * DIM; i += kAttnThreads)
+      qs[i / DIM][i % DIM] =
+          p.q[static_cast<int64_t>(b) * p.q_bs + static_cast<int64_t>(g * GS + i / DIM) * p.q_hs + i % DIM];
+    __syncthreads();
+  } else {
+    const int pos = L - 1;
+    for (int item = warp; item < GS + 2; item += kAttnWarps) {
+      float* dst = item < GS ? qs[item] : kvn[item - GS];
+      const float* src = item < GS ? p.q + static_cast<int64_t>(b) * p.q_bs + static_cast<int64_t>(g * GS + item) * p.q_hs
+                                   : (item == GS ? p.k_new : p.v_new) + static_cast<int64_t>(b) * p.q_bs + g * DIM;
+      float x[DPL];
+#pragma unroll
+      for (int i = 0; i < DPL; ++i) x[i] = src[lane * DPL + i];
+      if (item <= GS) {
+        const float* nw = item < GS ? p.q_norm : p.k_norm;
+        float ss = 0.f;
+#pragma unroll
+        for (int i = 0; i < DPL; ++i) ss = fmaf(x[i], x[i], ss);
+        ss = warp_sum(ss);
+        const float r = 1.0f / sqrtf(ss / static_cast<float>(DIM) + p.eps);
+#pragma unroll
+        for (int i = 0; i < DPL; ++i) {
+          x[i] = __fmul_rn(__fmul_rn(x[i], r), nw[lane * DPL + i]);
+          dst[lane * DPL + i] = x[i];
+        }
+        __syncwarp();
+        const int half = p.rope_dim >> 1;
+#pragma unroll
+        for (int i = 0; i < DPL; ++i) {
+          const int d = lane * DPL + i;
+          if (d < p.rope_dim) {
+            const float c = p.rope_cos[static_cast<int64_t>(pos) * p.rope_dim + d];
+            const float s = p.rope_sin[static_cast<int64_t>(pos) * p.rope_dim + d];
+            const float partner = d < half ? -dst[d + half] : dst[d - half];
+            x[i] = __fadd_rn(__fmul_rn(x[i], c), __fmul_rn(partner, s));
+          }
+        }
+        __syncwarp();
+      }
+#pragma unroll
+      for (int i = 0; i < DPL; ++i) dst[lane * DPL + i] = x[i];
+    }
+    __syncthreads();
+    if (pos >= t0 && pos < t1) {
+      float* kc = const_cast<float*>(static_cast<const float*>(p.k)) + static_cast<int64_t>(b) * p.kv_bs +
+                  static_cast<int64_t>(pos) * p.kv_ts + g * DIM;
+      float* vc = const_cast<float*>(static_cast<const float*>(p.v)) + static_cast<int64_t>(b) * p.kv_bs +
+                  static_cast<int64_t>(pos) * p.kv_ts + g * DIM;
+      for (int i = threadIdx.x; i < DIM; i += kAttnThreads) {
+        kc[i] = kvn[0][i];
+        vc[i] = kvn[1][i];
+      }
+      __threadfence_block();
+    }
+    __syncthreads();
+  }
+
+  float qr[GS][DPL], acc[GS][DPL];
+#pragma unroll
+  for (int h = 0; h < GS; ++h)
+#pragma unroll
+    for (int i = 0; i < DPL; ++i) {
+      qr[h][i] = qs[h][lane * DPL + i];
+      acc[h][i] = 0.f;
+    }
+  float m_run = -INFINITY, l_run = 0.f;
+  const float sl = p.scale * kLog2e;
+  const int64_t kvbase = static_cast<int64_t>(b) * p.kv_bs + g * DIM + lane * DPL;
+
+  for (int tb = t0 + warp * PB; tb < t1; tb += kAttnWarps * PB) {
+    float part[32];
+#pragma unroll
+    for (int pp = 0; pp < PB; ++pp) {
+      const int t = tb + pp;
+      float kf[DPL];
+      if (t < t1) {
+        KvRow<KV, DPL>::load(p.k, kvbase + static_cast<int64_t>(t) * p.kv_ts, kf);
+      } else {
+#pragma unroll
+        for (int i = 0; i < DPL; ++i) kf[i] = 0.f;
+      }
+#pragma unroll
+      for (int h = 0; h < GS; ++h) {
+        float s = 0.f;
+#pragma unroll
+        for (int i = 0; i < DPL; ++i) s = fmaf(qr[h][i], kf[i], s);
+        part[h * PB + pp] = s;
+      }
+    }
+    float score = reduce_scatter32(part, lane) * sl;
+    const bool valid = tb + (lane % PB) < t1;
+    if (!valid) score = -INFINITY;
+    float mx = score;
+#pragma unroll
+    for (int o = PB / 2; o >= 1; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    const float m_new = fmaxf(m_run, mx);
+    const float alpha = m_run == -INFINITY ? 0.f : exp2f(m_run - m_new);
+    const float pe = valid ? exp2f(score - m_new) : 0.f;
+    float ps = pe;
+#pragma unroll
+    for (int o = PB / 2; o >= 1; o >>= 1) ps += __shfl_xor_sync(0xffffffffu, ps, o);
+    l_run = l_run * alpha + ps;
+    m_run = m_new;
+#pragma unroll
+    for (int h = 0; h < GS; ++h) {
+      const float a = __shfl_sync(0xffffffffu, alpha, h * PB);
+#pragma unroll
+      for (int i = 0; i < DPL; ++i) acc[h][i] *= a;
+    }
+#pragma unroll
+    for (int pp = 0; pp < PB; ++pp) {
+      const int t = tb + pp;
+      if (t < t1) {
+        float vf[DPL];
+        KvRow<KV, DPL>::load(p.v, kvbase + static_cast<int64_t>(t) * p.kv_ts, vf);
+#pragma unroll
+        for (int h = 0; h < GS; ++h) {
+          const float w = __shfl_sync(0xffffffffu, pe, h * PB + pp);
+#pragma unroll
+          for (int i = 0; i < DPL; ++i) acc[h][i] = fmaf(w, vf[i], acc[h][i]);
+        }
+      }
+    }
+  }
+
+  // ---------------- merge the warps
+  if (lane % PB == 0) {
+    wm[warp][lane / PB] = m_run;
+    wl[warp][lane / PB] = l_run;
+  }
+#pragma unroll
+  for (int h = 0; h < GS; ++h)
+#pragma unroll
+    for (int i = 0; i < DPL; ++i) wacc[warp][h][lane * DPL + i] = acc[h][i];
+  __syncthreads();
+
+  const int64_t rec0 = ((static_cast<int64_t>(b) * p.kv_heads + g) * p.splits) * GS;
+  for (int e = threadIdx.x; e < GS * DIM; e += kAttnThreads) {
+    const int h = e / DIM, d = e % DIM;
+    float M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < kAttnWarps; ++w) M = fmaxf(M, wm[w][h]);
+    float Ls = 0.f, O = 0.f;
+#pragma unroll
+    for (int w = 0; w < kAttnWarps; ++w) {
+      if (wm[w][h] != -INFINITY) {
+        const float f = exp2f(wm[w][h] - M);
+        Ls = fmaf(wl[w][h], f, Ls);
+        O = fmaf(wacc[w][h][d], f, O);
+      }
+    }
+    if (p.splits == 1) {
+      float o = Ls > 0.f ? O / Ls : 0.f;
+      if (p.model)
+        o *= sigmoid_f(p.gate[static_cast<int64_t>(b) * p.q_bs + static_cast<int64_t>(g * GS + h) * p.q_hs + d]);
+      p.out[static_cast<int64_t>(b) * p.out_bs + static_cast<int64_t>(g * GS + h) * DIM + d] = o;
+    } else {
+      float* rec = p.part + (rec0 + static_cast<int64_t>(split) * GS + h) * (DIM + 2);
+      rec[d] = O;
+      if (d == 0) {
+        rec[DIM] = M;
+        rec[DIM + 1] = Ls;
+      }
+    }
+  }
+  if (p.splits == 1) return;
+
+  // ---------------- last CTA of the group merges the splits
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) s_ticket = atomicAdd(p.counters + static_cast<int64_t>(b) * p.kv_heads + g, 1u);
+  __syncthreads();
+  if (s_ticket != static_cast<uint32_t>(p.splits - 1)) return;
+  __threadfence();
+  for (int e = threadIdx.x; e < GS * DIM; e += kAttnThreads) {
+    const int h = e / DIM, d = e % DIM;
+    float M = -INFINITY;
+    for (int s = 0; s < p.splits; ++s)
+      M = fmaxf(M, __ldcg(p.part + (rec0 + static_cast<int64_t>(s) * GS + h) * (DIM + 2) + DIM));
+    float Ls = 0.f, O = 0.f;
+    for (int s = 0; s < p.splits; ++s) {
+      const float* rec = p.part + (rec0 + static_cast<int64_t>(s) * GS + h) * (DIM + 2);
+      const float ms = __ldcg(rec + DIM);
+      if (ms != -INFINITY) {
+        const float f = exp2f(ms - M);
+        Ls = fmaf(__ldcg(rec + DIM + 1), f, Ls);
+        O = fmaf(__ldcg(rec + d), f, O);
+      }
+    }
+    float o = Ls > 0.f ? O / Ls : 0.f;
+    if (p.model)
+      o *= sigmoid_f(p.gate[static_cast<int64_t>(b) * p.q_bs + static_cast<int64_t>(g * GS + h) * p.q_hs + d]);
+    p.out[static_cast<int64_t>(b) * p.out_bs + static_cast<int64_t>(g * GS + h) * DIM + d] = o;
+  }
+  if (threadIdx.x == 0) atomicExch(p.counters + static_cast<int64_t>(b) * p.kv_heads + g, 0u);
+}
+
+template <typename KV, int DPL, int GS>
+int launch_t(const AttnParams& p, cudaStream_t stream, bool pdl) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(p.splits, p.kv_heads, p.batch);
+  cfg.blockDim = dim3(kAttnThreads);
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, attn_decode_kernel<KV, DPL, GS>, p);
+  if (e != cudaSuccess) return fail_cuda(e, "attention launch");
+  return BT_OK;
+}
+
+template <typename KV>
+int launch_dtype(const AttnParams& p, cudaStream_t stream, bool pdl) {
+  const int gs = p.heads / p.kv_heads;
+  if (p.dim == 256 && gs == 4) return launch_t<KV, 8, 4>(p, stream, pdl);
+  if (p.dim == 256 && gs == 8) return launch_t<KV, 8, 8>(p, stream, pdl);
+  if (p.dim == 128 && gs == 4) return launch_t<KV, 4, 4>(p, stream, pdl);
+  if (p.dim == 128 && gs == 8) return launch_t<KV, 4, 8>(p, stream, pdl);
+  return fail(BT_ERR_UNSUPPORTED, "attention serves head_dim {128, 256} with 4 or 8 query heads per KV head (got dim %d, %d)",
+              p.dim, gs);
+}
+
+}  // namespace
+
+int attention_launch(const AttnParams& p, cudaStream_t stream, bool pdl) {
+  if (p.batch <= 0 || p.kv_heads <= 0 || p.heads <= 0 || p.heads % p.kv_heads != 0)
+    return fail(BT_ERR_INVALID, "attention: heads (%d) must be a positive multiple of kv_heads (%d)", p.heads,
+                p.kv_heads);
+  if (p.splits < 1 || p.splits > 1024) return fail(BT_ERR_INVALID, "attention: splits must be in [1, 1024]");
+  if (p.model && p.kv_dtype != BT_F32) return fail(BT_ERR_UNSUPPORTED, "model-mode attention keeps an f32 cache");
+  if (p.model && (p.rope_dim < 0 || p.rope_dim > p.dim || p.rope_dim % 2))
+    return fail(BT_ERR_INVALID, "attention: invalid rope_dim %d", p.rope_dim);
+  return p.kv_dtype == BT_BF16 ? launch_dtype<__nv_bfloat16>(p, stream, pdl) : launch_dtype<float>(p, stream, pdl);
+}
+
+}  // namespace bt

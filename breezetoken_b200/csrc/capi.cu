@@ -1,0 +1,250 @@
+// extern "C" entry points declared in include/bt_b200.h.
+#include <cstdarg>
+#include <cstdio>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "attention.cuh"
+#include "errors.h"
+#include "gdn.cuh"
+#include "gemv_q8.cuh"
+#include "ops.cuh"
+
+namespace bt {
+
+int64_t qwen35_proj_elems(const BtQwen35Dims& d);
+int64_t qwen35_workspace_bytes(const BtQwen35Dims& d);
+int qwen35_step(const BtQwen35Model& m, const BtQwen35Runtime& rt, int with_logits, cudaStream_t s);
+
+namespace {
+thread_local char g_last_error[512] = "";
+std::mutex g_sm_mutex;
+std::vector<int> g_sm_counts;
+}  // namespace
+
+int fail(int code, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_last_error, sizeof(g_last_error), fmt, ap);
+  va_end(ap);
+  return code;
+}
+
+int fail_cuda(cudaError_t err, const char* what) {
+  snprintf(g_last_error, sizeof(g_last_error), "%s: %s (%s)", what, cudaGetErrorString(err),
+           cudaGetErrorName(err));
+  return BT_ERR_CUDA;
+}
+
+int sm_count() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 148;
+  std::lock_guard<std::mutex> lock(g_sm_mutex);
+  if (dev >= static_cast<int>(g_sm_counts.size())) g_sm_counts.resize(dev + 1, 0);
+  if (!g_sm_counts[dev]) {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+    g_sm_counts[dev] = n;
+  }
+  return g_sm_counts[dev];
+}
+
+}  // namespace bt
+
+using bt::fail;
+
+namespace {
+inline cudaStream_t as_stream(void* s) { return static_cast<cudaStream_t>(s); }
+}  // namespace
+
+extern "C" {
+
+const char* bt_last_error(void) { return bt::g_last_error; }
+
+int bt_version(void) { return 100; }
+
+int bt_sm_count(void) { return bt::sm_count(); }
+
+int64_t bt_q8_row_bytes(int64_t k) {
+  const int64_t scale_bytes = (k / 32) * 2;
+  return (scale_bytes + 15) / 16 * 16 + k;
+}
+
+int bt_repack_q8_0(const void* src, void* dst, int64_t rows, int64_t k, int64_t dst_row0, int64_t dst_row_step,
+                   void* stream) {
+  return bt::repack_q8_0(src, dst, rows, k, dst_row0, dst_row_step, as_stream(stream));
+}
+
+int bt_dequant_q8_rows(const void* w, float* out, int64_t rows, int64_t k, void* stream) {
+  return bt::dequant_q8_rows(w, out, rows, k, as_stream(stream));
+}
+
+int bt_dequant_iq3_s(const void* raw, float* out, int64_t rows, int64_t cols, void* stream) {
+  return bt::dequant_iq3_s(raw, out, rows, cols, as_stream(stream));
+}
+
+int bt_linear_q8(const void* w, const float* x, float* y, int64_t n, int64_t k, int n_vec, void* stream) {
+  if (!w || !x || !y) return fail(BT_ERR_INVALID, "linear_q8: null pointer");
+  if (k > (1 << 20)) return fail(BT_ERR_UNSUPPORTED, "linear_q8: K too large");
+  if (n_vec != 1 && n_vec != 2 && n_vec != 4 && n_vec != 8)
+    return fail(BT_ERR_UNSUPPORTED, "linear_q8: n_vec must be 1, 2, 4 or 8 (got %d)", n_vec);
+  bt::GemvQ8Params p{};
+  p.w = static_cast<const uint8_t*>(w);
+  p.n_rows = n;
+  p.k = static_cast<int32_t>(k);
+  p.n_vec = n_vec;
+  p.prologue = bt::PRO_LOAD;
+  p.x = x;
+  p.epilogue = bt::EPI_STORE;
+  p.y = y;
+  p.y_stride = n;
+  bt::GemvQ8Launch L{};
+  int rc = bt::gemv_q8_plan(p, bt::sm_count(), L);
+  if (rc) return rc;
+  return bt::gemv_q8_launch(p, L, as_stream(stream), false);
+}
+
+int bt_linear_kn(const void* w, int w_dtype, const float* x, float* y, int64_t k, int64_t n, void* stream) {
+  return bt::linear_kn(w, w_dtype, x, y, k, n, as_stream(stream));
+}
+
+int bt_rms_norm(const float* x, const float* w, float* y, int64_t rows, int64_t n, float eps, void* stream) {
+  return bt::rms_norm(x, nullptr, w, nullptr, y, rows, n, eps, as_stream(stream));
+}
+
+int bt_fused_add_rms_norm(const float* a, const float* b, const float* w, float* h, float* xn, int64_t rows,
+                          int64_t n, float eps, void* stream) {
+  if (!b || !h) return fail(BT_ERR_INVALID, "fused_add_rms_norm: null pointer");
+  return bt::rms_norm(a, b, w, h, xn, rows, n, eps, as_stream(stream));
+}
+
+int bt_silu_mul(const float* g, const float* u, float* y, int64_t n, void* stream) {
+  return bt::silu_mul(g, u, y, n, as_stream(stream));
+}
+
+int bt_rope(const float* x, const float* cos_t, const float* sin_t, const int32_t* pos, float* y, int64_t rows,
+            int64_t dim, int64_t rope_dim, int64_t cap, void* stream) {
+  return bt::rope(x, cos_t, sin_t, pos, y, rows, dim, rope_dim, cap, as_stream(stream));
+}
+
+int64_t bt_attention_workspace_bytes(int64_t batch, int64_t kv_heads, int64_t heads, int64_t dim, int splits) {
+  if (batch < 1 || kv_heads < 1 || heads < 1 || dim < 1 || splits < 1) return 0;
+  const int64_t part = (4 * bt::attn_part_floats(batch, kv_heads, heads, dim, splits) + 255) / 256 * 256;
+  return part + (4 * batch * kv_heads + 255) / 256 * 256;
+}
+
+int bt_attention_decode(const float* q, const void* k, const void* v, int kv_dtype, const int32_t* lens, float* out,
+                        int64_t batch, int64_t heads, int64_t kv_heads, int64_t dim, int64_t cap, float scale,
+                        int splits, void* workspace, void* stream) {
+  if (!q || !k || !v || !lens || !out) return fail(BT_ERR_INVALID, "attention: null pointer");
+  if (splits > 1 && !workspace) return fail(BT_ERR_INVALID, "attention: splits > 1 needs a workspace");
+  if (batch > 65535 || cap < 1 || cap > (1LL << 30) || kv_heads > 65535)
+    return fail(BT_ERR_UNSUPPORTED, "attention: shape out of range");
+  bt::AttnParams p{};
+  p.q = q;
+  p.q_bs = heads * dim;
+  p.q_hs = static_cast<int32_t>(dim);
+  p.k = k;
+  p.v = v;
+  p.kv_dtype = kv_dtype;
+  p.kv_ts = static_cast<int32_t>(kv_heads * dim);
+  p.kv_bs = cap * kv_heads * dim;
+  p.lens = lens;
+  p.out = out;
+  p.out_bs = heads * dim;
+  p.batch = static_cast<int32_t>(batch);
+  p.heads = static_cast<int32_t>(heads);
+  p.kv_heads = static_cast<int32_t>(kv_heads);
+  p.dim = static_cast<int32_t>(dim);
+  p.cap = static_cast<int32_t>(cap);
+  p.splits = splits;
+  p.scale = scale;
+  if (splits > 1) {
+    p.part = static_cast<float*>(workspace);
+    const int64_t part_bytes = (4 * bt::attn_part_floats(batch, kv_heads, heads, dim, splits) + 255) / 256 * 256;
+    p.counters = reinterpret_cast<uint32_t*>(static_cast<uint8_t*>(workspace) + part_bytes);
+  }
+  return bt::attention_launch(p, as_stream(stream), false);
+}
+
+int bt_gdn_decode(const void* q, const void* k, const void* v, int in_dtype, const float* g, const float* beta,
+                  float* state, float* out, int64_t batch, int64_t heads_k, int64_t heads_v, int64_t dim, float scale,
+                  float eps, void* stream) {
+  if (!q || !k || !v || !g || !beta || !state || !out) return fail(BT_ERR_INVALID, "gdn_decode: null pointer");
+  if (in_dtype != BT_F32 && in_dtype != BT_BF16) return fail(BT_ERR_UNSUPPORTED, "gdn_decode: dtype %d", in_dtype);
+  if (batch * heads_v * (dim / 32) > 0x7fffffffLL) return fail(BT_ERR_UNSUPPORTED, "gdn_decode: grid too large");
+  bt::GdnParams p{};
+  p.q = q;
+  p.k = k;
+  p.v = v;
+  p.in_dtype = in_dtype;
+  p.q_bs = p.k_bs = heads_k * dim;
+  p.v_bs = heads_v * dim;
+  p.g = g;
+  p.beta = beta;
+  p.g_bs = p.beta_bs = heads_v;
+  p.state = state;
+  p.out = out;
+  p.out_bs = heads_v * dim;
+  p.batch = static_cast<int32_t>(batch);
+  p.heads_k = static_cast<int32_t>(heads_k);
+  p.heads_v = static_cast<int32_t>(heads_v);
+  p.dim = static_cast<int32_t>(dim);
+  p.scale = scale;
+  p.eps = eps;
+  return bt::gdn_decode_launch(p, as_stream(stream), false);
+}
+
+int64_t bt_argmax_workspace_bytes(int64_t rows) { return rows < 1 ? 0 : 12 * rows; }
+
+int bt_argmax(const float* x, int64_t rows, int64_t n, int32_t* out, void* workspace, void* stream) {
+  return bt::argmax(x, rows, n, out, workspace, as_stream(stream));
+}
+
+int64_t bt_qwen35_proj_elems(const BtQwen35Dims* dims) { return dims ? bt::qwen35_proj_elems(*dims) : 0; }
+
+int64_t bt_qwen35_workspace_bytes(const BtQwen35Dims* dims) { return dims ? bt::qwen35_workspace_bytes(*dims) : 0; }
+
+int bt_qwen35_step(const BtQwen35Model* model, const BtQwen35Runtime* rt, int with_logits, void* stream) {
+  if (!model || !rt) return fail(BT_ERR_INVALID, "qwen35_step: null model or runtime");
+  return bt::qwen35_step(*model, *rt, with_logits, as_stream(stream));
+}
+
+int bt_qwen35_graph_create(const BtQwen35Model* model, const BtQwen35Runtime* rt, int n_steps, void* stream,
+                           void** graph_out) {
+  if (!model || !rt || !graph_out || n_steps < 1) return fail(BT_ERR_INVALID, "graph_create: bad arguments");
+  if (!stream) return fail(BT_ERR_INVALID, "graph_create: capture needs a non-default stream");
+  cudaStream_t s = as_stream(stream);
+  cudaError_t e = cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal);
+  if (e != cudaSuccess) return bt::fail_cuda(e, "begin capture");
+  int rc = BT_OK;
+  for (int i = 0; i < n_steps && rc == BT_OK; ++i) rc = bt::qwen35_step(*model, *rt, 1, s);
+  cudaGraph_t graph = nullptr;
+  e = cudaStreamEndCapture(s, &graph);
+  if (rc != BT_OK) {
+    if (graph) cudaGraphDestroy(graph);
+    return rc;
+  }
+  if (e != cudaSuccess) return bt::fail_cuda(e, "end capture");
+  cudaGraphExec_t exec = nullptr;
+  e = cudaGraphInstantiate(&exec, graph, 0);
+  cudaGraphDestroy(graph);
+  if (e != cudaSuccess) return bt::fail_cuda(e, "graph instantiate");
+  *graph_out = exec;
+  return BT_OK;
+}
+
+int bt_graph_launch(void* graph, void* stream) {
+  if (!graph) return fail(BT_ERR_INVALID, "graph_launch: null graph");
+  cudaError_t e = cudaGraphLaunch(static_cast<cudaGraphExec_t>(graph), as_stream(stream));
+  return e == cudaSuccess ? BT_OK : bt::fail_cuda(e, "graph launch");
+}
+
+int bt_graph_destroy(void* graph) {
+  if (!graph) return BT_OK;
+  cudaError_t e = cudaGraphExecDestroy(static_cast<cudaGraphExec_t>(graph));
+  return e == cudaSuccess ? BT_OK : bt::fail_cuda(e, "graph destroy");
+}
+
+}  // extern "C"

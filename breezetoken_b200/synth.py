@@ -1,0 +1,234 @@
+"""Seeded synthetic checkpoints in GGUF form.
+
+No real checkpoint is available to this project, so the benchmarks and parity
+tests run on random-initialised models written as GGUF files that both this
+backend and the reference's loader (breezetoken/gguf.py, model/qwen35.py:166-219)
+read.  Generation is deterministic for a given seed and independent of the
+thread count: every tensor is filled in fixed 1 Mi-element chunks, chunk c of
+tensor t drawing from ``default_rng(SeedSequence(seed, spawn_key=(t, c)))``.
+
+Distributions (Q8_0 matrices follow the benchmark definition, N(0, 0.02)
+before quantisation; the f32 parameters are chosen so the recurrence and
+norms stay in a realistic range):
+
+* projection / embedding matrices: N(0, 0.02) -> Q8_0;
+* RMSNorm gammas (stored pre-folded, model/qwen35.py:9): 1 + N(0, 0.02);
+* ssm_a = -exp(U(0, log 16)) (GGUF stores -exp(A_log));
+* ssm_dt.bias = log(expm1(dt)), dt log-uniform in [1e-3, 1e-1];
+* ssm_conv1d: N(0, 0.25).
+"""
+
+from __future__ import annotations
+
+import concurrent.futures as cf
+import os
+from dataclasses import asdict, dataclass
+from pathlib import Path
+
+import numpy as np
+
+from breezetoken_b200.gguf import GGML_F32, GGML_IQ3_S, GGML_Q8_0, GGUFWriter
+from breezetoken_b200.quant import quantize_iq3_s, quantize_q8_0
+
+CHUNK = 1 << 20
+
+
+@dataclass(frozen=True)
+class Qwen35Spec:
+    """Shape of a Qwen3.5 hybrid decoder (qwen35 GGUF metadata)."""
+
+    hidden: int = 1024
+    n_layers: int = 24
+    n_heads: int = 8
+    n_kv: int = 2
+    head_dim: int = 256
+    rope_dim: int = 64
+    rope_theta: float = 1e7
+    ffn: int = 3584
+    vocab: int = 151936
+    ssm_inner: int = 2048
+    ssm_state: int = 128
+    ssm_heads: int = 16
+    conv_k: int = 4
+    attn_interval: int = 4
+    eps: float = 1e-6
+    context_length: int = 262144
+
+
+#: BASELINE config 1: the Qwen3.5-0.8B shape.
+QWEN35_0_8B = Qwen35Spec()
+#: A small model with the same per-layer kernel shapes (GQA 8/2x256, GDN 16x128)
+#: and one full [GDN, GDN, GDN, GQA] period, for fast parity tests.
+QWEN35_TINY = Qwen35Spec(hidden=512, n_layers=4, ffn=1024, vocab=8192)
+
+SPECS = {"qwen35-0.8b": QWEN35_0_8B, "qwen35-tiny": QWEN35_TINY}
+
+
+def _threads() -> int:
+    return max(1, min(16, os.cpu_count() or 1))
+
+
+def _fill(seed: int, tensor_id: int, n: int, kind: str, pool: cf.Executor) -> np.ndarray:
+    """n float32 values of distribution `kind`, chunked and seeded deterministically."""
+    out = np.empty(n, dtype=np.float32)
+
+    def chunk(c: int) -> None:
+        rng = np.random.default_rng(np.random.SeedSequence(seed, spawn_key=(tensor_id, c)))
+        view = out[c * CHUNK : min(n, (c + 1) * CHUNK)]
+        if kind == "normal":
+            rng.standard_normal(view.shape[0], dtype=np.float32, out=view)
+        else:  # uniform [0, 1)
+            rng.random(view.shape[0], dtype=np.float32, out=view)
+
+    list(pool.map(chunk, range((n + CHUNK - 1) // CHUNK)))
+    return out
+
+
+def _q8_rows(values: np.ndarray, rows: int, k: int, pool: cf.Executor) -> np.ndarray:
+    m = values.reshape(rows, k)
+    step = max(1, CHUNK // k)
+    parts = list(pool.map(lambda r: quantize_q8_0(m[r : r + step]), range(0, rows, step)))
+    return np.concatenate(parts, axis=0)
+
+
+def qwen35_tensors(spec: Qwen35Spec) -> list[tuple[str, tuple[int, ...], str]]:
+    """(name, logical shape, role) of every tensor, in file order."""
+    s = spec
+    t: list[tuple[str, tuple[int, ...], str]] = [
+        ("token_embd.weight", (s.vocab, s.hidden), "q8"),
+        ("output_norm.weight", (s.hidden,), "gamma"),
+    ]
+    for i in range(s.n_layers):
+        p = f"blk.{i}."
+        t += [
+            (p + "attn_norm.weight", (s.hidden,), "gamma"),
+            (p + "post_attention_norm.weight", (s.hidden,), "gamma"),
+            (p + "ffn_gate.weight", (s.ffn, s.hidden), "q8"),
+            (p + "ffn_up.weight", (s.ffn, s.hidden), "q8"),
+            (p + "ffn_down.weight", (s.hidden, s.ffn), "q8"),
+        ]
+        if (i + 1) % s.attn_interval == 0:
+            t += [
+                (p + "attn_q.weight", (2 * s.n_heads * s.head_dim, s.hidden), "q8"),
+                (p + "attn_k.weight", (s.n_kv * s.head_dim, s.hidden), "q8"),
+                (p + "attn_v.weight", (s.n_kv * s.head_dim, s.hidden), "q8"),
+                (p + "attn_output.weight", (s.hidden, s.n_heads * s.head_dim), "q8"),
+                (p + "attn_q_norm.weight", (s.head_dim,), "gamma"),
+                (p + "attn_k_norm.weight", (s.head_dim,), "gamma"),
+            ]
+        else:
+            t += [
+                (p + "attn_qkv.weight", (3 * s.ssm_inner, s.hidden), "q8"),
+                (p + "attn_gate.weight", (s.ssm_inner, s.hidden), "q8"),
+                (p + "ssm_conv1d.weight", (3 * s.ssm_inner, s.conv_k), "conv"),
+                (p + "ssm_alpha.weight", (s.ssm_heads, s.hidden), "q8"),
+                (p + "ssm_beta.weight", (s.ssm_heads, s.hidden), "q8"),
+                (p + "ssm_a", (s.ssm_heads,), "ssm_a"),
+                (p + "ssm_dt.bias", (s.ssm_heads,), "dt_bias"),
+                (p + "ssm_out.weight", (s.hidden, s.ssm_inner), "q8"),
+                (p + "ssm_norm.weight", (s.ssm_state,), "gamma"),
+            ]
+    return t
+
+
+def write_qwen35_gguf(path: str | Path, spec: Qwen35Spec = QWEN35_0_8B, seed: int = 0) -> Path:
+    """Write a seeded random Qwen3.5-shaped Q8_0/F32 GGUF to ``path``."""
+    s = spec
+    w = GGUFWriter()
+    w.add("general.architecture", "qwen35")
+    w.add("general.name", f"synthetic-qwen35-seed{seed}")
+    w.add("general.alignment", 32)
+    w.add("qwen35.block_count", s.n_layers)
+    w.add("qwen35.context_length", s.context_length)
+    w.add("qwen35.embedding_length", s.hidden)
+    w.add("qwen35.feed_forward_length", s.ffn)
+    w.add("qwen35.attention.head_count", s.n_heads)
+    w.add("qwen35.attention.head_count_kv", s.n_kv)
+    w.add("qwen35.attention.key_length", s.head_dim)
+    w.add("qwen35.attention.value_length", s.head_dim)
+    w.add("qwen35.attention.layer_norm_rms_epsilon", float(s.eps))
+    w.add("qwen35.rope.dimension_count", s.rope_dim)
+    w.add("qwen35.rope.freq_base", float(s.rope_theta))
+    w.add("qwen35.ssm.inner_size", s.ssm_inner)
+    w.add("qwen35.ssm.state_size", s.ssm_state)
+    w.add("qwen35.ssm.group_count", s.ssm_heads)
+    w.add("qwen35.ssm.conv_kernel", s.conv_k)
+    w.add("qwen35.full_attention_interval", s.attn_interval)
+    with cf.ThreadPoolExecutor(_threads()) as pool:
+        for tid, (name, shape, role) in enumerate(qwen35_tensors(s)):
+            n = int(np.prod(shape))
+            if role == "q8":
+                vals = _fill(seed, tid, n, "normal", pool) * np.float32(0.02)
+                w.add_tensor(name, shape, GGML_Q8_0, _q8_rows(vals, shape[0], shape[1], pool))
+                continue
+            if role == "gamma":
+                vals = np.float32(1.0) + _fill(seed, tid, n, "normal", pool) * np.float32(0.02)
+            elif role == "conv":
+                vals = _fill(seed, tid, n, "normal", pool) * np.float32(0.25)
+            elif role == "ssm_a":
+                vals = -np.exp(_fill(seed, tid, n, "uniform", pool) * np.float32(np.log(16.0)))
+            elif role == "dt_bias":
+                u = _fill(seed, tid, n, "uniform", pool)
+                dt = np.exp(np.log(1e-3) + u * (np.log(1e-1) - np.log(1e-3)))
+                vals = np.log(np.expm1(dt))
+            else:
+                raise AssertionError(role)
+            w.add_tensor(name, shape, GGML_F32, np.asarray(vals, dtype=np.float32).reshape(shape))
+    return w.write(path)
+
+
+def spec_dict(spec: Qwen35Spec) -> dict:
+    return asdict(spec)
+
+
+# --------------------------------------------------------------------------
+# MoE expert layer (the Qwen3.6-35B-A3B expert FFN shape)
+# --------------------------------------------------------------------------
+@dataclass(frozen=True)
+class MoeSpec:
+    hidden: int = 2048
+    n_experts: int = 256
+    top_k: int = 8
+    ffn: int = 512
+
+
+def make_moe_layer(spec: MoeSpec = MoeSpec(), seed: int = 3, n_experts: int | None = None):
+    """IQ3_S expert tensors of one MoE layer as GGUF-stored bytes.
+
+    Returns dict with ``gate``/``up`` (E, ffn, hidden) and ``down`` (E, hidden,
+    ffn) as uint8 arrays of shape (E * rows, row_bytes), plus the bf16 shared
+    expert (gate/up (ffn, hidden), down (hidden, ffn)) as float32 values
+    already rounded to bf16, and the shared-expert gate vector.
+    """
+    e = spec.n_experts if n_experts is None else n_experts
+    out: dict[str, np.ndarray] = {}
+    with cf.ThreadPoolExecutor(_threads()) as pool:
+        for tid, (name, rows, k) in enumerate(
+            (("gate", e * spec.ffn, spec.hidden), ("up", e * spec.ffn, spec.hidden), ("down", e * spec.hidden, spec.ffn))
+        ):
+            vals = (_fill(seed, 100 + tid, rows * k, "normal", pool) * np.float32(0.02)).reshape(rows, k)
+            step = max(1, CHUNK // k)
+            parts = list(pool.map(lambda r, v=vals: quantize_iq3_s(v[r : r + step]), range(0, rows, step)))
+            out[name] = np.concatenate(parts, axis=0)
+        import torch  # noqa: PLC0415 - bf16 rounding only
+
+        for tid, (name, shape) in enumerate(
+            (("sh_gate", (spec.ffn, spec.hidden)), ("sh_up", (spec.ffn, spec.hidden)), ("sh_down", (spec.hidden, spec.ffn)))
+        ):
+            vals = _fill(seed, 200 + tid, int(np.prod(shape)), "normal", pool) * np.float32(0.02)
+            out[name] = torch.from_numpy(vals.reshape(shape)).to(torch.bfloat16).float().numpy()
+        out["sh_gate_inp"] = _fill(seed, 210, spec.hidden, "normal", pool) * np.float32(0.02)
+    return out
+
+
+__all__ = [
+    "GGML_IQ3_S",
+    "MoeSpec",
+    "QWEN35_0_8B",
+    "QWEN35_TINY",
+    "Qwen35Spec",
+    "SPECS",
+    "make_moe_layer",
+    "qwen35_tensors",
+    "write_qwen35_gguf",
+]

@@ -1,0 +1,215 @@
+/*
+ * bt_b200.h -- C ABI of the B200 (sm_100a) decode-step library.
+ *
+ * Every entry point takes raw device pointers, element counts and a CUDA
+ * stream passed as `void*` (a cudaStream_t; NULL = legacy default stream).
+ * None of them allocates device memory or synchronises the stream: outputs
+ * and workspaces are owned by the caller, so every call can be captured in
+ * a CUDA graph.  Each returns a BT_* status code; bt_last_error() gives the
+ * message of the last failure on the calling thread.
+ *
+ * The entry points replace the operations of breezetoken's `Backend`
+ * interface (breezetoken/backends.py:28-98) and the per-token decode step of
+ * `Qwen35.forward_token` (breezetoken/model/qwen35.py:252-286) /
+ * `GraphMixin._graph_body` (breezetoken/model/graph.py:66-91).
+ *
+ * Weight layout used by the Q8_0 entry points ("q8 rows"): one row of K
+ * weights is stored as [K/32 fp16 block scales, zero-padded to a multiple of
+ * 16 bytes][K int8 quants]; rows are contiguous.  bt_q8_row_bytes(K) gives
+ * the row stride.  bt_repack_q8_0 converts GGUF Q8_0 blocks into it.
+ */
+#ifndef BT_B200_H
+#define BT_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define BT_API __attribute__((visibility("default")))
+#else
+#define BT_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ------------------------------------------------------------------ status */
+#define BT_OK 0
+#define BT_ERR_INVALID 1     /* bad pointer, shape or argument        */
+#define BT_ERR_UNSUPPORTED 2 /* shape/dtype this build does not serve */
+#define BT_ERR_CUDA 3        /* a CUDA runtime call failed            */
+#define BT_ERR_TIMEOUT 4     /* a bounded device-side wait gave up    */
+
+/* element types for the dtype arguments */
+#define BT_F32 0
+#define BT_BF16 1
+
+/* Message of the last failed call on this thread ("" if none). */
+BT_API const char* bt_last_error(void);
+/* Library ABI version (major*100 + minor). */
+BT_API int bt_version(void);
+/* Number of SMs of the current device (cached per device). */
+BT_API int bt_sm_count(void);
+/* Bytes of one q8 row of K weights (see the header comment). */
+BT_API int64_t bt_q8_row_bytes(int64_t k);
+
+/* ------------------------------------------------------- weight repacking */
+/* GGUF Q8_0 rows -> q8 rows.  `src` holds `rows` rows of K/32 34-byte blocks
+ * (fp16 d, 32 x int8), as stored in the GGUF file (gguf.py:184-212).  Source
+ * row i is written to destination row dst_row0 + i * dst_row_step, so two
+ * matrices can be interleaved row by row (gate/up) or concatenated.        */
+BT_API int bt_repack_q8_0(const void* src, void* dst, int64_t rows, int64_t k,
+                   int64_t dst_row0, int64_t dst_row_step, void* stream);
+
+/* Dequantise q8 rows to f32 (rows x k), exactly d * q
+ * (quant/dequant.py:72-75).                                               */
+BT_API int bt_dequant_q8_rows(const void* w, float* out, int64_t rows, int64_t k,
+                       void* stream);
+
+/* GGUF IQ3_S blocks (110 bytes per 256 weights) to f32, bit-exact with
+ * quant/dequant.py:164-185 (`_deq_iq3_s`).                                */
+BT_API int bt_dequant_iq3_s(const void* raw, float* out, int64_t rows, int64_t cols,
+                     void* stream);
+
+/* ------------------------------------------------------- Backend ops */
+/* Backend.linear with Q8_0 weights (backends.py:109-112):
+ * y[m][n] = sum_k x[m][k] * dequant(W)[n][k] for m < n_vec (<= 8).        */
+BT_API int bt_linear_q8(const void* w, const float* x, float* y, int64_t n, int64_t k,
+                 int n_vec, void* stream);
+
+/* Backend.linear with a dense (K, N) weight as the reference stores it
+ * (model/qwen35.py:148-153): y[n] = sum_k x[k] * W[k][n].
+ * w_dtype is BT_BF16 or BT_F32.                                           */
+BT_API int bt_linear_kn(const void* w, int w_dtype, const float* x, float* y,
+                 int64_t k, int64_t n, void* stream);
+
+/* Backend.rms_norm (backends.py:119-123) over rows of length n.           */
+BT_API int bt_rms_norm(const float* x, const float* w, float* y, int64_t rows,
+                int64_t n, float eps, void* stream);
+
+/* Backend.fused_add_rms_norm (backends.py:229-238): h = a + b,
+ * xn = rms_norm(h, w, eps).                                               */
+BT_API int bt_fused_add_rms_norm(const float* a, const float* b, const float* w,
+                          float* h, float* xn, int64_t rows, int64_t n,
+                          float eps, void* stream);
+
+/* Backend.silu_mul (backends.py:160-163): y = silu(g) * u.                */
+BT_API int bt_silu_mul(const float* g, const float* u, float* y, int64_t n,
+                void* stream);
+
+/* Backend.rope (backends.py:218-226): partial rotate-half RoPE on the first
+ * rope_dim of each row at position *pos (device int32); cos/sin are
+ * (cap, rope_dim) f32 tables.                                             */
+BT_API int bt_rope(const float* x, const float* cos_t, const float* sin_t,
+            const int32_t* pos, float* y, int64_t rows, int64_t dim,
+            int64_t rope_dim, int64_t cap, void* stream);
+
+/* Backend.attention / attention_fixed (backends.py:196-215, 682-706):
+ * GQA decode, one query per sequence.
+ *   q:   (batch, heads, dim) f32
+ *   k,v: (batch, cap, kv_heads, dim) in kv_dtype (BT_F32 or BT_BF16)
+ *   lens: (batch,) int32 device lengths (keys [0, lens[b]) are attended)
+ *   out: (batch, heads, dim) f32
+ * workspace: bt_attention_workspace_bytes() bytes, zeroed once before the
+ * first call (the kernel leaves it zeroed again).                         */
+BT_API int64_t bt_attention_workspace_bytes(int64_t batch, int64_t kv_heads,
+                                     int64_t heads, int64_t dim, int splits);
+BT_API int bt_attention_decode(const float* q, const void* k, const void* v,
+                        int kv_dtype, const int32_t* lens, float* out,
+                        int64_t batch, int64_t heads, int64_t kv_heads,
+                        int64_t dim, int64_t cap, float scale, int splits,
+                        void* workspace, void* stream);
+
+/* Backend.gdn_decode (backends.py:241-271): one gated-delta-rule step.
+ *   q,k: (batch, heads_k, dim), v: (batch, heads_v, dim) in in_dtype
+ *   g (log decay), beta (logits): (batch, heads_v) f32
+ *   state: (batch, heads_v, dim, dim) f32, updated in place
+ *   out: (batch, heads_v, dim) f32
+ * Value head h reads key head h % heads_k.                                */
+BT_API int bt_gdn_decode(const void* q, const void* k, const void* v, int in_dtype,
+                  const float* g, const float* beta, float* state, float* out,
+                  int64_t batch, int64_t heads_k, int64_t heads_v, int64_t dim,
+                  float scale, float eps, void* stream);
+
+/* argmax with torch.argmax's first-index tie rule over rows of length n.
+ * workspace: bt_argmax_workspace_bytes(rows) bytes, zeroed before first use. */
+BT_API int64_t bt_argmax_workspace_bytes(int64_t rows);
+BT_API int bt_argmax(const float* x, int64_t rows, int64_t n, int32_t* out,
+              void* workspace, void* stream);
+
+/* ------------------------------------------------- Qwen3.5 decode step */
+typedef struct BtQwen35Dims {
+  int32_t hidden, n_layers, n_heads, n_kv, head_dim, rope_dim, ffn, vocab;
+  int32_t ssm_inner, ssm_state, ssm_heads, conv_k, max_ctx, batch;
+  float eps, l2_eps;
+} BtQwen35Dims;
+
+typedef struct BtQwen35Layer {
+  int32_t is_attn, pad_;
+  const float* norm_in;   /* (hidden,) f32 */
+  const float* norm_post; /* (hidden,) */
+  const float* norm_next; /* next layer's norm_in, or output_norm */
+  const void* w_in;   /* GDN: q8 rows [qkv | z | alpha | beta]; attn: [q|gate per head, k, v] */
+  const void* w_out;  /* GDN: ssm_out (hidden x inner); attn: attn_output */
+  const void* w_gu;   /* q8 rows gate/up interleaved: row 2j = gate_j, 2j+1 = up_j */
+  const void* w_down; /* (hidden x ffn) */
+  const float* conv_w;   /* GDN (3*inner, conv_k) */
+  const float* a_log;    /* GDN (ssm_heads,) = -exp(A_log) */
+  const float* dt_bias;  /* GDN (ssm_heads,) */
+  const float* ssm_norm; /* GDN (ssm_state,) */
+  const float* q_norm;   /* attn (head_dim,) */
+  const float* k_norm;   /* attn (head_dim,) */
+  float* conv_state;     /* GDN (batch, 3*inner, conv_k-1) */
+  float* rec_state;      /* GDN (batch, ssm_heads, ssm_state, ssm_state) */
+  float* k_cache;        /* attn (batch, max_ctx, n_kv*head_dim) f32 */
+  float* v_cache;
+} BtQwen35Layer;
+
+typedef struct BtQwen35Model {
+  BtQwen35Dims dims;
+  const void* embed;     /* q8 rows (vocab x hidden): token_embd == tied head */
+  const float* rope_cos; /* (max_ctx, rope_dim) */
+  const float* rope_sin;
+  const BtQwen35Layer* layers; /* host array of n_layers */
+} BtQwen35Model;
+
+typedef struct BtQwen35Runtime {
+  int32_t* pos;       /* (batch,) device positions of the token being consumed */
+  int32_t* token;     /* (batch,) device token ids consumed by the next step */
+  int32_t* history;   /* (batch, max_ctx) tokens produced, indexed by pos+1; may be NULL */
+  float* logits;      /* (batch, vocab) or NULL (argmax only) */
+  float* h0;          /* (batch, hidden) residual ping */
+  float* h1;          /* (batch, hidden) residual pong */
+  float* delta;       /* (batch, hidden) mixer / mlp output */
+  float* proj;        /* (batch, bt_qwen35_proj_elems) in-projection outputs */
+  float* mix;         /* (batch, max(ssm_inner, n_heads*head_dim)) mixer output */
+  float* act;         /* (batch, ffn) silu(gate)*up */
+  void* workspace;    /* bt_qwen35_workspace_bytes(), zeroed once */
+  int32_t* status;    /* device word: BT_ERR_TIMEOUT if a bounded wait expired */
+} BtQwen35Runtime;
+
+BT_API int64_t bt_qwen35_proj_elems(const BtQwen35Dims* dims);
+BT_API int64_t bt_qwen35_workspace_bytes(const BtQwen35Dims* dims);
+
+/* Enqueue one decode step for every sequence in the batch: consume token[b]
+ * at pos[b], write logits (if rt->logits), token[b] = argmax, history, and
+ * pos[b] += 1.  Mirrors Qwen35.forward_token + the in-graph argmax and
+ * position increment of GraphMixin._graph_body.  `with_logits` = 0 skips
+ * the head and leaves token/pos untouched except pos += 1 (prefill).     */
+BT_API int bt_qwen35_step(const BtQwen35Model* model, const BtQwen35Runtime* rt,
+                   int with_logits, void* stream);
+
+/* Capture `n_steps` consecutive decode steps into one CUDA graph (native
+ * stream capture; the stream must not be the legacy default stream).  The
+ * model and runtime structs are copied into the graph; the device buffers
+ * they point to must outlive it.                                          */
+BT_API int bt_qwen35_graph_create(const BtQwen35Model* model, const BtQwen35Runtime* rt,
+                           int n_steps, void* stream, void** graph_out);
+BT_API int bt_graph_launch(void* graph, void* stream);
+BT_API int bt_graph_destroy(void* graph);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* BT_B200_H */
