@@ -341,6 +341,10 @@ int attention_launch(const AttnParams& p, cudaStream_t stream, bool pdl) {
                 p.kv_heads);
   if (p.splits < 1 || p.splits > 1024) return fail(BT_ERR_INVALID, "attention: splits must be in [1, 1024]");
   if (p.model && p.kv_dtype != BT_F32) return fail(BT_ERR_UNSUPPORTED, "model-mode attention keeps an f32 cache");
+  if ((reinterpret_cast<uintptr_t>(p.k) | reinterpret_cast<uintptr_t>(p.v)) & 15)
+    return fail(BT_ERR_INVALID, "attention: K/V must be 16-byte aligned (vector loads)");
+  if ((p.kv_ts * (p.kv_dtype == BT_BF16 ? 2 : 4)) % 16 || (p.kv_bs * (p.kv_dtype == BT_BF16 ? 2 : 4)) % 16)
+    return fail(BT_ERR_INVALID, "attention: K/V strides must be multiples of 16 bytes");
   if (p.model && (p.rope_dim < 0 || p.rope_dim > p.dim || p.rope_dim % 2))
     return fail(BT_ERR_INVALID, "attention: invalid rope_dim %d", p.rope_dim);
   return p.kv_dtype == BT_BF16 ? launch_dtype<__nv_bfloat16>(p, stream, pdl) : launch_dtype<float>(p, stream, pdl);

@@ -347,6 +347,10 @@ int gemv_q8_plan(GemvQ8Params& p, int sm_count, GemvQ8Launch& L) {
   if (p.k < 32 || p.k % 32 != 0) return fail(BT_ERR_UNSUPPORTED, "q8 GEMV needs K %% 32 == 0, got K=%d", p.k);
   if (p.n_rows < 1) return fail(BT_ERR_INVALID, "q8 GEMV needs at least one row");
   if (p.n_vec < 1 || p.n_vec > kMaxVec) return fail(BT_ERR_UNSUPPORTED, "q8 GEMV serves 1..8 vectors, got %d", p.n_vec);
+  if (!p.w || (reinterpret_cast<uintptr_t>(p.w) & 15))
+    return fail(BT_ERR_INVALID, "q8 GEMV weights must be 16-byte aligned (bulk copies)");
+  if (p.epilogue == EPI_ARGMAX && (!p.best || !p.counter))
+    return fail(BT_ERR_INVALID, "argmax epilogue needs its workspace");
   p.sb = static_cast<int32_t>(bt_q8_row_bytes(p.k) - p.k);
   p.row_bytes = static_cast<int32_t>(bt_q8_row_bytes(p.k));
   p.xs_stride = static_cast<int32_t>(gemv_x_stride(p.k));

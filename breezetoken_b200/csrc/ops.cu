@@ -224,6 +224,8 @@ int check_launch(const char* what) {
 int repack_q8_0(const void* src, void* dst, int64_t rows, int64_t k, int64_t dst_row0, int64_t dst_row_step,
                 cudaStream_t stream) {
   if (!src || !dst || rows < 0 || k < 32 || k % 32) return fail(BT_ERR_INVALID, "repack_q8_0: bad arguments (k=%lld)", (long long)k);
+  if ((reinterpret_cast<uintptr_t>(dst) & 15) || (reinterpret_cast<uintptr_t>(src) & 1))
+    return fail(BT_ERR_INVALID, "repack_q8_0: dst must be 16-byte and src 2-byte aligned");
   if (rows == 0) return BT_OK;
   const int64_t row_bytes = bt_q8_row_bytes(k);
   repack_q8_0_kernel<<<grid_for(rows * (k / 32), 256), 256, 0, stream>>>(
@@ -243,6 +245,7 @@ int dequant_q8_rows(const void* w, float* out, int64_t rows, int64_t k, cudaStre
 
 int dequant_iq3_s(const void* raw, float* out, int64_t rows, int64_t cols, cudaStream_t stream) {
   if (!raw || !out || rows < 0 || cols % 256) return fail(BT_ERR_INVALID, "dequant_iq3_s: cols must be a multiple of 256");
+  if (reinterpret_cast<uintptr_t>(out) & 15) return fail(BT_ERR_INVALID, "dequant_iq3_s: out must be 16-byte aligned");
   const int64_t n_blocks = rows * (cols / 256);
   if (n_blocks == 0) return BT_OK;
   dequant_iq3_s_kernel<<<grid_for(n_blocks * 32, 256), 256, 0, stream>>>(static_cast<const uint8_t*>(raw), out,
