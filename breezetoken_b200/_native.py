@@ -16,6 +16,23 @@ LIB_PATH = Path(__file__).resolve().parent / "lib" / "libbt_b200.so"
 
 BT_OK, BT_ERR_INVALID, BT_ERR_UNSUPPORTED, BT_ERR_CUDA, BT_ERR_TIMEOUT = range(5)
 BT_F32, BT_BF16 = 0, 1
+BT_STATUS_WORDS = 8
+
+_SITES = {
+    1: "GEMV producer waiting for a consumed stage",
+    2: "GEMV producer waiting for its last copies",
+    3: "GEMV consumer waiting for a stage",
+    4: "token id outside the vocabulary",
+    5: "attended length outside the cache",
+    6: "RoPE position outside the table",
+}
+
+
+def describe_status(rec) -> str:
+    """Human-readable form of a device status record [code, site, block, a, b, c, ...]."""
+    code, site, block, a, b, c = (list(rec) + [0] * 6)[:6]
+    what = "bounded wait expired" if code == BT_ERR_TIMEOUT else "invalid input"
+    return f"{what} at {_SITES.get(site, f'site {site}')} (block {block}, detail {a}, {b}, {c})"
 
 
 class B200Error(RuntimeError):

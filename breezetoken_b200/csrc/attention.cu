@@ -102,7 +102,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const __grid_
 
   int L = p.model ? p.pos[b] + 1 : p.lens[b];
   if (L < 0 || L > p.cap) {
-    if (threadIdx.x == 0) report_status(p.status, BT_ERR_INVALID);
+    if (threadIdx.x == 0) report_status(p.status, BT_ERR_INVALID, SITE_ATTN_LENGTH, L, p.cap, b);
     L = L < 0 ? 0 : p.cap;
   }
   const int chunk = (L + p.splits - 1) / p.splits;

@@ -35,8 +35,29 @@ __device__ __forceinline__ uint64_t global_ns() {
 // reports BT_ERR_TIMEOUT through the caller's status word.
 constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s
 
-__device__ __forceinline__ void report_status(int32_t* status, int32_t code) {
-  if (status) atomicCAS(reinterpret_cast<int*>(status), 0, code);
+// Where a device-side check fired (status word 1).
+enum StatusSite : int32_t {
+  SITE_GEMV_PRODUCER_EMPTY = 1,  // producer waiting for a consumed stage
+  SITE_GEMV_PRODUCER_DRAIN = 2,  // producer waiting for its last copies to land
+  SITE_GEMV_CONSUMER_FULL = 3,   // consumer waiting for a stage's bytes
+  SITE_EMBED_TOKEN = 4,          // token id outside the vocabulary
+  SITE_ATTN_LENGTH = 5,          // attended length outside [0, cap]
+  SITE_ROPE_POS = 6,             // RoPE position outside the table
+};
+
+// The caller's status record is BT_STATUS_WORDS int32: [code, site, block,
+// a, b, c, ...].  The first failure wins and fills the record.
+__device__ __forceinline__ void report_status(int32_t* status, int32_t code, int32_t site = 0, int32_t a = 0,
+                                              int32_t b = 0, int32_t c = 0) {
+  if (!status) return;
+  if (atomicCAS(reinterpret_cast<int*>(status), 0, code) == 0) {
+    status[1] = site;
+    status[2] = static_cast<int32_t>(blockIdx.x);
+    status[3] = a;
+    status[4] = b;
+    status[5] = c;
+    __threadfence();
+  }
 }
 
 // ----------------------------------------------------------- mbarrier
@@ -69,17 +90,15 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
-// Bounded wait for phase `parity` of `bar`; false (and status set) on timeout.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int32_t* status) {
+// Bounded wait for phase `parity` of `bar`; false on timeout (the caller
+// reports where).
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = global_ns();
   while (true) {
     for (int i = 0; i < 64; ++i)
       if (mbar_try_wait(bar, parity)) return true;
-    if (global_ns() - t0 > kWaitLimitNs) {
-      report_status(status, BT_ERR_TIMEOUT);
-      return false;
-    }
+    if (global_ns() - t0 > kWaitLimitNs) return false;
   }
 }
 

@@ -29,7 +29,7 @@ __device__ void gemv_prologue(const GemvQ8Params& p, float* xs, float* scratch) 
       if (p.prologue == PRO_EMBED_NORM) {
         int64_t tok = p.tokens[v];
         if (tok < 0 || tok >= p.embed_rows) {
-          if (tid == 0) report_status(p.status, BT_ERR_INVALID);
+          if (tid == 0) report_status(p.status, BT_ERR_INVALID, SITE_EMBED_TOKEN, static_cast<int32_t>(tok), v);
           tok = 0;
         }
         erow = p.embed + tok * static_cast<int64_t>(p.row_bytes);
@@ -137,11 +137,16 @@ __global__ void __launch_bounds__(kGemvThreads, 2)
   const int64_t row1 = u1 * 4 < p.n_rows ? u1 * 4 : p.n_rows;
   const int cta_rows = static_cast<int>(row1 - row0);
   const int n_iters = (cta_rows + p.stage_rows - 1) / p.stage_rows;
-  const int S = p.stages;
+  // Per-warp rings: iteration `it` belongs to consumer warp it % 8, which owns
+  // slots [w * SPW, (w + 1) * SPW) and consumes them strictly in order.  A
+  // waiter is therefore never more than one phase ahead of its barrier, so the
+  // mbarrier parity test cannot alias (a shared ring with more consumers than
+  // stages would let a warp pass on the parity of a phase two fills old).
+  const int SPW = p.stages;
   const uint32_t stage_bytes = static_cast<uint32_t>(p.stage_rows) * p.row_bytes;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < S; ++s) {
+    for (int s = 0; s < kConsumerWarps * SPW; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
@@ -156,8 +161,12 @@ __global__ void __launch_bounds__(kGemvThreads, 2)
       const uint64_t policy = l2_evict_first_policy();
       int issued = 0;
       for (int it = 0; it < n_iters; ++it) {
-        const int s = it % S;
-        if (it >= S && !mbar_wait(&empty[s], ((it / S) - 1) & 1, p.status)) break;
+        const int i = it / kConsumerWarps;  // this warp's i-th stage
+        const int s = (it % kConsumerWarps) * SPW + i % SPW;
+        if (i >= SPW && !mbar_wait(&empty[s], ((i / SPW) - 1) & 1)) {
+          report_status(p.status, BT_ERR_TIMEOUT, SITE_GEMV_PRODUCER_EMPTY, it, n_iters, SPW);
+          break;
+        }
         const int64_t r = row0 + static_cast<int64_t>(it) * p.stage_rows;
         const int nr = static_cast<int>(min(static_cast<int64_t>(p.stage_rows), row1 - r));
         const uint32_t bytes = static_cast<uint32_t>(nr) * p.row_bytes;
@@ -166,9 +175,16 @@ __global__ void __launch_bounds__(kGemvThreads, 2)
                  &full[s], policy);
         issued = it + 1;
       }
-      // Do not leave the CTA with copies in flight (bounded).
-      for (int it = max(0, issued - S); it < issued; ++it)
-        if (!mbar_wait(&full[it % S], (it / S) & 1, p.status)) break;
+      // Do not leave the CTA with copies in flight (bounded): wait for the
+      // last fill of every slot.
+      for (int it = max(0, issued - kConsumerWarps * SPW); it < issued; ++it) {
+        const int i = it / kConsumerWarps;
+        const int s = (it % kConsumerWarps) * SPW + i % SPW;
+        if (!mbar_wait(&full[s], (i / SPW) & 1)) {
+          report_status(p.status, BT_ERR_TIMEOUT, SITE_GEMV_PRODUCER_DRAIN, it, n_iters, SPW);
+          break;
+        }
+      }
     }
     return;
   }
@@ -187,9 +203,12 @@ __global__ void __launch_bounds__(kGemvThreads, 2)
   const float4* xs4 = reinterpret_cast<const float4*>(xs);
   const int xs4_stride = p.xs_stride >> 2;
 
-  for (int it = warp; it < n_iters; it += kConsumerWarps) {
-    const int s = it % S;
-    if (!mbar_wait(&full[s], (it / S) & 1, p.status)) break;
+  for (int it = warp, i = 0; it < n_iters; it += kConsumerWarps, ++i) {
+    const int s = warp * SPW + i % SPW;
+    if (!mbar_wait(&full[s], (i / SPW) & 1)) {
+      report_status(p.status, BT_ERR_TIMEOUT, SITE_GEMV_CONSUMER_FULL, it, n_iters, (warp << 16) | SPW);
+      break;
+    }
     const uint8_t* st = ring + static_cast<size_t>(s) * stage_bytes;
     const int64_t r0 = row0 + static_cast<int64_t>(it) * p.stage_rows;
     const int nr = static_cast<int>(min(static_cast<int64_t>(p.stage_rows), row1 - r0));
@@ -324,6 +343,9 @@ int launch_impl(const GemvQ8Params& p, const GemvQ8Launch& L, cudaStream_t strea
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          kSmemBudget + GemvSmem::kHeader + 1024);
     if (e != cudaSuccess) return fail_cuda(e, "gemv_q8 set smem");
+    // full shared-memory carveout, so the PDL successor's CTA fits beside this one
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+    if (e != cudaSuccess) return fail_cuda(e, "gemv_q8 set carveout");
     configured_device = dev;
   }
   cudaLaunchConfig_t cfg = {};
@@ -364,18 +386,23 @@ int gemv_q8_plan(GemvQ8Params& p, int sm_count, GemvQ8Launch& L) {
   p.group_rows = gr;
   const int64_t x_bytes = ((static_cast<int64_t>(p.n_vec) * p.xs_stride * 4 + 127) / 128) * 128;
   const int64_t ring_budget = kSmemBudget - x_bytes;
-  int64_t f_rows = std::max<int64_t>(1, rows_per_cta / (kConsumerWarps * gr));
-  int64_t f_bytes = std::max<int64_t>(1, 16384 / (static_cast<int64_t>(gr) * p.row_bytes));
+  // stage = gr * f rows, ~8 KB at most, and no more rows than keep all 8
+  // consumer warps busy
+  const int64_t f_rows = std::max<int64_t>(1, rows_per_cta / (kConsumerWarps * gr));
+  const int64_t f_bytes = std::max<int64_t>(1, 8192 / (static_cast<int64_t>(gr) * p.row_bytes));
   const int64_t f = std::min(f_rows, f_bytes);
   p.stage_rows = static_cast<int32_t>(gr * f);
   const int64_t stage_bytes = static_cast<int64_t>(p.stage_rows) * p.row_bytes;
-  if (stage_bytes > ring_budget)
+  if (kConsumerWarps * stage_bytes > ring_budget)
     return fail(BT_ERR_UNSUPPORTED, "q8 GEMV row of K=%d does not fit the stage budget", p.k);
+  // stages per consumer warp (each warp owns its own ring)
   const int64_t iters = (rows_per_cta + p.stage_rows - 1) / p.stage_rows;
-  p.stages = static_cast<int32_t>(std::min<int64_t>({kMaxStages, ring_budget / stage_bytes, std::max<int64_t>(1, iters)}));
+  const int64_t per_warp = (iters + kConsumerWarps - 1) / kConsumerWarps;
+  p.stages = static_cast<int32_t>(std::min<int64_t>(
+      {kMaxStages / kConsumerWarps, ring_budget / (kConsumerWarps * stage_bytes), std::max<int64_t>(1, per_warp)}));
   L.grid = grid;
   L.threads = kGemvThreads;
-  L.smem = GemvSmem::kHeader + x_bytes + static_cast<size_t>(p.stages) * stage_bytes;
+  L.smem = GemvSmem::kHeader + x_bytes + static_cast<size_t>(kConsumerWarps) * p.stages * stage_bytes;
   return BT_OK;
 }
 

@@ -53,7 +53,7 @@ struct GemvQ8Params {
   int32_t k, row_bytes, sb;  // K, bytes per row, scale bytes per row
   int32_t group_rows;        // rows per consumer task (1 or 4)
   int32_t stage_rows;        // rows per stage (multiple of group_rows)
-  int32_t stages;            // ring depth
+  int32_t stages;            // ring depth per consumer warp (each warp owns its slots)
   int32_t n_vec;             // activation vectors (batch)
   int32_t xs_stride;         // floats per vector in the smem x layout
   // prologue

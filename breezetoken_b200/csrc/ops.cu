@@ -156,7 +156,8 @@ __global__ void rope_kernel(const float* __restrict__ x, const float* __restrict
                             float* __restrict__ y, int64_t dim, int64_t rope_dim, int64_t cap, int32_t* status) {
   int64_t p = pos[0];
   if (p < 0 || p >= cap) {
-    if (threadIdx.x == 0 && blockIdx.x == 0) report_status(status, BT_ERR_INVALID);
+    if (threadIdx.x == 0 && blockIdx.x == 0)
+      report_status(status, BT_ERR_INVALID, SITE_ROPE_POS, static_cast<int32_t>(p), static_cast<int32_t>(cap));
     p = p < 0 ? 0 : cap - 1;
   }
   const int64_t row = blockIdx.x;

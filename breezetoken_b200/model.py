@@ -279,7 +279,7 @@ class Qwen35:
         self.mix = torch.zeros(B, mix, **f32)
         self.act = torch.zeros(B, cfg.ffn, **f32)
         self.workspace = torch.zeros(int(self.lib.bt_qwen35_workspace_bytes(C.byref(d))), dtype=torch.uint8, device=dev)
-        self.status = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.status = torch.zeros(N.BT_STATUS_WORDS, dtype=torch.int32, device=dev)
         attn = set(cfg.attn_layers)
         kv = cfg.n_kv * cfg.head_dim
         layer_structs = (N.BtQwen35Layer * cfg.n_layers)()
@@ -315,10 +315,10 @@ class Qwen35:
         return self.stream.cuda_stream
 
     def _check_status(self) -> None:
-        st = int(self.status.item())
-        if st:
+        rec = self.status.cpu().tolist()
+        if rec[0]:
             self.status.zero_()
-            raise N.B200Error(st, "device-side check failed (invalid token/position or a bounded wait expired)")
+            raise N.B200Error(rec[0], f"device-side check failed: {N.describe_status(rec)}")
 
     def step(self, with_logits: bool = True) -> None:
         """Enqueue one decode step on the model's stream (no host sync)."""

@@ -41,6 +41,9 @@ extern "C" {
 #define BT_ERR_CUDA 3        /* a CUDA runtime call failed            */
 #define BT_ERR_TIMEOUT 4     /* a bounded device-side wait gave up    */
 
+/* int32 words of a device status record (see BtQwen35Runtime.status) */
+#define BT_STATUS_WORDS 8
+
 /* element types for the dtype arguments */
 #define BT_F32 0
 #define BT_BF16 1
@@ -186,7 +189,10 @@ typedef struct BtQwen35Runtime {
   float* mix;         /* (batch, max(ssm_inner, n_heads*head_dim)) mixer output */
   float* act;         /* (batch, ffn) silu(gate)*up */
   void* workspace;    /* bt_qwen35_workspace_bytes(), zeroed once */
-  int32_t* status;    /* device word: BT_ERR_TIMEOUT if a bounded wait expired */
+  int32_t* status;    /* BT_STATUS_WORDS device int32, zeroed by the caller: on a
+                         device-side failure [0] = BT_ERR_TIMEOUT or
+                         BT_ERR_INVALID, [1] = site, [2] = block, [3..5] =
+                         site-specific detail; the first failure wins */
 } BtQwen35Runtime;
 
 BT_API int64_t bt_qwen35_proj_elems(const BtQwen35Dims* dims);

@@ -40,7 +40,8 @@ def be(cuda):
 def test_dequant_bit_exact(be) -> None:
     g = golden("dequant")
     out = torch.empty(64, 256, device="cuda")
-    N.call("bt_dequant_iq3_s", _t(g["iq3s_raw"]).data_ptr(), out.data_ptr(), 64, 256, 0)
+    raw_d = _t(g["iq3s_raw"])  # keep device inputs alive until the kernel ran
+    N.call("bt_dequant_iq3_s", raw_d.data_ptr(), out.data_ptr(), 64, 256, 0)
     assert np.array_equal(out.cpu().numpy().view(np.uint32), g["iq3s_out"].view(np.uint32))
     w = Q8Weight.from_gguf(g["q8_raw"], 64, 32, "cuda")
     assert np.array_equal(w.dequantize().cpu().numpy().view(np.uint32), g["q8_out"].view(np.uint32))
@@ -48,7 +49,8 @@ def test_dequant_bit_exact(be) -> None:
     rng = np.random.default_rng(11)
     raw = quantize_iq3_s(rng.standard_normal((96, 1024)).astype(np.float32))
     out = torch.empty(96, 1024, device="cuda")
-    N.call("bt_dequant_iq3_s", _t(raw).data_ptr(), out.data_ptr(), 96, 1024, 0)
+    raw_d = _t(raw)
+    N.call("bt_dequant_iq3_s", raw_d.data_ptr(), out.data_ptr(), 96, 1024, 0)
     assert np.array_equal(out.cpu().numpy(), dequant_iq3_s(raw.reshape(-1), 96, 1024))
 
 
@@ -64,6 +66,21 @@ def test_linear_q8_matches_oracle(be, n, k) -> None:
     y = be.linear(_t(x), w).cpu().numpy()
     ref = ops.linear(x, deq.T)
     assert np.all(np.abs(y - ref) <= _gemv_bound(x, deq))
+
+
+@pytest.mark.parametrize("n,k", [(151936, 1024), (40000, 2048), (9000, 3584)])
+def test_linear_q8_ring_refill(be, n, k) -> None:
+    """Row counts far above what one CTA's shared-memory ring holds, so every
+    consumer warp cycles its stages many times (the lm-head shape first)."""
+    rng = np.random.default_rng(k)
+    raw = quantize_q8_0(rng.standard_normal((n, k)).astype(np.float32) * 0.02)
+    deq = dequant_q8_0(raw, n, k)
+    w = Q8Weight.from_gguf(raw, n, k, "cuda")
+    x = rng.standard_normal(k).astype(np.float32)
+    xd = _t(x)
+    for _ in range(3):
+        y = be.linear(xd, w).cpu().numpy()
+        assert np.all(np.abs(y - deq @ x) <= _gemv_bound(x, deq))
 
 
 @pytest.mark.parametrize("nv", [2, 4, 8])
@@ -135,9 +152,11 @@ def test_gdn_decode_config2_256_steps(be, batch) -> None:
         g = -ops.softplus(rng.standard_normal((batch, H), dtype=np.float32))
         qb, kb, vb = (torch.from_numpy(a).to(torch.bfloat16) for a in (q, k, v))
         out = torch.empty(batch, H, D, device="cuda")
+        # device copies held in locals: they must outlive the asynchronous kernel
+        qd, kd, vd, gd, bd = qb.cuda(), kb.cuda(), vb.cuda(), _t(g), _t(beta)
         N.call(
-            "bt_gdn_decode", qb.cuda().data_ptr(), kb.cuda().data_ptr(), vb.cuda().data_ptr(), N.BT_BF16,
-            _t(g).data_ptr(), _t(beta).data_ptr(), state.data_ptr(), out.data_ptr(), batch, H, H, D,
+            "bt_gdn_decode", qd.data_ptr(), kd.data_ptr(), vd.data_ptr(), N.BT_BF16,
+            gd.data_ptr(), bd.data_ptr(), state.data_ptr(), out.data_ptr(), batch, H, H, D,
             1.0, 1e-6, 0,
         )
         o = out.cpu().numpy()
@@ -168,10 +187,10 @@ def test_attention_config3_bf16(be, batch, ctx, splits) -> None:
     out = torch.empty(batch, 8, 256, device="cuda")
     ws = torch.zeros(int(N.load().bt_attention_workspace_bytes(batch, 2, 8, 256, splits)), dtype=torch.uint8,
                      device="cuda")
-    kc, vc = k.cuda(), v.cuda()
+    kc, vc, qd, ld = k.cuda(), v.cuda(), _t(q), _t(lens)  # alive until the kernels ran
     for _ in range(2):  # second call checks the workspace is re-armed
         N.call(
-            "bt_attention_decode", _t(q).data_ptr(), kc.data_ptr(), vc.data_ptr(), N.BT_BF16, _t(lens).data_ptr(),
+            "bt_attention_decode", qd.data_ptr(), kc.data_ptr(), vc.data_ptr(), N.BT_BF16, ld.data_ptr(),
             out.data_ptr(), batch, 8, 2, 256, ctx, 1.0 / 16, splits, ws.data_ptr(), 0,
         )
         o = out.cpu().numpy()
