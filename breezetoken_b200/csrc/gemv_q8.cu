@@ -379,13 +379,17 @@ int gemv_q8_plan(GemvQ8Params& p, int sm_count, GemvQ8Launch& L) {
   const int64_t n_units = (p.n_rows + 3) / 4;
   const int grid = static_cast<int>(std::min<int64_t>(sm_count, n_units));
   const int64_t rows_per_cta = ((n_units + grid - 1) / grid) * 4;
-  int gr = 1;
-  if (p.epilogue == EPI_SILU_PAIR || (p.n_vec <= 2 && rows_per_cta >= 32)) gr = 4;
-  if (p.n_vec > 2 && p.epilogue == EPI_SILU_PAIR)
-    return fail(BT_ERR_UNSUPPORTED, "SiLU-pair epilogue serves at most 2 vectors");
-  p.group_rows = gr;
   const int64_t x_bytes = ((static_cast<int64_t>(p.n_vec) * p.xs_stride * 4 + 127) / 128) * 128;
   const int64_t ring_budget = kSmemBudget - x_bytes;
+  // 4-row groups reuse each activation chunk across rows; they need one
+  // 4-row stage per consumer warp in the ring.
+  const bool fits4 = kConsumerWarps * 4LL * p.row_bytes <= ring_budget;
+  int gr = 1;
+  if (p.epilogue == EPI_SILU_PAIR || (p.n_vec <= 2 && rows_per_cta >= 32 && fits4)) gr = 4;
+  if (p.epilogue == EPI_SILU_PAIR && (p.n_vec > 2 || !fits4))
+    return fail(BT_ERR_UNSUPPORTED, "SiLU-pair epilogue serves at most 2 vectors and K <= %lld",
+                static_cast<long long>(ring_budget / (4 * kConsumerWarps)));
+  p.group_rows = gr;
   // stage = gr * f rows, ~8 KB at most, and no more rows than keep all 8
   // consumer warps busy
   const int64_t f_rows = std::max<int64_t>(1, rows_per_cta / (kConsumerWarps * gr));

@@ -1,0 +1,138 @@
+"""Kernel microbenchmarks through the C ABI (CUDA-event timing).
+
+    python -m breezetoken_b200.kernel_bench gemv --n 151936 --k 1024
+    python -m breezetoken_b200.kernel_bench gdn --batch 64 --steps 256
+    python -m breezetoken_b200.kernel_bench attn --batch 64 --ctx 32768
+
+Each prints one JSON line: average launch time and achieved HBM GB/s from
+the algorithmic bytes of one launch (weights / state / KV read once).
+``gdn`` and ``attn`` are the stand-alone decode ops of BASELINE configs 2
+and 3 with their synthetic inputs (seeds 1 and 2).
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+
+import numpy as np
+import torch
+
+from breezetoken_b200 import _native as N
+from breezetoken_b200.backends import Q8Weight
+from breezetoken_b200.quant import quantize_q8_0
+
+
+def _time(fn, iters: int, stream: torch.cuda.Stream) -> float:
+    with torch.cuda.stream(stream):
+        for _ in range(3):
+            fn()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(iters):
+            fn()
+        e1.record(stream)
+    e1.synchronize()
+    return e0.elapsed_time(e1) / 1e3 / iters
+
+
+def bench_gemv(n: int, k: int, iters: int) -> dict:
+    rng = np.random.default_rng(0)
+    # random bytes are a valid Q8_0 stream for timing; quantise a small tile and tile it
+    tile = quantize_q8_0(rng.standard_normal((256, k)).astype(np.float32) * 0.02)
+    raw = np.tile(tile, ((n + 255) // 256, 1))[:n]
+    w = Q8Weight.from_gguf(raw, n, k, "cuda")
+    x = torch.randn(k, device="cuda")
+    y = torch.empty(n, device="cuda")
+    s = torch.cuda.Stream()
+    lib = N.load()
+
+    def run():
+        N.check(lib.bt_linear_q8(w.data.data_ptr(), x.data_ptr(), y.data_ptr(), n, k, 1, s.cuda_stream), "gemv")
+
+    sec = _time(run, iters, s)
+    nbytes = w.data.numel() + 4 * (k + n)
+    return {"kernel": "gemv_q8", "n": n, "k": k, "us": sec * 1e6, "bytes": nbytes, "gbs": nbytes / sec / 1e9}
+
+
+def bench_gdn(batch: int, steps: int, heads: int = 16, dim: int = 128) -> dict:
+    rng = np.random.default_rng(1)
+    q = torch.from_numpy(rng.standard_normal((batch, heads, dim), dtype=np.float32)).to("cuda", torch.bfloat16)
+    k = torch.from_numpy(rng.standard_normal((batch, heads, dim), dtype=np.float32)).to("cuda", torch.bfloat16)
+    v = torch.from_numpy(rng.standard_normal((batch, heads, dim), dtype=np.float32)).to("cuda", torch.bfloat16)
+    g = -torch.nn.functional.softplus(torch.from_numpy(rng.standard_normal((batch, heads), dtype=np.float32))).cuda()
+    beta = torch.from_numpy(rng.standard_normal((batch, heads), dtype=np.float32)).cuda()
+    state = torch.zeros(batch, heads, dim, dim, device="cuda")
+    out = torch.empty(batch, heads, dim, device="cuda")
+    s = torch.cuda.Stream()
+    lib = N.load()
+
+    def run():
+        N.check(
+            lib.bt_gdn_decode(q.data_ptr(), k.data_ptr(), v.data_ptr(), N.BT_BF16, g.data_ptr(), beta.data_ptr(),
+                              state.data_ptr(), out.data_ptr(), batch, heads, heads, dim, 1.0, 1e-6, s.cuda_stream),
+            "gdn",
+        )
+
+    sec = _time(run, steps, s)
+    nbytes = batch * (2 * heads * dim * dim * 4 + 3 * heads * dim * 2 + 2 * heads * 4 + heads * dim * 4)
+    return {"kernel": "gdn_decode", "batch": batch, "steps": steps, "us_per_step": sec * 1e6, "bytes": nbytes,
+            "gbs": nbytes / sec / 1e9}
+
+
+def bench_attn(batch: int, ctx: int, splits: int, iters: int) -> dict:
+    heads, kv_heads, dim = 8, 2, 256
+    gen = torch.Generator(device="cuda").manual_seed(2)
+    q = torch.randn(batch, heads, dim, device="cuda", generator=gen)
+    kc = torch.randn(batch, ctx, kv_heads, dim, device="cuda", generator=gen).to(torch.bfloat16)
+    vc = torch.randn(batch, ctx, kv_heads, dim, device="cuda", generator=gen).to(torch.bfloat16)
+    lens = torch.full((batch,), ctx, dtype=torch.int32, device="cuda")
+    out = torch.empty(batch, heads, dim, device="cuda")
+    lib = N.load()
+    if splits <= 0:
+        splits = max(1, min(256, (2 * N.load().bt_sm_count() + batch * kv_heads - 1) // (batch * kv_heads), ctx // 256))
+    ws = torch.zeros(int(lib.bt_attention_workspace_bytes(batch, kv_heads, heads, dim, splits)), dtype=torch.uint8,
+                     device="cuda")
+    s = torch.cuda.Stream()
+
+    def run():
+        N.check(
+            lib.bt_attention_decode(q.data_ptr(), kc.data_ptr(), vc.data_ptr(), N.BT_BF16, lens.data_ptr(),
+                                    out.data_ptr(), batch, heads, kv_heads, dim, ctx, 1.0 / 16, splits,
+                                    ws.data_ptr(), s.cuda_stream),
+            "attn",
+        )
+
+    sec = _time(run, iters, s)
+    nbytes = batch * ctx * kv_heads * dim * 2 * 2 + 2 * batch * heads * dim * 4
+    return {"kernel": "attn_decode", "batch": batch, "ctx": ctx, "splits": splits, "us": sec * 1e6, "bytes": nbytes,
+            "gbs": nbytes / sec / 1e9}
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser(description=__doc__)
+    sub = ap.add_subparsers(dest="cmd", required=True)
+    a = sub.add_parser("gemv")
+    a.add_argument("--n", type=int, default=151936)
+    a.add_argument("--k", type=int, default=1024)
+    a.add_argument("--iters", type=int, default=20)
+    b = sub.add_parser("gdn")
+    b.add_argument("--batch", type=int, default=1)
+    b.add_argument("--steps", type=int, default=256)
+    c = sub.add_parser("attn")
+    c.add_argument("--batch", type=int, default=1)
+    c.add_argument("--ctx", type=int, default=8192)
+    c.add_argument("--splits", type=int, default=0)
+    c.add_argument("--iters", type=int, default=20)
+    args = ap.parse_args()
+    if args.cmd == "gemv":
+        r = bench_gemv(args.n, args.k, args.iters)
+    elif args.cmd == "gdn":
+        r = bench_gdn(args.batch, args.steps)
+    else:
+        r = bench_attn(args.batch, args.ctx, args.splits, args.iters)
+    print(json.dumps(r), flush=True)
+
+
+if __name__ == "__main__":
+    main()
