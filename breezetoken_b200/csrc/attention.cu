@@ -29,6 +29,9 @@ namespace bt {
 namespace {
 
 constexpr int kAttnWarps = 4;
+// A split takes part only with at least this many positions: short contexts
+// run in one CTA per group and skip the cross-CTA merge.
+constexpr int kMinSplitLen = 64;
 constexpr int kAttnThreads = kAttnWarps * 32;
 constexpr float kLog2e = 1.4426950408889634f;
 
@@ -102,10 +105,14 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const __grid_
 
   int L = p.model ? p.pos[b] + 1 : p.lens[b];
   if (L < 0 || L > p.cap) {
-    if (threadIdx.x == 0) report_status(p.status, BT_ERR_INVALID, SITE_ATTN_LENGTH, L, p.cap, b);
+    if (threadIdx.x == 0 && split == 0) report_status(p.status, BT_ERR_INVALID, SITE_ATTN_LENGTH, L, p.cap, b);
     L = L < 0 ? 0 : p.cap;
   }
-  const int chunk = (L + p.splits - 1) / p.splits;
+  // Only as many splits as keep >= kMinSplitLen positions each take part; the
+  // others leave at once and are not counted by the merge ticket.
+  const int splits = max(1, min(p.splits, (L + kMinSplitLen - 1) / kMinSplitLen));
+  if (split >= splits) return;
+  const int chunk = (L + splits - 1) / splits;
   const int t0 = min(L, split * chunk), t1 = min(L, t0 + chunk);
 
   if (!p.model) {
@@ -245,6 +252,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const __grid_
     for (int i = 0; i < DPL; ++i) wacc[warp][h][lane * DPL + i] = acc[h][i];
   __syncthreads();
 
+  // records of this (sequence, group): split s, head h at rec0 + s*GS + h
   const int64_t rec0 = ((static_cast<int64_t>(b) * p.kv_heads + g) * p.splits) * GS;
   for (int e = threadIdx.x; e < GS * DIM; e += kAttnThreads) {
     const int h = e / DIM, d = e % DIM;
@@ -260,7 +268,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const __grid_
         O = fmaf(wacc[w][h][d], f, O);
       }
     }
-    if (p.splits == 1) {
+    if (splits == 1) {
       float o = Ls > 0.f ? O / Ls : 0.f;
       if (p.model)
         o *= sigmoid_f(p.gate[static_cast<int64_t>(b) * p.q_bs + static_cast<int64_t>(g * GS + h) * p.q_hs + d]);
@@ -274,31 +282,54 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const __grid_
       }
     }
   }
-  if (p.splits == 1) return;
+  if (splits == 1) return;
 
   // ---------------- last CTA of the group merges the splits
   __threadfence();
   __syncthreads();
   if (threadIdx.x == 0) s_ticket = atomicAdd(p.counters + static_cast<int64_t>(b) * p.kv_heads + g, 1u);
   __syncthreads();
-  if (s_ticket != static_cast<uint32_t>(p.splits - 1)) return;
+  if (s_ticket != static_cast<uint32_t>(splits - 1)) return;
   __threadfence();
-  for (int e = threadIdx.x; e < GS * DIM; e += kAttnThreads) {
-    const int h = e / DIM, d = e % DIM;
+  // per-head split weights 2^(m_s - M) and total sum, one warp per head
+  // (the warp-partial buffer is free again and holds GS * splits weights)
+  float* fw = &wacc[0][0][0];
+  __shared__ float s_sum[GS];
+  for (int h = warp; h < GS; h += kAttnWarps) {
     float M = -INFINITY;
-    for (int s = 0; s < p.splits; ++s)
+    for (int s = lane; s < splits; s += 32)
       M = fmaxf(M, __ldcg(p.part + (rec0 + static_cast<int64_t>(s) * GS + h) * (DIM + 2) + DIM));
-    float Ls = 0.f, O = 0.f;
-    for (int s = 0; s < p.splits; ++s) {
+    M = warp_max(M);
+    float Ls = 0.f;
+    for (int s = lane; s < splits; s += 32) {
       const float* rec = p.part + (rec0 + static_cast<int64_t>(s) * GS + h) * (DIM + 2);
       const float ms = __ldcg(rec + DIM);
-      if (ms != -INFINITY) {
-        const float f = exp2f(ms - M);
-        Ls = fmaf(__ldcg(rec + DIM + 1), f, Ls);
-        O = fmaf(__ldcg(rec + d), f, O);
-      }
+      const float f = ms == -INFINITY ? 0.f : exp2f(ms - M);
+      fw[h * splits + s] = f;
+      Ls = fmaf(__ldcg(rec + DIM + 1), f, Ls);
     }
-    float o = Ls > 0.f ? O / Ls : 0.f;
+    Ls = warp_sum(Ls);
+    if (lane == 0) s_sum[h] = Ls;
+  }
+  __syncthreads();
+  const int64_t rstride = static_cast<int64_t>(GS) * (DIM + 2);
+  for (int e = threadIdx.x; e < GS * DIM; e += kAttnThreads) {
+    const int h = e / DIM, d = e % DIM;
+    const float* base = p.part + (rec0 + h) * (DIM + 2) + d;
+    const float* f = fw + h * splits;
+    float O0 = 0.f, O1 = 0.f, O2 = 0.f, O3 = 0.f;
+    int s = 0;
+    for (; s + 4 <= splits; s += 4) {
+      const float a0 = __ldcg(base + s * rstride), a1 = __ldcg(base + (s + 1) * rstride);
+      const float a2 = __ldcg(base + (s + 2) * rstride), a3 = __ldcg(base + (s + 3) * rstride);
+      O0 = fmaf(a0, f[s], O0);
+      O1 = fmaf(a1, f[s + 1], O1);
+      O2 = fmaf(a2, f[s + 2], O2);
+      O3 = fmaf(a3, f[s + 3], O3);
+    }
+    for (; s < splits; ++s) O0 = fmaf(__ldcg(base + s * rstride), f[s], O0);
+    const float Ls = s_sum[h];
+    float o = Ls > 0.f ? ((O0 + O1) + (O2 + O3)) / Ls : 0.f;
     if (p.model)
       o *= sigmoid_f(p.gate[static_cast<int64_t>(b) * p.q_bs + static_cast<int64_t>(g * GS + h) * p.q_hs + d]);
     p.out[static_cast<int64_t>(b) * p.out_bs + static_cast<int64_t>(g * GS + h) * DIM + d] = o;
@@ -339,7 +370,8 @@ int attention_launch(const AttnParams& p, cudaStream_t stream, bool pdl) {
   if (p.batch <= 0 || p.kv_heads <= 0 || p.heads <= 0 || p.heads % p.kv_heads != 0)
     return fail(BT_ERR_INVALID, "attention: heads (%d) must be a positive multiple of kv_heads (%d)", p.heads,
                 p.kv_heads);
-  if (p.splits < 1 || p.splits > 1024) return fail(BT_ERR_INVALID, "attention: splits must be in [1, 1024]");
+  if (p.splits < 1 || p.splits > 4 * p.dim)
+    return fail(BT_ERR_INVALID, "attention: splits must be in [1, %d]", 4 * p.dim);
   if (p.model && p.kv_dtype != BT_F32) return fail(BT_ERR_UNSUPPORTED, "model-mode attention keeps an f32 cache");
   if ((reinterpret_cast<uintptr_t>(p.k) | reinterpret_cast<uintptr_t>(p.v)) & 15)
     return fail(BT_ERR_INVALID, "attention: K/V must be 16-byte aligned (vector loads)");

@@ -10,12 +10,12 @@
 // with value head h reading key head h % heads_k.
 //
 // Layout: state (batch, heads_v, dim_k, dim_v) f32, row d = key index.
-// One CTA owns 32 value columns of one head: warp w holds rows
-// [32w, 32w+32) of those columns in registers (32 floats per thread), so the
-// state is read and written exactly once per step with 128-B coalesced
-// accesses; the two column sums (S^T kn and S^T qn) reduce across warps in
-// shared memory.  Before griddepcontrol.wait the CTA only issues L2
-// prefetches of its state slice.
+// One CTA of 256 threads owns 16 value columns of one head: thread t holds
+// column t % 16 of the rows [R*(t/16), R*(t/16) + R) (R = dim/16) in
+// registers, so the state is read and written exactly once per step
+// (64-byte half-warp segments); the column sums S^T kn and S^T qn reduce
+// across the 16 row groups in shared memory.  Before griddepcontrol.wait the
+// CTA only issues L2 prefetches of its state slice.
 #include "errors.h"
 #include "gdn.cuh"
 
@@ -23,7 +23,9 @@ namespace bt {
 
 namespace {
 
-constexpr int kCols = 32;
+constexpr int kCols = 16;
+constexpr int kRowGroups = 16;
+constexpr int kThreads = kCols * kRowGroups;
 
 template <typename T>
 __device__ __forceinline__ float load_elem(const void* p, int64_t i);
@@ -36,91 +38,105 @@ __device__ __forceinline__ float load_elem<__nv_bfloat16>(const void* p, int64_t
   return __bfloat162float(static_cast<const __nv_bfloat16*>(p)[i]);
 }
 
-template <typename T>
-__global__ void __launch_bounds__(256) gdn_decode_kernel(const __grid_constant__ GdnParams p) {
-  __shared__ float red[8][kCols];
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int col_tiles = p.dim / kCols;
+template <typename T, int R>
+__global__ void __launch_bounds__(kThreads) gdn_decode_kernel(const __grid_constant__ GdnParams p) {
+  constexpr int DIM = R * kRowGroups;
+  __shared__ float red[kRowGroups][kCols];
+  __shared__ float sq[DIM], sk[DIM];
+  const int tid = threadIdx.x, lane = tid & 31;
+  const int col_l = tid % kCols, rg = tid / kCols;
+  const int col_tiles = DIM / kCols;
   const int tile = blockIdx.x % col_tiles;
   const int hv = (blockIdx.x / col_tiles) % p.heads_v;
   const int b = blockIdx.x / (col_tiles * p.heads_v);
   const int hk = hv % p.heads_k;
-  const int dim = p.dim;
-  const int col = tile * kCols + lane;
+  const int col = tile * kCols + col_l;
+  const int r0 = rg * R;
 
-  float* S = p.state + ((static_cast<int64_t>(b) * p.heads_v + hv) * dim) * dim;
-  const int d0 = warp * 32;
-  // L2 prefetch of the warp's 32 state rows (one 128-B line each) of this
-  // column tile: a cache hint only, so it is safe before the dependency wait.
-  asm volatile("prefetch.global.L2::evict_last [%0];" ::"l"(S + static_cast<int64_t>(d0 + lane) * dim +
-                                                            tile * kCols));
+  float* S = p.state + ((static_cast<int64_t>(b) * p.heads_v + hv) * DIM) * DIM;
+  // L2 prefetch of the tile's rows (64 B each): a cache hint only, safe
+  // before the dependency wait.
+  if (tid < DIM) asm volatile("prefetch.global.L2::evict_last [%0];" ::"l"(S + static_cast<int64_t>(tid) * DIM + tile * kCols));
   pdl_launch_dependents();
   pdl_wait();
 
-  // q/k of key head hk: every warp computes both norms (4-8 elements per lane).
-  const int64_t qoff = static_cast<int64_t>(b) * p.q_bs + static_cast<int64_t>(hk) * dim;
-  const int64_t koff = static_cast<int64_t>(b) * p.k_bs + static_cast<int64_t>(hk) * dim;
-  float qss = 0.f, kss = 0.f;
-  for (int i = lane; i < dim; i += 32) {
-    const float qv = load_elem<T>(p.q, qoff + i), kv = load_elem<T>(p.k, koff + i);
-    qss = fmaf(qv, qv, qss);
-    kss = fmaf(kv, kv, kss);
-  }
-  qss = warp_sum(qss);
-  kss = warp_sum(kss);
-  const float qr = 1.0f / sqrtf(qss + p.eps), kr = 1.0f / sqrtf(kss + p.eps);
-  // lane l of warp w holds qn/kn[d0 + l]; broadcast with shuffles below.
-  const float qn_l = __fmul_rn(__fmul_rn(load_elem<T>(p.q, qoff + d0 + lane), qr), p.scale);
-  const float kn_l = __fmul_rn(load_elem<T>(p.k, koff + d0 + lane), kr);
-
-  const float gval = p.g[static_cast<int64_t>(b) * p.g_bs + hv];
-  const float bval = p.beta[static_cast<int64_t>(b) * p.beta_bs + hv];
-  const float decay = expf(gval);
-  const float bsig = sigmoid_f(bval);
-
-  float s[32];
+  // normalised q/k of key head hk: warp 0 does q, warp 1 does k
+  const int warp = tid >> 5;
+  if (warp < 2) {
+    const void* src = warp == 0 ? p.q : p.k;
+    const int64_t off = static_cast<int64_t>(b) * (warp == 0 ? p.q_bs : p.k_bs) + static_cast<int64_t>(hk) * DIM;
+    float vals[DIM / 32];
+    float ss = 0.f;
 #pragma unroll
-  for (int i = 0; i < 32; ++i) s[i] = __fmul_rn(S[static_cast<int64_t>(d0 + i) * dim + col], decay);
+    for (int i = 0; i < DIM / 32; ++i) {
+      vals[i] = load_elem<T>(src, off + lane + 32 * i);
+      ss = fmaf(vals[i], vals[i], ss);
+    }
+    ss = warp_sum(ss);
+    const float r = 1.0f / sqrtf(ss + p.eps);
+    float* dst = warp == 0 ? sq : sk;
+#pragma unroll
+    for (int i = 0; i < DIM / 32; ++i)
+      dst[lane + 32 * i] = warp == 0 ? __fmul_rn(__fmul_rn(vals[i], r), p.scale) : __fmul_rn(vals[i], r);
+  }
+
+  const float decay = expf(p.g[static_cast<int64_t>(b) * p.g_bs + hv]);
+  const float bsig = sigmoid_f(p.beta[static_cast<int64_t>(b) * p.beta_bs + hv]);
+  float s[R];
+#pragma unroll
+  for (int i = 0; i < R; ++i) s[i] = __fmul_rn(S[static_cast<int64_t>(r0 + i) * DIM + col], decay);
+  __syncthreads();
 
   float rec = 0.f;
 #pragma unroll
-  for (int i = 0; i < 32; ++i) rec = fmaf(s[i], __shfl_sync(0xffffffffu, kn_l, i), rec);
-  red[warp][lane] = rec;
+  for (int i = 0; i < R; ++i) rec = fmaf(s[i], sk[r0 + i], rec);
+  red[rg][col_l] = rec;
   __syncthreads();
   float recalled = 0.f;
-  for (int w = 0; w < dim / 32; ++w) recalled += red[w][lane];
-  const float vv = load_elem<T>(p.v, static_cast<int64_t>(b) * p.v_bs + static_cast<int64_t>(hv) * dim + col);
+#pragma unroll
+  for (int w = 0; w < kRowGroups; ++w) recalled += red[w][col_l];
+  const float vv = load_elem<T>(p.v, static_cast<int64_t>(b) * p.v_bs + static_cast<int64_t>(hv) * DIM + col);
   const float delta = __fmul_rn(vv - recalled, bsig);
 
   float o = 0.f;
 #pragma unroll
-  for (int i = 0; i < 32; ++i) {
-    s[i] = __fadd_rn(s[i], __fmul_rn(__shfl_sync(0xffffffffu, kn_l, i), delta));
-    S[static_cast<int64_t>(d0 + i) * dim + col] = s[i];
-    o = fmaf(s[i], __shfl_sync(0xffffffffu, qn_l, i), o);
+  for (int i = 0; i < R; ++i) {
+    s[i] = __fadd_rn(s[i], __fmul_rn(sk[r0 + i], delta));
+    S[static_cast<int64_t>(r0 + i) * DIM + col] = s[i];
+    o = fmaf(s[i], sq[r0 + i], o);
   }
   __syncthreads();
-  red[warp][lane] = o;
+  red[rg][col_l] = o;
   __syncthreads();
-  if (warp == 0) {
+  if (tid < kCols) {
     float t = 0.f;
-    for (int w = 0; w < dim / 32; ++w) t += red[w][lane];
-    p.out[static_cast<int64_t>(b) * p.out_bs + static_cast<int64_t>(hv) * dim + col] = t;
+#pragma unroll
+    for (int w = 0; w < kRowGroups; ++w) t += red[w][tid];
+    p.out[static_cast<int64_t>(b) * p.out_bs + static_cast<int64_t>(hv) * DIM + tile * kCols + tid] = t;
+  }
+}
+
+template <typename T>
+cudaError_t launch_dim(const GdnParams& p, cudaLaunchConfig_t& cfg) {
+  switch (p.dim) {
+    case 64: return cudaLaunchKernelEx(&cfg, gdn_decode_kernel<T, 4>, p);
+    case 128: return cudaLaunchKernelEx(&cfg, gdn_decode_kernel<T, 8>, p);
+    default: return cudaLaunchKernelEx(&cfg, gdn_decode_kernel<T, 16>, p);
   }
 }
 
 }  // namespace
 
 int gdn_decode_launch(const GdnParams& p, cudaStream_t stream, bool pdl) {
-  if (p.dim % 32 != 0 || p.dim < 32 || p.dim > 256)
-    return fail(BT_ERR_UNSUPPORTED, "gdn_decode serves dim in {32..256} step 32, got %d", p.dim);
+  if (p.dim != 64 && p.dim != 128 && p.dim != 256)
+    return fail(BT_ERR_UNSUPPORTED, "gdn_decode serves dim 64, 128 or 256, got %d", p.dim);
   if (p.heads_k <= 0 || p.heads_v <= 0 || p.heads_v % p.heads_k != 0)
     return fail(BT_ERR_INVALID, "gdn_decode: value heads (%d) must be a positive multiple of key heads (%d)",
                 p.heads_v, p.heads_k);
   if (p.batch <= 0) return fail(BT_ERR_INVALID, "gdn_decode: batch must be positive");
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(static_cast<unsigned>(p.batch) * p.heads_v * (p.dim / kCols));
-  cfg.blockDim = dim3(p.dim);
+  cfg.blockDim = dim3(kThreads);
   cfg.dynamicSmemBytes = 0;
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
@@ -128,8 +144,7 @@ int gdn_decode_launch(const GdnParams& p, cudaStream_t stream, bool pdl) {
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 1 : 0;
-  cudaError_t e = p.in_dtype == BT_BF16 ? cudaLaunchKernelEx(&cfg, gdn_decode_kernel<__nv_bfloat16>, p)
-                                        : cudaLaunchKernelEx(&cfg, gdn_decode_kernel<float>, p);
+  const cudaError_t e = p.in_dtype == BT_BF16 ? launch_dim<__nv_bfloat16>(p, cfg) : launch_dim<float>(p, cfg);
   if (e != cudaSuccess) return fail_cuda(e, "gdn_decode launch");
   return BT_OK;
 }

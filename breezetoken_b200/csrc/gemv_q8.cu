@@ -11,20 +11,20 @@ namespace {
 constexpr int kSmemBudget = 104 * 1024;  // two CTAs (this kernel + the PDL successor) per SM
 
 // ------------------------------------------------------------------ prologue
+// Phase 1: the f32 activation vector(s) in natural layout (xf[v*K + k]).
 template <int NV>
-__device__ void gemv_prologue(const GemvQ8Params& p, float* xs, float* scratch) {
+__device__ void gemv_build_x(const GemvQ8Params& p, float* xs, float* scratch) {
   const int tid = threadIdx.x;
   const int K = p.k;
   const int64_t xbs = p.x_bs ? p.x_bs : K, x2bs = p.x2_bs ? p.x2_bs : K;
   if (p.prologue == PRO_LOAD) {
     for (int v = 0; v < NV && v < p.n_vec; ++v)
-      for (int k = tid; k < K; k += kConsumerThreads)
-        xs[v * p.xs_stride + x_perm(k)] = p.x[v * xbs + k];
+      for (int k = tid; k < K; k += kConsumerThreads) xs[v * K + k] = p.x[v * xbs + k];
     return;
   }
   if (p.prologue == PRO_RESID_NORM || p.prologue == PRO_EMBED_NORM) {
     for (int v = 0; v < NV && v < p.n_vec; ++v) {
-      float* xv = xs + v * p.xs_stride;
+      float* xv = xs + v * K;
       const uint8_t* erow = nullptr;
       if (p.prologue == PRO_EMBED_NORM) {
         int64_t tok = p.tokens[v];
@@ -44,16 +44,13 @@ __device__ void gemv_prologue(const GemvQ8Params& p, float* xs, float* scratch) 
           const float q = static_cast<float>(static_cast<int8_t>(erow[p.sb + k]));
           h = q * d;
         }
-        xv[x_perm(k)] = h;
+        xv[k] = h;
         ss = fmaf(h, h, ss);
         if (blockIdx.x == 0) p.h_out[static_cast<int64_t>(v) * K + k] = h;
       }
       const float total = group_sum<1>(ss, scratch, kConsumerWarps, kConsumerThreads);
       const float r = 1.0f / sqrtf(total / static_cast<float>(K) + p.eps);
-      for (int k = tid; k < K; k += kConsumerThreads) {
-        const int i = x_perm(k);
-        xv[i] = __fmul_rn(__fmul_rn(xv[i], r), p.norm_w[k]);
-      }
+      for (int k = tid; k < K; k += kConsumerThreads) xv[k] = __fmul_rn(__fmul_rn(xv[k], r), p.norm_w[k]);
     }
     return;
   }
@@ -74,9 +71,36 @@ __device__ void gemv_prologue(const GemvQ8Params& p, float* xs, float* scratch) 
       for (int i = lane; i < G; i += 32) {
         const int k = g * G + i;
         const float normed = __fmul_rn(__fmul_rn(o[k], r), p.norm_w[i]);
-        xs[v * p.xs_stride + x_perm(k)] = __fmul_rn(normed, z[k]);
+        xs[v * K + k] = __fmul_rn(normed, z[k]);
       }
     }
+  }
+}
+
+// Phase 2: per 32-element block, scale sx and three int8 digits of the
+// fixed-point value (see gemv_q8.cuh); one warp per block.
+template <int NV>
+__device__ void gemv_encode_x(const GemvQ8Params& p, const float* xf, uint8_t* xd, float* sx) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int K = p.k, nb = K / 32, J = (K + 511) / 512;
+  for (int item = warp; item < NV * nb; item += kConsumerWarps) {
+    const int v = item / nb, b = item % nb;
+    if (v >= p.n_vec) break;
+    const float x = xf[v * K + 32 * b + lane];
+    const float amax = warp_max(fabsf(x));
+    const float inv = amax > 0.f ? static_cast<float>(kXMax) / amax : 0.f;
+    int X = __float2int_rn(x * inv);
+    X = X > kXMax ? kXMax : (X < -kXMax ? -kXMax : X);
+    const int d0 = ((X + 128) & 255) - 128;
+    const int x1 = (X - d0) >> 8;
+    const int d1 = ((x1 + 128) & 255) - 128;
+    const int d2 = (x1 - d1) >> 8;
+    const int c = 2 * b + (lane >> 4), e = lane & 15;
+    uint8_t* base = xd + static_cast<int64_t>(v) * J * 1536 + ((c >> 5) * 3 * 32 + (c & 31)) * 16 + e;
+    base[0] = static_cast<uint8_t>(d2);
+    base[32 * 16] = static_cast<uint8_t>(d1);
+    base[64 * 16] = static_cast<uint8_t>(d0);
+    if (lane == 0) sx[v * nb + b] = amax / static_cast<float>(kXMax);
   }
 }
 
@@ -126,8 +150,11 @@ __global__ void __launch_bounds__(kGemvThreads, 2)
   uint64_t* empty = full + kMaxStages;
   float* scratch = reinterpret_cast<float*>(empty + kMaxStages);
   unsigned long long* amax = reinterpret_cast<unsigned long long*>(scratch + 64);
-  float* xs = reinterpret_cast<float*>(smem + GemvSmem::kHeader);
-  uint8_t* ring = smem + GemvSmem::kHeader + ((NV * p.xs_stride * 4 + 127) & ~127);
+  const XLayout xl = gemv_x_layout(p.k, NV);
+  float* xf = reinterpret_cast<float*>(smem + GemvSmem::kHeader + xl.xf);
+  uint8_t* xd = smem + GemvSmem::kHeader + xl.xd;
+  float* sx = reinterpret_cast<float*>(smem + GemvSmem::kHeader + xl.sx);
+  uint8_t* ring = smem + GemvSmem::kHeader + xl.total;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t n_units = (p.n_rows + 3) >> 2;
@@ -191,7 +218,9 @@ __global__ void __launch_bounds__(kGemvThreads, 2)
 
   // ---------------- consumers
   pdl_wait();
-  gemv_prologue<NV>(p, xs, scratch);
+  gemv_build_x<NV>(p, xf, scratch);
+  named_sync(1, kConsumerThreads);
+  gemv_encode_x<NV>(p, xf, xd, sx);
   named_sync(1, kConsumerThreads);
 
   unsigned long long best[NV];
@@ -200,8 +229,8 @@ __global__ void __launch_bounds__(kGemvThreads, 2)
 
   const int nchunks = p.k >> 4;
   const int J = (nchunks + 31) >> 5;
-  const float4* xs4 = reinterpret_cast<const float4*>(xs);
-  const int xs4_stride = p.xs_stride >> 2;
+  const int nb = p.k >> 5;
+  const uint4* xd4 = reinterpret_cast<const uint4*>(xd);
 
   for (int it = warp, i = 0; it < n_iters; it += kConsumerWarps, ++i) {
     const int s = warp * SPW + i % SPW;
@@ -223,11 +252,14 @@ __global__ void __launch_bounds__(kGemvThreads, 2)
       for (int j = 0; j < J; ++j) {
         const int c = lane + (j << 5);
         if (c < nchunks) {
-          float4 xv[NV][4];
+          uint4 dg[NV][3];
+          float xsc[NV];
 #pragma unroll
-          for (int v = 0; v < NV; ++v)
+          for (int v = 0; v < NV; ++v) {
 #pragma unroll
-            for (int m = 0; m < 4; ++m) xv[v][m] = xs4[v * xs4_stride + (j * 4 + m) * 32 + lane];
+            for (int t = 0; t < 3; ++t) dg[v][t] = xd4[(v * J + j) * 96 + t * 32 + lane];
+            xsc[v] = sx[v * nb + (c >> 1)];
+          }
 #pragma unroll
           for (int r = 0; r < GR; ++r) {
             if (g + r < nr) {
@@ -236,7 +268,7 @@ __global__ void __launch_bounds__(kGemvThreads, 2)
               const uint4 q = *reinterpret_cast<const uint4*>(row + p.sb + (c << 4));
 #pragma unroll
               for (int v = 0; v < NV; ++v)
-                acc[r][v] = fmaf(d, dot16(q, xv[v][0], xv[v][1], xv[v][2], xv[v][3]), acc[r][v]);
+                acc[r][v] = fmaf(d * xsc[v], dot16_digits(q, dg[v][0], dg[v][1], dg[v][2]), acc[r][v]);
             }
           }
         }
@@ -375,11 +407,10 @@ int gemv_q8_plan(GemvQ8Params& p, int sm_count, GemvQ8Launch& L) {
     return fail(BT_ERR_INVALID, "argmax epilogue needs its workspace");
   p.sb = static_cast<int32_t>(bt_q8_row_bytes(p.k) - p.k);
   p.row_bytes = static_cast<int32_t>(bt_q8_row_bytes(p.k));
-  p.xs_stride = static_cast<int32_t>(gemv_x_stride(p.k));
   const int64_t n_units = (p.n_rows + 3) / 4;
   const int grid = static_cast<int>(std::min<int64_t>(sm_count, n_units));
   const int64_t rows_per_cta = ((n_units + grid - 1) / grid) * 4;
-  const int64_t x_bytes = ((static_cast<int64_t>(p.n_vec) * p.xs_stride * 4 + 127) / 128) * 128;
+  const int64_t x_bytes = gemv_x_layout(p.k, p.n_vec).total;
   const int64_t ring_budget = kSmemBudget - x_bytes;
   // 4-row groups reuse each activation chunk across rows; they need one
   // 4-row stage per consumer warp in the ring.

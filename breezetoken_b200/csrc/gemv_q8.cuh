@@ -13,10 +13,12 @@
 //    completing on per-stage mbarriers.  It starts BEFORE griddepcontrol.wait,
 //    so under programmatic dependent launch the weight stream of this kernel
 //    overlaps the tail of the previous kernel;
-//  * warps 0-7 consume stages round-robin (warp w takes stages w, w+8, ...),
-//    build the activation vector(s) in shared memory in a lane-major layout
-//    (conflict-free LDS.128) after griddepcontrol.wait, convert int8 with a
-//    PRMT/FADD trick instead of I2F, accumulate in f32 and reduce with warp
+//  * warps 0-7 consume stages round-robin (warp w takes stages w, w+8, ...
+//    from its own ring), build the activation vector(s) in shared memory
+//    after griddepcontrol.wait, encoded per 32-element block as three int8
+//    digits of a 23-bit fixed-point value, so the int8 weights multiply by
+//    dp4a without any int->float conversion (12 dp4a per 16 weights);
+//    per-block sums are scaled and accumulated in f32 and reduced with warp
 //    shuffles (a 4-row reduce-scatter: 6 shuffles per 4 rows);
 //  * fused prologues (residual add + RMSNorm, embedding gather + RMSNorm,
 //    per-head RMSNorm * silu(z)) and epilogues (GDN conv window + SiLU,
@@ -55,7 +57,6 @@ struct GemvQ8Params {
   int32_t stage_rows;        // rows per stage (multiple of group_rows)
   int32_t stages;            // ring depth per consumer warp (each warp owns its slots)
   int32_t n_vec;             // activation vectors (batch)
-  int32_t xs_stride;         // floats per vector in the smem x layout
   // prologue
   int32_t prologue;
   const float* x;   // LOAD: x; RESID: h_in; GATED: o        ([v][k])
@@ -90,22 +91,35 @@ struct GemvQ8Params {
 
 // ------------------------------------------------------------ smem layout
 // [full mbar x stages][empty mbar x stages][scratch 64 floats][argmax 8 u64]
-// [x: n_vec * xs_stride floats][stages * stage_rows * row_bytes]
+// [activations: gemv_x_layout(k, n_vec)][8 * stages * stage_rows * row_bytes]
 struct GemvSmem {
   static constexpr int kHeader = 2 * kMaxStages * 8 + 64 * 4 + kConsumerWarps * kMaxVec * 8;
 };
 
-__host__ __device__ inline int64_t gemv_x_stride(int k) {
-  // J = ceil(k / 512) lane-major float4 slots of 16 elements per lane
-  return ((k + 511) / 512) * 512;
-}
+// Activation vectors in shared memory.  The prologue builds each vector in
+// f32 (natural layout, `xf`), then encodes every block of 32 elements in
+// fixed point: X = rint(x / sx) with sx = max|x_block| / kXMax, so |X| <=
+// 127 * 2^16, stored as three signed base-256 digits (X = d2*2^16 + d1*2^8 +
+// d0, each in [-128, 127]).  A chunk of 16 int8 weights q then dots with x
+// as sx * (2^16 * dp4a(q, d2) + 2^8 * dp4a(q, d1) + dp4a(q, d0)): the integer
+// sums are exact, so the only rounding beyond f32 accumulation is x itself,
+// represented to 2^-23 of its block maximum.  Digits are stored lane-major:
+// chunk c = lane + 32*j keeps its 16 d2, d1, d0 bytes in uint4 slots
+// ((3*j + t) * 32 + lane), so each lane's LDS.128 is bank-conflict free.
+constexpr int kXMax = 127 * 65536;
 
-// Index of element k of a vector in the lane-major x layout: chunk c = k/16
-// is owned by lane c % 32 at slot j = c / 32; element e = k % 16 sits in
-// float4 number e / 4 of that chunk.
-__device__ __forceinline__ int x_perm(int k) {
-  const int c = k >> 4, e = k & 15;
-  return ((((c >> 5) * 4 + (e >> 2)) * 32 + (c & 31)) << 2) + (e & 3);
+struct XLayout {
+  int64_t xf, xd, sx, total;  // byte offsets of each region and the total size
+};
+
+__host__ __device__ inline XLayout gemv_x_layout(int k, int nv) {
+  const int64_t J = (k + 511) / 512;
+  XLayout l;
+  l.xf = 0;
+  l.xd = ((static_cast<int64_t>(nv) * k * 4 + 127) / 128) * 128;
+  l.sx = l.xd + static_cast<int64_t>(nv) * J * 1536;
+  l.total = l.sx + ((static_cast<int64_t>(nv) * (k / 32) * 4 + 127) / 128) * 128;
+  return l;
 }
 
 __device__ __forceinline__ unsigned long long argmax_key(float v, int64_t idx) {
@@ -115,28 +129,23 @@ __device__ __forceinline__ unsigned long long argmax_key(float v, int64_t idx) {
          static_cast<unsigned long long>(0xFFFFFFFFu - static_cast<uint32_t>(idx));
 }
 
-// 16 products of one 16-byte chunk of int8 quants with 16 f32 activations.
-__device__ __forceinline__ float dot16(const uint4 q, const float4 x0, const float4 x1,
-                                       const float4 x2, const float4 x3) {
-  const uint32_t u0 = q.x ^ 0x80808080u, u1 = q.y ^ 0x80808080u;
-  const uint32_t u2 = q.z ^ 0x80808080u, u3 = q.w ^ 0x80808080u;
-  float s = biased_byte_to_f32<0>(u0) * x0.x;
-  s = fmaf(biased_byte_to_f32<1>(u0), x0.y, s);
-  s = fmaf(biased_byte_to_f32<2>(u0), x0.z, s);
-  s = fmaf(biased_byte_to_f32<3>(u0), x0.w, s);
-  s = fmaf(biased_byte_to_f32<0>(u1), x1.x, s);
-  s = fmaf(biased_byte_to_f32<1>(u1), x1.y, s);
-  s = fmaf(biased_byte_to_f32<2>(u1), x1.z, s);
-  s = fmaf(biased_byte_to_f32<3>(u1), x1.w, s);
-  s = fmaf(biased_byte_to_f32<0>(u2), x2.x, s);
-  s = fmaf(biased_byte_to_f32<1>(u2), x2.y, s);
-  s = fmaf(biased_byte_to_f32<2>(u2), x2.z, s);
-  s = fmaf(biased_byte_to_f32<3>(u2), x2.w, s);
-  s = fmaf(biased_byte_to_f32<0>(u3), x3.x, s);
-  s = fmaf(biased_byte_to_f32<1>(u3), x3.y, s);
-  s = fmaf(biased_byte_to_f32<2>(u3), x3.z, s);
-  s = fmaf(biased_byte_to_f32<3>(u3), x3.w, s);
-  return s;
+// sum_{i<16} q_i * X_i for one chunk of 16 int8 weights and the digits of X,
+// returned as f32 (exact integer sums, one rounding).
+__device__ __forceinline__ float dot16_digits(const uint4 q, const uint4 d2, const uint4 d1, const uint4 d0) {
+  int s2 = __dp4a(static_cast<int>(q.x), static_cast<int>(d2.x), 0);
+  int s1 = __dp4a(static_cast<int>(q.x), static_cast<int>(d1.x), 0);
+  int s0 = __dp4a(static_cast<int>(q.x), static_cast<int>(d0.x), 0);
+  s2 = __dp4a(static_cast<int>(q.y), static_cast<int>(d2.y), s2);
+  s1 = __dp4a(static_cast<int>(q.y), static_cast<int>(d1.y), s1);
+  s0 = __dp4a(static_cast<int>(q.y), static_cast<int>(d0.y), s0);
+  s2 = __dp4a(static_cast<int>(q.z), static_cast<int>(d2.z), s2);
+  s1 = __dp4a(static_cast<int>(q.z), static_cast<int>(d1.z), s1);
+  s0 = __dp4a(static_cast<int>(q.z), static_cast<int>(d0.z), s0);
+  s2 = __dp4a(static_cast<int>(q.w), static_cast<int>(d2.w), s2);
+  s1 = __dp4a(static_cast<int>(q.w), static_cast<int>(d1.w), s1);
+  s0 = __dp4a(static_cast<int>(q.w), static_cast<int>(d0.w), s0);
+  const int t = s1 * 256 + s0;  // |t| < 2^26
+  return fmaf(static_cast<float>(s2), 65536.0f, static_cast<float>(t));
 }
 
 struct GemvQ8Launch {
