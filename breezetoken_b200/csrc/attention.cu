@@ -186,25 +186,29 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const __grid_
   const int64_t kvbase = static_cast<int64_t>(b) * p.kv_bs + g * DIM + lane * DPL;
 
   for (int tb = t0 + warp * PB; tb < t1; tb += kAttnWarps * PB) {
+    // All PB key rows are loaded before any is used (positions past t1 read
+    // the last valid row and are masked below), so a batch costs one memory
+    // latency rather than PB.
+    float kf[PB][DPL];
+#pragma unroll
+    for (int pp = 0; pp < PB; ++pp)
+      KvRow<KV, DPL>::load(p.k, kvbase + static_cast<int64_t>(min(tb + pp, t1 - 1)) * p.kv_ts, kf[pp]);
     float part[32];
 #pragma unroll
     for (int pp = 0; pp < PB; ++pp) {
-      const int t = tb + pp;
-      float kf[DPL];
-      if (t < t1) {
-        KvRow<KV, DPL>::load(p.k, kvbase + static_cast<int64_t>(t) * p.kv_ts, kf);
-      } else {
-#pragma unroll
-        for (int i = 0; i < DPL; ++i) kf[i] = 0.f;
-      }
 #pragma unroll
       for (int h = 0; h < GS; ++h) {
         float s = 0.f;
 #pragma unroll
-        for (int i = 0; i < DPL; ++i) s = fmaf(qr[h][i], kf[i], s);
+        for (int i = 0; i < DPL; ++i) s = fmaf(qr[h][i], kf[pp][i], s);
         part[h * PB + pp] = s;
       }
     }
+    // value rows of the batch, issued before the softmax bookkeeping
+    float vf[PB][DPL];
+#pragma unroll
+    for (int pp = 0; pp < PB; ++pp)
+      KvRow<KV, DPL>::load(p.v, kvbase + static_cast<int64_t>(min(tb + pp, t1 - 1)) * p.kv_ts, vf[pp]);
     float score = reduce_scatter32(part, lane) * sl;
     const bool valid = tb + (lane % PB) < t1;
     if (!valid) score = -INFINITY;
@@ -227,16 +231,11 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const __grid_
     }
 #pragma unroll
     for (int pp = 0; pp < PB; ++pp) {
-      const int t = tb + pp;
-      if (t < t1) {
-        float vf[DPL];
-        KvRow<KV, DPL>::load(p.v, kvbase + static_cast<int64_t>(t) * p.kv_ts, vf);
 #pragma unroll
-        for (int h = 0; h < GS; ++h) {
-          const float w = __shfl_sync(0xffffffffu, pe, h * PB + pp);
+      for (int h = 0; h < GS; ++h) {
+        const float w = __shfl_sync(0xffffffffu, pe, h * PB + pp);  // 0 for masked positions
 #pragma unroll
-          for (int i = 0; i < DPL; ++i) acc[h][i] = fmaf(w, vf[i], acc[h][i]);
-        }
+        for (int i = 0; i < DPL; ++i) acc[h][i] = fmaf(w, vf[pp][i], acc[h][i]);
       }
     }
   }

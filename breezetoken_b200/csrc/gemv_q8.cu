@@ -11,97 +11,133 @@ namespace {
 constexpr int kSmemBudget = 104 * 1024;  // two CTAs (this kernel + the PDL successor) per SM
 
 // ------------------------------------------------------------------ prologue
-// Phase 1: the f32 activation vector(s) in natural layout (xf[v*K + k]).
+// Builds each activation vector and encodes it for the dp4a inner loop (see
+// gemv_q8.cuh).  Thread t owns float4 number f = t + 256*i of the vector, so
+// every global load of the prologue (x, residual, norm weights or the
+// embedding row) is issued before any is used: one memory latency on the
+// critical path instead of one per element loop.  A 32-element block is 8
+// consecutive float4 = 8 consecutive lanes, so its max is 3 xor-shuffles and
+// the digits go straight from registers to shared memory.
+constexpr int kMaxF4 = 4;  // float4 per thread per vector: K <= 4096
+
+__device__ __forceinline__ float4 f4_mul(float4 a, float4 b) {
+  return make_float4(__fmul_rn(a.x, b.x), __fmul_rn(a.y, b.y), __fmul_rn(a.z, b.z), __fmul_rn(a.w, b.w));
+}
+__device__ __forceinline__ float4 f4_scale(float4 a, float r) {
+  return make_float4(__fmul_rn(a.x, r), __fmul_rn(a.y, r), __fmul_rn(a.z, r), __fmul_rn(a.w, r));
+}
+
+__device__ __forceinline__ void encode_digits(float x, float inv, int& d2, int& d1, int& d0) {
+  int X = __float2int_rn(x * inv);
+  X = X > kXMax ? kXMax : (X < -kXMax ? -kXMax : X);
+  d0 = ((X + 128) & 255) - 128;
+  const int x1 = (X - d0) >> 8;
+  d1 = ((x1 + 128) & 255) - 128;
+  d2 = (x1 - d1) >> 8;
+}
+
+__device__ __forceinline__ uint32_t pack4(int a, int b, int c, int d) {
+  return (static_cast<uint32_t>(a) & 255u) | ((static_cast<uint32_t>(b) & 255u) << 8) |
+         ((static_cast<uint32_t>(c) & 255u) << 16) | ((static_cast<uint32_t>(d) & 255u) << 24);
+}
+
 template <int NV>
-__device__ void gemv_build_x(const GemvQ8Params& p, float* xs, float* scratch) {
-  const int tid = threadIdx.x;
-  const int K = p.k;
+__device__ void gemv_prologue(const GemvQ8Params& p, uint8_t* xd, float* sx, float* scratch) {
+  const int tid = threadIdx.x, lane = tid & 31;
+  const int K = p.k, nf4 = K >> 2, nb = K >> 5, J = (K + 511) / 512;
+  const int n_it = (nf4 + kConsumerThreads - 1) / kConsumerThreads;
   const int64_t xbs = p.x_bs ? p.x_bs : K, x2bs = p.x2_bs ? p.x2_bs : K;
-  if (p.prologue == PRO_LOAD) {
-    for (int v = 0; v < NV && v < p.n_vec; ++v)
-      for (int k = tid; k < K; k += kConsumerThreads) xs[v * K + k] = p.x[v * xbs + k];
-    return;
-  }
-  if (p.prologue == PRO_RESID_NORM || p.prologue == PRO_EMBED_NORM) {
-    for (int v = 0; v < NV && v < p.n_vec; ++v) {
-      float* xv = xs + v * K;
-      const uint8_t* erow = nullptr;
-      if (p.prologue == PRO_EMBED_NORM) {
-        int64_t tok = p.tokens[v];
-        if (tok < 0 || tok >= p.embed_rows) {
-          if (tid == 0) report_status(p.status, BT_ERR_INVALID, SITE_EMBED_TOKEN, static_cast<int32_t>(tok), v);
-          tok = 0;
-        }
-        erow = p.embed + tok * static_cast<int64_t>(p.row_bytes);
-      }
-      float ss = 0.f;
-      for (int k = tid; k < K; k += kConsumerThreads) {
-        float h;
-        if (p.prologue == PRO_RESID_NORM) {
-          h = p.x[v * xbs + k] + p.x2[v * x2bs + k];
+  const float4 zero4 = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int v = 0; v < NV; ++v) {
+    float4 h[kMaxF4], a2[kMaxF4], w4[kMaxF4];
+    // ---- all loads first
+#pragma unroll
+    for (int i = 0; i < kMaxF4; ++i) {
+      const int f = tid + kConsumerThreads * i;
+      h[i] = a2[i] = w4[i] = zero4;
+      if (i < n_it && f < nf4) {
+        if (p.prologue == PRO_EMBED_NORM) {
+          int64_t tok = p.tokens[v];
+          if (tok < 0 || tok >= p.embed_rows) {
+            if (f == 0) report_status(p.status, BT_ERR_INVALID, SITE_EMBED_TOKEN, static_cast<int32_t>(tok), v);
+            tok = 0;
+          }
+          const uint8_t* erow = p.embed + tok * static_cast<int64_t>(p.row_bytes);
+          const float d = __half2float(reinterpret_cast<const __half*>(erow)[f >> 3]);
+          const uint32_t q = *reinterpret_cast<const uint32_t*>(erow + p.sb + 4 * f);
+          h[i] = make_float4(static_cast<float>(static_cast<int8_t>(q & 255)) * d,
+                             static_cast<float>(static_cast<int8_t>((q >> 8) & 255)) * d,
+                             static_cast<float>(static_cast<int8_t>((q >> 16) & 255)) * d,
+                             static_cast<float>(static_cast<int8_t>(q >> 24)) * d);
         } else {
-          const float d = __half2float(reinterpret_cast<const __half*>(erow)[k >> 5]);
-          const float q = static_cast<float>(static_cast<int8_t>(erow[p.sb + k]));
-          h = q * d;
+          h[i] = reinterpret_cast<const float4*>(p.x + v * xbs)[f];
+          if (p.prologue != PRO_LOAD) a2[i] = reinterpret_cast<const float4*>(p.x2 + v * x2bs)[f];
         }
-        xv[k] = h;
-        ss = fmaf(h, h, ss);
-        if (blockIdx.x == 0) p.h_out[static_cast<int64_t>(v) * K + k] = h;
+        if (p.prologue == PRO_RESID_NORM || p.prologue == PRO_EMBED_NORM)
+          w4[i] = reinterpret_cast<const float4*>(p.norm_w)[f];
+        else if (p.prologue == PRO_GATED_NORM)
+          w4[i] = reinterpret_cast<const float4*>(p.norm_w)[f % (p.group >> 2)];
+      }
+    }
+    // ---- residual add and normalisation
+    if (p.prologue == PRO_RESID_NORM || p.prologue == PRO_EMBED_NORM) {
+      float ss = 0.f;
+#pragma unroll
+      for (int i = 0; i < kMaxF4; ++i) {
+        const int f = tid + kConsumerThreads * i;
+        if (i < n_it && f < nf4) {
+          if (p.prologue == PRO_RESID_NORM)
+            h[i] = make_float4(h[i].x + a2[i].x, h[i].y + a2[i].y, h[i].z + a2[i].z, h[i].w + a2[i].w);
+          if (blockIdx.x == 0) reinterpret_cast<float4*>(p.h_out + static_cast<int64_t>(v) * K)[f] = h[i];
+          ss = fmaf(h[i].x, h[i].x, ss);
+          ss = fmaf(h[i].y, h[i].y, ss);
+          ss = fmaf(h[i].z, h[i].z, ss);
+          ss = fmaf(h[i].w, h[i].w, ss);
+        }
       }
       const float total = group_sum<1>(ss, scratch, kConsumerWarps, kConsumerThreads);
       const float r = 1.0f / sqrtf(total / static_cast<float>(K) + p.eps);
-      for (int k = tid; k < K; k += kConsumerThreads) xv[k] = __fmul_rn(__fmul_rn(xv[k], r), p.norm_w[k]);
-    }
-    return;
-  }
-  // PRO_GATED_NORM: one warp per normalisation group
-  const int warp = tid >> 5, lane = tid & 31;
-  const int G = p.group, n_groups = K / G;
-  for (int v = 0; v < NV && v < p.n_vec; ++v) {
-    const float* o = p.x + v * xbs;
-    const float* z = p.x2 + v * x2bs;
-    for (int g = warp; g < n_groups; g += kConsumerWarps) {
-      float ss = 0.f;
-      for (int i = lane; i < G; i += 32) {
-        const float t = o[g * G + i];
-        ss = fmaf(t, t, ss);
-      }
-      ss = warp_sum(ss);
-      const float r = 1.0f / sqrtf(ss / static_cast<float>(G) + p.eps);
-      for (int i = lane; i < G; i += 32) {
-        const int k = g * G + i;
-        const float normed = __fmul_rn(__fmul_rn(o[k], r), p.norm_w[i]);
-        xs[v * K + k] = __fmul_rn(normed, z[k]);
+#pragma unroll
+      for (int i = 0; i < kMaxF4; ++i) h[i] = f4_mul(f4_scale(h[i], r), w4[i]);
+    } else if (p.prologue == PRO_GATED_NORM) {
+      // group of G elements = G/4 consecutive lanes of one warp
+      const int lanes = p.group >> 2;
+#pragma unroll
+      for (int i = 0; i < kMaxF4; ++i) {
+        if (i >= n_it) break;
+        float ss = fmaf(h[i].x, h[i].x, fmaf(h[i].y, h[i].y, fmaf(h[i].z, h[i].z, h[i].w * h[i].w)));
+        for (int o = lanes >> 1; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+        const float r = 1.0f / sqrtf(ss / static_cast<float>(p.group) + p.eps);
+        h[i] = f4_mul(f4_mul(f4_scale(h[i], r), w4[i]), a2[i]);
       }
     }
+    // ---- encode: block max over 8 lanes, digits from registers
+    uint8_t* xdv = xd + static_cast<int64_t>(v) * J * 1536;
+#pragma unroll
+    for (int i = 0; i < kMaxF4; ++i) {
+      if (i >= n_it) break;
+      const int f = tid + kConsumerThreads * i;
+      float m = fmaxf(fmaxf(fabsf(h[i].x), fabsf(h[i].y)), fmaxf(fabsf(h[i].z), fabsf(h[i].w)));
+      m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 1));
+      m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 2));
+      m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 4));
+      if (f < nf4) {
+        const float inv = m > 0.f ? static_cast<float>(kXMax) / m : 0.f;
+        int a[4], b[4], c[4];
+        encode_digits(h[i].x, inv, a[0], b[0], c[0]);
+        encode_digits(h[i].y, inv, a[1], b[1], c[1]);
+        encode_digits(h[i].z, inv, a[2], b[2], c[2]);
+        encode_digits(h[i].w, inv, a[3], b[3], c[3]);
+        const int ch = f >> 2;  // 16-element chunk
+        uint32_t* w = reinterpret_cast<uint32_t*>(xdv + ((ch >> 5) * 96 + (ch & 31)) * 16) + (f & 3);
+        w[0] = pack4(a[0], a[1], a[2], a[3]);
+        w[32 * 4] = pack4(b[0], b[1], b[2], b[3]);
+        w[64 * 4] = pack4(c[0], c[1], c[2], c[3]);
+        if ((f & 7) == 0) sx[v * nb + (f >> 3)] = m / static_cast<float>(kXMax);
+      }
+    }
   }
-}
-
-// Phase 2: per 32-element block, scale sx and three int8 digits of the
-// fixed-point value (see gemv_q8.cuh); one warp per block.
-template <int NV>
-__device__ void gemv_encode_x(const GemvQ8Params& p, const float* xf, uint8_t* xd, float* sx) {
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int K = p.k, nb = K / 32, J = (K + 511) / 512;
-  for (int item = warp; item < NV * nb; item += kConsumerWarps) {
-    const int v = item / nb, b = item % nb;
-    if (v >= p.n_vec) break;
-    const float x = xf[v * K + 32 * b + lane];
-    const float amax = warp_max(fabsf(x));
-    const float inv = amax > 0.f ? static_cast<float>(kXMax) / amax : 0.f;
-    int X = __float2int_rn(x * inv);
-    X = X > kXMax ? kXMax : (X < -kXMax ? -kXMax : X);
-    const int d0 = ((X + 128) & 255) - 128;
-    const int x1 = (X - d0) >> 8;
-    const int d1 = ((x1 + 128) & 255) - 128;
-    const int d2 = (x1 - d1) >> 8;
-    const int c = 2 * b + (lane >> 4), e = lane & 15;
-    uint8_t* base = xd + static_cast<int64_t>(v) * J * 1536 + ((c >> 5) * 3 * 32 + (c & 31)) * 16 + e;
-    base[0] = static_cast<uint8_t>(d2);
-    base[32 * 16] = static_cast<uint8_t>(d1);
-    base[64 * 16] = static_cast<uint8_t>(d0);
-    if (lane == 0) sx[v * nb + b] = amax / static_cast<float>(kXMax);
-  }
+  (void)lane;
 }
 
 // ------------------------------------------------------------------ epilogue
@@ -151,7 +187,6 @@ __global__ void __launch_bounds__(kGemvThreads, 2)
   float* scratch = reinterpret_cast<float*>(empty + kMaxStages);
   unsigned long long* amax = reinterpret_cast<unsigned long long*>(scratch + 64);
   const XLayout xl = gemv_x_layout(p.k, NV);
-  float* xf = reinterpret_cast<float*>(smem + GemvSmem::kHeader + xl.xf);
   uint8_t* xd = smem + GemvSmem::kHeader + xl.xd;
   float* sx = reinterpret_cast<float*>(smem + GemvSmem::kHeader + xl.sx);
   uint8_t* ring = smem + GemvSmem::kHeader + xl.total;
@@ -218,9 +253,7 @@ __global__ void __launch_bounds__(kGemvThreads, 2)
 
   // ---------------- consumers
   pdl_wait();
-  gemv_build_x<NV>(p, xf, scratch);
-  named_sync(1, kConsumerThreads);
-  gemv_encode_x<NV>(p, xf, xd, sx);
+  gemv_prologue<NV>(p, xd, sx, scratch);
   named_sync(1, kConsumerThreads);
 
   unsigned long long best[NV];
@@ -405,6 +438,17 @@ int gemv_q8_plan(GemvQ8Params& p, int sm_count, GemvQ8Launch& L) {
     return fail(BT_ERR_INVALID, "q8 GEMV weights must be 16-byte aligned (bulk copies)");
   if (p.epilogue == EPI_ARGMAX && (!p.best || !p.counter))
     return fail(BT_ERR_INVALID, "argmax epilogue needs its workspace");
+  if (p.k > kMaxF4 * kConsumerThreads * 4)
+    return fail(BT_ERR_UNSUPPORTED, "q8 GEMV serves K <= %d, got %d", kMaxF4 * kConsumerThreads * 4, p.k);
+  {
+    // the prologue reads activations and norm weights as float4
+    const uintptr_t a = reinterpret_cast<uintptr_t>(p.x) | reinterpret_cast<uintptr_t>(p.x2) |
+                        reinterpret_cast<uintptr_t>(p.norm_w) | reinterpret_cast<uintptr_t>(p.h_out);
+    if ((a & 15) || (p.x_bs & 3) || (p.x2_bs & 3))
+      return fail(BT_ERR_INVALID, "q8 GEMV activations must be 16-byte aligned with strides a multiple of 4");
+    if (p.prologue == PRO_GATED_NORM && p.group != 64 && p.group != 128)
+      return fail(BT_ERR_UNSUPPORTED, "gated-norm prologue serves groups of 64 or 128, got %d", p.group);
+  }
   p.sb = static_cast<int32_t>(bt_q8_row_bytes(p.k) - p.k);
   p.row_bytes = static_cast<int32_t>(bt_q8_row_bytes(p.k));
   const int64_t n_units = (p.n_rows + 3) / 4;

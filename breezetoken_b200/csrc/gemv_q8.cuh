@@ -97,8 +97,7 @@ struct GemvSmem {
 };
 
 // Activation vectors in shared memory.  The prologue builds each vector in
-// f32 (natural layout, `xf`), then encodes every block of 32 elements in
-// fixed point: X = rint(x / sx) with sx = max|x_block| / kXMax, so |X| <=
+// f32 registers, then encodes every block of 32 elements in fixed point: X = rint(x / sx) with sx = max|x_block| / kXMax, so |X| <=
 // 127 * 2^16, stored as three signed base-256 digits (X = d2*2^16 + d1*2^8 +
 // d0, each in [-128, 127]).  A chunk of 16 int8 weights q then dots with x
 // as sx * (2^16 * dp4a(q, d2) + 2^8 * dp4a(q, d1) + dp4a(q, d0)): the integer
@@ -109,15 +108,14 @@ struct GemvSmem {
 constexpr int kXMax = 127 * 65536;
 
 struct XLayout {
-  int64_t xf, xd, sx, total;  // byte offsets of each region and the total size
+  int64_t xd, sx, total;  // byte offsets of the digits and scales, total size
 };
 
 __host__ __device__ inline XLayout gemv_x_layout(int k, int nv) {
   const int64_t J = (k + 511) / 512;
   XLayout l;
-  l.xf = 0;
-  l.xd = ((static_cast<int64_t>(nv) * k * 4 + 127) / 128) * 128;
-  l.sx = l.xd + static_cast<int64_t>(nv) * J * 1536;
+  l.xd = 0;
+  l.sx = static_cast<int64_t>(nv) * J * 1536;
   l.total = l.sx + ((static_cast<int64_t>(nv) * (k / 32) * 4 + 127) / 128) * 128;
   return l;
 }
