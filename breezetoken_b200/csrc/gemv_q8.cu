@@ -1,5 +1,6 @@
 // Q8_0 GEMV kernel and its host-side planner.  See gemv_q8.cuh for the design.
 #include <algorithm>
+#include <cstdlib>
 
 #include "errors.h"
 #include "gemv_q8.cuh"
@@ -8,7 +9,30 @@ namespace bt {
 
 namespace {
 
-constexpr int kSmemBudget = 104 * 1024;  // two CTAs (this kernel + the PDL successor) per SM
+// Ring tiling.  Defaults keep two CTAs per SM (this kernel and its PDL
+// successor); BT_GEMV_SMEM_KB / BT_GEMV_STAGE_KB / BT_GEMV_MAX_SPW override
+// them for tuning sweeps (read once per process).
+struct GemvTuning {
+  int64_t smem_budget = 104 * 1024;  // activations + ring, bytes per CTA
+  int64_t stage_bytes = 8192;        // target bytes of one pipeline stage
+  int max_spw = 4;                   // stages per consumer warp
+};
+
+int env_int(const char* name, int dflt) {
+  const char* v = getenv(name);
+  return v && *v ? atoi(v) : dflt;
+}
+
+const GemvTuning& tuning() {
+  static const GemvTuning t = [] {
+    GemvTuning g;
+    g.smem_budget = std::min<int64_t>(220, std::max(32, env_int("BT_GEMV_SMEM_KB", 104))) * 1024;
+    g.stage_bytes = std::min<int64_t>(64, std::max(1, env_int("BT_GEMV_STAGE_KB", 8))) * 1024;
+    g.max_spw = std::min(kMaxStages / kConsumerWarps, std::max(1, env_int("BT_GEMV_MAX_SPW", 4)));
+    return g;
+  }();
+  return t;
+}
 
 // ------------------------------------------------------------------ prologue
 // Builds each activation vector and encodes it for the dp4a inner loop (see
@@ -406,7 +430,7 @@ int launch_impl(const GemvQ8Params& p, const GemvQ8Launch& L, cudaStream_t strea
   cudaGetDevice(&dev);
   if (configured_device != dev) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         kSmemBudget + GemvSmem::kHeader + 1024);
+                                         static_cast<int>(tuning().smem_budget) + GemvSmem::kHeader + 1024);
     if (e != cudaSuccess) return fail_cuda(e, "gemv_q8 set smem");
     // full shared-memory carveout, so the PDL successor's CTA fits beside this one
     e = cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
@@ -455,7 +479,8 @@ int gemv_q8_plan(GemvQ8Params& p, int sm_count, GemvQ8Launch& L) {
   const int grid = static_cast<int>(std::min<int64_t>(sm_count, n_units));
   const int64_t rows_per_cta = ((n_units + grid - 1) / grid) * 4;
   const int64_t x_bytes = gemv_x_layout(p.k, p.n_vec).total;
-  const int64_t ring_budget = kSmemBudget - x_bytes;
+  const GemvTuning& tune = tuning();
+  const int64_t ring_budget = tune.smem_budget - x_bytes;
   // 4-row groups reuse each activation chunk across rows; they need one
   // 4-row stage per consumer warp in the ring.
   const bool fits4 = kConsumerWarps * 4LL * p.row_bytes <= ring_budget;
@@ -468,7 +493,7 @@ int gemv_q8_plan(GemvQ8Params& p, int sm_count, GemvQ8Launch& L) {
   // stage = gr * f rows, ~8 KB at most, and no more rows than keep all 8
   // consumer warps busy
   const int64_t f_rows = std::max<int64_t>(1, rows_per_cta / (kConsumerWarps * gr));
-  const int64_t f_bytes = std::max<int64_t>(1, 8192 / (static_cast<int64_t>(gr) * p.row_bytes));
+  const int64_t f_bytes = std::max<int64_t>(1, tune.stage_bytes / (static_cast<int64_t>(gr) * p.row_bytes));
   const int64_t f = std::min(f_rows, f_bytes);
   p.stage_rows = static_cast<int32_t>(gr * f);
   const int64_t stage_bytes = static_cast<int64_t>(p.stage_rows) * p.row_bytes;
@@ -478,7 +503,7 @@ int gemv_q8_plan(GemvQ8Params& p, int sm_count, GemvQ8Launch& L) {
   const int64_t iters = (rows_per_cta + p.stage_rows - 1) / p.stage_rows;
   const int64_t per_warp = (iters + kConsumerWarps - 1) / kConsumerWarps;
   p.stages = static_cast<int32_t>(std::min<int64_t>(
-      {kMaxStages / kConsumerWarps, ring_budget / (kConsumerWarps * stage_bytes), std::max<int64_t>(1, per_warp)}));
+      {static_cast<int64_t>(tune.max_spw), ring_budget / (kConsumerWarps * stage_bytes), std::max<int64_t>(1, per_warp)}));
   L.grid = grid;
   L.threads = kGemvThreads;
   L.smem = GemvSmem::kHeader + x_bytes + static_cast<size_t>(kConsumerWarps) * p.stages * stage_bytes;

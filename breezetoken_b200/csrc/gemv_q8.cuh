@@ -32,7 +32,7 @@ namespace bt {
 constexpr int kConsumerWarps = 8;
 constexpr int kConsumerThreads = kConsumerWarps * 32;
 constexpr int kGemvThreads = kConsumerThreads + 32;
-constexpr int kMaxStages = 32;
+constexpr int kMaxStages = 64;
 constexpr int kMaxVec = 8;
 
 enum GemvPrologue : int {
