@@ -9,13 +9,12 @@ namespace bt {
 
 namespace {
 
-// Ring tiling.  Defaults keep two CTAs per SM (this kernel and its PDL
-// successor); BT_GEMV_SMEM_KB / BT_GEMV_STAGE_KB / BT_GEMV_MAX_SPW override
-// them for tuning sweeps (read once per process).
+// Bytes of its weight slice each CTA prefetches into L2 before the
+// dependency wait (BT_GEMV_PREFETCH_KB overrides it for tuning sweeps).
+constexpr int64_t kPrefetchPiece = 16 * 1024;
+
 struct GemvTuning {
-  int64_t smem_budget = 104 * 1024;  // activations + ring, bytes per CTA
-  int64_t stage_bytes = 8192;        // target bytes of one pipeline stage
-  int max_spw = 4;                   // stages per consumer warp
+  int64_t prefetch_bytes = 64 * 1024;
 };
 
 int env_int(const char* name, int dflt) {
@@ -26,9 +25,7 @@ int env_int(const char* name, int dflt) {
 const GemvTuning& tuning() {
   static const GemvTuning t = [] {
     GemvTuning g;
-    g.smem_budget = std::min<int64_t>(220, std::max(32, env_int("BT_GEMV_SMEM_KB", 104))) * 1024;
-    g.stage_bytes = std::min<int64_t>(64, std::max(1, env_int("BT_GEMV_STAGE_KB", 8))) * 1024;
-    g.max_spw = std::min(kMaxStages / kConsumerWarps, std::max(1, env_int("BT_GEMV_MAX_SPW", 4)));
+    g.prefetch_bytes = static_cast<int64_t>(std::min(1024, std::max(0, env_int("BT_GEMV_PREFETCH_KB", 64)))) * 1024;
     return g;
   }();
   return t;
@@ -202,18 +199,150 @@ __device__ __forceinline__ unsigned long long warp_max_u64(unsigned long long v)
 }
 
 // ------------------------------------------------------------------ kernel
-template <int NV, int GR>
-__global__ void __launch_bounds__(kGemvThreads, 2)
-    gemv_q8_kernel(const __grid_constant__ GemvQ8Params p) {
+// Weight stream: 16 bytes of int8 quants and the fp16 scale of their block,
+// read once without L1 allocation.
+__device__ __forceinline__ uint4 ldg_stream(const uint8_t* p) {
+  uint4 v;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p));
+  return v;
+}
+__device__ __forceinline__ unsigned short ldg_u16(const uint8_t* p) {
+  unsigned short v;
+  asm volatile("ld.global.nc.L1::no_allocate.u16 %0, [%1];" : "=h"(v) : "l"(p));
+  return v;
+}
+// Bulk prefetch of global bytes into L2 (no shared memory, no completion).
+__device__ __forceinline__ void prefetch_l2_bulk(const void* p, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
+
+// The weights of one row group as one lane holds them: chunk j of row r is
+// bytes [16c, 16c + 16) of the row's quants, c = lane + 32 j.
+template <int GR, int J>
+struct Tile {
+  uint4 q[GR][J];
+  unsigned short s[GR][J];
+};
+
+template <int GR, int J>
+__device__ __forceinline__ void load_tile(Tile<GR, J>& t, const GemvQ8Params& p, int64_t r0, int nr, int lane,
+                                          int nchunks) {
+#pragma unroll
+  for (int r = 0; r < GR; ++r) {
+    const uint8_t* row = p.w + (r0 + r) * static_cast<int64_t>(p.row_bytes);
+#pragma unroll
+    for (int j = 0; j < J; ++j) {
+      const int c = lane + 32 * j;
+      if (r < nr && c < nchunks) {
+        t.q[r][j] = ldg_stream(row + p.sb + 16 * c);
+        t.s[r][j] = ldg_u16(row + 2 * (c >> 1));
+      } else {
+        t.q[r][j] = make_uint4(0u, 0u, 0u, 0u);
+        t.s[r][j] = 0;
+      }
+    }
+  }
+}
+
+template <int NV, int GR, int J>
+__device__ __forceinline__ void process_tile(const Tile<GR, J>& t, const GemvQ8Params& p, int64_t r0, int nr,
+                                             int lane, int nchunks, const uint4* xd4, const float* sx,
+                                             unsigned long long (&best)[NV]) {
+  const int nb = p.k >> 5;
+  float acc[GR][NV];
+#pragma unroll
+  for (int r = 0; r < GR; ++r)
+#pragma unroll
+    for (int v = 0; v < NV; ++v) acc[r][v] = 0.f;
+#pragma unroll
+  for (int j = 0; j < J; ++j) {
+    const int c = lane + 32 * j;
+    if (c < nchunks) {
+#pragma unroll
+      for (int v = 0; v < NV; ++v) {
+        const uint4 d2 = xd4[(v * J + j) * 96 + lane];
+        const uint4 d1 = xd4[(v * J + j) * 96 + 32 + lane];
+        const uint4 d0 = xd4[(v * J + j) * 96 + 64 + lane];
+        const float xsc = sx[v * nb + (c >> 1)];
+#pragma unroll
+        for (int r = 0; r < GR; ++r) {
+          const float d = __half2float(__ushort_as_half(t.s[r][j]));
+          acc[r][v] = fmaf(d * xsc, dot16_digits(t.q[r][j], d2, d1, d0), acc[r][v]);
+        }
+      }
+    }
+  }
+
+  if constexpr (GR == 4) {
+    // reduce-scatter: lane l ends with the sum of row 2*bit4(l) + bit3(l)
+    const bool hi16 = (lane & 16) != 0, hi8 = (lane & 8) != 0;
+#pragma unroll
+    for (int v = 0; v < NV; ++v) {
+      const float s0 = hi16 ? acc[0][v] : acc[2][v];
+      const float s1 = hi16 ? acc[1][v] : acc[3][v];
+      const float r0v = __shfl_xor_sync(0xffffffffu, s0, 16);
+      const float r1v = __shfl_xor_sync(0xffffffffu, s1, 16);
+      const float b0 = (hi16 ? acc[2][v] : acc[0][v]) + r0v;
+      const float b1 = (hi16 ? acc[3][v] : acc[1][v]) + r1v;
+      const float send = hi8 ? b0 : b1;
+      float c = (hi8 ? b1 : b0) + __shfl_xor_sync(0xffffffffu, send, 8);
+      c += __shfl_xor_sync(0xffffffffu, c, 4);
+      c += __shfl_xor_sync(0xffffffffu, c, 2);
+      c += __shfl_xor_sync(0xffffffffu, c, 1);
+      const int lr = lane >> 3;  // row held by lanes 0, 8, 16, 24
+      if (p.epilogue == EPI_SILU_PAIR) {
+        const float up = __shfl_down_sync(0xffffffffu, c, 8);
+        if ((lane & 15) == 0 && lr + 1 < nr) {
+          const int64_t pair = (r0 + lr) >> 1;
+          p.y[static_cast<int64_t>(v) * p.y_stride + pair] = silu_f(c) * up;
+        }
+      } else if ((lane & 7) == 0 && lr < nr) {
+        const int64_t row = r0 + lr;
+        if (p.epilogue == EPI_ARGMAX) {
+          if (p.y) p.y[static_cast<int64_t>(v) * p.y_stride + row] = c;
+          const unsigned long long key = argmax_key(c, row);
+          best[v] = key > best[v] ? key : best[v];
+        } else {
+          epilogue_row(p, v, row, c);
+        }
+      }
+    }
+  } else {
+#pragma unroll
+    for (int v = 0; v < NV; ++v) {
+#pragma unroll
+      for (int r = 0; r < GR; ++r) {
+        const float c = warp_sum(acc[r][v]);
+        if (lane == 0 && r < nr) {
+          const int64_t row = r0 + r;
+          if (p.epilogue == EPI_ARGMAX) {
+            if (p.y) p.y[static_cast<int64_t>(v) * p.y_stride + row] = c;
+            const unsigned long long key = argmax_key(c, row);
+            best[v] = key > best[v] ? key : best[v];
+          } else {
+            epilogue_row(p, v, row, c);
+          }
+        }
+      }
+    }
+  }
+}
+
+// One CTA per SM streams a contiguous range of rows.  Warp w takes row groups
+// w, w+8, ...; each warp double-buffers its groups in registers (loads of
+// group g+8 are in flight while group g is computed).  Before the dependency
+// wait the CTA prefetches the head of its weight slice into L2 and loads its
+// first groups into registers: weights never depend on earlier kernels.
+template <int NV, int GR, int J>
+__global__ void __launch_bounds__(kGemvThreads, 2) gemv_q8_kernel(const __grid_constant__ GemvQ8Params p) {
   extern __shared__ __align__(128) uint8_t smem[];
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem);
-  uint64_t* empty = full + kMaxStages;
-  float* scratch = reinterpret_cast<float*>(empty + kMaxStages);
+  float* scratch = reinterpret_cast<float*>(smem);
   unsigned long long* amax = reinterpret_cast<unsigned long long*>(scratch + 64);
   const XLayout xl = gemv_x_layout(p.k, NV);
   uint8_t* xd = smem + GemvSmem::kHeader + xl.xd;
   float* sx = reinterpret_cast<float*>(smem + GemvSmem::kHeader + xl.sx);
-  uint8_t* ring = smem + GemvSmem::kHeader + xl.total;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t n_units = (p.n_rows + 3) >> 2;
@@ -222,168 +351,44 @@ __global__ void __launch_bounds__(kGemvThreads, 2)
   const int64_t row0 = u0 * 4;
   const int64_t row1 = u1 * 4 < p.n_rows ? u1 * 4 : p.n_rows;
   const int cta_rows = static_cast<int>(row1 - row0);
-  const int n_iters = (cta_rows + p.stage_rows - 1) / p.stage_rows;
-  // Per-warp rings: iteration `it` belongs to consumer warp it % 8, which owns
-  // slots [w * SPW, (w + 1) * SPW) and consumes them strictly in order.  A
-  // waiter is therefore never more than one phase ahead of its barrier, so the
-  // mbarrier parity test cannot alias (a shared ring with more consumers than
-  // stages would let a warp pass on the parity of a phase two fills old).
-  const int SPW = p.stages;
-  const uint32_t stage_bytes = static_cast<uint32_t>(p.stage_rows) * p.row_bytes;
+  const int n_groups = (cta_rows + GR - 1) / GR;
+  const int nchunks = p.k >> 4;
 
-  if (threadIdx.x == 0) {
-    for (int s = 0; s < kConsumerWarps * SPW; ++s) {
-      mbar_init(&full[s], 1);
-      mbar_init(&empty[s], 1);
+  // ---- before the dependency wait: weights only
+  {
+    const int64_t slice = static_cast<int64_t>(cta_rows) * p.row_bytes;
+    const int64_t pf = slice < p.prefetch_bytes ? slice : p.prefetch_bytes;
+    const int pieces = static_cast<int>((pf + kPrefetchPiece - 1) / kPrefetchPiece);
+    if (threadIdx.x < pieces) {
+      const int64_t off = static_cast<int64_t>(threadIdx.x) * kPrefetchPiece;
+      const int64_t n = pf - off < kPrefetchPiece ? pf - off : kPrefetchPiece;
+      prefetch_l2_bulk(p.w + row0 * p.row_bytes + off, static_cast<uint32_t>(n & ~15LL));
     }
-    mbar_fence_init();
   }
-  __syncthreads();
+  Tile<GR, J> A, B;
+  int g = warp;
+  if (g < n_groups) load_tile<GR, J>(A, p, row0 + static_cast<int64_t>(g) * GR, min(GR, cta_rows - g * GR), lane, nchunks);
   pdl_launch_dependents();
 
-  if (warp == kConsumerWarps) {
-    // ---------------- producer: weights only, so no pdl_wait needed
-    if (lane == 0) {
-      const uint64_t policy = l2_evict_first_policy();
-      int issued = 0;
-      for (int it = 0; it < n_iters; ++it) {
-        const int i = it / kConsumerWarps;  // this warp's i-th stage
-        const int s = (it % kConsumerWarps) * SPW + i % SPW;
-        if (i >= SPW && !mbar_wait(&empty[s], ((i / SPW) - 1) & 1)) {
-          report_status(p.status, BT_ERR_TIMEOUT, SITE_GEMV_PRODUCER_EMPTY, it, n_iters, SPW);
-          break;
-        }
-        const int64_t r = row0 + static_cast<int64_t>(it) * p.stage_rows;
-        const int nr = static_cast<int>(min(static_cast<int64_t>(p.stage_rows), row1 - r));
-        const uint32_t bytes = static_cast<uint32_t>(nr) * p.row_bytes;
-        mbar_arrive_expect_tx(&full[s], bytes);
-        bulk_g2s(ring + static_cast<size_t>(s) * stage_bytes, p.w + r * p.row_bytes, bytes,
-                 &full[s], policy);
-        issued = it + 1;
-      }
-      // Do not leave the CTA with copies in flight (bounded): wait for the
-      // last fill of every slot.
-      for (int it = max(0, issued - kConsumerWarps * SPW); it < issued; ++it) {
-        const int i = it / kConsumerWarps;
-        const int s = (it % kConsumerWarps) * SPW + i % SPW;
-        if (!mbar_wait(&full[s], (i / SPW) & 1)) {
-          report_status(p.status, BT_ERR_TIMEOUT, SITE_GEMV_PRODUCER_DRAIN, it, n_iters, SPW);
-          break;
-        }
-      }
-    }
-    return;
-  }
-
-  // ---------------- consumers
+  // ---- activations (after the wait)
   pdl_wait();
   gemv_prologue<NV>(p, xd, sx, scratch);
-  named_sync(1, kConsumerThreads);
+  __syncthreads();
 
   unsigned long long best[NV];
 #pragma unroll
   for (int v = 0; v < NV; ++v) best[v] = 0ull;
-
-  const int nchunks = p.k >> 4;
-  const int J = (nchunks + 31) >> 5;
-  const int nb = p.k >> 5;
   const uint4* xd4 = reinterpret_cast<const uint4*>(xd);
-
-  for (int it = warp, i = 0; it < n_iters; it += kConsumerWarps, ++i) {
-    const int s = warp * SPW + i % SPW;
-    if (!mbar_wait(&full[s], (i / SPW) & 1)) {
-      report_status(p.status, BT_ERR_TIMEOUT, SITE_GEMV_CONSUMER_FULL, it, n_iters, (warp << 16) | SPW);
-      break;
-    }
-    const uint8_t* st = ring + static_cast<size_t>(s) * stage_bytes;
-    const int64_t r0 = row0 + static_cast<int64_t>(it) * p.stage_rows;
-    const int nr = static_cast<int>(min(static_cast<int64_t>(p.stage_rows), row1 - r0));
-
-    for (int g = 0; g < nr; g += GR) {
-      float acc[GR][NV];
-#pragma unroll
-      for (int r = 0; r < GR; ++r)
-#pragma unroll
-        for (int v = 0; v < NV; ++v) acc[r][v] = 0.f;
-
-      for (int j = 0; j < J; ++j) {
-        const int c = lane + (j << 5);
-        if (c < nchunks) {
-          uint4 dg[NV][3];
-          float xsc[NV];
-#pragma unroll
-          for (int v = 0; v < NV; ++v) {
-#pragma unroll
-            for (int t = 0; t < 3; ++t) dg[v][t] = xd4[(v * J + j) * 96 + t * 32 + lane];
-            xsc[v] = sx[v * nb + (c >> 1)];
-          }
-#pragma unroll
-          for (int r = 0; r < GR; ++r) {
-            if (g + r < nr) {
-              const uint8_t* row = st + static_cast<size_t>(g + r) * p.row_bytes;
-              const float d = __half2float(reinterpret_cast<const __half*>(row)[c >> 1]);
-              const uint4 q = *reinterpret_cast<const uint4*>(row + p.sb + (c << 4));
-#pragma unroll
-              for (int v = 0; v < NV; ++v)
-                acc[r][v] = fmaf(d * xsc[v], dot16_digits(q, dg[v][0], dg[v][1], dg[v][2]), acc[r][v]);
-            }
-          }
-        }
-      }
-
-      if constexpr (GR == 4) {
-        // reduce-scatter: lane l ends with the sum of row 2*bit4(l) + bit3(l)
-        const bool hi16 = (lane & 16) != 0, hi8 = (lane & 8) != 0;
-#pragma unroll
-        for (int v = 0; v < NV; ++v) {
-          const float s0 = hi16 ? acc[0][v] : acc[2][v];
-          const float s1 = hi16 ? acc[1][v] : acc[3][v];
-          const float r0v = __shfl_xor_sync(0xffffffffu, s0, 16);
-          const float r1v = __shfl_xor_sync(0xffffffffu, s1, 16);
-          const float b0 = (hi16 ? acc[2][v] : acc[0][v]) + r0v;
-          const float b1 = (hi16 ? acc[3][v] : acc[1][v]) + r1v;
-          const float send = hi8 ? b0 : b1;
-          float c = (hi8 ? b1 : b0) + __shfl_xor_sync(0xffffffffu, send, 8);
-          c += __shfl_xor_sync(0xffffffffu, c, 4);
-          c += __shfl_xor_sync(0xffffffffu, c, 2);
-          c += __shfl_xor_sync(0xffffffffu, c, 1);
-          const int lr = g + (lane >> 3);  // local row held by lanes 0, 8, 16, 24
-          if (p.epilogue == EPI_SILU_PAIR) {
-            const float up = __shfl_down_sync(0xffffffffu, c, 8);
-            if ((lane & 15) == 0 && lr + 1 < nr) {
-              const int64_t pair = (r0 + lr) >> 1;
-              p.y[static_cast<int64_t>(v) * p.y_stride + pair] = silu_f(c) * up;
-            }
-          } else if ((lane & 7) == 0 && lr < nr) {
-            const int64_t row = r0 + lr;
-            if (p.epilogue == EPI_ARGMAX) {
-              if (p.y) p.y[static_cast<int64_t>(v) * p.y_stride + row] = c;
-              const unsigned long long key = argmax_key(c, row);
-              best[v] = key > best[v] ? key : best[v];
-            } else {
-              epilogue_row(p, v, row, c);
-            }
-          }
-        }
-      } else {
-#pragma unroll
-        for (int v = 0; v < NV; ++v) {
-          const float c = warp_sum(acc[0][v]);
-          if (lane == 0 && g < nr) {
-            const int64_t row = r0 + g;
-            if (p.epilogue == EPI_ARGMAX) {
-              if (p.y) p.y[static_cast<int64_t>(v) * p.y_stride + row] = c;
-              const unsigned long long key = argmax_key(c, row);
-              best[v] = key > best[v] ? key : best[v];
-            } else {
-              epilogue_row(p, v, row, c);
-            }
-          }
-        }
-      }
-    }
-    __syncwarp();
-    if (lane == 0) mbar_arrive(&empty[s]);
+  while (g < n_groups) {
+    int gn = g + kConsumerWarps;
+    if (gn < n_groups) load_tile<GR, J>(B, p, row0 + static_cast<int64_t>(gn) * GR, min(GR, cta_rows - gn * GR), lane, nchunks);
+    process_tile<NV, GR, J>(A, p, row0 + static_cast<int64_t>(g) * GR, min(GR, cta_rows - g * GR), lane, nchunks, xd4, sx, best);
+    g = gn;
+    if (g >= n_groups) break;
+    gn = g + kConsumerWarps;
+    if (gn < n_groups) load_tile<GR, J>(A, p, row0 + static_cast<int64_t>(gn) * GR, min(GR, cta_rows - gn * GR), lane, nchunks);
+    process_tile<NV, GR, J>(B, p, row0 + static_cast<int64_t>(g) * GR, min(GR, cta_rows - g * GR), lane, nchunks, xd4, sx, best);
+    g = gn;
   }
 
   if (p.epilogue != EPI_ARGMAX) return;
@@ -394,7 +399,7 @@ __global__ void __launch_bounds__(kGemvThreads, 2)
     const unsigned long long b = warp_max_u64(best[v]);
     if (lane == 0) amax[warp * kMaxVec + v] = b;
   }
-  named_sync(1, kConsumerThreads);
+  __syncthreads();
   if (threadIdx.x == 0) {
     for (int v = 0; v < p.n_vec && v < NV; ++v) {
       unsigned long long b = 0ull;
@@ -422,19 +427,15 @@ __global__ void __launch_bounds__(kGemvThreads, 2)
   }
 }
 
-template <int NV, int GR>
+template <int NV, int GR, int J>
 int launch_impl(const GemvQ8Params& p, const GemvQ8Launch& L, cudaStream_t stream, bool pdl) {
-  auto kern = gemv_q8_kernel<NV, GR>;
+  auto kern = gemv_q8_kernel<NV, GR, J>;
   static int configured_device = -1;
   int dev = 0;
   cudaGetDevice(&dev);
   if (configured_device != dev) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         static_cast<int>(tuning().smem_budget) + GemvSmem::kHeader + 1024);
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 100 * 1024);
     if (e != cudaSuccess) return fail_cuda(e, "gemv_q8 set smem");
-    // full shared-memory carveout, so the PDL successor's CTA fits beside this one
-    e = cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
-    if (e != cudaSuccess) return fail_cuda(e, "gemv_q8 set carveout");
     configured_device = dev;
   }
   cudaLaunchConfig_t cfg = {};
@@ -452,6 +453,18 @@ int launch_impl(const GemvQ8Params& p, const GemvQ8Launch& L, cudaStream_t strea
   return BT_OK;
 }
 
+template <int NV, int GR>
+int launch_j(const GemvQ8Params& p, const GemvQ8Launch& L, cudaStream_t stream, bool pdl) {
+  const int J = (p.k + 511) / 512;
+  if (J <= 1) return launch_impl<NV, GR, 1>(p, L, stream, pdl);
+  if (J <= 2) return launch_impl<NV, GR, 2>(p, L, stream, pdl);
+  if constexpr (GR == 1) {
+    if (J <= 4) return launch_impl<NV, GR, 4>(p, L, stream, pdl);
+    return launch_impl<NV, GR, 8>(p, L, stream, pdl);
+  }
+  return fail(BT_ERR_UNSUPPORTED, "q8 GEMV: 4-row groups serve K <= 1024");
+}
+
 }  // namespace
 
 int gemv_q8_plan(GemvQ8Params& p, int sm_count, GemvQ8Launch& L) {
@@ -459,7 +472,7 @@ int gemv_q8_plan(GemvQ8Params& p, int sm_count, GemvQ8Launch& L) {
   if (p.n_rows < 1) return fail(BT_ERR_INVALID, "q8 GEMV needs at least one row");
   if (p.n_vec < 1 || p.n_vec > kMaxVec) return fail(BT_ERR_UNSUPPORTED, "q8 GEMV serves 1..8 vectors, got %d", p.n_vec);
   if (!p.w || (reinterpret_cast<uintptr_t>(p.w) & 15))
-    return fail(BT_ERR_INVALID, "q8 GEMV weights must be 16-byte aligned (bulk copies)");
+    return fail(BT_ERR_INVALID, "q8 GEMV weights must be 16-byte aligned");
   if (p.epilogue == EPI_ARGMAX && (!p.best || !p.counter))
     return fail(BT_ERR_INVALID, "argmax epilogue needs its workspace");
   if (p.k > kMaxF4 * kConsumerThreads * 4)
@@ -478,46 +491,28 @@ int gemv_q8_plan(GemvQ8Params& p, int sm_count, GemvQ8Launch& L) {
   const int64_t n_units = (p.n_rows + 3) / 4;
   const int grid = static_cast<int>(std::min<int64_t>(sm_count, n_units));
   const int64_t rows_per_cta = ((n_units + grid - 1) / grid) * 4;
-  const int64_t x_bytes = gemv_x_layout(p.k, p.n_vec).total;
-  const GemvTuning& tune = tuning();
-  const int64_t ring_budget = tune.smem_budget - x_bytes;
-  // 4-row groups reuse each activation chunk across rows; they need one
-  // 4-row stage per consumer warp in the ring.
-  const bool fits4 = kConsumerWarps * 4LL * p.row_bytes <= ring_budget;
+  // 4-row groups reuse each activation chunk across rows (K <= 1024: a
+  // double-buffered 4-row tile stays within the register budget)
+  const bool g4_ok = p.k <= 1024 && p.n_vec <= 2;
   int gr = 1;
-  if (p.epilogue == EPI_SILU_PAIR || (p.n_vec <= 2 && rows_per_cta >= 32 && fits4)) gr = 4;
-  if (p.epilogue == EPI_SILU_PAIR && (p.n_vec > 2 || !fits4))
-    return fail(BT_ERR_UNSUPPORTED, "SiLU-pair epilogue serves at most 2 vectors and K <= %lld",
-                static_cast<long long>(ring_budget / (4 * kConsumerWarps)));
+  if (p.epilogue == EPI_SILU_PAIR || (g4_ok && rows_per_cta >= 32)) gr = 4;
+  if (p.epilogue == EPI_SILU_PAIR && !g4_ok)
+    return fail(BT_ERR_UNSUPPORTED, "SiLU-pair epilogue serves at most 2 vectors and K <= 1024");
   p.group_rows = gr;
-  // stage = gr * f rows, ~8 KB at most, and no more rows than keep all 8
-  // consumer warps busy
-  const int64_t f_rows = std::max<int64_t>(1, rows_per_cta / (kConsumerWarps * gr));
-  const int64_t f_bytes = std::max<int64_t>(1, tune.stage_bytes / (static_cast<int64_t>(gr) * p.row_bytes));
-  const int64_t f = std::min(f_rows, f_bytes);
-  p.stage_rows = static_cast<int32_t>(gr * f);
-  const int64_t stage_bytes = static_cast<int64_t>(p.stage_rows) * p.row_bytes;
-  if (kConsumerWarps * stage_bytes > ring_budget)
-    return fail(BT_ERR_UNSUPPORTED, "q8 GEMV row of K=%d does not fit the stage budget", p.k);
-  // stages per consumer warp (each warp owns its own ring)
-  const int64_t iters = (rows_per_cta + p.stage_rows - 1) / p.stage_rows;
-  const int64_t per_warp = (iters + kConsumerWarps - 1) / kConsumerWarps;
-  p.stages = static_cast<int32_t>(std::min<int64_t>(
-      {static_cast<int64_t>(tune.max_spw), ring_budget / (kConsumerWarps * stage_bytes), std::max<int64_t>(1, per_warp)}));
+  p.prefetch_bytes = tuning().prefetch_bytes;
   L.grid = grid;
   L.threads = kGemvThreads;
-  L.smem = GemvSmem::kHeader + x_bytes + static_cast<size_t>(kConsumerWarps) * p.stages * stage_bytes;
+  L.smem = GemvSmem::kHeader + gemv_x_layout(p.k, p.n_vec).total;
   return BT_OK;
 }
 
 int gemv_q8_launch(const GemvQ8Params& p, const GemvQ8Launch& L, cudaStream_t stream, bool pdl) {
   const bool g4 = p.group_rows == 4;
   switch (p.n_vec) {
-    case 1: return g4 ? launch_impl<1, 4>(p, L, stream, pdl) : launch_impl<1, 1>(p, L, stream, pdl);
-    case 2: return g4 ? launch_impl<2, 4>(p, L, stream, pdl) : launch_impl<2, 1>(p, L, stream, pdl);
-    case 3:
-    case 4: return launch_impl<4, 1>(p, L, stream, pdl);
-    default: return launch_impl<8, 1>(p, L, stream, pdl);
+    case 1: return g4 ? launch_j<1, 4>(p, L, stream, pdl) : launch_j<1, 1>(p, L, stream, pdl);
+    case 2: return g4 ? launch_j<2, 4>(p, L, stream, pdl) : launch_j<2, 1>(p, L, stream, pdl);
+    case 4: return launch_j<4, 1>(p, L, stream, pdl);
+    default: return launch_j<8, 1>(p, L, stream, pdl);
   }
 }
 

@@ -8,18 +8,18 @@
 // Design (sm_100a):
 //  * one CTA per SM; CTA b owns a contiguous range of rows, so its weights
 //    are one contiguous byte range;
-//  * warp 8 is the producer: one lane streams the CTA's rows into a ring of
-//    shared-memory stages with cp.async.bulk (TMA engine), L2 evict-first,
-//    completing on per-stage mbarriers.  It starts BEFORE griddepcontrol.wait,
-//    so under programmatic dependent launch the weight stream of this kernel
-//    overlaps the tail of the previous kernel;
-//  * warps 0-7 consume stages round-robin (warp w takes stages w, w+8, ...
-//    from its own ring), build the activation vector(s) in shared memory
-//    after griddepcontrol.wait, encoded per 32-element block as three int8
-//    digits of a 23-bit fixed-point value, so the int8 weights multiply by
-//    dp4a without any int->float conversion (12 dp4a per 16 weights);
-//    per-block sums are scaled and accumulated in f32 and reduced with warp
-//    shuffles (a 4-row reduce-scatter: 6 shuffles per 4 rows);
+//  * the 8 warps stream row groups (4 rows for K <= 1024, else 1) straight
+//    from HBM with 128-bit non-allocating loads, double-buffered in
+//    registers.  Before griddepcontrol.wait -- i.e. while the previous kernel
+//    still runs under programmatic dependent launch -- each CTA prefetches
+//    the head of its weight slice into L2 (cp.async.bulk.prefetch) and loads
+//    its first groups into registers; weights never depend on earlier work;
+//  * after the wait the activation vector(s) are built in shared memory,
+//    encoded per 32-element block as three int8 digits of a 23-bit
+//    fixed-point value, so the int8 weights multiply by dp4a without any
+//    int->float conversion (12 dp4a per 16 weights); per-block sums are
+//    scaled and accumulated in f32 and reduced with warp shuffles (a 4-row
+//    reduce-scatter: 6 shuffles per 4 rows);
 //  * fused prologues (residual add + RMSNorm, embedding gather + RMSNorm,
 //    per-head RMSNorm * silu(z)) and epilogues (GDN conv window + SiLU,
 //    softplus decay, SiLU-gate of interleaved gate/up rows, argmax).
@@ -31,8 +31,7 @@ namespace bt {
 
 constexpr int kConsumerWarps = 8;
 constexpr int kConsumerThreads = kConsumerWarps * 32;
-constexpr int kGemvThreads = kConsumerThreads + 32;
-constexpr int kMaxStages = 64;
+constexpr int kGemvThreads = kConsumerThreads;
 constexpr int kMaxVec = 8;
 
 enum GemvPrologue : int {
@@ -54,8 +53,7 @@ struct GemvQ8Params {
   int64_t n_rows;
   int32_t k, row_bytes, sb;  // K, bytes per row, scale bytes per row
   int32_t group_rows;        // rows per consumer task (1 or 4)
-  int32_t stage_rows;        // rows per stage (multiple of group_rows)
-  int32_t stages;            // ring depth per consumer warp (each warp owns its slots)
+  int64_t prefetch_bytes;    // weight bytes per CTA prefetched into L2 before the wait
   int32_t n_vec;             // activation vectors (batch)
   // prologue
   int32_t prologue;
@@ -90,10 +88,9 @@ struct GemvQ8Params {
 };
 
 // ------------------------------------------------------------ smem layout
-// [full mbar x stages][empty mbar x stages][scratch 64 floats][argmax 8 u64]
-// [activations: gemv_x_layout(k, n_vec)][8 * stages * stage_rows * row_bytes]
+// [scratch 64 floats][argmax 8 x 8 u64][activations: gemv_x_layout(k, n_vec)]
 struct GemvSmem {
-  static constexpr int kHeader = 2 * kMaxStages * 8 + 64 * 4 + kConsumerWarps * kMaxVec * 8;
+  static constexpr int kHeader = 64 * 4 + kConsumerWarps * kMaxVec * 8;
 };
 
 // Activation vectors in shared memory.  The prologue builds each vector in
