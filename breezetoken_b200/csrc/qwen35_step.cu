@@ -17,6 +17,7 @@
 // weight stream starts while its predecessor finishes; every write of a
 // kernel happens after its griddepcontrol.wait, so reusing buffers across
 // kernels is race-free.  The residual stream ping-pongs between h0 and h1.
+#include <cstdlib>
 #include <vector>
 
 #include "attention.cuh"
@@ -75,11 +76,21 @@ GemvQ8Params base_gemv(const BtQwen35Dims& d, const BtQwen35Runtime& rt) {
   return p;
 }
 
+// Programmatic dependent launch between the step's kernels (on by default;
+// BT_PDL=0 serialises them fully, for measurements).
+bool use_pdl() {
+  static const bool on = [] {
+    const char* v = getenv("BT_PDL");
+    return !(v && v[0] == '0');
+  }();
+  return on;
+}
+
 int run_gemv(GemvQ8Params& p, cudaStream_t s) {
   GemvQ8Launch L{};
   int rc = gemv_q8_plan(p, sm_count(), L);
   if (rc) return rc;
-  return gemv_q8_launch(p, L, s, true);
+  return gemv_q8_launch(p, L, s, use_pdl());
 }
 
 }  // namespace
@@ -169,7 +180,7 @@ int qwen35_step(const BtQwen35Model& m, const BtQwen35Runtime& rt, int with_logi
       g.scale = 1.0f / sqrtf(static_cast<float>(d.ssm_state));
       g.eps = d.l2_eps;
       g.status = rt.status;
-      if ((rc = gdn_decode_launch(g, s, true))) return rc;
+      if ((rc = gdn_decode_launch(g, s, use_pdl()))) return rc;
     } else {
       AttnParams a{};
       const int64_t qsz = 2LL * d.n_heads * d.head_dim;
@@ -204,7 +215,7 @@ int qwen35_step(const BtQwen35Model& m, const BtQwen35Runtime& rt, int with_logi
       a.part = ws.attn_part;
       a.counters = ws.attn_counters;
       a.status = rt.status;
-      if ((rc = attention_launch(a, s, true))) return rc;
+      if ((rc = attention_launch(a, s, use_pdl()))) return rc;
     }
 
     // ---- 3: out-projection
@@ -267,7 +278,7 @@ int qwen35_step(const BtQwen35Model& m, const BtQwen35Runtime& rt, int with_logi
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    cfg.numAttrs = use_pdl() ? 1 : 0;
     cudaError_t e = cudaLaunchKernelEx(&cfg, advance_pos_kernel, rt.pos, static_cast<int>(d.batch));
     return e == cudaSuccess ? BT_OK : fail_cuda(e, "advance_pos");
   }
