@@ -90,7 +90,10 @@ class BtQwen35Model(C.Structure):
 class BtQwen35Runtime(C.Structure):
     _fields_ = [
         (n, C.c_void_p)
-        for n in ("pos", "token", "history", "logits", "h0", "h1", "delta", "proj", "mix", "act", "workspace", "status")
+        for n in (
+            "pos", "token", "history", "logits", "h0", "h1", "delta", "proj", "mix", "act", "workspace", "trace",
+            "status",
+        )
     ]
 
 
@@ -118,6 +121,7 @@ _SIGS: dict[str, tuple[object, list]] = {
     "bt_gdn_decode": (C.c_int, [_P, _P, _P, C.c_int, _P, _P, _P, _P, _I64, _I64, _I64, _I64, C.c_float, C.c_float, _P]),
     "bt_argmax_workspace_bytes": (_I64, [_I64]),
     "bt_argmax": (C.c_int, [_P, _I64, _I64, _P, _P, _P]),
+    "bt_qwen35_kernels_per_step": (C.c_int, [C.POINTER(BtQwen35Dims)]),
     "bt_qwen35_proj_elems": (_I64, [C.POINTER(BtQwen35Dims)]),
     "bt_qwen35_workspace_bytes": (_I64, [C.POINTER(BtQwen35Dims)]),
     "bt_qwen35_step": (C.c_int, [C.POINTER(BtQwen35Model), C.POINTER(BtQwen35Runtime), C.c_int, _P]),

@@ -100,8 +100,10 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const __grid_
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int split = blockIdx.x, g = blockIdx.y, b = blockIdx.z;
+  trace_entry(p.trace);
   pdl_launch_dependents();
   pdl_wait();
+  trace_waited(p.trace);
 
   int L = p.model ? p.pos[b] + 1 : p.lens[b];
   if (L < 0 || L > p.cap) {
@@ -173,6 +175,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const __grid_
     __syncthreads();
   }
 
+  trace_ready(p.trace);
   float qr[GS][DPL], acc[GS][DPL];
 #pragma unroll
   for (int h = 0; h < GS; ++h)
@@ -281,14 +284,23 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const __grid_
       }
     }
   }
-  if (splits == 1) return;
+  if (splits == 1) {
+    if (p.trace) {
+      __syncthreads();
+      trace_exit(p.trace);
+    }
+    return;
+  }
 
   // ---------------- last CTA of the group merges the splits
   __threadfence();
   __syncthreads();
   if (threadIdx.x == 0) s_ticket = atomicAdd(p.counters + static_cast<int64_t>(b) * p.kv_heads + g, 1u);
   __syncthreads();
-  if (s_ticket != static_cast<uint32_t>(splits - 1)) return;
+  if (s_ticket != static_cast<uint32_t>(splits - 1)) {
+    trace_exit(p.trace);
+    return;
+  }
   __threadfence();
   // per-head split weights 2^(m_s - M) and total sum, one warp per head
   // (the warp-partial buffer is free again and holds GS * splits weights)
@@ -334,6 +346,10 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const __grid_
     p.out[static_cast<int64_t>(b) * p.out_bs + static_cast<int64_t>(g * GS + h) * DIM + d] = o;
   }
   if (threadIdx.x == 0) atomicExch(p.counters + static_cast<int64_t>(b) * p.kv_heads + g, 0u);
+  if (p.trace) {
+    __syncthreads();
+    trace_exit(p.trace);
+  }
 }
 
 template <typename KV, int DPL, int GS>

@@ -39,6 +39,7 @@ struct AttnParams {
   float* part;
   uint32_t* counters;
   int32_t* status;
+  TraceRec* trace;  // optional launch timeline record (null = off)
 };
 
 // Workspace floats for the partials, then one u32 counter per (b, g).

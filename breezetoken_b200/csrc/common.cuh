@@ -35,6 +35,39 @@ __device__ __forceinline__ uint64_t global_ns() {
 // reports BT_ERR_TIMEOUT through the caller's status word.
 constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s
 
+// ------------------------------------------------------------ step tracer
+// Optional per-launch timeline: every CTA folds %globaltimer stamps of four
+// points into one record per launch (first/last CTA entry, last CTA past the
+// dependency wait, last CTA past its prologue, first/last CTA exit).  Off
+// (null) in normal runs; the layout matches BtTraceRecord in bt_b200.h.
+struct TraceRec {
+  unsigned long long entry_min, entry_max, waited_min, waited_max, ready_max, exit_min, exit_max, pad;
+};
+__device__ __forceinline__ void trace_entry(TraceRec* t) {
+  if (t && threadIdx.x == 0) {
+    const unsigned long long now = global_ns();
+    atomicMin(&t->entry_min, now);
+    atomicMax(&t->entry_max, now);
+  }
+}
+__device__ __forceinline__ void trace_waited(TraceRec* t) {
+  if (t && threadIdx.x == 0) {
+    const unsigned long long now = global_ns();
+    atomicMin(&t->waited_min, now);
+    atomicMax(&t->waited_max, now);
+  }
+}
+__device__ __forceinline__ void trace_ready(TraceRec* t) {
+  if (t && threadIdx.x == 0) atomicMax(&t->ready_max, global_ns());
+}
+__device__ __forceinline__ void trace_exit(TraceRec* t) {
+  if (t && threadIdx.x == 0) {
+    const unsigned long long now = global_ns();
+    atomicMin(&t->exit_min, now);
+    atomicMax(&t->exit_max, now);
+  }
+}
+
 // Where a device-side check fired (status word 1).
 enum StatusSite : int32_t {
   SITE_GEMV_PRODUCER_EMPTY = 1,  // producer waiting for a consumed stage

@@ -53,12 +53,14 @@ __global__ void __launch_bounds__(kThreads) gdn_decode_kernel(const __grid_const
   const int col = tile * kCols + col_l;
   const int r0 = rg * R;
 
+  trace_entry(p.trace);
   float* S = p.state + ((static_cast<int64_t>(b) * p.heads_v + hv) * DIM) * DIM;
   // L2 prefetch of the tile's rows (64 B each): a cache hint only, safe
   // before the dependency wait.
   if (tid < DIM) asm volatile("prefetch.global.L2::evict_last [%0];" ::"l"(S + static_cast<int64_t>(tid) * DIM + tile * kCols));
   pdl_launch_dependents();
   pdl_wait();
+  trace_waited(p.trace);
 
   // normalised q/k of key head hk: warp 0 does q, warp 1 does k
   const int warp = tid >> 5;
@@ -86,6 +88,7 @@ __global__ void __launch_bounds__(kThreads) gdn_decode_kernel(const __grid_const
 #pragma unroll
   for (int i = 0; i < R; ++i) s[i] = __fmul_rn(S[static_cast<int64_t>(r0 + i) * DIM + col], decay);
   __syncthreads();
+  trace_ready(p.trace);
 
   float rec = 0.f;
 #pragma unroll
@@ -113,6 +116,10 @@ __global__ void __launch_bounds__(kThreads) gdn_decode_kernel(const __grid_const
 #pragma unroll
     for (int w = 0; w < kRowGroups; ++w) t += red[w][tid];
     p.out[static_cast<int64_t>(b) * p.out_bs + static_cast<int64_t>(hv) * DIM + tile * kCols + tid] = t;
+  }
+  if (p.trace) {
+    __syncthreads();
+    trace_exit(p.trace);
   }
 }
 

@@ -20,6 +20,7 @@ struct GdnParams {
   int32_t batch, heads_k, heads_v, dim;
   float scale, eps;
   int32_t* status;
+  TraceRec* trace;  // optional launch timeline record (null = off)
 };
 
 int gdn_decode_launch(const GdnParams& p, cudaStream_t stream, bool pdl);

@@ -353,6 +353,7 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_q8_kernel(const __grid_c
   const int cta_rows = static_cast<int>(row1 - row0);
   const int n_groups = (cta_rows + GR - 1) / GR;
   const int nchunks = p.k >> 4;
+  trace_entry(p.trace);
 
   // ---- before the dependency wait: weights only
   {
@@ -372,8 +373,10 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_q8_kernel(const __grid_c
 
   // ---- activations (after the wait)
   pdl_wait();
+  trace_waited(p.trace);
   gemv_prologue<NV>(p, xd, sx, scratch);
   __syncthreads();
+  trace_ready(p.trace);
 
   unsigned long long best[NV];
 #pragma unroll
@@ -391,7 +394,13 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_q8_kernel(const __grid_c
     g = gn;
   }
 
-  if (p.epilogue != EPI_ARGMAX) return;
+  if (p.epilogue != EPI_ARGMAX) {
+    if (p.trace) {
+      __syncthreads();
+      trace_exit(p.trace);
+    }
+    return;
+  }
 
   // ---------------- argmax: CTA reduce, one atomic per vector, last CTA finalises
 #pragma unroll
@@ -425,6 +434,7 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_q8_kernel(const __grid_c
       __threadfence();
     }
   }
+  trace_exit(p.trace);
 }
 
 template <int NV, int GR, int J>

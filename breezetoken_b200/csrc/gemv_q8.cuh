@@ -85,6 +85,7 @@ struct GemvQ8Params {
   int32_t* history;          // [v][history_stride] or null
   int32_t history_stride;
   int32_t* status;
+  TraceRec* trace;  // optional launch timeline record (null = off)
 };
 
 // ------------------------------------------------------------ smem layout

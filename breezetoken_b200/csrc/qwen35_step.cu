@@ -95,6 +95,8 @@ int run_gemv(GemvQ8Params& p, cudaStream_t s) {
 
 }  // namespace
 
+int qwen35_kernels_per_step(const BtQwen35Dims& d) { return 5 * d.n_layers + 1; }
+
 int64_t qwen35_proj_elems(const BtQwen35Dims& d) {
   const int64_t gdn = 4LL * d.ssm_inner + 2LL * d.ssm_heads;
   const int64_t attn = 2LL * d.n_heads * d.head_dim + 2LL * d.n_kv * d.head_dim;
@@ -119,6 +121,8 @@ int qwen35_step(const BtQwen35Model& m, const BtQwen35Runtime& rt, int with_logi
   const int64_t mix_stride = d.ssm_inner > d.n_heads * d.head_dim ? d.ssm_inner : d.n_heads * d.head_dim;
   float* hc = rt.h0;
   float* ho = rt.h1;
+  int kidx = 0;  // launch index within the step, for the optional tracer
+  auto trace = [&]() -> TraceRec* { return rt.trace ? static_cast<TraceRec*>(rt.trace) + kidx++ : nullptr; };
 
   for (int i = 0; i < d.n_layers; ++i) {
     const BtQwen35Layer& ly = m.layers[i];
@@ -157,6 +161,7 @@ int qwen35_step(const BtQwen35Model& m, const BtQwen35Runtime& rt, int with_logi
       p1.n_rows = 2LL * d.n_heads * d.head_dim + 2LL * d.n_kv * d.head_dim;
       p1.epilogue = EPI_STORE;
     }
+    p1.trace = trace();
     if ((rc = run_gemv(p1, s))) return rc;
 
     // ---- 2: the mixer
@@ -180,6 +185,7 @@ int qwen35_step(const BtQwen35Model& m, const BtQwen35Runtime& rt, int with_logi
       g.scale = 1.0f / sqrtf(static_cast<float>(d.ssm_state));
       g.eps = d.l2_eps;
       g.status = rt.status;
+      g.trace = trace();
       if ((rc = gdn_decode_launch(g, s, use_pdl()))) return rc;
     } else {
       AttnParams a{};
@@ -215,6 +221,7 @@ int qwen35_step(const BtQwen35Model& m, const BtQwen35Runtime& rt, int with_logi
       a.part = ws.attn_part;
       a.counters = ws.attn_counters;
       a.status = rt.status;
+      a.trace = trace();
       if ((rc = attention_launch(a, s, use_pdl()))) return rc;
     }
 
@@ -238,6 +245,7 @@ int qwen35_step(const BtQwen35Model& m, const BtQwen35Runtime& rt, int with_logi
       p3.k = d.n_heads * d.head_dim;
       p3.prologue = PRO_LOAD;
     }
+    p3.trace = trace();
     if ((rc = run_gemv(p3, s))) return rc;
 
     // ---- 4: gate/up with residual + RMSNorm in front, SiLU-gate behind
@@ -254,6 +262,7 @@ int qwen35_step(const BtQwen35Model& m, const BtQwen35Runtime& rt, int with_logi
     p4.epilogue = EPI_SILU_PAIR;
     p4.y = rt.act;
     p4.y_stride = d.ffn;
+    p4.trace = trace();
     if ((rc = run_gemv(p4, s))) return rc;
 
     // ---- 5: down
@@ -266,6 +275,7 @@ int qwen35_step(const BtQwen35Model& m, const BtQwen35Runtime& rt, int with_logi
     p5.epilogue = EPI_STORE;
     p5.y = rt.delta;
     p5.y_stride = d.hidden;
+    p5.trace = trace();
     if ((rc = run_gemv(p5, s))) return rc;
   }
 
@@ -302,6 +312,7 @@ int qwen35_step(const BtQwen35Model& m, const BtQwen35Runtime& rt, int with_logi
   ph.pos = rt.pos;
   ph.history = rt.history;
   ph.history_stride = d.max_ctx;
+  ph.trace = trace();
   return run_gemv(ph, s);
 }
 

@@ -426,6 +426,54 @@ class Qwen35:
             self._graphs[n_steps] = g
         return g
 
+    def trace_step(self, steps: int = 1) -> list[dict]:
+        """Device-side timeline of the last of ``steps`` decode steps, replayed
+        as one captured graph from the current state (which it advances).
+
+        Returns one dict per launch: name, start (first CTA entry), released
+        (last CTA past the dependency wait), ready (last CTA past its
+        prologue) and end (last CTA exit), in microseconds from the step's
+        first entry."""
+        n = int(self.lib.bt_qwen35_kernels_per_step(C.byref(self._dims)))
+        rec = torch.zeros(n, 8, dtype=torch.int64, device=self.device)
+        names = []
+        for i in range(self.cfg.n_layers):
+            if i in self.cfg.attn_layers:
+                names += [f"{i}.attn_in", f"{i}.attention", f"{i}.attn_out"]
+            else:
+                names += [f"{i}.gdn_in", f"{i}.gdn_step", f"{i}.gdn_out"]
+            names += [f"{i}.gate_up", f"{i}.down"]
+        names.append("head")
+        traced = N.BtQwen35Runtime.from_buffer_copy(self._rt)
+        traced.trace = rec.data_ptr()
+        handle = C.c_void_p()
+        self.stream.synchronize()
+        N.check(
+            self.lib.bt_qwen35_graph_create(C.byref(self._model), C.byref(traced), 1, self._sid(), C.byref(handle)),
+            "trace graph",
+        )
+        try:
+            for _ in range(steps):
+                with torch.cuda.stream(self.stream):
+                    rec[:, [0, 2, 5]] = -1  # all ones: unsigned max for the *_min fields
+                    rec[:, [1, 3, 4, 6, 7]] = 0
+                    N.check(self.lib.bt_graph_launch(handle.value, self._sid()), "trace replay")
+            self.stream.synchronize()
+        finally:
+            self.lib.bt_graph_destroy(handle.value)
+        r = rec.cpu().numpy().view(np.uint64)
+        t0 = int(r[:, 0].min())
+        out = []
+        for i, nm in enumerate(names):
+            out.append({
+                "name": nm,
+                "start": (int(r[i, 0]) - t0) / 1e3,
+                "released": (int(r[i, 3]) - t0) / 1e3,
+                "ready": (int(r[i, 4]) - t0) / 1e3,
+                "end": (int(r[i, 6]) - t0) / 1e3,
+            })
+        return out
+
     def replay(self, n_steps: int = 1) -> None:
         """Launch the captured n-step greedy graph (no host sync)."""
         N.check(self.lib.bt_graph_launch(self._graph(n_steps), self._sid()), "bt_graph_launch")

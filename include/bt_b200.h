@@ -189,12 +189,27 @@ typedef struct BtQwen35Runtime {
   float* mix;         /* (batch, max(ssm_inner, n_heads*head_dim)) mixer output */
   float* act;         /* (batch, ffn) silu(gate)*up */
   void* workspace;    /* bt_qwen35_workspace_bytes(), zeroed once */
+  void* trace;        /* optional timeline: bt_qwen35_kernels_per_step() records of
+                         BtTraceRecord, or NULL (no tracing) */
   int32_t* status;    /* BT_STATUS_WORDS device int32, zeroed by the caller: on a
                          device-side failure [0] = BT_ERR_TIMEOUT or
                          BT_ERR_INVALID, [1] = site, [2] = block, [3..5] =
                          site-specific detail; the first failure wins */
 } BtQwen35Runtime;
 
+/* One launch of the step as seen by the device-side tracer: %globaltimer
+ * nanoseconds folded over the launch's CTAs.  Set the *_min fields to
+ * UINT64_MAX and the others to 0 before a traced step. */
+typedef struct BtTraceRecord {
+  uint64_t entry_min, entry_max;   /* first / last CTA start                 */
+  uint64_t waited_min, waited_max; /* first / last CTA past the dependency wait */
+  uint64_t ready_max;              /* last CTA past its prologue             */
+  uint64_t exit_min, exit_max;     /* first / last CTA end                   */
+  uint64_t pad;
+} BtTraceRecord;
+
+/* Kernels one decode step launches (with logits): the trace record count. */
+BT_API int bt_qwen35_kernels_per_step(const BtQwen35Dims* dims);
 BT_API int64_t bt_qwen35_proj_elems(const BtQwen35Dims* dims);
 BT_API int64_t bt_qwen35_workspace_bytes(const BtQwen35Dims* dims);
 
