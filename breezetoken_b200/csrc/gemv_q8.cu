@@ -15,6 +15,7 @@ constexpr int64_t kPrefetchPiece = 16 * 1024;
 
 struct GemvTuning {
   int64_t prefetch_bytes = 64 * 1024;
+  int early_tile = 1;  // load the first register tile before the wait (BT_GEMV_EARLY_TILE)
 };
 
 int env_int(const char* name, int dflt) {
@@ -26,6 +27,7 @@ const GemvTuning& tuning() {
   static const GemvTuning t = [] {
     GemvTuning g;
     g.prefetch_bytes = static_cast<int64_t>(std::min(1024, std::max(0, env_int("BT_GEMV_PREFETCH_KB", 64)))) * 1024;
+    g.early_tile = env_int("BT_GEMV_EARLY_TILE", 1) != 0;
     return g;
   }();
   return t;
@@ -368,13 +370,16 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_q8_kernel(const __grid_c
   }
   Tile<GR, J> A, B;
   int g = warp;
-  if (g < n_groups) load_tile<GR, J>(A, p, row0 + static_cast<int64_t>(g) * GR, min(GR, cta_rows - g * GR), lane, nchunks);
+  if (p.early_tile && g < n_groups)
+    load_tile<GR, J>(A, p, row0 + static_cast<int64_t>(g) * GR, min(GR, cta_rows - g * GR), lane, nchunks);
   pdl_launch_dependents();
 
   // ---- activations (after the wait)
   pdl_wait();
   trace_waited(p.trace);
   gemv_prologue<NV>(p, xd, sx, scratch);
+  if (!p.early_tile && g < n_groups)
+    load_tile<GR, J>(A, p, row0 + static_cast<int64_t>(g) * GR, min(GR, cta_rows - g * GR), lane, nchunks);
   __syncthreads();
   trace_ready(p.trace);
 
@@ -510,6 +515,7 @@ int gemv_q8_plan(GemvQ8Params& p, int sm_count, GemvQ8Launch& L) {
     return fail(BT_ERR_UNSUPPORTED, "SiLU-pair epilogue serves at most 2 vectors and K <= 1024");
   p.group_rows = gr;
   p.prefetch_bytes = tuning().prefetch_bytes;
+  p.early_tile = tuning().early_tile;
   L.grid = grid;
   L.threads = kGemvThreads;
   L.smem = GemvSmem::kHeader + gemv_x_layout(p.k, p.n_vec).total;

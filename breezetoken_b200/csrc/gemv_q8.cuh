@@ -54,6 +54,7 @@ struct GemvQ8Params {
   int32_t k, row_bytes, sb;  // K, bytes per row, scale bytes per row
   int32_t group_rows;        // rows per consumer task (1 or 4)
   int64_t prefetch_bytes;    // weight bytes per CTA prefetched into L2 before the wait
+  int32_t early_tile;        // load the first register tile before the wait
   int32_t n_vec;             // activation vectors (batch)
   // prologue
   int32_t prologue;
