@@ -118,6 +118,10 @@ _SIGS: dict[str, tuple[object, list]] = {
         C.c_int,
         [_P, _P, _P, C.c_int, _P, _P, _I64, _I64, _I64, _I64, _I64, C.c_float, C.c_int, _P, _P],
     ),
+    "bt_attention_decode_noalloc": (
+        C.c_int,
+        [_P, _P, _P, C.c_int, _P, _P, _I64, _I64, _I64, _I64, _I64, C.c_float, C.c_int, _P],
+    ),
     "bt_gdn_decode": (C.c_int, [_P, _P, _P, C.c_int, _P, _P, _P, _P, _I64, _I64, _I64, _I64, C.c_float, C.c_float, _P]),
     "bt_argmax_workspace_bytes": (_I64, [_I64]),
     "bt_argmax": (C.c_int, [_P, _I64, _I64, _P, _P, _P]),

@@ -124,6 +124,29 @@ BT_API int bt_attention_decode(const float* q, const void* k, const void* v,
                         int64_t dim, int64_t cap, float scale, int splits,
                         void* workspace, void* stream);
 
+/* bt_attention_decode without a caller workspace, for callers that cannot
+ * allocate device memory at call time (a pre-sized arena or memory pool that
+ * owns every allocation, or a binding that only holds the buffers it was
+ * handed).  No counterpart in the reference: it is an addition of this
+ * library.  The split partials and merge counters live in one static device
+ * array of BT_NOALLOC_ATTN_SCRATCH_BYTES bytes that every GPU loading the
+ * library holds until the process exits; shapes needing more
+ * (4*batch*kv_heads*splits*(heads/kv_heads)*(dim+2) bytes rounded up to 256,
+ * plus 4*batch*kv_heads) are rejected with BT_ERR_INVALID.  The first call on
+ * a device looks up the array's device address (cudaGetSymbolAddress with
+ * that device current), so make that first call before any stream capture.
+ * All calls on a device share that device's array and it keeps the last
+ * call's contents: calls whose kernels overlap on the same GPU (for example
+ * on two streams) race on it, so the caller must serialise them.  The call
+ * allocates nothing; it clears the merge counters with an asynchronous
+ * memset on `stream` before the kernel.                                    */
+#define BT_NOALLOC_ATTN_SCRATCH_BYTES (8 * 1024 * 1024)
+BT_API int bt_attention_decode_noalloc(const float* q, const void* k, const void* v,
+                                       int kv_dtype, const int32_t* lens, float* out,
+                                       int64_t batch, int64_t heads, int64_t kv_heads,
+                                       int64_t dim, int64_t cap, float scale, int splits,
+                                       void* stream);
+
 /* Backend.gdn_decode (backends.py:241-271): one gated-delta-rule step.
  *   q,k: (batch, heads_k, dim), v: (batch, heads_v, dim) in in_dtype
  *   g (log decay), beta (logits): (batch, heads_v) f32
