@@ -21,8 +21,12 @@
 // (model/layers.py:55-82 / graph.py:35-64): per-head q/k RMSNorm, partial
 // rotate-half RoPE at the device position, the KV-cache write at that
 // position and the sigmoid output gate.
+#include <cooperative_groups.h>
+
 #include "attention.cuh"
 #include "errors.h"
+
+namespace cg = cooperative_groups;
 
 namespace bt {
 
@@ -88,11 +92,15 @@ struct KvRow<__nv_bfloat16, 4> {
   }
 };
 
-template <typename KV, int DPL, int GS>
+// CL = the splits of one (sequence, group) form a thread-block cluster and
+// merge through distributed shared memory instead of the global workspace.
+template <typename KV, int DPL, int GS, bool CL>
 __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const __grid_constant__ AttnParams p) {
   constexpr int DIM = DPL * 32;
   constexpr int PB = 32 / GS;
   __shared__ __align__(16) float qs[GS][DIM];
+  __shared__ __align__(16) float cpo[CL ? GS : 1][CL ? DIM : 1];  // this CTA's merged partial (cluster mode)
+  __shared__ float cm[GS], cl[GS];
   __shared__ __align__(16) float kvn[2][DIM];
   __shared__ float wm[kAttnWarps][GS], wl[kAttnWarps][GS];
   __shared__ __align__(16) float wacc[kAttnWarps][GS][DIM];
@@ -112,8 +120,10 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const __grid_
   }
   // Only as many splits as keep >= kMinSplitLen positions each take part; the
   // others leave at once and are not counted by the merge ticket.
-  const int splits = max(1, min(p.splits, (L + kMinSplitLen - 1) / kMinSplitLen));
-  if (split >= splits) return;
+  // (in cluster mode every CTA of the cluster takes part, possibly with no
+  // positions, because all of them meet at the cluster barriers)
+  const int splits = CL ? p.splits : max(1, min(p.splits, (L + kMinSplitLen - 1) / kMinSplitLen));
+  if (!CL && split >= splits) return;
   const int chunk = (L + splits - 1) / splits;
   const int t0 = min(L, split * chunk), t1 = min(L, t0 + chunk);
 
@@ -128,11 +138,20 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const __grid_
       float* dst = item < GS ? qs[item] : kvn[item - GS];
       const float* src = item < GS ? p.q + static_cast<int64_t>(b) * p.q_bs + static_cast<int64_t>(g * GS + item) * p.q_hs
                                    : (item == GS ? p.k_new : p.v_new) + static_cast<int64_t>(b) * p.q_bs + g * DIM;
-      float x[DPL];
+      // every load of the item (values, norm weights, RoPE row) in flight at once
+      const float* nw = item < GS ? p.q_norm : p.k_norm;
+      const float* crow = p.rope_cos + static_cast<int64_t>(pos) * p.rope_dim;
+      const float* srow = p.rope_sin + static_cast<int64_t>(pos) * p.rope_dim;
+      float x[DPL], nwv[DPL], cv[DPL], sv[DPL];
 #pragma unroll
-      for (int i = 0; i < DPL; ++i) x[i] = src[lane * DPL + i];
+      for (int i = 0; i < DPL; ++i) {
+        const int d = lane * DPL + i, dc = min(d, p.rope_dim - 1);
+        x[i] = src[d];
+        nwv[i] = nw[d];
+        cv[i] = crow[dc];
+        sv[i] = srow[dc];
+      }
       if (item <= GS) {
-        const float* nw = item < GS ? p.q_norm : p.k_norm;
         float ss = 0.f;
 #pragma unroll
         for (int i = 0; i < DPL; ++i) ss = fmaf(x[i], x[i], ss);
@@ -140,7 +159,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const __grid_
         const float r = 1.0f / sqrtf(ss / static_cast<float>(DIM) + p.eps);
 #pragma unroll
         for (int i = 0; i < DPL; ++i) {
-          x[i] = __fmul_rn(__fmul_rn(x[i], r), nw[lane * DPL + i]);
+          x[i] = __fmul_rn(__fmul_rn(x[i], r), nwv[i]);
           dst[lane * DPL + i] = x[i];
         }
         __syncwarp();
@@ -149,10 +168,8 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const __grid_
         for (int i = 0; i < DPL; ++i) {
           const int d = lane * DPL + i;
           if (d < p.rope_dim) {
-            const float c = p.rope_cos[static_cast<int64_t>(pos) * p.rope_dim + d];
-            const float s = p.rope_sin[static_cast<int64_t>(pos) * p.rope_dim + d];
             const float partner = d < half ? -dst[d + half] : dst[d - half];
-            x[i] = __fadd_rn(__fmul_rn(x[i], c), __fmul_rn(partner, s));
+            x[i] = __fadd_rn(__fmul_rn(x[i], cv[i]), __fmul_rn(partner, sv[i]));
           }
         }
         __syncwarp();
@@ -253,6 +270,55 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const __grid_
 #pragma unroll
     for (int i = 0; i < DPL; ++i) wacc[warp][h][lane * DPL + i] = acc[h][i];
   __syncthreads();
+
+  if constexpr (CL) {
+    // ---------------- cluster merge: partials stay in shared memory
+    for (int e = threadIdx.x; e < GS * DIM; e += kAttnThreads) {
+      const int h = e / DIM, d = e % DIM;
+      float M = -INFINITY;
+#pragma unroll
+      for (int w = 0; w < kAttnWarps; ++w) M = fmaxf(M, wm[w][h]);
+      float Ls = 0.f, O = 0.f;
+#pragma unroll
+      for (int w = 0; w < kAttnWarps; ++w) {
+        if (wm[w][h] != -INFINITY) {
+          const float f = exp2f(wm[w][h] - M);
+          Ls = fmaf(wl[w][h], f, Ls);
+          O = fmaf(wacc[w][h][d], f, O);
+        }
+      }
+      cpo[h][d] = O;
+      if (d == 0) {
+        cm[h] = M;
+        cl[h] = Ls;
+      }
+    }
+    cg::cluster_group cluster = cg::this_cluster();
+    cluster.sync();
+    // rank r finishes elements [r*per, (r+1)*per) reading every rank's partial
+    const int per = (GS * DIM + splits - 1) / splits;
+    for (int e = split * per + threadIdx.x; e < min(GS * DIM, (split + 1) * per); e += kAttnThreads) {
+      const int h = e / DIM, d = e % DIM;
+      float M = -INFINITY;
+      for (int s2 = 0; s2 < splits; ++s2) M = fmaxf(M, cluster.map_shared_rank(cm, s2)[h]);
+      float Ls = 0.f, O = 0.f;
+      for (int s2 = 0; s2 < splits; ++s2) {
+        const float ms = cluster.map_shared_rank(cm, s2)[h];
+        if (ms != -INFINITY) {
+          const float f = exp2f(ms - M);
+          Ls = fmaf(cluster.map_shared_rank(cl, s2)[h], f, Ls);
+          O = fmaf(cluster.map_shared_rank(&cpo[0][0], s2)[h * DIM + d], f, O);
+        }
+      }
+      float o = Ls > 0.f ? O / Ls : 0.f;
+      if (p.model)
+        o *= sigmoid_f(p.gate[static_cast<int64_t>(b) * p.q_bs + static_cast<int64_t>(g * GS + h) * p.q_hs + d]);
+      p.out[static_cast<int64_t>(b) * p.out_bs + static_cast<int64_t>(g * GS + h) * DIM + d] = o;
+    }
+    cluster.sync();  // no CTA leaves while others still read its shared memory
+    trace_exit(p.trace);
+    return;
+  }
 
   // records of this (sequence, group): split s, head h at rec0 + s*GS + h
   const int64_t rec0 = ((static_cast<int64_t>(b) * p.kv_heads + g) * p.splits) * GS;
@@ -358,12 +424,25 @@ int launch_t(const AttnParams& p, cudaStream_t stream, bool pdl) {
   cfg.gridDim = dim3(p.splits, p.kv_heads, p.batch);
   cfg.blockDim = dim3(kAttnThreads);
   cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchAttribute attr[2];
+  int n = 0;
+  if (pdl) {
+    attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[n].val.programmaticStreamSerializationAllowed = 1;
+    ++n;
+  }
+  const bool cl = p.cluster && GS == 4;
+  if (cl) {
+    attr[n].id = cudaLaunchAttributeClusterDimension;
+    attr[n].val.clusterDim.x = p.splits;
+    attr[n].val.clusterDim.y = 1;
+    attr[n].val.clusterDim.z = 1;
+    ++n;
+  }
   cfg.attrs = attr;
-  cfg.numAttrs = pdl ? 1 : 0;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, attn_decode_kernel<KV, DPL, GS>, p);
+  cfg.numAttrs = n;
+  cudaError_t e = cl ? cudaLaunchKernelEx(&cfg, attn_decode_kernel<KV, DPL, GS, (GS == 4)>, p)
+                     : cudaLaunchKernelEx(&cfg, attn_decode_kernel<KV, DPL, GS, false>, p);
   if (e != cudaSuccess) return fail_cuda(e, "attention launch");
   return BT_OK;
 }
@@ -392,8 +471,10 @@ int attention_launch(const AttnParams& p, cudaStream_t stream, bool pdl) {
     return fail(BT_ERR_INVALID, "attention: K/V must be 16-byte aligned (vector loads)");
   if ((p.kv_ts * (p.kv_dtype == BT_BF16 ? 2 : 4)) % 16 || (p.kv_bs * (p.kv_dtype == BT_BF16 ? 2 : 4)) % 16)
     return fail(BT_ERR_INVALID, "attention: K/V strides must be multiples of 16 bytes");
-  if (p.model && (p.rope_dim < 0 || p.rope_dim > p.dim || p.rope_dim % 2))
+  if (p.model && (p.rope_dim < 2 || p.rope_dim > p.dim || p.rope_dim % 2))
     return fail(BT_ERR_INVALID, "attention: invalid rope_dim %d", p.rope_dim);
+  if (p.cluster && (p.splits > 8 || p.heads != 4 * p.kv_heads))
+    return fail(BT_ERR_UNSUPPORTED, "cluster-merged attention serves <= 8 splits and 4 query heads per KV head");
   return p.kv_dtype == BT_BF16 ? launch_dtype<__nv_bfloat16>(p, stream, pdl) : launch_dtype<float>(p, stream, pdl);
 }
 

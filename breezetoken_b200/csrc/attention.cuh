@@ -21,6 +21,7 @@ struct AttnParams {
   float* out;
   int64_t out_bs;
   int32_t batch, heads, kv_heads, dim, cap, splits;
+  int32_t cluster;  // 1: the splits of a (sequence, group) form a cluster and merge in DSMEM
   float scale;
   // model mode (Qwen3.5 full-attention layer, model/layers.py:55-82):
   // q/k RMSNorm, partial RoPE at pos, KV-cache write at pos, sigmoid gate.

@@ -64,49 +64,61 @@ __device__ __forceinline__ uint32_t pack4(int a, int b, int c, int d) {
          ((static_cast<uint32_t>(c) & 255u) << 16) | ((static_cast<uint32_t>(d) & 255u) << 24);
 }
 
-template <int NV>
+template <int NV, int NIT>
 __device__ void gemv_prologue(const GemvQ8Params& p, uint8_t* xd, float* sx, float* scratch) {
   const int tid = threadIdx.x, lane = tid & 31;
   const int K = p.k, nf4 = K >> 2, nb = K >> 5, J = (K + 511) / 512;
-  const int n_it = (nf4 + kConsumerThreads - 1) / kConsumerThreads;
+  const int n_it = NIT;
   const int64_t xbs = p.x_bs ? p.x_bs : K, x2bs = p.x2_bs ? p.x2_bs : K;
   const float4 zero4 = make_float4(0.f, 0.f, 0.f, 0.f);
   for (int v = 0; v < NV; ++v) {
-    float4 h[kMaxF4], a2[kMaxF4], w4[kMaxF4];
-    // ---- all loads first
+    float4 h[NIT], a2[NIT], w4[NIT];
+    // ---- all loads first, unconditionally: indices past the vector are
+    //      clamped onto its last float4 and zeroed afterwards, so the loads
+    //      carry no control dependence and are all in flight at once.
+    if (p.prologue == PRO_EMBED_NORM) {
+      int64_t tok = p.tokens[v];
+      if (tok < 0 || tok >= p.embed_rows) {
+        if (tid == 0) report_status(p.status, BT_ERR_INVALID, SITE_EMBED_TOKEN, static_cast<int32_t>(tok), v);
+        tok = 0;
+      }
+      const uint8_t* erow = p.embed + tok * static_cast<int64_t>(p.row_bytes);
+      uint32_t q[NIT];
+      float d[NIT];
 #pragma unroll
-    for (int i = 0; i < kMaxF4; ++i) {
-      const int f = tid + kConsumerThreads * i;
-      h[i] = a2[i] = w4[i] = zero4;
-      if (i < n_it && f < nf4) {
-        if (p.prologue == PRO_EMBED_NORM) {
-          int64_t tok = p.tokens[v];
-          if (tok < 0 || tok >= p.embed_rows) {
-            if (f == 0) report_status(p.status, BT_ERR_INVALID, SITE_EMBED_TOKEN, static_cast<int32_t>(tok), v);
-            tok = 0;
-          }
-          const uint8_t* erow = p.embed + tok * static_cast<int64_t>(p.row_bytes);
-          const float d = __half2float(reinterpret_cast<const __half*>(erow)[f >> 3]);
-          const uint32_t q = *reinterpret_cast<const uint32_t*>(erow + p.sb + 4 * f);
-          h[i] = make_float4(static_cast<float>(static_cast<int8_t>(q & 255)) * d,
-                             static_cast<float>(static_cast<int8_t>((q >> 8) & 255)) * d,
-                             static_cast<float>(static_cast<int8_t>((q >> 16) & 255)) * d,
-                             static_cast<float>(static_cast<int8_t>(q >> 24)) * d);
-        } else {
-          h[i] = reinterpret_cast<const float4*>(p.x + v * xbs)[f];
-          if (p.prologue != PRO_LOAD) a2[i] = reinterpret_cast<const float4*>(p.x2 + v * x2bs)[f];
-        }
-        if (p.prologue == PRO_RESID_NORM || p.prologue == PRO_EMBED_NORM)
-          w4[i] = reinterpret_cast<const float4*>(p.norm_w)[f];
-        else if (p.prologue == PRO_GATED_NORM)
-          w4[i] = reinterpret_cast<const float4*>(p.norm_w)[f % (p.group >> 2)];
+      for (int i = 0; i < NIT; ++i) {
+        const int fc = min(tid + kConsumerThreads * i, nf4 - 1);
+        d[i] = __half2float(reinterpret_cast<const __half*>(erow)[fc >> 3]);
+        q[i] = *reinterpret_cast<const uint32_t*>(erow + p.sb + 4 * fc);
+        w4[i] = reinterpret_cast<const float4*>(p.norm_w)[fc];
+      }
+#pragma unroll
+      for (int i = 0; i < NIT; ++i)
+        h[i] = make_float4(static_cast<float>(static_cast<int8_t>(q[i] & 255)) * d[i],
+                           static_cast<float>(static_cast<int8_t>((q[i] >> 8) & 255)) * d[i],
+                           static_cast<float>(static_cast<int8_t>((q[i] >> 16) & 255)) * d[i],
+                           static_cast<float>(static_cast<int8_t>(q[i] >> 24)) * d[i]);
+    } else {
+      const float4* x4 = reinterpret_cast<const float4*>(p.x + v * xbs);
+      const float4* x24 = reinterpret_cast<const float4*>(p.x2 + v * x2bs);
+      const float4* n4 = reinterpret_cast<const float4*>(p.norm_w);
+      const int gq = p.group >> 2;
+#pragma unroll
+      for (int i = 0; i < NIT; ++i) {
+        const int fc = min(tid + kConsumerThreads * i, nf4 - 1);
+        h[i] = x4[fc];
+        a2[i] = p.prologue != PRO_LOAD ? x24[fc] : zero4;
+        w4[i] = p.prologue == PRO_RESID_NORM ? n4[fc] : (p.prologue == PRO_GATED_NORM ? n4[fc % gq] : zero4);
       }
     }
+#pragma unroll
+    for (int i = 0; i < NIT; ++i)
+      if (tid + kConsumerThreads * i >= nf4) h[i] = a2[i] = w4[i] = zero4;
     // ---- residual add and normalisation
     if (p.prologue == PRO_RESID_NORM || p.prologue == PRO_EMBED_NORM) {
       float ss = 0.f;
 #pragma unroll
-      for (int i = 0; i < kMaxF4; ++i) {
+      for (int i = 0; i < NIT; ++i) {
         const int f = tid + kConsumerThreads * i;
         if (i < n_it && f < nf4) {
           if (p.prologue == PRO_RESID_NORM)
@@ -121,12 +133,12 @@ __device__ void gemv_prologue(const GemvQ8Params& p, uint8_t* xd, float* sx, flo
       const float total = group_sum<1>(ss, scratch, kConsumerWarps, kConsumerThreads);
       const float r = 1.0f / sqrtf(total / static_cast<float>(K) + p.eps);
 #pragma unroll
-      for (int i = 0; i < kMaxF4; ++i) h[i] = f4_mul(f4_scale(h[i], r), w4[i]);
+      for (int i = 0; i < NIT; ++i) h[i] = f4_mul(f4_scale(h[i], r), w4[i]);
     } else if (p.prologue == PRO_GATED_NORM) {
       // group of G elements = G/4 consecutive lanes of one warp
       const int lanes = p.group >> 2;
 #pragma unroll
-      for (int i = 0; i < kMaxF4; ++i) {
+      for (int i = 0; i < NIT; ++i) {
         if (i >= n_it) break;
         float ss = fmaf(h[i].x, h[i].x, fmaf(h[i].y, h[i].y, fmaf(h[i].z, h[i].z, h[i].w * h[i].w)));
         for (int o = lanes >> 1; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
@@ -137,7 +149,7 @@ __device__ void gemv_prologue(const GemvQ8Params& p, uint8_t* xd, float* sx, flo
     // ---- encode: block max over 8 lanes, digits from registers
     uint8_t* xdv = xd + static_cast<int64_t>(v) * J * 1536;
 #pragma unroll
-    for (int i = 0; i < kMaxF4; ++i) {
+    for (int i = 0; i < NIT; ++i) {
       if (i >= n_it) break;
       const int f = tid + kConsumerThreads * i;
       float m = fmaxf(fmaxf(fabsf(h[i].x), fabsf(h[i].y)), fmaxf(fabsf(h[i].z), fabsf(h[i].w)));
@@ -164,28 +176,60 @@ __device__ void gemv_prologue(const GemvQ8Params& p, uint8_t* xd, float* sx, flo
 }
 
 // ------------------------------------------------------------------ epilogue
-__device__ __forceinline__ void epilogue_row(const GemvQ8Params& p, int v, int64_t r, float a) {
+// Operands of the GDN in-projection epilogue for one row, loaded before the
+// row's dot products so their latency hides behind the math: the conv window
+// (taps <= 3) and conv weights (conv_k <= 4) of a qkv channel, or a_log and
+// dt_bias of an alpha row.
+struct EpiOperands {
+  float cs[3], cw[4], a_log, dt_bias;
+};
+
+__device__ __forceinline__ void epi_prefetch(const GemvQ8Params& p, int v, int64_t r, EpiOperands& o) {
+  if (r < p.n_conv) {
+    const int taps = p.conv_k - 1;
+    const float* cs = p.conv_state + (static_cast<int64_t>(v) * p.n_conv + r) * taps;
+    const float* cw = p.conv_w + r * p.conv_k;
+#pragma unroll
+    for (int t = 0; t < 3; ++t) o.cs[t] = t < taps ? cs[t] : 0.f;
+#pragma unroll
+    for (int t = 0; t < 4; ++t) o.cw[t] = t < p.conv_k ? cw[t] : 0.f;
+  } else if (r >= p.n_conv + p.n_z && r < p.n_conv + p.n_z + p.n_gh) {
+    const int h = static_cast<int>(r - p.n_conv - p.n_z);
+    o.a_log = p.a_log[h];
+    o.dt_bias = p.dt_bias[h];
+  }
+}
+
+__device__ __forceinline__ void epilogue_row(const GemvQ8Params& p, int v, int64_t r, float a,
+                                             const EpiOperands& o) {
   float* y = p.y + static_cast<int64_t>(v) * p.y_stride;
   if (p.epilogue == EPI_STORE) {
     y[r] = a;
     return;
   }
-  // EPI_GDN_IN
+  // EPI_GDN_IN: conv window + SiLU (model/layers.py:90-93), silu(z),
+  // g = a_log * softplus(alpha + dt_bias) (:99-103), beta logits as they are
   if (r < p.n_conv) {
     const int taps = p.conv_k - 1;
-    float* cs = p.conv_state + (static_cast<int64_t>(v) * p.n_conv + r) * taps;
-    const float* cw = p.conv_w + r * p.conv_k;
     float sum = 0.f;
-    for (int t = 0; t < taps; ++t) sum = __fadd_rn(sum, __fmul_rn(cs[t], cw[t]));
-    sum = __fadd_rn(sum, __fmul_rn(a, cw[taps]));
-    for (int t = 0; t + 1 < taps; ++t) cs[t] = cs[t + 1];
+#pragma unroll
+    for (int t = 0; t < 3; ++t)
+      if (t < taps) sum = __fadd_rn(sum, __fmul_rn(o.cs[t], o.cw[t]));
+    float last = 0.f;
+#pragma unroll
+    for (int t = 0; t < 4; ++t)
+      if (t == taps) last = o.cw[t];
+    sum = __fadd_rn(sum, __fmul_rn(a, last));
+    float* cs = p.conv_state + (static_cast<int64_t>(v) * p.n_conv + r) * taps;
+#pragma unroll
+    for (int t = 0; t < 3; ++t)
+      if (t + 1 < taps) cs[t] = o.cs[t + 1];
     cs[taps - 1] = a;
     y[r] = silu_f(sum);
   } else if (r < p.n_conv + p.n_z) {
     y[r] = silu_f(a);
   } else if (r < p.n_conv + p.n_z + p.n_gh) {
-    const int h = static_cast<int>(r - p.n_conv - p.n_z);
-    y[r] = p.a_log[h] * softplus_f(a + p.dt_bias[h]);
+    y[r] = o.a_log * softplus_f(a + o.dt_bias);
   } else {
     y[r] = a;
   }
@@ -248,11 +292,34 @@ __device__ __forceinline__ void load_tile(Tile<GR, J>& t, const GemvQ8Params& p,
   }
 }
 
+template <int NE>
+__device__ __forceinline__ void epilogue_late(const GemvQ8Params& p, int v, int64_t row, float c,
+                                              const EpiOperands (&eo)[NE]) {
+  if (NE > 1 || v == 0) {
+    epilogue_row(p, v, row, c, eo[NE > 1 ? v : 0]);
+  } else {
+    EpiOperands o;
+    if (p.epilogue == EPI_GDN_IN) epi_prefetch(p, v, row, o);
+    epilogue_row(p, v, row, c, o);
+  }
+}
+
 template <int NV, int GR, int J>
 __device__ __forceinline__ void process_tile(const Tile<GR, J>& t, const GemvQ8Params& p, int64_t r0, int nr,
                                              int lane, int nchunks, const uint4* xd4, const float* sx,
                                              unsigned long long (&best)[NV]) {
   const int nb = p.k >> 5;
+  // epilogue operands of the row this lane will finish, in flight during the math
+  // (batches above 2 vectors load them at the epilogue instead: registers)
+  constexpr int NE = NV <= 2 ? NV : 1;
+  EpiOperands eo[NE];
+  if (NV <= 2 && p.epilogue == EPI_GDN_IN) {
+    const int my_r = GR == 4 ? (lane >> 3) : 0;
+    const bool mine = GR == 4 ? (lane & 7) == 0 : lane == 0;
+    if (mine && my_r < nr)
+#pragma unroll
+      for (int v = 0; v < NE; ++v) epi_prefetch(p, v, r0 + my_r, eo[v]);
+  }
   float acc[GR][NV];
 #pragma unroll
   for (int r = 0; r < GR; ++r)
@@ -307,7 +374,7 @@ __device__ __forceinline__ void process_tile(const Tile<GR, J>& t, const GemvQ8P
           const unsigned long long key = argmax_key(c, row);
           best[v] = key > best[v] ? key : best[v];
         } else {
-          epilogue_row(p, v, row, c);
+          epilogue_late(p, v, row, c, eo);
         }
       }
     }
@@ -324,7 +391,7 @@ __device__ __forceinline__ void process_tile(const Tile<GR, J>& t, const GemvQ8P
             const unsigned long long key = argmax_key(c, row);
             best[v] = key > best[v] ? key : best[v];
           } else {
-            epilogue_row(p, v, row, c);
+            epilogue_late(p, v, row, c, eo);
           }
         }
       }
@@ -377,7 +444,7 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_q8_kernel(const __grid_c
   // ---- activations (after the wait)
   pdl_wait();
   trace_waited(p.trace);
-  gemv_prologue<NV>(p, xd, sx, scratch);
+  gemv_prologue<NV, (J > 1 ? J / 2 : 1)>(p, xd, sx, scratch);
   if (!p.early_tile && g < n_groups)
     load_tile<GR, J>(A, p, row0 + static_cast<int64_t>(g) * GR, min(GR, cta_rows - g * GR), lane, nchunks);
   __syncthreads();

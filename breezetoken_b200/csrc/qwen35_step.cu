@@ -64,7 +64,7 @@ int validate(const BtQwen35Dims& d) {
   if (d.n_layers < 1 || d.hidden < 32 || d.hidden % 32) return fail(BT_ERR_INVALID, "bad hidden/layers");
   if (d.ssm_heads * d.ssm_state != d.ssm_inner) return fail(BT_ERR_INVALID, "ssm heads * state != inner");
   if (d.n_heads % d.n_kv) return fail(BT_ERR_INVALID, "n_heads must be a multiple of n_kv");
-  if (d.conv_k < 2) return fail(BT_ERR_INVALID, "conv kernel must be >= 2");
+  if (d.conv_k < 2 || d.conv_k > 4) return fail(BT_ERR_UNSUPPORTED, "conv kernel must be in [2, 4]");
   return BT_OK;
 }
 
@@ -209,6 +209,7 @@ int qwen35_step(const BtQwen35Model& m, const BtQwen35Runtime& rt, int with_logi
       a.dim = d.head_dim;
       a.cap = d.max_ctx;
       a.splits = kAttnSplits;
+      a.cluster = (d.n_heads == 4 * d.n_kv) ? 1 : 0;
       a.scale = 1.0f / sqrtf(static_cast<float>(d.head_dim));
       a.model = 1;
       a.pos = rt.pos;
