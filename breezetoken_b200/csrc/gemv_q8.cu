@@ -106,14 +106,26 @@ __device__ void gemv_prologue(const GemvQ8Params& p, uint8_t* xd, float* sx, flo
 #pragma unroll
       for (int i = 0; i < NIT; ++i) {
         const int fc = min(tid + kConsumerThreads * i, nf4 - 1);
-        h[i] = x4[fc];
-        a2[i] = p.prologue != PRO_LOAD ? x24[fc] : zero4;
+        if (p.prologue == PRO_SILU_PAIR) {
+          // interleaved (gate, up) pairs: float4s 2fc and 2fc+1 give x[4fc .. 4fc+3]
+          h[i] = x4[2 * fc];
+          a2[i] = x4[2 * fc + 1];
+        } else {
+          h[i] = x4[fc];
+          a2[i] = p.prologue != PRO_LOAD ? x24[fc] : zero4;
+        }
         w4[i] = p.prologue == PRO_RESID_NORM ? n4[fc] : (p.prologue == PRO_GATED_NORM ? n4[fc % gq] : zero4);
       }
     }
 #pragma unroll
     for (int i = 0; i < NIT; ++i)
       if (tid + kConsumerThreads * i >= nf4) h[i] = a2[i] = w4[i] = zero4;
+    if (p.prologue == PRO_SILU_PAIR) {
+#pragma unroll
+      for (int i = 0; i < NIT; ++i)
+        h[i] = make_float4(silu_f(h[i].x) * h[i].y, silu_f(h[i].z) * h[i].w, silu_f(a2[i].x) * a2[i].y,
+                           silu_f(a2[i].z) * a2[i].w);
+    }
     // ---- residual add and normalisation
     if (p.prologue == PRO_RESID_NORM || p.prologue == PRO_EMBED_NORM) {
       float ss = 0.f;
@@ -292,11 +304,13 @@ __device__ __forceinline__ void load_tile(Tile<GR, J>& t, const GemvQ8Params& p,
   }
 }
 
-template <int NE>
+// EPF: the GDN in-projection epilogue with its operands loaded before the
+// math (batches of <= 2 vectors); otherwise they are loaded here.
+template <bool EPF, int NE>
 __device__ __forceinline__ void epilogue_late(const GemvQ8Params& p, int v, int64_t row, float c,
                                               const EpiOperands (&eo)[NE]) {
-  if (NE > 1 || v == 0) {
-    epilogue_row(p, v, row, c, eo[NE > 1 ? v : 0]);
+  if constexpr (EPF) {
+    epilogue_row(p, v, row, c, eo[v]);
   } else {
     EpiOperands o;
     if (p.epilogue == EPI_GDN_IN) epi_prefetch(p, v, row, o);
@@ -304,16 +318,15 @@ __device__ __forceinline__ void epilogue_late(const GemvQ8Params& p, int v, int6
   }
 }
 
-template <int NV, int GR, int J>
+template <int NV, int GR, int J, bool EPF>
 __device__ __forceinline__ void process_tile(const Tile<GR, J>& t, const GemvQ8Params& p, int64_t r0, int nr,
                                              int lane, int nchunks, const uint4* xd4, const float* sx,
                                              unsigned long long (&best)[NV]) {
   const int nb = p.k >> 5;
   // epilogue operands of the row this lane will finish, in flight during the math
-  // (batches above 2 vectors load them at the epilogue instead: registers)
-  constexpr int NE = NV <= 2 ? NV : 1;
+  constexpr int NE = EPF ? NV : 1;
   EpiOperands eo[NE];
-  if (NV <= 2 && p.epilogue == EPI_GDN_IN) {
+  if constexpr (EPF) {
     const int my_r = GR == 4 ? (lane >> 3) : 0;
     const bool mine = GR == 4 ? (lane & 7) == 0 : lane == 0;
     if (mine && my_r < nr)
@@ -374,7 +387,7 @@ __device__ __forceinline__ void process_tile(const Tile<GR, J>& t, const GemvQ8P
           const unsigned long long key = argmax_key(c, row);
           best[v] = key > best[v] ? key : best[v];
         } else {
-          epilogue_late(p, v, row, c, eo);
+          epilogue_late<EPF>(p, v, row, c, eo);
         }
       }
     }
@@ -391,7 +404,7 @@ __device__ __forceinline__ void process_tile(const Tile<GR, J>& t, const GemvQ8P
             const unsigned long long key = argmax_key(c, row);
             best[v] = key > best[v] ? key : best[v];
           } else {
-            epilogue_late(p, v, row, c, eo);
+            epilogue_late<EPF>(p, v, row, c, eo);
           }
         }
       }
@@ -404,7 +417,7 @@ __device__ __forceinline__ void process_tile(const Tile<GR, J>& t, const GemvQ8P
 // group g+8 are in flight while group g is computed).  Before the dependency
 // wait the CTA prefetches the head of its weight slice into L2 and loads its
 // first groups into registers: weights never depend on earlier kernels.
-template <int NV, int GR, int J>
+template <int NV, int GR, int J, bool EPF>
 __global__ void __launch_bounds__(kGemvThreads, 2) gemv_q8_kernel(const __grid_constant__ GemvQ8Params p) {
   extern __shared__ __align__(128) uint8_t smem[];
   float* scratch = reinterpret_cast<float*>(smem);
@@ -457,12 +470,12 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_q8_kernel(const __grid_c
   while (g < n_groups) {
     int gn = g + kConsumerWarps;
     if (gn < n_groups) load_tile<GR, J>(B, p, row0 + static_cast<int64_t>(gn) * GR, min(GR, cta_rows - gn * GR), lane, nchunks);
-    process_tile<NV, GR, J>(A, p, row0 + static_cast<int64_t>(g) * GR, min(GR, cta_rows - g * GR), lane, nchunks, xd4, sx, best);
+    process_tile<NV, GR, J, EPF>(A, p, row0 + static_cast<int64_t>(g) * GR, min(GR, cta_rows - g * GR), lane, nchunks, xd4, sx, best);
     g = gn;
     if (g >= n_groups) break;
     gn = g + kConsumerWarps;
     if (gn < n_groups) load_tile<GR, J>(A, p, row0 + static_cast<int64_t>(gn) * GR, min(GR, cta_rows - gn * GR), lane, nchunks);
-    process_tile<NV, GR, J>(B, p, row0 + static_cast<int64_t>(g) * GR, min(GR, cta_rows - g * GR), lane, nchunks, xd4, sx, best);
+    process_tile<NV, GR, J, EPF>(B, p, row0 + static_cast<int64_t>(g) * GR, min(GR, cta_rows - g * GR), lane, nchunks, xd4, sx, best);
     g = gn;
   }
 
@@ -509,9 +522,9 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_q8_kernel(const __grid_c
   trace_exit(p.trace);
 }
 
-template <int NV, int GR, int J>
+template <int NV, int GR, int J, bool EPF>
 int launch_impl(const GemvQ8Params& p, const GemvQ8Launch& L, cudaStream_t stream, bool pdl) {
-  auto kern = gemv_q8_kernel<NV, GR, J>;
+  auto kern = gemv_q8_kernel<NV, GR, J, EPF>;
   static int configured_device = -1;
   int dev = 0;
   cudaGetDevice(&dev);
@@ -535,14 +548,14 @@ int launch_impl(const GemvQ8Params& p, const GemvQ8Launch& L, cudaStream_t strea
   return BT_OK;
 }
 
-template <int NV, int GR>
+template <int NV, int GR, bool EPF = false>
 int launch_j(const GemvQ8Params& p, const GemvQ8Launch& L, cudaStream_t stream, bool pdl) {
   const int J = (p.k + 511) / 512;
-  if (J <= 1) return launch_impl<NV, GR, 1>(p, L, stream, pdl);
-  if (J <= 2) return launch_impl<NV, GR, 2>(p, L, stream, pdl);
+  if (J <= 1) return launch_impl<NV, GR, 1, EPF>(p, L, stream, pdl);
+  if (J <= 2) return launch_impl<NV, GR, 2, EPF>(p, L, stream, pdl);
   if constexpr (GR == 1) {
-    if (J <= 4) return launch_impl<NV, GR, 4>(p, L, stream, pdl);
-    return launch_impl<NV, GR, 8>(p, L, stream, pdl);
+    if (J <= 4) return launch_impl<NV, GR, 4, EPF>(p, L, stream, pdl);
+    return launch_impl<NV, GR, 8, EPF>(p, L, stream, pdl);
   }
   return fail(BT_ERR_UNSUPPORTED, "q8 GEMV: 4-row groups serve K <= 1024");
 }
@@ -567,6 +580,7 @@ int gemv_q8_plan(GemvQ8Params& p, int sm_count, GemvQ8Launch& L) {
       return fail(BT_ERR_INVALID, "q8 GEMV activations must be 16-byte aligned with strides a multiple of 4");
     if (p.prologue == PRO_GATED_NORM && p.group != 64 && p.group != 128)
       return fail(BT_ERR_UNSUPPORTED, "gated-norm prologue serves groups of 64 or 128, got %d", p.group);
+    if (p.prologue == PRO_SILU_PAIR && p.x_bs == 0) p.x_bs = 2LL * p.k;
   }
   p.sb = static_cast<int32_t>(bt_q8_row_bytes(p.k) - p.k);
   p.row_bytes = static_cast<int32_t>(bt_q8_row_bytes(p.k));
@@ -590,10 +604,14 @@ int gemv_q8_plan(GemvQ8Params& p, int sm_count, GemvQ8Launch& L) {
 }
 
 int gemv_q8_launch(const GemvQ8Params& p, const GemvQ8Launch& L, cudaStream_t stream, bool pdl) {
-  const bool g4 = p.group_rows == 4;
+  const bool g4 = p.group_rows == 4, epf = p.epilogue == EPI_GDN_IN;
   switch (p.n_vec) {
-    case 1: return g4 ? launch_j<1, 4>(p, L, stream, pdl) : launch_j<1, 1>(p, L, stream, pdl);
-    case 2: return g4 ? launch_j<2, 4>(p, L, stream, pdl) : launch_j<2, 1>(p, L, stream, pdl);
+    case 1:
+      if (epf) return g4 ? launch_j<1, 4, true>(p, L, stream, pdl) : launch_j<1, 1, true>(p, L, stream, pdl);
+      return g4 ? launch_j<1, 4>(p, L, stream, pdl) : launch_j<1, 1>(p, L, stream, pdl);
+    case 2:
+      if (epf) return g4 ? launch_j<2, 4, true>(p, L, stream, pdl) : launch_j<2, 1, true>(p, L, stream, pdl);
+      return g4 ? launch_j<2, 4>(p, L, stream, pdl) : launch_j<2, 1>(p, L, stream, pdl);
     case 4: return launch_j<4, 1>(p, L, stream, pdl);
     default: return launch_j<8, 1>(p, L, stream, pdl);
   }

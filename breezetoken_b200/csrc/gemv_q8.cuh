@@ -39,6 +39,7 @@ enum GemvPrologue : int {
   PRO_RESID_NORM = 1,  // h = h_in + delta -> h_out (CTA 0); x = rmsnorm(h) * w
   PRO_EMBED_NORM = 2,  // h = dequant(embed[token]) -> h_out (CTA 0); x = rmsnorm(h) * w
   PRO_GATED_NORM = 3,  // x = rmsnorm_per_group(o) * w[k % group] * silu_z
+  PRO_SILU_PAIR = 4,   // src = (gate_0, up_0, gate_1, up_1, ...): x[j] = silu(gate_j) * up_j
 };
 
 enum GemvEpilogue : int {

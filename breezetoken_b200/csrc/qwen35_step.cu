@@ -260,9 +260,12 @@ int qwen35_step(const BtQwen35Model& m, const BtQwen35Runtime& rt, int with_logi
     p4.h_out = ho;
     std::swap(hc, ho);
     p4.norm_w = ly.norm_post;
-    p4.epilogue = EPI_SILU_PAIR;
+    // batches of <= 2 pair gate/up rows in the epilogue (4-row groups);
+    // wider batches store them interleaved and the down projection pairs them
+    const bool pair_late = d.batch > 2;
+    p4.epilogue = pair_late ? EPI_STORE : EPI_SILU_PAIR;
     p4.y = rt.act;
-    p4.y_stride = d.ffn;
+    p4.y_stride = pair_late ? 2LL * d.ffn : d.ffn;
     p4.trace = trace();
     if ((rc = run_gemv(p4, s))) return rc;
 
@@ -271,8 +274,9 @@ int qwen35_step(const BtQwen35Model& m, const BtQwen35Runtime& rt, int with_logi
     p5.w = static_cast<const uint8_t*>(ly.w_down);
     p5.n_rows = d.hidden;
     p5.k = d.ffn;
-    p5.prologue = PRO_LOAD;
+    p5.prologue = pair_late ? PRO_SILU_PAIR : PRO_LOAD;
     p5.x = rt.act;
+    p5.x_bs = pair_late ? 2LL * d.ffn : d.ffn;
     p5.epilogue = EPI_STORE;
     p5.y = rt.delta;
     p5.y_stride = d.hidden;

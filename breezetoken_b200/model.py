@@ -277,7 +277,7 @@ class Qwen35:
         self.delta = torch.zeros(B, cfg.hidden, **f32)
         self.proj = torch.zeros(B, proj, **f32)
         self.mix = torch.zeros(B, mix, **f32)
-        self.act = torch.zeros(B, cfg.ffn, **f32)
+        self.act = torch.zeros(B, 2 * cfg.ffn, **f32)
         self.workspace = torch.zeros(int(self.lib.bt_qwen35_workspace_bytes(C.byref(d))), dtype=torch.uint8, device=dev)
         self.status = torch.zeros(N.BT_STATUS_WORDS, dtype=torch.int32, device=dev)
         attn = set(cfg.attn_layers)

@@ -210,7 +210,7 @@ typedef struct BtQwen35Runtime {
   float* delta;       /* (batch, hidden) mixer / mlp output */
   float* proj;        /* (batch, bt_qwen35_proj_elems) in-projection outputs */
   float* mix;         /* (batch, max(ssm_inner, n_heads*head_dim)) mixer output */
-  float* act;         /* (batch, ffn) silu(gate)*up */
+  float* act;         /* (batch, 2*ffn): silu(gate)*up, or (gate, up) pairs when batch > 2 */
   void* workspace;    /* bt_qwen35_workspace_bytes(), zeroed once */
   void* trace;        /* optional timeline: bt_qwen35_kernels_per_step() records of
                          BtTraceRecord, or NULL (no tracing) */

@@ -63,20 +63,22 @@ def test_tiny_graph_burst_equals_stepwise(tiny) -> None:
     assert burst == g["tokens"].tolist()
 
 
-def test_tiny_batch_lockstep(cuda, tiny_gguf) -> None:
-    """Sequences decoded together in one step match each decoded alone."""
+@pytest.mark.parametrize("batch", [2, 4, 8])
+def test_tiny_batch_lockstep(cuda, tiny_gguf, batch) -> None:
+    """Sequences decoded together in one step match each decoded alone
+    (every batch width the step serves: the GEMV specialises per width)."""
     g = golden("qwen35_tiny")
     p0 = g["prompt"].tolist()
     rng = np.random.default_rng(9)
-    p1 = rng.integers(0, 8192, len(p0)).tolist()
+    prompts = [p0] + [rng.integers(0, 8192, len(p0)).tolist() for _ in range(batch - 1)]
     m1 = Qwen35(tiny_gguf, max_context=256)
-    solo = [m1.decode_greedy([p], 12)[0] for p in (p0, p1)]
+    solo = [m1.decode_greedy([p], 12)[0] for p in prompts]
     m1.close()
-    m2 = Qwen35(tiny_gguf, max_context=256, batch=2)
-    both = m2.decode_greedy([p0, p1], 12)
-    m2.close()
-    assert both == solo
-    assert both[0] == g["tokens"][:12].tolist()
+    mb = Qwen35(tiny_gguf, max_context=256, batch=batch)
+    together = mb.decode_greedy(prompts, 12)
+    mb.close()
+    assert together == solo
+    assert together[0] == g["tokens"][:12].tolist()
 
 
 def test_invalid_inputs_raise(tiny) -> None:
