@@ -41,7 +41,7 @@ constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s
 // dependency wait, last CTA past its prologue, first/last CTA exit).  Off
 // (null) in normal runs; the layout matches BtTraceRecord in bt_b200.h.
 struct TraceRec {
-  unsigned long long entry_min, entry_max, waited_min, waited_max, ready_max, exit_min, exit_max, pad;
+  unsigned long long entry_min, entry_max, waited_min, waited_max, ready_max, exit_min, exit_max, loaded_max;
 };
 __device__ __forceinline__ void trace_entry(TraceRec* t) {
   if (t && threadIdx.x == 0) {
@@ -56,6 +56,11 @@ __device__ __forceinline__ void trace_waited(TraceRec* t) {
     atomicMin(&t->waited_min, now);
     atomicMax(&t->waited_max, now);
   }
+}
+// `dep` is a value computed from the loads being timed; the branch on it
+// orders the timer read after their arrival.
+__device__ __forceinline__ void trace_loaded(TraceRec* t, float dep) {
+  if (t && threadIdx.x == 0 && __float_as_uint(dep) != 0x7fbadbadu) atomicMax(&t->loaded_max, global_ns());
 }
 __device__ __forceinline__ void trace_ready(TraceRec* t) {
   if (t && threadIdx.x == 0) atomicMax(&t->ready_max, global_ns());

@@ -15,7 +15,7 @@
 //    the head of its weight slice into L2 (cp.async.bulk.prefetch) and loads
 //    its first groups into registers; weights never depend on earlier work;
 //  * after the wait the activation vector(s) are built in shared memory,
-//    encoded per 32-element block as three int8 digits of a 23-bit
+//    encoded per 32-element block as three int8 digits of a 22-bit
 //    fixed-point value, so the int8 weights multiply by dp4a without any
 //    int->float conversion (12 dp4a per 16 weights); per-block sums are
 //    scaled and accumulated in f32 and reduced with warp shuffles (a 4-row
@@ -55,7 +55,6 @@ struct GemvQ8Params {
   int32_t k, row_bytes, sb;  // K, bytes per row, scale bytes per row
   int32_t group_rows;        // rows per consumer task (1 or 4)
   int64_t prefetch_bytes;    // weight bytes per CTA prefetched into L2 before the wait
-  int32_t early_tile;        // load the first register tile before the wait
   int32_t n_vec;             // activation vectors (batch)
   // prologue
   int32_t prologue;
@@ -97,16 +96,16 @@ struct GemvSmem {
 };
 
 // Activation vectors in shared memory.  The prologue builds each vector in
-// f32 registers, then encodes every block of 32 elements in fixed point: X = rint(x / sx) with sx = max|x_block| / kXMax, so |X| <=
-// 127 * 2^16, stored as three signed base-256 digits (X = d2*2^16 + d1*2^8 +
-// d0, each in [-128, 127]).  A chunk of 16 int8 weights q then dots with x
-// as sx * (2^16 * dp4a(q, d2) + 2^8 * dp4a(q, d1) + dp4a(q, d0)): the integer
-// sums are exact, so the only rounding beyond f32 accumulation is x itself,
-// represented to 2^-23 of its block maximum.  Digits are stored lane-major:
+// f32 registers, then encodes every block of 32 elements in fixed point:
+// X = rint(x / sx) with sx the power of two for which max|x_block| / sx lies
+// in [2^21, 2^22), so |X| <= 2^22, stored as three signed base-256 digits
+// (X = d2*2^16 + d1*2^8 + d0, each in [-128, 127]).  A chunk of 16 int8
+// weights q then dots with x as sx * (2^16 * dp4a(q, d2) + 2^8 * dp4a(q, d1)
+// + dp4a(q, d0)): the integer sums are exact and the scaling by sx is exact,
+// so the only rounding beyond f32 accumulation is x itself, represented to
+// at most 2^-22 of its block maximum.  Digits are stored lane-major:
 // chunk c = lane + 32*j keeps its 16 d2, d1, d0 bytes in uint4 slots
 // ((3*j + t) * 32 + lane), so each lane's LDS.128 is bank-conflict free.
-constexpr int kXMax = 127 * 65536;
-
 struct XLayout {
   int64_t xd, sx, total;  // byte offsets of the digits and scales, total size
 };

@@ -1,0 +1,10 @@
+// Q8_0 GEMV kernels of the kinds below (one file per group so the
+// instantiations compile in parallel).
+#include "gemv_q8_impl.cuh"
+
+namespace bt {
+namespace gemv_detail {
+BT_GEMV_INSTANTIATE(PRO_EMBED_NORM, EPI_STORE)
+BT_GEMV_INSTANTIATE(PRO_EMBED_NORM, EPI_GDN_IN)
+}  // namespace gemv_detail
+}  // namespace bt

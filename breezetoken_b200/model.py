@@ -470,6 +470,7 @@ class Qwen35:
                 "start": (int(r[i, 0]) - t0) / 1e3,
                 "released": (int(r[i, 3]) - t0) / 1e3,
                 "ready": (int(r[i, 4]) - t0) / 1e3,
+                "loaded": (int(r[i, 7]) - t0) / 1e3 if r[i, 7] else None,
                 "end": (int(r[i, 6]) - t0) / 1e3,
             })
         return out

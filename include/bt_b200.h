@@ -228,7 +228,8 @@ typedef struct BtTraceRecord {
   uint64_t waited_min, waited_max; /* first / last CTA past the dependency wait */
   uint64_t ready_max;              /* last CTA past its prologue             */
   uint64_t exit_min, exit_max;     /* first / last CTA end                   */
-  uint64_t pad;
+  uint64_t loaded_max;             /* GEMV: last CTA with its activation loads
+                                      back (0 for other kernels)             */
 } BtTraceRecord;
 
 /* Kernels one decode step launches (with logits): the trace record count. */
