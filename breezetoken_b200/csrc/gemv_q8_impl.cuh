@@ -411,10 +411,12 @@ __device__ __forceinline__ void process_tile(const Tile<GR, J>& t, const GemvQ8P
 // ------------------------------------------------------------------ kernel
 // One CTA (or two, for long matrices) per SM streams a contiguous range of
 // rows.  Warp w takes row groups w, w+8, ...; each warp double-buffers its
-// groups in registers (loads of group g+8 are in flight while group g is
-// computed).  Before the dependency wait the CTA prefetches the head of its
-// weight slice into L2 and loads its first groups into registers: weights
-// never depend on earlier kernels.
+// groups in registers (the load of group g+8 is in flight while group g is
+// computed).  Before the dependency wait -- weights never depend on earlier
+// kernels -- the CTA prefetches the head of its weight slice into L2 and
+// each warp loads its first two groups into registers, so a short slice
+// needs no memory round trip after the wait.  Past the prefetched head, each
+// warp keeps a bulk L2 prefetch running two groups ahead of its loads.
 template <int PRO, int EPI, int NV, int GR, int J>
 __global__ void __launch_bounds__(kGemvThreads, 2) gemv_q8_kernel(const __grid_constant__ GemvQ8Params p) {
   extern __shared__ __align__(128) uint8_t smem[];
@@ -450,12 +452,21 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_q8_kernel(const __grid_c
   int g = warp;
   if (g < n_groups)
     load_tile<GR, J>(A, p, row0 + static_cast<int64_t>(g) * GR, min(GR, cta_rows - g * GR), lane, nchunks);
+  // (the second group waits for the prologue where both together would
+  // leave the prologue too few registers: long rows with a normalising one)
+  constexpr bool kEarlyB = J <= 4 || PRO == PRO_LOAD;
+  if (kEarlyB && g + kConsumerWarps < n_groups)
+    load_tile<GR, J>(B, p, row0 + static_cast<int64_t>(g + kConsumerWarps) * GR,
+                     min(GR, cta_rows - (g + kConsumerWarps) * GR), lane, nchunks);
   pdl_launch_dependents();
 
   // ---- activations (after the wait)
   pdl_wait();
   trace_waited(p.trace);
   gemv_prologue<PRO, NV, (J > 1 ? J / 2 : 1)>(p, xd, sx, scratch);
+  if (!kEarlyB && g + kConsumerWarps < n_groups)
+    load_tile<GR, J>(B, p, row0 + static_cast<int64_t>(g + kConsumerWarps) * GR,
+                     min(GR, cta_rows - (g + kConsumerWarps) * GR), lane, nchunks);
   __syncthreads();
   trace_ready(p.trace);
 
@@ -463,20 +474,27 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_q8_kernel(const __grid_c
 #pragma unroll
   for (int v = 0; v < NV; ++v) best[v] = 0ull;
   const uint4* xd4 = reinterpret_cast<const uint4*>(xd);
+  // group gl's rows start gl*GR*row_bytes into the slice; the pre-wait
+  // prefetch covered the first prefetch_bytes of it
+  const int64_t group_bytes = static_cast<int64_t>(GR) * p.row_bytes;
+  auto refill = [&](Tile<GR, J>& t, int gl) {
+    if (gl >= n_groups) return;
+    load_tile<GR, J>(t, p, row0 + static_cast<int64_t>(gl) * GR, min(GR, cta_rows - gl * GR), lane, nchunks);
+    const int gp = gl + 2 * kConsumerWarps;
+    if (lane == 0 && gp < n_groups && gp * group_bytes >= p.prefetch_bytes)
+      prefetch_l2_bulk(p.w + (row0 + static_cast<int64_t>(gp) * GR) * p.row_bytes,
+                       static_cast<uint32_t>(min(GR, cta_rows - gp * GR) * p.row_bytes));
+  };
   while (g < n_groups) {
-    int gn = g + kConsumerWarps;
-    if (gn < n_groups)
-      load_tile<GR, J>(B, p, row0 + static_cast<int64_t>(gn) * GR, min(GR, cta_rows - gn * GR), lane, nchunks);
     process_tile<EPI, NV, GR, J>(A, p, row0 + static_cast<int64_t>(g) * GR, min(GR, cta_rows - g * GR), lane,
                                  nchunks, xd4, sx, best);
-    g = gn;
+    refill(A, g + 2 * kConsumerWarps);
+    g += kConsumerWarps;
     if (g >= n_groups) break;
-    gn = g + kConsumerWarps;
-    if (gn < n_groups)
-      load_tile<GR, J>(A, p, row0 + static_cast<int64_t>(gn) * GR, min(GR, cta_rows - gn * GR), lane, nchunks);
     process_tile<EPI, NV, GR, J>(B, p, row0 + static_cast<int64_t>(g) * GR, min(GR, cta_rows - g * GR), lane,
                                  nchunks, xd4, sx, best);
-    g = gn;
+    refill(B, g + 2 * kConsumerWarps);
+    g += kConsumerWarps;
   }
 
   if constexpr (EPI != EPI_ARGMAX) {
