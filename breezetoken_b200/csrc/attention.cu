@@ -38,6 +38,12 @@ constexpr int kAttnWarps = 4;
 constexpr int kMinSplitLen = 64;
 constexpr int kAttnThreads = kAttnWarps * 32;
 constexpr float kLog2e = 1.4426950408889634f;
+// K/V rows per CTA prefetched into L2 as soon as the slice is known.
+constexpr int kPrefetchRows = 64;
+
+__device__ __forceinline__ void prefetch_l2_bulk(const void* p, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
 
 // Sum 32 per-lane values across the warp; lane l returns the total of value l.
 __device__ __forceinline__ float reduce_scatter32(float (&v)[32], int lane) {
@@ -94,7 +100,7 @@ struct KvRow<__nv_bfloat16, 4> {
 
 // CL = the splits of one (sequence, group) form a thread-block cluster and
 // merge through distributed shared memory instead of the global workspace.
-template <typename KV, int DPL, int GS, bool CL>
+template <typename KV, int DPL, int GS, bool CL, bool MODEL>
 __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const __grid_constant__ AttnParams p) {
   constexpr int DIM = DPL * 32;
   constexpr int PB = 32 / GS;
@@ -113,7 +119,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const __grid_
   pdl_wait();
   trace_waited(p.trace);
 
-  int L = p.model ? p.pos[b] + 1 : p.lens[b];
+  int L = MODEL ? p.pos[b] + 1 : p.lens[b];
   if (L < 0 || L > p.cap) {
     if (threadIdx.x == 0 && split == 0) report_status(p.status, BT_ERR_INVALID, SITE_ATTN_LENGTH, L, p.cap, b);
     L = L < 0 ? 0 : p.cap;
@@ -126,41 +132,73 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const __grid_
   if (!CL && split >= splits) return;
   const int chunk = (L + splits - 1) / splits;
   const int t0 = min(L, split * chunk), t1 = min(L, t0 + chunk);
+  {
+    // K/V rows of the first kPrefetchRows positions of the slice on their way
+    // into L2 while the queries are prepared (one bulk prefetch per row)
+    const int n = min(t1 - t0, kPrefetchRows);
+    const int r = threadIdx.x < n ? threadIdx.x : threadIdx.x - n;
+    if (threadIdx.x < 2 * n) {
+      const KV* base = static_cast<const KV*>(threadIdx.x < n ? p.k : p.v);
+      prefetch_l2_bulk(base + static_cast<int64_t>(b) * p.kv_bs + static_cast<int64_t>(t0 + r) * p.kv_ts + g * DIM,
+                       DIM * sizeof(KV));
+    }
+  }
+  // the output element this thread finishes first in a cluster merge, and its gate
+  const int per = (GS * DIM + splits - 1) / splits;
+  const int e_first = split * per + threadIdx.x;
+  float gate_first = 0.f;
+  if (CL && MODEL && e_first < min(GS * DIM, (split + 1) * per))
+    gate_first = p.gate[static_cast<int64_t>(b) * p.q_bs + static_cast<int64_t>(g * GS + e_first / DIM) * p.q_hs +
+                        e_first % DIM];
 
-  if (!p.model) {
+  if constexpr (!MODEL) {
     for (int i = threadIdx.x; i < GS * DIM; i += kAttnThreads)
       qs[i / DIM][i % DIM] =
           p.q[static_cast<int64_t>(b) * p.q_bs + static_cast<int64_t>(g * GS + i / DIM) * p.q_hs + i % DIM];
     __syncthreads();
   } else {
-    const int pos = L - 1;
-    for (int item = warp; item < GS + 2; item += kAttnWarps) {
-      float* dst = item < GS ? qs[item] : kvn[item - GS];
+    const int pos = max(L - 1, 0);  // (L == 0 only after a reported invalid position)
+    // items: GS query heads, then k and v of the group; warp w takes items
+    // w, w + 4, ...  Every load of all its items (values, norm weights, RoPE
+    // row) is issued before any is used.
+    constexpr int NI = (GS + 2 + kAttnWarps - 1) / kAttnWarps;
+    const float* crow = p.rope_cos + static_cast<int64_t>(pos) * p.rope_dim;
+    const float* srow = p.rope_sin + static_cast<int64_t>(pos) * p.rope_dim;
+    float x[NI][DPL], nwv[NI][DPL], cv[DPL], sv[DPL];
+#pragma unroll
+    for (int i = 0; i < DPL; ++i) {
+      const int dc = min(lane * DPL + i, p.rope_dim - 1);
+      cv[i] = crow[dc];
+      sv[i] = srow[dc];
+    }
+#pragma unroll
+    for (int it = 0; it < NI; ++it) {
+      const int item = min(warp + it * kAttnWarps, GS + 1);
       const float* src = item < GS ? p.q + static_cast<int64_t>(b) * p.q_bs + static_cast<int64_t>(g * GS + item) * p.q_hs
                                    : (item == GS ? p.k_new : p.v_new) + static_cast<int64_t>(b) * p.q_bs + g * DIM;
-      // every load of the item (values, norm weights, RoPE row) in flight at once
       const float* nw = item < GS ? p.q_norm : p.k_norm;
-      const float* crow = p.rope_cos + static_cast<int64_t>(pos) * p.rope_dim;
-      const float* srow = p.rope_sin + static_cast<int64_t>(pos) * p.rope_dim;
-      float x[DPL], nwv[DPL], cv[DPL], sv[DPL];
 #pragma unroll
       for (int i = 0; i < DPL; ++i) {
-        const int d = lane * DPL + i, dc = min(d, p.rope_dim - 1);
-        x[i] = src[d];
-        nwv[i] = nw[d];
-        cv[i] = crow[dc];
-        sv[i] = srow[dc];
+        x[it][i] = src[lane * DPL + i];
+        nwv[it][i] = nw[lane * DPL + i];
       }
+    }
+#pragma unroll
+    for (int it = 0; it < NI; ++it) {
+      const int item = warp + it * kAttnWarps;
+      if (item >= GS + 2) break;
+      float* dst = item < GS ? qs[item] : kvn[item - GS];
       if (item <= GS) {
+        // RMSNorm then rotate-half RoPE on the first rope_dim dims (q and k)
         float ss = 0.f;
 #pragma unroll
-        for (int i = 0; i < DPL; ++i) ss = fmaf(x[i], x[i], ss);
+        for (int i = 0; i < DPL; ++i) ss = fmaf(x[it][i], x[it][i], ss);
         ss = warp_sum(ss);
         const float r = 1.0f / sqrtf(ss / static_cast<float>(DIM) + p.eps);
 #pragma unroll
         for (int i = 0; i < DPL; ++i) {
-          x[i] = __fmul_rn(__fmul_rn(x[i], r), nwv[i]);
-          dst[lane * DPL + i] = x[i];
+          x[it][i] = __fmul_rn(__fmul_rn(x[it][i], r), nwv[it][i]);
+          dst[lane * DPL + i] = x[it][i];
         }
         __syncwarp();
         const int half = p.rope_dim >> 1;
@@ -169,13 +207,13 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const __grid_
           const int d = lane * DPL + i;
           if (d < p.rope_dim) {
             const float partner = d < half ? -dst[d + half] : dst[d - half];
-            x[i] = __fadd_rn(__fmul_rn(x[i], cv[i]), __fmul_rn(partner, sv[i]));
+            x[it][i] = __fadd_rn(__fmul_rn(x[it][i], cv[i]), __fmul_rn(partner, sv[i]));
           }
         }
         __syncwarp();
       }
 #pragma unroll
-      for (int i = 0; i < DPL; ++i) dst[lane * DPL + i] = x[i];
+      for (int i = 0; i < DPL; ++i) dst[lane * DPL + i] = x[it][i];
     }
     __syncthreads();
     if (pos >= t0 && pos < t1) {
@@ -296,7 +334,6 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const __grid_
     cg::cluster_group cluster = cg::this_cluster();
     cluster.sync();
     // rank r finishes elements [r*per, (r+1)*per) reading every rank's partial
-    const int per = (GS * DIM + splits - 1) / splits;
     for (int e = split * per + threadIdx.x; e < min(GS * DIM, (split + 1) * per); e += kAttnThreads) {
       const int h = e / DIM, d = e % DIM;
       float M = -INFINITY;
@@ -311,8 +348,12 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const __grid_
         }
       }
       float o = Ls > 0.f ? O / Ls : 0.f;
-      if (p.model)
-        o *= sigmoid_f(p.gate[static_cast<int64_t>(b) * p.q_bs + static_cast<int64_t>(g * GS + h) * p.q_hs + d]);
+      if constexpr (MODEL) {
+        const float gt = e == e_first ? gate_first
+                                      : p.gate[static_cast<int64_t>(b) * p.q_bs +
+                                               static_cast<int64_t>(g * GS + h) * p.q_hs + d];
+        o *= sigmoid_f(gt);
+      }
       p.out[static_cast<int64_t>(b) * p.out_bs + static_cast<int64_t>(g * GS + h) * DIM + d] = o;
     }
     cluster.sync();  // no CTA leaves while others still read its shared memory
@@ -338,7 +379,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const __grid_
     }
     if (splits == 1) {
       float o = Ls > 0.f ? O / Ls : 0.f;
-      if (p.model)
+      if constexpr (MODEL)
         o *= sigmoid_f(p.gate[static_cast<int64_t>(b) * p.q_bs + static_cast<int64_t>(g * GS + h) * p.q_hs + d]);
       p.out[static_cast<int64_t>(b) * p.out_bs + static_cast<int64_t>(g * GS + h) * DIM + d] = o;
     } else {
@@ -407,7 +448,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const __grid_
     for (; s < splits; ++s) O0 = fmaf(__ldcg(base + s * rstride), f[s], O0);
     const float Ls = s_sum[h];
     float o = Ls > 0.f ? ((O0 + O1) + (O2 + O3)) / Ls : 0.f;
-    if (p.model)
+    if constexpr (MODEL)
       o *= sigmoid_f(p.gate[static_cast<int64_t>(b) * p.q_bs + static_cast<int64_t>(g * GS + h) * p.q_hs + d]);
     p.out[static_cast<int64_t>(b) * p.out_bs + static_cast<int64_t>(g * GS + h) * DIM + d] = o;
   }
@@ -441,8 +482,15 @@ int launch_t(const AttnParams& p, cudaStream_t stream, bool pdl) {
   }
   cfg.attrs = attr;
   cfg.numAttrs = n;
-  cudaError_t e = cl ? cudaLaunchKernelEx(&cfg, attn_decode_kernel<KV, DPL, GS, (GS == 4)>, p)
-                     : cudaLaunchKernelEx(&cfg, attn_decode_kernel<KV, DPL, GS, false>, p);
+  cudaError_t e;
+  if (p.model) {
+    // the model keeps an f32 cache (checked by attention_launch)
+    e = cl ? cudaLaunchKernelEx(&cfg, attn_decode_kernel<float, DPL, GS, (GS == 4), true>, p)
+           : cudaLaunchKernelEx(&cfg, attn_decode_kernel<float, DPL, GS, false, true>, p);
+  } else {
+    e = cl ? cudaLaunchKernelEx(&cfg, attn_decode_kernel<KV, DPL, GS, (GS == 4), false>, p)
+           : cudaLaunchKernelEx(&cfg, attn_decode_kernel<KV, DPL, GS, false, false>, p);
+  }
   if (e != cudaSuccess) return fail_cuda(e, "attention launch");
   return BT_OK;
 }
