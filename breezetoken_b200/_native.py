@@ -125,7 +125,7 @@ _SIGS: dict[str, tuple[object, list]] = {
     "bt_gdn_decode": (C.c_int, [_P, _P, _P, C.c_int, _P, _P, _P, _P, _I64, _I64, _I64, _I64, C.c_float, C.c_float, _P]),
     "bt_argmax_workspace_bytes": (_I64, [_I64]),
     "bt_argmax": (C.c_int, [_P, _I64, _I64, _P, _P, _P]),
-    "bt_qwen35_kernels_per_step": (C.c_int, [C.POINTER(BtQwen35Dims)]),
+    "bt_qwen35_kernels_per_step": (C.c_int, [C.POINTER(BtQwen35Model)]),
     "bt_qwen35_proj_elems": (_I64, [C.POINTER(BtQwen35Dims)]),
     "bt_qwen35_workspace_bytes": (_I64, [C.POINTER(BtQwen35Dims)]),
     "bt_qwen35_step": (C.c_int, [C.POINTER(BtQwen35Model), C.POINTER(BtQwen35Runtime), C.c_int, _P]),

@@ -14,7 +14,7 @@
 namespace bt {
 
 int64_t qwen35_proj_elems(const BtQwen35Dims& d);
-int qwen35_kernels_per_step(const BtQwen35Dims& d);
+int qwen35_kernels_per_step(const BtQwen35Model& m);
 int64_t qwen35_workspace_bytes(const BtQwen35Dims& d);
 int qwen35_step(const BtQwen35Model& m, const BtQwen35Runtime& rt, int with_logits, cudaStream_t s);
 
@@ -203,7 +203,9 @@ int bt_argmax(const float* x, int64_t rows, int64_t n, int32_t* out, void* works
   return bt::argmax(x, rows, n, out, workspace, as_stream(stream));
 }
 
-int bt_qwen35_kernels_per_step(const BtQwen35Dims* dims) { return dims ? bt::qwen35_kernels_per_step(*dims) : 0; }
+int bt_qwen35_kernels_per_step(const BtQwen35Model* model) {
+  return model && model->layers ? bt::qwen35_kernels_per_step(*model) : 0;
+}
 
 int64_t bt_qwen35_proj_elems(const BtQwen35Dims* dims) { return dims ? bt::qwen35_proj_elems(*dims) : 0; }
 

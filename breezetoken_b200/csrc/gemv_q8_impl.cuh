@@ -219,29 +219,35 @@ __device__ __forceinline__ void gdn_operands(const GemvQ8Params& p, int v, int64
   }
 }
 
-// GDN in-projection epilogue of row r (value a): causal conv window + SiLU
-// of a qkv channel (model/layers.py:90-93), silu(z), the decay
-// g = a_log * softplus(alpha + dt_bias) (:99-103), beta logits as they are.
+// Causal conv window + SiLU of conv channel ch with its new input a
+// (model/layers.py:90-93); shifts the channel's conv state.
+__device__ __forceinline__ float conv_silu(const GemvQ8Params& p, int v, int64_t ch, float a, const EpiOperands& o) {
+  const int taps = p.conv_k - 1;
+  float sum = 0.f;
+#pragma unroll
+  for (int t = 0; t < 3; ++t)
+    if (t < taps) sum = __fadd_rn(sum, __fmul_rn(o.cs[t], o.cw[t]));
+  float last = 0.f;
+#pragma unroll
+  for (int t = 0; t < 4; ++t)
+    if (t == taps) last = o.cw[t];
+  sum = __fadd_rn(sum, __fmul_rn(a, last));
+  float* cs = p.conv_state + (static_cast<int64_t>(v) * p.n_conv + ch) * taps;
+#pragma unroll
+  for (int t = 0; t < 3; ++t)
+    if (t + 1 < taps) cs[t] = o.cs[t + 1];
+  cs[taps - 1] = a;
+  return silu_f(sum);
+}
+
+// GDN in-projection epilogue of row r (value a): conv + SiLU of a qkv
+// channel, silu(z), the decay g = a_log * softplus(alpha + dt_bias)
+// (model/layers.py:99-103), beta logits as they are.
 __device__ __forceinline__ void gdn_epilogue(const GemvQ8Params& p, int v, int64_t r, float a,
                                              const EpiOperands& o) {
   float* y = p.y + static_cast<int64_t>(v) * p.y_stride;
   if (r < p.n_conv) {
-    const int taps = p.conv_k - 1;
-    float sum = 0.f;
-#pragma unroll
-    for (int t = 0; t < 3; ++t)
-      if (t < taps) sum = __fadd_rn(sum, __fmul_rn(o.cs[t], o.cw[t]));
-    float last = 0.f;
-#pragma unroll
-    for (int t = 0; t < 4; ++t)
-      if (t == taps) last = o.cw[t];
-    sum = __fadd_rn(sum, __fmul_rn(a, last));
-    float* cs = p.conv_state + (static_cast<int64_t>(v) * p.n_conv + r) * taps;
-#pragma unroll
-    for (int t = 0; t < 3; ++t)
-      if (t + 1 < taps) cs[t] = o.cs[t + 1];
-    cs[taps - 1] = a;
-    y[r] = silu_f(sum);
+    y[r] = conv_silu(p, v, r, a, o);
   } else if (r < p.n_conv + p.n_z) {
     y[r] = silu_f(a);
   } else if (r < p.n_conv + p.n_z + p.n_gh) {
@@ -329,22 +335,11 @@ __device__ __forceinline__ void finish_row(const GemvQ8Params& p, int v, int64_t
   }
 }
 
-template <int EPI, int NV, int GR, int J>
-__device__ __forceinline__ void process_tile(const Tile<GR, J>& t, const GemvQ8Params& p, int64_t r0, int nr,
-                                             int lane, int nchunks, const uint4* xd4, const float* sx,
-                                             unsigned long long (&best)[NV]) {
-  const int nb = p.k >> 5;
-  // GDN epilogue operands of the row this lane finishes, in flight during the math
-  constexpr bool EPF = EPI == EPI_GDN_IN && NV <= 2;
-  EpiOperands eo[EPF ? NV : 1];
-  if constexpr (EPF) {
-    const int my_r = GR == 4 ? (lane >> 3) : 0;
-    const bool mine = GR == 4 ? (lane & 7) == 0 : lane == 0;
-    if (mine && my_r < nr)
-#pragma unroll
-      for (int v = 0; v < NV; ++v) gdn_operands(p, v, r0 + my_r, eo[v]);
-  }
-  float acc[GR][NV];
+// Per-lane partial dot products of a row group with the NV encoded vectors
+// (summed over the lane's chunks; the warp reduction follows).
+template <int NV, int GR, int J>
+__device__ __forceinline__ void tile_dot(const Tile<GR, J>& t, int lane, int nchunks, int nb, const uint4* xd4,
+                                         const float* sx, float (&acc)[GR][NV]) {
 #pragma unroll
   for (int r = 0; r < GR; ++r)
 #pragma unroll
@@ -367,23 +362,49 @@ __device__ __forceinline__ void process_tile(const Tile<GR, J>& t, const GemvQ8P
       }
     }
   }
+}
+
+// 4-row reduce-scatter of vector v: lane l ends with the total of row l >> 3
+// (lanes 0, 8, 16, 24 hold rows 0..3; 6 shuffles for the 4 rows).
+template <int NV>
+__device__ __forceinline__ float reduce_rows4(const float (&acc)[4][NV], int v, int lane) {
+  const bool hi16 = (lane & 16) != 0, hi8 = (lane & 8) != 0;
+  const float s0 = hi16 ? acc[0][v] : acc[2][v];
+  const float s1 = hi16 ? acc[1][v] : acc[3][v];
+  const float r0v = __shfl_xor_sync(0xffffffffu, s0, 16);
+  const float r1v = __shfl_xor_sync(0xffffffffu, s1, 16);
+  const float b0 = (hi16 ? acc[2][v] : acc[0][v]) + r0v;
+  const float b1 = (hi16 ? acc[3][v] : acc[1][v]) + r1v;
+  const float send = hi8 ? b0 : b1;
+  float c = (hi8 ? b1 : b0) + __shfl_xor_sync(0xffffffffu, send, 8);
+  c += __shfl_xor_sync(0xffffffffu, c, 4);
+  c += __shfl_xor_sync(0xffffffffu, c, 2);
+  c += __shfl_xor_sync(0xffffffffu, c, 1);
+  return c;
+}
+
+template <int EPI, int NV, int GR, int J>
+__device__ __forceinline__ void process_tile(const Tile<GR, J>& t, const GemvQ8Params& p, int64_t r0, int nr,
+                                             int lane, int nchunks, const uint4* xd4, const float* sx,
+                                             unsigned long long (&best)[NV]) {
+  const int nb = p.k >> 5;
+  // GDN epilogue operands of the row this lane finishes, in flight during the math
+  constexpr bool EPF = EPI == EPI_GDN_IN && NV <= 2;
+  EpiOperands eo[EPF ? NV : 1];
+  if constexpr (EPF) {
+    const int my_r = GR == 4 ? (lane >> 3) : 0;
+    const bool mine = GR == 4 ? (lane & 7) == 0 : lane == 0;
+    if (mine && my_r < nr)
+#pragma unroll
+      for (int v = 0; v < NV; ++v) gdn_operands(p, v, r0 + my_r, eo[v]);
+  }
+  float acc[GR][NV];
+  tile_dot<NV, GR, J>(t, lane, nchunks, nb, xd4, sx, acc);
 
   if constexpr (GR == 4) {
-    // reduce-scatter: lane l ends with the sum of row 2*bit4(l) + bit3(l)
-    const bool hi16 = (lane & 16) != 0, hi8 = (lane & 8) != 0;
 #pragma unroll
     for (int v = 0; v < NV; ++v) {
-      const float s0 = hi16 ? acc[0][v] : acc[2][v];
-      const float s1 = hi16 ? acc[1][v] : acc[3][v];
-      const float r0v = __shfl_xor_sync(0xffffffffu, s0, 16);
-      const float r1v = __shfl_xor_sync(0xffffffffu, s1, 16);
-      const float b0 = (hi16 ? acc[2][v] : acc[0][v]) + r0v;
-      const float b1 = (hi16 ? acc[3][v] : acc[1][v]) + r1v;
-      const float send = hi8 ? b0 : b1;
-      float c = (hi8 ? b1 : b0) + __shfl_xor_sync(0xffffffffu, send, 8);
-      c += __shfl_xor_sync(0xffffffffu, c, 4);
-      c += __shfl_xor_sync(0xffffffffu, c, 2);
-      c += __shfl_xor_sync(0xffffffffu, c, 1);
+      const float c = reduce_rows4<NV>(acc, v, lane);
       const int lr = lane >> 3;  // row held by lanes 0, 8, 16, 24
       if constexpr (EPI == EPI_SILU_PAIR) {
         // rows (2j, 2j+1) = (gate_j, up_j): lanes 0 and 16 hold the gates

@@ -23,6 +23,7 @@
 #include "attention.cuh"
 #include "errors.h"
 #include "gdn.cuh"
+#include "gdn_fused.cuh"
 #include "gemv_q8.cuh"
 
 namespace bt {
@@ -86,6 +87,17 @@ bool use_pdl() {
   return on;
 }
 
+// The fused GDN layer kernel where it serves the shapes (on by default;
+// BT_GDN_FUSED=0 runs in-projection, recurrence and gated-norm out-projection
+// as three kernels, for measurements).
+bool gdn_fused_enabled(const BtQwen35Dims& d) {
+  static const bool on = [] {
+    const char* v = getenv("BT_GDN_FUSED");
+    return !(v && v[0] == '0');
+  }();
+  return on && gdn_fused_supported(d.hidden, d.ssm_heads, d.ssm_heads, d.ssm_state, d.batch);
+}
+
 int run_gemv(GemvQ8Params& p, cudaStream_t s) {
   GemvQ8Launch L{};
   int rc = gemv_q8_plan(p, sm_count(), L);
@@ -95,7 +107,12 @@ int run_gemv(GemvQ8Params& p, cudaStream_t s) {
 
 }  // namespace
 
-int qwen35_kernels_per_step(const BtQwen35Dims& d) { return 5 * d.n_layers + 1; }
+int qwen35_kernels_per_step(const BtQwen35Model& m) {
+  const BtQwen35Dims& d = m.dims;
+  int n = 1;  // the head
+  for (int i = 0; i < d.n_layers; ++i) n += (!m.layers[i].is_attn && gdn_fused_enabled(d)) ? 4 : 5;
+  return n;
+}
 
 int64_t qwen35_proj_elems(const BtQwen35Dims& d) {
   const int64_t gdn = 4LL * d.ssm_inner + 2LL * d.ssm_heads;
@@ -146,6 +163,7 @@ int qwen35_step(const BtQwen35Model& m, const BtQwen35Runtime& rt, int with_logi
       p1.h_out = ho;
       std::swap(hc, ho);
     }
+    const bool fused = !ly.is_attn && gdn_fused_enabled(d);
     if (!ly.is_attn) {
       p1.n_rows = 4LL * d.ssm_inner + 2LL * d.ssm_heads;
       p1.epilogue = EPI_GDN_IN;
@@ -162,10 +180,28 @@ int qwen35_step(const BtQwen35Model& m, const BtQwen35Runtime& rt, int with_logi
       p1.epilogue = EPI_STORE;
     }
     p1.trace = trace();
-    if ((rc = run_gemv(p1, s))) return rc;
+    if (fused) {
+      // ---- 1+2: in-projection, conv, recurrence and gated norm in one kernel
+      GdnFusedParams f{};
+      f.g = p1;
+      f.heads = d.ssm_heads;
+      f.dim = d.ssm_state;
+      f.state = ly.rec_state;
+      f.scale = 1.0f / sqrtf(static_cast<float>(d.ssm_state));
+      f.l2_eps = d.l2_eps;
+      f.norm_w = ly.ssm_norm;
+      f.norm_eps = d.eps;
+      f.out = rt.mix;
+      f.out_bs = mix_stride;
+      if ((rc = gdn_fused_launch(f, s, use_pdl()))) return rc;
+    } else if ((rc = run_gemv(p1, s))) {
+      return rc;
+    }
 
     // ---- 2: the mixer
-    if (!ly.is_attn) {
+    if (fused) {
+      // done above
+    } else if (!ly.is_attn) {
       GdnParams g{};
       g.q = rt.proj;
       g.k = rt.proj + d.ssm_inner;
@@ -235,7 +271,10 @@ int qwen35_step(const BtQwen35Model& m, const BtQwen35Runtime& rt, int with_logi
     p3.y = rt.delta;
     p3.y_stride = d.hidden;
     p3.epilogue = EPI_STORE;
-    if (!ly.is_attn) {
+    if (fused) {
+      p3.k = d.ssm_inner;
+      p3.prologue = PRO_LOAD;
+    } else if (!ly.is_attn) {
       p3.k = d.ssm_inner;
       p3.prologue = PRO_GATED_NORM;
       p3.x2 = rt.proj + 3LL * d.ssm_inner;

@@ -392,8 +392,10 @@ class Qwen35:
                         L[key][:, :upto].copy_(snap[f"{i}.{key}"], non_blocking=True)
 
     def kernels_per_step(self) -> int:
-        """Kernels one decode step launches: 5 per layer plus the head."""
-        return 5 * self.cfg.n_layers + 1
+        """Kernels one decode step launches: 5 per attention layer, 4 per GDN
+        layer (in-projection and recurrence fused) or 5 where that fusion
+        does not serve the shapes, plus the head."""
+        return int(self.lib.bt_qwen35_kernels_per_step(C.byref(self._model)))
 
     def step_bytes(self, context: float) -> float:
         """Algorithmic HBM bytes of one decode step per sequence at attended length
@@ -434,12 +436,16 @@ class Qwen35:
         (last CTA past the dependency wait), ready (last CTA past its
         prologue) and end (last CTA exit), in microseconds from the step's
         first entry."""
-        n = int(self.lib.bt_qwen35_kernels_per_step(C.byref(self._dims)))
+        n = self.kernels_per_step()
         rec = torch.zeros(n, 8, dtype=torch.int64, device=self.device)
+        n_attn = len(self.cfg.attn_layers)
+        fused = n == 5 * n_attn + 4 * (self.cfg.n_layers - n_attn) + 1
         names = []
         for i in range(self.cfg.n_layers):
             if i in self.cfg.attn_layers:
                 names += [f"{i}.attn_in", f"{i}.attention", f"{i}.attn_out"]
+            elif fused:
+                names += [f"{i}.gdn_fused", f"{i}.gdn_out"]
             else:
                 names += [f"{i}.gdn_in", f"{i}.gdn_step", f"{i}.gdn_out"]
             names += [f"{i}.gate_up", f"{i}.down"]

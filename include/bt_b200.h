@@ -232,8 +232,9 @@ typedef struct BtTraceRecord {
                                       back (0 for other kernels)             */
 } BtTraceRecord;
 
-/* Kernels one decode step launches (with logits): the trace record count. */
-BT_API int bt_qwen35_kernels_per_step(const BtQwen35Dims* dims);
+/* Kernels one decode step of `model` launches (with logits): the trace
+ * record count.  0 for a null model. */
+BT_API int bt_qwen35_kernels_per_step(const BtQwen35Model* model);
 BT_API int64_t bt_qwen35_proj_elems(const BtQwen35Dims* dims);
 BT_API int64_t bt_qwen35_workspace_bytes(const BtQwen35Dims* dims);
 

@@ -105,3 +105,43 @@ def test_0_8b_greedy_128_steps_match_reference(cuda, gguf_0_8b) -> None:
     finally:
         m.close()
     torch.cuda.synchronize()
+
+
+_PATH_SCRIPT = """
+import sys
+import numpy as np
+sys.path.insert(0, sys.argv[1])
+from breezetoken_b200.model import Qwen35
+m = Qwen35(sys.argv[2], max_context=64)
+tok, rows = 3, []
+for pos in range(12):
+    lg = m.forward_token(tok, pos).cpu().numpy()
+    rows.append(lg)
+    tok = int(lg.argmax())
+np.save(sys.argv[3], np.stack(rows))
+m.close()
+"""
+
+
+def test_gdn_fused_layer_matches_three_kernel_path(cuda, tiny_gguf, tmp_path) -> None:
+    """The fused GDN layer kernel (in-projection, conv, recurrence and gated
+    norm in one cluster launch) against the in-projection GEMV, recurrence
+    kernel and gated-norm out-projection it replaces: same greedy tokens,
+    logits within 1e-5 of their scale (the gated norm's sum of squares is
+    added in a different order)."""
+    import os
+    import subprocess
+    import sys
+    from pathlib import Path
+
+    root = str(Path(__file__).resolve().parents[1])
+    out = {}
+    for fused in ("1", "0"):
+        dst = tmp_path / f"logits_{fused}.npy"
+        env = dict(os.environ, BT_GDN_FUSED=fused)
+        subprocess.run([sys.executable, "-c", _PATH_SCRIPT, root, str(tiny_gguf), str(dst)], env=env, check=True,
+                       timeout=600)
+        out[fused] = np.load(dst)
+    a, b = out["1"], out["0"]
+    assert (a.argmax(-1) == b.argmax(-1)).all()
+    assert np.abs(a - b).max() <= 1e-5 * np.abs(b).max()
