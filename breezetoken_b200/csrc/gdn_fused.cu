@@ -11,9 +11,10 @@
 // the conv of those q/k/v channels, and the recurrence for value columns
 // 16j..16j+15 (a 128 x 16 slice of the state).  The recurrence needs the
 // whole normalised q and k of the head, so the slices are exchanged through
-// distributed shared memory after one cluster barrier; the gated norm's sum
-// of squares over the head's 128 outputs is a second exchange.  CTA 0 also
-// computes the head's alpha and beta rows.  Before the dependency wait a CTA
+// distributed shared memory: each CTA stores its slices into every CTA of
+// the cluster, then one cluster barrier; the gated norm's sum of squares over
+// the head's 128 outputs is a second such exchange.  CTAs 0 and 1 also
+// compute the head's alpha and beta rows.  Before the dependency wait a CTA
 // prefetches its 70 KB of weights and its state slice into L2 and loads its
 // first row groups into registers; after it the state slice streams into
 // shared memory (cp.async) while the activation prologue and the GEMV run.
@@ -40,9 +41,9 @@ constexpr int kSeg = 16;       // rows of each of q, k, v, z per CTA (= value co
 constexpr int kR = kDim / 16;  // state rows per thread in the recurrence
 constexpr int kMaxSmem = 200 * 1024;
 
-// Dynamic shared memory: [gemv header][fused scalars/vectors][state slices][activations]
+// Dynamic shared memory: [gemv header][fused vectors][state slices][activations]
 struct FusedLayout {
-  int64_t sq, sk, sv, sz, sg, sb, gdec, gbeta, qf, kf, ot, ssp, red, st, x, total;
+  int64_t sv, sz, gdec, gbeta, qf, kf, ot, ssq, red, st, x, total;
 };
 
 __host__ __device__ inline FusedLayout fused_layout(int k, int nv) {
@@ -53,18 +54,14 @@ __host__ __device__ inline FusedLayout fused_layout(int k, int nv) {
     o += ((floats * 4 + 15) / 16) * 16;
     return at;
   };
-  l.sq = take(nv * kSeg);
-  l.sk = take(nv * kSeg);
   l.sv = take(nv * kSeg);
   l.sz = take(nv * kSeg);
-  l.sg = take(nv);
-  l.sb = take(nv);
   l.gdec = take(nv);
   l.gbeta = take(nv);
   l.qf = take(nv * kDim);
   l.kf = take(nv * kDim);
   l.ot = take(nv * kSeg);
-  l.ssp = take(nv);
+  l.ssq = take(nv * kC);
   l.red = take(16 * 16);
   l.st = take(static_cast<int64_t>(nv) * kDim * kSeg);
   o = (o + 127) / 128 * 128;
@@ -79,6 +76,17 @@ __device__ __forceinline__ void cp_async16(void* smem_dst, const void* gsrc) {
 }
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+// Split cluster barrier: every thread of every CTA arrives, then waits.
+__device__ __forceinline__ void cluster_arrive_relaxed() {
+  asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait() { asm volatile("barrier.cluster.wait.aligned;" ::: "memory"); }
+
+// Store v into the same shared-memory slot of every CTA of the cluster.
+__device__ __forceinline__ void push_all(cg::cluster_group& cluster, float* slot, float v) {
+#pragma unroll
+  for (int r = 0; r < kC; ++r) *cluster.map_shared_rank(slot, r) = v;
+}
 
 template <int PRO, int NV, int GR, int J>
 __global__ void __launch_bounds__(kGemvThreads, (J <= 4 ? 2 : 1)) gdn_fused_kernel(const __grid_constant__ GdnFusedParams P) {
@@ -88,20 +96,16 @@ __global__ void __launch_bounds__(kGemvThreads, (J <= 4 ? 2 : 1)) gdn_fused_kern
   extern __shared__ __align__(128) uint8_t smem[];
   const FusedLayout L = fused_layout(p.k, NV);
   float* scratch = reinterpret_cast<float*>(smem);
-  float* sq = reinterpret_cast<float*>(smem + L.sq);    // conv(q) slice [v][16]
-  float* sk = reinterpret_cast<float*>(smem + L.sk);    // conv(k) slice
-  float* sv = reinterpret_cast<float*>(smem + L.sv);    // conv(v) slice
-  float* sz = reinterpret_cast<float*>(smem + L.sz);    // silu(z) slice
-  float* sg = reinterpret_cast<float*>(smem + L.sg);    // decay logit g (CTA 0)
-  float* sb = reinterpret_cast<float*>(smem + L.sb);    // beta logit (CTA 0)
-  float* gdec = reinterpret_cast<float*>(smem + L.gdec);
-  float* gbeta = reinterpret_cast<float*>(smem + L.gbeta);
-  float* qf = reinterpret_cast<float*>(smem + L.qf);    // normalised q of the head [v][128]
+  float* sv = reinterpret_cast<float*>(smem + L.sv);      // conv(v) slice [v][16]
+  float* sz = reinterpret_cast<float*>(smem + L.sz);      // silu(z) slice
+  float* gdec = reinterpret_cast<float*>(smem + L.gdec);  // decay logit g (pushed by CTA 0)
+  float* gbeta = reinterpret_cast<float*>(smem + L.gbeta);  // beta logit (pushed by CTA 1)
+  float* qf = reinterpret_cast<float*>(smem + L.qf);      // q of the head [v][128] (every CTA's slice)
   float* kf = reinterpret_cast<float*>(smem + L.kf);
-  float* ot = reinterpret_cast<float*>(smem + L.ot);    // recurrence output slice [v][16]
-  float* ssp = reinterpret_cast<float*>(smem + L.ssp);  // sum of squares of the output slice
+  float* ot = reinterpret_cast<float*>(smem + L.ot);      // recurrence output slice [v][16]
+  float* ssq = reinterpret_cast<float*>(smem + L.ssq);    // per-CTA sums of squares of the output [v][8]
   float (*red)[16] = reinterpret_cast<float (*)[16]>(smem + L.red);
-  float* st = reinterpret_cast<float*>(smem + L.st);    // state slices [v][128][16]
+  float* st = reinterpret_cast<float*>(smem + L.st);      // state slices [v][128][16]
   const XLayout xl = gemv_x_layout(p.k, NV);
   uint8_t* xd = smem + L.x + xl.xd;
   float* sx = reinterpret_cast<float*>(smem + L.x + xl.sx);
@@ -113,29 +117,47 @@ __global__ void __launch_bounds__(kGemvThreads, (J <= 4 ? 2 : 1)) gdn_fused_kern
   const int inner = P.heads * kDim;
   const int nchunks = p.k >> 4, nb = p.k >> 5;
   trace_entry(p.trace);
+  // every CTA of the cluster has started once this barrier completes (it is
+  // waited on before the first store into another CTA's shared memory)
+  cluster_arrive_relaxed();
 
   // first row of segment s (0 q, 1 k, 2 v, 3 z) of this CTA
   auto seg_row = [&](int s) -> int64_t { return static_cast<int64_t>(s) * inner + h * kDim + j * kSeg; };
-  const int64_t alpha_row = 4LL * inner + h, beta_row = 4LL * inner + P.heads + h;
+  auto group_row = [&](int gi) -> int64_t { return seg_row(gi / GPS) + (gi % GPS) * GR; };
+  // CTA 0 computes the head's alpha row, CTA 1 its beta row (warp 0)
+  const bool has_e = j < 2 && warp == 0;
+  const int64_t e_row = 4LL * inner + (j == 0 ? 0 : P.heads) + h;
   const float* S = P.state + static_cast<int64_t>(h) * kDim * kDim + j * kSeg;  // + b*heads*dim*dim
 
-  // ---- before the dependency wait: weights and state (L2), first groups (registers)
+  // ---- before the dependency wait: weights and parameters only
   if (tid < 4) prefetch_l2_bulk(p.w + seg_row(tid) * p.row_bytes, static_cast<uint32_t>(kSeg * p.row_bytes));
-  if (j == 0 && (tid == 4 || tid == 5))
-    prefetch_l2_bulk(p.w + (tid == 4 ? alpha_row : beta_row) * p.row_bytes, static_cast<uint32_t>(p.row_bytes));
+  if (has_e && lane == 0) prefetch_l2_bulk(p.w + e_row * p.row_bytes, static_cast<uint32_t>(p.row_bytes));
   for (int i = tid; i < NV * kDim; i += kGemvThreads) {
     const int v = i / kDim, r = i % kDim;
     asm volatile("prefetch.global.L2::evict_last [%0];" ::"l"(S + static_cast<int64_t>(v) * P.heads * kDim * kDim +
                                                               static_cast<int64_t>(r) * kDim));
   }
-  auto group_row = [&](int gi) -> int64_t { return seg_row(gi / GPS) + (gi % GPS) * GR; };
   Tile<GR, J> A, B;
-  Tile<1, J> E;  // CTA 0, warps 0/1: the alpha / beta row
-  const bool has_e = j == 0 && warp < 2;
+  Tile<1, J> E;
   int g = warp;
   if (g < NG) load_tile<GR, J>(A, p, group_row(g), GR, lane, nchunks);
   if (g + kConsumerWarps < NG) load_tile<GR, J>(B, p, group_row(g + kConsumerWarps), GR, lane, nchunks);
-  if (has_e) load_tile<1, J>(E, p, warp == 0 ? alpha_row : beta_row, 1, lane, nchunks);
+  if (has_e) load_tile<1, J>(E, p, e_row, 1, lane, nchunks);
+  // conv weights of the rows this lane finishes in its first two groups
+  const int my_r = GR == 4 ? (lane >> 3) : 0;
+  const bool mine = GR == 4 ? (lane & 7) == 0 : lane == 0;
+  float cwA[4] = {0.f, 0.f, 0.f, 0.f}, cwB[4] = {0.f, 0.f, 0.f, 0.f};
+  auto conv_w = [&](int gi, float (&cw)[4]) {
+    if (mine && gi < NG && gi / GPS < 3) {
+      const float* w = p.conv_w + (group_row(gi) + my_r) * p.conv_k;
+#pragma unroll
+      for (int t = 0; t < 4; ++t) cw[t] = t < p.conv_k ? w[t] : 0.f;
+    }
+  };
+  conv_w(g, cwA);
+  conv_w(g + kConsumerWarps, cwB);
+  const float a_log = has_e && j == 0 ? p.a_log[h] : 0.f, dt_bias = has_e && j == 0 ? p.dt_bias[h] : 0.f;
+  const float gnw = tid < NV * kSeg ? P.norm_w[j * kSeg + tid % kSeg] : 0.f;
   pdl_launch_dependents();
 
   pdl_wait();
@@ -150,29 +172,30 @@ __global__ void __launch_bounds__(kGemvThreads, (J <= 4 ? 2 : 1)) gdn_fused_kern
   gemv_prologue<PRO, NV, (J > 1 ? J / 2 : 1)>(p, xd, sx, scratch);
   __syncthreads();
   trace_ready(p.trace);
+  cluster_wait();
 
-  // ---- in-projection rows of the slice, conv + SiLU / silu(z) into shared memory
+  // ---- in-projection rows of the slice: q/k after conv + SiLU go to every
+  //      CTA of the cluster, v and silu(z) stay here
   const uint4* xd4 = reinterpret_cast<const uint4*>(xd);
-  auto finish = [&](int gi, int r, int v, float c, const EpiOperands& o) {
-    const int s = gi / GPS, ri = (gi % GPS) * GR + r;
-    if (s < 3) {
-      const float y = conv_silu(p, v, seg_row(s) + ri, c, o);
-      (s == 0 ? sq : s == 1 ? sk : sv)[v * kSeg + ri] = y;
-    } else {
-      sz[v * kSeg + ri] = silu_f(c);
-    }
-  };
-  auto run_group = [&](const Tile<GR, J>& t, int gi) {
-    // conv operands of the row this lane finishes, loaded before the math
+  auto run_group = [&](const Tile<GR, J>& t, int gi, const float (&cw)[4]) {
+    const int s = gi / GPS, ri = (gi % GPS) * GR + my_r;
+    const bool conv_row = s < 3;
+    // conv state of the row this lane finishes (batches of <= 2 vectors:
+    // loaded before the math; wider ones: at the epilogue, for registers)
     constexpr bool kEarly = NV <= 2;
+    const int taps = p.conv_k - 1;
+    auto load_ops = [&](int v, EpiOperands& o) {
+      const float* cs = p.conv_state + (static_cast<int64_t>(v) * p.n_conv + group_row(gi) + my_r) * taps;
+#pragma unroll
+      for (int tp = 0; tp < 3; ++tp) o.cs[tp] = tp < taps ? cs[tp] : 0.f;
+#pragma unroll
+      for (int tp = 0; tp < 4; ++tp) o.cw[tp] = cw[tp];
+    };
     EpiOperands eo[kEarly ? NV : 1];
-    const int my_r = GR == 4 ? (lane >> 3) : 0;
-    const bool mine = GR == 4 ? (lane & 7) == 0 : lane == 0;
-    const bool conv_row = gi / GPS < 3;
     if constexpr (kEarly) {
       if (mine && conv_row)
 #pragma unroll
-        for (int v = 0; v < NV; ++v) gdn_operands(p, v, group_row(gi) + my_r, eo[v]);
+        for (int v = 0; v < NV; ++v) load_ops(v, eo[v]);
     }
     float acc[GR][NV];
     tile_dot<NV, GR, J>(t, lane, nchunks, nb, xd4, sx, acc);
@@ -184,22 +207,42 @@ __global__ void __launch_bounds__(kGemvThreads, (J <= 4 ? 2 : 1)) gdn_fused_kern
       else
         c = warp_sum(acc[0][v]);
       if (mine) {
-        if constexpr (kEarly) {
-          finish(gi, my_r, v, c, eo[v]);
-        } else {
+        if (conv_row) {
           EpiOperands o;
-          if (conv_row) gdn_operands(p, v, group_row(gi) + my_r, o);
-          finish(gi, my_r, v, c, o);
+          if constexpr (kEarly)
+            o = eo[v];
+          else
+            load_ops(v, o);
+          const float y = conv_silu(p, v, group_row(gi) + my_r, c, o);
+          if (s == 2)
+            sv[v * kSeg + ri] = y;
+          else
+            push_all(cluster, (s == 0 ? qf : kf) + v * kDim + j * kSeg + ri, y);
+        } else {
+          sz[v * kSeg + ri] = silu_f(c);
         }
       }
     }
   };
   while (g < NG) {
-    run_group(A, g);
+    float cw[4] = {0.f, 0.f, 0.f, 0.f};
+    if (g < 2 * kConsumerWarps) {
+#pragma unroll
+      for (int t = 0; t < 4; ++t) cw[t] = cwA[t];
+    } else {
+      conv_w(g, cw);
+    }
+    run_group(A, g, cw);
     if (g + 2 * kConsumerWarps < NG) load_tile<GR, J>(A, p, group_row(g + 2 * kConsumerWarps), GR, lane, nchunks);
     g += kConsumerWarps;
     if (g >= NG) break;
-    run_group(B, g);
+    if (g < 2 * kConsumerWarps) {
+#pragma unroll
+      for (int t = 0; t < 4; ++t) cw[t] = cwB[t];
+    } else {
+      conv_w(g, cw);
+    }
+    run_group(B, g, cw);
     if (g + 2 * kConsumerWarps < NG) load_tile<GR, J>(B, p, group_row(g + 2 * kConsumerWarps), GR, lane, nchunks);
     g += kConsumerWarps;
   }
@@ -210,28 +253,16 @@ __global__ void __launch_bounds__(kGemvThreads, (J <= 4 ? 2 : 1)) gdn_fused_kern
     for (int v = 0; v < NV; ++v) {
       const float c = warp_sum(acc[0][v]);
       if (lane == 0) {
-        if (warp == 0)
-          sg[v] = p.a_log[h] * softplus_f(c + p.dt_bias[h]);  // decay logit (model/layers.py:99-103)
+        if (j == 0)
+          push_all(cluster, gdec + v, a_log * softplus_f(c + dt_bias));  // decay logit (model/layers.py:99-103)
         else
-          sb[v] = c;
+          push_all(cluster, gbeta + v, c);
       }
     }
   }
-  __syncthreads();
-  cluster.sync();
+  cluster.sync();  // q, k, g and beta of the head are now in every CTA
 
-  // ---- the head's q and k from every CTA of the cluster, g and beta from CTA 0
-  for (int i = tid; i < NV * 2 * kDim; i += kGemvThreads) {
-    const int v = i / (2 * kDim), w = i % (2 * kDim), which = w / kDim, e = w % kDim;
-    const float* src = cluster.map_shared_rank(which ? sk : sq, e / kSeg);
-    (which ? kf : qf)[v * kDim + e] = src[v * kSeg + e % kSeg];
-  }
-  if (tid < NV) {
-    gdec[tid] = cluster.map_shared_rank(sg, 0)[tid];
-    gbeta[tid] = cluster.map_shared_rank(sb, 0)[tid];
-  }
-  __syncthreads();
-  // L2 norms (backends.py:251-253): one warp per (vector, q|k)
+  // ---- L2 norms (backends.py:251-253): one warp per (vector, q|k)
   for (int t = warp; t < 2 * NV; t += kConsumerWarps) {
     const int v = t >> 1;
     float* x = ((t & 1) ? kf : qf) + v * kDim;
@@ -294,28 +325,26 @@ __global__ void __launch_bounds__(kGemvThreads, (J <= 4 ? 2 : 1)) gdn_fused_kern
   }
 
   // ---- gated RMSNorm over the head's 128 outputs (model/layers.py:113-116):
-  //      per-CTA sums of squares exchanged through the cluster
+  //      each CTA's sum of squares goes to every CTA, which add them in rank order
   if (warp == 0) {
     for (int v = 0; v < NV; ++v) {
       const float x = lane < kSeg ? ot[v * kSeg + lane] : 0.f;
       float ss = x * x;
 #pragma unroll
       for (int o = 8; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-      if (lane == 0) ssp[v] = ss;
+      if (lane == 0) push_all(cluster, ssq + v * kC + j, ss);
     }
   }
-  __syncthreads();
-  cluster.sync();
+  cluster.sync();  // (no shared memory of another CTA is touched after this)
   if (tid < NV * kSeg) {
     const int v = tid / kSeg, c = tid % kSeg;
     float total = 0.f;
 #pragma unroll
-    for (int r = 0; r < kC; ++r) total += cluster.map_shared_rank(ssp, r)[v];
+    for (int r = 0; r < kC; ++r) total += ssq[v * kC + r];
     const float rn = 1.0f / sqrtf(total / static_cast<float>(kDim) + P.norm_eps);
-    const float y = __fmul_rn(__fmul_rn(__fmul_rn(ot[v * kSeg + c], rn), P.norm_w[j * kSeg + c]), sz[v * kSeg + c]);
+    const float y = __fmul_rn(__fmul_rn(__fmul_rn(ot[v * kSeg + c], rn), gnw), sz[v * kSeg + c]);
     P.out[static_cast<int64_t>(v) * P.out_bs + static_cast<int64_t>(h) * kDim + j * kSeg + c] = y;
   }
-  cluster.sync();  // no CTA leaves while another may still read its shared memory
   trace_exit(p.trace);
 }
 
