@@ -3,9 +3,12 @@
     python -m breezetoken_b200.kernel_bench gemv --n 151936 --k 1024
     python -m breezetoken_b200.kernel_bench gdn --batch 64 --steps 256
     python -m breezetoken_b200.kernel_bench attn --batch 64 --ctx 32768
+    python -m breezetoken_b200.kernel_bench trace --gguf model.gguf
 
 Each prints one JSON line: average launch time and achieved HBM GB/s from
 the algorithmic bytes of one launch (weights / state / KV read once).
+``trace`` prints the device-side timeline of one Qwen3.5 decode step (per
+kernel kind: release gap, prologue, body) after a 16-token prefill.
 ``gdn`` and ``attn`` are the stand-alone decode ops of BASELINE configs 2
 and 3 with their synthetic inputs (seeds 1 and 2).
 """
@@ -109,6 +112,42 @@ def bench_attn(batch: int, ctx: int, splits: int, iters: int) -> dict:
             "gbs": nbytes / sec / 1e9}
 
 
+def trace_step(gguf: str, max_context: int, steps: int) -> str:
+    """Per-kernel-kind device timeline of a decode step (model.Qwen35.trace_step):
+    gap = previous kernel's last CTA exit -> this kernel's last CTA past the
+    dependency wait; prologue = -> last CTA ready for its main loop; body =
+    -> last CTA exit; loads = -> last CTA with its activation loads back (GEMV)."""
+    from breezetoken_b200.model import Qwen35
+
+    m = Qwen35(gguf, max_context=max_context)
+    try:
+        prompt = np.random.default_rng(0).integers(0, m.cfg.vocab, 16).tolist()
+        m.prefill([prompt])
+        for _ in range(4):
+            m.replay(1)
+        m.stream.synchronize()
+        tl = m.trace_step(steps=steps)
+    finally:
+        m.close()
+    agg: dict[str, list[float]] = {}
+    prev_end = 0.0
+    for t in tl:
+        kind = t["name"].split(".")[-1]
+        a = agg.setdefault(kind, [0, 0.0, 0.0, 0.0, 0.0, 0.0])
+        a[0] += 1
+        a[1] += t["released"] - prev_end
+        a[2] += t["ready"] - t["released"]
+        a[3] += t["end"] - t["ready"]
+        a[4] += t["end"] - prev_end
+        a[5] += (t["loaded"] - t["released"]) if t.get("loaded") else 0.0
+        prev_end = t["end"]
+    lines = [f"step: {len(tl)} kernels, {tl[-1]['end']:.1f} us from first entry to last exit",
+             f"{'kind':11s} {'n':>3s} {'total us':>9s} {'gap':>6s} {'prologue':>9s} {'(loads)':>8s} {'body':>7s}"]
+    for k, (n, gap, pro, body, tot, ld) in sorted(agg.items(), key=lambda x: -x[1][4]):
+        lines.append(f"{k:11s} {n:3d} {tot:9.1f} {gap / n:6.2f} {pro / n:9.2f} {ld / n:8.2f} {body / n:7.2f}")
+    return "\n".join(lines)
+
+
 def main() -> None:
     ap = argparse.ArgumentParser(description=__doc__)
     sub = ap.add_subparsers(dest="cmd", required=True)
@@ -124,7 +163,14 @@ def main() -> None:
     c.add_argument("--ctx", type=int, default=8192)
     c.add_argument("--splits", type=int, default=0)
     c.add_argument("--iters", type=int, default=20)
+    t = sub.add_parser("trace")
+    t.add_argument("--gguf", required=True)
+    t.add_argument("--max-context", type=int, default=1024)
+    t.add_argument("--steps", type=int, default=3)
     args = ap.parse_args()
+    if args.cmd == "trace":
+        print(trace_step(args.gguf, args.max_context, args.steps), flush=True)
+        return
     if args.cmd == "gemv":
         r = bench_gemv(args.n, args.k, args.iters)
     elif args.cmd == "gdn":

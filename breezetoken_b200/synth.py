@@ -232,3 +232,21 @@ __all__ = [
     "qwen35_tensors",
     "write_qwen35_gguf",
 ]
+
+
+def main() -> None:
+    """``python -m breezetoken_b200.synth {0.8b,tiny} OUT.gguf [--seed N]``:
+    write a seeded random-init Qwen3.5-shaped Q8_0 GGUF."""
+    import argparse
+
+    ap = argparse.ArgumentParser(description=main.__doc__)
+    ap.add_argument("shape", choices=("0.8b", "tiny"))
+    ap.add_argument("out")
+    ap.add_argument("--seed", type=int, default=0)
+    args = ap.parse_args()
+    spec = QWEN35_0_8B if args.shape == "0.8b" else QWEN35_TINY
+    print(write_qwen35_gguf(args.out, spec, seed=args.seed))
+
+
+if __name__ == "__main__":
+    main()
