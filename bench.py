@@ -214,6 +214,7 @@ def run_b200(args) -> None:
     import torch.distributed as dist
 
     from breezetoken_b200.model import Qwen35
+    from breezetoken_b200.shard import aggregate_rate, max_over_ranks, rank_prompts
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -226,8 +227,7 @@ def run_b200(args) -> None:
     path = _gguf_path(rank, world)
     B = args.batch
     model = Qwen35(path, device=f"cuda:{local}", max_context=1024, batch=B)
-    prompts = [np.random.default_rng(rank * B + b).integers(0, model.cfg.vocab, PROMPT_LEN).tolist()
-               for b in range(B)]
+    prompts = rank_prompts(rank, B, model.cfg.vocab, PROMPT_LEN)
     s = model.stream
     chunk = 16
     model.prefill(prompts)
@@ -291,12 +291,8 @@ def run_b200(args) -> None:
         done += 1
     e2e_sec = time.perf_counter() - t0
 
-    times = torch.tensor([sec, e2e_sec], dtype=torch.float64, device=model.device)
-    if world > 1:
-        dist.all_reduce(times, op=dist.ReduceOp.MAX)
-    sec, e2e_sec = float(times[0]), float(times[1])
-    tokens = args.steps * B * world
-    value = tokens / sec
+    sec, e2e_sec = max_over_ranks([sec, e2e_sec], model.device)
+    value = aggregate_rate(args.steps * B, world, sec)
 
     # step roofline: algorithmic bytes per token vs measured per-GPU token time
     mean_ctx = PROMPT_LEN + (DECODE_STEPS + 1) / 2.0
@@ -328,7 +324,7 @@ def run_b200(args) -> None:
                 "per_gpu_tok_s": per_gpu_tok_s,
             },
             "cpu_baseline": cb,
-            "e2e": {"value": e2e_steps * B * world / e2e_sec, "unit": UNIT, "h2d_bytes_per_step": 4 * B,
+            "e2e": {"value": aggregate_rate(e2e_steps * B, world, e2e_sec), "unit": UNIT, "h2d_bytes_per_step": 4 * B,
                     "d2h_bytes_per_step": 4 * B, "note": "public API: host token in, graph step, host token out, sync"},
             "gpu_launches": args.steps * model.kernels_per_step(),
             "clocks": clk.summary(),
