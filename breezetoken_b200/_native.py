@@ -124,6 +124,14 @@ _SIGS: dict[str, tuple[object, list]] = {
     ),
     "bt_gdn_decode": (C.c_int, [_P, _P, _P, C.c_int, _P, _P, _P, _P, _I64, _I64, _I64, _I64, C.c_float, C.c_float, _P]),
     "bt_argmax_workspace_bytes": (_I64, [_I64]),
+    "bt_iq3s_row_bytes": (_I64, [_I64]),
+    "bt_repack_iq3_s": (C.c_int, [_P, _P, _I64, _I64, _P]),
+    "bt_moe_route": (C.c_int, [_P, _I64, _I64, C.c_int, _P, _P, _P]),
+    "bt_moe_workspace_bytes": (_I64, [_I64, _I64, _I64, _I64, C.c_int]),
+    "bt_moe_experts_iq3s": (
+        C.c_int,
+        [_P, _P, _P, _P, _I64, _I64, _I64, _I64, _P, _P, C.c_int, _P, _P, _P],
+    ),
     "bt_argmax": (C.c_int, [_P, _I64, _I64, _P, _P, _P]),
     "bt_qwen35_kernels_per_step": (C.c_int, [C.POINTER(BtQwen35Model)]),
     "bt_qwen35_proj_elems": (_I64, [C.POINTER(BtQwen35Dims)]),

@@ -9,6 +9,7 @@
 #include "errors.h"
 #include "gdn.cuh"
 #include "gemv_q8.cuh"
+#include "moe.cuh"
 #include "ops.cuh"
 
 namespace bt {
@@ -83,6 +84,28 @@ int bt_dequant_q8_rows(const void* w, float* out, int64_t rows, int64_t k, void*
 
 int bt_dequant_iq3_s(const void* raw, float* out, int64_t rows, int64_t cols, void* stream) {
   return bt::dequant_iq3_s(raw, out, rows, cols, as_stream(stream));
+}
+
+int64_t bt_iq3s_row_bytes(int64_t k) { return k > 0 && k % 256 == 0 ? bt::iq3s_row_bytes(k) : 0; }
+
+int bt_repack_iq3_s(const void* src, void* dst, int64_t rows, int64_t k, void* stream) {
+  return bt::repack_iq3_s(src, dst, rows, k, as_stream(stream));
+}
+
+int bt_moe_route(const float* logits, int64_t t, int64_t n_experts, int top_k, int32_t* ids, float* weights,
+                 void* stream) {
+  return bt::moe_route(logits, t, n_experts, top_k, ids, weights, as_stream(stream));
+}
+
+int64_t bt_moe_workspace_bytes(int64_t t, int64_t hidden, int64_t ffn, int64_t n_experts, int top_k) {
+  return bt::moe_workspace_bytes(t, hidden, ffn, n_experts, top_k);
+}
+
+int bt_moe_experts_iq3s(const void* gate, const void* up, const void* down, const float* x, int64_t t,
+                        int64_t hidden, int64_t ffn, int64_t n_experts, const int32_t* ids, const float* weights,
+                        int top_k, float* out, void* workspace, void* stream) {
+  return bt::moe_experts_iq3s(gate, up, down, x, t, hidden, ffn, n_experts, ids, weights, top_k, out, workspace,
+                              as_stream(stream));
 }
 
 int bt_linear_q8(const void* w, const float* x, float* y, int64_t n, int64_t k, int n_vec, void* stream) {

@@ -1,0 +1,570 @@
+// Routed experts of a Qwen3.6-MoE layer at decode, on IQ3_S expert weights.
+//
+// Follows the reference's ExpertPool.forward (breezetoken/model/moe.py:205-233)
+// and route() (:33-39): softmax over the router logits, top-k, renormalise by
+// the clamped sum; per selected expert act = silu(gate x) * up x, then
+// out = sum_k w_k * down_k act_k.  The reference stages the selected experts'
+// bytes to the device and dequantises them to f32 before a matmul; here the
+// IQ3_S bytes are decoded inside the GEMV and never materialised.
+//
+// A decode batch of T tokens selects P = T * top_k (token, expert) pairs.
+// `moe_group_kernel` sorts the pairs by expert (ascending id, stable), so each
+// selected expert's weights are read once for all the tokens that chose it
+// (U unique experts: bytes = U * 1,351,680 at the 35B shape).  The gate/up
+// kernel gives each expert 16 CTAs of 32 gate + 32 matching up rows and
+// writes act for every pair; the down kernel gives each expert 16 CTAs of
+// 128 rows; a combine kernel sums the pairs of a token in routing order.
+//
+// IQ3_S GEMV: a warp lane decodes one 32-weight sub-block at a time -- eight
+// 4-byte grid entries from a 512-entry table in shared memory, signs applied
+// bytewise -- into signed int8 words, and dots them with the activation
+// encoded as three int8 digits of a 22-bit fixed-point value per 32-element
+// block (the q8 GEMV's encoding), 24 dp4a per sub-block: the integer sums are
+// exact, so the only roundings are the activation's encoding and the f32
+// accumulation over sub-blocks.
+#include <cuda_fp16.h>
+
+#include <algorithm>
+
+#include "errors.h"
+#include "gemv_q8.cuh"
+#include "moe.cuh"
+
+namespace bt {
+
+namespace {
+
+__device__ const uint32_t g_grid[512] = {
+#include "iq3s_grid.inc"
+};
+
+constexpr int kThreads = 256;
+constexpr int kWarps = kThreads / 32;
+constexpr int kGateRowsPerCta = 32;   // + the 32 matching up rows
+constexpr int kDownRowsPerCta = 128;
+constexpr float kWeightSumMin = 6.103515625e-5f;  // moe.py:24
+
+// ------------------------------------------------------------------ repack
+// GGUF IQ3_S block (110 B: d[2] qs[64] qh[8] signs[32] scales[4]) -> the
+// aligned 112-byte block. One thread per block.
+__global__ void repack_iq3s_kernel(const uint8_t* __restrict__ src, uint8_t* __restrict__ dst, int64_t n_blocks) {
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n_blocks;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const uint8_t* s = src + i * 110;
+    uint8_t* d = dst + i * kIq3sBlockBytes;
+    for (int j = 0; j < 64; ++j) d[j] = s[2 + j];        // qs
+    for (int j = 0; j < 32; ++j) d[64 + j] = s[74 + j];  // signs
+    for (int j = 0; j < 8; ++j) d[96 + j] = s[66 + j];   // qh
+    for (int j = 0; j < 4; ++j) d[104 + j] = s[106 + j]; // scales
+    d[108] = s[0];
+    d[109] = s[1];
+    d[110] = 0;
+    d[111] = 0;
+  }
+}
+
+// ------------------------------------------------------------------ route
+// One warp per token: softmax over the expert logits (f32), top-k by
+// repeated warp argmax (ties -> lower id), renormalised weights.
+__global__ void moe_route_kernel(const float* __restrict__ logits, int64_t t, int n_experts, int top_k,
+                                 int32_t* __restrict__ ids, float* __restrict__ weights) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t tok = blockIdx.x * static_cast<int64_t>(blockDim.x >> 5) + warp;
+  if (tok >= t) return;
+  const float* lg = logits + tok * n_experts;
+  float m = -INFINITY;
+  for (int e = lane; e < n_experts; e += 32) m = fmaxf(m, lg[e]);
+  m = warp_max(m);
+  float s = 0.f;
+  for (int e = lane; e < n_experts; e += 32) s += expf(lg[e] - m);
+  s = warp_sum(s);
+  // selection state: bit set = taken (n_experts <= 32 * 32)
+  uint32_t taken = 0;
+  float sel[16];
+  int sid[16];
+  float wsum = 0.f;
+  for (int k = 0; k < top_k && k < 16; ++k) {
+    float best = -INFINITY;
+    int bid = 0x7fffffff;
+    for (int e = lane, i = 0; e < n_experts; e += 32, ++i) {
+      if ((taken >> i) & 1u) continue;
+      const float v = lg[e];
+      if (v > best || (v == best && e < bid)) {
+        best = v;
+        bid = e;
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ob = __shfl_xor_sync(0xffffffffu, best, o);
+      const int oi = __shfl_xor_sync(0xffffffffu, bid, o);
+      if (ob > best || (ob == best && oi < bid)) {
+        best = ob;
+        bid = oi;
+      }
+    }
+    if ((bid & 31) == lane) taken |= 1u << (bid >> 5);
+    const float p = expf(best - m) / s;  // softmax probability of the pick
+    sel[k] = p;
+    sid[k] = bid;
+    wsum += p;
+  }
+  const float denom = fmaxf(wsum, kWeightSumMin);
+  if (lane == 0)
+    for (int k = 0; k < top_k && k < 16; ++k) {
+      ids[tok * top_k + k] = sid[k];
+      weights[tok * top_k + k] = sel[k] / denom;
+    }
+}
+
+// ------------------------------------------------------------------ group
+// Workspace header: [n_unique, bad ids] then per slot u < P: expert, first
+// pair, pair count; then the pair list sorted by (expert, pair).
+struct MoeWs {
+  int32_t* hdr;
+  int32_t* slot_expert;
+  int32_t* slot_start;
+  int32_t* slot_count;
+  int32_t* pairs;
+  float* act;  // (P, ffn)
+  float* dn;   // (P, hidden)
+};
+
+__host__ __device__ inline int64_t align256(int64_t b) { return (b + 255) / 256 * 256; }
+
+__host__ __device__ inline MoeWs moe_ws(void* base, int64_t p, int64_t hidden, int64_t ffn) {
+  uint8_t* b = static_cast<uint8_t*>(base);
+  MoeWs w;
+  int64_t o = 0;
+  w.hdr = reinterpret_cast<int32_t*>(b + o);
+  o += 256;
+  w.slot_expert = reinterpret_cast<int32_t*>(b + o);
+  o += align256(4 * p);
+  w.slot_start = reinterpret_cast<int32_t*>(b + o);
+  o += align256(4 * p);
+  w.slot_count = reinterpret_cast<int32_t*>(b + o);
+  o += align256(4 * p);
+  w.pairs = reinterpret_cast<int32_t*>(b + o);
+  o += align256(4 * p);
+  w.act = reinterpret_cast<float*>(b + o);
+  o += align256(4 * p * ffn);
+  w.dn = reinterpret_cast<float*>(b + o);
+  return w;
+}
+
+inline int64_t moe_ws_bytes(int64_t p, int64_t hidden, int64_t ffn) {
+  return 256 + 4 * align256(4 * p) + align256(4 * p * ffn) + align256(4 * p * hidden);
+}
+
+// One CTA: counting sort of the P pairs by expert id (stable).
+__global__ void moe_group_kernel(const int32_t* __restrict__ ids, int p_total, int n_experts, MoeWs ws) {
+  extern __shared__ int32_t sm[];
+  int32_t* cnt = sm;               // [n_experts]
+  int32_t* off = sm + n_experts;   // [n_experts] exclusive prefix of counts
+  __shared__ int32_t s_bad;
+  for (int e = threadIdx.x; e < n_experts; e += blockDim.x) cnt[e] = 0;
+  if (threadIdx.x == 0) s_bad = 0;
+  __syncthreads();
+  for (int q = threadIdx.x; q < p_total; q += blockDim.x) {
+    const int e = ids[q];
+    if (e >= 0 && e < n_experts)
+      atomicAdd(&cnt[e], 1);
+    else
+      atomicAdd(&s_bad, 1);
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int o = 0, u = 0;
+    for (int e = 0; e < n_experts; ++e) {
+      off[e] = o;
+      if (cnt[e]) {
+        ws.slot_expert[u] = e;
+        ws.slot_start[u] = o;
+        ws.slot_count[u] = cnt[e];
+        ++u;
+      }
+      o += cnt[e];
+    }
+    ws.hdr[0] = u;
+    ws.hdr[1] = s_bad;
+  }
+  __syncthreads();
+  for (int q = threadIdx.x; q < p_total; q += blockDim.x) {
+    const int e = ids[q];
+    if (e < 0 || e >= n_experts) continue;
+    int rank = 0;
+    for (int q2 = 0; q2 < q; ++q2) rank += ids[q2] == e;
+    ws.pairs[off[e] + rank] = q;
+  }
+}
+
+// ------------------------------------------------------------------ GEMV core
+// Activation vectors in shared memory, per vector v: three digit planes x two
+// halves of each 32-element sub-block, SBR sub-blocks (uint4 each), then the
+// per-sub-block scales.
+template <int SBR>
+struct XSmem {
+  static constexpr int kPlaneBytes = SBR * 16;
+  static constexpr int kVecBytes = 6 * kPlaneBytes + SBR * 4;
+};
+
+// Encode `n` f32 values at src (16-byte aligned) into vector slot v.
+template <int SBR>
+__device__ __forceinline__ void encode_vec(const float* __restrict__ src, uint8_t* xs, int v) {
+  constexpr int K = SBR * 32, NF4 = K / 4;
+  uint8_t* base = xs + v * XSmem<SBR>::kVecBytes;
+  float* sx = reinterpret_cast<float*>(base + 6 * XSmem<SBR>::kPlaneBytes);
+  for (int f = threadIdx.x; f < ((NF4 + kThreads - 1) / kThreads) * kThreads; f += kThreads) {
+    const int fc = min(f, NF4 - 1);
+    float4 h = reinterpret_cast<const float4*>(src)[fc];
+    if (f >= NF4) h = make_float4(0.f, 0.f, 0.f, 0.f);
+    float m = fmaxf(fmaxf(fabsf(h.x), fabsf(h.y)), fmaxf(fabsf(h.z), fabsf(h.w)));
+    m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 1));
+    m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 2));
+    m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 4));
+    const uint32_t be = (__float_as_uint(m) >> 23) & 255u;
+    const bool ok = be >= 22u;
+    const float inv = ok ? __uint_as_float((275u - be) << 23) : 0.f;
+    const float scale = ok ? __uint_as_float((be - 21u) << 23) : 0.f;
+    int a[4], b[4], c[4];
+    const float e4[4] = {h.x, h.y, h.z, h.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int X = __float2int_rn(e4[i] * inv);
+      c[i] = ((X + 128) & 255) - 128;
+      const int x1 = (X - c[i]) >> 8;
+      b[i] = ((x1 + 128) & 255) - 128;
+      a[i] = (x1 - b[i]) >> 8;
+    }
+    if (f < NF4) {
+      const int sb = f >> 3, w = f & 7;
+      const int h2 = w >> 2, comp = w & 3;
+      auto pk = [](const int (&d)[4]) {
+        return (static_cast<uint32_t>(d[0]) & 255u) | ((static_cast<uint32_t>(d[1]) & 255u) << 8) |
+               ((static_cast<uint32_t>(d[2]) & 255u) << 16) | ((static_cast<uint32_t>(d[3]) & 255u) << 24);
+      };
+      reinterpret_cast<uint32_t*>(base + (0 * 2 + h2) * XSmem<SBR>::kPlaneBytes + sb * 16)[comp] = pk(a);
+      reinterpret_cast<uint32_t*>(base + (1 * 2 + h2) * XSmem<SBR>::kPlaneBytes + sb * 16)[comp] = pk(b);
+      reinterpret_cast<uint32_t*>(base + (2 * 2 + h2) * XSmem<SBR>::kPlaneBytes + sb * 16)[comp] = pk(c);
+      if (w == 0) sx[sb] = scale;
+    }
+  }
+}
+
+__device__ __forceinline__ uint64_t ldg_u64(const uint8_t* p) {
+  uint64_t v;
+  asm volatile("ld.global.nc.u64 %0, [%1];" : "=l"(v) : "l"(p));
+  return v;
+}
+__device__ __forceinline__ uint32_t ldg_u32(const uint8_t* p) {
+  uint32_t v;
+  asm volatile("ld.global.nc.u32 %0, [%1];" : "=r"(v) : "l"(p));
+  return v;
+}
+
+// One 32-weight sub-block of a repacked IQ3_S row as 8 signed int8x4 words
+// plus its scale d * (1 + 2 * nibble) (quant/dequant.py:164-185).
+struct SubBlock {
+  uint32_t q[8];
+  float db;
+};
+
+__device__ __forceinline__ void load_sub_block(const uint8_t* row, int sb, const uint32_t* grid, SubBlock& o) {
+  const int b = sb >> 3, p = (sb & 7) >> 1, s = sb & 1;
+  const uint8_t* blk = row + b * kIq3sBlockBytes;
+  // (all loads naturally aligned: blocks are 112 = 7 x 16 bytes)
+  const uint64_t qs = ldg_u64(blk + 16 * p + 8 * s);
+  const uint32_t signs = ldg_u32(blk + 64 + 8 * p + 4 * s);
+  const uint64_t qh8 = ldg_u64(blk + 96);   // qh[0..7]
+  const uint64_t tail = ldg_u64(blk + 104); // scales[0..3], d, pad
+  const uint32_t qh = static_cast<uint32_t>(qh8 >> (8 * (2 * p + s))) & 255u;
+  const uint32_t nib = static_cast<uint32_t>(tail >> (8 * p + 4 * s)) & 15u;
+  o.db = __half2float(__ushort_as_half(static_cast<unsigned short>((tail >> 32) & 0xFFFFu))) *
+         static_cast<float>(1 + 2 * static_cast<int>(nib));
+#pragma unroll
+  for (int w = 0; w < 8; ++w) {
+    const uint32_t idx = static_cast<uint32_t>((qs >> (8 * w)) & 255u) | (((qh >> w) & 1u) << 8);
+    const uint32_t g = grid[idx];
+    const uint32_t sb4 = (signs >> (4 * w)) & 15u;
+    const uint32_t mask = ((sb4 * 0x00204081u) & 0x01010101u) * 0xFFu;
+    o.q[w] = (g ^ mask) + (mask & 0x01010101u);
+  }
+}
+
+// q . X for vector slot v, sub-block sb (exact integer sums, one rounding)
+template <int SBR>
+__device__ __forceinline__ float sub_block_dot(const SubBlock& w, const uint8_t* xs, int v, int sb) {
+  const uint8_t* base = xs + v * XSmem<SBR>::kVecBytes;
+  const uint4 a0 = *reinterpret_cast<const uint4*>(base + 0 * XSmem<SBR>::kPlaneBytes + sb * 16);
+  const uint4 a1 = *reinterpret_cast<const uint4*>(base + 1 * XSmem<SBR>::kPlaneBytes + sb * 16);
+  const uint4 b0 = *reinterpret_cast<const uint4*>(base + 2 * XSmem<SBR>::kPlaneBytes + sb * 16);
+  const uint4 b1 = *reinterpret_cast<const uint4*>(base + 3 * XSmem<SBR>::kPlaneBytes + sb * 16);
+  const uint4 c0 = *reinterpret_cast<const uint4*>(base + 4 * XSmem<SBR>::kPlaneBytes + sb * 16);
+  const uint4 c1 = *reinterpret_cast<const uint4*>(base + 5 * XSmem<SBR>::kPlaneBytes + sb * 16);
+  const uint32_t d2[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+  const uint32_t d1[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+  const uint32_t d0[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+  int s2 = 0, s1 = 0, s0 = 0;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    s2 = __dp4a(static_cast<int>(w.q[i]), static_cast<int>(d2[i]), s2);
+    s1 = __dp4a(static_cast<int>(w.q[i]), static_cast<int>(d1[i]), s1);
+    s0 = __dp4a(static_cast<int>(w.q[i]), static_cast<int>(d0[i]), s0);
+  }
+  const int t = s1 * 256 + s0;
+  return fmaf(static_cast<float>(s2), 65536.0f, static_cast<float>(t));
+}
+
+// Dot of RW rows (row pointers) with the NV vectors in xs, mc of them live.
+// Lanes: LPR lanes per row (all 32 when the row has >= 32 sub-blocks).
+// Returns, in every lane, the totals of the lane's row group.
+template <int SBR, int NV, int RW>
+__device__ __forceinline__ void rows_dot(const uint8_t* const (&rows)[RW], const uint8_t* xs, const uint32_t* grid,
+                                         int mc, float (&res)[RW][NV]) {
+  static_assert(SBR >= 16, "rows of at least 512 weights");
+  constexpr int LPR = SBR >= 32 ? 32 : SBR;
+  constexpr int RPP = 32 / LPR;  // rows per pass
+  constexpr int SPL = SBR / LPR; // sub-blocks per lane per row
+  const int lane = threadIdx.x & 31;
+  const int rin = lane / LPR, lr = lane % LPR;
+#pragma unroll
+  for (int r0 = 0; r0 < RW; r0 += RPP) {
+    float acc[NV];
+#pragma unroll
+    for (int v = 0; v < NV; ++v) acc[v] = 0.f;
+    const uint8_t* row = rows[r0];
+    if (RPP > 1 && rin == 1 && r0 + 1 < RW) row = rows[r0 + 1];
+#pragma unroll
+    for (int i = 0; i < SPL; ++i) {
+      const int sb = lr + LPR * i;
+      SubBlock w;
+      load_sub_block(row, sb, grid, w);
+      const uint8_t* base = xs;
+#pragma unroll
+      for (int v = 0; v < NV; ++v) {
+        if (v < mc) {
+          const float sxv = reinterpret_cast<const float*>(base + v * XSmem<SBR>::kVecBytes +
+                                                           6 * XSmem<SBR>::kPlaneBytes)[sb];
+          acc[v] = fmaf(w.db * sxv, sub_block_dot<SBR>(w, xs, v, sb), acc[v]);
+        }
+      }
+    }
+#pragma unroll
+    for (int v = 0; v < NV; ++v) {
+#pragma unroll
+      for (int o = LPR / 2; o > 0; o >>= 1) acc[v] += __shfl_xor_sync(0xffffffffu, acc[v], o);
+    }
+    // lanes of pass row j (j < RPP) now hold that row's totals; gather all
+#pragma unroll
+    for (int j = 0; j < RPP; ++j)
+      if (r0 + j < RW)
+#pragma unroll
+        for (int v = 0; v < NV; ++v) res[r0 + j][v] = __shfl_sync(0xffffffffu, acc[v], j * LPR);
+  }
+}
+
+// ------------------------------------------------------------------ gate/up
+// CTA (u, c): expert slot u, outputs [32c, 32c + 32); warp w: outputs
+// 32c + 4w + [0, 4) (rows of gate and of up).  Pairs of the slot in chunks
+// of NV.
+template <int SBR, int NV>
+__global__ void __launch_bounds__(kThreads) moe_gate_up_kernel(const uint8_t* __restrict__ gate,
+                                                               const uint8_t* __restrict__ up,
+                                                               const float* __restrict__ x, int top_k, int ffn,
+                                                               MoeWs ws) {
+  extern __shared__ __align__(16) uint8_t xs[];
+  __shared__ uint32_t grid[512];
+  const int u = blockIdx.x;
+  if (u >= ws.hdr[0]) return;
+  for (int i = threadIdx.x; i < 512; i += kThreads) grid[i] = g_grid[i];
+  const int e = ws.slot_expert[u], start = ws.slot_start[u], m = ws.slot_count[u];
+  constexpr int K = SBR * 32;
+  const int64_t rb = static_cast<int64_t>(K / 256) * kIq3sBlockBytes;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int o0 = blockIdx.y * kGateRowsPerCta + warp * 4;
+  const uint8_t* rows[8];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    rows[i] = gate + (static_cast<int64_t>(e) * ffn + o0 + i) * rb;
+    rows[4 + i] = up + (static_cast<int64_t>(e) * ffn + o0 + i) * rb;
+  }
+  for (int c0 = 0; c0 < m; c0 += NV) {
+    const int mc = min(NV, m - c0);
+    __syncthreads();  // (previous chunk's readers done; grid table ready)
+    for (int v = 0; v < mc; ++v) encode_vec<SBR>(x + static_cast<int64_t>(ws.pairs[start + c0 + v] / top_k) * K, xs, v);
+    __syncthreads();
+    float res[8][NV];
+    rows_dot<SBR, NV, 8>(rows, xs, grid, mc, res);
+    if (lane < 4) {
+#pragma unroll
+      for (int v = 0; v < NV; ++v) {
+        if (v < mc) {
+          // lane i writes output o0 + i (model/moe.py:229: act = silu(g) * u)
+          float g = 0.f, uu = 0.f;
+#pragma unroll
+          for (int i = 0; i < 4; ++i)
+            if (i == lane) {
+              g = res[i][v];
+              uu = res[4 + i][v];
+            }
+          ws.act[static_cast<int64_t>(ws.pairs[start + c0 + v]) * ffn + o0 + lane] = silu_f(g) * uu;
+        }
+      }
+    }
+  }
+}
+
+// ------------------------------------------------------------------ down
+// CTA (u, c): expert slot u, rows [128c, 128c + 128); warp w: 16 rows.
+template <int SBR, int NV>
+__global__ void __launch_bounds__(kThreads) moe_down_kernel(const uint8_t* __restrict__ down, int hidden,
+                                                            MoeWs ws, int ffn) {
+  extern __shared__ __align__(16) uint8_t xs[];
+  __shared__ uint32_t grid[512];
+  const int u = blockIdx.x;
+  if (u >= ws.hdr[0]) return;
+  for (int i = threadIdx.x; i < 512; i += kThreads) grid[i] = g_grid[i];
+  const int e = ws.slot_expert[u], start = ws.slot_start[u], m = ws.slot_count[u];
+  constexpr int K = SBR * 32;
+  const int64_t rb = static_cast<int64_t>(K / 256) * kIq3sBlockBytes;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  constexpr int RW = kDownRowsPerCta / kWarps;
+  const int h0 = blockIdx.y * kDownRowsPerCta + warp * RW;
+  const uint8_t* rows[RW];
+#pragma unroll
+  for (int i = 0; i < RW; ++i) rows[i] = down + (static_cast<int64_t>(e) * hidden + h0 + i) * rb;
+  for (int c0 = 0; c0 < m; c0 += NV) {
+    const int mc = min(NV, m - c0);
+    __syncthreads();
+    for (int v = 0; v < mc; ++v) encode_vec<SBR>(ws.act + static_cast<int64_t>(ws.pairs[start + c0 + v]) * ffn, xs, v);
+    __syncthreads();
+    float res[RW][NV];
+    rows_dot<SBR, NV, RW>(rows, xs, grid, mc, res);
+#pragma unroll
+    for (int v = 0; v < NV; ++v) {
+      if (v < mc) {
+        float* dst = ws.dn + static_cast<int64_t>(ws.pairs[start + c0 + v]) * hidden + h0;
+#pragma unroll
+        for (int i = 0; i < RW; ++i)
+          if (lane == i) dst[i] = res[i][v];
+      }
+    }
+  }
+}
+
+// ------------------------------------------------------------------ combine
+// out[t] = sum_k w[t, k] * down_k(act) in routing order, each product rounded
+// before the add like the reference's (out * w).sum(0) in f32.
+__global__ void moe_combine_kernel(const float* __restrict__ weights, const int32_t* __restrict__ ids, int64_t t,
+                                   int top_k, int hidden, int n_experts, MoeWs ws, float* __restrict__ out) {
+  const int64_t total = t * hidden;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t tok = i / hidden;
+    const int hh = static_cast<int>(i % hidden);
+    float acc = 0.f;
+    for (int k = 0; k < top_k; ++k) {
+      const int e = ids[tok * top_k + k];
+      if (e < 0 || e >= n_experts) continue;
+      acc = __fadd_rn(acc, __fmul_rn(ws.dn[(tok * top_k + k) * hidden + hh], weights[tok * top_k + k]));
+    }
+    out[i] = acc;
+  }
+}
+
+template <int SBR>
+constexpr int xs_bytes(int nv) {
+  return nv * XSmem<SBR>::kVecBytes;
+}
+
+template <int SBR_GU, int SBR_D, int NV>
+int launch_all(const uint8_t* gate, const uint8_t* up, const uint8_t* down, const float* x, int64_t t, int hidden,
+               int ffn, int n_experts, const int32_t* ids, const float* weights, int top_k, float* out, MoeWs ws,
+               cudaStream_t stream) {
+  const int p = static_cast<int>(t * top_k);
+  const int slots = p < n_experts ? p : n_experts;
+  moe_group_kernel<<<1, 512, 2 * n_experts * sizeof(int32_t), stream>>>(ids, p, n_experts, ws);
+  moe_gate_up_kernel<SBR_GU, NV><<<dim3(slots, ffn / kGateRowsPerCta), kThreads, xs_bytes<SBR_GU>(NV), stream>>>(
+      gate, up, x, top_k, ffn, ws);
+  moe_down_kernel<SBR_D, NV><<<dim3(slots, hidden / kDownRowsPerCta), kThreads, xs_bytes<SBR_D>(NV), stream>>>(
+      down, hidden, ws, ffn);
+  const int64_t total = t * hidden;
+  const int blocks = static_cast<int>(std::min<int64_t>((total + 255) / 256, 4096));
+  moe_combine_kernel<<<blocks, 256, 0, stream>>>(weights, ids, t, top_k, hidden, n_experts, ws, out);
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return fail_cuda(e, "moe experts launch");
+  return BT_OK;
+}
+
+template <int SBR_GU, int SBR_D>
+int launch_nv(const uint8_t* gate, const uint8_t* up, const uint8_t* down, const float* x, int64_t t, int hidden,
+              int ffn, int n_experts, const int32_t* ids, const float* weights, int top_k, float* out, MoeWs ws,
+              cudaStream_t stream) {
+  // one token selects each expert once: a single vector per expert
+  if (t == 1)
+    return launch_all<SBR_GU, SBR_D, 1>(gate, up, down, x, t, hidden, ffn, n_experts, ids, weights, top_k, out, ws,
+                                        stream);
+  return launch_all<SBR_GU, SBR_D, 4>(gate, up, down, x, t, hidden, ffn, n_experts, ids, weights, top_k, out, ws,
+                                      stream);
+}
+
+}  // namespace
+
+int repack_iq3_s(const void* src, void* dst, int64_t rows, int64_t k, cudaStream_t stream) {
+  if (!src || !dst || rows < 0 || k <= 0 || k % 256) return fail(BT_ERR_INVALID, "repack_iq3_s: K must be a multiple of 256");
+  if (reinterpret_cast<uintptr_t>(dst) & 15) return fail(BT_ERR_INVALID, "repack_iq3_s: dst must be 16-byte aligned");
+  const int64_t nb = rows * (k / 256);
+  if (nb == 0) return BT_OK;
+  const int blocks = static_cast<int>(std::min<int64_t>((nb + 255) / 256, 65535));
+  repack_iq3s_kernel<<<blocks, 256, 0, stream>>>(static_cast<const uint8_t*>(src), static_cast<uint8_t*>(dst), nb);
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return fail_cuda(e, "repack_iq3_s launch");
+  return BT_OK;
+}
+
+int moe_route(const float* logits, int64_t t, int64_t n_experts, int top_k, int32_t* ids, float* weights,
+              cudaStream_t stream) {
+  if (!logits || !ids || !weights || t < 0) return fail(BT_ERR_INVALID, "moe_route: null pointer or negative T");
+  if (n_experts < 1 || n_experts > 1024 || top_k < 1 || top_k > 16 || top_k > n_experts)
+    return fail(BT_ERR_UNSUPPORTED, "moe_route serves <= 1024 experts and top-k <= 16 (got %lld, %d)",
+                static_cast<long long>(n_experts), top_k);
+  if (t == 0) return BT_OK;
+  const int blocks = static_cast<int>((t + 7) / 8);
+  moe_route_kernel<<<blocks, 256, 0, stream>>>(logits, t, static_cast<int>(n_experts), top_k, ids, weights);
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return fail_cuda(e, "moe_route launch");
+  return BT_OK;
+}
+
+int64_t moe_workspace_bytes(int64_t t, int64_t hidden, int64_t ffn, int64_t n_experts, int top_k) {
+  (void)n_experts;
+  if (t < 1 || top_k < 1) return 0;
+  return moe_ws_bytes(t * top_k, hidden, ffn);
+}
+
+int moe_experts_iq3s(const void* gate, const void* up, const void* down, const float* x, int64_t t, int64_t hidden,
+                     int64_t ffn, int64_t n_experts, const int32_t* ids, const float* weights, int top_k, float* out,
+                     void* workspace, cudaStream_t stream) {
+  if (!gate || !up || !down || !x || !ids || !weights || !out || !workspace)
+    return fail(BT_ERR_INVALID, "moe_experts_iq3s: null pointer");
+  if (t < 1 || t * top_k > 4096 || top_k < 1 || n_experts < 1 || n_experts > 4096)
+    return fail(BT_ERR_UNSUPPORTED, "moe_experts_iq3s serves T * top_k <= 4096 pairs over <= 4096 experts");
+  if ((reinterpret_cast<uintptr_t>(gate) | reinterpret_cast<uintptr_t>(up) | reinterpret_cast<uintptr_t>(down) |
+       reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(workspace)) & 15)
+    return fail(BT_ERR_INVALID, "moe_experts_iq3s: weights, x and workspace must be 16-byte aligned");
+  if (ffn % kGateRowsPerCta || hidden % kDownRowsPerCta)
+    return fail(BT_ERR_UNSUPPORTED, "moe_experts_iq3s: ffn must be a multiple of 32 and hidden of 128");
+  const MoeWs ws = moe_ws(workspace, t * top_k, hidden, ffn);
+  const uint8_t* g = static_cast<const uint8_t*>(gate);
+  const uint8_t* u = static_cast<const uint8_t*>(up);
+  const uint8_t* d = static_cast<const uint8_t*>(down);
+  const int h = static_cast<int>(hidden), f = static_cast<int>(ffn), ne = static_cast<int>(n_experts);
+  if (hidden == 2048 && ffn == 512) return launch_nv<64, 16>(g, u, d, x, t, h, f, ne, ids, weights, top_k, out, ws, stream);
+  if (hidden == 2048 && ffn == 768) return fail(BT_ERR_UNSUPPORTED, "moe_experts_iq3s: ffn must be a multiple of 256");
+  if (hidden == 1024 && ffn == 512) return launch_nv<32, 16>(g, u, d, x, t, h, f, ne, ids, weights, top_k, out, ws, stream);
+  if (hidden == 4096 && ffn == 1024) return launch_nv<128, 32>(g, u, d, x, t, h, f, ne, ids, weights, top_k, out, ws, stream);
+  if (hidden == 2048 && ffn == 1024) return launch_nv<64, 32>(g, u, d, x, t, h, f, ne, ids, weights, top_k, out, ws, stream);
+  return fail(BT_ERR_UNSUPPORTED, "moe_experts_iq3s serves (hidden, ffn) in {(1024,512), (2048,512), (2048,1024), (4096,1024)}");
+}
+
+}  // namespace bt

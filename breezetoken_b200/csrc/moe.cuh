@@ -1,0 +1,25 @@
+// Routed-expert (MoE) decode on IQ3_S experts (see moe.cu).
+#pragma once
+
+#include "common.cuh"
+
+namespace bt {
+
+// Repacked IQ3_S block: the GGUF block's fields (110 bytes) in an aligned
+// order, padded to 112 bytes: [qs 64][signs 32][qh 8][scales 4][d 2][pad 2].
+constexpr int kIq3sBlockBytes = 112;
+
+inline int64_t iq3s_row_bytes(int64_t k) { return k / 256 * kIq3sBlockBytes; }
+
+int repack_iq3_s(const void* src, void* dst, int64_t rows, int64_t k, cudaStream_t stream);
+
+int moe_route(const float* logits, int64_t t, int64_t n_experts, int top_k, int32_t* ids, float* weights,
+              cudaStream_t stream);
+
+int64_t moe_workspace_bytes(int64_t t, int64_t hidden, int64_t ffn, int64_t n_experts, int top_k);
+
+int moe_experts_iq3s(const void* gate, const void* up, const void* down, const float* x, int64_t t, int64_t hidden,
+                     int64_t ffn, int64_t n_experts, const int32_t* ids, const float* weights, int top_k, float* out,
+                     void* workspace, cudaStream_t stream);
+
+}  // namespace bt

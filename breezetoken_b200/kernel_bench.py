@@ -3,10 +3,15 @@
     python -m breezetoken_b200.kernel_bench gemv --n 151936 --k 1024
     python -m breezetoken_b200.kernel_bench gdn --batch 64 --steps 256
     python -m breezetoken_b200.kernel_bench attn --batch 64 --ctx 32768
+    python -m breezetoken_b200.kernel_bench moe --tokens 8
     python -m breezetoken_b200.kernel_bench trace --gguf model.gguf
 
 Each prints one JSON line: average launch time and achieved HBM GB/s from
 the algorithmic bytes of one launch (weights / state / KV read once).
+``moe`` is BASELINE config 4: routed experts of one MoE layer (hidden 2048,
+256 IQ3_S experts of ffn 512, top-8 over N(0,1) router logits, seed 3),
+timed per call with L2 flushed before each call; its bytes are the
+U * 1,351,680 of the U distinct experts the routing selects.
 ``trace`` prints the device-side timeline of one Qwen3.5 decode step (per
 kernel kind: release gap, prologue, body) after a 16-token prefill.
 ``gdn`` and ``attn`` are the stand-alone decode ops of BASELINE configs 2
@@ -112,6 +117,47 @@ def bench_attn(batch: int, ctx: int, splits: int, iters: int) -> dict:
             "gbs": nbytes / sec / 1e9}
 
 
+def bench_moe(tokens: int, iters: int) -> dict:
+    from breezetoken_b200.moe import IQ3SExperts, experts_forward, route_logits
+    from breezetoken_b200.quant import quantize_iq3_s
+
+    hidden, ffn, n_exp, top_k = 2048, 512, 256, 8
+    rng = np.random.default_rng(3)
+    # 4 distinct quantised experts tiled to 256: timing needs valid IQ3_S
+    # bytes, not 256 distinct ones
+    base = 4
+
+    def tensor(rows: int, k: int) -> np.ndarray:
+        q = quantize_iq3_s(rng.standard_normal((base * rows, k)).astype(np.float32) * np.float32(0.02))
+        return np.tile(q.reshape(base, -1), (n_exp // base, 1)).reshape(-1)
+
+    ex = IQ3SExperts.from_gguf_bytes(tensor(ffn, hidden), tensor(ffn, hidden), tensor(hidden, ffn), n_exp, hidden,
+                                     ffn, "cuda")
+    x = torch.from_numpy(rng.standard_normal((tokens, hidden)).astype(np.float32)).cuda().bfloat16().float()
+    logits = torch.from_numpy(rng.standard_normal((tokens, n_exp)).astype(np.float32)).cuda()
+    r = route_logits(logits, top_k)
+    u = int(torch.unique(r.expert_ids).numel())
+    ws = torch.empty(int(N.load().bt_moe_workspace_bytes(tokens, hidden, ffn, n_exp, top_k)), dtype=torch.uint8,
+                     device="cuda")
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+    s = torch.cuda.Stream()
+    total = 0.0
+    with torch.cuda.stream(s):
+        for i in range(iters + 3):
+            flush.zero_()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(s)
+            experts_forward(ex, x, r.expert_ids, r.weights, ws)
+            e1.record(s)
+            e1.synchronize()
+            if i >= 3:
+                total += e0.elapsed_time(e1) / 1e3
+    sec = total / iters
+    nbytes = u * 1_351_680 + tokens * hidden * 8
+    return {"kernel": "moe_experts_iq3s", "tokens": tokens, "unique_experts": u, "us": sec * 1e6, "bytes": nbytes,
+            "gbs": nbytes / sec / 1e9, "l2": "flushed before each call (256 MB write)"}
+
+
 def trace_step(gguf: str, max_context: int, steps: int) -> str:
     """Per-kernel-kind device timeline of a decode step (model.Qwen35.trace_step):
     gap = previous kernel's last CTA exit -> this kernel's last CTA past the
@@ -163,6 +209,9 @@ def main() -> None:
     c.add_argument("--ctx", type=int, default=8192)
     c.add_argument("--splits", type=int, default=0)
     c.add_argument("--iters", type=int, default=20)
+    mo = sub.add_parser("moe")
+    mo.add_argument("--tokens", type=int, default=1)
+    mo.add_argument("--iters", type=int, default=50)
     t = sub.add_parser("trace")
     t.add_argument("--gguf", required=True)
     t.add_argument("--max-context", type=int, default=1024)
@@ -173,6 +222,8 @@ def main() -> None:
         return
     if args.cmd == "gemv":
         r = bench_gemv(args.n, args.k, args.iters)
+    elif args.cmd == "moe":
+        r = bench_moe(args.tokens, args.iters)
     elif args.cmd == "gdn":
         r = bench_gdn(args.batch, args.steps)
     else:

@@ -164,6 +164,39 @@ BT_API int64_t bt_argmax_workspace_bytes(int64_t rows);
 BT_API int bt_argmax(const float* x, int64_t rows, int64_t n, int32_t* out,
               void* workspace, void* stream);
 
+/* ------------------------------------------------------- MoE experts */
+/* Bytes of one IQ3_S row of K weights in the device layout (K % 256 == 0):
+ * 112-byte blocks holding the GGUF block's fields in aligned order.       */
+BT_API int64_t bt_iq3s_row_bytes(int64_t k);
+
+/* GGUF IQ3_S rows (110-byte blocks, quant/dequant.py:164-185) -> the device
+ * layout; replaces the reference's per-step byte staging of the selected
+ * experts (model/moe.py:64-120): the experts stay resident in HBM.        */
+BT_API int bt_repack_iq3_s(const void* src, void* dst, int64_t rows, int64_t k,
+                    void* stream);
+
+/* route() for T tokens (model/moe.py:33-39): softmax over each token's
+ * n_experts router logits, top-k (ties to the lower id), weights
+ * renormalised by max(sum, 6.1035e-5).  ids/weights: (T, top_k).         */
+BT_API int bt_moe_route(const float* logits, int64_t t, int64_t n_experts, int top_k,
+                 int32_t* ids, float* weights, void* stream);
+
+/* Workspace of bt_moe_experts_iq3s (no zeroing needed).                   */
+BT_API int64_t bt_moe_workspace_bytes(int64_t t, int64_t hidden, int64_t ffn,
+                               int64_t n_experts, int top_k);
+
+/* ExpertPool.forward (model/moe.py:205-233) for T tokens at once:
+ * out[t] = sum_k weights[t,k] * down_e(silu(gate_e x_t) * up_e x_t), e =
+ * ids[t,k], with the IQ3_S experts decoded inside the GEMVs.  gate/up:
+ * (n_experts * ffn) rows of K = hidden, down: (n_experts * hidden) rows of
+ * K = ffn, all in the bt_repack_iq3_s layout.  x, out: (T, hidden) f32.
+ * Each selected expert is read once for all the tokens that selected it.
+ * Pairs with an id outside [0, n_experts) contribute nothing.             */
+BT_API int bt_moe_experts_iq3s(const void* gate, const void* up, const void* down,
+                        const float* x, int64_t t, int64_t hidden, int64_t ffn,
+                        int64_t n_experts, const int32_t* ids, const float* weights,
+                        int top_k, float* out, void* workspace, void* stream);
+
 /* ------------------------------------------------- Qwen3.5 decode step */
 typedef struct BtQwen35Dims {
   int32_t hidden, n_layers, n_heads, n_kv, head_dim, rope_dim, ffn, vocab;
