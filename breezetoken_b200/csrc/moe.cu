@@ -251,17 +251,6 @@ __device__ __forceinline__ void encode_vec(const float* __restrict__ src, uint8_
   }
 }
 
-__device__ __forceinline__ uint64_t ldg_u64(const uint8_t* p) {
-  uint64_t v;
-  asm volatile("ld.global.nc.u64 %0, [%1];" : "=l"(v) : "l"(p));
-  return v;
-}
-__device__ __forceinline__ uint32_t ldg_u32(const uint8_t* p) {
-  uint32_t v;
-  asm volatile("ld.global.nc.u32 %0, [%1];" : "=r"(v) : "l"(p));
-  return v;
-}
-
 // One 32-weight sub-block of a repacked IQ3_S row as 8 signed int8x4 words
 // plus its scale d * (1 + 2 * nibble) (quant/dequant.py:164-185).
 struct SubBlock {
@@ -270,13 +259,14 @@ struct SubBlock {
 };
 
 __device__ __forceinline__ void load_sub_block(const uint8_t* row, int sb, const uint32_t* grid, SubBlock& o) {
+  // `row` is a shared-memory copy; all loads are naturally aligned (blocks
+  // are 112 = 7 x 16 bytes)
   const int b = sb >> 3, p = (sb & 7) >> 1, s = sb & 1;
   const uint8_t* blk = row + b * kIq3sBlockBytes;
-  // (all loads naturally aligned: blocks are 112 = 7 x 16 bytes)
-  const uint64_t qs = ldg_u64(blk + 16 * p + 8 * s);
-  const uint32_t signs = ldg_u32(blk + 64 + 8 * p + 4 * s);
-  const uint64_t qh8 = ldg_u64(blk + 96);   // qh[0..7]
-  const uint64_t tail = ldg_u64(blk + 104); // scales[0..3], d, pad
+  const uint64_t qs = *reinterpret_cast<const uint64_t*>(blk + 16 * p + 8 * s);
+  const uint32_t signs = *reinterpret_cast<const uint32_t*>(blk + 64 + 8 * p + 4 * s);
+  const uint64_t qh8 = *reinterpret_cast<const uint64_t*>(blk + 96);   // qh[0..7]
+  const uint64_t tail = *reinterpret_cast<const uint64_t*>(blk + 104); // scales[0..3], d, pad
   const uint32_t qh = static_cast<uint32_t>(qh8 >> (8 * (2 * p + s))) & 255u;
   const uint32_t nib = static_cast<uint32_t>(tail >> (8 * p + 4 * s)) & 15u;
   o.db = __half2float(__ushort_as_half(static_cast<unsigned short>((tail >> 32) & 0xFFFFu))) *
@@ -363,35 +353,88 @@ __device__ __forceinline__ void rows_dot(const uint8_t* const (&rows)[RW], const
   }
 }
 
+// ------------------------------------------------------------------ staging
+__device__ __forceinline__ void cp_async16(void* smem_dst, const void* gsrc) {
+  const uint32_t d = static_cast<uint32_t>(__cvta_generic_to_shared(smem_dst));
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(d), "l"(gsrc) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+
+// Copy `bytes` (a multiple of 16) from global to shared memory, all threads.
+__device__ __forceinline__ void stage(uint8_t* dst, const uint8_t* src, int64_t bytes) {
+  for (int64_t i = threadIdx.x; i < bytes / 16; i += kThreads) cp_async16(dst + 16 * i, src + 16 * i);
+}
+
+// The expert slot a CTA serves: from the grouping kernel, or (one token,
+// whose top-k experts are distinct) straight from the routing ids.
+struct Slot {
+  int expert, start, count;
+};
+
+__device__ __forceinline__ bool slot_of(int u, bool direct, const int32_t* ids, int n_experts, const MoeWs& ws,
+                                        Slot& s) {
+  if (direct) {
+    s.expert = ids[u];
+    s.start = u;
+    s.count = 1;
+    return s.expert >= 0 && s.expert < n_experts;
+  }
+  if (u >= ws.hdr[0]) return false;
+  s.expert = ws.slot_expert[u];
+  s.start = ws.slot_start[u];
+  s.count = ws.slot_count[u];
+  return true;
+}
+
+__device__ __forceinline__ int pair_of(bool direct, const MoeWs& ws, int i) { return direct ? i : ws.pairs[i]; }
+
 // ------------------------------------------------------------------ gate/up
 // CTA (u, c): expert slot u, outputs [32c, 32c + 32); warp w: outputs
-// 32c + 4w + [0, 4) (rows of gate and of up).  Pairs of the slot in chunks
-// of NV.
+// 32c + 4w + [0, 4) (its 4 gate rows and 4 up rows).  The CTA's 64 rows are
+// copied into shared memory first (cp.async, all in flight at once); in
+// direct mode that copy starts before the dependency wait.  Pairs of the
+// slot in chunks of NV.
 template <int SBR, int NV>
 __global__ void __launch_bounds__(kThreads) moe_gate_up_kernel(const uint8_t* __restrict__ gate,
                                                                const uint8_t* __restrict__ up,
-                                                               const float* __restrict__ x, int top_k, int ffn,
+                                                               const float* __restrict__ x, const int32_t* ids,
+                                                               int n_experts, int direct, int top_k, int ffn,
                                                                MoeWs ws) {
-  extern __shared__ __align__(16) uint8_t xs[];
-  __shared__ uint32_t grid[512];
-  const int u = blockIdx.x;
-  if (u >= ws.hdr[0]) return;
-  for (int i = threadIdx.x; i < 512; i += kThreads) grid[i] = g_grid[i];
-  const int e = ws.slot_expert[u], start = ws.slot_start[u], m = ws.slot_count[u];
   constexpr int K = SBR * 32;
-  const int64_t rb = static_cast<int64_t>(K / 256) * kIq3sBlockBytes;
+  constexpr int RB = K / 256 * kIq3sBlockBytes;
+  constexpr int WBYTES = 2 * kGateRowsPerCta * RB;
+  extern __shared__ __align__(16) uint8_t smem[];
+  uint8_t* wsm = smem;                 // [gate rows 32][up rows 32]
+  uint8_t* xs = smem + WBYTES;         // encoded vectors
+  __shared__ uint32_t grid[512];
+  const int u = blockIdx.x, c = blockIdx.y;
+  for (int i = threadIdx.x; i < 512; i += kThreads) grid[i] = g_grid[i];
+  // The op's inputs (ids, x) come from whatever ran before: read them only
+  // after the wait, and let the down kernel start only then, so that it may
+  // read them before its own wait.
+  pdl_wait();
+  pdl_launch_dependents();
+  Slot sl{};
+  if (!slot_of(u, direct != 0, ids, n_experts, ws, sl)) return;
+  stage(wsm, gate + (static_cast<int64_t>(sl.expert) * ffn + c * kGateRowsPerCta) * RB, kGateRowsPerCta * RB);
+  stage(wsm + kGateRowsPerCta * RB, up + (static_cast<int64_t>(sl.expert) * ffn + c * kGateRowsPerCta) * RB,
+        kGateRowsPerCta * RB);
+  cp_async_commit();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int o0 = blockIdx.y * kGateRowsPerCta + warp * 4;
+  const int o0 = c * kGateRowsPerCta + warp * 4;
   const uint8_t* rows[8];
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
-    rows[i] = gate + (static_cast<int64_t>(e) * ffn + o0 + i) * rb;
-    rows[4 + i] = up + (static_cast<int64_t>(e) * ffn + o0 + i) * rb;
+    rows[i] = wsm + (warp * 4 + i) * RB;
+    rows[4 + i] = wsm + (kGateRowsPerCta + warp * 4 + i) * RB;
   }
-  for (int c0 = 0; c0 < m; c0 += NV) {
-    const int mc = min(NV, m - c0);
-    __syncthreads();  // (previous chunk's readers done; grid table ready)
-    for (int v = 0; v < mc; ++v) encode_vec<SBR>(x + static_cast<int64_t>(ws.pairs[start + c0 + v] / top_k) * K, xs, v);
+  for (int c0 = 0; c0 < sl.count; c0 += NV) {
+    const int mc = min(NV, sl.count - c0);
+    __syncthreads();  // (previous chunk's readers done)
+    for (int v = 0; v < mc; ++v)
+      encode_vec<SBR>(x + static_cast<int64_t>(pair_of(direct != 0, ws, sl.start + c0 + v) / top_k) * K, xs, v);
+    cp_async_wait_all();
     __syncthreads();
     float res[8][NV];
     rows_dot<SBR, NV, 8>(rows, xs, grid, mc, res);
@@ -407,7 +450,7 @@ __global__ void __launch_bounds__(kThreads) moe_gate_up_kernel(const uint8_t* __
               g = res[i][v];
               uu = res[4 + i][v];
             }
-          ws.act[static_cast<int64_t>(ws.pairs[start + c0 + v]) * ffn + o0 + lane] = silu_f(g) * uu;
+          ws.act[static_cast<int64_t>(pair_of(direct != 0, ws, sl.start + c0 + v)) * ffn + o0 + lane] = silu_f(g) * uu;
         }
       }
     }
@@ -415,35 +458,51 @@ __global__ void __launch_bounds__(kThreads) moe_gate_up_kernel(const uint8_t* __
 }
 
 // ------------------------------------------------------------------ down
-// CTA (u, c): expert slot u, rows [128c, 128c + 128); warp w: 16 rows.
+// CTA (u, c): expert slot u, rows [128c, 128c + 128) staged into shared
+// memory before the dependency wait: the gate/up kernel lets this kernel
+// start only after its own wait, so the routing ids and the grouping
+// kernel's slots are complete by then; warp w: 16 rows.
 template <int SBR, int NV>
-__global__ void __launch_bounds__(kThreads) moe_down_kernel(const uint8_t* __restrict__ down, int hidden,
-                                                            MoeWs ws, int ffn) {
-  extern __shared__ __align__(16) uint8_t xs[];
-  __shared__ uint32_t grid[512];
-  const int u = blockIdx.x;
-  if (u >= ws.hdr[0]) return;
-  for (int i = threadIdx.x; i < 512; i += kThreads) grid[i] = g_grid[i];
-  const int e = ws.slot_expert[u], start = ws.slot_start[u], m = ws.slot_count[u];
+__global__ void __launch_bounds__(kThreads) moe_down_kernel(const uint8_t* __restrict__ down, const int32_t* ids,
+                                                            int n_experts, int direct, int hidden, MoeWs ws,
+                                                            int ffn) {
   constexpr int K = SBR * 32;
-  const int64_t rb = static_cast<int64_t>(K / 256) * kIq3sBlockBytes;
+  constexpr int RB = K / 256 * kIq3sBlockBytes;
+  constexpr int WBYTES = kDownRowsPerCta * RB;
+  extern __shared__ __align__(16) uint8_t smem[];
+  uint8_t* wsm = smem;
+  uint8_t* xs = smem + WBYTES;
+  __shared__ uint32_t grid[512];
+  const int u = blockIdx.x, c = blockIdx.y;
+  for (int i = threadIdx.x; i < 512; i += kThreads) grid[i] = g_grid[i];
+  Slot sl{};
+  const bool live = slot_of(u, direct != 0, ids, n_experts, ws, sl);
+  if (live) {
+    stage(wsm, down + (static_cast<int64_t>(sl.expert) * hidden + c * kDownRowsPerCta) * RB, WBYTES);
+    cp_async_commit();
+  }
+  pdl_launch_dependents();
+  pdl_wait();
+  if (!live) return;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   constexpr int RW = kDownRowsPerCta / kWarps;
-  const int h0 = blockIdx.y * kDownRowsPerCta + warp * RW;
+  const int h0 = c * kDownRowsPerCta + warp * RW;
   const uint8_t* rows[RW];
 #pragma unroll
-  for (int i = 0; i < RW; ++i) rows[i] = down + (static_cast<int64_t>(e) * hidden + h0 + i) * rb;
-  for (int c0 = 0; c0 < m; c0 += NV) {
-    const int mc = min(NV, m - c0);
+  for (int i = 0; i < RW; ++i) rows[i] = wsm + (warp * RW + i) * RB;
+  for (int c0 = 0; c0 < sl.count; c0 += NV) {
+    const int mc = min(NV, sl.count - c0);
     __syncthreads();
-    for (int v = 0; v < mc; ++v) encode_vec<SBR>(ws.act + static_cast<int64_t>(ws.pairs[start + c0 + v]) * ffn, xs, v);
+    for (int v = 0; v < mc; ++v)
+      encode_vec<SBR>(ws.act + static_cast<int64_t>(pair_of(direct != 0, ws, sl.start + c0 + v)) * ffn, xs, v);
+    cp_async_wait_all();
     __syncthreads();
     float res[RW][NV];
     rows_dot<SBR, NV, RW>(rows, xs, grid, mc, res);
 #pragma unroll
     for (int v = 0; v < NV; ++v) {
       if (v < mc) {
-        float* dst = ws.dn + static_cast<int64_t>(ws.pairs[start + c0 + v]) * hidden + h0;
+        float* dst = ws.dn + static_cast<int64_t>(pair_of(direct != 0, ws, sl.start + c0 + v)) * hidden + h0;
 #pragma unroll
         for (int i = 0; i < RW; ++i)
           if (lane == i) dst[i] = res[i][v];
@@ -457,6 +516,8 @@ __global__ void __launch_bounds__(kThreads) moe_down_kernel(const uint8_t* __res
 // before the add like the reference's (out * w).sum(0) in f32.
 __global__ void moe_combine_kernel(const float* __restrict__ weights, const int32_t* __restrict__ ids, int64_t t,
                                    int top_k, int hidden, int n_experts, MoeWs ws, float* __restrict__ out) {
+  pdl_launch_dependents();
+  pdl_wait();
   const int64_t total = t * hidden;
   for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
        i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
@@ -477,21 +538,55 @@ constexpr int xs_bytes(int nv) {
   return nv * XSmem<SBR>::kVecBytes;
 }
 
+template <typename Kern, typename... Args>
+cudaError_t launch_pdl(Kern kern, dim3 grid, size_t smem, cudaStream_t stream, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, args...);
+}
+
 template <int SBR_GU, int SBR_D, int NV>
 int launch_all(const uint8_t* gate, const uint8_t* up, const uint8_t* down, const float* x, int64_t t, int hidden,
                int ffn, int n_experts, const int32_t* ids, const float* weights, int top_k, float* out, MoeWs ws,
                cudaStream_t stream) {
   const int p = static_cast<int>(t * top_k);
-  const int slots = p < n_experts ? p : n_experts;
-  moe_group_kernel<<<1, 512, 2 * n_experts * sizeof(int32_t), stream>>>(ids, p, n_experts, ws);
-  moe_gate_up_kernel<SBR_GU, NV><<<dim3(slots, ffn / kGateRowsPerCta), kThreads, xs_bytes<SBR_GU>(NV), stream>>>(
-      gate, up, x, top_k, ffn, ws);
-  moe_down_kernel<SBR_D, NV><<<dim3(slots, hidden / kDownRowsPerCta), kThreads, xs_bytes<SBR_D>(NV), stream>>>(
-      down, hidden, ws, ffn);
+  // one token selects top_k distinct experts: no grouping needed
+  const int direct = t == 1 ? 1 : 0;
+  const int slots = direct ? top_k : (p < n_experts ? p : n_experts);
+  if (!direct) moe_group_kernel<<<1, 512, 2 * n_experts * sizeof(int32_t), stream>>>(ids, p, n_experts, ws);
+  constexpr int gu_w = 2 * kGateRowsPerCta * (SBR_GU * 32 / 256) * kIq3sBlockBytes;
+  constexpr int d_w = kDownRowsPerCta * (SBR_D * 32 / 256) * kIq3sBlockBytes;
+  const size_t gu_smem = gu_w + xs_bytes<SBR_GU>(NV), d_smem = d_w + xs_bytes<SBR_D>(NV);
+  static int configured_device = -1;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (configured_device != dev) {
+    cudaError_t e = cudaFuncSetAttribute(moe_gate_up_kernel<SBR_GU, NV>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(gu_smem));
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(moe_down_kernel<SBR_D, NV>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               static_cast<int>(d_smem));
+    if (e != cudaSuccess) return fail_cuda(e, "moe set smem");
+    configured_device = dev;
+  }
+  cudaError_t e = launch_pdl(moe_gate_up_kernel<SBR_GU, NV>, dim3(slots, ffn / kGateRowsPerCta), gu_smem, stream, gate,
+                             up, x, ids, n_experts, direct, top_k, ffn, ws);
+  if (e == cudaSuccess)
+    e = launch_pdl(moe_down_kernel<SBR_D, NV>, dim3(slots, hidden / kDownRowsPerCta), d_smem, stream, down, ids,
+                   n_experts, direct, hidden, ws, ffn);
   const int64_t total = t * hidden;
   const int blocks = static_cast<int>(std::min<int64_t>((total + 255) / 256, 4096));
-  moe_combine_kernel<<<blocks, 256, 0, stream>>>(weights, ids, t, top_k, hidden, n_experts, ws, out);
-  const cudaError_t e = cudaGetLastError();
+  if (e == cudaSuccess)
+    e = launch_pdl(moe_combine_kernel, dim3(blocks), 0, stream, weights, ids, t, top_k, hidden, n_experts, ws, out);
+  if (e == cudaSuccess) e = cudaGetLastError();
   if (e != cudaSuccess) return fail_cuda(e, "moe experts launch");
   return BT_OK;
 }
