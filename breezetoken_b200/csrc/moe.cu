@@ -43,6 +43,9 @@ constexpr int kWarps = kThreads / 32;
 constexpr int kGateRowsPerCta = 32;   // + the 32 matching up rows
 constexpr int kDownRowsPerCta = 128;
 constexpr float kWeightSumMin = 6.103515625e-5f;  // moe.py:24
+// Workspace header words [kTicketBase, kTicketBase + hidden / 128): the
+// one-token combine's arrival counters (zero between calls).
+constexpr int kTicketBase = 16;
 
 // ------------------------------------------------------------------ repack
 // GGUF IQ3_S block (110 B: d[2] qs[64] qh[8] signs[32] scales[4]) -> the
@@ -161,12 +164,14 @@ __global__ void moe_group_kernel(const int32_t* __restrict__ ids, int p_total, i
   extern __shared__ int32_t sm[];
   int32_t* cnt = sm;               // [n_experts]
   int32_t* off = sm + n_experts;   // [n_experts] exclusive prefix of counts
+  int32_t* sid = off + n_experts;  // [p_total] the ids
   __shared__ int32_t s_bad;
   for (int e = threadIdx.x; e < n_experts; e += blockDim.x) cnt[e] = 0;
+  for (int q = threadIdx.x; q < p_total; q += blockDim.x) sid[q] = ids[q];
   if (threadIdx.x == 0) s_bad = 0;
   __syncthreads();
   for (int q = threadIdx.x; q < p_total; q += blockDim.x) {
-    const int e = ids[q];
+    const int e = sid[q];
     if (e >= 0 && e < n_experts)
       atomicAdd(&cnt[e], 1);
     else
@@ -190,10 +195,10 @@ __global__ void moe_group_kernel(const int32_t* __restrict__ ids, int p_total, i
   }
   __syncthreads();
   for (int q = threadIdx.x; q < p_total; q += blockDim.x) {
-    const int e = ids[q];
+    const int e = sid[q];
     if (e < 0 || e >= n_experts) continue;
     int rank = 0;
-    for (int q2 = 0; q2 < q; ++q2) rank += ids[q2] == e;
+    for (int q2 = 0; q2 < q; ++q2) rank += sid[q2] == e;
     ws.pairs[off[e] + rank] = q;
   }
 }
@@ -464,6 +469,7 @@ __global__ void __launch_bounds__(kThreads) moe_gate_up_kernel(const uint8_t* __
 // kernel's slots are complete by then; warp w: 16 rows.
 template <int SBR, int NV>
 __global__ void __launch_bounds__(kThreads) moe_down_kernel(const uint8_t* __restrict__ down, const int32_t* ids,
+                                                            const float* __restrict__ weights, float* out,
                                                             int n_experts, int direct, int hidden, MoeWs ws,
                                                             int ffn) {
   constexpr int K = SBR * 32;
@@ -483,14 +489,14 @@ __global__ void __launch_bounds__(kThreads) moe_down_kernel(const uint8_t* __res
   }
   pdl_launch_dependents();
   pdl_wait();
-  if (!live) return;
+  if (!live && !direct) return;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   constexpr int RW = kDownRowsPerCta / kWarps;
   const int h0 = c * kDownRowsPerCta + warp * RW;
   const uint8_t* rows[RW];
 #pragma unroll
   for (int i = 0; i < RW; ++i) rows[i] = wsm + (warp * RW + i) * RB;
-  for (int c0 = 0; c0 < sl.count; c0 += NV) {
+  for (int c0 = 0; live && c0 < sl.count; c0 += NV) {
     const int mc = min(NV, sl.count - c0);
     __syncthreads();
     for (int v = 0; v < mc; ++v)
@@ -509,6 +515,29 @@ __global__ void __launch_bounds__(kThreads) moe_down_kernel(const uint8_t* __res
       }
     }
   }
+  if (!direct) return;
+  // one token: the last of the top_k CTAs of this row chunk sums the experts'
+  // rows in routing order (atomic ticket, re-armed for the next call)
+  __shared__ int s_last;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    s_last = atomicAdd(ws.hdr + kTicketBase + c, 1) == static_cast<int>(gridDim.x) - 1;
+  }
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  for (int r = threadIdx.x; r < kDownRowsPerCta; r += kThreads) {
+    const int hh = c * kDownRowsPerCta + r;
+    float acc = 0.f;
+    for (int k = 0; k < static_cast<int>(gridDim.x); ++k) {
+      const int e = ids[k];
+      if (e < 0 || e >= n_experts) continue;
+      acc = __fadd_rn(acc, __fmul_rn(__ldcg(ws.dn + static_cast<int64_t>(k) * hidden + hh), weights[k]));
+    }
+    out[hh] = acc;
+  }
+  if (threadIdx.x == 0) atomicExch(ws.hdr + kTicketBase + c, 0);
 }
 
 // ------------------------------------------------------------------ combine
@@ -561,7 +590,7 @@ int launch_all(const uint8_t* gate, const uint8_t* up, const uint8_t* down, cons
   // one token selects top_k distinct experts: no grouping needed
   const int direct = t == 1 ? 1 : 0;
   const int slots = direct ? top_k : (p < n_experts ? p : n_experts);
-  if (!direct) moe_group_kernel<<<1, 512, 2 * n_experts * sizeof(int32_t), stream>>>(ids, p, n_experts, ws);
+  if (!direct) moe_group_kernel<<<1, 512, (2 * n_experts + p) * sizeof(int32_t), stream>>>(ids, p, n_experts, ws);
   constexpr int gu_w = 2 * kGateRowsPerCta * (SBR_GU * 32 / 256) * kIq3sBlockBytes;
   constexpr int d_w = kDownRowsPerCta * (SBR_D * 32 / 256) * kIq3sBlockBytes;
   const size_t gu_smem = gu_w + xs_bytes<SBR_GU>(NV), d_smem = d_w + xs_bytes<SBR_D>(NV);
@@ -581,10 +610,10 @@ int launch_all(const uint8_t* gate, const uint8_t* up, const uint8_t* down, cons
                              up, x, ids, n_experts, direct, top_k, ffn, ws);
   if (e == cudaSuccess)
     e = launch_pdl(moe_down_kernel<SBR_D, NV>, dim3(slots, hidden / kDownRowsPerCta), d_smem, stream, down, ids,
-                   n_experts, direct, hidden, ws, ffn);
+                   weights, out, n_experts, direct, hidden, ws, ffn);
   const int64_t total = t * hidden;
   const int blocks = static_cast<int>(std::min<int64_t>((total + 255) / 256, 4096));
-  if (e == cudaSuccess)
+  if (e == cudaSuccess && !direct)
     e = launch_pdl(moe_combine_kernel, dim3(blocks), 0, stream, weights, ids, t, top_k, hidden, n_experts, ws, out);
   if (e == cudaSuccess) e = cudaGetLastError();
   if (e != cudaSuccess) return fail_cuda(e, "moe experts launch");
@@ -647,8 +676,8 @@ int moe_experts_iq3s(const void* gate, const void* up, const void* down, const f
   if ((reinterpret_cast<uintptr_t>(gate) | reinterpret_cast<uintptr_t>(up) | reinterpret_cast<uintptr_t>(down) |
        reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(workspace)) & 15)
     return fail(BT_ERR_INVALID, "moe_experts_iq3s: weights, x and workspace must be 16-byte aligned");
-  if (ffn % kGateRowsPerCta || hidden % kDownRowsPerCta)
-    return fail(BT_ERR_UNSUPPORTED, "moe_experts_iq3s: ffn must be a multiple of 32 and hidden of 128");
+  if (ffn % kGateRowsPerCta || hidden % kDownRowsPerCta || hidden / kDownRowsPerCta > 64 - kTicketBase)
+    return fail(BT_ERR_UNSUPPORTED, "moe_experts_iq3s: ffn must be a multiple of 32 and hidden of 128 (<= 6144)");
   const MoeWs ws = moe_ws(workspace, t * top_k, hidden, ffn);
   const uint8_t* g = static_cast<const uint8_t*>(gate);
   const uint8_t* u = static_cast<const uint8_t*>(up);

@@ -137,7 +137,7 @@ def bench_moe(tokens: int, iters: int) -> dict:
     logits = torch.from_numpy(rng.standard_normal((tokens, n_exp)).astype(np.float32)).cuda()
     r = route_logits(logits, top_k)
     u = int(torch.unique(r.expert_ids).numel())
-    ws = torch.empty(int(N.load().bt_moe_workspace_bytes(tokens, hidden, ffn, n_exp, top_k)), dtype=torch.uint8,
+    ws = torch.zeros(int(N.load().bt_moe_workspace_bytes(tokens, hidden, ffn, n_exp, top_k)), dtype=torch.uint8,
                      device="cuda")
     flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
     s = torch.cuda.Stream()

@@ -90,7 +90,7 @@ def experts_forward(ex: IQ3SExperts, x: torch.Tensor, ids: torch.Tensor, weights
     lib = N.load()
     need = int(lib.bt_moe_workspace_bytes(t, ex.hidden, ex.ffn, ex.n_experts, top_k))
     if workspace is None or workspace.numel() < need:
-        workspace = torch.empty(need, dtype=torch.uint8, device=x2.device)
+        workspace = torch.zeros(need, dtype=torch.uint8, device=x2.device)
     out = torch.empty(t, ex.hidden, dtype=torch.float32, device=x2.device)
     N.call("bt_moe_experts_iq3s", ex.gate.data_ptr(), ex.up.data_ptr(), ex.down.data_ptr(), x2.data_ptr(), t,
            ex.hidden, ex.ffn, ex.n_experts, ids2.data_ptr(), w2.data_ptr(), top_k, out.data_ptr(),
@@ -129,7 +129,7 @@ class ExpertPool:
         t, k = x.reshape(-1, ex.hidden).shape[0], ids.reshape(x.reshape(-1, ex.hidden).shape[0], -1).shape[1]
         need = int(N.load().bt_moe_workspace_bytes(t, ex.hidden, ex.ffn, ex.n_experts, k))
         if self._ws is None or self._ws.numel() < need:
-            self._ws = torch.empty(need, dtype=torch.uint8, device=x.device)
+            self._ws = torch.zeros(need, dtype=torch.uint8, device=x.device)
         return experts_forward(ex, x, ids, weights, self._ws)
 
 

@@ -181,7 +181,8 @@ BT_API int bt_repack_iq3_s(const void* src, void* dst, int64_t rows, int64_t k,
 BT_API int bt_moe_route(const float* logits, int64_t t, int64_t n_experts, int top_k,
                  int32_t* ids, float* weights, void* stream);
 
-/* Workspace of bt_moe_experts_iq3s (no zeroing needed).                   */
+/* Workspace of bt_moe_experts_iq3s: zeroed once before first use; the
+ * calls leave it reusable (its arrival counters are re-armed).            */
 BT_API int64_t bt_moe_workspace_bytes(int64_t t, int64_t hidden, int64_t ffn,
                                int64_t n_experts, int top_k);
 
