@@ -11,13 +11,13 @@
 // `moe_group_kernel` sorts the pairs by expert (ascending id, stable), so each
 // selected expert's weights are read once for all the tokens that chose it
 // (U unique experts: bytes = U * 1,351,680 at the 35B shape).  The gate/up
-// kernel gives each expert 16 CTAs of 32 gate + 32 matching up rows and
-// writes act for every pair; the down kernel gives each expert 16 CTAs of
-// 128 rows; a combine kernel sums the pairs of a token in routing order.
+// kernel gives each expert 32 CTAs of 16 gate + 16 matching up rows and
+// writes act for every pair; the down kernel gives each expert 32 CTAs of
+// 64 rows; the pairs of a token are summed in routing order.
 //
 // IQ3_S GEMV: a warp lane decodes one 32-weight sub-block at a time -- eight
-// 4-byte grid entries from a 512-entry table in shared memory, signs applied
-// bytewise -- into signed int8 words, and dots them with the activation
+// loads from the sign-applied codebook (8192 entries, in shared memory) --
+// into signed int8 words, and dots them with the activation
 // encoded as three int8 digits of a 22-bit fixed-point value per 32-element
 // block (the q8 GEMV's encoding), 24 dp4a per sub-block: the integer sums are
 // exact, so the only roundings are the activation's encoding and the f32
@@ -34,18 +34,39 @@ namespace bt {
 
 namespace {
 
-__device__ const uint32_t g_grid[512] = {
+// The IQ3_S codebook with the 4 sign bits of a group applied: entry
+// idx9 | (signs4 << 9) holds the group's 4 signed int8 weights (before the
+// sub-block scale), so decoding a group is one table load.
+constexpr uint32_t kGrid[512] = {
 #include "iq3s_grid.inc"
 };
 
+struct SignedGrid {
+  uint32_t v[8192];
+};
+
+constexpr SignedGrid make_signed_grid() {
+  SignedGrid t{};
+  for (int i = 0; i < 8192; ++i) {
+    const uint32_t g = kGrid[i & 511], sb4 = static_cast<uint32_t>(i) >> 9;
+    // bit j of sb4 -> 0xFF in byte j; then per-byte two's-complement negation
+    const uint32_t mask = ((sb4 * 0x00204081u) & 0x01010101u) * 0xFFu;
+    t.v[i] = (g ^ mask) + (mask & 0x01010101u);
+  }
+  return t;
+}
+
+__device__ const SignedGrid g_signed = make_signed_grid();
+
 constexpr int kThreads = 256;
 constexpr int kWarps = kThreads / 32;
-constexpr int kGateRowsPerCta = 32;   // + the 32 matching up rows
-constexpr int kDownRowsPerCta = 128;
+constexpr int kGateRowsPerCta = 16;   // + the 16 matching up rows
+constexpr int kDownRowsPerCta = 64;
 constexpr float kWeightSumMin = 6.103515625e-5f;  // moe.py:24
-// Workspace header words [kTicketBase, kTicketBase + hidden / 128): the
+// Workspace header words [kTicketBase, kTicketBase + hidden / 64): the
 // one-token combine's arrival counters (zero between calls).
 constexpr int kTicketBase = 16;
+constexpr int kHeaderBytes = 512;
 
 // ------------------------------------------------------------------ repack
 // GGUF IQ3_S block (110 B: d[2] qs[64] qh[8] signs[32] scales[4]) -> the
@@ -140,7 +161,7 @@ __host__ __device__ inline MoeWs moe_ws(void* base, int64_t p, int64_t hidden, i
   MoeWs w;
   int64_t o = 0;
   w.hdr = reinterpret_cast<int32_t*>(b + o);
-  o += 256;
+  o += kHeaderBytes;
   w.slot_expert = reinterpret_cast<int32_t*>(b + o);
   o += align256(4 * p);
   w.slot_start = reinterpret_cast<int32_t*>(b + o);
@@ -156,7 +177,7 @@ __host__ __device__ inline MoeWs moe_ws(void* base, int64_t p, int64_t hidden, i
 }
 
 inline int64_t moe_ws_bytes(int64_t p, int64_t hidden, int64_t ffn) {
-  return 256 + 4 * align256(4 * p) + align256(4 * p * ffn) + align256(4 * p * hidden);
+  return kHeaderBytes + 4 * align256(4 * p) + align256(4 * p * ffn) + align256(4 * p * hidden);
 }
 
 // One CTA: counting sort of the P pairs by expert id (stable).
@@ -263,7 +284,7 @@ struct SubBlock {
   float db;
 };
 
-__device__ __forceinline__ void load_sub_block(const uint8_t* row, int sb, const uint32_t* grid, SubBlock& o) {
+__device__ __forceinline__ void load_sub_block(const uint8_t* row, int sb, const uint32_t* lut, SubBlock& o) {
   // `row` is a shared-memory copy; all loads are naturally aligned (blocks
   // are 112 = 7 x 16 bytes)
   const int b = sb >> 3, p = (sb & 7) >> 1, s = sb & 1;
@@ -278,11 +299,9 @@ __device__ __forceinline__ void load_sub_block(const uint8_t* row, int sb, const
          static_cast<float>(1 + 2 * static_cast<int>(nib));
 #pragma unroll
   for (int w = 0; w < 8; ++w) {
-    const uint32_t idx = static_cast<uint32_t>((qs >> (8 * w)) & 255u) | (((qh >> w) & 1u) << 8);
-    const uint32_t g = grid[idx];
-    const uint32_t sb4 = (signs >> (4 * w)) & 15u;
-    const uint32_t mask = ((sb4 * 0x00204081u) & 0x01010101u) * 0xFFu;
-    o.q[w] = (g ^ mask) + (mask & 0x01010101u);
+    const uint32_t idx = static_cast<uint32_t>((qs >> (8 * w)) & 255u) | (((qh >> w) & 1u) << 8) |
+                         (((signs >> (4 * w)) & 15u) << 9);
+    o.q[w] = lut[idx];
   }
 }
 
@@ -314,7 +333,7 @@ __device__ __forceinline__ float sub_block_dot(const SubBlock& w, const uint8_t*
 // Lanes: LPR lanes per row (all 32 when the row has >= 32 sub-blocks).
 // Returns, in every lane, the totals of the lane's row group.
 template <int SBR, int NV, int RW>
-__device__ __forceinline__ void rows_dot(const uint8_t* const (&rows)[RW], const uint8_t* xs, const uint32_t* grid,
+__device__ __forceinline__ void rows_dot(const uint8_t* const (&rows)[RW], const uint8_t* xs, const uint32_t* lut,
                                          int mc, float (&res)[RW][NV]) {
   static_assert(SBR >= 16, "rows of at least 512 weights");
   constexpr int LPR = SBR >= 32 ? 32 : SBR;
@@ -333,7 +352,7 @@ __device__ __forceinline__ void rows_dot(const uint8_t* const (&rows)[RW], const
     for (int i = 0; i < SPL; ++i) {
       const int sb = lr + LPR * i;
       SubBlock w;
-      load_sub_block(row, sb, grid, w);
+      load_sub_block(row, sb, lut, w);
       const uint8_t* base = xs;
 #pragma unroll
       for (int v = 0; v < NV; ++v) {
@@ -395,8 +414,8 @@ __device__ __forceinline__ bool slot_of(int u, bool direct, const int32_t* ids, 
 __device__ __forceinline__ int pair_of(bool direct, const MoeWs& ws, int i) { return direct ? i : ws.pairs[i]; }
 
 // ------------------------------------------------------------------ gate/up
-// CTA (u, c): expert slot u, outputs [32c, 32c + 32); warp w: outputs
-// 32c + 4w + [0, 4) (its 4 gate rows and 4 up rows).  The CTA's 64 rows are
+// CTA (u, c): expert slot u, outputs [16c, 16c + 16); warp w: outputs
+// 16c + 2w + [0, 2) (its 2 gate rows and 2 up rows).  The CTA's 32 rows are
 // copied into shared memory first (cp.async, all in flight at once); in
 // direct mode that copy starts before the dependency wait.  Pairs of the
 // slot in chunks of NV.
@@ -412,9 +431,10 @@ __global__ void __launch_bounds__(kThreads) moe_gate_up_kernel(const uint8_t* __
   extern __shared__ __align__(16) uint8_t smem[];
   uint8_t* wsm = smem;                 // [gate rows 32][up rows 32]
   uint8_t* xs = smem + WBYTES;         // encoded vectors
-  __shared__ uint32_t grid[512];
+  __shared__ __align__(16) uint32_t lut[8192];
   const int u = blockIdx.x, c = blockIdx.y;
-  for (int i = threadIdx.x; i < 512; i += kThreads) grid[i] = g_grid[i];
+  stage(reinterpret_cast<uint8_t*>(lut), reinterpret_cast<const uint8_t*>(g_signed.v), sizeof(lut));
+  cp_async_commit();
   // The op's inputs (ids, x) come from whatever ran before: read them only
   // after the wait, and let the down kernel start only then, so that it may
   // read them before its own wait.
@@ -427,12 +447,13 @@ __global__ void __launch_bounds__(kThreads) moe_gate_up_kernel(const uint8_t* __
         kGateRowsPerCta * RB);
   cp_async_commit();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int o0 = c * kGateRowsPerCta + warp * 4;
-  const uint8_t* rows[8];
+  constexpr int OPW = kGateRowsPerCta / kWarps;  // outputs per warp
+  const int o0 = c * kGateRowsPerCta + warp * OPW;
+  const uint8_t* rows[2 * OPW];
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    rows[i] = wsm + (warp * 4 + i) * RB;
-    rows[4 + i] = wsm + (kGateRowsPerCta + warp * 4 + i) * RB;
+  for (int i = 0; i < OPW; ++i) {
+    rows[i] = wsm + (warp * OPW + i) * RB;
+    rows[OPW + i] = wsm + (kGateRowsPerCta + warp * OPW + i) * RB;
   }
   for (int c0 = 0; c0 < sl.count; c0 += NV) {
     const int mc = min(NV, sl.count - c0);
@@ -441,19 +462,19 @@ __global__ void __launch_bounds__(kThreads) moe_gate_up_kernel(const uint8_t* __
       encode_vec<SBR>(x + static_cast<int64_t>(pair_of(direct != 0, ws, sl.start + c0 + v) / top_k) * K, xs, v);
     cp_async_wait_all();
     __syncthreads();
-    float res[8][NV];
-    rows_dot<SBR, NV, 8>(rows, xs, grid, mc, res);
-    if (lane < 4) {
+    float res[2 * OPW][NV];
+    rows_dot<SBR, NV, 2 * OPW>(rows, xs, lut, mc, res);
+    if (lane < OPW) {
 #pragma unroll
       for (int v = 0; v < NV; ++v) {
         if (v < mc) {
           // lane i writes output o0 + i (model/moe.py:229: act = silu(g) * u)
           float g = 0.f, uu = 0.f;
 #pragma unroll
-          for (int i = 0; i < 4; ++i)
+          for (int i = 0; i < OPW; ++i)
             if (i == lane) {
               g = res[i][v];
-              uu = res[4 + i][v];
+              uu = res[OPW + i][v];
             }
           ws.act[static_cast<int64_t>(pair_of(direct != 0, ws, sl.start + c0 + v)) * ffn + o0 + lane] = silu_f(g) * uu;
         }
@@ -463,10 +484,10 @@ __global__ void __launch_bounds__(kThreads) moe_gate_up_kernel(const uint8_t* __
 }
 
 // ------------------------------------------------------------------ down
-// CTA (u, c): expert slot u, rows [128c, 128c + 128) staged into shared
+// CTA (u, c): expert slot u, rows [64c, 64c + 64) staged into shared
 // memory before the dependency wait: the gate/up kernel lets this kernel
 // start only after its own wait, so the routing ids and the grouping
-// kernel's slots are complete by then; warp w: 16 rows.
+// kernel's slots are complete by then; warp w: 8 rows.
 template <int SBR, int NV>
 __global__ void __launch_bounds__(kThreads) moe_down_kernel(const uint8_t* __restrict__ down, const int32_t* ids,
                                                             const float* __restrict__ weights, float* out,
@@ -478,9 +499,10 @@ __global__ void __launch_bounds__(kThreads) moe_down_kernel(const uint8_t* __res
   extern __shared__ __align__(16) uint8_t smem[];
   uint8_t* wsm = smem;
   uint8_t* xs = smem + WBYTES;
-  __shared__ uint32_t grid[512];
+  __shared__ __align__(16) uint32_t lut[8192];
   const int u = blockIdx.x, c = blockIdx.y;
-  for (int i = threadIdx.x; i < 512; i += kThreads) grid[i] = g_grid[i];
+  stage(reinterpret_cast<uint8_t*>(lut), reinterpret_cast<const uint8_t*>(g_signed.v), sizeof(lut));
+  cp_async_commit();
   Slot sl{};
   const bool live = slot_of(u, direct != 0, ids, n_experts, ws, sl);
   if (live) {
@@ -504,7 +526,7 @@ __global__ void __launch_bounds__(kThreads) moe_down_kernel(const uint8_t* __res
     cp_async_wait_all();
     __syncthreads();
     float res[RW][NV];
-    rows_dot<SBR, NV, RW>(rows, xs, grid, mc, res);
+    rows_dot<SBR, NV, RW>(rows, xs, lut, mc, res);
 #pragma unroll
     for (int v = 0; v < NV; ++v) {
       if (v < mc) {
@@ -676,8 +698,8 @@ int moe_experts_iq3s(const void* gate, const void* up, const void* down, const f
   if ((reinterpret_cast<uintptr_t>(gate) | reinterpret_cast<uintptr_t>(up) | reinterpret_cast<uintptr_t>(down) |
        reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(workspace)) & 15)
     return fail(BT_ERR_INVALID, "moe_experts_iq3s: weights, x and workspace must be 16-byte aligned");
-  if (ffn % kGateRowsPerCta || hidden % kDownRowsPerCta || hidden / kDownRowsPerCta > 64 - kTicketBase)
-    return fail(BT_ERR_UNSUPPORTED, "moe_experts_iq3s: ffn must be a multiple of 32 and hidden of 128 (<= 6144)");
+  if (ffn % kGateRowsPerCta || hidden % kDownRowsPerCta || hidden / kDownRowsPerCta > kHeaderBytes / 4 - kTicketBase)
+    return fail(BT_ERR_UNSUPPORTED, "moe_experts_iq3s: ffn must be a multiple of 16 and hidden of 64 (<= 7168)");
   const MoeWs ws = moe_ws(workspace, t * top_k, hidden, ffn);
   const uint8_t* g = static_cast<const uint8_t*>(gate);
   const uint8_t* u = static_cast<const uint8_t*>(up);

@@ -10,7 +10,8 @@ Each prints one JSON line: average launch time and achieved HBM GB/s from
 the algorithmic bytes of one launch (weights / state / KV read once).
 ``moe`` is BASELINE config 4: routed experts of one MoE layer (hidden 2048,
 256 IQ3_S experts of ffn 512, top-8 over N(0,1) router logits, seed 3),
-timed per call with L2 flushed before each call; its bytes are the
+timed per call after reading a 256 MB buffer (the experts are not in L2);
+its bytes are the
 U * 1,351,680 of the U distinct experts the routing selects.
 ``trace`` prints the device-side timeline of one Qwen3.5 decode step (per
 kernel kind: release gap, prologue, body) after a 16-token prefill.
@@ -139,12 +140,12 @@ def bench_moe(tokens: int, iters: int) -> dict:
     u = int(torch.unique(r.expert_ids).numel())
     ws = torch.zeros(int(N.load().bt_moe_workspace_bytes(tokens, hidden, ffn, n_exp, top_k)), dtype=torch.uint8,
                      device="cuda")
-    flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+    flush = torch.ones(256 << 20, dtype=torch.uint8, device="cuda")
     s = torch.cuda.Stream()
     total = 0.0
     with torch.cuda.stream(s):
         for i in range(iters + 3):
-            flush.zero_()
+            flush.sum(dtype=torch.int32)  # read 256 MB: afterwards L2 holds only clean lines
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             e0.record(s)
             experts_forward(ex, x, r.expert_ids, r.weights, ws)
@@ -155,7 +156,7 @@ def bench_moe(tokens: int, iters: int) -> dict:
     sec = total / iters
     nbytes = u * 1_351_680 + tokens * hidden * 8
     return {"kernel": "moe_experts_iq3s", "tokens": tokens, "unique_experts": u, "us": sec * 1e6, "bytes": nbytes,
-            "gbs": nbytes / sec / 1e9, "l2": "flushed before each call (256 MB write)"}
+            "gbs": nbytes / sec / 1e9, "l2": "flushed before each call (256 MB read)"}
 
 
 def trace_step(gguf: str, max_context: int, steps: int) -> str:
