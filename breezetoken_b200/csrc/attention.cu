@@ -45,6 +45,25 @@ __device__ __forceinline__ void prefetch_l2_bulk(const void* p, uint32_t bytes) 
   asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
 }
 
+// Loads issued exactly where they stand (volatile asm keeps their order):
+// the model prologue puts every load that does not depend on the position
+// ahead of the position load, so the two L2 round trips overlap.
+__device__ __forceinline__ float4 ld_f4_now(const float* p) {
+  float4 v;
+  asm volatile("ld.global.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "l"(p));
+  return v;
+}
+__device__ __forceinline__ float ld_f32_now(const float* p) {
+  float v;
+  asm volatile("ld.global.f32 %0, [%1];" : "=f"(v) : "l"(p));
+  return v;
+}
+__device__ __forceinline__ int ld_s32_now(const int32_t* p) {
+  int v;
+  asm volatile("ld.global.s32 %0, [%1];" : "=r"(v) : "l"(p));
+  return v;
+}
+
 // Sum 32 per-lane values across the warp; lane l returns the total of value l.
 __device__ __forceinline__ float reduce_scatter32(float (&v)[32], int lane) {
 #pragma unroll
@@ -115,11 +134,50 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const __grid_
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int split = blockIdx.x, g = blockIdx.y, b = blockIdx.z;
   trace_entry(p.trace);
+  // model mode: the q/k/v values of this warp's items and the norm weights
+  // (items: GS query heads, then k and v of the group; warp w takes items
+  // w, w + 4, ...); the weights before the dependency wait
+  constexpr int NI = (GS + 2 + kAttnWarps - 1) / kAttnWarps;
+  float x[MODEL ? NI : 1][DPL], nwv[MODEL ? NI : 1][DPL];
+  if constexpr (MODEL) {
+#pragma unroll
+    for (int it = 0; it < NI; ++it) {
+      const int item = min(warp + it * kAttnWarps, GS + 1);
+      const float* nw = (item < GS ? p.q_norm : p.k_norm) + lane * DPL;
+#pragma unroll
+      for (int i = 0; i < DPL; i += 4) {
+        const float4 t = reinterpret_cast<const float4*>(nw)[i / 4];
+        nwv[it][i] = t.x, nwv[it][i + 1] = t.y, nwv[it][i + 2] = t.z, nwv[it][i + 3] = t.w;
+      }
+    }
+  }
   pdl_launch_dependents();
   pdl_wait();
   trace_waited(p.trace);
 
-  int L = MODEL ? p.pos[b] + 1 : p.lens[b];
+  float gate_first = 0.f;
+  const int e_first0 = split * ((GS * DIM + p.splits - 1) / p.splits) + threadIdx.x;
+  int L;
+  if constexpr (MODEL) {
+#pragma unroll
+    for (int it = 0; it < NI; ++it) {
+      const int item = min(warp + it * kAttnWarps, GS + 1);
+      const float* src = item < GS ? p.q + static_cast<int64_t>(b) * p.q_bs + static_cast<int64_t>(g * GS + item) * p.q_hs
+                                   : (item == GS ? p.k_new : p.v_new) + static_cast<int64_t>(b) * p.q_bs + g * DIM;
+#pragma unroll
+      for (int i = 0; i < DPL; i += 4) {
+        const float4 t = ld_f4_now(src + lane * DPL + i);
+        x[it][i] = t.x, x[it][i + 1] = t.y, x[it][i + 2] = t.z, x[it][i + 3] = t.w;
+      }
+    }
+    // (cluster mode: every CTA merges per = GS*DIM/splits outputs, 1 per thread here)
+    if (CL && e_first0 < min(GS * DIM, (split + 1) * ((GS * DIM + p.splits - 1) / p.splits)))
+      gate_first = ld_f32_now(p.gate + static_cast<int64_t>(b) * p.q_bs +
+                              static_cast<int64_t>(g * GS + e_first0 / DIM) * p.q_hs + e_first0 % DIM);
+    L = ld_s32_now(p.pos + b) + 1;
+  } else {
+    L = p.lens[b];
+  }
   if (L < 0 || L > p.cap) {
     if (threadIdx.x == 0 && split == 0) report_status(p.status, BT_ERR_INVALID, SITE_ATTN_LENGTH, L, p.cap, b);
     L = L < 0 ? 0 : p.cap;
@@ -143,13 +201,10 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const __grid_
                        DIM * sizeof(KV));
     }
   }
-  // the output element this thread finishes first in a cluster merge, and its gate
+  // the output element this thread finishes first in a cluster merge
+  // (cluster mode uses all p.splits CTAs)
   const int per = (GS * DIM + splits - 1) / splits;
   const int e_first = split * per + threadIdx.x;
-  float gate_first = 0.f;
-  if (CL && MODEL && e_first < min(GS * DIM, (split + 1) * per))
-    gate_first = p.gate[static_cast<int64_t>(b) * p.q_bs + static_cast<int64_t>(g * GS + e_first / DIM) * p.q_hs +
-                        e_first % DIM];
 
   if constexpr (!MODEL) {
     for (int i = threadIdx.x; i < GS * DIM; i += kAttnThreads)
@@ -158,30 +213,15 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const __grid_
     __syncthreads();
   } else {
     const int pos = max(L - 1, 0);  // (L == 0 only after a reported invalid position)
-    // items: GS query heads, then k and v of the group; warp w takes items
-    // w, w + 4, ...  Every load of all its items (values, norm weights, RoPE
-    // row) is issued before any is used.
-    constexpr int NI = (GS + 2 + kAttnWarps - 1) / kAttnWarps;
+    // the RoPE row at the position (the values and weights are in flight or here)
     const float* crow = p.rope_cos + static_cast<int64_t>(pos) * p.rope_dim;
     const float* srow = p.rope_sin + static_cast<int64_t>(pos) * p.rope_dim;
-    float x[NI][DPL], nwv[NI][DPL], cv[DPL], sv[DPL];
+    float cv[DPL], sv[DPL];
 #pragma unroll
     for (int i = 0; i < DPL; ++i) {
       const int dc = min(lane * DPL + i, p.rope_dim - 1);
-      cv[i] = crow[dc];
-      sv[i] = srow[dc];
-    }
-#pragma unroll
-    for (int it = 0; it < NI; ++it) {
-      const int item = min(warp + it * kAttnWarps, GS + 1);
-      const float* src = item < GS ? p.q + static_cast<int64_t>(b) * p.q_bs + static_cast<int64_t>(g * GS + item) * p.q_hs
-                                   : (item == GS ? p.k_new : p.v_new) + static_cast<int64_t>(b) * p.q_bs + g * DIM;
-      const float* nw = item < GS ? p.q_norm : p.k_norm;
-#pragma unroll
-      for (int i = 0; i < DPL; ++i) {
-        x[it][i] = src[lane * DPL + i];
-        nwv[it][i] = nw[lane * DPL + i];
-      }
+      cv[i] = ld_f32_now(crow + dc);
+      sv[i] = ld_f32_now(srow + dc);
     }
 #pragma unroll
     for (int it = 0; it < NI; ++it) {
@@ -521,6 +561,12 @@ int attention_launch(const AttnParams& p, cudaStream_t stream, bool pdl) {
     return fail(BT_ERR_INVALID, "attention: K/V strides must be multiples of 16 bytes");
   if (p.model && (p.rope_dim < 2 || p.rope_dim > p.dim || p.rope_dim % 2))
     return fail(BT_ERR_INVALID, "attention: invalid rope_dim %d", p.rope_dim);
+  if (p.model && (((reinterpret_cast<uintptr_t>(p.q) | reinterpret_cast<uintptr_t>(p.k_new) |
+                    reinterpret_cast<uintptr_t>(p.v_new) | reinterpret_cast<uintptr_t>(p.q_norm) |
+                    reinterpret_cast<uintptr_t>(p.k_norm)) & 15) ||
+                  (p.q_bs & 3) || (p.q_hs & 3)))
+    return fail(BT_ERR_INVALID, "model-mode attention reads q/k/v and norm weights as float4: 16-byte aligned, "
+                                "strides a multiple of 4");
   if (p.cluster && (p.splits > 8 || p.heads != 4 * p.kv_heads))
     return fail(BT_ERR_UNSUPPORTED, "cluster-merged attention serves <= 8 splits and 4 query heads per KV head");
   return p.kv_dtype == BT_BF16 ? launch_dtype<__nv_bfloat16>(p, stream, pdl) : launch_dtype<float>(p, stream, pdl);

@@ -117,7 +117,8 @@ int qwen35_kernels_per_step(const BtQwen35Model& m) {
 int64_t qwen35_proj_elems(const BtQwen35Dims& d) {
   const int64_t gdn = 4LL * d.ssm_inner + 2LL * d.ssm_heads;
   const int64_t attn = 2LL * d.n_heads * d.head_dim + 2LL * d.n_kv * d.head_dim;
-  return gdn > attn ? gdn : attn;
+  const int64_t n = gdn > attn ? gdn : attn;
+  return (n + 3) / 4 * 4;  // rows of the buffer stay 16-byte aligned
 }
 
 int64_t qwen35_workspace_bytes(const BtQwen35Dims& d) {
