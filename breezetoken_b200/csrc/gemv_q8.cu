@@ -21,6 +21,8 @@ struct GemvTuning {
   int64_t prefetch_bytes = 64 * 1024;
   // CTAs per SM for long matrices (BT_GEMV_BIG_GRID: 1 or 2)
   int big_grid = 2;
+  // row units (4 rows) per SM from which a matrix counts as long (BT_GEMV_BIG_UNITS)
+  int big_units = 8;
 };
 
 int env_int(const char* name, int dflt) {
@@ -33,6 +35,7 @@ const GemvTuning& tuning() {
     GemvTuning g;
     g.prefetch_bytes = static_cast<int64_t>(std::min(1024, std::max(0, env_int("BT_GEMV_PREFETCH_KB", 64)))) * 1024;
     g.big_grid = std::min(2, std::max(1, env_int("BT_GEMV_BIG_GRID", 2)));
+    g.big_units = std::max(1, env_int("BT_GEMV_BIG_UNITS", 8));
     return g;
   }();
   return t;
@@ -65,9 +68,11 @@ int gemv_q8_plan(GemvQ8Params& p, int sm_count, GemvQ8Launch& L) {
   p.sb = static_cast<int32_t>(bt_q8_row_bytes(p.k) - p.k);
   p.row_bytes = static_cast<int32_t>(bt_q8_row_bytes(p.k));
   const int64_t n_units = (p.n_rows + 3) / 4;
-  // long matrices (>= 64 row units per SM) run two CTAs per SM: twice the
-  // weight bytes in flight
-  const int64_t ctas = n_units >= 64LL * sm_count ? static_cast<int64_t>(tuning().big_grid) * sm_count : sm_count;
+  // matrices of >= 8 row units per SM run two CTAs per SM: twice the weight
+  // bytes in flight and half the rows per CTA after the dependency wait
+  const int64_t ctas = n_units >= static_cast<int64_t>(tuning().big_units) * sm_count
+                           ? static_cast<int64_t>(tuning().big_grid) * sm_count
+                           : sm_count;
   const int grid = static_cast<int>(std::min<int64_t>(ctas, n_units));
   const int64_t rows_per_cta = ((n_units + grid - 1) / grid) * 4;
   // 4-row groups reuse each activation chunk across rows (K <= 1024: a
