@@ -40,6 +40,14 @@ constexpr int kAttnThreads = kAttnWarps * 32;
 constexpr float kLog2e = 1.4426950408889634f;
 // K/V rows per CTA prefetched into L2 as soon as the slice is known.
 constexpr int kPrefetchRows = 64;
+// Model mode with a cluster merge: the first kStageRows K and V rows of a
+// CTA's slice are copied into shared memory (cp.async) during the prologue.
+constexpr int kStageRows = 16;
+
+__device__ __forceinline__ void cp_async16(void* smem_dst, const void* gsrc) {
+  const uint32_t d = static_cast<uint32_t>(__cvta_generic_to_shared(smem_dst));
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(d), "l"(gsrc) : "memory");
+}
 
 __device__ __forceinline__ void prefetch_l2_bulk(const void* p, uint32_t bytes) {
   asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
@@ -124,8 +132,12 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const __grid_
   constexpr int DIM = DPL * 32;
   constexpr int PB = 32 / GS;
   __shared__ __align__(16) float qs[GS][DIM];
-  __shared__ __align__(16) float cpo[CL ? GS : 1][CL ? DIM : 1];  // this CTA's merged partial (cluster mode)
-  __shared__ float cm[GS], cl[GS];
+  // cluster mode: the partials other CTAs store here for the elements this
+  // CTA finishes ([split][element], `per` elements per split), and every
+  // split's max / sum per head
+  __shared__ __align__(16) float rx[CL ? GS * DIM + 8 : 1];
+  __shared__ float rm[CL ? 8 : 1][GS], rl[CL ? 8 : 1][GS];
+  extern __shared__ __align__(16) float kv_stage[];  // CL && MODEL: [K rows][V rows] of kStageRows x DIM
   __shared__ __align__(16) float kvn[2][DIM];
   __shared__ float wm[kAttnWarps][GS], wl[kAttnWarps][GS];
   __shared__ __align__(16) float wacc[kAttnWarps][GS][DIM];
@@ -134,6 +146,9 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const __grid_
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int split = blockIdx.x, g = blockIdx.y, b = blockIdx.z;
   trace_entry(p.trace);
+  // (cluster mode: every CTA of the cluster has started once this barrier
+  // completes; it is waited on before the first store into another CTA)
+  if constexpr (CL) asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
   // model mode: the q/k/v values of this warp's items and the norm weights
   // (items: GS query heads, then k and v of the group; warp w takes items
   // w, w + 4, ...); the weights before the dependency wait
@@ -190,14 +205,27 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const __grid_
   if (!CL && split >= splits) return;
   const int chunk = (L + splits - 1) / splits;
   const int t0 = min(L, split * chunk), t1 = min(L, t0 + chunk);
+  // CL && MODEL: the first kStageRows K and V rows of the slice -> shared memory
+  const int staged = (CL && MODEL) ? min(t1 - t0, kStageRows) : 0;
+  if constexpr (CL && MODEL) {
+    constexpr int C16 = DIM / 4;  // 16-byte pieces per row
+    for (int i = threadIdx.x; i < 2 * staged * C16; i += kAttnThreads) {
+      const int kv = i / (staged * C16), r = (i / C16) % staged, c = i % C16;
+      const float* src = static_cast<const float*>(kv ? p.v : p.k) + static_cast<int64_t>(b) * p.kv_bs +
+                         static_cast<int64_t>(t0 + r) * p.kv_ts + g * DIM + 4 * c;
+      cp_async16(kv_stage + (kv * kStageRows + r) * DIM + 4 * c, src);
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+  }
   {
-    // K/V rows of the first kPrefetchRows positions of the slice on their way
-    // into L2 while the queries are prepared (one bulk prefetch per row)
-    const int n = min(t1 - t0, kPrefetchRows);
+    // K/V rows of the next positions of the slice on their way into L2 while
+    // the queries are prepared (one bulk prefetch per row)
+    const int n = min(t1 - t0 - staged, kPrefetchRows);
     const int r = threadIdx.x < n ? threadIdx.x : threadIdx.x - n;
     if (threadIdx.x < 2 * n) {
       const KV* base = static_cast<const KV*>(threadIdx.x < n ? p.k : p.v);
-      prefetch_l2_bulk(base + static_cast<int64_t>(b) * p.kv_bs + static_cast<int64_t>(t0 + r) * p.kv_ts + g * DIM,
+      prefetch_l2_bulk(base + static_cast<int64_t>(b) * p.kv_bs + static_cast<int64_t>(t0 + staged + r) * p.kv_ts +
+                           g * DIM,
                        DIM * sizeof(KV));
     }
   }
@@ -267,6 +295,16 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const __grid_
       }
       __threadfence_block();
     }
+    if constexpr (CL) {
+      // the staged rows are in; the new position's row replaces its stale copy
+      asm volatile("cp.async.wait_all;" ::: "memory");
+      __syncthreads();
+      if (pos >= t0 && pos < t0 + staged)
+        for (int i = threadIdx.x; i < DIM; i += kAttnThreads) {
+          kv_stage[(pos - t0) * DIM + i] = kvn[0][i];
+          kv_stage[(kStageRows + pos - t0) * DIM + i] = kvn[1][i];
+        }
+    }
     __syncthreads();
   }
 
@@ -287,10 +325,16 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const __grid_
     // All PB key rows are loaded before any is used (positions past t1 read
     // the last valid row and are masked below), so a batch costs one memory
     // latency rather than PB.
+    // (rows staged in shared memory are read from there)
     float kf[PB][DPL];
 #pragma unroll
-    for (int pp = 0; pp < PB; ++pp)
-      KvRow<KV, DPL>::load(p.k, kvbase + static_cast<int64_t>(min(tb + pp, t1 - 1)) * p.kv_ts, kf[pp]);
+    for (int pp = 0; pp < PB; ++pp) {
+      const int t = min(tb + pp, t1 - 1);
+      if (CL && MODEL && t - t0 < staged)
+        KvRow<KV, DPL>::load(kv_stage, (t - t0) * DIM + lane * DPL, kf[pp]);
+      else
+        KvRow<KV, DPL>::load(p.k, kvbase + static_cast<int64_t>(t) * p.kv_ts, kf[pp]);
+    }
     float part[32];
 #pragma unroll
     for (int pp = 0; pp < PB; ++pp) {
@@ -305,8 +349,13 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const __grid_
     // value rows of the batch, issued before the softmax bookkeeping
     float vf[PB][DPL];
 #pragma unroll
-    for (int pp = 0; pp < PB; ++pp)
-      KvRow<KV, DPL>::load(p.v, kvbase + static_cast<int64_t>(min(tb + pp, t1 - 1)) * p.kv_ts, vf[pp]);
+    for (int pp = 0; pp < PB; ++pp) {
+      const int t = min(tb + pp, t1 - 1);
+      if (CL && MODEL && t - t0 < staged)
+        KvRow<KV, DPL>::load(kv_stage, (kStageRows + t - t0) * DIM + lane * DPL, vf[pp]);
+      else
+        KvRow<KV, DPL>::load(p.v, kvbase + static_cast<int64_t>(t) * p.kv_ts, vf[pp]);
+    }
     float score = reduce_scatter32(part, lane) * sl;
     const bool valid = tb + (lane % PB) < t1;
     if (!valid) score = -INFINITY;
@@ -350,7 +399,12 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const __grid_
   __syncthreads();
 
   if constexpr (CL) {
-    // ---------------- cluster merge: partials stay in shared memory
+    // ---------------- cluster merge: each CTA stores its partial of element e
+    // into the CTA that finishes e (rank e / per), and its per-head max / sum
+    // into every CTA; after one cluster barrier each CTA combines locally,
+    // splits in rank order.
+    cg::cluster_group cluster = cg::this_cluster();
+    asm volatile("barrier.cluster.wait.aligned;" ::: "memory");  // every CTA has started
     for (int e = threadIdx.x; e < GS * DIM; e += kAttnThreads) {
       const int h = e / DIM, d = e % DIM;
       float M = -INFINITY;
@@ -365,26 +419,26 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const __grid_
           O = fmaf(wacc[w][h][d], f, O);
         }
       }
-      cpo[h][d] = O;
-      if (d == 0) {
-        cm[h] = M;
-        cl[h] = Ls;
-      }
+      const int owner = e / per;
+      *cluster.map_shared_rank(&rx[split * per + (e - owner * per)], owner) = O;
+      if (d == 0)
+        for (int r = 0; r < splits; ++r) {
+          *cluster.map_shared_rank(&rm[split][h], r) = M;
+          *cluster.map_shared_rank(&rl[split][h], r) = Ls;
+        }
     }
-    cg::cluster_group cluster = cg::this_cluster();
-    cluster.sync();
-    // rank r finishes elements [r*per, (r+1)*per) reading every rank's partial
+    cluster.sync();  // (no shared memory of another CTA is touched after this)
     for (int e = split * per + threadIdx.x; e < min(GS * DIM, (split + 1) * per); e += kAttnThreads) {
       const int h = e / DIM, d = e % DIM;
       float M = -INFINITY;
-      for (int s2 = 0; s2 < splits; ++s2) M = fmaxf(M, cluster.map_shared_rank(cm, s2)[h]);
+      for (int s2 = 0; s2 < splits; ++s2) M = fmaxf(M, rm[s2][h]);
       float Ls = 0.f, O = 0.f;
       for (int s2 = 0; s2 < splits; ++s2) {
-        const float ms = cluster.map_shared_rank(cm, s2)[h];
+        const float ms = rm[s2][h];
         if (ms != -INFINITY) {
           const float f = exp2f(ms - M);
-          Ls = fmaf(cluster.map_shared_rank(cl, s2)[h], f, Ls);
-          O = fmaf(cluster.map_shared_rank(&cpo[0][0], s2)[h * DIM + d], f, O);
+          Ls = fmaf(rl[s2][h], f, Ls);
+          O = fmaf(rx[s2 * per + (e - split * per)], f, O);
         }
       }
       float o = Ls > 0.f ? O / Ls : 0.f;
@@ -396,7 +450,6 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const __grid_
       }
       p.out[static_cast<int64_t>(b) * p.out_bs + static_cast<int64_t>(g * GS + h) * DIM + d] = o;
     }
-    cluster.sync();  // no CTA leaves while others still read its shared memory
     trace_exit(p.trace);
     return;
   }
@@ -525,8 +578,22 @@ int launch_t(const AttnParams& p, cudaStream_t stream, bool pdl) {
   cudaError_t e;
   if (p.model) {
     // the model keeps an f32 cache (checked by attention_launch)
-    e = cl ? cudaLaunchKernelEx(&cfg, attn_decode_kernel<float, DPL, GS, (GS == 4), true>, p)
-           : cudaLaunchKernelEx(&cfg, attn_decode_kernel<float, DPL, GS, false, true>, p);
+    if (cl) {
+      auto kern = attn_decode_kernel<float, DPL, GS, (GS == 4), true>;
+      const int stage_bytes = 2 * kStageRows * DPL * 32 * static_cast<int>(sizeof(float));
+      static int configured_device = -1;
+      int dev = 0;
+      cudaGetDevice(&dev);
+      if (configured_device != dev) {
+        e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, stage_bytes);
+        if (e != cudaSuccess) return fail_cuda(e, "attention set smem");
+        configured_device = dev;
+      }
+      cfg.dynamicSmemBytes = stage_bytes;
+      e = cudaLaunchKernelEx(&cfg, kern, p);
+    } else {
+      e = cudaLaunchKernelEx(&cfg, attn_decode_kernel<float, DPL, GS, false, true>, p);
+    }
   } else {
     e = cl ? cudaLaunchKernelEx(&cfg, attn_decode_kernel<KV, DPL, GS, (GS == 4), false>, p)
            : cudaLaunchKernelEx(&cfg, attn_decode_kernel<KV, DPL, GS, false, false>, p);
