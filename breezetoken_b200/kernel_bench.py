@@ -32,6 +32,28 @@ from breezetoken_b200.backends import Q8Weight
 from breezetoken_b200.quant import quantize_q8_0
 
 
+def _time_graph(fn, iters: int, stream: torch.cuda.Stream) -> float:
+    """Device time per call with `iters` calls captured in one CUDA graph (no
+    host launch cost between them), averaged over 3 replays."""
+    with torch.cuda.stream(stream):
+        for _ in range(3):
+            fn()
+    stream.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=stream):
+        for _ in range(iters):
+            fn()
+    with torch.cuda.stream(stream):
+        g.replay()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(3):
+            g.replay()
+        e1.record(stream)
+    e1.synchronize()
+    return e0.elapsed_time(e1) / 1e3 / (3 * iters)
+
+
 def _time(fn, iters: int, stream: torch.cuda.Stream) -> float:
     with torch.cuda.stream(stream):
         for _ in range(3):
@@ -84,9 +106,12 @@ def bench_gdn(batch: int, steps: int, heads: int = 16, dim: int = 128) -> dict:
         )
 
     sec = _time(run, steps, s)
+    gsec = _time_graph(run, steps, s)
     nbytes = batch * (2 * heads * dim * dim * 4 + 3 * heads * dim * 2 + 2 * heads * 4 + heads * dim * 4)
-    return {"kernel": "gdn_decode", "batch": batch, "steps": steps, "us_per_step": sec * 1e6, "bytes": nbytes,
-            "gbs": nbytes / sec / 1e9}
+    return {"kernel": "gdn_decode", "batch": batch, "steps": steps, "us_per_step": sec * 1e6,
+            "us_per_step_graph": gsec * 1e6, "bytes": nbytes, "gbs": nbytes / sec / 1e9,
+            "gbs_graph": nbytes / gsec / 1e9,
+            "note": "graph: the steps captured in one CUDA graph (device time; a B=1 state stays in L2)"}
 
 
 def bench_attn(batch: int, ctx: int, splits: int, iters: int) -> dict:
@@ -113,9 +138,10 @@ def bench_attn(batch: int, ctx: int, splits: int, iters: int) -> dict:
         )
 
     sec = _time(run, iters, s)
+    gsec = _time_graph(run, iters, s)
     nbytes = batch * ctx * kv_heads * dim * 2 * 2 + 2 * batch * heads * dim * 4
-    return {"kernel": "attn_decode", "batch": batch, "ctx": ctx, "splits": splits, "us": sec * 1e6, "bytes": nbytes,
-            "gbs": nbytes / sec / 1e9}
+    return {"kernel": "attn_decode", "batch": batch, "ctx": ctx, "splits": splits, "us": sec * 1e6,
+            "us_graph": gsec * 1e6, "bytes": nbytes, "gbs": nbytes / sec / 1e9, "gbs_graph": nbytes / gsec / 1e9}
 
 
 def bench_moe(tokens: int, iters: int) -> dict:
