@@ -492,60 +492,103 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const __grid_
     return;
   }
 
-  // ---------------- last CTA of the group merges the splits
-  __threadfence();
-  __syncthreads();
-  if (threadIdx.x == 0) s_ticket = atomicAdd(p.counters + static_cast<int64_t>(b) * p.kv_heads + g, 1u);
-  __syncthreads();
-  if (s_ticket != static_cast<uint32_t>(splits - 1)) {
-    trace_exit(p.trace);
-    return;
-  }
-  __threadfence();
-  // per-head split weights 2^(m_s - M) and total sum, one warp per head
-  // (the warp-partial buffer is free again and holds GS * splits weights)
-  float* fw = &wacc[0][0][0];
+  // ---------------- merge the splits: the last CTA of a (sequence, group)
+  // merges them, in two levels past kMergeGroup splits (the last CTA of each
+  // group of kMergeGroup splits merges its group into a group record)
+  const int ngrp = static_cast<int>(attn_groups(splits));
+  const int64_t bg = static_cast<int64_t>(b) * p.kv_heads + g;
+  const int64_t grec0 = static_cast<int64_t>(p.batch) * p.kv_heads * p.splits * GS + bg * ngrp * GS;
+  uint32_t* const top_counter = p.counters + bg;
+  float* fw = &wacc[0][0][0];  // (the warp-partial buffer is free again: GS x records weights)
   __shared__ float s_sum[GS];
-  for (int h = warp; h < GS; h += kAttnWarps) {
-    float M = -INFINITY;
-    for (int s = lane; s < splits; s += 32)
-      M = fmaxf(M, __ldcg(p.part + (rec0 + static_cast<int64_t>(s) * GS + h) * (DIM + 2) + DIM));
-    M = warp_max(M);
-    float Ls = 0.f;
-    for (int s = lane; s < splits; s += 32) {
-      const float* rec = p.part + (rec0 + static_cast<int64_t>(s) * GS + h) * (DIM + 2);
-      const float ms = __ldcg(rec + DIM);
-      const float f = ms == -INFINITY ? 0.f : exp2f(ms - M);
-      fw[h * splits + s] = f;
-      Ls = fmaf(__ldcg(rec + DIM + 1), f, Ls);
+  // merges `count` records starting at record index r0 (stride GS records);
+  // final: output (normalised, gated), else one record at record index dst
+  auto merge = [&](int64_t r0, int count, bool final, int64_t dst) {
+    for (int h = warp; h < GS; h += kAttnWarps) {
+      float M = -INFINITY;
+      for (int s = lane; s < count; s += 32)
+        M = fmaxf(M, __ldcg(p.part + (r0 + static_cast<int64_t>(s) * GS + h) * (DIM + 2) + DIM));
+      M = warp_max(M);
+      float Ls = 0.f;
+      for (int s = lane; s < count; s += 32) {
+        const float* rec = p.part + (r0 + static_cast<int64_t>(s) * GS + h) * (DIM + 2);
+        const float ms = __ldcg(rec + DIM);
+        const float f = ms == -INFINITY ? 0.f : exp2f(ms - M);
+        fw[h * count + s] = f;
+        Ls = fmaf(__ldcg(rec + DIM + 1), f, Ls);
+      }
+      Ls = warp_sum(Ls);
+      if (lane == 0) {
+        s_sum[h] = Ls;
+        if (!final) {
+          float* out_rec = p.part + (dst + h) * (DIM + 2);
+          out_rec[DIM] = M;
+          out_rec[DIM + 1] = Ls;
+        }
+      }
     }
-    Ls = warp_sum(Ls);
-    if (lane == 0) s_sum[h] = Ls;
-  }
-  __syncthreads();
-  const int64_t rstride = static_cast<int64_t>(GS) * (DIM + 2);
-  for (int e = threadIdx.x; e < GS * DIM; e += kAttnThreads) {
-    const int h = e / DIM, d = e % DIM;
-    const float* base = p.part + (rec0 + h) * (DIM + 2) + d;
-    const float* f = fw + h * splits;
-    float O0 = 0.f, O1 = 0.f, O2 = 0.f, O3 = 0.f;
-    int s = 0;
-    for (; s + 4 <= splits; s += 4) {
-      const float a0 = __ldcg(base + s * rstride), a1 = __ldcg(base + (s + 1) * rstride);
-      const float a2 = __ldcg(base + (s + 2) * rstride), a3 = __ldcg(base + (s + 3) * rstride);
-      O0 = fmaf(a0, f[s], O0);
-      O1 = fmaf(a1, f[s + 1], O1);
-      O2 = fmaf(a2, f[s + 2], O2);
-      O3 = fmaf(a3, f[s + 3], O3);
+    __syncthreads();
+    const int64_t rstride = static_cast<int64_t>(GS) * (DIM + 2);
+    for (int e = threadIdx.x; e < GS * DIM; e += kAttnThreads) {
+      const int h = e / DIM, d = e % DIM;
+      const float* base = p.part + (r0 + h) * (DIM + 2) + d;
+      const float* f = fw + h * count;
+      float O0 = 0.f, O1 = 0.f, O2 = 0.f, O3 = 0.f;
+      int s = 0;
+      for (; s + 4 <= count; s += 4) {
+        const float a0 = __ldcg(base + s * rstride), a1 = __ldcg(base + (s + 1) * rstride);
+        const float a2 = __ldcg(base + (s + 2) * rstride), a3 = __ldcg(base + (s + 3) * rstride);
+        O0 = fmaf(a0, f[s], O0);
+        O1 = fmaf(a1, f[s + 1], O1);
+        O2 = fmaf(a2, f[s + 2], O2);
+        O3 = fmaf(a3, f[s + 3], O3);
+      }
+      for (; s < count; ++s) O0 = fmaf(__ldcg(base + s * rstride), f[s], O0);
+      const float O = (O0 + O1) + (O2 + O3);
+      if (final) {
+        const float Ls = s_sum[h];
+        float o = Ls > 0.f ? O / Ls : 0.f;
+        if constexpr (MODEL)
+          o *= sigmoid_f(p.gate[static_cast<int64_t>(b) * p.q_bs + static_cast<int64_t>(g * GS + h) * p.q_hs + d]);
+        p.out[static_cast<int64_t>(b) * p.out_bs + static_cast<int64_t>(g * GS + h) * DIM + d] = o;
+      } else {
+        p.part[(dst + h) * (DIM + 2) + d] = O;
+      }
     }
-    for (; s < splits; ++s) O0 = fmaf(__ldcg(base + s * rstride), f[s], O0);
-    const float Ls = s_sum[h];
-    float o = Ls > 0.f ? ((O0 + O1) + (O2 + O3)) / Ls : 0.f;
-    if constexpr (MODEL)
-      o *= sigmoid_f(p.gate[static_cast<int64_t>(b) * p.q_bs + static_cast<int64_t>(g * GS + h) * p.q_hs + d]);
-    p.out[static_cast<int64_t>(b) * p.out_bs + static_cast<int64_t>(g * GS + h) * DIM + d] = o;
+  };
+  // arrival: returns true in the last of `n` CTAs counted by *counter (then re-armed)
+  auto last_of = [&](uint32_t* counter, int n) -> bool {
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      s_ticket = atomicAdd(counter, 1u);
+      if (s_ticket == static_cast<uint32_t>(n - 1)) atomicExch(counter, 0u);
+    }
+    __syncthreads();
+    const bool last = s_ticket == static_cast<uint32_t>(n - 1);
+    if (last) __threadfence();
+    return last;
+  };
+  if (ngrp == 0) {
+    if (!last_of(top_counter, splits)) {
+      trace_exit(p.trace);
+      return;
+    }
+    merge(rec0, splits, true, 0);
+  } else {
+    const int grp = split / kMergeGroup;
+    const int in_grp = min(kMergeGroup, splits - grp * kMergeGroup);
+    if (!last_of(p.counters + static_cast<int64_t>(p.batch) * p.kv_heads + bg * ngrp + grp, in_grp)) {
+      trace_exit(p.trace);
+      return;
+    }
+    merge(rec0 + static_cast<int64_t>(grp) * kMergeGroup * GS, in_grp, false, grec0 + grp * GS);
+    if (!last_of(top_counter, ngrp)) {
+      trace_exit(p.trace);
+      return;
+    }
+    merge(grec0, ngrp, true, 0);
   }
-  if (threadIdx.x == 0) atomicExch(p.counters + static_cast<int64_t>(b) * p.kv_heads + g, 0u);
   if (p.trace) {
     __syncthreads();
     trace_exit(p.trace);

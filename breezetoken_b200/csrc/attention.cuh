@@ -43,11 +43,23 @@ struct AttnParams {
   TraceRec* trace;  // optional launch timeline record (null = off)
 };
 
-// Workspace floats for the partials, then one u32 counter per (b, g).
+// More than kMergeGroup splits merge in two levels: the last CTA of each
+// group of kMergeGroup splits merges the group, the last group merger the
+// groups.
+constexpr int kMergeGroup = 16;
+__host__ __device__ inline int64_t attn_groups(int64_t splits) {
+  return splits > kMergeGroup ? (splits + kMergeGroup - 1) / kMergeGroup : 0;
+}
+
+// Workspace floats for the split (and group) partial records...
 inline int64_t attn_part_floats(int64_t batch, int64_t kv_heads, int64_t heads, int64_t dim,
                                 int64_t splits) {
   const int64_t gs = heads / kv_heads;
-  return batch * kv_heads * splits * gs * (dim + 2);
+  return batch * kv_heads * (splits + attn_groups(splits)) * gs * (dim + 2);
+}
+// ... then the u32 arrival counters: one per (b, g), then one per group.
+inline int64_t attn_counters(int64_t batch, int64_t kv_heads, int64_t splits) {
+  return batch * kv_heads * (1 + attn_groups(splits));
 }
 
 int attention_launch(const AttnParams& p, cudaStream_t stream, bool pdl);

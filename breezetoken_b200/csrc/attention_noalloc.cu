@@ -58,7 +58,7 @@ extern "C" int bt_attention_decode_noalloc(const float* q, const void* k, const 
       cap > (1LL << 30) || splits < 1)
     return fail(BT_ERR_INVALID, "noalloc attention: shape out of range");
   const int64_t part_bytes = (4 * bt::attn_part_floats(batch, kv_heads, heads, dim, splits) + 255) / 256 * 256;
-  const int64_t counter_bytes = 4 * batch * kv_heads;
+  const int64_t counter_bytes = 4 * bt::attn_counters(batch, kv_heads, splits);
   if (part_bytes + counter_bytes > bt::kNoallocScratchBytes)
     return fail(BT_ERR_INVALID,
                 "noalloc attention: batch %lld x kv_heads %lld x splits %d needs %lld scratch bytes, above the "

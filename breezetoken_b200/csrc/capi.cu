@@ -155,7 +155,7 @@ int bt_rope(const float* x, const float* cos_t, const float* sin_t, const int32_
 int64_t bt_attention_workspace_bytes(int64_t batch, int64_t kv_heads, int64_t heads, int64_t dim, int splits) {
   if (batch < 1 || kv_heads < 1 || heads < 1 || dim < 1 || splits < 1) return 0;
   const int64_t part = (4 * bt::attn_part_floats(batch, kv_heads, heads, dim, splits) + 255) / 256 * 256;
-  return part + (4 * batch * kv_heads + 255) / 256 * 256;
+  return part + (4 * bt::attn_counters(batch, kv_heads, splits) + 255) / 256 * 256;
 }
 
 int bt_attention_decode(const float* q, const void* k, const void* v, int kv_dtype, const int32_t* lens, float* out,

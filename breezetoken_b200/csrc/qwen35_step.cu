@@ -124,7 +124,7 @@ int64_t qwen35_proj_elems(const BtQwen35Dims& d) {
 int64_t qwen35_workspace_bytes(const BtQwen35Dims& d) {
   return align256(8LL * d.batch) + 256 +
          align256(4 * attn_part_floats(d.batch, d.n_kv, d.n_heads, d.head_dim, kAttnSplits)) +
-         align256(4LL * d.batch * d.n_kv);
+         align256(4 * attn_counters(d.batch, d.n_kv, kAttnSplits));
 }
 
 int qwen35_step(const BtQwen35Model& m, const BtQwen35Runtime& rt, int with_logits, cudaStream_t s) {
