@@ -5,23 +5,34 @@
 // the clamped sum; per selected expert act = silu(gate x) * up x, then
 // out = sum_k w_k * down_k act_k.  The reference stages the selected experts'
 // bytes to the device and dequantises them to f32 before a matmul; here the
-// IQ3_S bytes are decoded inside the GEMV and never materialised.
+// IQ3_S bytes are decoded in registers and fed to the tensor cores.
 //
 // A decode batch of T tokens selects P = T * top_k (token, expert) pairs.
-// `moe_group_kernel` sorts the pairs by expert (ascending id, stable), so each
+// `moe_prep_kernel` sorts the pairs by expert (ascending id, stable), so each
 // selected expert's weights are read once for all the tokens that chose it
-// (U unique experts: bytes = U * 1,351,680 at the 35B shape).  The gate/up
-// kernel gives each expert 32 CTAs of 16 gate + 16 matching up rows and
-// writes act for every pair; the down kernel gives each expert 32 CTAs of
-// 64 rows; the pairs of a token are summed in routing order.
+// (U unique experts: bytes = U * 1,351,680 at the 35B shape), and encodes
+// each token's activation once.  The gate/up and down kernels are persistent
+// (one 16-warp CTA per SM, each taking a contiguous range of (expert, row
+// chunk) items); every warp decodes two 16-row tiles of one 256-weight
+// column block per item and loads the next item's tiles while it computes.
 //
-// IQ3_S GEMV: a warp lane decodes one 32-weight sub-block at a time -- eight
-// loads from the sign-applied codebook (8192 entries, in shared memory) --
-// into signed int8 words, and dots them with the activation
-// encoded as three int8 digits of a 22-bit fixed-point value per 32-element
-// block (the q8 GEMV's encoding), 24 dp4a per sub-block: the integer sums are
-// exact, so the only roundings are the activation's encoding and the f32
-// accumulation over sub-blocks.
+// Weights: `bt_repack_iq3_s` stores each 16-row x 256-weight tile (16 GGUF
+// blocks) as one 1792-byte chunk laid out for the m16n8k16 MMA: lane (g, t)
+// loads, with three 16-byte and a few small coalesced loads, the quant bytes
+// of rows g and g+8 for groups 2t and 2t+1 (weights 8t..8t+7) of all 8
+// sub-blocks, so each decoded 4-weight group is two of the MMA's A-fragment
+// registers (the k order inside a sub-block is permuted identically on both
+// operands).  A group is one 8-byte load from the codebook in shared memory,
+// stored as fp16 (exact: |value| <= 15) in 16 bank-interleaved copies so a
+// warp's lookups never conflict, and its 4 sign bits XORed into the fp16
+// sign bits.
+//
+// Activations: each vector x is scaled by a power of two (max |x| in
+// [2^13, 2^14)) and split into fp16 hi + lo planes (hi = fp16(x), lo =
+// fp16(x - hi): ~22 significant bits); B columns 2j and 2j+1 are token j's
+// hi and lo planes, so one MMA pair serves 4 tokens and a lane's C fragment
+// holds both planes of its token.  Products are exact and accumulate in f32;
+// per sub-block the rows' scales d * (1 + 2 * nibble) multiply the sums.
 #include <cuda_fp16.h>
 
 #include <algorithm>
@@ -34,56 +45,126 @@ namespace bt {
 
 namespace {
 
-// The IQ3_S codebook with the 4 sign bits of a group applied: entry
-// idx9 | (signs4 << 9) holds the group's 4 signed int8 weights (before the
-// sub-block scale), so decoding a group is one table load.
+// The IQ3_S codebook (quant/_tables.py:1042): 512 entries of 4 unsigned
+// weights, byte j = weight j of the group.
 constexpr uint32_t kGrid[512] = {
 #include "iq3s_grid.inc"
 };
 
-struct SignedGrid {
-  uint32_t v[8192];
-};
+constexpr bool grid_values_small() {
+  for (int i = 0; i < 512; ++i)
+    for (int j = 0; j < 4; ++j)
+      if (((kGrid[i] >> (8 * j)) & 255u) > 15u) return false;
+  return true;
+}
+static_assert(grid_values_small(), "IQ3_S codebook values must be <= 15 (exact fp16 operands)");
 
-constexpr SignedGrid make_signed_grid() {
-  SignedGrid t{};
-  for (int i = 0; i < 8192; ++i) {
-    const uint32_t g = kGrid[i & 511], sb4 = static_cast<uint32_t>(i) >> 9;
-    // bit j of sb4 -> 0xFF in byte j; then per-byte two's-complement negation
-    const uint32_t mask = ((sb4 * 0x00204081u) & 0x01010101u) * 0xFFu;
-    t.v[i] = (g ^ mask) + (mask & 0x01010101u);
-  }
-  return t;
+// fp16 bit pattern of a non-negative integer n < 2048 (exact).
+constexpr uint32_t half_bits(uint32_t n) {
+  if (n == 0) return 0;
+  int e = 0;
+  while ((n >> (e + 1)) != 0) ++e;
+  return (static_cast<uint32_t>(e + 15) << 10) | ((n << (10 - e)) & 0x3FFu);
 }
 
-__device__ const SignedGrid g_signed = make_signed_grid();
+// Codebook in its shared-memory layout: row (b, qh) at byte b * 256 + qh *
+// 128 holds 16 copies of the 4 fp16 weights of entry qh * 256 + b (8 bytes
+// each).  Lane L reads copy L % 16: a half warp touches each bank once.
+struct alignas(8) Half4 {
+  uint32_t lo, hi;  // (w0, w1), (w2, w3)
+};
+struct __align__(16) HalfGrid {
+  Half4 v[512 * 16];
+};
+constexpr HalfGrid make_half_grid() {
+  HalfGrid t{};
+  for (int b = 0; b < 256; ++b)
+    for (int qh = 0; qh < 2; ++qh) {
+      const uint32_t e = kGrid[qh * 256 + b];
+      const uint32_t lo = half_bits(e & 255u) | (half_bits((e >> 8) & 255u) << 16);
+      const uint32_t hi = half_bits((e >> 16) & 255u) | (half_bits(e >> 24) << 16);
+      for (int c = 0; c < 16; ++c) {
+        t.v[(b * 2 + qh) * 16 + c].lo = lo;
+        t.v[(b * 2 + qh) * 16 + c].hi = hi;
+      }
+    }
+  return t;
+}
+__device__ const HalfGrid g_half_grid = make_half_grid();
+constexpr int kLutBytes = static_cast<int>(sizeof(HalfGrid));
+static_assert(kLutBytes == 64 * 1024, "codebook layout");
 
-constexpr int kThreads = 256;
+constexpr int kThreads = 512;  // expert kernels: 16 warps
 constexpr int kWarps = kThreads / 32;
-constexpr int kGateRowsPerCta = 16;   // + the 16 matching up rows
-constexpr int kDownRowsPerCta = 64;
 constexpr float kWeightSumMin = 6.103515625e-5f;  // moe.py:24
-// Workspace header words [kTicketBase, kTicketBase + hidden / 64): the
-// one-token combine's arrival counters (zero between calls).
+// Workspace header words [kTicketBase, kTicketBase + hidden / rows per item):
+// the one-token combine's arrival counters (zero between calls).
 constexpr int kTicketBase = 16;
 constexpr int kHeaderBytes = 512;
 
+// Tile chunk: 16 rows x 256 weights.  Sections (lane L = 4 g + t, group
+// q = 2 s + h of the lane's 16 per row: sub-block s, weights 8t + 4h ..):
+//   [0, 512)     qs of row g:   16 B per lane, byte q = qs[8s + 2t + h]
+//   [512, 1024)  qs of row g+8: same
+//   [1024, 1536) signs: per lane (row g: S0, S1; row g+8: S0, S1); S0 bit
+//                15 - q / 31 - q = sign of weight 0 / 1 of group q, S1 the
+//                same for weights 2 / 3
+//   [1536, 1664) qh: per lane one word, bit 16r + q = qh[s] bit 2t + h
+//   [1664, 1792) per row: scales[4], d (fp16), 2 pad bytes
+constexpr int kChunkBytes = 16 * kIq3sBlockBytes;
+constexpr int kQsA = 0, kQsB = 512, kSigns = 1024, kQh = 1536, kScales = 1664;
+static_assert(kChunkBytes == 1792, "tile chunk");
+
+constexpr int kTokensPerPass = 4;              // 8 MMA columns: hi and lo per token
+constexpr int kRedBytes = kWarps * 32 * 4 * 4;  // 4 partial sums per lane
+constexpr int kMiscBytes = 256;                 // token scales, block maxima
+
+// fp16 planes of one vector of K elements in shared memory: hi at 0, lo at
+// plane_stride (== 64 mod 128 bytes, so a quarter warp's hi and lo reads
+// fall on disjoint banks), vectors token_stride apart.
+__host__ __device__ constexpr int plane_stride(int k) { return 2 * k + 64; }
+__host__ __device__ constexpr int token_stride(int k) { return 2 * plane_stride(k); }
+
 // ------------------------------------------------------------------ repack
-// GGUF IQ3_S block (110 B: d[2] qs[64] qh[8] signs[32] scales[4]) -> the
-// aligned 112-byte block. One thread per block.
-__global__ void repack_iq3s_kernel(const uint8_t* __restrict__ src, uint8_t* __restrict__ dst, int64_t n_blocks) {
-  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n_blocks;
+// GGUF IQ3_S rows (110-byte blocks: d[2] qs[64] qh[8] signs[32] scales[4])
+// -> tile chunks.  One thread per (chunk, lane).
+__global__ void repack_iq3s_kernel(const uint8_t* __restrict__ src, uint8_t* __restrict__ dst, int64_t n_chunks,
+                                   int kb_per_row) {
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n_chunks * 32;
        i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-    const uint8_t* s = src + i * 110;
-    uint8_t* d = dst + i * kIq3sBlockBytes;
-    for (int j = 0; j < 64; ++j) d[j] = s[2 + j];        // qs
-    for (int j = 0; j < 32; ++j) d[64 + j] = s[74 + j];  // signs
-    for (int j = 0; j < 8; ++j) d[96 + j] = s[66 + j];   // qh
-    for (int j = 0; j < 4; ++j) d[104 + j] = s[106 + j]; // scales
-    d[108] = s[0];
-    d[109] = s[1];
-    d[110] = 0;
-    d[111] = 0;
+    const int64_t chunk = i >> 5;
+    const int lane = static_cast<int>(i & 31), g = lane >> 2, t = lane & 3;
+    const int64_t tile = chunk / kb_per_row;
+    const int kb = static_cast<int>(chunk % kb_per_row);
+    uint8_t* d = dst + chunk * kChunkBytes;
+    uint32_t qh = 0;
+    for (int r = 0; r < 2; ++r) {
+      const uint8_t* blk = src + ((tile * 16 + g + 8 * r) * kb_per_row + kb) * 110;
+      uint8_t* q = d + (r ? kQsB : kQsA) + 16 * lane;
+      uint32_t s01 = 0, s23 = 0;
+      for (int s = 0; s < 8; ++s)
+        for (int h = 0; h < 2; ++h) {
+          const int grp = 2 * s + h;
+          q[grp] = blk[2 + 8 * s + 2 * t + h];
+          const uint32_t nib = (blk[74 + 4 * s + t] >> (4 * h)) & 15u;
+          s01 |= ((nib & 1u) << (15 - grp)) | (((nib >> 1) & 1u) << (31 - grp));
+          s23 |= (((nib >> 2) & 1u) << (15 - grp)) | (((nib >> 3) & 1u) << (31 - grp));
+          qh |= ((static_cast<uint32_t>(blk[66 + s]) >> (2 * t + h)) & 1u) << (16 * r + grp);
+        }
+      uint32_t* sw = reinterpret_cast<uint32_t*>(d + kSigns + 16 * lane + 8 * r);
+      sw[0] = s01;
+      sw[1] = s23;
+    }
+    *reinterpret_cast<uint32_t*>(d + kQh + 4 * lane) = qh;
+    if (lane < 16) {
+      const uint8_t* blk = src + ((tile * 16 + lane) * kb_per_row + kb) * 110;
+      uint8_t* rec = d + kScales + 8 * lane;
+      for (int j = 0; j < 4; ++j) rec[j] = blk[106 + j];
+      rec[4] = blk[0];
+      rec[5] = blk[1];
+      rec[6] = 0;
+      rec[7] = 0;
+    }
   }
 }
 
@@ -141,22 +222,25 @@ __global__ void moe_route_kernel(const float* __restrict__ logits, int64_t t, in
     }
 }
 
-// ------------------------------------------------------------------ group
-// Workspace header: [n_unique, bad ids] then per slot u < P: expert, first
-// pair, pair count; then the pair list sorted by (expert, pair).
+// ------------------------------------------------------------------ workspace
+// Header: [n_unique, bad ids, ..., tickets]; per slot u < P: expert, first
+// pair, pair count; the pair list sorted by (expert, pair); every token's
+// fp16 planes and scale; every pair's act and down output (f32).
 struct MoeWs {
   int32_t* hdr;
   int32_t* slot_expert;
   int32_t* slot_start;
   int32_t* slot_count;
   int32_t* pairs;
-  float* act;  // (P, ffn)
-  float* dn;   // (P, hidden)
+  uint8_t* xenc;  // (T, 4 * hidden): hi plane, lo plane
+  float* xscale;  // (T): x = (hi + lo) * xscale
+  float* act;     // (P, ffn)
+  float* dn;      // (P, hidden)
 };
 
 __host__ __device__ inline int64_t align256(int64_t b) { return (b + 255) / 256 * 256; }
 
-__host__ __device__ inline MoeWs moe_ws(void* base, int64_t p, int64_t hidden, int64_t ffn) {
+__host__ __device__ inline MoeWs moe_ws(void* base, int64_t t, int64_t p, int64_t hidden, int64_t ffn) {
   uint8_t* b = static_cast<uint8_t*>(base);
   MoeWs w;
   int64_t o = 0;
@@ -170,18 +254,87 @@ __host__ __device__ inline MoeWs moe_ws(void* base, int64_t p, int64_t hidden, i
   o += align256(4 * p);
   w.pairs = reinterpret_cast<int32_t*>(b + o);
   o += align256(4 * p);
+  w.xenc = b + o;
+  o += align256(4 * t * hidden);
+  w.xscale = reinterpret_cast<float*>(b + o);
+  o += align256(4 * t);
   w.act = reinterpret_cast<float*>(b + o);
   o += align256(4 * p * ffn);
   w.dn = reinterpret_cast<float*>(b + o);
   return w;
 }
 
-inline int64_t moe_ws_bytes(int64_t p, int64_t hidden, int64_t ffn) {
-  return kHeaderBytes + 4 * align256(4 * p) + align256(4 * p * ffn) + align256(4 * p * hidden);
+inline int64_t moe_ws_bytes(int64_t t, int64_t p, int64_t hidden, int64_t ffn) {
+  return kHeaderBytes + 4 * align256(4 * p) + align256(4 * t * hidden) + align256(4 * t) + align256(4 * p * ffn) +
+         align256(4 * p * hidden);
 }
 
-// One CTA: counting sort of the P pairs by expert id (stable).
-__global__ void moe_group_kernel(const int32_t* __restrict__ ids, int p_total, int n_experts, MoeWs ws) {
+// ------------------------------------------------------------------ encode
+// Power-of-two scale of a vector with max |x| = m: inv = 2^e with m * inv in
+// [2^13, 2^14) (fp16 holds it with room), sx = 1 / inv.  Vectors with
+// m < 2^-113 (all-zero ones included) encode as zero.
+__device__ __forceinline__ void vector_scale(float m, float& inv, float& sx) {
+  const uint32_t be = (__float_as_uint(m) >> 23) & 255u;  // biased exponent; m >= 0
+  const bool ok = be >= 14u;
+  inv = ok ? __uint_as_float((267u - be) << 23) : 0.f;
+  sx = ok ? __uint_as_float((be - 13u) << 23) : 0.f;
+}
+
+// hi = fp16(x * inv), lo = fp16(x * inv - hi): hi + lo = x * inv to ~22 bits.
+__device__ __forceinline__ void split_half(float x, float inv, __half& hi, __half& lo) {
+  const float v = x * inv;  // exact (power of two)
+  hi = __float2half_rn(v);
+  lo = __float2half_rn(v - __half2float(hi));
+}
+
+__device__ __forceinline__ void store_planes(const float4& h, float inv, uint8_t* hi_dst, uint8_t* lo_dst) {
+  __half a[4], b[4];
+  split_half(h.x, inv, a[0], b[0]);
+  split_half(h.y, inv, a[1], b[1]);
+  split_half(h.z, inv, a[2], b[2]);
+  split_half(h.w, inv, a[3], b[3]);
+  *reinterpret_cast<uint2*>(hi_dst) = make_uint2(__half_as_ushort(a[0]) | (__half_as_ushort(a[1]) << 16),
+                                                 __half_as_ushort(a[2]) | (__half_as_ushort(a[3]) << 16));
+  *reinterpret_cast<uint2*>(lo_dst) = make_uint2(__half_as_ushort(b[0]) | (__half_as_ushort(b[1]) << 16),
+                                                 __half_as_ushort(b[2]) | (__half_as_ushort(b[3]) << 16));
+}
+
+// Max over the CTA (all threads call it; `red` holds kWarps floats).
+__device__ __forceinline__ float cta_max(float v, float* red) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  v = warp_max(v);
+  __syncthreads();  // earlier readers of red are done
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  return warp_max(lane < kWarps ? red[lane] : 0.f);
+}
+
+// ------------------------------------------------------------------ prep
+// Block 0 (T > 1): counting sort of the P pairs by expert id (stable) into
+// slots.  The other blocks: encode token (block - 1) (T == 1: token 0).
+__global__ void __launch_bounds__(kThreads) moe_prep_kernel(const int32_t* __restrict__ ids, int p_total,
+                                                            int n_experts, int direct, const float* __restrict__ x,
+                                                            int hidden, MoeWs ws) {
+  pdl_wait();
+  pdl_launch_dependents();
+  if (direct || blockIdx.x > 0) {
+    __shared__ float red[kWarps];
+    const int tok = blockIdx.x - (direct ? 0 : 1);
+    const float4* src = reinterpret_cast<const float4*>(x + static_cast<int64_t>(tok) * hidden);
+    float m = 0.f;
+    for (int f = threadIdx.x; f < hidden / 4; f += kThreads) {
+      const float4 h = src[f];
+      m = fmaxf(m, fmaxf(fmaxf(fabsf(h.x), fabsf(h.y)), fmaxf(fabsf(h.z), fabsf(h.w))));
+    }
+    m = cta_max(m, red);
+    float inv, sx;
+    vector_scale(m, inv, sx);
+    uint8_t* dst = ws.xenc + static_cast<int64_t>(tok) * 4 * hidden;
+    for (int f = threadIdx.x; f < hidden / 4; f += kThreads)
+      store_planes(src[f], inv, dst + 8 * f, dst + 2 * hidden + 8 * f);
+    if (threadIdx.x == 0) ws.xscale[tok] = sx;
+    return;
+  }
   extern __shared__ int32_t sm[];
   int32_t* cnt = sm;               // [n_experts]
   int32_t* off = sm + n_experts;   // [n_experts] exclusive prefix of counts
@@ -224,156 +377,146 @@ __global__ void moe_group_kernel(const int32_t* __restrict__ ids, int p_total, i
   }
 }
 
-// ------------------------------------------------------------------ GEMV core
-// Activation vectors in shared memory, per vector v: three digit planes x two
-// halves of each 32-element sub-block, SBR sub-blocks (uint4 each), then the
-// per-sub-block scales.
-template <int SBR>
-struct XSmem {
-  static constexpr int kPlaneBytes = SBR * 16;
-  static constexpr int kVecBytes = 6 * kPlaneBytes + SBR * 4;
+// ------------------------------------------------------------------ MMA core
+__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
+  uint32_t d;
+  asm("prmt.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(sel));
+  return d;
+}
+
+__device__ __forceinline__ uint4 ld_stream16(const uint8_t* p) {
+  uint4 v;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p));
+  return v;
+}
+__device__ __forceinline__ uint32_t ld_stream4(const uint8_t* p) {
+  uint32_t v;
+  asm volatile("ld.global.nc.L1::no_allocate.u32 %0, [%1];" : "=r"(v) : "l"(p));
+  return v;
+}
+
+// A lane's share of one tile chunk (rows g and g+8).
+struct Tile {
+  uint4 qa, qb, sg;
+  uint32_t qh;
+  uint2 ra, rb;  // scale records of rows g, g+8
 };
 
-// Encode `n` f32 values at src (16-byte aligned) into vector slot v.
-template <int SBR>
-__device__ __forceinline__ void encode_vec(const float* __restrict__ src, uint8_t* xs, int v) {
-  constexpr int K = SBR * 32, NF4 = K / 4;
-  uint8_t* base = xs + v * XSmem<SBR>::kVecBytes;
-  float* sx = reinterpret_cast<float*>(base + 6 * XSmem<SBR>::kPlaneBytes);
-  for (int f = threadIdx.x; f < ((NF4 + kThreads - 1) / kThreads) * kThreads; f += kThreads) {
-    const int fc = min(f, NF4 - 1);
-    float4 h = reinterpret_cast<const float4*>(src)[fc];
-    if (f >= NF4) h = make_float4(0.f, 0.f, 0.f, 0.f);
-    float m = fmaxf(fmaxf(fabsf(h.x), fabsf(h.y)), fmaxf(fabsf(h.z), fabsf(h.w)));
-    m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 1));
-    m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 2));
-    m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 4));
-    const uint32_t be = (__float_as_uint(m) >> 23) & 255u;
-    const bool ok = be >= 22u;
-    const float inv = ok ? __uint_as_float((275u - be) << 23) : 0.f;
-    const float scale = ok ? __uint_as_float((be - 21u) << 23) : 0.f;
-    int a[4], b[4], c[4];
-    const float e4[4] = {h.x, h.y, h.z, h.w};
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const int X = __float2int_rn(e4[i] * inv);
-      c[i] = ((X + 128) & 255) - 128;
-      const int x1 = (X - c[i]) >> 8;
-      b[i] = ((x1 + 128) & 255) - 128;
-      a[i] = (x1 - b[i]) >> 8;
-    }
-    if (f < NF4) {
-      const int sb = f >> 3, w = f & 7;
-      const int h2 = w >> 2, comp = w & 3;
-      auto pk = [](const int (&d)[4]) {
-        return (static_cast<uint32_t>(d[0]) & 255u) | ((static_cast<uint32_t>(d[1]) & 255u) << 8) |
-               ((static_cast<uint32_t>(d[2]) & 255u) << 16) | ((static_cast<uint32_t>(d[3]) & 255u) << 24);
-      };
-      reinterpret_cast<uint32_t*>(base + (0 * 2 + h2) * XSmem<SBR>::kPlaneBytes + sb * 16)[comp] = pk(a);
-      reinterpret_cast<uint32_t*>(base + (1 * 2 + h2) * XSmem<SBR>::kPlaneBytes + sb * 16)[comp] = pk(b);
-      reinterpret_cast<uint32_t*>(base + (2 * 2 + h2) * XSmem<SBR>::kPlaneBytes + sb * 16)[comp] = pk(c);
-      if (w == 0) sx[sb] = scale;
-    }
-  }
+__device__ __forceinline__ void load_tile(const uint8_t* chunk, int lane, Tile& T) {
+  T.qa = ld_stream16(chunk + kQsA + 16 * lane);
+  T.qb = ld_stream16(chunk + kQsB + 16 * lane);
+  T.sg = ld_stream16(chunk + kSigns + 16 * lane);
+  T.qh = ld_stream4(chunk + kQh + 4 * lane);
+  const int g = lane >> 2;
+  T.ra = __ldg(reinterpret_cast<const uint2*>(chunk + kScales) + g);
+  T.rb = __ldg(reinterpret_cast<const uint2*>(chunk + kScales) + g + 8);
 }
 
-// One 32-weight sub-block of a repacked IQ3_S row as 8 signed int8x4 words
-// plus its scale d * (1 + 2 * nibble) (quant/dequant.py:164-185).
-struct SubBlock {
-  uint32_t q[8];
-  float db;
+// A tile's words for the current pair of sub-blocks; block_steps advances
+// it by two sub-blocks per step of a rolled loop, so the code of one step is
+// all that is live beside the tiles.
+struct Cursor {
+  uint4 qa, qb;              // .x: qs bytes of the current pair (byte 2s+h)
+  uint32_t s0a, s1a, s0b, s1b;  // sign words of rows g, g+8, shifted to the pair
+  uint32_t qh;               // bits 2s+h (row g), 16+2s+h (row g+8)
+  uint32_t sca, scb;         // scale nibbles of rows g, g+8 (nibble s)
+  float da, db;              // d of rows g, g+8
 };
 
-__device__ __forceinline__ void load_sub_block(const uint8_t* row, int sb, const uint32_t* lut, SubBlock& o) {
-  // `row` is a shared-memory copy; all loads are naturally aligned (blocks
-  // are 112 = 7 x 16 bytes)
-  const int b = sb >> 3, p = (sb & 7) >> 1, s = sb & 1;
-  const uint8_t* blk = row + b * kIq3sBlockBytes;
-  const uint64_t qs = *reinterpret_cast<const uint64_t*>(blk + 16 * p + 8 * s);
-  const uint32_t signs = *reinterpret_cast<const uint32_t*>(blk + 64 + 8 * p + 4 * s);
-  const uint64_t qh8 = *reinterpret_cast<const uint64_t*>(blk + 96);   // qh[0..7]
-  const uint64_t tail = *reinterpret_cast<const uint64_t*>(blk + 104); // scales[0..3], d, pad
-  const uint32_t qh = static_cast<uint32_t>(qh8 >> (8 * (2 * p + s))) & 255u;
-  const uint32_t nib = static_cast<uint32_t>(tail >> (8 * p + 4 * s)) & 15u;
-  o.db = __half2float(__ushort_as_half(static_cast<unsigned short>((tail >> 32) & 0xFFFFu))) *
-         static_cast<float>(1 + 2 * static_cast<int>(nib));
-#pragma unroll
-  for (int w = 0; w < 8; ++w) {
-    const uint32_t idx = static_cast<uint32_t>((qs >> (8 * w)) & 255u) | (((qh >> w) & 1u) << 8) |
-                         (((signs >> (4 * w)) & 15u) << 9);
-    o.q[w] = lut[idx];
-  }
+__device__ __forceinline__ Cursor cursor_of(const Tile& T) {
+  Cursor c;
+  c.qa = T.qa;
+  c.qb = T.qb;
+  c.s0a = T.sg.x;
+  c.s1a = T.sg.y;
+  c.s0b = T.sg.z;
+  c.s1b = T.sg.w;
+  c.qh = T.qh;
+  c.sca = T.ra.x;
+  c.scb = T.rb.x;
+  c.da = __half2float(__ushort_as_half(static_cast<unsigned short>(T.ra.y & 0xFFFFu)));
+  c.db = __half2float(__ushort_as_half(static_cast<unsigned short>(T.rb.y & 0xFFFFu)));
+  return c;
 }
 
-// q . X for vector slot v, sub-block sb (exact integer sums, one rounding)
-template <int SBR>
-__device__ __forceinline__ float sub_block_dot(const SubBlock& w, const uint8_t* xs, int v, int sb) {
-  const uint8_t* base = xs + v * XSmem<SBR>::kVecBytes;
-  const uint4 a0 = *reinterpret_cast<const uint4*>(base + 0 * XSmem<SBR>::kPlaneBytes + sb * 16);
-  const uint4 a1 = *reinterpret_cast<const uint4*>(base + 1 * XSmem<SBR>::kPlaneBytes + sb * 16);
-  const uint4 b0 = *reinterpret_cast<const uint4*>(base + 2 * XSmem<SBR>::kPlaneBytes + sb * 16);
-  const uint4 b1 = *reinterpret_cast<const uint4*>(base + 3 * XSmem<SBR>::kPlaneBytes + sb * 16);
-  const uint4 c0 = *reinterpret_cast<const uint4*>(base + 4 * XSmem<SBR>::kPlaneBytes + sb * 16);
-  const uint4 c1 = *reinterpret_cast<const uint4*>(base + 5 * XSmem<SBR>::kPlaneBytes + sb * 16);
-  const uint32_t d2[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
-  const uint32_t d1[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
-  const uint32_t d0[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
-  int s2 = 0, s1 = 0, s0 = 0;
-#pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    s2 = __dp4a(static_cast<int>(w.q[i]), static_cast<int>(d2[i]), s2);
-    s1 = __dp4a(static_cast<int>(w.q[i]), static_cast<int>(d1[i]), s1);
-    s0 = __dp4a(static_cast<int>(w.q[i]), static_cast<int>(d0[i]), s0);
-  }
-  const int t = s1 * 256 + s0;
-  return fmaf(static_cast<float>(s2), 65536.0f, static_cast<float>(t));
+__device__ __forceinline__ void cursor_next(Cursor& c) {
+  c.qa = make_uint4(c.qa.y, c.qa.z, c.qa.w, 0u);
+  c.qb = make_uint4(c.qb.y, c.qb.z, c.qb.w, 0u);
+  c.s0a <<= 4;
+  c.s1a <<= 4;
+  c.s0b <<= 4;
+  c.s1b <<= 4;
+  c.qh >>= 4;
+  c.sca >>= 8;
+  c.scb >>= 8;
 }
 
-// Dot of RW rows (row pointers) with the NV vectors in xs, mc of them live.
-// Lanes: LPR lanes per row (all 32 when the row has >= 32 sub-blocks).
-// Returns, in every lane, the totals of the lane's row group.
-template <int SBR, int NV, int RW>
-__device__ __forceinline__ void rows_dot(const uint8_t* const (&rows)[RW], const uint8_t* xs, const uint32_t* lut,
-                                         int mc, float (&res)[RW][NV]) {
-  static_assert(SBR >= 16, "rows of at least 512 weights");
-  constexpr int LPR = SBR >= 32 ? 32 : SBR;
-  constexpr int RPP = 32 / LPR;  // rows per pass
-  constexpr int SPL = SBR / LPR; // sub-blocks per lane per row
-  const int lane = threadIdx.x & 31;
-  const int rin = lane / LPR, lr = lane % LPR;
-#pragma unroll
-  for (int r0 = 0; r0 < RW; r0 += RPP) {
-    float acc[NV];
-#pragma unroll
-    for (int v = 0; v < NV; ++v) acc[v] = 0.f;
-    const uint8_t* row = rows[r0];
-    if (RPP > 1 && rin == 1 && r0 + 1 < RW) row = rows[r0 + 1];
-#pragma unroll
-    for (int i = 0; i < SPL; ++i) {
-      const int sb = lr + LPR * i;
-      SubBlock w;
-      load_sub_block(row, sb, lut, w);
-      const uint8_t* base = xs;
-#pragma unroll
-      for (int v = 0; v < NV; ++v) {
-        if (v < mc) {
-          const float sxv = reinterpret_cast<const float*>(base + v * XSmem<SBR>::kVecBytes +
-                                                           6 * XSmem<SBR>::kPlaneBytes)[sb];
-          acc[v] = fmaf(w.db * sxv, sub_block_dot<SBR>(w, xs, v, sb), acc[v]);
-        }
-      }
-    }
-#pragma unroll
-    for (int v = 0; v < NV; ++v) {
-#pragma unroll
-      for (int o = LPR / 2; o > 0; o >>= 1) acc[v] += __shfl_xor_sync(0xffffffffu, acc[v], o);
-    }
-    // lanes of pass row j (j < RPP) now hold that row's totals; gather all
-#pragma unroll
-    for (int j = 0; j < RPP; ++j)
-      if (r0 + j < RW)
-#pragma unroll
-        for (int v = 0; v < NV; ++v) res[r0 + j][v] = __shfl_sync(0xffffffffu, acc[v], j * LPR);
+// fp16 weights (w0, w1), (w2, w3) of group 2t+H of sub-block S (0/1 within
+// the current pair), row g (R = 0) or g+8.  `lut` is the codebook's shared
+// memory, `lane_off` this lane's copy offset (byte 0 of the word).
+template <int S, int R, int H>
+__device__ __forceinline__ uint2 tile_word(const Cursor& c, const uint8_t* lut, uint32_t lane_off) {
+  const uint32_t qw = R ? c.qb.x : c.qa.x;
+  // (qs byte << 8) | lane_off
+  constexpr uint32_t kSel = 4u | (static_cast<uint32_t>((S << 1) | H) << 4) | (5u << 8) | (5u << 12);
+  constexpr int QB = 16 * R + 2 * S + H;
+  const uint32_t hb = QB >= 7 ? (c.qh >> (QB - 7)) : (c.qh << (7 - QB));
+  const uint32_t off = prmt(qw, lane_off, kSel) | (hb & 0x80u);
+  uint2 w = *reinterpret_cast<const uint2*>(lut + off);
+  constexpr int SH = 2 * S + H;
+  w.x ^= ((R ? c.s0b : c.s0a) << SH) & 0x80008000u;
+  w.y ^= ((R ? c.s1b : c.s1a) << SH) & 0x80008000u;
+  return w;
+}
+
+template <int S>
+__device__ __forceinline__ float row_scale(uint32_t nibbles, float d) {
+  const uint32_t nib = (nibbles >> (4 * S)) & 15u;
+  return d * static_cast<float>(1 + 2 * static_cast<int>(nib));  // quant/dequant.py:164-185
+}
+
+__device__ __forceinline__ void mma_f16(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                        uint32_t b0, uint32_t b1) {
+  asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+      "{%0, %1, %2, %3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// acc[r] += db(row) * (hi + lo sums of sub-block S) for rows g (r = 0) and
+// g+8, token column pair t.  `b`: elements 8t..8t+7 of the sub-block of
+// this lane's B column (token g/2, plane g%2).
+template <int S>
+__device__ __forceinline__ void tile_step(const Cursor& c, const uint8_t* lut, uint32_t lane_off, const uint4& b,
+                                          float (&acc)[2]) {
+  const uint2 w00 = tile_word<S, 0, 0>(c, lut, lane_off), w10 = tile_word<S, 1, 0>(c, lut, lane_off);
+  const uint2 w01 = tile_word<S, 0, 1>(c, lut, lane_off), w11 = tile_word<S, 1, 1>(c, lut, lane_off);
+  float cc[4] = {0.f, 0.f, 0.f, 0.f};
+  mma_f16(cc, w00.x, w10.x, w00.y, w10.y, b.x, b.y);  // groups 2t: weights 8t .. 8t+3
+  mma_f16(cc, w01.x, w11.x, w01.y, w11.y, b.z, b.w);  // groups 2t+1: weights 8t+4 .. 8t+7
+  acc[0] = fmaf(row_scale<S>(c.sca, c.da), cc[0] + cc[1], acc[0]);
+  acc[1] = fmaf(row_scale<S>(c.scb, c.db), cc[2] + cc[3], acc[1]);
+}
+
+// All 8 sub-blocks of K-block `kb` for two tiles sharing the B operands,
+// two sub-blocks per step of a rolled loop.  `xl`: this lane's B column
+// base (token g/2, plane g%2, element 8t).
+__device__ __forceinline__ void block_steps(const Tile& ta, const Tile& tb, const uint8_t* lut, uint32_t lane_off,
+                                            const uint8_t* xl, int kb, float (&acc)[2][2]) {
+  Cursor ca = cursor_of(ta), cb = cursor_of(tb);
+  const uint8_t* xq = xl + kb * 512;  // 8 sub-blocks x 32 fp16
+#pragma unroll 1
+  for (int p = 0; p < 4; ++p) {
+    const uint4 b0 = *reinterpret_cast<const uint4*>(xq + 128 * p);
+    const uint4 b1 = *reinterpret_cast<const uint4*>(xq + 128 * p + 64);
+    tile_step<0>(ca, lut, lane_off, b0, acc[0]);
+    tile_step<0>(cb, lut, lane_off, b0, acc[1]);
+    tile_step<1>(ca, lut, lane_off, b1, acc[0]);
+    tile_step<1>(cb, lut, lane_off, b1, acc[1]);
+    cursor_next(ca);
+    cursor_next(cb);
   }
 }
 
@@ -385,13 +528,14 @@ __device__ __forceinline__ void cp_async16(void* smem_dst, const void* gsrc) {
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
 
-// Copy `bytes` (a multiple of 16) from global to shared memory, all threads.
-__device__ __forceinline__ void stage(uint8_t* dst, const uint8_t* src, int64_t bytes) {
-  for (int64_t i = threadIdx.x; i < bytes / 16; i += kThreads) cp_async16(dst + 16 * i, src + 16 * i);
+__device__ __forceinline__ void stage_lut(uint8_t* lut) {
+  const uint8_t* src = reinterpret_cast<const uint8_t*>(g_half_grid.v);
+  for (int i = threadIdx.x; i < kLutBytes / 16; i += kThreads) cp_async16(lut + 16 * i, src + 16 * i);
+  cp_async_commit();
 }
 
-// The expert slot a CTA serves: from the grouping kernel, or (one token,
-// whose top-k experts are distinct) straight from the routing ids.
+// The expert slot an item serves: from the prep kernel's sort, or (one
+// token, whose top-k experts are distinct) straight from the routing ids.
 struct Slot {
   int expert, start, count;
 };
@@ -404,7 +548,6 @@ __device__ __forceinline__ bool slot_of(int u, bool direct, const int32_t* ids, 
     s.count = 1;
     return s.expert >= 0 && s.expert < n_experts;
   }
-  if (u >= ws.hdr[0]) return false;
   s.expert = ws.slot_expert[u];
   s.start = ws.slot_start[u];
   s.count = ws.slot_count[u];
@@ -414,152 +557,218 @@ __device__ __forceinline__ bool slot_of(int u, bool direct, const int32_t* ids, 
 __device__ __forceinline__ int pair_of(bool direct, const MoeWs& ws, int i) { return direct ? i : ws.pairs[i]; }
 
 // ------------------------------------------------------------------ gate/up
-// CTA (u, c): expert slot u, outputs [16c, 16c + 16); warp w: outputs
-// 16c + 2w + [0, 2) (its 2 gate rows and 2 up rows).  The CTA's 32 rows are
-// copied into shared memory first (cp.async, all in flight at once); in
-// direct mode that copy starts before the dependency wait.  Pairs of the
-// slot in chunks of NV.
-template <int SBR, int NV>
-__global__ void __launch_bounds__(kThreads) moe_gate_up_kernel(const uint8_t* __restrict__ gate,
-                                                               const uint8_t* __restrict__ up,
-                                                               const float* __restrict__ x, const int32_t* ids,
-                                                               int n_experts, int direct, int top_k, int ffn,
-                                                               MoeWs ws) {
-  constexpr int K = SBR * 32;
-  constexpr int RB = K / 256 * kIq3sBlockBytes;
-  constexpr int WBYTES = 2 * kGateRowsPerCta * RB;
+// Items (slot u, chunk c): gate/up rows [OUT c, OUT c + OUT) of the slot's
+// expert, OUT = 16 * TP, TP = 16 / KB tile pairs.  Warp w: tile pair
+// tp = w % TP (gate rows + the same up rows) over K-block kb = w / TP.  The
+// K-blocks meet in shared memory; act = silu(g) * u (model/moe.py:229).
+template <int KB>
+__global__ void __launch_bounds__(kThreads, 1)
+    moe_gate_up_kernel(const uint8_t* __restrict__ gate, const uint8_t* __restrict__ up, const int32_t* ids,
+                       int n_experts, int direct, int top_k, int ffn, MoeWs ws) {
+  constexpr int K = KB * 256, TP = kWarps / KB, OUT = 16 * TP;
+  static_assert(kWarps % KB == 0, "K blocks per item");
   extern __shared__ __align__(16) uint8_t smem[];
-  uint8_t* wsm = smem;                 // [gate rows 32][up rows 32]
-  uint8_t* xs = smem + WBYTES;         // encoded vectors
-  __shared__ __align__(16) uint32_t lut[8192];
-  const int u = blockIdx.x, c = blockIdx.y;
-  stage(reinterpret_cast<uint8_t*>(lut), reinterpret_cast<const uint8_t*>(g_signed.v), sizeof(lut));
-  cp_async_commit();
+  uint8_t* lut = smem;
+  float* red = reinterpret_cast<float*>(smem + kLutBytes);
+  float* xsc = reinterpret_cast<float*>(smem + kLutBytes + kRedBytes);
+  uint8_t* xs = smem + kLutBytes + kRedBytes + kMiscBytes;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+  stage_lut(lut);
   // The op's inputs (ids, x) come from whatever ran before: read them only
   // after the wait, and let the down kernel start only then, so that it may
-  // read them before its own wait.
+  // read the slots before its own wait.
   pdl_wait();
   pdl_launch_dependents();
-  Slot sl{};
-  if (!slot_of(u, direct != 0, ids, n_experts, ws, sl)) return;
-  stage(wsm, gate + (static_cast<int64_t>(sl.expert) * ffn + c * kGateRowsPerCta) * RB, kGateRowsPerCta * RB);
-  stage(wsm + kGateRowsPerCta * RB, up + (static_cast<int64_t>(sl.expert) * ffn + c * kGateRowsPerCta) * RB,
-        kGateRowsPerCta * RB);
-  cp_async_commit();
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  constexpr int OPW = kGateRowsPerCta / kWarps;  // outputs per warp
-  const int o0 = c * kGateRowsPerCta + warp * OPW;
-  const uint8_t* rows[2 * OPW];
-#pragma unroll
-  for (int i = 0; i < OPW; ++i) {
-    rows[i] = wsm + (warp * OPW + i) * RB;
-    rows[OPW + i] = wsm + (kGateRowsPerCta + warp * OPW + i) * RB;
-  }
-  for (int c0 = 0; c0 < sl.count; c0 += NV) {
-    const int mc = min(NV, sl.count - c0);
-    __syncthreads();  // (previous chunk's readers done)
-    for (int v = 0; v < mc; ++v)
-      encode_vec<SBR>(x + static_cast<int64_t>(pair_of(direct != 0, ws, sl.start + c0 + v) / top_k) * K, xs, v);
-    cp_async_wait_all();
-    __syncthreads();
-    float res[2 * OPW][NV];
-    rows_dot<SBR, NV, 2 * OPW>(rows, xs, lut, mc, res);
-    if (lane < OPW) {
-#pragma unroll
-      for (int v = 0; v < NV; ++v) {
-        if (v < mc) {
-          // lane i writes output o0 + i (model/moe.py:229: act = silu(g) * u)
-          float g = 0.f, uu = 0.f;
-#pragma unroll
-          for (int i = 0; i < OPW; ++i)
-            if (i == lane) {
-              g = res[i][v];
-              uu = res[OPW + i][v];
-            }
-          ws.act[static_cast<int64_t>(pair_of(direct != 0, ws, sl.start + c0 + v)) * ffn + o0 + lane] = silu_f(g) * uu;
+  const int chunks = ffn / OUT;
+  const int n_items = (direct ? top_k : ws.hdr[0]) * chunks;
+  const int i0 = static_cast<int>(static_cast<int64_t>(blockIdx.x) * n_items / gridDim.x);
+  const int i1 = static_cast<int>(static_cast<int64_t>(blockIdx.x + 1) * n_items / gridDim.x);
+  const int tp = warp % TP, kb = warp / TP;
+  const uint32_t lane_off = static_cast<uint32_t>(lane & 15) * 8u;
+  const uint8_t* xl = xs + (g >> 1) * token_stride(K) + (g & 1) * plane_stride(K) + 16 * t;
+  auto load_item = [&](int it, Tile& tg, Tile& tu) {
+    const int u = it / chunks, c = it - u * chunks;
+    Slot s;
+    if (!slot_of(u, direct != 0, ids, n_experts, ws, s)) return;
+    const int64_t off = ((static_cast<int64_t>(s.expert) * (ffn / 16) + c * TP + tp) * KB + kb) * kChunkBytes;
+    load_tile(gate + off, lane, tg);
+    load_tile(up + off, lane, tu);
+  };
+  Tile tg{}, tu{}, ng{}, nu{};
+  if (i0 < i1) load_item(i0, tg, tu);
+  int staged = -1;  // (slot, first pair) whose tokens are in xs
+  for (int it = i0; it < i1; ++it) {
+    const int u = it / chunks, c = it - u * chunks;
+    Slot s;
+    const bool live = slot_of(u, direct != 0, ids, n_experts, ws, s);
+    if (it + 1 < i1) load_item(it + 1, ng, nu);
+    for (int c0 = 0; live && c0 < s.count; c0 += kTokensPerPass) {
+      const int mc = min(kTokensPerPass, s.count - c0);
+      if (c0 > 0) load_item(it, tg, tu);  // a later pass re-reads the tiles
+      if (u * 4096 + c0 != staged) {
+        __syncthreads();  // readers of xs are done
+        for (int i = threadIdx.x; i < mc * (K / 4); i += kThreads) {  // 16-byte pieces, K/8 per plane
+          const int v = i / (K / 4), j = i - v * (K / 4), plane = j / (K / 8), piece = j - plane * (K / 8);
+          const int tok = pair_of(direct != 0, ws, s.start + c0 + v) / top_k;
+          cp_async16(xs + v * token_stride(K) + plane * plane_stride(K) + 16 * piece,
+                     ws.xenc + static_cast<int64_t>(tok) * 4 * K + plane * 2 * K + 16 * piece);
         }
+        cp_async_commit();
+        if (threadIdx.x < mc) xsc[threadIdx.x] = ws.xscale[pair_of(direct != 0, ws, s.start + c0 + threadIdx.x) / top_k];
+        cp_async_wait_all();
+        __syncthreads();
+        staged = u * 4096 + c0;
       }
+      float acc[2][2] = {};
+      block_steps(tg, tu, lut, lane_off, xl, kb, acc);
+      reinterpret_cast<float4*>(red)[warp * 32 + lane] = make_float4(acc[0][0], acc[0][1], acc[1][0], acc[1][1]);
+      __syncthreads();
+      for (int i = threadIdx.x; i < OUT * mc; i += kThreads) {
+        const int v = i / OUT, o = i - v * OUT;
+        const int otp = o >> 4, r = o & 15, src = (r & 7) * 4 + v, reg = r >> 3;
+        float gs = 0.f, us = 0.f;
+#pragma unroll
+        for (int k = 0; k < KB; ++k) {
+          const float* rr = red + ((k * TP + otp) * 32 + src) * 4;
+          gs += rr[reg];
+          us += rr[2 + reg];
+        }
+        gs *= xsc[v];
+        us *= xsc[v];
+        const int pair = pair_of(direct != 0, ws, s.start + c0 + v);
+        ws.act[static_cast<int64_t>(pair) * ffn + c * OUT + o] = silu_f(gs) * us;
+      }
+      __syncthreads();  // red and xsc readers done
     }
+    tg = ng;
+    tu = nu;
   }
 }
 
 // ------------------------------------------------------------------ down
-// CTA (u, c): expert slot u, rows [64c, 64c + 64) staged into shared
-// memory before the dependency wait: the gate/up kernel lets this kernel
-// start only after its own wait, so the routing ids and the grouping
-// kernel's slots are complete by then; warp w: 8 rows.
-template <int SBR, int NV>
-__global__ void __launch_bounds__(kThreads) moe_down_kernel(const uint8_t* __restrict__ down, const int32_t* ids,
-                                                            const float* __restrict__ weights, float* out,
-                                                            int n_experts, int direct, int hidden, MoeWs ws,
-                                                            int ffn) {
-  constexpr int K = SBR * 32;
-  constexpr int RB = K / 256 * kIq3sBlockBytes;
-  constexpr int WBYTES = kDownRowsPerCta * RB;
+// Items (slot u, chunk c): rows [ROWS c, ROWS c + ROWS) of the slot's
+// expert, ROWS = 32 * TP, TP = 16 / KB tile pairs.  Warp w: tiles 2tp and
+// 2tp+1 (tp = w % TP) over K-block kb = w / TP.  The slots come from the
+// prep kernel, which completed before the gate/up kernel released this one,
+// so the first item's tiles are loaded before the dependency wait.  Each
+// pass encodes its pairs' act (f32, from the gate/up kernel) into fp16
+// planes in shared memory.
+template <int KB>
+__global__ void __launch_bounds__(kThreads, 1)
+    moe_down_kernel(const uint8_t* __restrict__ down, const int32_t* ids, const float* __restrict__ weights,
+                    float* out, int n_experts, int direct, int top_k, int hidden, MoeWs ws) {
+  constexpr int K = KB * 256, TP = kWarps / KB, ROWS = 32 * TP;
+  static_assert(kWarps % KB == 0, "K blocks per item");
   extern __shared__ __align__(16) uint8_t smem[];
-  uint8_t* wsm = smem;
-  uint8_t* xs = smem + WBYTES;
-  __shared__ __align__(16) uint32_t lut[8192];
-  const int u = blockIdx.x, c = blockIdx.y;
-  stage(reinterpret_cast<uint8_t*>(lut), reinterpret_cast<const uint8_t*>(g_signed.v), sizeof(lut));
-  cp_async_commit();
-  Slot sl{};
-  const bool live = slot_of(u, direct != 0, ids, n_experts, ws, sl);
-  if (live) {
-    stage(wsm, down + (static_cast<int64_t>(sl.expert) * hidden + c * kDownRowsPerCta) * RB, WBYTES);
-    cp_async_commit();
-  }
+  uint8_t* lut = smem;
+  float* red = reinterpret_cast<float*>(smem + kLutBytes);
+  float* xsc = reinterpret_cast<float*>(smem + kLutBytes + kRedBytes);
+  float* wmax = xsc + 16;
+  uint8_t* xs = smem + kLutBytes + kRedBytes + kMiscBytes;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+  stage_lut(lut);
+  const int chunks = hidden / ROWS;
+  const int n_items = (direct ? top_k : ws.hdr[0]) * chunks;
+  const int i0 = static_cast<int>(static_cast<int64_t>(blockIdx.x) * n_items / gridDim.x);
+  const int i1 = static_cast<int>(static_cast<int64_t>(blockIdx.x + 1) * n_items / gridDim.x);
+  const int tp = warp % TP, kb = warp / TP;
+  const uint32_t lane_off = static_cast<uint32_t>(lane & 15) * 8u;
+  const uint8_t* xl = xs + (g >> 1) * token_stride(K) + (g & 1) * plane_stride(K) + 16 * t;
+  auto load_item = [&](int it, Tile& ta, Tile& tb) {
+    const int u = it / chunks, c = it - u * chunks;
+    Slot s;
+    if (!slot_of(u, direct != 0, ids, n_experts, ws, s)) return;
+    const int64_t tile = static_cast<int64_t>(s.expert) * (hidden / 16) + c * 2 * TP + 2 * tp;
+    load_tile(down + (tile * KB + kb) * kChunkBytes, lane, ta);
+    load_tile(down + ((tile + 1) * KB + kb) * kChunkBytes, lane, tb);
+  };
+  Tile ta{}, tb{}, na{}, nb{};
+  if (i0 < i1) load_item(i0, ta, tb);
   pdl_launch_dependents();
   pdl_wait();
-  if (!live && !direct) return;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  constexpr int RW = kDownRowsPerCta / kWarps;
-  const int h0 = c * kDownRowsPerCta + warp * RW;
-  const uint8_t* rows[RW];
-#pragma unroll
-  for (int i = 0; i < RW; ++i) rows[i] = wsm + (warp * RW + i) * RB;
-  for (int c0 = 0; live && c0 < sl.count; c0 += NV) {
-    const int mc = min(NV, sl.count - c0);
-    __syncthreads();
-    for (int v = 0; v < mc; ++v)
-      encode_vec<SBR>(ws.act + static_cast<int64_t>(pair_of(direct != 0, ws, sl.start + c0 + v)) * ffn, xs, v);
-    cp_async_wait_all();
-    __syncthreads();
-    float res[RW][NV];
-    rows_dot<SBR, NV, RW>(rows, xs, lut, mc, res);
-#pragma unroll
-    for (int v = 0; v < NV; ++v) {
-      if (v < mc) {
-        float* dst = ws.dn + static_cast<int64_t>(pair_of(direct != 0, ws, sl.start + c0 + v)) * hidden + h0;
-#pragma unroll
-        for (int i = 0; i < RW; ++i)
-          if (lane == i) dst[i] = res[i][v];
-      }
-    }
-  }
-  if (!direct) return;
-  // one token: the last of the top_k CTAs of this row chunk sums the experts'
-  // rows in routing order (atomic ticket, re-armed for the next call)
   __shared__ int s_last;
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    __threadfence();
-    s_last = atomicAdd(ws.hdr + kTicketBase + c, 1) == static_cast<int>(gridDim.x) - 1;
-  }
-  __syncthreads();
-  if (!s_last) return;
-  __threadfence();
-  for (int r = threadIdx.x; r < kDownRowsPerCta; r += kThreads) {
-    const int hh = c * kDownRowsPerCta + r;
-    float acc = 0.f;
-    for (int k = 0; k < static_cast<int>(gridDim.x); ++k) {
-      const int e = ids[k];
-      if (e < 0 || e >= n_experts) continue;
-      acc = __fadd_rn(acc, __fmul_rn(__ldcg(ws.dn + static_cast<int64_t>(k) * hidden + hh), weights[k]));
+  int staged = -1;
+  for (int it = i0; it < i1; ++it) {
+    const int u = it / chunks, c = it - u * chunks;
+    Slot s;
+    const bool live = slot_of(u, direct != 0, ids, n_experts, ws, s);
+    if (it + 1 < i1) load_item(it + 1, na, nb);
+    for (int c0 = 0; live && c0 < s.count; c0 += kTokensPerPass) {
+      const int mc = min(kTokensPerPass, s.count - c0);
+      if (c0 > 0) load_item(it, ta, tb);
+      if (u * 4096 + c0 != staged) {
+        // act of pair slot v: threads [128 v, 128 v + 128) -> fp16 planes
+        const int v = threadIdx.x >> 7, j = threadIdx.x & 127;
+        constexpr int F4 = K / 4 / 128;  // float4 per thread
+        float4 h[F4];
+        float m = 0.f;
+        const float4* src = nullptr;
+        if (v < mc) src = reinterpret_cast<const float4*>(ws.act + static_cast<int64_t>(pair_of(direct != 0, ws, s.start + c0 + v)) * K);
+#pragma unroll
+        for (int i = 0; i < F4; ++i) {
+          h[i] = v < mc ? __ldcg(src + j + 128 * i) : make_float4(0.f, 0.f, 0.f, 0.f);
+          m = fmaxf(m, fmaxf(fmaxf(fabsf(h[i].x), fabsf(h[i].y)), fmaxf(fabsf(h[i].z), fabsf(h[i].w))));
+        }
+        m = warp_max(m);
+        __syncthreads();  // readers of xs, xsc and wmax are done
+        if (lane == 0) wmax[warp] = m;
+        __syncthreads();
+        m = fmaxf(fmaxf(wmax[4 * v], wmax[4 * v + 1]), fmaxf(wmax[4 * v + 2], wmax[4 * v + 3]));
+        float inv, sx;
+        vector_scale(m, inv, sx);
+        if (v < mc) {
+          uint8_t* dst = xs + v * token_stride(K);
+#pragma unroll
+          for (int i = 0; i < F4; ++i)
+            store_planes(h[i], inv, dst + 8 * (j + 128 * i), dst + plane_stride(K) + 8 * (j + 128 * i));
+          if (j == 0) xsc[v] = sx;
+        }
+        __syncthreads();
+        staged = u * 4096 + c0;
+      }
+      float acc[2][2] = {};
+      block_steps(ta, tb, lut, lane_off, xl, kb, acc);
+      reinterpret_cast<float4*>(red)[warp * 32 + lane] = make_float4(acc[0][0], acc[0][1], acc[1][0], acc[1][1]);
+      __syncthreads();
+      for (int i = threadIdx.x; i < ROWS * mc; i += kThreads) {
+        const int v = i / ROWS, o = i - v * ROWS;
+        const int otp = o >> 5, jt = (o >> 4) & 1, r = o & 15;
+        const int src = (r & 7) * 4 + v, reg = jt * 2 + (r >> 3);
+        float sum = 0.f;
+#pragma unroll
+        for (int k = 0; k < KB; ++k) sum += red[((k * TP + otp) * 32 + src) * 4 + reg];
+        const int pair = pair_of(direct != 0, ws, s.start + c0 + v);
+        ws.dn[static_cast<int64_t>(pair) * hidden + c * ROWS + o] = sum * xsc[v];
+      }
+      __syncthreads();
     }
-    out[hh] = acc;
+    if (direct) {
+      // one token: the last of the top_k items of this row chunk sums the
+      // experts' rows in routing order (atomic ticket, re-armed after)
+      if (threadIdx.x == 0) {
+        __threadfence();
+        s_last = atomicAdd(ws.hdr + kTicketBase + c, 1) == top_k - 1;
+      }
+      __syncthreads();
+      if (s_last) {
+        __threadfence();
+        for (int r = threadIdx.x; r < ROWS; r += kThreads) {
+          const int hh = c * ROWS + r;
+          float a = 0.f;
+          for (int k = 0; k < top_k; ++k) {
+            const int e = ids[k];
+            if (e < 0 || e >= n_experts) continue;
+            a = __fadd_rn(a, __fmul_rn(__ldcg(ws.dn + static_cast<int64_t>(k) * hidden + hh), weights[k]));
+          }
+          out[hh] = a;
+        }
+        if (threadIdx.x == 0) atomicExch(ws.hdr + kTicketBase + c, 0);
+      }
+      __syncthreads();  // s_last readers done
+    }
+    ta = na;
+    tb = nb;
   }
-  if (threadIdx.x == 0) atomicExch(ws.hdr + kTicketBase + c, 0);
 }
 
 // ------------------------------------------------------------------ combine
@@ -584,11 +793,6 @@ __global__ void moe_combine_kernel(const float* __restrict__ weights, const int3
   }
 }
 
-template <int SBR>
-constexpr int xs_bytes(int nv) {
-  return nv * XSmem<SBR>::kVecBytes;
-}
-
 template <typename Kern, typename... Args>
 cudaError_t launch_pdl(Kern kern, dim3 grid, size_t smem, cudaStream_t stream, Args... args) {
   cudaLaunchConfig_t cfg = {};
@@ -604,37 +808,43 @@ cudaError_t launch_pdl(Kern kern, dim3 grid, size_t smem, cudaStream_t stream, A
   return cudaLaunchKernelEx(&cfg, kern, args...);
 }
 
-template <int SBR_GU, int SBR_D, int NV>
+template <int KBG, int KBD>
 int launch_all(const uint8_t* gate, const uint8_t* up, const uint8_t* down, const float* x, int64_t t, int hidden,
                int ffn, int n_experts, const int32_t* ids, const float* weights, int top_k, float* out, MoeWs ws,
                cudaStream_t stream) {
   const int p = static_cast<int>(t * top_k);
   // one token selects top_k distinct experts: no grouping needed
   const int direct = t == 1 ? 1 : 0;
-  const int slots = direct ? top_k : (p < n_experts ? p : n_experts);
-  if (!direct) moe_group_kernel<<<1, 512, (2 * n_experts + p) * sizeof(int32_t), stream>>>(ids, p, n_experts, ws);
-  constexpr int gu_w = 2 * kGateRowsPerCta * (SBR_GU * 32 / 256) * kIq3sBlockBytes;
-  constexpr int d_w = kDownRowsPerCta * (SBR_D * 32 / 256) * kIq3sBlockBytes;
-  const size_t gu_smem = gu_w + xs_bytes<SBR_GU>(NV), d_smem = d_w + xs_bytes<SBR_D>(NV);
+  constexpr int kGuOut = 16 * (kWarps / KBG), kDnRows = 32 * (kWarps / KBD);
+  constexpr size_t gu_smem = kLutBytes + kRedBytes + kMiscBytes + kTokensPerPass * token_stride(KBG * 256);
+  constexpr size_t d_smem = kLutBytes + kRedBytes + kMiscBytes + kTokensPerPass * token_stride(KBD * 256);
   static int configured_device = -1;
   int dev = 0;
   cudaGetDevice(&dev);
   if (configured_device != dev) {
-    cudaError_t e = cudaFuncSetAttribute(moe_gate_up_kernel<SBR_GU, NV>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    cudaError_t e = cudaFuncSetAttribute(moe_gate_up_kernel<KBG>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          static_cast<int>(gu_smem));
     if (e == cudaSuccess)
-      e = cudaFuncSetAttribute(moe_down_kernel<SBR_D, NV>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+      e = cudaFuncSetAttribute(moe_down_kernel<KBD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                static_cast<int>(d_smem));
     if (e != cudaSuccess) return fail_cuda(e, "moe set smem");
     configured_device = dev;
   }
-  cudaError_t e = launch_pdl(moe_gate_up_kernel<SBR_GU, NV>, dim3(slots, ffn / kGateRowsPerCta), gu_smem, stream, gate,
-                             up, x, ids, n_experts, direct, top_k, ffn, ws);
+  // persistent grids: one CTA per SM, or one per item when there are fewer
+  const int sms = sm_count();
+  const int gu_grid = direct ? std::min(top_k * (ffn / kGuOut), sms) : sms;
+  const int d_grid = direct ? std::min(top_k * (hidden / kDnRows), sms) : sms;
+  const size_t prep_smem = direct ? 0 : (2 * n_experts + p) * sizeof(int32_t);
+  cudaError_t e = launch_pdl(moe_prep_kernel, dim3(direct ? 1 : 1 + static_cast<int>(t)), prep_smem, stream, ids, p,
+                             n_experts, direct, x, hidden, ws);
   if (e == cudaSuccess)
-    e = launch_pdl(moe_down_kernel<SBR_D, NV>, dim3(slots, hidden / kDownRowsPerCta), d_smem, stream, down, ids,
-                   weights, out, n_experts, direct, hidden, ws, ffn);
+    e = launch_pdl(moe_gate_up_kernel<KBG>, dim3(gu_grid), gu_smem, stream, gate, up, ids, n_experts, direct, top_k,
+                   ffn, ws);
+  if (e == cudaSuccess)
+    e = launch_pdl(moe_down_kernel<KBD>, dim3(d_grid), d_smem, stream, down, ids, weights, out, n_experts, direct,
+                   top_k, hidden, ws);
   const int64_t total = t * hidden;
-  const int blocks = static_cast<int>(std::min<int64_t>((total + 255) / 256, 4096));
+  const int blocks = static_cast<int>(std::min<int64_t>((total + kThreads - 1) / kThreads, 4096));
   if (e == cudaSuccess && !direct)
     e = launch_pdl(moe_combine_kernel, dim3(blocks), 0, stream, weights, ids, t, top_k, hidden, n_experts, ws, out);
   if (e == cudaSuccess) e = cudaGetLastError();
@@ -642,27 +852,18 @@ int launch_all(const uint8_t* gate, const uint8_t* up, const uint8_t* down, cons
   return BT_OK;
 }
 
-template <int SBR_GU, int SBR_D>
-int launch_nv(const uint8_t* gate, const uint8_t* up, const uint8_t* down, const float* x, int64_t t, int hidden,
-              int ffn, int n_experts, const int32_t* ids, const float* weights, int top_k, float* out, MoeWs ws,
-              cudaStream_t stream) {
-  // one token selects each expert once: a single vector per expert
-  if (t == 1)
-    return launch_all<SBR_GU, SBR_D, 1>(gate, up, down, x, t, hidden, ffn, n_experts, ids, weights, top_k, out, ws,
-                                        stream);
-  return launch_all<SBR_GU, SBR_D, 4>(gate, up, down, x, t, hidden, ffn, n_experts, ids, weights, top_k, out, ws,
-                                      stream);
-}
-
 }  // namespace
 
 int repack_iq3_s(const void* src, void* dst, int64_t rows, int64_t k, cudaStream_t stream) {
-  if (!src || !dst || rows < 0 || k <= 0 || k % 256) return fail(BT_ERR_INVALID, "repack_iq3_s: K must be a multiple of 256");
+  if (!src || !dst || rows < 0 || k <= 0 || k % 256)
+    return fail(BT_ERR_INVALID, "repack_iq3_s: K must be a multiple of 256");
+  if (rows % 16) return fail(BT_ERR_INVALID, "repack_iq3_s: rows must be a multiple of 16 (tiles of 16 rows)");
   if (reinterpret_cast<uintptr_t>(dst) & 15) return fail(BT_ERR_INVALID, "repack_iq3_s: dst must be 16-byte aligned");
-  const int64_t nb = rows * (k / 256);
-  if (nb == 0) return BT_OK;
-  const int blocks = static_cast<int>(std::min<int64_t>((nb + 255) / 256, 65535));
-  repack_iq3s_kernel<<<blocks, 256, 0, stream>>>(static_cast<const uint8_t*>(src), static_cast<uint8_t*>(dst), nb);
+  const int64_t chunks = rows / 16 * (k / 256);
+  if (chunks == 0) return BT_OK;
+  const int blocks = static_cast<int>(std::min<int64_t>((chunks * 32 + 255) / 256, 65535));
+  repack_iq3s_kernel<<<blocks, 256, 0, stream>>>(static_cast<const uint8_t*>(src), static_cast<uint8_t*>(dst), chunks,
+                                                 static_cast<int>(k / 256));
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return fail_cuda(e, "repack_iq3_s launch");
   return BT_OK;
@@ -685,7 +886,7 @@ int moe_route(const float* logits, int64_t t, int64_t n_experts, int top_k, int3
 int64_t moe_workspace_bytes(int64_t t, int64_t hidden, int64_t ffn, int64_t n_experts, int top_k) {
   (void)n_experts;
   if (t < 1 || top_k < 1) return 0;
-  return moe_ws_bytes(t * top_k, hidden, ffn);
+  return moe_ws_bytes(t, t * top_k, hidden, ffn);
 }
 
 int moe_experts_iq3s(const void* gate, const void* up, const void* down, const float* x, int64_t t, int64_t hidden,
@@ -693,24 +894,21 @@ int moe_experts_iq3s(const void* gate, const void* up, const void* down, const f
                      void* workspace, cudaStream_t stream) {
   if (!gate || !up || !down || !x || !ids || !weights || !out || !workspace)
     return fail(BT_ERR_INVALID, "moe_experts_iq3s: null pointer");
-  if (t < 1 || t * top_k > 4096 || top_k < 1 || n_experts < 1 || n_experts > 4096)
+  if (t < 1 || t * top_k > 4096 || top_k < 1 || top_k > 64 || n_experts < 1 || n_experts > 4096)
     return fail(BT_ERR_UNSUPPORTED, "moe_experts_iq3s serves T * top_k <= 4096 pairs over <= 4096 experts");
   if ((reinterpret_cast<uintptr_t>(gate) | reinterpret_cast<uintptr_t>(up) | reinterpret_cast<uintptr_t>(down) |
        reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(workspace)) & 15)
     return fail(BT_ERR_INVALID, "moe_experts_iq3s: weights, x and workspace must be 16-byte aligned");
-  if (ffn % kGateRowsPerCta || hidden % kDownRowsPerCta || hidden / kDownRowsPerCta > kHeaderBytes / 4 - kTicketBase)
-    return fail(BT_ERR_UNSUPPORTED, "moe_experts_iq3s: ffn must be a multiple of 16 and hidden of 64 (<= 7168)");
-  const MoeWs ws = moe_ws(workspace, t * top_k, hidden, ffn);
+  const MoeWs ws = moe_ws(workspace, t, t * top_k, hidden, ffn);
   const uint8_t* g = static_cast<const uint8_t*>(gate);
   const uint8_t* u = static_cast<const uint8_t*>(up);
   const uint8_t* d = static_cast<const uint8_t*>(down);
   const int h = static_cast<int>(hidden), f = static_cast<int>(ffn), ne = static_cast<int>(n_experts);
-  if (hidden == 2048 && ffn == 512) return launch_nv<64, 16>(g, u, d, x, t, h, f, ne, ids, weights, top_k, out, ws, stream);
-  if (hidden == 2048 && ffn == 768) return fail(BT_ERR_UNSUPPORTED, "moe_experts_iq3s: ffn must be a multiple of 256");
-  if (hidden == 1024 && ffn == 512) return launch_nv<32, 16>(g, u, d, x, t, h, f, ne, ids, weights, top_k, out, ws, stream);
-  if (hidden == 4096 && ffn == 1024) return launch_nv<128, 32>(g, u, d, x, t, h, f, ne, ids, weights, top_k, out, ws, stream);
-  if (hidden == 2048 && ffn == 1024) return launch_nv<64, 32>(g, u, d, x, t, h, f, ne, ids, weights, top_k, out, ws, stream);
-  return fail(BT_ERR_UNSUPPORTED, "moe_experts_iq3s serves (hidden, ffn) in {(1024,512), (2048,512), (2048,1024), (4096,1024)}");
+  const int k = top_k;
+  if (hidden == 2048 && ffn == 512) return launch_all<8, 2>(g, u, d, x, t, h, f, ne, ids, weights, k, out, ws, stream);
+  if (hidden == 1024 && ffn == 512) return launch_all<4, 2>(g, u, d, x, t, h, f, ne, ids, weights, k, out, ws, stream);
+  if (hidden == 2048 && ffn == 1024) return launch_all<8, 4>(g, u, d, x, t, h, f, ne, ids, weights, k, out, ws, stream);
+  return fail(BT_ERR_UNSUPPORTED, "moe_experts_iq3s serves (hidden, ffn) in {(1024,512), (2048,512), (2048,1024)}");
 }
 
 }  // namespace bt

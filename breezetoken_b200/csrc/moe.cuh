@@ -5,8 +5,9 @@
 
 namespace bt {
 
-// Repacked IQ3_S block: the GGUF block's fields (110 bytes) in an aligned
-// order, padded to 112 bytes: [qs 64][signs 32][qh 8][scales 4][d 2][pad 2].
+// Device IQ3_S layout: rows in tiles of 16; each 16-row x 256-weight tile
+// (16 GGUF blocks of 110 bytes) is a 1792-byte chunk arranged for the
+// m16n8k32 int8 MMA's A fragments (moe.cu), i.e. 112 bytes per row and block.
 constexpr int kIq3sBlockBytes = 112;
 
 inline int64_t iq3s_row_bytes(int64_t k) { return k / 256 * kIq3sBlockBytes; }

@@ -168,21 +168,35 @@ def bench_moe(tokens: int, iters: int) -> dict:
                      device="cuda")
     flush = torch.ones(256 << 20, dtype=torch.uint8, device="cuda")
     s = torch.cuda.Stream()
+
+    def flush_l2() -> None:
+        flush.sum(dtype=torch.int32)  # read 256 MB: afterwards L2 holds only clean lines
+
+    def call() -> None:
+        experts_forward(ex, x, r.expert_ids, r.weights, ws)
+
+    # launch-timed: events around each call, L2 flushed before it
     total = 0.0
     with torch.cuda.stream(s):
         for i in range(iters + 3):
-            flush.sum(dtype=torch.int32)  # read 256 MB: afterwards L2 holds only clean lines
+            flush_l2()
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             e0.record(s)
-            experts_forward(ex, x, r.expert_ids, r.weights, ws)
+            call()
             e1.record(s)
             e1.synchronize()
             if i >= 3:
                 total += e0.elapsed_time(e1) / 1e3
     sec = total / iters
+    # device time: (flush + call) and flush alone, each captured `iters` times
+    # in one CUDA graph (no host launch gaps)
+    both = _time_graph(lambda: (flush_l2(), call()), iters, s)
+    alone = _time_graph(flush_l2, iters, s)
+    gsec = both - alone
     nbytes = u * 1_351_680 + tokens * hidden * 8
-    return {"kernel": "moe_experts_iq3s", "tokens": tokens, "unique_experts": u, "us": sec * 1e6, "bytes": nbytes,
-            "gbs": nbytes / sec / 1e9, "l2": "flushed before each call (256 MB read)"}
+    return {"kernel": "moe_experts_iq3s", "tokens": tokens, "unique_experts": u, "us": sec * 1e6,
+            "us_graph": gsec * 1e6, "bytes": nbytes, "gbs": nbytes / sec / 1e9, "gbs_graph": nbytes / gsec / 1e9,
+            "l2": "flushed before each call (256 MB read)"}
 
 
 def trace_step(gguf: str, max_context: int, steps: int) -> str:

@@ -165,13 +165,15 @@ BT_API int bt_argmax(const float* x, int64_t rows, int64_t n, int32_t* out,
               void* workspace, void* stream);
 
 /* ------------------------------------------------------- MoE experts */
-/* Bytes of one IQ3_S row of K weights in the device layout (K % 256 == 0):
- * 112-byte blocks holding the GGUF block's fields in aligned order.       */
+/* Bytes per IQ3_S row of K weights in the device layout (K % 256 == 0):
+ * K / 256 * 112.  Rows are stored in tiles of 16; a tile's 16 GGUF blocks of
+ * one 256-weight column block form one 1792-byte chunk ordered for the
+ * integer tensor-core MMA (chunks of a tile contiguous, tiles in row order). */
 BT_API int64_t bt_iq3s_row_bytes(int64_t k);
 
 /* GGUF IQ3_S rows (110-byte blocks, quant/dequant.py:164-185) -> the device
- * layout; replaces the reference's per-step byte staging of the selected
- * experts (model/moe.py:64-120): the experts stay resident in HBM.        */
+ * layout (rows % 16 == 0); replaces the reference's per-step byte staging of
+ * the selected experts (model/moe.py:64-120): they stay resident in HBM.  */
 BT_API int bt_repack_iq3_s(const void* src, void* dst, int64_t rows, int64_t k,
                     void* stream);
 
@@ -191,6 +193,7 @@ BT_API int64_t bt_moe_workspace_bytes(int64_t t, int64_t hidden, int64_t ffn,
  * ids[t,k], with the IQ3_S experts decoded inside the GEMVs.  gate/up:
  * (n_experts * ffn) rows of K = hidden, down: (n_experts * hidden) rows of
  * K = ffn, all in the bt_repack_iq3_s layout.  x, out: (T, hidden) f32.
+ * (hidden, ffn) in {(1024, 512), (2048, 512), (2048, 1024)}.
  * Each selected expert is read once for all the tokens that selected it.
  * Pairs with an id outside [0, n_experts) contribute nothing.             */
 BT_API int bt_moe_experts_iq3s(const void* gate, const void* up, const void* down,

@@ -39,16 +39,52 @@ def layer(cuda):
     return m, ex
 
 
-def test_iq3s_repack_keeps_every_block(layer) -> None:
-    """The device layout holds the same weights: dequantising its blocks back
-    (through the GGUF-block dequant op, after undoing the field order)
-    matches the oracle's dequantisation bit for bit."""
+def pack_iq3s_tiles(raw: np.ndarray, rows: int, k: int) -> np.ndarray:
+    """The device layout of bt_repack_iq3_s, restated in numpy: per 16-row
+    tile and 256-weight block, a 1792-byte chunk of [qs of rows g (512 B),
+    qs of rows g+8 (512 B), sign words (512 B), qh words (128 B), per-row
+    scales + d (128 B)], lane L = 4g + t holding groups 2t, 2t+1 of every
+    sub-block (quant/dequant.py:164-185 field meanings); group q = 2s + h of
+    a lane's row has its weight-0/1 signs at bits 15 - q / 31 - q of sign
+    word S0 and its weight-2/3 signs at the same bits of S1."""
+    kb = k // 256
+    b = np.ascontiguousarray(raw).reshape(rows // 16, 2, 8, kb, 110)  # (tile, half r, g, block, byte)
+    qs = b[..., 2:66].reshape(rows // 16, 2, 8, kb, 8, 4, 2)  # (.., s, t, h)
+    qs = qs.transpose(0, 3, 1, 2, 5, 4, 6).reshape(rows // 16, kb, 2, 512)  # (tile, block, r, g t s h)
+    sg = b[..., 74:106].reshape(rows // 16, 2, 8, kb, 8, 4).astype(np.uint32)  # (.., s, t)
+    words = np.zeros((rows // 16, 2, 8, kb, 4, 2), np.uint32)  # (.., t, word S0 / S1)
+    for s in range(8):
+        for h in range(2):
+            nib = (sg[..., s, :] >> (4 * h)) & 15
+            q = 2 * s + h
+            for i in range(4):  # weight i of the group: word i // 2, bit 15 - q (+ 16 for odd i)
+                words[..., i >> 1] |= ((nib >> i) & 1) << (16 * (i & 1) + 15 - q)
+    signs = words.transpose(0, 3, 2, 4, 1, 5).reshape(rows // 16, kb, 32 * 4)  # (tile, block, g t r w)
+    qhb = b[..., 66:74].astype(np.uint32)  # (tile, r, g, block, s)
+    qh = np.zeros((rows // 16, kb, 8, 4), np.uint32)  # (tile, block, g, t)
+    for r in range(2):
+        for s in range(8):
+            for h in range(2):
+                for t in range(4):
+                    bit = (qhb[:, r, :, :, s] >> (2 * t + h)) & 1  # (tile, g, block)
+                    qh[:, :, :, t] |= bit.transpose(0, 2, 1) << (16 * r + 2 * s + h)
+    rec = np.concatenate([b[..., 106:110], b[..., 0:2], np.zeros(b.shape[:-1] + (2,), np.uint8)], -1)
+    rec = rec.transpose(0, 3, 1, 2, 4).reshape(rows // 16, kb, 128)  # (tile, block, row 0..15, 8 B)
+    chunk = np.concatenate([qs.reshape(rows // 16, kb, 1024), signs.view(np.uint8).reshape(rows // 16, kb, 512),
+                            qh.view(np.uint8).reshape(rows // 16, kb, 128), rec], -1)
+    return chunk.reshape(-1)
+
+
+def test_iq3s_repack_matches_layout(layer) -> None:
+    """The device layout holds the GGUF bytes exactly where the restated
+    packer puts them (every field of every block of the 16 experts)."""
     m, ex = layer
-    rb = int(N.load().bt_iq3s_row_bytes(m["hidden"]))
-    dev = ex.gate[: 4 * rb].view(-1, 112).cpu().numpy()
-    gguf_blocks = np.concatenate([dev[:, 108:110], dev[:, 0:64], dev[:, 96:104], dev[:, 64:96], dev[:, 104:108]], 1)
-    src = np.ascontiguousarray(m["gate"]).reshape(-1, 110)[: gguf_blocks.shape[0]]
-    assert (gguf_blocks == src).all()
+    for dev, raw, rows, k in ((ex.gate, m["gate"], 16 * m["ffn"], m["hidden"]),
+                              (ex.down, m["down"], 16 * m["hidden"], m["ffn"])):
+        want = pack_iq3s_tiles(raw, rows, k)
+        got = dev.cpu().numpy()
+        assert got.shape == want.shape
+        assert (got == want).all()
 
 
 def test_moe_experts_match_reference_golden(layer) -> None:
@@ -84,6 +120,26 @@ def test_moe_experts_batch_shares_experts(layer) -> None:
     for i in range(t):
         want = oracle_experts(x[i], gr, ur, dr, ids[i], ws[i], m["hidden"], m["ffn"])
         _close(got[i], want)
+
+
+def test_moe_experts_passes_of_eight_tokens(layer) -> None:
+    """20 tokens that all select expert 3 (and 7 others): the expert's 20
+    pairs take three 8-token MMA passes; every token matches the oracle."""
+    m, ex = layer
+    rng = np.random.default_rng(6)
+    t = 20
+    x = rng.standard_normal((t, m["hidden"])).astype(np.float32)
+    others = [e for e in range(16) if e != 3]
+    ids = np.array([[3] + [others[(i + j) % 15] for j in range(7)] for i in range(t)], np.int32)
+    ws = rng.random((t, 8)).astype(np.float32)
+    ws /= ws.sum(1, keepdims=True)
+    got = experts_forward(ex, torch.from_numpy(x).cuda(), torch.from_numpy(ids).cuda(),
+                          torch.from_numpy(ws).cuda()).cpu().numpy()
+    gr = np.ascontiguousarray(m["gate"]).reshape(16 * m["ffn"], -1)
+    ur = np.ascontiguousarray(m["up"]).reshape(16 * m["ffn"], -1)
+    dr = np.ascontiguousarray(m["down"]).reshape(16 * m["hidden"], -1)
+    for i in range(t):
+        _close(got[i], oracle_experts(x[i], gr, ur, dr, ids[i], ws[i], m["hidden"], m["ffn"]))
 
 
 def test_moe_route_matches_oracle(cuda) -> None:
