@@ -12,9 +12,10 @@
 // selected expert's weights are read once for all the tokens that chose it
 // (U unique experts: bytes = U * 1,351,680 at the 35B shape), and encodes
 // each token's activation once.  The gate/up and down kernels are persistent
-// (one 16-warp CTA per SM, each taking a contiguous range of (expert, row
-// chunk) items); every warp decodes two 16-row tiles of one 256-weight
-// column block per item and loads the next item's tiles while it computes.
+// (two 8-warp CTAs per SM, each taking a contiguous range of (expert, row
+// chunk) items, balanced by token passes); every warp decodes two 16-row
+// tiles of one 256-weight column block per item and loads the next item's
+// tiles while it computes.
 //
 // Weights: `bt_repack_iq3_s` stores each 16-row x 256-weight tile (16 GGUF
 // blocks) as one 1792-byte chunk laid out for the m16n8k16 MMA: lane (g, t)
@@ -94,13 +95,18 @@ __device__ const HalfGrid g_half_grid = make_half_grid();
 constexpr int kLutBytes = static_cast<int>(sizeof(HalfGrid));
 static_assert(kLutBytes == 64 * 1024, "codebook layout");
 
-constexpr int kThreads = 512;  // expert kernels: 16 warps
+constexpr int kThreads = 256;  // 8 warps; the expert kernels run two CTAs per SM
 constexpr int kWarps = kThreads / 32;
 constexpr float kWeightSumMin = 6.103515625e-5f;  // moe.py:24
 // Workspace header words [kTicketBase, kTicketBase + hidden / rows per item):
 // the one-token combine's arrival counters (zero between calls).
 constexpr int kTicketBase = 16;
 constexpr int kHeaderBytes = 512;
+// Item ranges of the expert kernels' CTAs (T > 1): gate/up at [0, 2G), down
+// at [kRangeDown, kRangeDown + 2G), G <= kMaxGrid.
+constexpr int kMaxGrid = 512;
+constexpr int kRangeDown = 2 * kMaxGrid;
+constexpr int kRangeBytes = 4 * 2 * kRangeDown;
 
 // Tile chunk: 16 rows x 256 weights.  Sections (lane L = 4 g + t, group
 // q = 2 s + h of the lane's 16 per row: sub-block s, weights 8t + 4h ..):
@@ -228,6 +234,7 @@ __global__ void moe_route_kernel(const float* __restrict__ logits, int64_t t, in
 // fp16 planes and scale; every pair's act and down output (f32).
 struct MoeWs {
   int32_t* hdr;
+  int32_t* ranges;  // per CTA [first item, end item)
   int32_t* slot_expert;
   int32_t* slot_start;
   int32_t* slot_count;
@@ -246,6 +253,8 @@ __host__ __device__ inline MoeWs moe_ws(void* base, int64_t t, int64_t p, int64_
   int64_t o = 0;
   w.hdr = reinterpret_cast<int32_t*>(b + o);
   o += kHeaderBytes;
+  w.ranges = reinterpret_cast<int32_t*>(b + o);
+  o += kRangeBytes;
   w.slot_expert = reinterpret_cast<int32_t*>(b + o);
   o += align256(4 * p);
   w.slot_start = reinterpret_cast<int32_t*>(b + o);
@@ -265,7 +274,7 @@ __host__ __device__ inline MoeWs moe_ws(void* base, int64_t t, int64_t p, int64_
 }
 
 inline int64_t moe_ws_bytes(int64_t t, int64_t p, int64_t hidden, int64_t ffn) {
-  return kHeaderBytes + 4 * align256(4 * p) + align256(4 * t * hidden) + align256(4 * t) + align256(4 * p * ffn) +
+  return kHeaderBytes + kRangeBytes + 4 * align256(4 * p) + align256(4 * t * hidden) + align256(4 * t) + align256(4 * p * ffn) +
          align256(4 * p * hidden);
 }
 
@@ -310,11 +319,28 @@ __device__ __forceinline__ float cta_max(float v, float* red) {
 }
 
 // ------------------------------------------------------------------ prep
+// The first item of a CTA whose share of the work starts at cost w: items
+// (u, c) of slot u cost passes(u) = cum[u + 1] - cum[u] each and are
+// ordered by (u, c); an item belongs to the CTA its start cost falls in.
+__device__ __forceinline__ int item_at(const int32_t* cum, int n_slots, int chunks, int64_t w) {
+  if (w >= static_cast<int64_t>(cum[n_slots]) * chunks) return n_slots * chunks;
+  int lo = 0, hi = n_slots - 1;  // last slot with cum[u] * chunks <= w
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (static_cast<int64_t>(cum[mid]) * chunks <= w) lo = mid; else hi = mid - 1;
+  }
+  const int64_t rem = w - static_cast<int64_t>(cum[lo]) * chunks;
+  const int pu = cum[lo + 1] - cum[lo];
+  return lo * chunks + static_cast<int>((rem + pu - 1) / pu);
+}
+
 // Block 0 (T > 1): counting sort of the P pairs by expert id (stable) into
-// slots.  The other blocks: encode token (block - 1) (T == 1: token 0).
+// slots, and each expert-kernel CTA's contiguous item range, balanced by
+// token passes.  The other blocks: encode token (block - 1) (T == 1: token 0).
 __global__ void __launch_bounds__(kThreads) moe_prep_kernel(const int32_t* __restrict__ ids, int p_total,
                                                             int n_experts, int direct, const float* __restrict__ x,
-                                                            int hidden, MoeWs ws) {
+                                                            int hidden, MoeWs ws, int gu_grid, int gu_chunks,
+                                                            int d_grid, int d_chunks) {
   pdl_wait();
   pdl_launch_dependents();
   if (direct || blockIdx.x > 0) {
@@ -338,8 +364,9 @@ __global__ void __launch_bounds__(kThreads) moe_prep_kernel(const int32_t* __res
   extern __shared__ int32_t sm[];
   int32_t* cnt = sm;               // [n_experts]
   int32_t* off = sm + n_experts;   // [n_experts] exclusive prefix of counts
-  int32_t* sid = off + n_experts;  // [p_total] the ids
-  __shared__ int32_t s_bad;
+  int32_t* cum = off + n_experts;  // [n_experts + 1] prefix of the slots' passes
+  int32_t* sid = cum + n_experts + 1;  // [p_total] the ids
+  __shared__ int32_t s_bad, s_slots;
   for (int e = threadIdx.x; e < n_experts; e += blockDim.x) cnt[e] = 0;
   for (int q = threadIdx.x; q < p_total; q += blockDim.x) sid[q] = ids[q];
   if (threadIdx.x == 0) s_bad = 0;
@@ -354,20 +381,34 @@ __global__ void __launch_bounds__(kThreads) moe_prep_kernel(const int32_t* __res
   __syncthreads();
   if (threadIdx.x == 0) {
     int o = 0, u = 0;
+    cum[0] = 0;
     for (int e = 0; e < n_experts; ++e) {
       off[e] = o;
       if (cnt[e]) {
         ws.slot_expert[u] = e;
         ws.slot_start[u] = o;
         ws.slot_count[u] = cnt[e];
+        cum[u + 1] = cum[u] + (cnt[e] + kTokensPerPass - 1) / kTokensPerPass;
         ++u;
       }
       o += cnt[e];
     }
     ws.hdr[0] = u;
     ws.hdr[1] = s_bad;
+    s_slots = u;
   }
   __syncthreads();
+  const int n_slots = s_slots;
+  for (int b = threadIdx.x; b < gu_grid; b += blockDim.x) {
+    const int64_t w = static_cast<int64_t>(cum[n_slots]) * gu_chunks;
+    ws.ranges[2 * b] = item_at(cum, n_slots, gu_chunks, b * w / gu_grid);
+    ws.ranges[2 * b + 1] = item_at(cum, n_slots, gu_chunks, (b + 1) * w / gu_grid);
+  }
+  for (int b = threadIdx.x; b < d_grid; b += blockDim.x) {
+    const int64_t w = static_cast<int64_t>(cum[n_slots]) * d_chunks;
+    ws.ranges[kRangeDown + 2 * b] = item_at(cum, n_slots, d_chunks, b * w / d_grid);
+    ws.ranges[kRangeDown + 2 * b + 1] = item_at(cum, n_slots, d_chunks, (b + 1) * w / d_grid);
+  }
   for (int q = threadIdx.x; q < p_total; q += blockDim.x) {
     const int e = sid[q];
     if (e < 0 || e >= n_experts) continue;
@@ -558,11 +599,11 @@ __device__ __forceinline__ int pair_of(bool direct, const MoeWs& ws, int i) { re
 
 // ------------------------------------------------------------------ gate/up
 // Items (slot u, chunk c): gate/up rows [OUT c, OUT c + OUT) of the slot's
-// expert, OUT = 16 * TP, TP = 16 / KB tile pairs.  Warp w: tile pair
+// expert, OUT = 16 * TP, TP = 8 / KB tile pairs.  Warp w: tile pair
 // tp = w % TP (gate rows + the same up rows) over K-block kb = w / TP.  The
 // K-blocks meet in shared memory; act = silu(g) * u (model/moe.py:229).
 template <int KB>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kThreads, 2)
     moe_gate_up_kernel(const uint8_t* __restrict__ gate, const uint8_t* __restrict__ up, const int32_t* ids,
                        int n_experts, int direct, int top_k, int ffn, MoeWs ws) {
   constexpr int K = KB * 256, TP = kWarps / KB, OUT = 16 * TP;
@@ -580,9 +621,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   pdl_wait();
   pdl_launch_dependents();
   const int chunks = ffn / OUT;
-  const int n_items = (direct ? top_k : ws.hdr[0]) * chunks;
-  const int i0 = static_cast<int>(static_cast<int64_t>(blockIdx.x) * n_items / gridDim.x);
-  const int i1 = static_cast<int>(static_cast<int64_t>(blockIdx.x + 1) * n_items / gridDim.x);
+  const int i0 = direct ? blockIdx.x * top_k * chunks / gridDim.x : ws.ranges[2 * blockIdx.x];
+  const int i1 = direct ? (blockIdx.x + 1) * top_k * chunks / gridDim.x : ws.ranges[2 * blockIdx.x + 1];
   const int tp = warp % TP, kb = warp / TP;
   const uint32_t lane_off = static_cast<uint32_t>(lane & 15) * 8u;
   const uint8_t* xl = xs + (g >> 1) * token_stride(K) + (g & 1) * plane_stride(K) + 16 * t;
@@ -647,14 +687,14 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 // ------------------------------------------------------------------ down
 // Items (slot u, chunk c): rows [ROWS c, ROWS c + ROWS) of the slot's
-// expert, ROWS = 32 * TP, TP = 16 / KB tile pairs.  Warp w: tiles 2tp and
+// expert, ROWS = 32 * TP, TP = 8 / KB tile pairs.  Warp w: tiles 2tp and
 // 2tp+1 (tp = w % TP) over K-block kb = w / TP.  The slots come from the
 // prep kernel, which completed before the gate/up kernel released this one,
 // so the first item's tiles are loaded before the dependency wait.  Each
 // pass encodes its pairs' act (f32, from the gate/up kernel) into fp16
 // planes in shared memory.
 template <int KB>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kThreads, 2)
     moe_down_kernel(const uint8_t* __restrict__ down, const int32_t* ids, const float* __restrict__ weights,
                     float* out, int n_experts, int direct, int top_k, int hidden, MoeWs ws) {
   constexpr int K = KB * 256, TP = kWarps / KB, ROWS = 32 * TP;
@@ -668,9 +708,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
   stage_lut(lut);
   const int chunks = hidden / ROWS;
-  const int n_items = (direct ? top_k : ws.hdr[0]) * chunks;
-  const int i0 = static_cast<int>(static_cast<int64_t>(blockIdx.x) * n_items / gridDim.x);
-  const int i1 = static_cast<int>(static_cast<int64_t>(blockIdx.x + 1) * n_items / gridDim.x);
+  const int i0 = direct ? blockIdx.x * top_k * chunks / gridDim.x : ws.ranges[kRangeDown + 2 * blockIdx.x];
+  const int i1 = direct ? (blockIdx.x + 1) * top_k * chunks / gridDim.x : ws.ranges[kRangeDown + 2 * blockIdx.x + 1];
   const int tp = warp % TP, kb = warp / TP;
   const uint32_t lane_off = static_cast<uint32_t>(lane & 15) * 8u;
   const uint8_t* xl = xs + (g >> 1) * token_stride(K) + (g & 1) * plane_stride(K) + 16 * t;
@@ -697,30 +736,32 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int mc = min(kTokensPerPass, s.count - c0);
       if (c0 > 0) load_item(it, ta, tb);
       if (u * 4096 + c0 != staged) {
-        // act of pair slot v: threads [128 v, 128 v + 128) -> fp16 planes
-        const int v = threadIdx.x >> 7, j = threadIdx.x & 127;
-        constexpr int F4 = K / 4 / 128;  // float4 per thread
+        // act of pair slot v: threads [64 v, 64 v + 64) (warps 2v, 2v+1) -> fp16 planes
+        const int v = threadIdx.x >> 6, j = threadIdx.x & 63;
+        constexpr int F4 = K / 4 / 64;  // float4 per thread
         float4 h[F4];
         float m = 0.f;
         const float4* src = nullptr;
-        if (v < mc) src = reinterpret_cast<const float4*>(ws.act + static_cast<int64_t>(pair_of(direct != 0, ws, s.start + c0 + v)) * K);
+        if (v < mc)
+          src = reinterpret_cast<const float4*>(ws.act +
+                                                static_cast<int64_t>(pair_of(direct != 0, ws, s.start + c0 + v)) * K);
 #pragma unroll
         for (int i = 0; i < F4; ++i) {
-          h[i] = v < mc ? __ldcg(src + j + 128 * i) : make_float4(0.f, 0.f, 0.f, 0.f);
+          h[i] = v < mc ? __ldcg(src + j + 64 * i) : make_float4(0.f, 0.f, 0.f, 0.f);
           m = fmaxf(m, fmaxf(fmaxf(fabsf(h[i].x), fabsf(h[i].y)), fmaxf(fabsf(h[i].z), fabsf(h[i].w))));
         }
         m = warp_max(m);
         __syncthreads();  // readers of xs, xsc and wmax are done
         if (lane == 0) wmax[warp] = m;
         __syncthreads();
-        m = fmaxf(fmaxf(wmax[4 * v], wmax[4 * v + 1]), fmaxf(wmax[4 * v + 2], wmax[4 * v + 3]));
+        m = fmaxf(wmax[2 * v], wmax[2 * v + 1]);
         float inv, sx;
         vector_scale(m, inv, sx);
         if (v < mc) {
           uint8_t* dst = xs + v * token_stride(K);
 #pragma unroll
           for (int i = 0; i < F4; ++i)
-            store_planes(h[i], inv, dst + 8 * (j + 128 * i), dst + plane_stride(K) + 8 * (j + 128 * i));
+            store_planes(h[i], inv, dst + 8 * (j + 64 * i), dst + plane_stride(K) + 8 * (j + 64 * i));
           if (j == 0) xsc[v] = sx;
         }
         __syncthreads();
@@ -816,6 +857,7 @@ int launch_all(const uint8_t* gate, const uint8_t* up, const uint8_t* down, cons
   // one token selects top_k distinct experts: no grouping needed
   const int direct = t == 1 ? 1 : 0;
   constexpr int kGuOut = 16 * (kWarps / KBG), kDnRows = 32 * (kWarps / KBD);
+  static_assert(kWarps % KBG == 0 && kWarps % KBD == 0, "K blocks per item");
   constexpr size_t gu_smem = kLutBytes + kRedBytes + kMiscBytes + kTokensPerPass * token_stride(KBG * 256);
   constexpr size_t d_smem = kLutBytes + kRedBytes + kMiscBytes + kTokensPerPass * token_stride(KBD * 256);
   static int configured_device = -1;
@@ -830,13 +872,15 @@ int launch_all(const uint8_t* gate, const uint8_t* up, const uint8_t* down, cons
     if (e != cudaSuccess) return fail_cuda(e, "moe set smem");
     configured_device = dev;
   }
-  // persistent grids: one CTA per SM, or one per item when there are fewer
-  const int sms = sm_count();
-  const int gu_grid = direct ? std::min(top_k * (ffn / kGuOut), sms) : sms;
-  const int d_grid = direct ? std::min(top_k * (hidden / kDnRows), sms) : sms;
-  const size_t prep_smem = direct ? 0 : (2 * n_experts + p) * sizeof(int32_t);
+  // persistent grids: two CTAs per SM, or one per item when there are fewer
+  const int slots_max = std::min(2 * sm_count(), kMaxGrid);
+  const int gu_chunks = ffn / kGuOut, d_chunks = hidden / kDnRows;
+  const int gu_grid = direct ? std::min(top_k * gu_chunks, slots_max) : slots_max;
+  const int d_grid = direct ? std::min(top_k * d_chunks, slots_max) : slots_max;
+  const size_t prep_smem = direct ? 0 : (3 * n_experts + 1 + p) * sizeof(int32_t);
+  if (prep_smem > 48 * 1024) return fail(BT_ERR_UNSUPPORTED, "moe_experts_iq3s: too many experts + pairs");
   cudaError_t e = launch_pdl(moe_prep_kernel, dim3(direct ? 1 : 1 + static_cast<int>(t)), prep_smem, stream, ids, p,
-                             n_experts, direct, x, hidden, ws);
+                             n_experts, direct, x, hidden, ws, gu_grid, gu_chunks, d_grid, d_chunks);
   if (e == cudaSuccess)
     e = launch_pdl(moe_gate_up_kernel<KBG>, dim3(gu_grid), gu_smem, stream, gate, up, ids, n_experts, direct, top_k,
                    ffn, ws);
