@@ -43,6 +43,11 @@ class B200Error(RuntimeError):
         self.code = code
 
 
+class BtMoeShared(C.Structure):
+    _fields_ = [("gate", C.c_void_p), ("up", C.c_void_p), ("down", C.c_void_p), ("gate_inp", C.c_void_p),
+                ("ffn", C.c_int64)]
+
+
 class BtQwen35Dims(C.Structure):
     _fields_ = [
         (n, C.c_int32)
@@ -131,6 +136,11 @@ _SIGS: dict[str, tuple[object, list]] = {
     "bt_moe_experts_iq3s": (
         C.c_int,
         [_P, _P, _P, _P, _I64, _I64, _I64, _I64, _P, _P, C.c_int, _P, _P, _P],
+    ),
+    "bt_moe_layer_workspace_bytes": (_I64, [_I64, _I64, _I64, _I64, _I64, C.c_int]),
+    "bt_moe_layer_iq3s": (
+        C.c_int,
+        [_P, _P, _P, C.POINTER(BtMoeShared), _P, _I64, _I64, _I64, _I64, _P, _P, C.c_int, _P, _P, _P],
     ),
     "bt_argmax": (C.c_int, [_P, _I64, _I64, _P, _P, _P]),
     "bt_qwen35_kernels_per_step": (C.c_int, [C.POINTER(BtQwen35Model)]),

@@ -98,14 +98,30 @@ int bt_moe_route(const float* logits, int64_t t, int64_t n_experts, int top_k, i
 }
 
 int64_t bt_moe_workspace_bytes(int64_t t, int64_t hidden, int64_t ffn, int64_t n_experts, int top_k) {
-  return bt::moe_workspace_bytes(t, hidden, ffn, n_experts, top_k);
+  return bt::moe_workspace_bytes(t, hidden, ffn, 0, n_experts, top_k);
 }
 
 int bt_moe_experts_iq3s(const void* gate, const void* up, const void* down, const float* x, int64_t t,
                         int64_t hidden, int64_t ffn, int64_t n_experts, const int32_t* ids, const float* weights,
                         int top_k, float* out, void* workspace, void* stream) {
-  return bt::moe_experts_iq3s(gate, up, down, x, t, hidden, ffn, n_experts, ids, weights, top_k, out, workspace,
-                              as_stream(stream));
+  return bt::moe_layer_iq3s(gate, up, down, nullptr, x, t, hidden, ffn, n_experts, ids, weights, top_k, out,
+                            workspace, as_stream(stream));
+}
+
+int64_t bt_moe_layer_workspace_bytes(int64_t t, int64_t hidden, int64_t ffn, int64_t shared_ffn, int64_t n_experts,
+                                     int top_k) {
+  return bt::moe_workspace_bytes(t, hidden, ffn, shared_ffn, n_experts, top_k);
+}
+
+int bt_moe_layer_iq3s(const void* gate, const void* up, const void* down, const BtMoeShared* shared, const float* x,
+                      int64_t t, int64_t hidden, int64_t ffn, int64_t n_experts, const int32_t* ids,
+                      const float* weights, int top_k, float* out, void* workspace, void* stream) {
+  if (!shared)
+    return bt::moe_layer_iq3s(gate, up, down, nullptr, x, t, hidden, ffn, n_experts, ids, weights, top_k, out,
+                              workspace, as_stream(stream));
+  const bt::MoeShared sh{shared->gate, shared->up, shared->down, shared->gate_inp, shared->ffn};
+  return bt::moe_layer_iq3s(gate, up, down, &sh, x, t, hidden, ffn, n_experts, ids, weights, top_k, out, workspace,
+                            as_stream(stream));
 }
 
 int bt_linear_q8(const void* w, const float* x, float* y, int64_t n, int64_t k, int n_vec, void* stream) {

@@ -34,6 +34,7 @@
 // hi and lo planes, so one MMA pair serves 4 tokens and a lane's C fragment
 // holds both planes of its token.  Products are exact and accumulate in f32;
 // per sub-block the rows' scales d * (1 + 2 * nibble) multiply the sums.
+#include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
 #include <algorithm>
@@ -243,11 +244,16 @@ struct MoeWs {
   float* xscale;  // (T): x = (hi + lo) * xscale
   float* act;     // (P, ffn)
   float* dn;      // (P, hidden)
+  // shared expert (model/qwen36_moe.py:634-642), when the layer has one
+  uint16_t* ab;   // (T, 3, shared ffn) bf16 planes of the shared act
+  float* sgate;   // (T): sigmoid(x . gate_inp)
+  float* sout;    // (T, hidden): shared down output
 };
 
 __host__ __device__ inline int64_t align256(int64_t b) { return (b + 255) / 256 * 256; }
 
-__host__ __device__ inline MoeWs moe_ws(void* base, int64_t t, int64_t p, int64_t hidden, int64_t ffn) {
+__host__ __device__ inline MoeWs moe_ws(void* base, int64_t t, int64_t p, int64_t hidden, int64_t ffn,
+                                        int64_t sffn) {
   uint8_t* b = static_cast<uint8_t*>(base);
   MoeWs w;
   int64_t o = 0;
@@ -270,12 +276,19 @@ __host__ __device__ inline MoeWs moe_ws(void* base, int64_t t, int64_t p, int64_
   w.act = reinterpret_cast<float*>(b + o);
   o += align256(4 * p * ffn);
   w.dn = reinterpret_cast<float*>(b + o);
+  o += align256(4 * p * hidden);
+  w.ab = reinterpret_cast<uint16_t*>(b + o);
+  o += align256(6 * t * sffn);
+  w.sgate = reinterpret_cast<float*>(b + o);
+  o += align256(4 * t * (sffn > 0));
+  w.sout = reinterpret_cast<float*>(b + o);
   return w;
 }
 
-inline int64_t moe_ws_bytes(int64_t t, int64_t p, int64_t hidden, int64_t ffn) {
-  return kHeaderBytes + kRangeBytes + 4 * align256(4 * p) + align256(4 * t * hidden) + align256(4 * t) + align256(4 * p * ffn) +
-         align256(4 * p * hidden);
+inline int64_t moe_ws_bytes(int64_t t, int64_t p, int64_t hidden, int64_t ffn, int64_t sffn) {
+  const int64_t shared = sffn > 0 ? align256(6 * t * sffn) + align256(4 * t) + align256(4 * t * hidden) : 0;
+  return kHeaderBytes + kRangeBytes + 4 * align256(4 * p) + align256(4 * t * hidden) + align256(4 * t) +
+         align256(4 * p * ffn) + align256(4 * p * hidden) + shared;
 }
 
 // ------------------------------------------------------------------ encode
@@ -308,6 +321,18 @@ __device__ __forceinline__ void store_planes(const float4& h, float inv, uint8_t
                                                  __half_as_ushort(b[2]) | (__half_as_ushort(b[3]) << 16));
 }
 
+// x = hi + mid + lo in bf16: each remainder is exact in f32, so the three
+// planes hold x to its 24 bits.
+__device__ __forceinline__ void split3_bf16(float x, uint16_t& hi, uint16_t& mid, uint16_t& lo) {
+  const __nv_bfloat16 h = __float2bfloat16_rn(x);
+  const float r1 = x - __bfloat162float(h);
+  const __nv_bfloat16 m = __float2bfloat16_rn(r1);
+  const float r2 = r1 - __bfloat162float(m);
+  hi = __bfloat16_as_ushort(h);
+  mid = __bfloat16_as_ushort(m);
+  lo = __bfloat16_as_ushort(__float2bfloat16_rn(r2));
+}
+
 // Max over the CTA (all threads call it; `red` holds kWarps floats).
 __device__ __forceinline__ float cta_max(float v, float* red) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -316,6 +341,162 @@ __device__ __forceinline__ float cta_max(float v, float* red) {
   if (lane == 0) red[warp] = v;
   __syncthreads();
   return warp_max(lane < kWarps ? red[lane] : 0.f);
+}
+
+// ------------------------------------------------------------------ shared expert
+// model/qwen36_moe.py:634-642: shared = down(silu(gate x) * up x), scaled by
+// sigmoid(x . gate_inp) and added to the routed output.  bf16 weight rows
+// (GGUF (out, in) orientation) are the A fragments of m16n8k16 bf16 MMAs
+// as loaded (16 bytes per lane: weights 8t .. 8t+7 of a 32-column step, the
+// k order permuted identically on both operands); x (and act) are three
+// bf16 planes whose MMAs accumulate into the same f32 sums, so the products
+// carry x to 24 bits.  8 tokens per pass (MMA columns).
+__device__ __forceinline__ void mma_bf16(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                         uint32_t b0, uint32_t b1) {
+  asm("mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+      "{%0, %1, %2, %3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// c += rows (ra: row g, rb: row g+8; 8 bf16 each) x the 3 planes of the
+// lane's B column (8 bf16 each): 32 columns of K.
+__device__ __forceinline__ void bf16_step(float (&c)[4], const uint4& ra, const uint4& rb, const uint4 (&b)[3]) {
+#pragma unroll
+  for (int p = 0; p < 3; ++p) {
+    mma_bf16(c, ra.x, rb.x, ra.y, rb.y, b[p].x, b[p].y);
+    mma_bf16(c, ra.z, rb.z, ra.w, rb.w, b[p].z, b[p].w);
+  }
+}
+
+// Planes of token `tok` (< t, else zeros) at column `col` of a K-row.
+__device__ __forceinline__ void load_planes(const uint16_t* planes, int64_t tok, int t_total, int k, int col,
+                                            uint4 (&b)[3]) {
+#pragma unroll
+  for (int p = 0; p < 3; ++p)
+    b[p] = tok < t_total ? __ldcg(reinterpret_cast<const uint4*>(planes + (tok * 3 + p) * k + col))
+                         : make_uint4(0u, 0u, 0u, 0u);
+}
+
+// The same from f32 values: x[col .. col + 8) of token `tok`, split here.
+__device__ __forceinline__ void split_planes(const float* x, int64_t tok, int t_total, int k, int col,
+                                             uint4 (&b)[3]) {
+  float v[8];
+  if (tok < t_total) {
+    const float4 a = __ldcg(reinterpret_cast<const float4*>(x + tok * k + col));
+    const float4 c = __ldcg(reinterpret_cast<const float4*>(x + tok * k + col + 4));
+    v[0] = a.x, v[1] = a.y, v[2] = a.z, v[3] = a.w, v[4] = c.x, v[5] = c.y, v[6] = c.z, v[7] = c.w;
+  } else {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v[i] = 0.f;
+  }
+  uint32_t w[3][4];
+#pragma unroll
+  for (int i = 0; i < 8; i += 2) {
+    uint16_t h0, m0, l0, h1, m1, l1;
+    split3_bf16(v[i], h0, m0, l0);
+    split3_bf16(v[i + 1], h1, m1, l1);
+    w[0][i / 2] = h0 | (static_cast<uint32_t>(h1) << 16);
+    w[1][i / 2] = m0 | (static_cast<uint32_t>(m1) << 16);
+    w[2][i / 2] = l0 | (static_cast<uint32_t>(l1) << 16);
+  }
+#pragma unroll
+  for (int p = 0; p < 3; ++p) b[p] = make_uint4(w[p][0], w[p][1], w[p][2], w[p][3]);
+}
+
+constexpr int kSharedPass = 8;  // tokens per shared-expert pass (MMA columns)
+
+__host__ __device__ inline int shared_passes(int64_t t) { return static_cast<int>((t + kSharedPass - 1) / kSharedPass); }
+
+// Shared gate/up block b (run as extra blocks of the prep kernel): pass
+// b / (ffn/16 + 1), row tile i = b % (ffn/16 + 1).  i < ffn/16: gate and up
+// rows [16 i, 16 i + 16), warp w over columns [w K/8, (w+1) K/8); act =
+// silu(g) * u (model/qwen36_moe.py:640) stored as bf16 planes.  i == ffn/16:
+// sigmoid(x . gate_inp) for the pass's tokens.
+__device__ void shared_gu_block(int b, const MoeShared& sh, const float* __restrict__ x, int t_total, int hidden,
+                                const MoeWs& ws) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+  const int sffn = static_cast<int>(sh.ffn), tiles = sffn / 16;
+  const int i = b % (tiles + 1), c0 = (b / (tiles + 1)) * kSharedPass;
+  if (i == tiles) {
+    for (int tok = c0 + warp; tok < min(c0 + kSharedPass, t_total); tok += kWarps) {
+      float a = 0.f;
+      for (int k = lane; k < hidden; k += 32) a = fmaf(sh.gate_inp[k], x[static_cast<int64_t>(tok) * hidden + k], a);
+      a = warp_sum(a);
+      if (lane == 0) ws.sgate[tok] = sigmoid_f(a);
+    }
+    return;
+  }
+  __shared__ float4 red[kWarps][32][2];
+  const int span = hidden / kWarps;
+  const uint16_t* ga = static_cast<const uint16_t*>(sh.gate) + static_cast<int64_t>(16 * i + g) * hidden;
+  const uint16_t* ua = static_cast<const uint16_t*>(sh.up) + static_cast<int64_t>(16 * i + g) * hidden;
+  float cg[4] = {0.f, 0.f, 0.f, 0.f}, cu[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll 4  // span / 32 is a multiple of 4: four steps' loads in flight
+  for (int k0 = warp * span; k0 < (warp + 1) * span; k0 += 32) {
+    const int col = k0 + 8 * t;
+    const uint4 g0 = __ldg(reinterpret_cast<const uint4*>(ga + col));
+    const uint4 g1 = __ldg(reinterpret_cast<const uint4*>(ga + 8 * hidden + col));
+    const uint4 u0 = __ldg(reinterpret_cast<const uint4*>(ua + col));
+    const uint4 u1 = __ldg(reinterpret_cast<const uint4*>(ua + 8 * hidden + col));
+    uint4 bp[3];
+    split_planes(x, c0 + g, t_total, hidden, col, bp);
+    bf16_step(cg, g0, g1, bp);
+    bf16_step(cu, u0, u1, bp);
+  }
+  red[warp][lane][0] = make_float4(cg[0], cg[1], cg[2], cg[3]);
+  red[warp][lane][1] = make_float4(cu[0], cu[1], cu[2], cu[3]);
+  __syncthreads();
+  if (threadIdx.x < 16 * kSharedPass) {  // (row r, token v) of the pass
+    const int r = threadIdx.x & 15, v = threadIdx.x >> 4;
+    const int src = (r & 7) * 4 + (v >> 1), reg = (r >> 3) * 2 + (v & 1);
+    float gs = 0.f, us = 0.f;
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) {
+      gs += reinterpret_cast<const float*>(&red[w][src][0])[reg];
+      us += reinterpret_cast<const float*>(&red[w][src][1])[reg];
+    }
+    if (c0 + v < t_total) {
+      uint16_t a, bb, c;
+      split3_bf16(silu_f(gs) * us, a, bb, c);
+      uint16_t* dst = ws.ab + static_cast<int64_t>(c0 + v) * 3 * sffn + 16 * i + r;
+      dst[0] = a;
+      dst[sffn] = bb;
+      dst[2 * sffn] = c;
+    }
+  }
+}
+
+// Shared down block b (run as the first blocks of the routed gate/up
+// kernel, after its dependency wait): pass b / (hidden/64), rows [64 i,
+// 64 i + 64) (4 tiles), i = b % (hidden/64); warp w: tile w & 3 over
+// columns [(w >> 2) K/2, ...).
+__device__ void shared_down_block(int b, const MoeShared& sh, int t_total, int hidden, const MoeWs& ws) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+  const int sffn = static_cast<int>(sh.ffn), groups = hidden / 64;
+  const int i = b % groups, c0 = (b / groups) * kSharedPass;
+  __shared__ float4 red[kWarps][32];
+  const int tile = 4 * i + (warp & 3), half = warp >> 2, span = sffn / 2;
+  const uint16_t* da = static_cast<const uint16_t*>(sh.down) + static_cast<int64_t>(16 * tile + g) * sffn;
+  float cc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll 4  // span / 32 is a multiple of 4: four steps' loads in flight
+  for (int k0 = half * span; k0 < (half + 1) * span; k0 += 32) {
+    const int col = k0 + 8 * t;
+    const uint4 d0 = __ldg(reinterpret_cast<const uint4*>(da + col));
+    const uint4 d1 = __ldg(reinterpret_cast<const uint4*>(da + 8 * sffn + col));
+    uint4 bp[3];
+    load_planes(ws.ab, c0 + g, t_total, sffn, col, bp);
+    bf16_step(cc, d0, d1, bp);
+  }
+  red[warp][lane] = make_float4(cc[0], cc[1], cc[2], cc[3]);
+  __syncthreads();
+  for (int o = threadIdx.x; o < 64 * kSharedPass; o += kThreads) {  // (row, token v) of the pass
+    const int row = o & 63, v = o >> 6, tl = row >> 4, r = row & 15;
+    const int src = (r & 7) * 4 + (v >> 1), reg = (r >> 3) * 2 + (v & 1);
+    const float sum = reinterpret_cast<const float*>(&red[tl][src])[reg] +
+                      reinterpret_cast<const float*>(&red[4 + tl][src])[reg];
+    if (c0 + v < t_total) ws.sout[static_cast<int64_t>(c0 + v) * hidden + 64 * i + row] = sum;
+  }
 }
 
 // ------------------------------------------------------------------ prep
@@ -336,13 +517,19 @@ __device__ __forceinline__ int item_at(const int32_t* cum, int n_slots, int chun
 
 // Block 0 (T > 1): counting sort of the P pairs by expert id (stable) into
 // slots, and each expert-kernel CTA's contiguous item range, balanced by
-// token passes.  The other blocks: encode token (block - 1) (T == 1: token 0).
+// token passes.  The next T blocks: encode token (block - 1) (T == 1: block
+// 0, token 0).  The rest: the shared expert's gate/up blocks.
 __global__ void __launch_bounds__(kThreads) moe_prep_kernel(const int32_t* __restrict__ ids, int p_total,
                                                             int n_experts, int direct, const float* __restrict__ x,
-                                                            int hidden, MoeWs ws, int gu_grid, int gu_chunks,
-                                                            int d_grid, int d_chunks) {
+                                                            int t_total, int hidden, MoeWs ws, int gu_grid,
+                                                            int gu_chunks, int d_grid, int d_chunks, MoeShared sh) {
   pdl_wait();
   pdl_launch_dependents();
+  const int enc0 = direct ? 0 : 1;
+  if (static_cast<int>(blockIdx.x) >= enc0 + t_total) {
+    shared_gu_block(blockIdx.x - enc0 - t_total, sh, x, t_total, hidden, ws);
+    return;
+  }
   if (direct || blockIdx.x > 0) {
     __shared__ float red[kWarps];
     const int tok = blockIdx.x - (direct ? 0 : 1);
@@ -605,7 +792,8 @@ __device__ __forceinline__ int pair_of(bool direct, const MoeWs& ws, int i) { re
 template <int KB>
 __global__ void __launch_bounds__(kThreads, 2)
     moe_gate_up_kernel(const uint8_t* __restrict__ gate, const uint8_t* __restrict__ up, const int32_t* ids,
-                       int n_experts, int direct, int top_k, int ffn, MoeWs ws) {
+                       int n_experts, int direct, int top_k, int ffn, MoeWs ws, int gu_grid, MoeShared sh,
+                       int s_blocks, int t_total, int hidden) {
   constexpr int K = KB * 256, TP = kWarps / KB, OUT = 16 * TP;
   static_assert(kWarps % KB == 0, "K blocks per item");
   extern __shared__ __align__(16) uint8_t smem[];
@@ -614,6 +802,13 @@ __global__ void __launch_bounds__(kThreads, 2)
   float* xsc = reinterpret_cast<float*>(smem + kLutBytes + kRedBytes);
   uint8_t* xs = smem + kLutBytes + kRedBytes + kMiscBytes;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+  if (static_cast<int>(blockIdx.x) < s_blocks) {  // the shared expert's down rows
+    pdl_wait();
+    pdl_launch_dependents();
+    shared_down_block(blockIdx.x, sh, t_total, hidden, ws);
+    return;
+  }
+  const int rb = blockIdx.x - s_blocks;  // routed CTA
   stage_lut(lut);
   // The op's inputs (ids, x) come from whatever ran before: read them only
   // after the wait, and let the down kernel start only then, so that it may
@@ -621,8 +816,8 @@ __global__ void __launch_bounds__(kThreads, 2)
   pdl_wait();
   pdl_launch_dependents();
   const int chunks = ffn / OUT;
-  const int i0 = direct ? blockIdx.x * top_k * chunks / gridDim.x : ws.ranges[2 * blockIdx.x];
-  const int i1 = direct ? (blockIdx.x + 1) * top_k * chunks / gridDim.x : ws.ranges[2 * blockIdx.x + 1];
+  const int i0 = direct ? rb * top_k * chunks / gu_grid : ws.ranges[2 * rb];
+  const int i1 = direct ? (rb + 1) * top_k * chunks / gu_grid : ws.ranges[2 * rb + 1];
   const int tp = warp % TP, kb = warp / TP;
   const uint32_t lane_off = static_cast<uint32_t>(lane & 15) * 8u;
   const uint8_t* xl = xs + (g >> 1) * token_stride(K) + (g & 1) * plane_stride(K) + 16 * t;
@@ -696,7 +891,7 @@ __global__ void __launch_bounds__(kThreads, 2)
 template <int KB>
 __global__ void __launch_bounds__(kThreads, 2)
     moe_down_kernel(const uint8_t* __restrict__ down, const int32_t* ids, const float* __restrict__ weights,
-                    float* out, int n_experts, int direct, int top_k, int hidden, MoeWs ws) {
+                    float* out, int n_experts, int direct, int top_k, int hidden, MoeWs ws, int shared) {
   constexpr int K = KB * 256, TP = kWarps / KB, ROWS = 32 * TP;
   static_assert(kWarps % KB == 0, "K blocks per item");
   extern __shared__ __align__(16) uint8_t smem[];
@@ -801,6 +996,7 @@ __global__ void __launch_bounds__(kThreads, 2)
             if (e < 0 || e >= n_experts) continue;
             a = __fadd_rn(a, __fmul_rn(__ldcg(ws.dn + static_cast<int64_t>(k) * hidden + hh), weights[k]));
           }
+          if (shared) a = __fadd_rn(a, __fmul_rn(__ldcg(ws.sgate), __ldcg(ws.sout + hh)));  // routed + gate * shared
           out[hh] = a;
         }
         if (threadIdx.x == 0) atomicExch(ws.hdr + kTicketBase + c, 0);
@@ -816,7 +1012,8 @@ __global__ void __launch_bounds__(kThreads, 2)
 // out[t] = sum_k w[t, k] * down_k(act) in routing order, each product rounded
 // before the add like the reference's (out * w).sum(0) in f32.
 __global__ void moe_combine_kernel(const float* __restrict__ weights, const int32_t* __restrict__ ids, int64_t t,
-                                   int top_k, int hidden, int n_experts, MoeWs ws, float* __restrict__ out) {
+                                   int top_k, int hidden, int n_experts, MoeWs ws, int shared,
+                                   float* __restrict__ out) {
   pdl_launch_dependents();
   pdl_wait();
   const int64_t total = t * hidden;
@@ -830,6 +1027,7 @@ __global__ void moe_combine_kernel(const float* __restrict__ weights, const int3
       if (e < 0 || e >= n_experts) continue;
       acc = __fadd_rn(acc, __fmul_rn(ws.dn[(tok * top_k + k) * hidden + hh], weights[tok * top_k + k]));
     }
+    if (shared) acc = __fadd_rn(acc, __fmul_rn(ws.sgate[tok], ws.sout[i]));  // routed + gate * shared
     out[i] = acc;
   }
 }
@@ -850,9 +1048,10 @@ cudaError_t launch_pdl(Kern kern, dim3 grid, size_t smem, cudaStream_t stream, A
 }
 
 template <int KBG, int KBD>
-int launch_all(const uint8_t* gate, const uint8_t* up, const uint8_t* down, const float* x, int64_t t, int hidden,
-               int ffn, int n_experts, const int32_t* ids, const float* weights, int top_k, float* out, MoeWs ws,
-               cudaStream_t stream) {
+int launch_all(const uint8_t* gate, const uint8_t* up, const uint8_t* down, const MoeShared* sh, const float* x,
+               int64_t t, int hidden, int ffn, int n_experts, const int32_t* ids, const float* weights, int top_k,
+               float* out, MoeWs ws, cudaStream_t stream) {
+  const int shared = sh ? 1 : 0;
   const int p = static_cast<int>(t * top_k);
   // one token selects top_k distinct experts: no grouping needed
   const int direct = t == 1 ? 1 : 0;
@@ -879,18 +1078,26 @@ int launch_all(const uint8_t* gate, const uint8_t* up, const uint8_t* down, cons
   const int d_grid = direct ? std::min(top_k * d_chunks, slots_max) : slots_max;
   const size_t prep_smem = direct ? 0 : (3 * n_experts + 1 + p) * sizeof(int32_t);
   if (prep_smem > 48 * 1024) return fail(BT_ERR_UNSUPPORTED, "moe_experts_iq3s: too many experts + pairs");
-  cudaError_t e = launch_pdl(moe_prep_kernel, dim3(direct ? 1 : 1 + static_cast<int>(t)), prep_smem, stream, ids, p,
-                             n_experts, direct, x, hidden, ws, gu_grid, gu_chunks, d_grid, d_chunks);
+  // the shared expert rides along: its gate/up blocks after the prep
+  // kernel's, its down blocks ahead of the routed gate/up CTAs
+  const MoeShared shv = sh ? *sh : MoeShared{};
+  const int passes = shared ? shared_passes(t) : 0;
+  const int sgu_blocks = shared ? (static_cast<int>(shv.ffn) / 16 + 1) * passes : 0;
+  const int sd_blocks = shared ? hidden / 64 * passes : 0;
+  const int prep_blocks = (direct ? 1 : 1 + static_cast<int>(t)) + sgu_blocks;
+  cudaError_t e = launch_pdl(moe_prep_kernel, dim3(prep_blocks), prep_smem, stream, ids, p, n_experts, direct, x,
+                             static_cast<int>(t), hidden, ws, gu_grid, gu_chunks, d_grid, d_chunks, shv);
   if (e == cudaSuccess)
-    e = launch_pdl(moe_gate_up_kernel<KBG>, dim3(gu_grid), gu_smem, stream, gate, up, ids, n_experts, direct, top_k,
-                   ffn, ws);
+    e = launch_pdl(moe_gate_up_kernel<KBG>, dim3(sd_blocks + gu_grid), gu_smem, stream, gate, up, ids, n_experts,
+                   direct, top_k, ffn, ws, gu_grid, shv, sd_blocks, static_cast<int>(t), hidden);
   if (e == cudaSuccess)
     e = launch_pdl(moe_down_kernel<KBD>, dim3(d_grid), d_smem, stream, down, ids, weights, out, n_experts, direct,
-                   top_k, hidden, ws);
+                   top_k, hidden, ws, shared);
   const int64_t total = t * hidden;
   const int blocks = static_cast<int>(std::min<int64_t>((total + kThreads - 1) / kThreads, 4096));
   if (e == cudaSuccess && !direct)
-    e = launch_pdl(moe_combine_kernel, dim3(blocks), 0, stream, weights, ids, t, top_k, hidden, n_experts, ws, out);
+    e = launch_pdl(moe_combine_kernel, dim3(blocks), 0, stream, weights, ids, t, top_k, hidden, n_experts, ws, shared,
+                   out);
   if (e == cudaSuccess) e = cudaGetLastError();
   if (e != cudaSuccess) return fail_cuda(e, "moe experts launch");
   return BT_OK;
@@ -927,15 +1134,15 @@ int moe_route(const float* logits, int64_t t, int64_t n_experts, int top_k, int3
   return BT_OK;
 }
 
-int64_t moe_workspace_bytes(int64_t t, int64_t hidden, int64_t ffn, int64_t n_experts, int top_k) {
+int64_t moe_workspace_bytes(int64_t t, int64_t hidden, int64_t ffn, int64_t shared_ffn, int64_t n_experts, int top_k) {
   (void)n_experts;
-  if (t < 1 || top_k < 1) return 0;
-  return moe_ws_bytes(t, t * top_k, hidden, ffn);
+  if (t < 1 || top_k < 1 || shared_ffn < 0) return 0;
+  return moe_ws_bytes(t, t * top_k, hidden, ffn, shared_ffn);
 }
 
-int moe_experts_iq3s(const void* gate, const void* up, const void* down, const float* x, int64_t t, int64_t hidden,
-                     int64_t ffn, int64_t n_experts, const int32_t* ids, const float* weights, int top_k, float* out,
-                     void* workspace, cudaStream_t stream) {
+int moe_layer_iq3s(const void* gate, const void* up, const void* down, const MoeShared* shared, const float* x,
+                   int64_t t, int64_t hidden, int64_t ffn, int64_t n_experts, const int32_t* ids, const float* weights,
+                   int top_k, float* out, void* workspace, cudaStream_t stream) {
   if (!gate || !up || !down || !x || !ids || !weights || !out || !workspace)
     return fail(BT_ERR_INVALID, "moe_experts_iq3s: null pointer");
   if (t < 1 || t * top_k > 4096 || top_k < 1 || top_k > 64 || n_experts < 1 || n_experts > 4096)
@@ -943,15 +1150,27 @@ int moe_experts_iq3s(const void* gate, const void* up, const void* down, const f
   if ((reinterpret_cast<uintptr_t>(gate) | reinterpret_cast<uintptr_t>(up) | reinterpret_cast<uintptr_t>(down) |
        reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(workspace)) & 15)
     return fail(BT_ERR_INVALID, "moe_experts_iq3s: weights, x and workspace must be 16-byte aligned");
-  const MoeWs ws = moe_ws(workspace, t, t * top_k, hidden, ffn);
+  if (shared) {
+    if (!shared->gate || !shared->up || !shared->down || !shared->gate_inp)
+      return fail(BT_ERR_INVALID, "moe shared expert: null pointer");
+    if (shared->ffn < 256 || shared->ffn % 256 || shared->ffn > 8192 || hidden % 1024)
+      return fail(BT_ERR_UNSUPPORTED, "moe shared expert: ffn must be a multiple of 256 and hidden of 1024");
+    if ((reinterpret_cast<uintptr_t>(shared->gate) | reinterpret_cast<uintptr_t>(shared->up) |
+         reinterpret_cast<uintptr_t>(shared->down)) & 15)
+      return fail(BT_ERR_INVALID, "moe shared expert: weights must be 16-byte aligned");
+  }
+  const MoeWs ws = moe_ws(workspace, t, t * top_k, hidden, ffn, shared ? shared->ffn : 0);
   const uint8_t* g = static_cast<const uint8_t*>(gate);
   const uint8_t* u = static_cast<const uint8_t*>(up);
   const uint8_t* d = static_cast<const uint8_t*>(down);
   const int h = static_cast<int>(hidden), f = static_cast<int>(ffn), ne = static_cast<int>(n_experts);
   const int k = top_k;
-  if (hidden == 2048 && ffn == 512) return launch_all<8, 2>(g, u, d, x, t, h, f, ne, ids, weights, k, out, ws, stream);
-  if (hidden == 1024 && ffn == 512) return launch_all<4, 2>(g, u, d, x, t, h, f, ne, ids, weights, k, out, ws, stream);
-  if (hidden == 2048 && ffn == 1024) return launch_all<8, 4>(g, u, d, x, t, h, f, ne, ids, weights, k, out, ws, stream);
+  if (hidden == 2048 && ffn == 512)
+    return launch_all<8, 2>(g, u, d, shared, x, t, h, f, ne, ids, weights, k, out, ws, stream);
+  if (hidden == 1024 && ffn == 512)
+    return launch_all<4, 2>(g, u, d, shared, x, t, h, f, ne, ids, weights, k, out, ws, stream);
+  if (hidden == 2048 && ffn == 1024)
+    return launch_all<8, 4>(g, u, d, shared, x, t, h, f, ne, ids, weights, k, out, ws, stream);
   return fail(BT_ERR_UNSUPPORTED, "moe_experts_iq3s serves (hidden, ffn) in {(1024,512), (2048,512), (2048,1024)}");
 }
 

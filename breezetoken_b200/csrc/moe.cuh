@@ -17,10 +17,20 @@ int repack_iq3_s(const void* src, void* dst, int64_t rows, int64_t k, cudaStream
 int moe_route(const float* logits, int64_t t, int64_t n_experts, int top_k, int32_t* ids, float* weights,
               cudaStream_t stream);
 
-int64_t moe_workspace_bytes(int64_t t, int64_t hidden, int64_t ffn, int64_t n_experts, int top_k);
+// The layer's shared expert: bf16 (out, in) rows, f32 gate vector.
+struct MoeShared {
+  const void* gate;      // (ffn, hidden)
+  const void* up;        // (ffn, hidden)
+  const void* down;      // (hidden, ffn)
+  const float* gate_inp; // (hidden,)
+  int64_t ffn;
+};
 
-int moe_experts_iq3s(const void* gate, const void* up, const void* down, const float* x, int64_t t, int64_t hidden,
-                     int64_t ffn, int64_t n_experts, const int32_t* ids, const float* weights, int top_k, float* out,
-                     void* workspace, cudaStream_t stream);
+int64_t moe_workspace_bytes(int64_t t, int64_t hidden, int64_t ffn, int64_t shared_ffn, int64_t n_experts, int top_k);
+
+// shared may be null (routed experts only).
+int moe_layer_iq3s(const void* gate, const void* up, const void* down, const MoeShared* shared, const float* x,
+                   int64_t t, int64_t hidden, int64_t ffn, int64_t n_experts, const int32_t* ids, const float* weights,
+                   int top_k, float* out, void* workspace, cudaStream_t stream);
 
 }  // namespace bt

@@ -144,8 +144,8 @@ def bench_attn(batch: int, ctx: int, splits: int, iters: int) -> dict:
             "us_graph": gsec * 1e6, "bytes": nbytes, "gbs": nbytes / sec / 1e9, "gbs_graph": nbytes / gsec / 1e9}
 
 
-def bench_moe(tokens: int, iters: int) -> dict:
-    from breezetoken_b200.moe import IQ3SExperts, experts_forward, route_logits
+def bench_moe(tokens: int, iters: int, shared: bool = True) -> dict:
+    from breezetoken_b200.moe import IQ3SExperts, SharedExpert, moe_forward, route_logits
     from breezetoken_b200.quant import quantize_iq3_s
 
     hidden, ffn, n_exp, top_k = 2048, 512, 256, 8
@@ -172,8 +172,17 @@ def bench_moe(tokens: int, iters: int) -> dict:
     def flush_l2() -> None:
         flush.sum(dtype=torch.int32)  # read 256 MB: afterwards L2 holds only clean lines
 
+    se = None
+    if shared:  # one bf16 shared expert of ffn 512
+        def w(*shape) -> torch.Tensor:
+            return torch.from_numpy(rng.standard_normal(shape).astype(np.float32) * np.float32(0.02))
+
+        se = SharedExpert.from_tensors(w(ffn, hidden), w(ffn, hidden), w(hidden, ffn), w(hidden), "cuda")
+        ws = torch.zeros(int(N.load().bt_moe_layer_workspace_bytes(tokens, hidden, ffn, ffn, n_exp, top_k)),
+                         dtype=torch.uint8, device="cuda")
+
     def call() -> None:
-        experts_forward(ex, x, r.expert_ids, r.weights, ws)
+        moe_forward(ex, se, x, r.expert_ids, r.weights, ws)
 
     # launch-timed: events around each call, L2 flushed before it
     total = 0.0
@@ -193,8 +202,10 @@ def bench_moe(tokens: int, iters: int) -> dict:
     both = _time_graph(lambda: (flush_l2(), call()), iters, s)
     alone = _time_graph(flush_l2, iters, s)
     gsec = both - alone
-    nbytes = u * 1_351_680 + tokens * hidden * 8
-    return {"kernel": "moe_experts_iq3s", "tokens": tokens, "unique_experts": u, "us": sec * 1e6,
+    # algorithmic bytes: the selected experts, the bf16 shared expert, x in and out
+    nbytes = u * 1_351_680 + (6_291_456 if shared else 0) + tokens * hidden * 8
+    return {"kernel": "moe_layer_iq3s", "tokens": tokens, "unique_experts": u, "shared_expert": shared,
+            "us": sec * 1e6,
             "us_graph": gsec * 1e6, "bytes": nbytes, "gbs": nbytes / sec / 1e9, "gbs_graph": nbytes / gsec / 1e9,
             "l2": "flushed before each call (256 MB read)"}
 
@@ -253,6 +264,7 @@ def main() -> None:
     mo = sub.add_parser("moe")
     mo.add_argument("--tokens", type=int, default=1)
     mo.add_argument("--iters", type=int, default=50)
+    mo.add_argument("--no-shared", action="store_true", help="routed experts only")
     t = sub.add_parser("trace")
     t.add_argument("--gguf", required=True)
     t.add_argument("--max-context", type=int, default=1024)
@@ -264,7 +276,7 @@ def main() -> None:
     if args.cmd == "gemv":
         r = bench_gemv(args.n, args.k, args.iters)
     elif args.cmd == "moe":
-        r = bench_moe(args.tokens, args.iters)
+        r = bench_moe(args.tokens, args.iters, shared=not args.no_shared)
     elif args.cmd == "gdn":
         r = bench_gdn(args.batch, args.steps)
     else:

@@ -13,6 +13,7 @@ on an unsupported shape or a missing library; there is no CPU path.
 
 from __future__ import annotations
 
+import ctypes
 from dataclasses import dataclass
 
 import numpy as np
@@ -98,6 +99,63 @@ def experts_forward(ex: IQ3SExperts, x: torch.Tensor, ids: torch.Tensor, weights
     return out
 
 
+@dataclass
+class SharedExpert:
+    """A layer's shared expert (model/qwen36_moe.py:276-283): gate, up (ffn,
+    hidden) and down (hidden, ffn) bf16 rows in the GGUF orientation, and
+    the f32 gate vector (hidden,)."""
+
+    gate: torch.Tensor
+    up: torch.Tensor
+    down: torch.Tensor
+    gate_inp: torch.Tensor
+
+    @property
+    def ffn(self) -> int:
+        return int(self.gate.shape[0])
+
+    @classmethod
+    def from_tensors(cls, gate, up, down, gate_inp, device: str = "cuda") -> SharedExpert:
+        def rows(w) -> torch.Tensor:
+            return torch.as_tensor(w).to(device=device, dtype=torch.bfloat16).contiguous()
+
+        g, u, d = rows(gate), rows(up), rows(down)
+        gi = torch.as_tensor(gate_inp).to(device=device, dtype=torch.float32).reshape(-1).contiguous()
+        ffn, hidden = g.shape
+        if u.shape != g.shape or d.shape != (hidden, ffn) or gi.numel() != hidden:
+            raise ValueError(f"shared expert shapes: gate {tuple(g.shape)}, up {tuple(u.shape)}, "
+                             f"down {tuple(d.shape)}, gate_inp {gi.numel()}")
+        return cls(g, u, d, gi)
+
+
+def moe_forward(ex: IQ3SExperts, shared: SharedExpert | None, x: torch.Tensor, ids: torch.Tensor,
+                weights: torch.Tensor, workspace: torch.Tensor | None = None) -> torch.Tensor:
+    """Qwen36Moe._moe after routing (model/qwen36_moe.py:634-642) for x (T,
+    hidden) f32: the routed experts plus, when given, the shared expert gated
+    by sigmoid(x . gate_inp)."""
+    x2 = x.float().reshape(-1, ex.hidden).contiguous()
+    t = x2.shape[0]
+    ids2 = ids.to(torch.int32).reshape(t, -1).contiguous()
+    w2 = weights.float().reshape(t, -1).contiguous()
+    top_k = ids2.shape[1]
+    sffn = shared.ffn if shared is not None else 0
+    lib = N.load()
+    need = int(lib.bt_moe_layer_workspace_bytes(t, ex.hidden, ex.ffn, sffn, ex.n_experts, top_k))
+    if workspace is None or workspace.numel() < need:
+        workspace = torch.zeros(need, dtype=torch.uint8, device=x2.device)
+    out = torch.empty(t, ex.hidden, dtype=torch.float32, device=x2.device)
+    sh = None
+    if shared is not None:
+        if shared.gate.shape[1] != ex.hidden:
+            raise ValueError(f"shared expert hidden {shared.gate.shape[1]} != {ex.hidden}")
+        sh = N.BtMoeShared(shared.gate.data_ptr(), shared.up.data_ptr(), shared.down.data_ptr(),
+                           shared.gate_inp.data_ptr(), sffn)
+    N.call("bt_moe_layer_iq3s", ex.gate.data_ptr(), ex.up.data_ptr(), ex.down.data_ptr(),
+           None if sh is None else ctypes.byref(sh), x2.data_ptr(), t, ex.hidden, ex.ffn, ex.n_experts,
+           ids2.data_ptr(), w2.data_ptr(), top_k, out.data_ptr(), workspace.data_ptr(), _stream())
+    return out
+
+
 class ExpertPool:
     """Per-layer IQ3_S expert tensors resident on the device (model/moe.py:42-233)."""
 
@@ -133,4 +191,5 @@ class ExpertPool:
         return experts_forward(ex, x, ids, weights, self._ws)
 
 
-__all__ = ["ExpertPool", "IQ3SExperts", "RouterOutput", "experts_forward", "route", "route_logits"]
+__all__ = ["ExpertPool", "IQ3SExperts", "RouterOutput", "SharedExpert", "experts_forward", "moe_forward", "route",
+           "route_logits"]

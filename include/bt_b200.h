@@ -201,6 +201,28 @@ BT_API int bt_moe_experts_iq3s(const void* gate, const void* up, const void* dow
                         int64_t n_experts, const int32_t* ids, const float* weights,
                         int top_k, float* out, void* workspace, void* stream);
 
+/* Qwen36Moe._moe (model/qwen36_moe.py:634-642) for T tokens: the routed
+ * experts as bt_moe_experts_iq3s plus, when `shared` is not NULL, the
+ * shared expert: out[t] = routed[t] + sigmoid(x_t . gate_inp) *
+ * down(silu(gate x_t) * up x_t).  Shared weights are bf16 rows in the GGUF
+ * (out, in) orientation (gate, up: (ffn, hidden); down: (hidden, ffn)),
+ * 16-byte aligned; gate_inp is f32 (hidden,); ffn % 256 == 0.
+ * workspace: bt_moe_layer_workspace_bytes() bytes, zeroed once.           */
+typedef struct BtMoeShared {
+  const void* gate;
+  const void* up;
+  const void* down;
+  const float* gate_inp;
+  int64_t ffn;
+} BtMoeShared;
+BT_API int64_t bt_moe_layer_workspace_bytes(int64_t t, int64_t hidden, int64_t ffn,
+                                     int64_t shared_ffn, int64_t n_experts, int top_k);
+BT_API int bt_moe_layer_iq3s(const void* gate, const void* up, const void* down,
+                      const BtMoeShared* shared, const float* x, int64_t t,
+                      int64_t hidden, int64_t ffn, int64_t n_experts,
+                      const int32_t* ids, const float* weights, int top_k,
+                      float* out, void* workspace, void* stream);
+
 /* ------------------------------------------------- Qwen3.5 decode step */
 typedef struct BtQwen35Dims {
   int32_t hidden, n_layers, n_heads, n_kv, head_dim, rope_dim, ffn, vocab;

@@ -13,6 +13,8 @@ records, on seeded inputs, what its torch f32 path computes:
   ``_torch_rope``, rms_norm, fused_add_rms_norm, silu_mul;
 * ``moe.npz``       -- ``route`` on N(0,1) router logits (BASELINE config 4
   shape) and one ``ExpertPool``-style expert evaluation from IQ3_S bytes;
+* ``moe_shared.npz`` -- ``Qwen36Moe._moe`` (routed output + gated bf16 shared
+  expert) run on a stand-in object around moe.npz's routed output;
 * ``qwen35_tiny.npz`` / ``qwen35_0_8b.npz`` -- greedy token ids of
   ``Qwen35(backend="torch", device="cpu").generate`` on the seeded synthetic
   checkpoints of breezetoken_b200.synth, with per-step top-2 logit margins and
@@ -192,6 +194,48 @@ def gen_moe(out: Path) -> None:
     )
 
 
+def moe_shared_inputs():
+    """Seeded bf16 shared expert for moe_inputs() (one
+    bf16 shared expert of ffn 512), as f32 arrays holding bf16 values."""
+    rng = np.random.default_rng(4)
+    m = moe_inputs()
+    hidden, ffn = m["hidden"], 512
+
+    def bf16(a: np.ndarray) -> np.ndarray:
+        return torch.from_numpy(a.astype(np.float32)).bfloat16().float().numpy()
+
+    return dict(
+        gate=bf16(rng.standard_normal((ffn, hidden)) * 0.02), up=bf16(rng.standard_normal((ffn, hidden)) * 0.02),
+        down=bf16(rng.standard_normal((hidden, ffn)) * 0.02),
+        gate_inp=(rng.standard_normal(hidden) * 0.02).astype(np.float32), ffn=ffn,
+    )
+
+
+def gen_moe_shared(out: Path) -> None:
+    """The reference's Qwen36Moe._moe (model/qwen36_moe.py:634-642), run on a
+    stand-in object: the routed output is moe.npz's `y` (the stand-in expert
+    pool returns it), the shared expert is moe_shared_inputs() in f32."""
+    import types
+
+    from breezetoken.model.qwen36_moe import Qwen36Moe
+
+    m, sh = moe_inputs(), moe_shared_inputs()
+    routed = torch.from_numpy(np.load(HERE / "moe.npz")["y"])
+    stub = types.SimpleNamespace()
+    stub.cfg = types.SimpleNamespace(top_k=8, shared_ffn=sh["ffn"])
+    stub.layers = [{
+        "router": torch.zeros(16, m["hidden"]),
+        "shexp_gu": torch.from_numpy(np.concatenate([sh["gate"], sh["up"]])),
+        "shexp_down": torch.from_numpy(sh["down"]),
+        "shexp_gate": torch.from_numpy(sh["gate_inp"]),
+    }]
+    stub.experts = types.SimpleNamespace(forward=lambda i, gguf, xn, routing: routed.clone())
+    stub._gguf = None
+    stub._linear = lambda w, x: Qwen36Moe._linear(stub, w, x)
+    y = Qwen36Moe._moe(stub, 0, torch.from_numpy(m["x"]))
+    np.savez_compressed(out, y=y.numpy())
+
+
 def gen_model(out: Path, spec, steps: int, max_context: int, keep_logits: int) -> None:
     from breezetoken.gguf import GGUFFile
     from breezetoken.model.qwen35 import Qwen35
@@ -230,11 +274,16 @@ def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True)
     ap.add_argument("--skip-0_8b", action="store_true")
+    ap.add_argument("--only", help="regenerate one fixture (e.g. moe_shared)")
     args = ap.parse_args()
     sys.path.insert(0, args.reference)
+    if args.only == "moe_shared":
+        gen_moe_shared(HERE / "moe_shared.npz")
+        return
     gen_dequant(HERE / "dequant.npz")
     gen_ops(HERE / "ops.npz")
     gen_moe(HERE / "moe.npz")
+    gen_moe_shared(HERE / "moe_shared.npz")
     gen_model(HERE / "qwen35_tiny.npz", QWEN35_TINY, steps=32, max_context=512, keep_logits=4)
     if not args.skip_0_8b:
         gen_model(HERE / "qwen35_0_8b.npz", QWEN35_0_8B, steps=128, max_context=1024, keep_logits=1)

@@ -15,12 +15,13 @@ import pytest
 import torch
 
 from breezetoken_b200 import _native as N
-from breezetoken_b200.moe import IQ3SExperts, experts_forward, route_logits
+from breezetoken_b200.moe import IQ3SExperts, SharedExpert, experts_forward, moe_forward, route_logits
 from breezetoken_b200.quant import quantize_iq3_s
 from oracle.moe import experts as oracle_experts
 from oracle.moe import route as oracle_route
+from oracle.moe import shared_expert as oracle_shared
 from tests.conftest import golden
-from tests.golden.make_golden import moe_inputs
+from tests.golden.make_golden import moe_inputs, moe_shared_inputs
 
 pytestmark = pytest.mark.gpu
 
@@ -140,6 +141,47 @@ def test_moe_experts_passes_of_eight_tokens(layer) -> None:
     dr = np.ascontiguousarray(m["down"]).reshape(16 * m["hidden"], -1)
     for i in range(t):
         _close(got[i], oracle_experts(x[i], gr, ur, dr, ids[i], ws[i], m["hidden"], m["ffn"]))
+
+
+@pytest.fixture(scope="module")
+def shared(cuda):
+    sh = moe_shared_inputs()
+    return sh, SharedExpert.from_tensors(torch.from_numpy(sh["gate"]), torch.from_numpy(sh["up"]),
+                                         torch.from_numpy(sh["down"]), torch.from_numpy(sh["gate_inp"]), "cuda")
+
+
+def test_moe_layer_with_shared_expert_matches_reference_golden(layer, shared) -> None:
+    """One token: routed experts + the gated bf16 shared expert against the
+    reference's Qwen36Moe._moe output (moe_shared golden)."""
+    m, ex = layer
+    _, se = shared
+    x = torch.from_numpy(m["x"]).cuda().reshape(1, -1)
+    ids = torch.tensor([m["ids"]], dtype=torch.int32, device="cuda")
+    w = torch.from_numpy(m["w"]).reshape(1, -1).cuda()
+    for _ in range(2):
+        got = moe_forward(ex, se, x, ids, w).cpu().numpy()[0]
+        _close(got, golden("moe_shared")["y"])
+
+
+def test_moe_layer_with_shared_expert_batch(layer, shared) -> None:
+    """12 tokens (two 8-token passes of the shared expert) against the oracle."""
+    m, ex = layer
+    sh, se = shared
+    rng = np.random.default_rng(8)
+    t = 12
+    x = rng.standard_normal((t, m["hidden"])).astype(np.float32)
+    logits = rng.standard_normal((t, 16)).astype(np.float32)
+    ids, ws = zip(*[(oracle_route(lg, 8)[1], oracle_route(lg, 8)[0]) for lg in logits], strict=True)
+    ids, ws = np.stack(ids).astype(np.int32), np.stack(ws)
+    got = moe_forward(ex, se, torch.from_numpy(x).cuda(), torch.from_numpy(ids).cuda(),
+                      torch.from_numpy(ws).cuda()).cpu().numpy()
+    gr = np.ascontiguousarray(m["gate"]).reshape(16 * m["ffn"], -1)
+    ur = np.ascontiguousarray(m["up"]).reshape(16 * m["ffn"], -1)
+    dr = np.ascontiguousarray(m["down"]).reshape(16 * m["hidden"], -1)
+    for i in range(t):
+        want = oracle_experts(x[i], gr, ur, dr, ids[i], ws[i], m["hidden"], m["ffn"])
+        want = want + oracle_shared(x[i], sh["gate"], sh["up"], sh["down"], sh["gate_inp"])
+        _close(got[i], want)
 
 
 def test_moe_route_matches_oracle(cuda) -> None:

@@ -77,6 +77,17 @@ def test_moe_route_and_experts_match_reference() -> None:
     np.testing.assert_allclose(y, g["y"], rtol=1e-4, atol=1e-5)
 
 
+def test_moe_shared_expert_matches_reference() -> None:
+    """routed + sigmoid(x . gate_inp) * shared(x) against the reference's
+    Qwen36Moe._moe (model/qwen36_moe.py:634-642) on the same inputs."""
+    from oracle.moe import shared_expert
+    from tests.golden.make_golden import moe_shared_inputs
+
+    g, m, sh = golden("moe_shared"), moe_inputs(), moe_shared_inputs()
+    y = golden("moe")["y"] + shared_expert(m["x"], sh["gate"], sh["up"], sh["down"], sh["gate_inp"])
+    assert np.abs(y - g["y"]).max() <= 1e-6 * np.abs(g["y"]).max()
+
+
 def test_tiny_model_greedy_tokens_match_reference(tiny_gguf) -> None:
     from oracle.qwen35 import Qwen35Oracle
 
