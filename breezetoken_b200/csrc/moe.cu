@@ -406,6 +406,11 @@ __device__ __forceinline__ void split_planes(const float* x, int64_t tok, int t_
 
 constexpr int kSharedPass = 8;  // tokens per shared-expert pass (MMA columns)
 
+// Bulk prefetch of [p, p + bytes) into L2 (p 16-byte aligned, bytes % 16 == 0).
+__device__ __forceinline__ void prefetch_l2(const void* p, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
+
 __host__ __device__ inline int shared_passes(int64_t t) { return static_cast<int>((t + kSharedPass - 1) / kSharedPass); }
 
 // Shared gate/up block b (run as extra blocks of the prep kernel): pass
@@ -418,17 +423,30 @@ __device__ void shared_gu_block(int b, const MoeShared& sh, const float* __restr
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
   const int sffn = static_cast<int>(sh.ffn), tiles = sffn / 16;
   const int i = b % (tiles + 1), c0 = (b / (tiles + 1)) * kSharedPass;
+  const int span = hidden / kWarps;
+  if (i < tiles) {  // the warp's 32 row slices (16 gate + 16 up rows x span columns) into L2 at once
+    const uint16_t* m = lane < 16 ? static_cast<const uint16_t*>(sh.gate) : static_cast<const uint16_t*>(sh.up);
+    prefetch_l2(m + static_cast<int64_t>(16 * i + (lane & 15)) * hidden + warp * span, 2 * span);
+  }
+  pdl_wait();  // x comes from earlier kernels; the weights do not
   if (i == tiles) {
-    for (int tok = c0 + warp; tok < min(c0 + kSharedPass, t_total); tok += kWarps) {
+    static_assert(kSharedPass == kWarps, "one token of the pass per warp");
+    const int tok = c0 + warp;
+    if (tok < t_total) {
+      const float4* gv = reinterpret_cast<const float4*>(sh.gate_inp);
+      const float4* xv = reinterpret_cast<const float4*>(x + static_cast<int64_t>(tok) * hidden);
       float a = 0.f;
-      for (int k = lane; k < hidden; k += 32) a = fmaf(sh.gate_inp[k], x[static_cast<int64_t>(tok) * hidden + k], a);
+#pragma unroll 8  // independent loads: eight in flight per lane
+      for (int f = lane; f < hidden / 4; f += 32) {
+        const float4 u = __ldg(gv + f), v = __ldcg(xv + f);
+        a = fmaf(u.x, v.x, fmaf(u.y, v.y, fmaf(u.z, v.z, fmaf(u.w, v.w, a))));
+      }
       a = warp_sum(a);
       if (lane == 0) ws.sgate[tok] = sigmoid_f(a);
     }
     return;
   }
   __shared__ float4 red[kWarps][32][2];
-  const int span = hidden / kWarps;
   const uint16_t* ga = static_cast<const uint16_t*>(sh.gate) + static_cast<int64_t>(16 * i + g) * hidden;
   const uint16_t* ua = static_cast<const uint16_t*>(sh.up) + static_cast<int64_t>(16 * i + g) * hidden;
   float cg[4] = {0.f, 0.f, 0.f, 0.f}, cu[4] = {0.f, 0.f, 0.f, 0.f};
@@ -478,6 +496,11 @@ __device__ void shared_down_block(int b, const MoeShared& sh, int t_total, int h
   __shared__ float4 red[kWarps][32];
   const int tile = 4 * i + (warp & 3), half = warp >> 2, span = sffn / 2;
   const uint16_t* da = static_cast<const uint16_t*>(sh.down) + static_cast<int64_t>(16 * tile + g) * sffn;
+  if (lane < 16)  // the warp's 16 row slices into L2 at once
+    prefetch_l2(static_cast<const uint16_t*>(sh.down) + static_cast<int64_t>(16 * tile + lane) * sffn + half * span,
+                2 * span);
+  pdl_wait();  // act comes from the prep kernel; the weights do not
+  pdl_launch_dependents();
   float cc[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll 4  // span / 32 is a multiple of 4: four steps' loads in flight
   for (int k0 = half * span; k0 < (half + 1) * span; k0 += 32) {
@@ -523,13 +546,13 @@ __global__ void __launch_bounds__(kThreads) moe_prep_kernel(const int32_t* __res
                                                             int n_experts, int direct, const float* __restrict__ x,
                                                             int t_total, int hidden, MoeWs ws, int gu_grid,
                                                             int gu_chunks, int d_grid, int d_chunks, MoeShared sh) {
-  pdl_wait();
   pdl_launch_dependents();
   const int enc0 = direct ? 0 : 1;
   if (static_cast<int>(blockIdx.x) >= enc0 + t_total) {
-    shared_gu_block(blockIdx.x - enc0 - t_total, sh, x, t_total, hidden, ws);
+    shared_gu_block(blockIdx.x - enc0 - t_total, sh, x, t_total, hidden, ws);  // waits after its L2 prefetch
     return;
   }
+  pdl_wait();
   if (direct || blockIdx.x > 0) {
     __shared__ float red[kWarps];
     const int tok = blockIdx.x - (direct ? 0 : 1);
@@ -784,6 +807,31 @@ __device__ __forceinline__ bool slot_of(int u, bool direct, const int32_t* ids, 
 
 __device__ __forceinline__ int pair_of(bool direct, const MoeWs& ws, int i) { return direct ? i : ws.pairs[i]; }
 
+// sum_k w[k] * dn[k * stride] over a token's top_k pairs in routing order,
+// each product rounded before the add like the reference's (out * w).sum(0)
+// in f32; pairs with an invalid id contribute nothing.  Eight pairs' loads
+// are in flight at a time.
+__device__ __forceinline__ float routed_sum(const int32_t* ids, const float* w, const float* dn, int64_t stride,
+                                            int top_k, int n_experts) {
+  float a = 0.f;
+  for (int k0 = 0; k0 < top_k; k0 += 8) {
+    float v[8], wk[8];
+    bool ok[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int k = k0 + j;
+      const int e = k < top_k ? ids[k] : -1;
+      ok[j] = e >= 0 && e < n_experts;
+      v[j] = ok[j] ? __ldcg(dn + k * stride) : 0.f;
+      wk[j] = ok[j] ? w[k] : 0.f;
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      if (ok[j]) a = __fadd_rn(a, __fmul_rn(v[j], wk[j]));
+  }
+  return a;
+}
+
 // ------------------------------------------------------------------ gate/up
 // Items (slot u, chunk c): gate/up rows [OUT c, OUT c + OUT) of the slot's
 // expert, OUT = 16 * TP, TP = 8 / KB tile pairs.  Warp w: tile pair
@@ -803,8 +851,6 @@ __global__ void __launch_bounds__(kThreads, 2)
   uint8_t* xs = smem + kLutBytes + kRedBytes + kMiscBytes;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
   if (static_cast<int>(blockIdx.x) < s_blocks) {  // the shared expert's down rows
-    pdl_wait();
-    pdl_launch_dependents();
     shared_down_block(blockIdx.x, sh, t_total, hidden, ws);
     return;
   }
@@ -990,12 +1036,7 @@ __global__ void __launch_bounds__(kThreads, 2)
         __threadfence();
         for (int r = threadIdx.x; r < ROWS; r += kThreads) {
           const int hh = c * ROWS + r;
-          float a = 0.f;
-          for (int k = 0; k < top_k; ++k) {
-            const int e = ids[k];
-            if (e < 0 || e >= n_experts) continue;
-            a = __fadd_rn(a, __fmul_rn(__ldcg(ws.dn + static_cast<int64_t>(k) * hidden + hh), weights[k]));
-          }
+          float a = routed_sum(ids, weights, ws.dn + hh, hidden, top_k, n_experts);
           if (shared) a = __fadd_rn(a, __fmul_rn(__ldcg(ws.sgate), __ldcg(ws.sout + hh)));  // routed + gate * shared
           out[hh] = a;
         }
@@ -1021,12 +1062,8 @@ __global__ void moe_combine_kernel(const float* __restrict__ weights, const int3
        i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
     const int64_t tok = i / hidden;
     const int hh = static_cast<int>(i % hidden);
-    float acc = 0.f;
-    for (int k = 0; k < top_k; ++k) {
-      const int e = ids[tok * top_k + k];
-      if (e < 0 || e >= n_experts) continue;
-      acc = __fadd_rn(acc, __fmul_rn(ws.dn[(tok * top_k + k) * hidden + hh], weights[tok * top_k + k]));
-    }
+    float acc = routed_sum(ids + tok * top_k, weights + tok * top_k, ws.dn + tok * top_k * hidden + hh, hidden,
+                           top_k, n_experts);
     if (shared) acc = __fadd_rn(acc, __fmul_rn(ws.sgate[tok], ws.sout[i]));  // routed + gate * shared
     out[i] = acc;
   }
