@@ -9,6 +9,7 @@
 #include "errors.h"
 #include "gdn.cuh"
 #include "gemv_q8.cuh"
+#include "linear_rows.cuh"
 #include "moe.cuh"
 #include "ops.cuh"
 
@@ -147,6 +148,11 @@ int bt_linear_q8(const void* w, const float* x, float* y, int64_t n, int64_t k, 
 
 int bt_linear_kn(const void* w, int w_dtype, const float* x, float* y, int64_t k, int64_t n, void* stream) {
   return bt::linear_kn(w, w_dtype, x, y, k, n, as_stream(stream));
+}
+
+int bt_linear_rows(const void* w, int w_dtype, const float* x, float* y, int64_t n, int64_t k, int64_t t,
+                   void* stream) {
+  return bt::linear_rows(w, w_dtype, x, y, n, k, t, as_stream(stream));
 }
 
 int bt_rms_norm(const float* x, const float* w, float* y, int64_t rows, int64_t n, float eps, void* stream) {

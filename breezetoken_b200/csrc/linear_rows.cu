@@ -1,0 +1,158 @@
+// Dense projection of T tokens by bf16 or f32 weight rows on the tensor cores:
+// y[t][n] = sum_k W[n][k] x[t][k], W (N, K) in the GGUF (out, in)
+// orientation, x (T, K) f32, y (T, N) f32 -- the reference's _linear /
+// _linear_b of model/qwen36_moe.py:352-358 in its f32 form (weights exact in
+// f32, activations f32).
+//
+// One block per 16-row tile and 8-token pass (grid (N/16, ceil(T/8))); its 8
+// warps split K.  Per 32-column step a lane loads weights 8t .. 8t+7 of rows
+// g and g+8 (16-byte loads; the k order inside the step is permuted
+// identically on both MMA operands) and the same columns of token column g's
+// x.  x is split into three bf16 planes (x = hi + mid + lo, each remainder
+// exact in f32), f32 weights likewise; every plane product accumulates into
+// one f32 sum (m16n8k16 bf16 MMAs), so the sums carry both operands to their
+// 24 bits.  Before the dependency wait each warp bulk-prefetches its weight
+// slices into L2: the weights never depend on earlier kernels.
+#include <cuda_bf16.h>
+
+#include <algorithm>
+
+#include "errors.h"
+#include "linear_rows.cuh"
+
+namespace bt {
+namespace {
+
+constexpr int kThreads = 256, kWarps = 8, kPass = 8;
+
+__device__ __forceinline__ void mma_bf16(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                         uint32_t b0, uint32_t b1) {
+  asm("mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+      "{%0, %1, %2, %3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ uint32_t bf16_pair(float a, float b) {
+  return __bfloat16_as_ushort(__float2bfloat16_rn(a)) |
+         (static_cast<uint32_t>(__bfloat16_as_ushort(__float2bfloat16_rn(b))) << 16);
+}
+
+// Eight f32 values as three bf16 planes (8 bf16 each): v = hi + mid + lo.
+__device__ __forceinline__ void split8(const float (&v)[8], uint4 (&p)[3]) {
+  float r1[8], r2[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    r1[i] = v[i] - __bfloat162float(__float2bfloat16_rn(v[i]));
+    r2[i] = r1[i] - __bfloat162float(__float2bfloat16_rn(r1[i]));
+  }
+  p[0] = make_uint4(bf16_pair(v[0], v[1]), bf16_pair(v[2], v[3]), bf16_pair(v[4], v[5]), bf16_pair(v[6], v[7]));
+  p[1] = make_uint4(bf16_pair(r1[0], r1[1]), bf16_pair(r1[2], r1[3]), bf16_pair(r1[4], r1[5]),
+                    bf16_pair(r1[6], r1[7]));
+  p[2] = make_uint4(bf16_pair(r2[0], r2[1]), bf16_pair(r2[2], r2[3]), bf16_pair(r2[4], r2[5]),
+                    bf16_pair(r2[6], r2[7]));
+}
+
+__device__ __forceinline__ void load8(const float* p, float (&v)[8]) {
+  const float4 a = __ldg(reinterpret_cast<const float4*>(p));
+  const float4 b = __ldg(reinterpret_cast<const float4*>(p + 4));
+  v[0] = a.x, v[1] = a.y, v[2] = a.z, v[3] = a.w, v[4] = b.x, v[5] = b.y, v[6] = b.z, v[7] = b.w;
+}
+
+// c += (A planes of rows g, g+8) x (B planes): 32 columns.
+template <int NA>
+__device__ __forceinline__ void step(float (&c)[4], const uint4 (&ra)[NA], const uint4 (&rb)[NA], const uint4 (&b)[3]) {
+#pragma unroll
+  for (int i = 0; i < NA; ++i)
+#pragma unroll
+    for (int j = 0; j < 3; ++j) {
+      mma_bf16(c, ra[i].x, rb[i].x, ra[i].y, rb[i].y, b[j].x, b[j].y);
+      mma_bf16(c, ra[i].z, rb[i].z, ra[i].w, rb[i].w, b[j].z, b[j].w);
+    }
+}
+
+__device__ __forceinline__ void prefetch_l2(const void* p, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
+
+template <bool F32W>
+__global__ void __launch_bounds__(kThreads) linear_rows_kernel(const void* __restrict__ w, const float* __restrict__ x,
+                                                               float* __restrict__ y, int n, int k, int t_total) {
+  using Elem = typename std::conditional<F32W, float, __nv_bfloat16>::type;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+  const int tile = blockIdx.x, c0 = blockIdx.y * kPass, span = k / kWarps;
+  const Elem* wr = static_cast<const Elem*>(w) + static_cast<int64_t>(16 * tile + g) * k;
+  if (lane < 16)
+    prefetch_l2(static_cast<const Elem*>(w) + static_cast<int64_t>(16 * tile + lane) * k + warp * span,
+                static_cast<uint32_t>(span * sizeof(Elem)));
+  pdl_wait();  // x comes from earlier kernels
+  pdl_launch_dependents();
+  const int tok = c0 + g;
+  const float* xr = x + static_cast<int64_t>(min(tok, t_total - 1)) * k;
+  float c[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll 2
+  for (int k0 = warp * span; k0 < (warp + 1) * span; k0 += 32) {
+    const int col = k0 + 8 * t;
+    constexpr int NA = F32W ? 3 : 1;
+    uint4 ra[NA], rb[NA];
+    if constexpr (F32W) {
+      float va[8], vb[8];
+      load8(reinterpret_cast<const float*>(wr) + col, va);
+      load8(reinterpret_cast<const float*>(wr) + 8 * static_cast<int64_t>(k) + col, vb);
+      split8(va, ra);
+      split8(vb, rb);
+    } else {
+      ra[0] = __ldg(reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(wr) + col));
+      rb[0] = __ldg(reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(wr) +
+                                                   8 * static_cast<int64_t>(k) + col));
+    }
+    float xv[8];
+    load8(xr + col, xv);
+    if (tok >= t_total)
+#pragma unroll
+      for (int i = 0; i < 8; ++i) xv[i] = 0.f;
+    uint4 b[3];
+    split8(xv, b);
+    step<NA>(c, ra, rb, b);
+  }
+  __shared__ float4 red[kWarps][32];
+  red[warp][lane] = make_float4(c[0], c[1], c[2], c[3]);
+  __syncthreads();
+  if (threadIdx.x < 16 * kPass) {  // (row r, token v) of the pass, K slices summed in order
+    const int r = threadIdx.x & 15, v = threadIdx.x >> 4;
+    const int src = (r & 7) * 4 + (v >> 1), reg = (r >> 3) * 2 + (v & 1);
+    float s = 0.f;
+#pragma unroll
+    for (int i = 0; i < kWarps; ++i) s += reinterpret_cast<const float*>(&red[i][src])[reg];
+    if (c0 + v < t_total) y[static_cast<int64_t>(c0 + v) * n + 16 * tile + r] = s;
+  }
+}
+
+}  // namespace
+
+int linear_rows(const void* w, int w_dtype, const float* x, float* y, int64_t n, int64_t k, int64_t t,
+                cudaStream_t stream) {
+  if (!w || !x || !y || n < 1 || k < 1 || t < 1) return fail(BT_ERR_INVALID, "linear_rows: bad arguments");
+  if (w_dtype != BT_BF16 && w_dtype != BT_F32) return fail(BT_ERR_UNSUPPORTED, "linear_rows: weights bf16 or f32");
+  if (n % 16 || k % 256 || n / 16 > 2147483647LL || (t + kPass - 1) / kPass > 65535)
+    return fail(BT_ERR_UNSUPPORTED, "linear_rows: N must be a multiple of 16 and K of 256 (got %lld x %lld)",
+                static_cast<long long>(n), static_cast<long long>(k));
+  if ((reinterpret_cast<uintptr_t>(w) | reinterpret_cast<uintptr_t>(x)) & 15)
+    return fail(BT_ERR_INVALID, "linear_rows: w and x must be 16-byte aligned");
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(n / 16), static_cast<unsigned>((t + kPass - 1) / kPass));
+  cfg.blockDim = dim3(kThreads);
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const int nn = static_cast<int>(n), kk = static_cast<int>(k), tt = static_cast<int>(t);
+  const cudaError_t e = w_dtype == BT_F32 ? cudaLaunchKernelEx(&cfg, linear_rows_kernel<true>, w, x, y, nn, kk, tt)
+                                          : cudaLaunchKernelEx(&cfg, linear_rows_kernel<false>, w, x, y, nn, kk, tt);
+  if (e != cudaSuccess) return fail_cuda(e, "linear_rows launch");
+  return BT_OK;
+}
+
+}  // namespace bt

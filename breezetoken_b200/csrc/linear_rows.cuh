@@ -1,0 +1,11 @@
+// Dense projection by bf16 / f32 weight rows (see linear_rows.cu).
+#pragma once
+
+#include "common.cuh"
+
+namespace bt {
+
+int linear_rows(const void* w, int w_dtype, const float* x, float* y, int64_t n, int64_t k, int64_t t,
+                cudaStream_t stream);
+
+}  // namespace bt

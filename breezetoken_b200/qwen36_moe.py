@@ -1,0 +1,329 @@
+"""Qwen3.6-35B-A3B-shaped (qwen35moe) decoder on the B200 library.
+
+Mirrors breezetoken/model/qwen36_moe.py: the same config keys, weight names
+and orientation, and per-token math -- forward_token (:646-664), _attn
+(:432-457), _gdn (:459-483), _moe (:634-642).  The projections (bf16 / f32
+weight rows), RMSNorms, RoPE, attention, gated-delta step, routing, IQ3_S
+experts + shared expert and argmax run on this library's kernels; the
+elementwise glue between them (conv window, output gates, residual adds, KV
+writes) runs as torch device ops, as in the reference's model layer.
+
+B sequences decode in lockstep at one position (how BASELINE config 5's 64
+sequences per GPU run).  Prompts are fed token by token: the reference
+switches to a batched prefill with bf16 expert math for prompts of 8 or more
+tokens (_prefill_batch, :588-612), which this mirror does not reproduce.
+Everything raises on an unsupported shape or a missing library.
+"""
+
+from __future__ import annotations
+
+from collections.abc import Sequence
+from dataclasses import dataclass
+
+import numpy as np
+import torch
+
+from breezetoken_b200 import _native as N
+from breezetoken_b200.backends import B200Backend, _stream, resolve_device
+from breezetoken_b200.gguf import GGML_BF16, GGML_F32, GGUFFile
+from breezetoken_b200.moe import IQ3SExperts, SharedExpert, moe_forward, route_logits
+
+
+@dataclass(frozen=True)
+class Qwen36Config:
+    """model/qwen36_moe.py Qwen36Config (from the qwen35moe GGUF metadata)."""
+
+    hidden: int
+    n_layers: int
+    n_heads: int
+    n_kv: int
+    head_dim: int
+    rope_dim: int
+    rope_theta: float
+    max_context: int
+    n_experts: int
+    top_k: int
+    expert_ffn: int
+    shared_ffn: int
+    gdn_key_heads: int
+    gdn_value_heads: int
+    gdn_k_dim: int
+    gdn_inner: int
+    gdn_conv: int
+    vocab: int
+    eps: float
+    l2_eps: float = 1e-6
+
+    @property
+    def attn_layers(self) -> tuple[int, ...]:
+        return tuple(i for i in range(self.n_layers) if (i + 1) % 4 == 0)
+
+    @property
+    def conv_dim(self) -> int:
+        return 2 * self.gdn_key_heads * self.gdn_k_dim + self.gdn_inner
+
+    @property
+    def gdn_value_dim(self) -> int:
+        return self.gdn_inner // self.gdn_value_heads
+
+    @classmethod
+    def from_gguf(cls, gguf: GGUFFile, max_context: int | None = None) -> Qwen36Config:
+        md = gguf.metadata
+        a = "qwen35moe."
+        ctx = int(md.get(a + "context_length", 262144))
+        want = 8192 if max_context is None else int(max_context)
+        if want <= 0:
+            raise ValueError("max_context must be positive")
+        return cls(
+            hidden=int(md[a + "embedding_length"]),
+            n_layers=int(md[a + "block_count"]) - int(md.get(a + "nextn_predict_layers", 0)),
+            n_heads=int(md[a + "attention.head_count"]),
+            n_kv=int(md[a + "attention.head_count_kv"]),
+            head_dim=int(md[a + "attention.key_length"]),
+            rope_dim=int(md.get(a + "rope.dimension_count", 64)),
+            rope_theta=float(md.get(a + "rope.freq_base", 1.0e7)),
+            max_context=min(ctx, want),
+            n_experts=int(md[a + "expert_count"]),
+            top_k=int(md[a + "expert_used_count"]),
+            expert_ffn=int(md[a + "expert_feed_forward_length"]),
+            shared_ffn=int(md[a + "expert_shared_feed_forward_length"]),
+            gdn_key_heads=int(md[a + "ssm.group_count"]),
+            gdn_value_heads=int(md[a + "ssm.inner_size"]) // int(md[a + "ssm.state_size"]),
+            gdn_k_dim=int(md[a + "ssm.state_size"]),
+            gdn_inner=int(md[a + "ssm.inner_size"]),
+            gdn_conv=int(md[a + "ssm.conv_kernel"]),
+            vocab=int(gguf.tensor_info("token_embd.weight")[0][0]),
+            eps=float(md.get(a + "attention.layer_norm_rms_epsilon", 1e-6)),
+        )
+
+
+def rope_tables(cfg: Qwen36Config) -> tuple[torch.Tensor, torch.Tensor]:
+    """model/qwen36_moe.py:226-229 on the CPU in f32, widened to the full
+    rotary width (cos | cos, sin | sin) the RoPE kernel reads."""
+    half = cfg.rope_dim // 2
+    inv = cfg.rope_theta ** (-torch.arange(0, half, dtype=torch.float32) / half)
+    phases = torch.outer(torch.arange(cfg.max_context, dtype=torch.float32), inv)
+    cos, sin = phases.cos(), phases.sin()
+    return torch.cat([cos, cos], 1).contiguous(), torch.cat([sin, sin], 1).contiguous()
+
+
+class Qwen36Moe:
+    """A loaded qwen35moe decoder: ``forward_token`` / ``generate`` keep the
+    reference's names and argument meaning; ``decode_batch`` steps B
+    sequences together."""
+
+    def __init__(self, gguf: GGUFFile | str, *, device: str = "cuda", max_context: int | None = None,
+                 batch: int = 1) -> None:
+        own = not isinstance(gguf, GGUFFile)
+        g = GGUFFile(gguf) if own else gguf
+        try:
+            self.cfg = Qwen36Config.from_gguf(g, max_context)
+            self.device = resolve_device(device)
+            self.batch = int(batch)
+            self._load(g)
+        finally:
+            if own:
+                g.close()
+        self._alloc()
+
+    # ------------------------------------------------------------------ load
+    def _rows(self, g: GGUFFile, name: str) -> torch.Tensor:
+        """A 2-D bf16 or f32 weight in its (out, in) orientation."""
+        shape, ttype, _ = g.tensor_layout(name)
+        raw = torch.from_numpy(np.array(g.raw(name)))  # a writable copy of the mapped bytes
+        if ttype == GGML_BF16:
+            t = raw.view(torch.int16).view(torch.bfloat16)
+        elif ttype == GGML_F32:
+            t = raw.view(torch.float32)
+        else:
+            raise ValueError(f"{name}: dense weights must be bf16 or f32")
+        return t.reshape(shape).to(self.device).contiguous()
+
+    def _vec(self, g: GGUFFile, name: str) -> torch.Tensor:
+        return torch.from_numpy(np.array(g.f32(name))).to(self.device).contiguous()
+
+    def _load(self, g: GGUFFile) -> None:
+        cfg = self.cfg
+        self.embd = self._rows(g, "token_embd.weight")
+        self.head = self._rows(g, "output.weight")
+        self.norm_f = self._vec(g, "output_norm.weight")
+        self.layers: list[dict] = []
+        attn = set(cfg.attn_layers)
+        for i in range(cfg.n_layers):
+            p = f"blk.{i}."
+            layer = {
+                "norm_in": self._vec(g, p + "attn_norm.weight"),
+                "norm_post": self._vec(g, p + "post_attention_norm.weight"),
+                "router": self._rows(g, p + "ffn_gate_inp.weight").float().contiguous(),
+                "experts": IQ3SExperts.from_gguf_bytes(
+                    g.raw(p + "ffn_gate_exps.weight"), g.raw(p + "ffn_up_exps.weight"),
+                    g.raw(p + "ffn_down_exps.weight"), cfg.n_experts, cfg.hidden, cfg.expert_ffn, self.device),
+                "shared": SharedExpert.from_tensors(
+                    self._rows(g, p + "ffn_gate_shexp.weight"), self._rows(g, p + "ffn_up_shexp.weight"),
+                    self._rows(g, p + "ffn_down_shexp.weight"), self._vec(g, p + "ffn_gate_inp_shexp.weight"),
+                    self.device),
+            }
+            if i in attn:
+                layer.update(
+                    q=self._rows(g, p + "attn_q.weight"), k=self._rows(g, p + "attn_k.weight"),
+                    v=self._rows(g, p + "attn_v.weight"), o=self._rows(g, p + "attn_output.weight"),
+                    q_norm=self._vec(g, p + "attn_q_norm.weight"), k_norm=self._vec(g, p + "attn_k_norm.weight"),
+                )
+            else:
+                layer.update(
+                    qkv=self._rows(g, p + "attn_qkv.weight"), z=self._rows(g, p + "attn_gate.weight"),
+                    out=self._rows(g, p + "ssm_out.weight"),
+                    conv=self._vec(g, p + "ssm_conv1d.weight").reshape(cfg.conv_dim, cfg.gdn_conv),
+                    w_alpha=self._rows(g, p + "ssm_alpha.weight").float().contiguous(),
+                    w_beta=self._rows(g, p + "ssm_beta.weight").float().contiguous(),
+                    a_log=self._vec(g, p + "ssm_a"), dt_bias=self._vec(g, p + "ssm_dt.bias"),
+                    ssm_norm=self._vec(g, p + "ssm_norm.weight"),
+                )
+            self.layers.append(layer)
+
+    def _alloc(self) -> None:
+        cfg, b, dev = self.cfg, self.batch, self.device
+        self.backend = B200Backend(dev)
+        self.rope_cos, self.rope_sin = (t.to(dev) for t in rope_tables(cfg))
+        self.kv = {i: (torch.zeros(b, cfg.max_context, cfg.n_kv, cfg.head_dim, device=dev),
+                       torch.zeros(b, cfg.max_context, cfg.n_kv, cfg.head_dim, device=dev))
+                   for i in cfg.attn_layers}
+        dv = cfg.gdn_value_dim
+        self.conv_state = {i: torch.zeros(b, cfg.conv_dim, cfg.gdn_conv - 1, device=dev)
+                           for i in range(cfg.n_layers) if i not in self.kv}
+        self.rec_state = {i: torch.zeros(b, cfg.gdn_value_heads, cfg.gdn_k_dim, dv, device=dev)
+                          for i in self.conv_state}
+        splits = self._splits()
+        nbytes = int(N.load().bt_attention_workspace_bytes(b, cfg.n_kv, cfg.n_heads, cfg.head_dim, splits))
+        self._attn_ws = torch.zeros(max(nbytes, 256), dtype=torch.uint8, device=dev)
+        self._moe_ws = torch.zeros(int(N.load().bt_moe_layer_workspace_bytes(
+            b, cfg.hidden, cfg.expert_ffn, cfg.shared_ffn, cfg.n_experts, cfg.top_k)), dtype=torch.uint8, device=dev)
+
+    def _splits(self) -> int:
+        return max(1, min(16, self.cfg.max_context // 256))
+
+    def reset(self) -> None:
+        for st in (*self.conv_state.values(), *self.rec_state.values()):
+            st.zero_()
+
+    def close(self) -> None:
+        self.layers.clear()
+        self.kv.clear()
+        self.backend.close()
+
+    # ------------------------------------------------------------------ ops
+    def _lin(self, w: torch.Tensor, x: torch.Tensor) -> torch.Tensor:
+        """x (T, K) f32 -> (T, N) f32 through weight rows w (N, K)."""
+        n, k = w.shape
+        x2 = x.float().reshape(-1, k).contiguous()
+        y = torch.empty(x2.shape[0], n, dtype=torch.float32, device=self.device)
+        dt = N.BT_BF16 if w.dtype == torch.bfloat16 else N.BT_F32
+        N.call("bt_linear_rows", w.data_ptr(), dt, x2.data_ptr(), y.data_ptr(), n, k, x2.shape[0], _stream())
+        return y
+
+    def _rms(self, x: torch.Tensor, gamma: torch.Tensor) -> torch.Tensor:
+        return self.backend.rms_norm(x, gamma, self.cfg.eps)
+
+    def _rope(self, x: torch.Tensor, pos_t: torch.Tensor) -> torch.Tensor:
+        return self.backend.rope(x, self.rope_cos, self.rope_sin, pos_t, self.cfg.rope_dim)
+
+    def _attn(self, i: int, xn: torch.Tensor, pos: int, pos_t: torch.Tensor) -> torch.Tensor:
+        cfg, layer = self.cfg, self.layers[i]
+        b, H, D = xn.shape[0], cfg.n_heads, cfg.head_dim
+        q_full = self._lin(layer["q"], xn).view(b, H, 2 * D)
+        q, gate = q_full[..., :D].contiguous(), q_full[..., D:]
+        k = self._lin(layer["k"], xn).view(b, cfg.n_kv, D)
+        v = self._lin(layer["v"], xn).view(b, cfg.n_kv, D)
+        q = self._rope(self._rms(q, layer["q_norm"]), pos_t)
+        k = self._rope(self._rms(k, layer["k_norm"]), pos_t)
+        k_cache, v_cache = self.kv[i]
+        k_cache[:, pos] = k
+        v_cache[:, pos] = v
+        lens = torch.full((b,), pos + 1, dtype=torch.int32, device=self.device)
+        out = torch.empty(b, H, D, dtype=torch.float32, device=self.device)
+        N.call("bt_attention_decode", q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), N.BT_F32,
+               lens.data_ptr(), out.data_ptr(), b, H, cfg.n_kv, D, cfg.max_context, float(D ** -0.5),
+               self._splits(), self._attn_ws.data_ptr(), _stream())
+        out = out * torch.sigmoid(gate)
+        return self._lin(layer["o"], out.reshape(b, -1))
+
+    def _gdn(self, i: int, xn: torch.Tensor) -> torch.Tensor:
+        cfg, layer = self.cfg, self.layers[i]
+        b, hk, hv, dk = xn.shape[0], cfg.gdn_key_heads, cfg.gdn_value_heads, cfg.gdn_k_dim
+        inner = cfg.gdn_inner
+        entry = self._lin(layer["qkv"], xn)  # (B, C)
+        conv = self.conv_state[i]
+        window = torch.cat((conv, entry.unsqueeze(2)), dim=2)  # (B, C, conv)
+        mixed = torch.nn.functional.silu((window * layer["conv"]).sum(dim=-1))
+        conv.copy_(window[:, :, 1:])
+        q = mixed[:, : inner // 2].reshape(b, hk, dk).contiguous()
+        k = mixed[:, inner // 2 : inner].reshape(b, hk, dk).contiguous()
+        v = mixed[:, inner:].reshape(b, hv, dk).contiguous()
+        beta = self._lin(layer["w_beta"], xn)
+        g = layer["a_log"] * torch.nn.functional.softplus(self._lin(layer["w_alpha"], xn) + layer["dt_bias"])
+        read = torch.empty(b, hv, cfg.gdn_value_dim, dtype=torch.float32, device=self.device)
+        N.call("bt_gdn_decode", q.data_ptr(), k.data_ptr(), v.data_ptr(), N.BT_F32, g.contiguous().data_ptr(),
+               beta.contiguous().data_ptr(), self.rec_state[i].data_ptr(), read.data_ptr(), b, hk, hv, dk,
+               float(dk ** -0.5), float(cfg.l2_eps), _stream())
+        z = self._lin(layer["z"], xn).view(b, hv, dk)
+        gated = (self._rms(read, layer["ssm_norm"]) * torch.nn.functional.silu(z)).reshape(b, -1)
+        return self._lin(layer["out"], gated)
+
+    def _moe(self, i: int, xn: torch.Tensor) -> torch.Tensor:
+        layer = self.layers[i]
+        r = route_logits(self._lin(layer["router"], xn), self.cfg.top_k)
+        return moe_forward(layer["experts"], layer["shared"], xn, r.expert_ids, r.weights, self._moe_ws)
+
+    # ------------------------------------------------------------------ step
+    @torch.inference_mode()
+    def _step(self, tokens: torch.Tensor, pos: int, logits: bool) -> torch.Tensor | None:
+        cfg = self.cfg
+        if not 0 <= pos < cfg.max_context:
+            raise ValueError(f"position {pos} outside [0, {cfg.max_context})")
+        if int(tokens.min()) < 0 or int(tokens.max()) >= cfg.vocab:
+            raise ValueError("token id outside the vocabulary")
+        pos_t = torch.full((1,), pos, dtype=torch.int32, device=self.device)
+        h = self.embd[tokens.long()].float()
+        attn = set(cfg.attn_layers)
+        for i in range(cfg.n_layers):
+            layer = self.layers[i]
+            xn = self._rms(h, layer["norm_in"])
+            h = h + (self._attn(i, xn, pos, pos_t) if i in attn else self._gdn(i, xn))
+            xn = self._rms(h, layer["norm_post"])
+            h = h + self._moe(i, xn)
+        if not logits:
+            return None
+        return self._lin(self.head, self._rms(h, self.norm_f))
+
+    def forward_token(self, token: int, pos: int, *, logits: bool = True) -> torch.Tensor | None:
+        """model/qwen36_moe.py:646-664 for sequence 0: (V,) f32 logits."""
+        if self.batch != 1:
+            raise ValueError("forward_token serves batch 1; use decode_batch")
+        out = self._step(torch.tensor([token], device=self.device), pos, logits)
+        return None if out is None else out[0]
+
+    def decode_batch(self, tokens: torch.Tensor, pos: int) -> torch.Tensor:
+        """One greedy step of the B sequences at position `pos`: next ids (B,) int32."""
+        if tokens.numel() != self.batch:
+            raise ValueError(f"expected {self.batch} tokens, got {tokens.numel()}")
+        return self.backend.argmax(self._step(tokens.reshape(-1).to(self.device), pos, True))
+
+    def generate(self, ids: Sequence[int], max_new: int) -> list[int]:
+        """Greedy decode of one sequence (model/qwen36_moe.py:893-900 with
+        temperature 0), the prompt fed token by token."""
+        if not ids:
+            raise ValueError("prompt must contain at least one token")
+        self.reset()
+        logits = None
+        for i, t in enumerate(ids):
+            logits = self.forward_token(int(t), i, logits=(i == len(ids) - 1))
+        out: list[int] = []
+        for step in range(max_new):
+            nxt = int(self.backend.argmax(logits)[0])
+            out.append(nxt)
+            if step + 1 < max_new:
+                logits = self.forward_token(nxt, len(ids) + step)
+        return out
+
+
+__all__ = ["Qwen36Config", "Qwen36Moe", "rope_tables"]

@@ -27,7 +27,7 @@ from pathlib import Path
 
 import numpy as np
 
-from breezetoken_b200.gguf import GGML_F32, GGML_IQ3_S, GGML_Q8_0, GGUFWriter
+from breezetoken_b200.gguf import GGML_BF16, GGML_F32, GGML_IQ3_S, GGML_Q8_0, GGUFWriter
 from breezetoken_b200.quant import quantize_iq3_s, quantize_q8_0
 
 CHUNK = 1 << 20
@@ -221,8 +221,162 @@ def make_moe_layer(spec: MoeSpec = MoeSpec(), seed: int = 3, n_experts: int | No
     return out
 
 
+# --------------------------------------------------------------------------
+# Qwen3.6-35B-A3B-shaped hybrid MoE decoder (qwen35moe GGUF)
+# --------------------------------------------------------------------------
+@dataclass(frozen=True)
+class Qwen36Spec:
+    """Shape of a qwen35moe decoder (BASELINE config 5 with the defaults)."""
+
+    hidden: int = 2048
+    n_layers: int = 40
+    n_heads: int = 16
+    n_kv: int = 2
+    head_dim: int = 256
+    rope_dim: int = 64
+    rope_theta: float = 1e7
+    vocab: int = 151936
+    n_experts: int = 256
+    top_k: int = 8
+    expert_ffn: int = 512
+    shared_ffn: int = 512
+    gdn_key_heads: int = 16
+    gdn_value_heads: int = 32
+    gdn_dim: int = 128
+    conv_k: int = 4
+    attn_interval: int = 4
+    eps: float = 1e-6
+    context_length: int = 262144
+
+    @property
+    def gdn_inner(self) -> int:
+        return self.gdn_value_heads * self.gdn_dim
+
+    @property
+    def conv_dim(self) -> int:
+        return 2 * self.gdn_key_heads * self.gdn_dim + self.gdn_inner
+
+
+#: BASELINE config 5.
+QWEN36_35B = Qwen36Spec()
+#: The config-5 layer shapes (hidden 2048, GQA 16/2x256, GDN 16K/32V x128,
+#: experts of ffn 512 + a shared expert) with one [GDN, GDN, GDN, GQA]
+#: period, 16 experts and a small vocabulary, for parity against the
+#: reference's CPU path.
+QWEN36_TINY = Qwen36Spec(n_layers=4, vocab=8192, n_experts=16)
+
+
+def qwen36_tensors(spec: Qwen36Spec) -> list[tuple[str, tuple[int, ...], str]]:
+    """(name, logical shape, role) of every tensor of a qwen35moe GGUF, in
+    the names and orientations model/qwen36_moe.py:259-307 loads."""
+    s = spec
+    t: list[tuple[str, tuple[int, ...], str]] = [
+        ("token_embd.weight", (s.vocab, s.hidden), "bf16"),
+        ("output.weight", (s.vocab, s.hidden), "bf16"),
+        ("output_norm.weight", (s.hidden,), "gamma"),
+    ]
+    for i in range(s.n_layers):
+        p = f"blk.{i}."
+        t += [
+            (p + "attn_norm.weight", (s.hidden,), "gamma"),
+            (p + "post_attention_norm.weight", (s.hidden,), "gamma"),
+            (p + "ffn_gate_inp.weight", (s.n_experts, s.hidden), "f32w"),
+            (p + "ffn_gate_inp_shexp.weight", (s.hidden,), "f32w"),
+            (p + "ffn_gate_shexp.weight", (s.shared_ffn, s.hidden), "bf16"),
+            (p + "ffn_up_shexp.weight", (s.shared_ffn, s.hidden), "bf16"),
+            (p + "ffn_down_shexp.weight", (s.hidden, s.shared_ffn), "bf16"),
+            (p + "ffn_gate_exps.weight", (s.n_experts, s.expert_ffn, s.hidden), "iq3s"),
+            (p + "ffn_up_exps.weight", (s.n_experts, s.expert_ffn, s.hidden), "iq3s"),
+            (p + "ffn_down_exps.weight", (s.n_experts, s.hidden, s.expert_ffn), "iq3s"),
+        ]
+        if (i + 1) % s.attn_interval == 0:
+            t += [
+                (p + "attn_q.weight", (2 * s.n_heads * s.head_dim, s.hidden), "bf16"),
+                (p + "attn_k.weight", (s.n_kv * s.head_dim, s.hidden), "bf16"),
+                (p + "attn_v.weight", (s.n_kv * s.head_dim, s.hidden), "bf16"),
+                (p + "attn_output.weight", (s.hidden, s.n_heads * s.head_dim), "bf16"),
+                (p + "attn_q_norm.weight", (s.head_dim,), "gamma"),
+                (p + "attn_k_norm.weight", (s.head_dim,), "gamma"),
+            ]
+        else:
+            t += [
+                (p + "attn_qkv.weight", (s.conv_dim, s.hidden), "bf16"),
+                (p + "attn_gate.weight", (s.gdn_inner, s.hidden), "bf16"),
+                (p + "ssm_conv1d.weight", (s.conv_dim, s.conv_k), "conv"),
+                (p + "ssm_alpha.weight", (s.gdn_value_heads, s.hidden), "f32w"),
+                (p + "ssm_beta.weight", (s.gdn_value_heads, s.hidden), "f32w"),
+                (p + "ssm_a", (s.gdn_value_heads,), "ssm_a"),
+                (p + "ssm_dt.bias", (s.gdn_value_heads,), "dt_bias"),
+                (p + "ssm_out.weight", (s.hidden, s.gdn_inner), "bf16"),
+                (p + "ssm_norm.weight", (s.gdn_dim,), "gamma"),
+            ]
+    return t
+
+
+def write_qwen36_gguf(path: str | Path, spec: Qwen36Spec = QWEN36_TINY, seed: int = 4) -> Path:
+    """Write a seeded random qwen35moe GGUF: bf16 projections, IQ3_S experts
+    (N(0, 0.02) before quantisation), f32 router, gate vectors, norms and
+    SSM parameters (distributions as for the Qwen3.5 checkpoints)."""
+    import torch  # noqa: PLC0415 - bf16 rounding
+
+    s = spec
+    w = GGUFWriter()
+    w.add("general.architecture", "qwen35moe")
+    w.add("general.name", f"synthetic-qwen35moe-seed{seed}")
+    w.add("general.alignment", 32)
+    a = "qwen35moe."
+    for key, val in (
+        ("block_count", s.n_layers), ("context_length", s.context_length), ("embedding_length", s.hidden),
+        ("attention.head_count", s.n_heads), ("attention.head_count_kv", s.n_kv),
+        ("attention.key_length", s.head_dim), ("attention.value_length", s.head_dim),
+        ("attention.layer_norm_rms_epsilon", float(s.eps)), ("rope.dimension_count", s.rope_dim),
+        ("rope.freq_base", float(s.rope_theta)), ("expert_count", s.n_experts), ("expert_used_count", s.top_k),
+        ("expert_feed_forward_length", s.expert_ffn), ("expert_shared_feed_forward_length", s.shared_ffn),
+        ("ssm.group_count", s.gdn_key_heads), ("ssm.inner_size", s.gdn_inner), ("ssm.state_size", s.gdn_dim),
+        ("ssm.conv_kernel", s.conv_k), ("full_attention_interval", s.attn_interval), ("nextn_predict_layers", 0),
+    ):
+        w.add(a + key, val)
+    with cf.ThreadPoolExecutor(_threads()) as pool:
+        for tid, (name, shape, role) in enumerate(qwen36_tensors(s)):
+            n = int(np.prod(shape))
+            if role == "bf16":
+                vals = _fill(seed, tid, n, "normal", pool) * np.float32(0.02)
+                bf = torch.from_numpy(vals).to(torch.bfloat16).view(torch.int16).numpy().view(np.uint16)
+                w.add_tensor(name, shape, GGML_BF16, bf.reshape(shape))
+                continue
+            if role == "iq3s":
+                k = shape[-1]
+                rows = n // k
+                vals = (_fill(seed, tid, n, "normal", pool) * np.float32(0.02)).reshape(rows, k)
+                step = max(1, CHUNK // k)
+                parts = list(pool.map(lambda r, v=vals: quantize_iq3_s(v[r : r + step]), range(0, rows, step)))
+                w.add_tensor(name, shape, GGML_IQ3_S, np.concatenate(parts, axis=0))
+                continue
+            if role == "gamma":
+                vals = np.float32(1.0) + _fill(seed, tid, n, "normal", pool) * np.float32(0.02)
+            elif role == "f32w":
+                vals = _fill(seed, tid, n, "normal", pool) * np.float32(0.02)
+            elif role == "conv":
+                vals = _fill(seed, tid, n, "normal", pool) * np.float32(0.25)
+            elif role == "ssm_a":
+                vals = -np.exp(_fill(seed, tid, n, "uniform", pool) * np.float32(np.log(16.0)))
+            elif role == "dt_bias":
+                u = _fill(seed, tid, n, "uniform", pool)
+                dt = np.exp(np.log(1e-3) + u * (np.log(1e-1) - np.log(1e-3)))
+                vals = np.log(np.expm1(dt))
+            else:
+                raise AssertionError(role)
+            w.add_tensor(name, shape, GGML_F32, np.asarray(vals, dtype=np.float32).reshape(shape))
+    return w.write(path)
+
+
 __all__ = [
     "GGML_IQ3_S",
+    "QWEN36_35B",
+    "QWEN36_TINY",
+    "Qwen36Spec",
+    "qwen36_tensors",
+    "write_qwen36_gguf",
     "MoeSpec",
     "QWEN35_0_8B",
     "QWEN35_TINY",

@@ -87,6 +87,14 @@ BT_API int bt_linear_q8(const void* w, const float* x, float* y, int64_t n, int6
 BT_API int bt_linear_kn(const void* w, int w_dtype, const float* x, float* y,
                  int64_t k, int64_t n, void* stream);
 
+/* Qwen36Moe._linear / _linear_b (model/qwen36_moe.py:352-358) for T
+ * tokens: y[t][n] = sum_k W[n][k] * x[t][k] with W (N, K) rows in the GGUF
+ * (out, in) orientation, bf16 or f32 (w_dtype), on the tensor cores with
+ * both operands carried to 24 bits.  x (T, K), y (T, N) f32; N % 16 == 0,
+ * K % 256 == 0; w and x 16-byte aligned.                                  */
+BT_API int bt_linear_rows(const void* w, int w_dtype, const float* x, float* y,
+                   int64_t n, int64_t k, int64_t t, void* stream);
+
 /* Backend.rms_norm (backends.py:119-123) over rows of length n.           */
 BT_API int bt_rms_norm(const float* x, const float* w, float* y, int64_t rows,
                 int64_t n, float eps, void* stream);

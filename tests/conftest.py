@@ -39,6 +39,13 @@ def gguf_0_8b(tmp_path_factory) -> Path:
 
 
 @pytest.fixture(scope="session")
+def qwen36_tiny_gguf(tmp_path_factory) -> Path:
+    from breezetoken_b200.synth import QWEN36_TINY, write_qwen36_gguf
+
+    return write_qwen36_gguf(tmp_path_factory.mktemp("q36") / "q36.gguf", QWEN36_TINY, seed=4)
+
+
+@pytest.fixture(scope="session")
 def cuda():
     import torch
 

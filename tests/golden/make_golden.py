@@ -15,6 +15,9 @@ records, on seeded inputs, what its torch f32 path computes:
   shape) and one ``ExpertPool``-style expert evaluation from IQ3_S bytes;
 * ``moe_shared.npz`` -- ``Qwen36Moe._moe`` (routed output + gated bf16 shared
   expert) run on a stand-in object around moe.npz's routed output;
+* ``qwen36_tiny.npz`` -- greedy token ids, top-2 margins and the first
+  logits of the reference's ``Qwen36Moe`` (CPU, f32) on the seeded tiny
+  qwen35moe checkpoint (BASELINE config 5 layer shapes);
 * ``qwen35_tiny.npz`` / ``qwen35_0_8b.npz`` -- greedy token ids of
   ``Qwen35(backend="torch", device="cpu").generate`` on the seeded synthetic
   checkpoints of breezetoken_b200.synth, with per-step top-2 logit margins and
@@ -236,6 +239,39 @@ def gen_moe_shared(out: Path) -> None:
     np.savez_compressed(out, y=y.numpy())
 
 
+def gen_qwen36_tiny(out: Path, steps: int = 24) -> None:
+    """Greedy decode of the reference's Qwen36Moe (model/qwen36_moe.py,
+    device="cpu", dtype="f32") on the seeded tiny qwen35moe checkpoint of
+    breezetoken_b200.synth (BASELINE config 5 layer shapes, 4 layers, 16
+    experts).  The 7-token prompt stays below the reference's batched-prefill
+    threshold (8 tokens), so every token takes its per-token f32 path."""
+    from breezetoken.model.qwen36_moe import Qwen36Moe
+
+    from breezetoken_b200.synth import QWEN36_TINY, write_qwen36_gguf
+
+    with tempfile.TemporaryDirectory() as d:
+        path = write_qwen36_gguf(Path(d) / "q36.gguf", QWEN36_TINY, seed=4)
+        m = Qwen36Moe(str(path), device="cpu", dtype="f32", max_context=64)
+        prompt = np.random.default_rng(4).integers(0, QWEN36_TINY.vocab, 7).tolist()
+        t0 = time.time()
+        with torch.inference_mode():
+            m.reset()
+            for i, tok in enumerate(prompt):
+                logits = m.forward_token(tok, i, logits=(i == len(prompt) - 1))
+            tokens, margins, first = [], [], logits.numpy().copy()
+            for step in range(steps):
+                top2 = torch.topk(logits, 2).values
+                margins.append(float(top2[0] - top2[1]))
+                tok = int(logits.argmax())
+                tokens.append(tok)
+                if step + 1 < steps:
+                    logits = m.forward_token(tok, len(prompt) + step, logits=True)
+        np.savez_compressed(
+            out, prompt=np.array(prompt), tokens=np.array(tokens), margins=np.array(margins, dtype=np.float32),
+            logits=first[None], steps=np.array(steps), max_context=np.array(64), seconds=np.array(time.time() - t0),
+        )
+
+
 def gen_model(out: Path, spec, steps: int, max_context: int, keep_logits: int) -> None:
     from breezetoken.gguf import GGUFFile
     from breezetoken.model.qwen35 import Qwen35
@@ -280,10 +316,14 @@ def main() -> None:
     if args.only == "moe_shared":
         gen_moe_shared(HERE / "moe_shared.npz")
         return
+    if args.only == "qwen36_tiny":
+        gen_qwen36_tiny(HERE / "qwen36_tiny.npz")
+        return
     gen_dequant(HERE / "dequant.npz")
     gen_ops(HERE / "ops.npz")
     gen_moe(HERE / "moe.npz")
     gen_moe_shared(HERE / "moe_shared.npz")
+    gen_qwen36_tiny(HERE / "qwen36_tiny.npz")
     gen_model(HERE / "qwen35_tiny.npz", QWEN35_TINY, steps=32, max_context=512, keep_logits=4)
     if not args.skip_0_8b:
         gen_model(HERE / "qwen35_0_8b.npz", QWEN35_0_8B, steps=128, max_context=1024, keep_logits=1)

@@ -1,0 +1,94 @@
+"""GPU parity of the config-5 (Qwen3.6-35B-A3B-shaped, qwen35moe) decoder.
+
+The tiny checkpoint has the config-5 layer shapes (hidden 2048, GQA 16q/2kv
+x 256, GDN 16 key / 32 value heads x 128, IQ3_S experts of ffn 512 + a bf16
+shared expert) with 4 layers and 16 experts.  Greedy tokens must be
+identical to the reference's Qwen36Moe (CPU, f32) over 24 steps; the first
+logits within 1e-4 of the logit scale.  The golden fixture records the top-2
+margin of every step.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from breezetoken_b200 import _native as N
+from breezetoken_b200.qwen36_moe import Qwen36Moe
+from tests.conftest import golden
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def model(cuda, qwen36_tiny_gguf):
+    m = Qwen36Moe(qwen36_tiny_gguf, max_context=int(golden("qwen36_tiny")["max_context"]))
+    yield m
+    m.close()
+
+
+def test_qwen36_first_logits_match_reference(model) -> None:
+    g = golden("qwen36_tiny")
+    prompt = g["prompt"].tolist()
+    model.reset()
+    for i, t in enumerate(prompt):
+        logits = model.forward_token(t, i, logits=(i == len(prompt) - 1))
+    got, want = logits.cpu().numpy(), g["logits"][0]
+    assert np.abs(got - want).max() <= 1e-4 * np.abs(want).max()
+
+
+def test_qwen36_greedy_tokens_match_reference(model) -> None:
+    g = golden("qwen36_tiny")
+    got = model.generate(g["prompt"].tolist(), int(g["steps"]))
+    want = g["tokens"].tolist()
+    first = next((i for i, (a, b) in enumerate(zip(got, want, strict=True)) if a != b), None)
+    assert got == want, f"first mismatch at {first} (margins {g['margins'][:8]})"
+
+
+def test_qwen36_batch_lockstep(cuda, qwen36_tiny_gguf, model) -> None:
+    """Four sequences decoded together match each decoded alone."""
+    g = golden("qwen36_tiny")
+    p0 = g["prompt"].tolist()
+    rng = np.random.default_rng(11)
+    prompts = [p0] + [rng.integers(0, 8192, len(p0)).tolist() for _ in range(3)]
+    solo = [model.generate(p, 6) for p in prompts]
+    mb = Qwen36Moe(qwen36_tiny_gguf, max_context=64, batch=4)
+    try:
+        toks = torch.tensor([p[0] for p in prompts], device="cuda")
+        for i in range(1, len(p0)):
+            mb._step(toks, i - 1, logits=False)
+            toks = torch.tensor([p[i] for p in prompts], device="cuda")
+        together = [[] for _ in prompts]
+        for step in range(6):
+            toks = mb.decode_batch(toks, len(p0) - 1 + step)
+            for b, t in enumerate(toks.tolist()):
+                together[b].append(t)
+    finally:
+        mb.close()
+    assert together == solo
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+@pytest.mark.parametrize("t", [1, 5, 20])
+def test_linear_rows_matches_f64(cuda, dtype, t) -> None:
+    """y = x W^T against an f64 product: within 2e-6 of sum |x||w| per output."""
+    rng = np.random.default_rng(12)
+    n, k = 96, 512
+    w = torch.from_numpy(rng.standard_normal((n, k)).astype(np.float32) * 0.02).to(dtype)
+    x = torch.from_numpy(rng.standard_normal((t, k)).astype(np.float32))
+    y = torch.empty(t, n, device="cuda")
+    wd, xd = w.cuda().contiguous(), x.cuda().contiguous()
+    N.call("bt_linear_rows", wd.data_ptr(), N.BT_BF16 if dtype == torch.bfloat16 else N.BT_F32, xd.data_ptr(),
+           y.data_ptr(), n, k, t, 0)
+    wf = w.double().numpy()
+    want = x.double().numpy() @ wf.T
+    bound = np.abs(x.double().numpy()) @ np.abs(wf).T
+    assert (np.abs(y.cpu().double().numpy() - want) <= 2e-6 * bound).all()
+
+
+def test_linear_rows_rejects_bad_shapes(cuda) -> None:
+    buf = torch.zeros(1 << 16, dtype=torch.uint8, device="cuda")
+    p = buf.data_ptr()
+    assert N.load().bt_linear_rows(p, N.BT_BF16, p, p, 24, 512, 1, 0) == N.BT_ERR_UNSUPPORTED
+    assert N.load().bt_linear_rows(p, N.BT_BF16, p, p, 32, 500, 1, 0) == N.BT_ERR_UNSUPPORTED
