@@ -4,9 +4,11 @@
 // _linear_b of model/qwen36_moe.py:352-358 in its f32 form (weights exact in
 // f32, activations f32).
 //
-// One block per 16-row tile and 8-token pass (grid (N/16, ceil(T/8))); its 8
-// warps split K.  Per 32-column step a lane loads weights 8t .. 8t+7 of rows
-// g and g+8 (16-byte loads; the k order inside the step is permuted
+// One block per 16-row tile and up to 8 passes of 8 tokens (grid (N/16,
+// ceil(T/64)) for T > 32); its 8 warps split K, and every pass reuses the
+// weight fragments a warp loaded, so the weights are read once per 64
+// tokens.  Per 32-column step a lane loads weights 8t .. 8t+7 of rows g and
+// g+8 (16-byte loads; the k order inside the step is permuted
 // identically on both MMA operands) and the same columns of token column g's
 // x.  x is split into three bf16 planes (x = hi + mid + lo, each remainder
 // exact in f32), f32 weights likewise; every plane product accumulates into
@@ -75,21 +77,22 @@ __device__ __forceinline__ void prefetch_l2(const void* p, uint32_t bytes) {
   asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
 }
 
-template <bool F32W>
+template <bool F32W, int NP>
 __global__ void __launch_bounds__(kThreads) linear_rows_kernel(const void* __restrict__ w, const float* __restrict__ x,
                                                                float* __restrict__ y, int n, int k, int t_total) {
   using Elem = typename std::conditional<F32W, float, __nv_bfloat16>::type;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
-  const int tile = blockIdx.x, c0 = blockIdx.y * kPass, span = k / kWarps;
+  const int tile = blockIdx.x, c0 = blockIdx.y * kPass * NP, span = k / kWarps;
   const Elem* wr = static_cast<const Elem*>(w) + static_cast<int64_t>(16 * tile + g) * k;
   if (lane < 16)
     prefetch_l2(static_cast<const Elem*>(w) + static_cast<int64_t>(16 * tile + lane) * k + warp * span,
                 static_cast<uint32_t>(span * sizeof(Elem)));
   pdl_wait();  // x comes from earlier kernels
   pdl_launch_dependents();
-  const int tok = c0 + g;
-  const float* xr = x + static_cast<int64_t>(min(tok, t_total - 1)) * k;
-  float c[4] = {0.f, 0.f, 0.f, 0.f};
+  const float* xr[NP];
+#pragma unroll
+  for (int p = 0; p < NP; ++p) xr[p] = x + static_cast<int64_t>(min(c0 + kPass * p + g, t_total - 1)) * k;
+  float c[NP][4] = {};
 #pragma unroll 2
   for (int k0 = warp * span; k0 < (warp + 1) * span; k0 += 32) {
     const int col = k0 + 8 * t;
@@ -106,25 +109,39 @@ __global__ void __launch_bounds__(kThreads) linear_rows_kernel(const void* __res
       rb[0] = __ldg(reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(wr) +
                                                    8 * static_cast<int64_t>(k) + col));
     }
-    float xv[8];
-    load8(xr + col, xv);
-    if (tok >= t_total)
 #pragma unroll
-      for (int i = 0; i < 8; ++i) xv[i] = 0.f;
-    uint4 b[3];
-    split8(xv, b);
-    step<NA>(c, ra, rb, b);
+    for (int p = 0; p < NP; ++p) {  // every pass reuses the weight fragments
+      float xv[8];
+      load8(xr[p] + col, xv);
+      if (c0 + kPass * p + g >= t_total)
+#pragma unroll
+        for (int i = 0; i < 8; ++i) xv[i] = 0.f;
+      uint4 b[3];
+      split8(xv, b);
+      step<NA>(c[p], ra, rb, b);
+    }
   }
-  __shared__ float4 red[kWarps][32];
-  red[warp][lane] = make_float4(c[0], c[1], c[2], c[3]);
+  __shared__ float4 red[kWarps][NP][32];
+#pragma unroll
+  for (int p = 0; p < NP; ++p) red[warp][p][lane] = make_float4(c[p][0], c[p][1], c[p][2], c[p][3]);
   __syncthreads();
-  if (threadIdx.x < 16 * kPass) {  // (row r, token v) of the pass, K slices summed in order
-    const int r = threadIdx.x & 15, v = threadIdx.x >> 4;
-    const int src = (r & 7) * 4 + (v >> 1), reg = (r >> 3) * 2 + (v & 1);
+  for (int i = threadIdx.x; i < 16 * kPass * NP; i += kThreads) {  // (row r, token v), K slices summed in order
+    const int r = i & 15, v = i >> 4, p = v / kPass, vv = v % kPass;
+    const int src = (r & 7) * 4 + (vv >> 1), reg = (r >> 3) * 2 + (vv & 1);
     float s = 0.f;
 #pragma unroll
-    for (int i = 0; i < kWarps; ++i) s += reinterpret_cast<const float*>(&red[i][src])[reg];
+    for (int j = 0; j < kWarps; ++j) s += reinterpret_cast<const float*>(&red[j][p][src])[reg];
     if (c0 + v < t_total) y[static_cast<int64_t>(c0 + v) * n + 16 * tile + r] = s;
+  }
+}
+
+template <bool F32W>
+cudaError_t launch_np(cudaLaunchConfig_t& cfg, int np, const void* w, const float* x, float* y, int n, int k, int t) {
+  switch (np) {
+    case 1: return cudaLaunchKernelEx(&cfg, linear_rows_kernel<F32W, 1>, w, x, y, n, k, t);
+    case 2: return cudaLaunchKernelEx(&cfg, linear_rows_kernel<F32W, 2>, w, x, y, n, k, t);
+    case 4: return cudaLaunchKernelEx(&cfg, linear_rows_kernel<F32W, 4>, w, x, y, n, k, t);
+    default: return cudaLaunchKernelEx(&cfg, linear_rows_kernel<F32W, 8>, w, x, y, n, k, t);
   }
 }
 
@@ -139,8 +156,10 @@ int linear_rows(const void* w, int w_dtype, const float* x, float* y, int64_t n,
                 static_cast<long long>(n), static_cast<long long>(k));
   if ((reinterpret_cast<uintptr_t>(w) | reinterpret_cast<uintptr_t>(x)) & 15)
     return fail(BT_ERR_INVALID, "linear_rows: w and x must be 16-byte aligned");
+  // passes of 8 tokens per block: the weights are read once per 64 tokens
+  const int np = t <= 8 ? 1 : t <= 16 ? 2 : t <= 32 ? 4 : 8;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(static_cast<unsigned>(n / 16), static_cast<unsigned>((t + kPass - 1) / kPass));
+  cfg.gridDim = dim3(static_cast<unsigned>(n / 16), static_cast<unsigned>((t + kPass * np - 1) / (kPass * np)));
   cfg.blockDim = dim3(kThreads);
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
@@ -149,8 +168,8 @@ int linear_rows(const void* w, int w_dtype, const float* x, float* y, int64_t n,
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   const int nn = static_cast<int>(n), kk = static_cast<int>(k), tt = static_cast<int>(t);
-  const cudaError_t e = w_dtype == BT_F32 ? cudaLaunchKernelEx(&cfg, linear_rows_kernel<true>, w, x, y, nn, kk, tt)
-                                          : cudaLaunchKernelEx(&cfg, linear_rows_kernel<false>, w, x, y, nn, kk, tt);
+  const cudaError_t e = w_dtype == BT_F32 ? launch_np<true>(cfg, np, w, x, y, nn, kk, tt)
+                                          : launch_np<false>(cfg, np, w, x, y, nn, kk, tt);
   if (e != cudaSuccess) return fail_cuda(e, "linear_rows launch");
   return BT_OK;
 }

@@ -4,6 +4,7 @@
     python -m breezetoken_b200.kernel_bench gdn --batch 64 --steps 256
     python -m breezetoken_b200.kernel_bench attn --batch 64 --ctx 32768
     python -m breezetoken_b200.kernel_bench moe --tokens 8
+    python -m breezetoken_b200.kernel_bench qwen36 --batch 64 --prompt 512 --steps 256
     python -m breezetoken_b200.kernel_bench trace --gguf model.gguf
 
 Each prints one JSON line: average launch time and achieved HBM GB/s from
@@ -13,6 +14,8 @@ the algorithmic bytes of one launch (weights / state / KV read once).
 timed per call after reading a 256 MB buffer (the experts are not in L2);
 its bytes are the
 U * 1,351,680 of the U distinct experts the routing selects.
+``qwen36`` is BASELINE config 5 on one GPU (Qwen3.6-35B-A3B shape, seeded
+random weights built on the device, 64 sequences in lockstep).
 ``trace`` prints the device-side timeline of one Qwen3.5 decode step (per
 kernel kind: release gap, prologue, body) after a 16-token prefill.
 ``gdn`` and ``attn`` are the stand-alone decode ops of BASELINE configs 2
@@ -23,6 +26,7 @@ from __future__ import annotations
 
 import argparse
 import json
+import time
 
 import numpy as np
 import torch
@@ -210,6 +214,52 @@ def bench_moe(tokens: int, iters: int, shared: bool = True) -> dict:
             "l2": "flushed before each call (256 MB read)"}
 
 
+def bench_qwen36(batch: int, prompt: int, steps: int, layers: int) -> dict:
+    """BASELINE config 5 on one GPU: `batch` sequences of a `prompt`-token
+    random prompt, fed in lockstep, then `steps` greedy steps timed with CUDA
+    events; seeded random weights of the Qwen3.6-35B-A3B shape (with
+    `layers` layers) built on the device."""
+    from dataclasses import replace
+
+    from breezetoken_b200.qwen36_moe import Qwen36Moe
+    from breezetoken_b200.synth import QWEN36_35B
+
+    spec = replace(QWEN36_35B, n_layers=layers)
+    m = Qwen36Moe.random(spec, batch=batch, max_context=prompt + steps)
+    rng = np.random.default_rng(4)
+    toks = torch.from_numpy(rng.integers(0, spec.vocab, (prompt, batch))).cuda()
+    t0 = time.time()
+    for i in range(prompt - 1):
+        m._step(toks[i], i, logits=False)
+    nxt = m.decode_batch(toks[prompt - 1], prompt - 1)
+    torch.cuda.synchronize()
+    prefill_s = time.time() - t0
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for s in range(steps):
+        nxt = m.decode_batch(nxt, prompt + s)
+    e1.record()
+    e1.synchronize()
+    sec = e0.elapsed_time(e1) / 1e3
+    cfg = m.cfg
+    # per-step algorithmic bytes (bf16 non-expert weights without the
+    # embedding gather, selected experts at the expected number of distinct
+    # experts per layer, GDN state r+w, f32 KV read at the mean context)
+    u = cfg.n_experts * (1 - (1 - cfg.top_k / cfg.n_experts) ** batch)
+    dense = sum(t.numel() * t.element_size() for layer in m.layers for k, t in layer.items()
+                if isinstance(t, torch.Tensor)) + m.head.numel() * 2
+    dense += sum(sum(x.numel() * x.element_size() for x in (la["shared"].gate, la["shared"].up, la["shared"].down))
+                 for la in m.layers)
+    n_gdn = cfg.n_layers - len(cfg.attn_layers)
+    state = batch * n_gdn * cfg.gdn_value_heads * cfg.gdn_k_dim * cfg.gdn_value_dim * 4 * 2
+    kv = batch * (prompt + steps / 2) * len(cfg.attn_layers) * 2 * cfg.n_kv * cfg.head_dim * 4
+    step_bytes = dense + cfg.n_layers * u * 1_351_680 + state + kv
+    m.close()
+    return {"kernel": "qwen36_35b_decode", "layers": layers, "batch": batch, "prompt": prompt, "steps": steps,
+            "tok_s": batch * steps / sec, "ms_per_step": sec / steps * 1e3, "prefill_s": prefill_s,
+            "expected_unique_experts": u, "step_bytes": step_bytes, "gbs": step_bytes * steps / sec / 1e9}
+
+
 def trace_step(gguf: str, max_context: int, steps: int) -> str:
     """Per-kernel-kind device timeline of a decode step (model.Qwen35.trace_step):
     gap = previous kernel's last CTA exit -> this kernel's last CTA past the
@@ -265,6 +315,11 @@ def main() -> None:
     mo.add_argument("--tokens", type=int, default=1)
     mo.add_argument("--iters", type=int, default=50)
     mo.add_argument("--no-shared", action="store_true", help="routed experts only")
+    q6 = sub.add_parser("qwen36")
+    q6.add_argument("--batch", type=int, default=64)
+    q6.add_argument("--prompt", type=int, default=512)
+    q6.add_argument("--steps", type=int, default=256)
+    q6.add_argument("--layers", type=int, default=40)
     t = sub.add_parser("trace")
     t.add_argument("--gguf", required=True)
     t.add_argument("--max-context", type=int, default=1024)
@@ -275,6 +330,8 @@ def main() -> None:
         return
     if args.cmd == "gemv":
         r = bench_gemv(args.n, args.k, args.iters)
+    elif args.cmd == "qwen36":
+        r = bench_qwen36(args.batch, args.prompt, args.steps, args.layers)
     elif args.cmd == "moe":
         r = bench_moe(args.tokens, args.iters, shared=not args.no_shared)
     elif args.cmd == "gdn":

@@ -181,6 +181,70 @@ class Qwen36Moe:
                 )
             self.layers.append(layer)
 
+    @classmethod
+    def random(cls, spec, *, batch: int, max_context: int, device: str = "cuda", seed: int = 4) -> Qwen36Moe:
+        """A model of `spec`'s shape (breezetoken_b200.synth.Qwen36Spec) with
+        seeded random weights built on the device, for throughput runs at
+        sizes whose checkpoint would take minutes to write: bf16 projections
+        and the f32 router N(0, 0.02); IQ3_S experts from random quant bytes
+        with d = 2^-12 (weights of the magnitude an N(0, 0.02) quantisation
+        gives); gammas 1 + N(0, 0.02); SSM parameters as in the synthetic
+        checkpoints.  No reference output exists for it."""
+        import math
+
+        self = cls.__new__(cls)
+        self.cfg = Qwen36Config(
+            hidden=spec.hidden, n_layers=spec.n_layers, n_heads=spec.n_heads, n_kv=spec.n_kv,
+            head_dim=spec.head_dim, rope_dim=spec.rope_dim, rope_theta=spec.rope_theta, max_context=max_context,
+            n_experts=spec.n_experts, top_k=spec.top_k, expert_ffn=spec.expert_ffn, shared_ffn=spec.shared_ffn,
+            gdn_key_heads=spec.gdn_key_heads, gdn_value_heads=spec.gdn_value_heads, gdn_k_dim=spec.gdn_dim,
+            gdn_inner=spec.gdn_inner, gdn_conv=spec.conv_k, vocab=spec.vocab, eps=spec.eps,
+        )
+        self.device, self.batch = resolve_device(device), int(batch)
+        cfg, dev = self.cfg, self.device
+        gen = torch.Generator(device=dev)
+        gen.manual_seed(seed)
+
+        def normal(*shape, std=0.02, dtype=torch.bfloat16):
+            return (torch.randn(*shape, generator=gen, device=dev) * std).to(dtype).contiguous()
+
+        def uniform(*shape):
+            return torch.rand(*shape, generator=gen, device=dev)
+
+        def iq3s(rows: int, k: int) -> torch.Tensor:
+            raw = torch.randint(0, 256, (rows * (k // 256), 110), generator=gen, device=dev, dtype=torch.uint8)
+            raw[:, 0], raw[:, 1] = 0x00, 0x0C  # d = 2^-12 (fp16 0x0C00, little-endian)
+            return IQ3SExperts._repack(raw.reshape(-1), rows, k, dev)
+
+        self.embd = normal(cfg.vocab, cfg.hidden)
+        self.head = normal(cfg.vocab, cfg.hidden)
+        self.norm_f = 1 + normal(cfg.hidden, dtype=torch.float32)
+        self.layers = []
+        e, h, f, sf = cfg.n_experts, cfg.hidden, cfg.expert_ffn, cfg.shared_ffn
+        for i in range(cfg.n_layers):
+            layer = {
+                "norm_in": 1 + normal(h, dtype=torch.float32), "norm_post": 1 + normal(h, dtype=torch.float32),
+                "router": normal(e, h, dtype=torch.float32),
+                "experts": IQ3SExperts(iq3s(e * f, h), iq3s(e * f, h), iq3s(e * h, f), e, h, f),
+                "shared": SharedExpert(normal(sf, h), normal(sf, h), normal(h, sf), normal(h, dtype=torch.float32)),
+            }
+            if i in cfg.attn_layers:
+                D = cfg.head_dim
+                layer.update(q=normal(2 * cfg.n_heads * D, h), k=normal(cfg.n_kv * D, h), v=normal(cfg.n_kv * D, h),
+                             o=normal(h, cfg.n_heads * D), q_norm=1 + normal(D, dtype=torch.float32),
+                             k_norm=1 + normal(D, dtype=torch.float32))
+            else:
+                hv = cfg.gdn_value_heads
+                dt = torch.exp(math.log(1e-3) + uniform(hv) * (math.log(1e-1) - math.log(1e-3)))
+                layer.update(qkv=normal(cfg.conv_dim, h), z=normal(cfg.gdn_inner, h), out=normal(h, cfg.gdn_inner),
+                             conv=normal(cfg.conv_dim, cfg.gdn_conv, std=0.25, dtype=torch.float32),
+                             w_alpha=normal(hv, h, dtype=torch.float32), w_beta=normal(hv, h, dtype=torch.float32),
+                             a_log=-torch.exp(uniform(hv) * math.log(16.0)), dt_bias=torch.log(torch.expm1(dt)),
+                             ssm_norm=1 + normal(cfg.gdn_k_dim, dtype=torch.float32))
+            self.layers.append(layer)
+        self._alloc()
+        return self
+
     def _alloc(self) -> None:
         cfg, b, dev = self.cfg, self.batch, self.device
         self.backend = B200Backend(dev)

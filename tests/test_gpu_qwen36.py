@@ -70,7 +70,7 @@ def test_qwen36_batch_lockstep(cuda, qwen36_tiny_gguf, model) -> None:
 
 
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
-@pytest.mark.parametrize("t", [1, 5, 20])
+@pytest.mark.parametrize("t", [1, 5, 20, 70])
 def test_linear_rows_matches_f64(cuda, dtype, t) -> None:
     """y = x W^T against an f64 product: within 2e-6 of sum |x||w| per output."""
     rng = np.random.default_rng(12)
