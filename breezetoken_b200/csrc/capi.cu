@@ -150,9 +150,13 @@ int bt_linear_kn(const void* w, int w_dtype, const float* x, float* y, int64_t k
   return bt::linear_kn(w, w_dtype, x, y, k, n, as_stream(stream));
 }
 
-int bt_linear_rows(const void* w, int w_dtype, const float* x, float* y, int64_t n, int64_t k, int64_t t,
+int bt_bf16_planes(const float* x, void* planes, int64_t t, int64_t k, void* stream) {
+  return bt::bf16_planes(x, planes, t, k, as_stream(stream));
+}
+
+int bt_linear_rows(const void* w, int w_dtype, const void* x_planes, float* y, int64_t n, int64_t k, int64_t t,
                    void* stream) {
-  return bt::linear_rows(w, w_dtype, x, y, n, k, t, as_stream(stream));
+  return bt::linear_rows(w, w_dtype, x_planes, y, n, k, t, as_stream(stream));
 }
 
 int bt_rms_norm(const float* x, const float* w, float* y, int64_t rows, int64_t n, float eps, void* stream) {

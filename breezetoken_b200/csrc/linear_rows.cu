@@ -1,19 +1,20 @@
 // Dense projection of T tokens by bf16 or f32 weight rows on the tensor cores:
 // y[t][n] = sum_k W[n][k] x[t][k], W (N, K) in the GGUF (out, in)
-// orientation, x (T, K) f32, y (T, N) f32 -- the reference's _linear /
-// _linear_b of model/qwen36_moe.py:352-358 in its f32 form (weights exact in
-// f32, activations f32).
+// orientation, y (T, N) f32 -- the reference's _linear / _linear_b of
+// model/qwen36_moe.py:352-358 in its f32 form (weights exact in f32,
+// activations f32).
 //
-// One block per 16-row tile and up to 8 passes of 8 tokens (grid (N/16,
-// ceil(T/64)) for T > 32); its 8 warps split K, and every pass reuses the
-// weight fragments a warp loaded, so the weights are read once per 64
-// tokens.  Per 32-column step a lane loads weights 8t .. 8t+7 of rows g and
-// g+8 (16-byte loads; the k order inside the step is permuted
+// x enters as three bf16 planes (x = hi + mid + lo, each remainder exact in
+// f32: 24 bits), split once by bf16_planes_kernel and shared by every
+// projection of the same input.  One block per 16-row tile and NP passes of
+// 8 tokens; its 8 warps split K, and every pass reuses the weight fragments
+// a warp loaded.  Per 32-column step a lane loads weights 8t .. 8t+7 of rows
+// g and g+8 (16-byte loads; the k order inside the step is permuted
 // identically on both MMA operands) and the same columns of token column g's
-// x.  x is split into three bf16 planes (x = hi + mid + lo, each remainder
-// exact in f32), f32 weights likewise; every plane product accumulates into
-// one f32 sum (m16n8k16 bf16 MMAs), so the sums carry both operands to their
-// 24 bits.  Before the dependency wait each warp bulk-prefetches its weight
+// planes.  f32 weights are split into three bf16 planes in registers; the
+// plane products that reach 2^-24 of the largest are summed (all 3 for bf16
+// weights, 6 of 9 for f32), into one f32 sum per output (m16n8k16 bf16
+// MMAs).  Before the dependency wait each warp bulk-prefetches its weight
 // slices into L2: the weights never depend on earlier kernels.
 #include <cuda_bf16.h>
 
@@ -61,16 +62,38 @@ __device__ __forceinline__ void load8(const float* p, float (&v)[8]) {
   v[0] = a.x, v[1] = a.y, v[2] = a.z, v[3] = a.w, v[4] = b.x, v[5] = b.y, v[6] = b.z, v[7] = b.w;
 }
 
-// c += (A planes of rows g, g+8) x (B planes): 32 columns.
+// c += (A planes of rows g, g+8) x (B planes): 32 columns.  bf16 weights:
+// the weight times the three x planes; f32 weights: the six plane products
+// with plane-index sum <= 2 (the others lie below 2^-24 of the largest).
 template <int NA>
 __device__ __forceinline__ void step(float (&c)[4], const uint4 (&ra)[NA], const uint4 (&rb)[NA], const uint4 (&b)[3]) {
 #pragma unroll
   for (int i = 0; i < NA; ++i)
 #pragma unroll
     for (int j = 0; j < 3; ++j) {
+      if (i + j > 2) continue;
       mma_bf16(c, ra[i].x, rb[i].x, ra[i].y, rb[i].y, b[j].x, b[j].y);
       mma_bf16(c, ra[i].z, rb[i].z, ra[i].w, rb[i].w, b[j].z, b[j].w);
     }
+}
+
+// x (T, K) f32 -> planes (T, 3, K) bf16, 8 values per thread.
+__global__ void bf16_planes_kernel(const float* __restrict__ x, __nv_bfloat16* __restrict__ planes, int64_t t,
+                                   int k) {
+  pdl_wait();
+  pdl_launch_dependents();
+  const int64_t chunks = t * (k / 8);
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < chunks;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t tok = i / (k / 8);
+    const int col = static_cast<int>(i - tok * (k / 8)) * 8;
+    float v[8];
+    load8(x + tok * k + col, v);
+    uint4 p[3];
+    split8(v, p);
+#pragma unroll
+    for (int j = 0; j < 3; ++j) *reinterpret_cast<uint4*>(planes + (tok * 3 + j) * k + col) = p[j];
+  }
 }
 
 __device__ __forceinline__ void prefetch_l2(const void* p, uint32_t bytes) {
@@ -78,7 +101,8 @@ __device__ __forceinline__ void prefetch_l2(const void* p, uint32_t bytes) {
 }
 
 template <bool F32W, int NP>
-__global__ void __launch_bounds__(kThreads) linear_rows_kernel(const void* __restrict__ w, const float* __restrict__ x,
+__global__ void __launch_bounds__(kThreads) linear_rows_kernel(const void* __restrict__ w,
+                                                               const __nv_bfloat16* __restrict__ xp,
                                                                float* __restrict__ y, int n, int k, int t_total) {
   using Elem = typename std::conditional<F32W, float, __nv_bfloat16>::type;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
@@ -87,13 +111,18 @@ __global__ void __launch_bounds__(kThreads) linear_rows_kernel(const void* __res
   if (lane < 16)
     prefetch_l2(static_cast<const Elem*>(w) + static_cast<int64_t>(16 * tile + lane) * k + warp * span,
                 static_cast<uint32_t>(span * sizeof(Elem)));
-  pdl_wait();  // x comes from earlier kernels
+  pdl_wait();  // the planes come from earlier kernels
   pdl_launch_dependents();
-  const float* xr[NP];
+  const __nv_bfloat16* xr[NP];
+  bool live[NP];
 #pragma unroll
-  for (int p = 0; p < NP; ++p) xr[p] = x + static_cast<int64_t>(min(c0 + kPass * p + g, t_total - 1)) * k;
+  for (int p = 0; p < NP; ++p) {
+    const int tok = c0 + kPass * p + g;
+    live[p] = tok < t_total;
+    xr[p] = xp + static_cast<int64_t>(live[p] ? tok : 0) * 3 * k;
+  }
   float c[NP][4] = {};
-#pragma unroll 2
+#pragma unroll(NP < 4 ? 2 : 1)  // the passes of a step already give the loads to overlap
   for (int k0 = warp * span; k0 < (warp + 1) * span; k0 += 32) {
     const int col = k0 + 8 * t;
     constexpr int NA = F32W ? 3 : 1;
@@ -111,13 +140,10 @@ __global__ void __launch_bounds__(kThreads) linear_rows_kernel(const void* __res
     }
 #pragma unroll
     for (int p = 0; p < NP; ++p) {  // every pass reuses the weight fragments
-      float xv[8];
-      load8(xr[p] + col, xv);
-      if (c0 + kPass * p + g >= t_total)
-#pragma unroll
-        for (int i = 0; i < 8; ++i) xv[i] = 0.f;
       uint4 b[3];
-      split8(xv, b);
+#pragma unroll
+      for (int j = 0; j < 3; ++j)
+        b[j] = live[p] ? __ldcg(reinterpret_cast<const uint4*>(xr[p] + j * k + col)) : make_uint4(0u, 0u, 0u, 0u);
       step<NA>(c[p], ra, rb, b);
     }
   }
@@ -136,40 +162,65 @@ __global__ void __launch_bounds__(kThreads) linear_rows_kernel(const void* __res
 }
 
 template <bool F32W>
-cudaError_t launch_np(cudaLaunchConfig_t& cfg, int np, const void* w, const float* x, float* y, int n, int k, int t) {
+cudaError_t launch_np(cudaLaunchConfig_t& cfg, int np, const void* w, const __nv_bfloat16* xp, float* y, int n, int k,
+                      int t) {
   switch (np) {
-    case 1: return cudaLaunchKernelEx(&cfg, linear_rows_kernel<F32W, 1>, w, x, y, n, k, t);
-    case 2: return cudaLaunchKernelEx(&cfg, linear_rows_kernel<F32W, 2>, w, x, y, n, k, t);
-    case 4: return cudaLaunchKernelEx(&cfg, linear_rows_kernel<F32W, 4>, w, x, y, n, k, t);
-    default: return cudaLaunchKernelEx(&cfg, linear_rows_kernel<F32W, 8>, w, x, y, n, k, t);
+    case 1: return cudaLaunchKernelEx(&cfg, linear_rows_kernel<F32W, 1>, w, xp, y, n, k, t);
+    case 2: return cudaLaunchKernelEx(&cfg, linear_rows_kernel<F32W, 2>, w, xp, y, n, k, t);
+    case 4: return cudaLaunchKernelEx(&cfg, linear_rows_kernel<F32W, 4>, w, xp, y, n, k, t);
+    default: return cudaLaunchKernelEx(&cfg, linear_rows_kernel<F32W, 8>, w, xp, y, n, k, t);
   }
 }
 
-}  // namespace
-
-int linear_rows(const void* w, int w_dtype, const float* x, float* y, int64_t n, int64_t k, int64_t t,
-                cudaStream_t stream) {
-  if (!w || !x || !y || n < 1 || k < 1 || t < 1) return fail(BT_ERR_INVALID, "linear_rows: bad arguments");
-  if (w_dtype != BT_BF16 && w_dtype != BT_F32) return fail(BT_ERR_UNSUPPORTED, "linear_rows: weights bf16 or f32");
-  if (n % 16 || k % 256 || n / 16 > 2147483647LL || (t + kPass - 1) / kPass > 65535)
-    return fail(BT_ERR_UNSUPPORTED, "linear_rows: N must be a multiple of 16 and K of 256 (got %lld x %lld)",
-                static_cast<long long>(n), static_cast<long long>(k));
-  if ((reinterpret_cast<uintptr_t>(w) | reinterpret_cast<uintptr_t>(x)) & 15)
-    return fail(BT_ERR_INVALID, "linear_rows: w and x must be 16-byte aligned");
-  // passes of 8 tokens per block: the weights are read once per 64 tokens
-  const int np = t <= 8 ? 1 : t <= 16 ? 2 : t <= 32 ? 4 : 8;
+cudaLaunchConfig_t pdl_config(dim3 grid, cudaStream_t stream, cudaLaunchAttribute* attr) {
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(static_cast<unsigned>(n / 16), static_cast<unsigned>((t + kPass * np - 1) / (kPass * np)));
+  cfg.gridDim = grid;
   cfg.blockDim = dim3(kThreads);
   cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
+  return cfg;
+}
+
+}  // namespace
+
+int bf16_planes(const float* x, void* planes, int64_t t, int64_t k, cudaStream_t stream) {
+  if (!x || !planes || t < 1 || k < 8 || k % 8) return fail(BT_ERR_INVALID, "bf16_planes: bad arguments");
+  if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(planes)) & 15)
+    return fail(BT_ERR_INVALID, "bf16_planes: x and planes must be 16-byte aligned");
+  const int64_t chunks = t * (k / 8);
+  cudaLaunchAttribute attr[1];
+  cudaLaunchConfig_t cfg =
+      pdl_config(dim3(static_cast<unsigned>(std::min<int64_t>((chunks + kThreads - 1) / kThreads, 4096))), stream, attr);
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, bf16_planes_kernel, x, static_cast<__nv_bfloat16*>(planes), t,
+                                           static_cast<int>(k));
+  if (e != cudaSuccess) return fail_cuda(e, "bf16_planes launch");
+  return BT_OK;
+}
+
+int linear_rows(const void* w, int w_dtype, const void* x_planes, float* y, int64_t n, int64_t k, int64_t t,
+                cudaStream_t stream) {
+  if (!w || !x_planes || !y || n < 1 || k < 1 || t < 1) return fail(BT_ERR_INVALID, "linear_rows: bad arguments");
+  if (w_dtype != BT_BF16 && w_dtype != BT_F32) return fail(BT_ERR_UNSUPPORTED, "linear_rows: weights bf16 or f32");
+  if (n % 16 || k % 256 || n / 16 > 2147483647LL || (t + kPass - 1) / kPass > 65535)
+    return fail(BT_ERR_UNSUPPORTED, "linear_rows: N must be a multiple of 16 and K of 256 (got %lld x %lld)",
+                static_cast<long long>(n), static_cast<long long>(k));
+  if ((reinterpret_cast<uintptr_t>(w) | reinterpret_cast<uintptr_t>(x_planes)) & 15)
+    return fail(BT_ERR_INVALID, "linear_rows: w and the planes must be 16-byte aligned");
+  // passes of 8 tokens per block: as many as keep >= 2 blocks per SM busy
+  // (fewer weight re-reads), one when the matrix is small
+  const int64_t tiles = n / 16, passes = (t + kPass - 1) / kPass, want = 2 * sm_count();
+  int np = 8;
+  while (np > 1 && (np > passes || tiles * ((passes + np - 1) / np) < want)) np >>= 1;
+  cudaLaunchAttribute attr[1];
+  cudaLaunchConfig_t cfg = pdl_config(dim3(static_cast<unsigned>(tiles), static_cast<unsigned>((passes + np - 1) / np)),
+                                      stream, attr);
   const int nn = static_cast<int>(n), kk = static_cast<int>(k), tt = static_cast<int>(t);
-  const cudaError_t e = w_dtype == BT_F32 ? launch_np<true>(cfg, np, w, x, y, nn, kk, tt)
-                                          : launch_np<false>(cfg, np, w, x, y, nn, kk, tt);
+  const auto* xp = static_cast<const __nv_bfloat16*>(x_planes);
+  const cudaError_t e = w_dtype == BT_F32 ? launch_np<true>(cfg, np, w, xp, y, nn, kk, tt)
+                                          : launch_np<false>(cfg, np, w, xp, y, nn, kk, tt);
   if (e != cudaSuccess) return fail_cuda(e, "linear_rows launch");
   return BT_OK;
 }

@@ -5,7 +5,9 @@
 
 namespace bt {
 
-int linear_rows(const void* w, int w_dtype, const float* x, float* y, int64_t n, int64_t k, int64_t t,
+int bf16_planes(const float* x, void* planes, int64_t t, int64_t k, cudaStream_t stream);
+
+int linear_rows(const void* w, int w_dtype, const void* x_planes, float* y, int64_t n, int64_t k, int64_t t,
                 cudaStream_t stream);
 
 }  // namespace bt

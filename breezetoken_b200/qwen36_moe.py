@@ -271,18 +271,28 @@ class Qwen36Moe:
             st.zero_()
 
     def close(self) -> None:
+        self._graph = None
         self.layers.clear()
         self.kv.clear()
         self.backend.close()
 
     # ------------------------------------------------------------------ ops
-    def _lin(self, w: torch.Tensor, x: torch.Tensor) -> torch.Tensor:
-        """x (T, K) f32 -> (T, N) f32 through weight rows w (N, K)."""
+    def _planes(self, x: torch.Tensor) -> torch.Tensor:
+        """x (T, K) f32 as the three bf16 planes the projections read (split
+        once per activation, shared by every projection of it)."""
+        x2 = x.float().reshape(x.shape[0], -1).contiguous()
+        p = torch.empty(x2.shape[0], 3, x2.shape[1], dtype=torch.bfloat16, device=self.device)
+        N.call("bt_bf16_planes", x2.data_ptr(), p.data_ptr(), x2.shape[0], x2.shape[1], _stream())
+        return p
+
+    def _lin(self, w: torch.Tensor, xp: torch.Tensor) -> torch.Tensor:
+        """Planes xp (T, 3, K) -> (T, N) f32 through weight rows w (N, K)."""
         n, k = w.shape
-        x2 = x.float().reshape(-1, k).contiguous()
-        y = torch.empty(x2.shape[0], n, dtype=torch.float32, device=self.device)
+        if xp.shape[-1] != k:
+            raise ValueError(f"projection of {xp.shape[-1]} columns through a ({n}, {k}) weight")
+        y = torch.empty(xp.shape[0], n, dtype=torch.float32, device=self.device)
         dt = N.BT_BF16 if w.dtype == torch.bfloat16 else N.BT_F32
-        N.call("bt_linear_rows", w.data_ptr(), dt, x2.data_ptr(), y.data_ptr(), n, k, x2.shape[0], _stream())
+        N.call("bt_linear_rows", w.data_ptr(), dt, xp.data_ptr(), y.data_ptr(), n, k, xp.shape[0], _stream())
         return y
 
     def _rms(self, x: torch.Tensor, gamma: torch.Tensor) -> torch.Tensor:
@@ -291,31 +301,34 @@ class Qwen36Moe:
     def _rope(self, x: torch.Tensor, pos_t: torch.Tensor) -> torch.Tensor:
         return self.backend.rope(x, self.rope_cos, self.rope_sin, pos_t, self.cfg.rope_dim)
 
-    def _attn(self, i: int, xn: torch.Tensor, pos: int, pos_t: torch.Tensor) -> torch.Tensor:
+    def _attn(self, i: int, xn: torch.Tensor, pos_t: torch.Tensor) -> torch.Tensor:
         cfg, layer = self.cfg, self.layers[i]
         b, H, D = xn.shape[0], cfg.n_heads, cfg.head_dim
-        q_full = self._lin(layer["q"], xn).view(b, H, 2 * D)
+        xp = self._planes(xn)
+        q_full = self._lin(layer["q"], xp).view(b, H, 2 * D)
         q, gate = q_full[..., :D].contiguous(), q_full[..., D:]
-        k = self._lin(layer["k"], xn).view(b, cfg.n_kv, D)
-        v = self._lin(layer["v"], xn).view(b, cfg.n_kv, D)
+        k = self._lin(layer["k"], xp).view(b, cfg.n_kv, D)
+        v = self._lin(layer["v"], xp).view(b, cfg.n_kv, D)
         q = self._rope(self._rms(q, layer["q_norm"]), pos_t)
         k = self._rope(self._rms(k, layer["k_norm"]), pos_t)
         k_cache, v_cache = self.kv[i]
-        k_cache[:, pos] = k
-        v_cache[:, pos] = v
-        lens = torch.full((b,), pos + 1, dtype=torch.int32, device=self.device)
+        idx = pos_t.long()  # the KV write and the attended length follow the device position
+        k_cache.index_copy_(1, idx, k.unsqueeze(1))
+        v_cache.index_copy_(1, idx, v.unsqueeze(1))
+        lens = (pos_t + 1).expand(b).contiguous()
         out = torch.empty(b, H, D, dtype=torch.float32, device=self.device)
         N.call("bt_attention_decode", q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), N.BT_F32,
                lens.data_ptr(), out.data_ptr(), b, H, cfg.n_kv, D, cfg.max_context, float(D ** -0.5),
                self._splits(), self._attn_ws.data_ptr(), _stream())
         out = out * torch.sigmoid(gate)
-        return self._lin(layer["o"], out.reshape(b, -1))
+        return self._lin(layer["o"], self._planes(out.reshape(b, -1)))
 
     def _gdn(self, i: int, xn: torch.Tensor) -> torch.Tensor:
         cfg, layer = self.cfg, self.layers[i]
         b, hk, hv, dk = xn.shape[0], cfg.gdn_key_heads, cfg.gdn_value_heads, cfg.gdn_k_dim
         inner = cfg.gdn_inner
-        entry = self._lin(layer["qkv"], xn)  # (B, C)
+        xp = self._planes(xn)
+        entry = self._lin(layer["qkv"], xp)  # (B, C)
         conv = self.conv_state[i]
         window = torch.cat((conv, entry.unsqueeze(2)), dim=2)  # (B, C, conv)
         mixed = torch.nn.functional.silu((window * layer["conv"]).sum(dim=-1))
@@ -323,22 +336,38 @@ class Qwen36Moe:
         q = mixed[:, : inner // 2].reshape(b, hk, dk).contiguous()
         k = mixed[:, inner // 2 : inner].reshape(b, hk, dk).contiguous()
         v = mixed[:, inner:].reshape(b, hv, dk).contiguous()
-        beta = self._lin(layer["w_beta"], xn)
-        g = layer["a_log"] * torch.nn.functional.softplus(self._lin(layer["w_alpha"], xn) + layer["dt_bias"])
+        beta = self._lin(layer["w_beta"], xp)
+        g = layer["a_log"] * torch.nn.functional.softplus(self._lin(layer["w_alpha"], xp) + layer["dt_bias"])
         read = torch.empty(b, hv, cfg.gdn_value_dim, dtype=torch.float32, device=self.device)
         N.call("bt_gdn_decode", q.data_ptr(), k.data_ptr(), v.data_ptr(), N.BT_F32, g.contiguous().data_ptr(),
                beta.contiguous().data_ptr(), self.rec_state[i].data_ptr(), read.data_ptr(), b, hk, hv, dk,
                float(dk ** -0.5), float(cfg.l2_eps), _stream())
-        z = self._lin(layer["z"], xn).view(b, hv, dk)
+        z = self._lin(layer["z"], xp).view(b, hv, dk)
         gated = (self._rms(read, layer["ssm_norm"]) * torch.nn.functional.silu(z)).reshape(b, -1)
-        return self._lin(layer["out"], gated)
+        return self._lin(layer["out"], self._planes(gated))
 
     def _moe(self, i: int, xn: torch.Tensor) -> torch.Tensor:
         layer = self.layers[i]
-        r = route_logits(self._lin(layer["router"], xn), self.cfg.top_k)
+        r = route_logits(self._lin(layer["router"], self._planes(xn)), self.cfg.top_k)
         return moe_forward(layer["experts"], layer["shared"], xn, r.expert_ids, r.weights, self._moe_ws)
 
     # ------------------------------------------------------------------ step
+    def _step_t(self, tokens: torch.Tensor, pos_t: torch.Tensor, logits: bool) -> torch.Tensor | None:
+        """One step with the position as a device tensor (int32 (1,)): no
+        host synchronisation, so it can be captured in a CUDA graph."""
+        cfg = self.cfg
+        h = self.embd[tokens.long()].float()
+        attn = set(cfg.attn_layers)
+        for i in range(cfg.n_layers):
+            layer = self.layers[i]
+            xn = self._rms(h, layer["norm_in"])
+            h = h + (self._attn(i, xn, pos_t) if i in attn else self._gdn(i, xn))
+            xn = self._rms(h, layer["norm_post"])
+            h = h + self._moe(i, xn)
+        if not logits:
+            return None
+        return self._lin(self.head, self._planes(self._rms(h, self.norm_f)))
+
     @torch.inference_mode()
     def _step(self, tokens: torch.Tensor, pos: int, logits: bool) -> torch.Tensor | None:
         cfg = self.cfg
@@ -346,18 +375,41 @@ class Qwen36Moe:
             raise ValueError(f"position {pos} outside [0, {cfg.max_context})")
         if int(tokens.min()) < 0 or int(tokens.max()) >= cfg.vocab:
             raise ValueError("token id outside the vocabulary")
-        pos_t = torch.full((1,), pos, dtype=torch.int32, device=self.device)
-        h = self.embd[tokens.long()].float()
-        attn = set(cfg.attn_layers)
-        for i in range(cfg.n_layers):
-            layer = self.layers[i]
-            xn = self._rms(h, layer["norm_in"])
-            h = h + (self._attn(i, xn, pos, pos_t) if i in attn else self._gdn(i, xn))
-            xn = self._rms(h, layer["norm_post"])
-            h = h + self._moe(i, xn)
-        if not logits:
-            return None
-        return self._lin(self.head, self._rms(h, self.norm_f))
+        return self._step_t(tokens, torch.full((1,), pos, dtype=torch.int32, device=self.device), logits)
+
+    @torch.inference_mode()
+    def graph_decode(self, tokens: torch.Tensor, pos: int, steps: int) -> torch.Tensor:
+        """`steps` greedy steps of the B sequences, the first feeding `tokens`
+        at position `pos`, replayed from a CUDA graph of one step (token,
+        position and the generated ids stay on the device; no host sync
+        between steps).  Returns the generated ids (B, steps).  Call an eager
+        step first so that every lazily configured kernel is set up."""
+        cfg, b = self.cfg, self.batch
+        if tokens.numel() != b:
+            raise ValueError(f"expected {b} tokens, got {tokens.numel()}")
+        if not 0 <= pos or pos + steps > cfg.max_context:
+            raise ValueError(f"positions {pos}..{pos + steps - 1} outside [0, {cfg.max_context})")
+        if getattr(self, "_graph", None) is None or self._hist.shape[1] < steps:
+            self._tok = torch.zeros(b, dtype=torch.int64, device=self.device)
+            self._pos = torch.zeros(1, dtype=torch.int32, device=self.device)
+            self._n = torch.zeros(1, dtype=torch.int64, device=self.device)
+            self._hist = torch.zeros(b, max(steps, 1), dtype=torch.int64, device=self.device)
+            self.backend._workspace(("argmax", b), int(N.load().bt_argmax_workspace_bytes(b)))
+            stream = torch.cuda.Stream(device=self.device)
+            stream.wait_stream(torch.cuda.current_stream())
+            self._graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(self._graph, stream=stream):
+                nxt = self.backend.argmax(self._step_t(self._tok, self._pos, True)).long()
+                self._hist.index_copy_(1, self._n, nxt.unsqueeze(1))
+                self._tok.copy_(nxt)
+                self._pos.add_(1)
+                self._n.add_(1)
+        self._tok.copy_(tokens.reshape(-1))
+        self._pos.fill_(pos)
+        self._n.zero_()
+        for _ in range(steps):
+            self._graph.replay()
+        return self._hist[:, :steps].clone()
 
     def forward_token(self, token: int, pos: int, *, logits: bool = True) -> torch.Tensor | None:
         """model/qwen36_moe.py:646-664 for sequence 0: (V,) f32 logits."""

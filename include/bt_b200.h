@@ -87,12 +87,19 @@ BT_API int bt_linear_q8(const void* w, const float* x, float* y, int64_t n, int6
 BT_API int bt_linear_kn(const void* w, int w_dtype, const float* x, float* y,
                  int64_t k, int64_t n, void* stream);
 
+/* x (T, K) f32 -> planes (T, 3, K) bf16 with x = hi + mid + lo (each
+ * remainder exact in f32, so the planes carry x's 24 bits): the input form
+ * of bt_linear_rows, split once per activation and shared by every
+ * projection of it.  K % 8 == 0; both 16-byte aligned.                    */
+BT_API int bt_bf16_planes(const float* x, void* planes, int64_t t, int64_t k,
+                   void* stream);
+
 /* Qwen36Moe._linear / _linear_b (model/qwen36_moe.py:352-358) for T
  * tokens: y[t][n] = sum_k W[n][k] * x[t][k] with W (N, K) rows in the GGUF
- * (out, in) orientation, bf16 or f32 (w_dtype), on the tensor cores with
- * both operands carried to 24 bits.  x (T, K), y (T, N) f32; N % 16 == 0,
- * K % 256 == 0; w and x 16-byte aligned.                                  */
-BT_API int bt_linear_rows(const void* w, int w_dtype, const float* x, float* y,
+ * (out, in) orientation, bf16 or f32 (w_dtype), x given as the planes of
+ * bt_bf16_planes, on the tensor cores (both operands to 24 bits).  y (T, N)
+ * f32; N % 16 == 0, K % 256 == 0; w and the planes 16-byte aligned.       */
+BT_API int bt_linear_rows(const void* w, int w_dtype, const void* x_planes, float* y,
                    int64_t n, int64_t k, int64_t t, void* stream);
 
 /* Backend.rms_norm (backends.py:119-123) over rows of length n.           */

@@ -69,6 +69,18 @@ def test_qwen36_batch_lockstep(cuda, qwen36_tiny_gguf, model) -> None:
     assert together == solo
 
 
+def test_qwen36_graph_decode_matches_reference(model) -> None:
+    """The CUDA-graph decode (device-side token, position and history)
+    reproduces the reference's greedy tokens."""
+    g = golden("qwen36_tiny")
+    prompt = g["prompt"].tolist()
+    model.reset()
+    for i, t in enumerate(prompt[:-1]):
+        model._step(torch.tensor([t], device="cuda"), i, logits=False)
+    got = model.graph_decode(torch.tensor([prompt[-1]], device="cuda"), len(prompt) - 1, int(g["steps"]))
+    assert got[0].tolist() == g["tokens"].tolist()
+
+
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
 @pytest.mark.parametrize("t", [1, 5, 20, 70])
 def test_linear_rows_matches_f64(cuda, dtype, t) -> None:
@@ -79,7 +91,10 @@ def test_linear_rows_matches_f64(cuda, dtype, t) -> None:
     x = torch.from_numpy(rng.standard_normal((t, k)).astype(np.float32))
     y = torch.empty(t, n, device="cuda")
     wd, xd = w.cuda().contiguous(), x.cuda().contiguous()
-    N.call("bt_linear_rows", wd.data_ptr(), N.BT_BF16 if dtype == torch.bfloat16 else N.BT_F32, xd.data_ptr(),
+    planes = torch.empty(t, 3, k, dtype=torch.bfloat16, device="cuda")
+    N.call("bt_bf16_planes", xd.data_ptr(), planes.data_ptr(), t, k, 0)
+    assert torch.equal(planes.float().sum(1), xd)  # the planes hold x exactly
+    N.call("bt_linear_rows", wd.data_ptr(), N.BT_BF16 if dtype == torch.bfloat16 else N.BT_F32, planes.data_ptr(),
            y.data_ptr(), n, k, t, 0)
     wf = w.double().numpy()
     want = x.double().numpy() @ wf.T
