@@ -150,6 +150,11 @@ int bt_linear_kn(const void* w, int w_dtype, const float* x, float* y, int64_t k
   return bt::linear_kn(w, w_dtype, x, y, k, n, as_stream(stream));
 }
 
+int bt_conv_silu(const float* entry, float* state, const float* w, float* out, int64_t batch, int64_t channels,
+                 int64_t taps, void* stream) {
+  return bt::conv_silu(entry, state, w, out, batch, channels, taps, as_stream(stream));
+}
+
 int bt_bf16_planes(const float* x, void* planes, int64_t t, int64_t k, void* stream) {
   return bt::bf16_planes(x, planes, t, k, as_stream(stream));
 }

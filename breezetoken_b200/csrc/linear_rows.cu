@@ -100,17 +100,18 @@ __device__ __forceinline__ void prefetch_l2(const void* p, uint32_t bytes) {
   asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
 }
 
-template <bool F32W, int NP>
+template <bool F32W, int NP, int TW>
 __global__ void __launch_bounds__(kThreads) linear_rows_kernel(const void* __restrict__ w,
                                                                const __nv_bfloat16* __restrict__ xp,
                                                                float* __restrict__ y, int n, int k, int t_total) {
   using Elem = typename std::conditional<F32W, float, __nv_bfloat16>::type;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
-  const int tile = blockIdx.x, c0 = blockIdx.y * kPass * NP, span = k / kWarps;
-  const Elem* wr = static_cast<const Elem*>(w) + static_cast<int64_t>(16 * tile + g) * k;
+  const int tile0 = blockIdx.x * TW, c0 = blockIdx.y * kPass * NP, span = k / kWarps;
   if (lane < 16)
-    prefetch_l2(static_cast<const Elem*>(w) + static_cast<int64_t>(16 * tile + lane) * k + warp * span,
-                static_cast<uint32_t>(span * sizeof(Elem)));
+#pragma unroll
+    for (int j = 0; j < TW; ++j)
+      prefetch_l2(static_cast<const Elem*>(w) + static_cast<int64_t>(16 * (tile0 + j) + lane) * k + warp * span,
+                  static_cast<uint32_t>(span * sizeof(Elem)));
   pdl_wait();  // the planes come from earlier kernels
   pdl_launch_dependents();
   const __nv_bfloat16* xr[NP];
@@ -121,54 +122,64 @@ __global__ void __launch_bounds__(kThreads) linear_rows_kernel(const void* __res
     live[p] = tok < t_total;
     xr[p] = xp + static_cast<int64_t>(live[p] ? tok : 0) * 3 * k;
   }
-  float c[NP][4] = {};
-#pragma unroll(NP < 4 ? 2 : 1)  // the passes of a step already give the loads to overlap
+  float c[TW][NP][4] = {};
+#pragma unroll(NP * TW < 4 ? 2 : 1)  // the passes of a step already give the loads to overlap
   for (int k0 = warp * span; k0 < (warp + 1) * span; k0 += 32) {
     const int col = k0 + 8 * t;
     constexpr int NA = F32W ? 3 : 1;
-    uint4 ra[NA], rb[NA];
-    if constexpr (F32W) {
-      float va[8], vb[8];
-      load8(reinterpret_cast<const float*>(wr) + col, va);
-      load8(reinterpret_cast<const float*>(wr) + 8 * static_cast<int64_t>(k) + col, vb);
-      split8(va, ra);
-      split8(vb, rb);
-    } else {
-      ra[0] = __ldg(reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(wr) + col));
-      rb[0] = __ldg(reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(wr) +
-                                                   8 * static_cast<int64_t>(k) + col));
+    uint4 ra[TW][NA], rb[TW][NA];
+#pragma unroll
+    for (int j = 0; j < TW; ++j) {
+      const Elem* wr = static_cast<const Elem*>(w) + static_cast<int64_t>(16 * (tile0 + j) + g) * k;
+      if constexpr (F32W) {
+        float va[8], vb[8];
+        load8(reinterpret_cast<const float*>(wr) + col, va);
+        load8(reinterpret_cast<const float*>(wr) + 8 * static_cast<int64_t>(k) + col, vb);
+        split8(va, ra[j]);
+        split8(vb, rb[j]);
+      } else {
+        ra[j][0] = __ldg(reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(wr) + col));
+        rb[j][0] = __ldg(reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(wr) +
+                                                        8 * static_cast<int64_t>(k) + col));
+      }
     }
 #pragma unroll
-    for (int p = 0; p < NP; ++p) {  // every pass reuses the weight fragments
+    for (int p = 0; p < NP; ++p) {  // every pass reuses the weight fragments, every tile the x planes
       uint4 b[3];
 #pragma unroll
-      for (int j = 0; j < 3; ++j)
-        b[j] = live[p] ? __ldcg(reinterpret_cast<const uint4*>(xr[p] + j * k + col)) : make_uint4(0u, 0u, 0u, 0u);
-      step<NA>(c[p], ra, rb, b);
+      for (int q = 0; q < 3; ++q)
+        b[q] = live[p] ? __ldcg(reinterpret_cast<const uint4*>(xr[p] + q * k + col)) : make_uint4(0u, 0u, 0u, 0u);
+#pragma unroll
+      for (int j = 0; j < TW; ++j) step<NA>(c[j][p], ra[j], rb[j], b);
     }
   }
-  __shared__ float4 red[kWarps][NP][32];
+  __shared__ float4 red[kWarps][TW * NP][32];
 #pragma unroll
-  for (int p = 0; p < NP; ++p) red[warp][p][lane] = make_float4(c[p][0], c[p][1], c[p][2], c[p][3]);
+  for (int j = 0; j < TW; ++j)
+#pragma unroll
+    for (int p = 0; p < NP; ++p)
+      red[warp][j * NP + p][lane] = make_float4(c[j][p][0], c[j][p][1], c[j][p][2], c[j][p][3]);
   __syncthreads();
-  for (int i = threadIdx.x; i < 16 * kPass * NP; i += kThreads) {  // (row r, token v), K slices summed in order
-    const int r = i & 15, v = i >> 4, p = v / kPass, vv = v % kPass;
+  for (int i = threadIdx.x; i < TW * 16 * kPass * NP; i += kThreads) {  // (tile j, row r, token v), K slices in order
+    const int r = i & 15, v = (i >> 4) % (kPass * NP), j = (i >> 4) / (kPass * NP);
+    const int p = v / kPass, vv = v % kPass;
     const int src = (r & 7) * 4 + (vv >> 1), reg = (r >> 3) * 2 + (vv & 1);
     float s = 0.f;
 #pragma unroll
-    for (int j = 0; j < kWarps; ++j) s += reinterpret_cast<const float*>(&red[j][p][src])[reg];
-    if (c0 + v < t_total) y[static_cast<int64_t>(c0 + v) * n + 16 * tile + r] = s;
+    for (int q = 0; q < kWarps; ++q) s += reinterpret_cast<const float*>(&red[q][j * NP + p][src])[reg];
+    if (c0 + v < t_total) y[static_cast<int64_t>(c0 + v) * n + 16 * (tile0 + j) + r] = s;
   }
 }
 
-template <bool F32W>
+template <bool F32W, int TW>
 cudaError_t launch_np(cudaLaunchConfig_t& cfg, int np, const void* w, const __nv_bfloat16* xp, float* y, int n, int k,
                       int t) {
   switch (np) {
-    case 1: return cudaLaunchKernelEx(&cfg, linear_rows_kernel<F32W, 1>, w, xp, y, n, k, t);
-    case 2: return cudaLaunchKernelEx(&cfg, linear_rows_kernel<F32W, 2>, w, xp, y, n, k, t);
-    case 4: return cudaLaunchKernelEx(&cfg, linear_rows_kernel<F32W, 4>, w, xp, y, n, k, t);
-    default: return cudaLaunchKernelEx(&cfg, linear_rows_kernel<F32W, 8>, w, xp, y, n, k, t);
+    case 1: return cudaLaunchKernelEx(&cfg, linear_rows_kernel<F32W, 1, TW>, w, xp, y, n, k, t);
+    case 2: return cudaLaunchKernelEx(&cfg, linear_rows_kernel<F32W, 2, TW>, w, xp, y, n, k, t);
+    case 4: return cudaLaunchKernelEx(&cfg, linear_rows_kernel<F32W, 4, TW>, w, xp, y, n, k, t);
+    default:  // two tiles per warp stop at 4 passes (the reduction's shared memory)
+      return cudaLaunchKernelEx(&cfg, linear_rows_kernel<F32W, (TW == 2 ? 4 : 8), TW>, w, xp, y, n, k, t);
   }
 }
 
@@ -209,18 +220,22 @@ int linear_rows(const void* w, int w_dtype, const void* x_planes, float* y, int6
                 static_cast<long long>(n), static_cast<long long>(k));
   if ((reinterpret_cast<uintptr_t>(w) | reinterpret_cast<uintptr_t>(x_planes)) & 15)
     return fail(BT_ERR_INVALID, "linear_rows: w and the planes must be 16-byte aligned");
-  // passes of 8 tokens per block: as many as keep >= 2 blocks per SM busy
-  // (fewer weight re-reads), one when the matrix is small
+  // Two 16-row tiles per block when there are rows enough (each x plane load
+  // then serves 32 rows); passes of 8 tokens per block: as many as keep
+  // >= 2 blocks per SM busy (fewer weight re-reads), one when the matrix is
+  // small.  bf16 weights only: f32 ones are the small matrices.
   const int64_t tiles = n / 16, passes = (t + kPass - 1) / kPass, want = 2 * sm_count();
-  int np = 8;
-  while (np > 1 && (np > passes || tiles * ((passes + np - 1) / np) < want)) np >>= 1;
+  const int tw = (w_dtype == BT_BF16 && tiles % 2 == 0 && tiles / 2 >= want / 2 && passes > 1) ? 2 : 1;
+  int np = tw == 2 ? 4 : 8;
+  while (np > 1 && (np > passes || tiles / tw * ((passes + np - 1) / np) < want)) np >>= 1;
   cudaLaunchAttribute attr[1];
-  cudaLaunchConfig_t cfg = pdl_config(dim3(static_cast<unsigned>(tiles), static_cast<unsigned>((passes + np - 1) / np)),
-                                      stream, attr);
+  cudaLaunchConfig_t cfg = pdl_config(
+      dim3(static_cast<unsigned>(tiles / tw), static_cast<unsigned>((passes + np - 1) / np)), stream, attr);
   const int nn = static_cast<int>(n), kk = static_cast<int>(k), tt = static_cast<int>(t);
   const auto* xp = static_cast<const __nv_bfloat16*>(x_planes);
-  const cudaError_t e = w_dtype == BT_F32 ? launch_np<true>(cfg, np, w, xp, y, nn, kk, tt)
-                                          : launch_np<false>(cfg, np, w, xp, y, nn, kk, tt);
+  const cudaError_t e = w_dtype == BT_F32 ? launch_np<true, 1>(cfg, np, w, xp, y, nn, kk, tt)
+                        : tw == 2         ? launch_np<false, 2>(cfg, np, w, xp, y, nn, kk, tt)
+                                          : launch_np<false, 1>(cfg, np, w, xp, y, nn, kk, tt);
   if (e != cudaSuccess) return fail_cuda(e, "linear_rows launch");
   return BT_OK;
 }

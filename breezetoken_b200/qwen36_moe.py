@@ -329,10 +329,9 @@ class Qwen36Moe:
         inner = cfg.gdn_inner
         xp = self._planes(xn)
         entry = self._lin(layer["qkv"], xp)  # (B, C)
-        conv = self.conv_state[i]
-        window = torch.cat((conv, entry.unsqueeze(2)), dim=2)  # (B, C, conv)
-        mixed = torch.nn.functional.silu((window * layer["conv"]).sum(dim=-1))
-        conv.copy_(window[:, :, 1:])
+        mixed = torch.empty_like(entry)
+        N.call("bt_conv_silu", entry.data_ptr(), self.conv_state[i].data_ptr(), layer["conv"].data_ptr(),
+               mixed.data_ptr(), b, cfg.conv_dim, cfg.gdn_conv, _stream())
         q = mixed[:, : inner // 2].reshape(b, hk, dk).contiguous()
         k = mixed[:, inner // 2 : inner].reshape(b, hk, dk).contiguous()
         v = mixed[:, inner:].reshape(b, hv, dk).contiguous()

@@ -173,6 +173,14 @@ BT_API int bt_gdn_decode(const void* q, const void* k, const void* v, int in_dty
                   int64_t batch, int64_t heads_k, int64_t heads_v, int64_t dim,
                   float scale, float eps, void* stream);
 
+/* The GDN short conv (model/qwen36_moe.py:465-468) for `batch` sequences:
+ * window = [state (taps-1 per channel) | entry], out = silu(sum_j window[j] *
+ * w[c][j]) in tap order, state <- window[1:] (in place).  entry, out:
+ * (batch, channels); state: (batch, channels, taps-1); w: (channels, taps);
+ * taps in [2, 8].                                                         */
+BT_API int bt_conv_silu(const float* entry, float* state, const float* w, float* out,
+                 int64_t batch, int64_t channels, int64_t taps, void* stream);
+
 /* argmax with torch.argmax's first-index tie rule over rows of length n.
  * workspace: bt_argmax_workspace_bytes(rows) bytes, zeroed before first use. */
 BT_API int64_t bt_argmax_workspace_bytes(int64_t rows);
