@@ -214,20 +214,37 @@ def bench_moe(tokens: int, iters: int, shared: bool = True) -> dict:
             "l2": "flushed before each call (256 MB read)"}
 
 
-def bench_qwen36(batch: int, prompt: int, steps: int, layers: int) -> dict:
-    """BASELINE config 5 on one GPU: `batch` sequences of a `prompt`-token
-    random prompt, fed in lockstep, then `steps` greedy steps timed with CUDA
-    events; seeded random weights of the Qwen3.6-35B-A3B shape (with
-    `layers` layers) built on the device."""
+def bench_qwen36(batch: int, prompt: int, steps: int, layers: int) -> dict | None:
+    """`batch` sequences of a `prompt`-token random prompt,
+    fed in lockstep, then `steps` greedy steps timed with CUDA events; seeded
+    random weights of the Qwen3.6-35B-A3B shape (with `layers` layers) built
+    on the device.  Under torchrun the sequences are sharded: each of the N
+    ranks holds a full replica and decodes batch / N sequences, the timed
+    region is bracketed by barriers and the slowest rank's time counts; rank
+    0 returns the result, the others None."""
+    import os
     from dataclasses import replace
 
     from breezetoken_b200.qwen36_moe import Qwen36Moe
+    from breezetoken_b200.shard import aggregate_rate, max_over_ranks
     from breezetoken_b200.synth import QWEN36_35B
 
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", "0")))
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600))
+        if batch % world:
+            raise ValueError(f"batch {batch} does not split over {world} GPUs")
+    local = batch // world
     spec = replace(QWEN36_35B, n_layers=layers)
-    m = Qwen36Moe.random(spec, batch=batch, max_context=prompt + steps + 1)
-    rng = np.random.default_rng(4)
-    toks = torch.from_numpy(rng.integers(0, spec.vocab, (prompt, batch))).cuda()
+    m = Qwen36Moe.random(spec, batch=local, max_context=prompt + steps + 1)
+    rng = np.random.default_rng(4 + rank)
+    toks = torch.from_numpy(rng.integers(0, spec.vocab, (prompt, local))).cuda()
     t0 = time.time()
     for i in range(prompt - 1):
         m._step(toks[i], i, logits=False)
@@ -236,6 +253,8 @@ def bench_qwen36(batch: int, prompt: int, steps: int, layers: int) -> dict:
     prefill_s = time.time() - t0
     m.graph_decode(nxt, prompt, 1)  # capture (and one step)
     torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
     h0 = time.perf_counter()
@@ -243,25 +262,33 @@ def bench_qwen36(batch: int, prompt: int, steps: int, layers: int) -> dict:
     host = time.perf_counter() - h0  # enqueue time: close to `sec` when launches, not kernels, bound the step
     e1.record()
     e1.synchronize()
-    sec = e0.elapsed_time(e1) / 1e3
+    sec, prefill_s = max_over_ranks([e0.elapsed_time(e1) / 1e3, prefill_s], "cuda")
+    if world > 1:
+        dist.barrier()
     cfg = m.cfg
     # per-step algorithmic bytes (bf16 non-expert weights without the
     # embedding gather, selected experts at the expected number of distinct
     # experts per layer, GDN state r+w, f32 KV read at the mean context)
-    u = cfg.n_experts * (1 - (1 - cfg.top_k / cfg.n_experts) ** batch)
+    u = cfg.n_experts * (1 - (1 - cfg.top_k / cfg.n_experts) ** local)
     dense = sum(t.numel() * t.element_size() for layer in m.layers for k, t in layer.items()
                 if isinstance(t, torch.Tensor)) + m.head.numel() * 2
     dense += sum(sum(x.numel() * x.element_size() for x in (la["shared"].gate, la["shared"].up, la["shared"].down))
                  for la in m.layers)
     n_gdn = cfg.n_layers - len(cfg.attn_layers)
-    state = batch * n_gdn * cfg.gdn_value_heads * cfg.gdn_k_dim * cfg.gdn_value_dim * 4 * 2
-    kv = batch * (prompt + steps / 2) * len(cfg.attn_layers) * 2 * cfg.n_kv * cfg.head_dim * 4
-    step_bytes = dense + cfg.n_layers * u * 1_351_680 + state + kv
+    state = local * n_gdn * cfg.gdn_value_heads * cfg.gdn_k_dim * cfg.gdn_value_dim * 4 * 2
+    kv = local * (prompt + steps / 2) * len(cfg.attn_layers) * 2 * cfg.n_kv * cfg.head_dim * 4
+    step_bytes = dense + cfg.n_layers * u * 1_351_680 + state + kv  # per GPU
     m.close()
-    return {"kernel": "qwen36_35b_decode", "layers": layers, "batch": batch, "prompt": prompt, "steps": steps,
-            "tok_s": batch * steps / sec, "ms_per_step": sec / steps * 1e3,
+    if world > 1:
+        dist.destroy_process_group()
+    if rank != 0:
+        return None
+    return {"kernel": "qwen36_35b_decode", "layers": layers, "n_gpus": world, "batch": batch, "batch_per_gpu": local,
+            "prompt": prompt, "steps": steps, "tok_s": aggregate_rate(local * steps, world, sec),
+            "scaling": "strong (64 sequences split over the GPUs)", "ms_per_step": sec / steps * 1e3,
             "host_enqueue_ms_per_step": host / steps * 1e3, "prefill_s": prefill_s,
-            "expected_unique_experts": u, "step_bytes": step_bytes, "gbs": step_bytes * steps / sec / 1e9}
+            "expected_unique_experts": u, "step_bytes_per_gpu": step_bytes,
+            "gbs_per_gpu": step_bytes * steps / sec / 1e9}
 
 
 def trace_step(gguf: str, max_context: int, steps: int) -> str:
@@ -342,7 +369,8 @@ def main() -> None:
         r = bench_gdn(args.batch, args.steps)
     else:
         r = bench_attn(args.batch, args.ctx, args.splits, args.iters)
-    print(json.dumps(r), flush=True)
+    if r is not None:
+        print(json.dumps(r), flush=True)
 
 
 if __name__ == "__main__":
