@@ -293,6 +293,8 @@ def bench_qwen36(batch: int, prompt: int, steps: int, layers: int) -> dict | Non
 
 def trace_step(gguf: str, max_context: int, steps: int) -> str:
     """Per-kernel-kind device timeline of a decode step (model.Qwen35.trace_step):
+    entered = previous kernel's last CTA exit -> this kernel's last CTA entry
+    (negative: resident before the previous kernel ended);
     gap = previous kernel's last CTA exit -> this kernel's last CTA past the
     dependency wait; prologue = -> last CTA ready for its main loop; body =
     -> last CTA exit; loads = -> last CTA with its activation loads back (GEMV)."""
@@ -312,18 +314,21 @@ def trace_step(gguf: str, max_context: int, steps: int) -> str:
     prev_end = 0.0
     for t in tl:
         kind = t["name"].split(".")[-1]
-        a = agg.setdefault(kind, [0, 0.0, 0.0, 0.0, 0.0, 0.0])
+        a = agg.setdefault(kind, [0, 0.0, 0.0, 0.0, 0.0, 0.0, 0.0])
         a[0] += 1
         a[1] += t["released"] - prev_end
         a[2] += t["ready"] - t["released"]
         a[3] += t["end"] - t["ready"]
         a[4] += t["end"] - prev_end
         a[5] += (t["loaded"] - t["released"]) if t.get("loaded") else 0.0
+        a[6] += t["entered"] - prev_end
         prev_end = t["end"]
     lines = [f"step: {len(tl)} kernels, {tl[-1]['end']:.1f} us from first entry to last exit",
-             f"{'kind':11s} {'n':>3s} {'total us':>9s} {'gap':>6s} {'prologue':>9s} {'(loads)':>8s} {'body':>7s}"]
-    for k, (n, gap, pro, body, tot, ld) in sorted(agg.items(), key=lambda x: -x[1][4]):
-        lines.append(f"{k:11s} {n:3d} {tot:9.1f} {gap / n:6.2f} {pro / n:9.2f} {ld / n:8.2f} {body / n:7.2f}")
+             f"{'kind':11s} {'n':>3s} {'total us':>9s} {'entered':>8s} {'gap':>6s} {'prologue':>9s} {'(loads)':>8s}"
+             f" {'body':>7s}"]
+    for k, (n, gap, pro, body, tot, ld, ent) in sorted(agg.items(), key=lambda x: -x[1][4]):
+        lines.append(f"{k:11s} {n:3d} {tot:9.1f} {ent / n:8.2f} {gap / n:6.2f} {pro / n:9.2f} {ld / n:8.2f} "
+                     f"{body / n:7.2f}")
     return "\n".join(lines)
 
 

@@ -432,8 +432,8 @@ class Qwen35:
         """Device-side timeline of the last of ``steps`` decode steps, replayed
         as one captured graph from the current state (which it advances).
 
-        Returns one dict per launch: name, start (first CTA entry), released
-        (last CTA past the dependency wait), ready (last CTA past its
+        Returns one dict per launch: name, start (first CTA entry), entered
+        (last CTA entry), released (last CTA past the dependency wait), ready (last CTA past its
         prologue) and end (last CTA exit), in microseconds from the step's
         first entry."""
         n = self.kernels_per_step()
@@ -474,6 +474,7 @@ class Qwen35:
             out.append({
                 "name": nm,
                 "start": (int(r[i, 0]) - t0) / 1e3,
+                "entered": (int(r[i, 1]) - t0) / 1e3,
                 "released": (int(r[i, 3]) - t0) / 1e3,
                 "ready": (int(r[i, 4]) - t0) / 1e3,
                 "loaded": (int(r[i, 7]) - t0) / 1e3 if r[i, 7] else None,
