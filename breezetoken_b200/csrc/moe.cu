@@ -807,6 +807,44 @@ __device__ __forceinline__ bool slot_of(int u, bool direct, const int32_t* ids, 
 
 __device__ __forceinline__ int pair_of(bool direct, const MoeWs& ws, int i) { return direct ? i : ws.pairs[i]; }
 
+// The slot records of a CTA's item range, read once into shared memory so
+// that looking up the next item (to load its tiles ahead) costs no global
+// round trip.  A CTA's contiguous range spans a few slots; one past the
+// cache falls back to global memory.
+constexpr int kSlotCache = 16;
+struct SlotCache {
+  int first, n;
+  int expert[kSlotCache], start[kSlotCache], count[kSlotCache], live[kSlotCache];
+};
+
+__device__ __forceinline__ void fill_slots(SlotCache& sc, int i0, int i1, int chunks, bool direct, const int32_t* ids,
+                                           int n_experts, const MoeWs& ws) {
+  const int first = i0 / chunks;
+  const int n = i1 > i0 ? min(kSlotCache, (i1 - 1) / chunks - first + 1) : 0;
+  if (threadIdx.x < n) {
+    Slot s{};
+    sc.live[threadIdx.x] = slot_of(first + threadIdx.x, direct, ids, n_experts, ws, s) ? 1 : 0;
+    sc.expert[threadIdx.x] = s.expert;
+    sc.start[threadIdx.x] = s.start;
+    sc.count[threadIdx.x] = s.count;
+  }
+  if (threadIdx.x == 0) {
+    sc.first = first;
+    sc.n = n;
+  }
+  __syncthreads();
+}
+
+__device__ __forceinline__ bool cached_slot(const SlotCache& sc, int u, bool direct, const int32_t* ids,
+                                            int n_experts, const MoeWs& ws, Slot& s) {
+  const int i = u - sc.first;
+  if (i < 0 || i >= sc.n) return slot_of(u, direct, ids, n_experts, ws, s);
+  s.expert = sc.expert[i];
+  s.start = sc.start[i];
+  s.count = sc.count[i];
+  return sc.live[i] != 0;
+}
+
 // sum_k w[k] * dn[k * stride] over a token's top_k pairs in routing order,
 // each product rounded before the add like the reference's (out * w).sum(0)
 // in f32; pairs with an invalid id contribute nothing.  Eight pairs' loads
@@ -867,10 +905,12 @@ __global__ void __launch_bounds__(kThreads, 2)
   const int tp = warp % TP, kb = warp / TP;
   const uint32_t lane_off = static_cast<uint32_t>(lane & 15) * 8u;
   const uint8_t* xl = xs + (g >> 1) * token_stride(K) + (g & 1) * plane_stride(K) + 16 * t;
+  __shared__ SlotCache sc;
+  fill_slots(sc, i0, i1, chunks, direct != 0, ids, n_experts, ws);
   auto load_item = [&](int it, Tile& tg, Tile& tu) {
     const int u = it / chunks, c = it - u * chunks;
     Slot s;
-    if (!slot_of(u, direct != 0, ids, n_experts, ws, s)) return;
+    if (!cached_slot(sc, u, direct != 0, ids, n_experts, ws, s)) return;
     const int64_t off = ((static_cast<int64_t>(s.expert) * (ffn / 16) + c * TP + tp) * KB + kb) * kChunkBytes;
     load_tile(gate + off, lane, tg);
     load_tile(up + off, lane, tu);
@@ -881,7 +921,7 @@ __global__ void __launch_bounds__(kThreads, 2)
   for (int it = i0; it < i1; ++it) {
     const int u = it / chunks, c = it - u * chunks;
     Slot s;
-    const bool live = slot_of(u, direct != 0, ids, n_experts, ws, s);
+    const bool live = cached_slot(sc, u, direct != 0, ids, n_experts, ws, s);
     if (it + 1 < i1) load_item(it + 1, ng, nu);
     for (int c0 = 0; live && c0 < s.count; c0 += kTokensPerPass) {
       const int mc = min(kTokensPerPass, s.count - c0);
@@ -954,10 +994,12 @@ __global__ void __launch_bounds__(kThreads, 2)
   const int tp = warp % TP, kb = warp / TP;
   const uint32_t lane_off = static_cast<uint32_t>(lane & 15) * 8u;
   const uint8_t* xl = xs + (g >> 1) * token_stride(K) + (g & 1) * plane_stride(K) + 16 * t;
+  __shared__ SlotCache sc;
+  fill_slots(sc, i0, i1, chunks, direct != 0, ids, n_experts, ws);
   auto load_item = [&](int it, Tile& ta, Tile& tb) {
     const int u = it / chunks, c = it - u * chunks;
     Slot s;
-    if (!slot_of(u, direct != 0, ids, n_experts, ws, s)) return;
+    if (!cached_slot(sc, u, direct != 0, ids, n_experts, ws, s)) return;
     const int64_t tile = static_cast<int64_t>(s.expert) * (hidden / 16) + c * 2 * TP + 2 * tp;
     load_tile(down + (tile * KB + kb) * kChunkBytes, lane, ta);
     load_tile(down + ((tile + 1) * KB + kb) * kChunkBytes, lane, tb);
@@ -971,7 +1013,7 @@ __global__ void __launch_bounds__(kThreads, 2)
   for (int it = i0; it < i1; ++it) {
     const int u = it / chunks, c = it - u * chunks;
     Slot s;
-    const bool live = slot_of(u, direct != 0, ids, n_experts, ws, s);
+    const bool live = cached_slot(sc, u, direct != 0, ids, n_experts, ws, s);
     if (it + 1 < i1) load_item(it + 1, na, nb);
     for (int c0 = 0; live && c0 < s.count; c0 += kTokensPerPass) {
       const int mc = min(kTokensPerPass, s.count - c0);
