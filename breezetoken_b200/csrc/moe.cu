@@ -40,7 +40,6 @@
 #include <algorithm>
 
 #include "errors.h"
-#include "gemv_q8.cuh"
 #include "moe.cuh"
 
 namespace bt {
