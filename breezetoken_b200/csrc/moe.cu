@@ -110,7 +110,11 @@ constexpr int kRangeBytes = 4 * 2 * kRangeDown;
 
 // Tile chunk: 16 rows x 256 weights.  Sections (lane L = 4 g + t, group
 // q = 2 s + h of the lane's 16 per row: sub-block s, weights 8t + 4h ..):
-//   [0, 512)     qs of row g:   16 B per lane, byte q = qs[8s + 2t + h]
+//   [0, 512)     qs of row g:   16 B per lane, byte 4 (q % 4) + q / 4 =
+//                qs[8s + 2t + h] (word j = q % 4 holds the four sub-block
+//                pairs' bytes of that group position, so the kernels pick
+//                pair p's byte with a prmt selector instead of rotating
+//                registers)
 //   [512, 1024)  qs of row g+8: same
 //   [1024, 1536) signs: per lane (row g: S0, S1; row g+8: S0, S1); S0 bit
 //                15 - q / 31 - q = sign of weight 0 / 1 of group q, S1 the
@@ -151,7 +155,7 @@ __global__ void repack_iq3s_kernel(const uint8_t* __restrict__ src, uint8_t* __r
       for (int s = 0; s < 8; ++s)
         for (int h = 0; h < 2; ++h) {
           const int grp = 2 * s + h;
-          q[grp] = blk[2 + 8 * s + 2 * t + h];
+          q[4 * (grp & 3) + (grp >> 2)] = blk[2 + 8 * s + 2 * t + h];
           const uint32_t nib = (blk[74 + 4 * s + t] >> (4 * h)) & 15u;
           s01 |= ((nib & 1u) << (15 - grp)) | (((nib >> 1) & 1u) << (31 - grp));
           s23 |= (((nib >> 2) & 1u) << (15 - grp)) | (((nib >> 3) & 1u) << (31 - grp));
@@ -664,21 +668,20 @@ __device__ __forceinline__ void load_tile(const uint8_t* chunk, int lane, Tile& 
   T.rb = __ldg(reinterpret_cast<const uint2*>(chunk + kScales) + g + 8);
 }
 
-// A tile's words for the current pair of sub-blocks; block_steps advances
-// it by two sub-blocks per step of a rolled loop, so the code of one step is
-// all that is live beside the tiles.
+// A tile's sign, qh and scale words for the current pair of sub-blocks;
+// block_steps advances it by two sub-blocks per step of a rolled loop, so the
+// code of one step is all that is live beside the tiles.  (The qs words stay
+// in the tile: a step picks its pair's bytes with a prmt selector.)
 struct Cursor {
-  uint4 qa, qb;              // .x: qs bytes of the current pair (byte 2s+h)
   uint32_t s0a, s1a, s0b, s1b;  // sign words of rows g, g+8, shifted to the pair
-  uint32_t qh;               // bits 2s+h (row g), 16+2s+h (row g+8)
-  uint32_t sca, scb;         // scale nibbles of rows g, g+8 (nibble s)
-  float da, db;              // d of rows g, g+8
+  uint32_t qh;                  // bits 2s+h (row g), 16+2s+h (row g+8)
+  uint32_t sca, scb;            // scale nibbles of rows g, g+8 (nibble s)
+  float da, db;                 // d of rows g, g+8
+  float dna, dnb;               // -2^23 d (exact: a power-of-two multiple)
 };
 
 __device__ __forceinline__ Cursor cursor_of(const Tile& T) {
   Cursor c;
-  c.qa = T.qa;
-  c.qb = T.qb;
   c.s0a = T.sg.x;
   c.s1a = T.sg.y;
   c.s0b = T.sg.z;
@@ -688,12 +691,12 @@ __device__ __forceinline__ Cursor cursor_of(const Tile& T) {
   c.scb = T.rb.x;
   c.da = __half2float(__ushort_as_half(static_cast<unsigned short>(T.ra.y & 0xFFFFu)));
   c.db = __half2float(__ushort_as_half(static_cast<unsigned short>(T.rb.y & 0xFFFFu)));
+  c.dna = -8388608.0f * c.da;
+  c.dnb = -8388608.0f * c.db;
   return c;
 }
 
 __device__ __forceinline__ void cursor_next(Cursor& c) {
-  c.qa = make_uint4(c.qa.y, c.qa.z, c.qa.w, 0u);
-  c.qb = make_uint4(c.qb.y, c.qb.z, c.qb.w, 0u);
   c.s0a <<= 4;
   c.s1a <<= 4;
   c.s0b <<= 4;
@@ -705,26 +708,32 @@ __device__ __forceinline__ void cursor_next(Cursor& c) {
 
 // fp16 weights (w0, w1), (w2, w3) of group 2t+H of sub-block S (0/1 within
 // the current pair), row g (R = 0) or g+8.  `lut` is the codebook's shared
-// memory, `lane_off` this lane's copy offset (byte 0 of the word).
+// memory, `lane_off` this lane's copy offset (byte 0 of the word), `sel` the
+// prmt selector of the current pair p: (qs byte p of word 2S+H << 8) |
+// lane_off.
 template <int S, int R, int H>
-__device__ __forceinline__ uint2 tile_word(const Cursor& c, const uint8_t* lut, uint32_t lane_off) {
-  const uint32_t qw = R ? c.qb.x : c.qa.x;
-  // (qs byte << 8) | lane_off
-  constexpr uint32_t kSel = 4u | (static_cast<uint32_t>((S << 1) | H) << 4) | (5u << 8) | (5u << 12);
-  constexpr int QB = 16 * R + 2 * S + H;
+__device__ __forceinline__ uint2 tile_word(const Tile& T, const Cursor& c, const uint8_t* lut, uint32_t lane_off,
+                                           uint32_t sel) {
+  constexpr int J = 2 * S + H;
+  const uint4& q = R ? T.qb : T.qa;
+  const uint32_t qw = J == 0 ? q.x : J == 1 ? q.y : J == 2 ? q.z : q.w;
+  constexpr int QB = 16 * R + J;
   const uint32_t hb = QB >= 7 ? (c.qh >> (QB - 7)) : (c.qh << (7 - QB));
-  const uint32_t off = prmt(qw, lane_off, kSel) | (hb & 0x80u);
+  const uint32_t off = prmt(qw, lane_off, sel) | (hb & 0x80u);
   uint2 w = *reinterpret_cast<const uint2*>(lut + off);
-  constexpr int SH = 2 * S + H;
-  w.x ^= ((R ? c.s0b : c.s0a) << SH) & 0x80008000u;
-  w.y ^= ((R ? c.s1b : c.s1a) << SH) & 0x80008000u;
+  w.x ^= ((R ? c.s0b : c.s0a) << J) & 0x80008000u;
+  w.y ^= ((R ? c.s1b : c.s1a) << J) & 0x80008000u;
   return w;
 }
 
+// d * (1 + 2 * nibble s) (quant/dequant.py:164-185), as one fma: the float
+// with bits 0x4B000000 | (2n + 1) is 2^23 + 2n + 1, so m * d - 2^23 d is
+// (2n + 1) d exactly (an 11-bit by 5-bit product), rounded once: the same
+// value as the f32 product.
 template <int S>
-__device__ __forceinline__ float row_scale(uint32_t nibbles, float d) {
-  const uint32_t nib = (nibbles >> (4 * S)) & 15u;
-  return d * static_cast<float>(1 + 2 * static_cast<int>(nib));  // quant/dequant.py:164-185
+__device__ __forceinline__ float row_scale(uint32_t nibbles, float d, float dneg) {
+  const uint32_t two_n = (S == 0 ? (nibbles << 1) : (nibbles >> 3)) & 0x1Eu;
+  return fmaf(__uint_as_float(0x4B000001u | two_n), d, dneg);
 }
 
 __device__ __forceinline__ void mma_f16(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
@@ -739,15 +748,15 @@ __device__ __forceinline__ void mma_f16(float (&c)[4], uint32_t a0, uint32_t a1,
 // g+8, token column pair t.  `b`: elements 8t..8t+7 of the sub-block of
 // this lane's B column (token g/2, plane g%2).
 template <int S>
-__device__ __forceinline__ void tile_step(const Cursor& c, const uint8_t* lut, uint32_t lane_off, const uint4& b,
-                                          float (&acc)[2]) {
-  const uint2 w00 = tile_word<S, 0, 0>(c, lut, lane_off), w10 = tile_word<S, 1, 0>(c, lut, lane_off);
-  const uint2 w01 = tile_word<S, 0, 1>(c, lut, lane_off), w11 = tile_word<S, 1, 1>(c, lut, lane_off);
+__device__ __forceinline__ void tile_step(const Tile& T, const Cursor& c, const uint8_t* lut, uint32_t lane_off,
+                                          uint32_t sel, const uint4& b, float (&acc)[2]) {
+  const uint2 w00 = tile_word<S, 0, 0>(T, c, lut, lane_off, sel), w10 = tile_word<S, 1, 0>(T, c, lut, lane_off, sel);
+  const uint2 w01 = tile_word<S, 0, 1>(T, c, lut, lane_off, sel), w11 = tile_word<S, 1, 1>(T, c, lut, lane_off, sel);
   float cc[4] = {0.f, 0.f, 0.f, 0.f};
   mma_f16(cc, w00.x, w10.x, w00.y, w10.y, b.x, b.y);  // groups 2t: weights 8t .. 8t+3
   mma_f16(cc, w01.x, w11.x, w01.y, w11.y, b.z, b.w);  // groups 2t+1: weights 8t+4 .. 8t+7
-  acc[0] = fmaf(row_scale<S>(c.sca, c.da), cc[0] + cc[1], acc[0]);
-  acc[1] = fmaf(row_scale<S>(c.scb, c.db), cc[2] + cc[3], acc[1]);
+  acc[0] = fmaf(row_scale<S>(c.sca, c.da, c.dna), cc[0] + cc[1], acc[0]);
+  acc[1] = fmaf(row_scale<S>(c.scb, c.db, c.dnb), cc[2] + cc[3], acc[1]);
 }
 
 // All 8 sub-blocks of K-block `kb` for two tiles sharing the B operands,
@@ -757,14 +766,17 @@ __device__ __forceinline__ void block_steps(const Tile& ta, const Tile& tb, cons
                                             const uint8_t* xl, int kb, float (&acc)[2][2]) {
   Cursor ca = cursor_of(ta), cb = cursor_of(tb);
   const uint8_t* xq = xl + kb * 512;  // 8 sub-blocks x 32 fp16
+  // prmt selector: byte 0 <- lane_off byte 0, byte 1 <- qs word byte p,
+  // bytes 2, 3 <- lane_off byte 1 (zero)
+  uint32_t sel = 0x5504u;
 #pragma unroll 1
-  for (int p = 0; p < 4; ++p) {
+  for (int p = 0; p < 4; ++p, sel += 0x10u) {
     const uint4 b0 = *reinterpret_cast<const uint4*>(xq + 128 * p);
     const uint4 b1 = *reinterpret_cast<const uint4*>(xq + 128 * p + 64);
-    tile_step<0>(ca, lut, lane_off, b0, acc[0]);
-    tile_step<0>(cb, lut, lane_off, b0, acc[1]);
-    tile_step<1>(ca, lut, lane_off, b1, acc[0]);
-    tile_step<1>(cb, lut, lane_off, b1, acc[1]);
+    tile_step<0>(ta, ca, lut, lane_off, sel, b0, acc[0]);
+    tile_step<0>(tb, cb, lut, lane_off, sel, b0, acc[1]);
+    tile_step<1>(ta, ca, lut, lane_off, sel, b1, acc[0]);
+    tile_step<1>(tb, cb, lut, lane_off, sel, b1, acc[1]);
     cursor_next(ca);
     cursor_next(cb);
   }

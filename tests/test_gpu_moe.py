@@ -46,12 +46,14 @@ def pack_iq3s_tiles(raw: np.ndarray, rows: int, k: int) -> np.ndarray:
     qs of rows g+8 (512 B), sign words (512 B), qh words (128 B), per-row
     scales + d (128 B)], lane L = 4g + t holding groups 2t, 2t+1 of every
     sub-block (quant/dequant.py:164-185 field meanings); group q = 2s + h of
-    a lane's row has its weight-0/1 signs at bits 15 - q / 31 - q of sign
-    word S0 and its weight-2/3 signs at the same bits of S1."""
+    a lane's row has its qs byte at byte 4 (q % 4) + q // 4 of the lane's 16,
+    its weight-0/1 signs at bits 15 - q / 31 - q of sign word S0 and its
+    weight-2/3 signs at the same bits of S1."""
     kb = k // 256
     b = np.ascontiguousarray(raw).reshape(rows // 16, 2, 8, kb, 110)  # (tile, half r, g, block, byte)
     qs = b[..., 2:66].reshape(rows // 16, 2, 8, kb, 8, 4, 2)  # (.., s, t, h)
-    qs = qs.transpose(0, 3, 1, 2, 5, 4, 6).reshape(rows // 16, kb, 2, 512)  # (tile, block, r, g t s h)
+    qs = qs.reshape(rows // 16, 2, 8, kb, 4, 2, 4, 2)  # (.., pair p, S, t, h): s = 2p + S
+    qs = qs.transpose(0, 3, 1, 2, 6, 5, 7, 4).reshape(rows // 16, kb, 2, 512)  # (tile, block, r, g t S h p)
     sg = b[..., 74:106].reshape(rows // 16, 2, 8, kb, 8, 4).astype(np.uint32)  # (.., s, t)
     words = np.zeros((rows // 16, 2, 8, kb, 4, 2), np.uint32)  # (.., t, word S0 / S1)
     for s in range(8):

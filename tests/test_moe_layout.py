@@ -1,5 +1,6 @@
 """CPU checks of the IQ3_S expert tile layout and the decode rules the
-expert kernels apply to it (moe.cu: tile_word, row_scale, cursor_next),
+expert kernels apply to it (moe.cu: tile_word, row_scale, cursor_next,
+block_steps),
 restated here lane by lane: the layout keeps every GGUF byte, and the decode
 reproduces the oracle's dequantisation (quant/dequant.py:164-185) bit for
 bit."""
@@ -42,7 +43,7 @@ def test_tile_layout_keeps_every_gguf_byte() -> None:
                     for s in range(8):
                         for h in range(2):
                             q = 2 * s + h
-                            out[row, kb, 2 + 8 * s + 2 * t + h] = qs[q]
+                            out[row, kb, 2 + 8 * s + 2 * t + h] = qs[4 * (q & 3) + (q >> 2)]
                             nib = ((s01 >> (15 - q)) & 1) | (((s01 >> (31 - q)) & 1) << 1)
                             nib |= (((s23 >> (15 - q)) & 1) << 2) | (((s23 >> (31 - q)) & 1) << 3)
                             out[row, kb, 74 + 4 * s + t] |= nib << (4 * h)
@@ -79,25 +80,35 @@ def test_kernel_decode_rules_reproduce_the_dequantisation() -> None:
                 rec = [c[1664 + 8 * g:1672 + 8 * g], c[1664 + 8 * (g + 8):1672 + 8 * (g + 8)]]
                 sc = [_u32(x[:4]) for x in rec]
                 d = [np.frombuffer(x[4:6].tobytes(), np.float16)[0].astype(np.float32) for x in rec]
+                dneg = [np.float32(-8388608.0) * x for x in d]
                 lane_off = (lane & 15) * 8
                 for p in range(4):
+                    sel = 0x5504 + 16 * p
                     for S in range(2):
                         for R in range(2):
                             for H in range(2):
-                                byte = ((cur["qb"] if R else cur["qa"])[0] >> (8 * ((S << 1) | H))) & 255
+                                qw = (cur["qb"] if R else cur["qa"])[(S << 1) | H]
+                                src = qw | (lane_off << 32)  # prmt: bytes 0-3 of a, 4-7 of b
+                                off = 0
+                                for i in range(4):
+                                    off |= ((src >> (8 * ((sel >> (4 * i)) & 7))) & 255) << (8 * i)
+                                assert off == (((qw >> (8 * p)) & 255) << 8) | lane_off
                                 qb = 16 * R + 2 * S + H
                                 hb = (cur["qh"] >> (qb - 7)) if qb >= 7 else ((cur["qh"] << (7 - qb)) & mask)
-                                off = (byte << 8) | lane_off | (hb & 0x80)
+                                off |= hb & 0x80
                                 wx, wy = _u32(lut[off:off + 4]), _u32(lut[off + 4:off + 8])
                                 sh = 2 * S + H
                                 wx ^= ((cur["s0b"] if R else cur["s0a"]) << sh) & 0x80008000
                                 wy ^= ((cur["s1b"] if R else cur["s1a"]) << sh) & 0x80008000
                                 w4 = np.frombuffer(np.array([wx, wy], np.uint32).tobytes(), np.float16)
+                                two_n = ((sc[R] << 1) if S == 0 else (sc[R] >> 3)) & 0x1E
+                                m = np.frombuffer(np.uint32(0x4B000001 | two_n).tobytes(), np.float32)[0]
+                                # fma(m, d, -2^23 d), restated exactly in f64, rounded once to f32
+                                db = np.float32(np.float64(m) * np.float64(d[R]) + np.float64(dneg[R]))
                                 nib = (sc[R] >> (4 * S)) & 15
-                                db = np.float32(d[R]) * np.float32(1 + 2 * nib)
+                                assert db == np.float32(d[R]) * np.float32(1 + 2 * nib)
                                 base = kb * 256 + 32 * (2 * p + S) + 8 * t + 4 * H
                                 got[16 * tile + g + 8 * R, base:base + 4] = db * w4.astype(np.float32)
-                    cur["qa"], cur["qb"] = cur["qa"][1:] + [0], cur["qb"][1:] + [0]
                     for key in ("s0a", "s1a", "s0b", "s1b"):
                         cur[key] = (cur[key] << 4) & mask
                     cur["qh"] >>= 4
