@@ -126,8 +126,14 @@ constexpr int kQsA = 0, kQsB = 512, kSigns = 1024, kQh = 1536, kScales = 1664;
 static_assert(kChunkBytes == 1792, "tile chunk");
 
 constexpr int kTokensPerPass = 4;              // 8 MMA columns: hi and lo per token
-constexpr int kRedBytes = kWarps * 32 * 4 * 4;  // 4 partial sums per lane
-constexpr int kMiscBytes = 256;                 // token scales, block maxima
+// 4 partial sums per lane; two buffers, so that a pass may write its sums
+// while the previous pass's epilogue still reads the other buffer
+constexpr int kRedFloats = kWarps * 32 * 4;
+constexpr int kRedBytes = 2 * kRedFloats * 4;
+// token scales [0, 16), block maxima [16, 24), the staged tokens' pair ids
+// (ints) [32, 32 + kTokensPerPass)
+constexpr int kMiscBytes = 256;
+constexpr int kMiscPair = 32;
 
 // fp16 planes of one vector of K elements in shared memory: hi at 0, lo at
 // plane_stride (== 64 mod 128 bytes, so a quarter warp's hi and lo reads
@@ -897,6 +903,7 @@ __global__ void __launch_bounds__(kThreads, 2)
   uint8_t* lut = smem;
   float* red = reinterpret_cast<float*>(smem + kLutBytes);
   float* xsc = reinterpret_cast<float*>(smem + kLutBytes + kRedBytes);
+  int* spair = reinterpret_cast<int*>(xsc) + kMiscPair;
   uint8_t* xs = smem + kLutBytes + kRedBytes + kMiscBytes;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
   if (static_cast<int>(blockIdx.x) < s_blocks) {  // the shared expert's down rows
@@ -929,6 +936,7 @@ __global__ void __launch_bounds__(kThreads, 2)
   Tile tg{}, tu{}, ng{}, nu{};
   if (i0 < i1) load_item(i0, tg, tu);
   int staged = -1;  // (slot, first pair) whose tokens are in xs
+  int npass = 0;    // passes so far: the reduction buffer of a pass is npass & 1
   for (int it = i0; it < i1; ++it) {
     const int u = it / chunks, c = it - u * chunks;
     Slot s;
@@ -946,31 +954,36 @@ __global__ void __launch_bounds__(kThreads, 2)
                      ws.xenc + static_cast<int64_t>(tok) * 4 * K + plane * 2 * K + 16 * piece);
         }
         cp_async_commit();
-        if (threadIdx.x < mc) xsc[threadIdx.x] = ws.xscale[pair_of(direct != 0, ws, s.start + c0 + threadIdx.x) / top_k];
+        if (threadIdx.x < mc) {
+          const int pair = pair_of(direct != 0, ws, s.start + c0 + threadIdx.x);
+          spair[threadIdx.x] = pair;
+          xsc[threadIdx.x] = ws.xscale[pair / top_k];
+        }
         cp_async_wait_all();
         __syncthreads();
         staged = u * 4096 + c0;
       }
       float acc[2][2] = {};
       block_steps(tg, tu, lut, lane_off, xl, kb, acc);
-      reinterpret_cast<float4*>(red)[warp * 32 + lane] = make_float4(acc[0][0], acc[0][1], acc[1][0], acc[1][1]);
+      float* rb = red + (npass++ & 1) * kRedFloats;
+      reinterpret_cast<float4*>(rb)[warp * 32 + lane] = make_float4(acc[0][0], acc[0][1], acc[1][0], acc[1][1]);
       __syncthreads();
+      // (no barrier after the epilogue: the next pass writes the other
+      // buffer, and a restaging of xs/xsc/spair starts with a barrier)
       for (int i = threadIdx.x; i < OUT * mc; i += kThreads) {
         const int v = i / OUT, o = i - v * OUT;
         const int otp = o >> 4, r = o & 15, src = (r & 7) * 4 + v, reg = r >> 3;
         float gs = 0.f, us = 0.f;
 #pragma unroll
         for (int k = 0; k < KB; ++k) {
-          const float* rr = red + ((k * TP + otp) * 32 + src) * 4;
+          const float* rr = rb + ((k * TP + otp) * 32 + src) * 4;
           gs += rr[reg];
           us += rr[2 + reg];
         }
         gs *= xsc[v];
         us *= xsc[v];
-        const int pair = pair_of(direct != 0, ws, s.start + c0 + v);
-        ws.act[static_cast<int64_t>(pair) * ffn + c * OUT + o] = silu_f(gs) * us;
+        ws.act[static_cast<int64_t>(spair[v]) * ffn + c * OUT + o] = silu_f(gs) * us;
       }
-      __syncthreads();  // red and xsc readers done
     }
     tg = ng;
     tu = nu;
@@ -996,6 +1009,7 @@ __global__ void __launch_bounds__(kThreads, 2)
   float* red = reinterpret_cast<float*>(smem + kLutBytes);
   float* xsc = reinterpret_cast<float*>(smem + kLutBytes + kRedBytes);
   float* wmax = xsc + 16;
+  int* spair = reinterpret_cast<int*>(xsc) + kMiscPair;
   uint8_t* xs = smem + kLutBytes + kRedBytes + kMiscBytes;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
   stage_lut(lut);
@@ -1021,6 +1035,7 @@ __global__ void __launch_bounds__(kThreads, 2)
   pdl_wait();
   __shared__ int s_last;
   int staged = -1;
+  int npass = 0;  // the reduction buffer of a pass is npass & 1
   for (int it = i0; it < i1; ++it) {
     const int u = it / chunks, c = it - u * chunks;
     Slot s;
@@ -1036,9 +1051,8 @@ __global__ void __launch_bounds__(kThreads, 2)
         float4 h[F4];
         float m = 0.f;
         const float4* src = nullptr;
-        if (v < mc)
-          src = reinterpret_cast<const float4*>(ws.act +
-                                                static_cast<int64_t>(pair_of(direct != 0, ws, s.start + c0 + v)) * K);
+        const int pair = v < mc ? pair_of(direct != 0, ws, s.start + c0 + v) : 0;
+        if (v < mc) src = reinterpret_cast<const float4*>(ws.act + static_cast<int64_t>(pair) * K);
 #pragma unroll
         for (int i = 0; i < F4; ++i) {
           h[i] = v < mc ? __ldcg(src + j + 64 * i) : make_float4(0.f, 0.f, 0.f, 0.f);
@@ -1056,14 +1070,18 @@ __global__ void __launch_bounds__(kThreads, 2)
 #pragma unroll
           for (int i = 0; i < F4; ++i)
             store_planes(h[i], inv, dst + 8 * (j + 64 * i), dst + plane_stride(K) + 8 * (j + 64 * i));
-          if (j == 0) xsc[v] = sx;
+          if (j == 0) {
+            xsc[v] = sx;
+            spair[v] = pair;
+          }
         }
         __syncthreads();
         staged = u * 4096 + c0;
       }
       float acc[2][2] = {};
       block_steps(ta, tb, lut, lane_off, xl, kb, acc);
-      reinterpret_cast<float4*>(red)[warp * 32 + lane] = make_float4(acc[0][0], acc[0][1], acc[1][0], acc[1][1]);
+      float* rb = red + (npass++ & 1) * kRedFloats;
+      reinterpret_cast<float4*>(rb)[warp * 32 + lane] = make_float4(acc[0][0], acc[0][1], acc[1][0], acc[1][1]);
       __syncthreads();
       for (int i = threadIdx.x; i < ROWS * mc; i += kThreads) {
         const int v = i / ROWS, o = i - v * ROWS;
@@ -1071,11 +1089,13 @@ __global__ void __launch_bounds__(kThreads, 2)
         const int src = (r & 7) * 4 + v, reg = jt * 2 + (r >> 3);
         float sum = 0.f;
 #pragma unroll
-        for (int k = 0; k < KB; ++k) sum += red[((k * TP + otp) * 32 + src) * 4 + reg];
-        const int pair = pair_of(direct != 0, ws, s.start + c0 + v);
-        ws.dn[static_cast<int64_t>(pair) * hidden + c * ROWS + o] = sum * xsc[v];
+        for (int k = 0; k < KB; ++k) sum += rb[((k * TP + otp) * 32 + src) * 4 + reg];
+        ws.dn[static_cast<int64_t>(spair[v]) * hidden + c * ROWS + o] = sum * xsc[v];
       }
-      __syncthreads();
+      // one token: every dn store of the block precedes thread 0's ticket;
+      // more tokens: the next pass writes the other buffer, and a restaging
+      // starts with a barrier
+      if (direct) __syncthreads();
     }
     if (direct) {
       // one token: the last of the top_k items of this row chunk sums the
