@@ -16,12 +16,26 @@
 // weights, 6 of 9 for f32), into one f32 sum per output (m16n8k16 bf16
 // MMAs).  Before the dependency wait each warp bulk-prefetches its weight
 // slices into L2: the weights never depend on earlier kernels.
+//
+// More than 16 tokens with bf16 weights (the batched decode of many
+// sequences) run as a tiled product instead, where the x planes would
+// otherwise be re-read from L2 by every 16-row block: a block owns 64 rows
+// and up to 64 tokens, and stages 32-column slices of its weight rows and of
+// all its tokens' planes through a 4-deep cp.async pipeline in shared
+// memory (rows padded to 80 bytes, so ldmatrix reads are conflict-free);
+// 8 warps = 2 row halves x 4 token quarters, MMA operands by ldmatrix.  K is
+// split over the CTAs of a thread-block cluster (up to 8), whose partial
+// sums meet through distributed shared memory and are added in split order
+// (deterministic, no workspace).
+#include <cooperative_groups.h>
 #include <cuda_bf16.h>
 
 #include <algorithm>
 
 #include "errors.h"
 #include "linear_rows.cuh"
+
+namespace cg = cooperative_groups;
 
 namespace bt {
 namespace {
@@ -171,6 +185,134 @@ __global__ void __launch_bounds__(kThreads) linear_rows_kernel(const void* __res
   }
 }
 
+// ------------------------------------------------------------------ tiled path
+constexpr int kTileRows = 64;                // weight rows per block
+constexpr int kKStage = 32;                  // K columns per pipeline stage
+constexpr int kStages = 4;
+constexpr int kRowBytes = 2 * kKStage + 16;  // padded shared-memory row: 8 rows of a ldmatrix hit distinct banks
+constexpr int kMaxSplits = 8;                // cluster size (portable limit)
+
+__device__ __forceinline__ void cp_async16(void* smem_dst, const void* gsrc) {
+  const uint32_t d = static_cast<uint32_t>(__cvta_generic_to_shared(smem_dst));
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(d), "l"(gsrc) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+__device__ __forceinline__ void ldmatrix_x4(uint32_t (&r)[4], const void* smem) {
+  const uint32_t a = static_cast<uint32_t>(__cvta_generic_to_shared(smem));
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(a));
+}
+
+template <int GW>
+constexpr int tiled_stage_bytes() {
+  return kTileRows * kRowBytes + 3 * 32 * GW * kRowBytes;
+}
+template <int GW>
+constexpr int tiled_smem_bytes() {
+  return kStages * tiled_stage_bytes<GW>();
+}
+
+// Block (row block, split, token chunk): rows [64 x, 64 x + 64), K columns
+// [K/S * split, K/S * (split + 1)), tokens [NT z, NT z + NT), NT = 32 GW.
+// Warp w: rows 32 (w & 1) .. + 32 (two 16-row tiles), token groups
+// GW (w >> 1) .. + GW (8 tokens each), all three planes, summed into one
+// f32 accumulator per output like the per-tile kernel.  Tokens past T load
+// the last token's planes and are not stored.
+template <int GW>
+__global__ void __launch_bounds__(kThreads, 2)
+    linear_rows_tiled_kernel(const __nv_bfloat16* __restrict__ w, const __nv_bfloat16* __restrict__ xp,
+                             float* __restrict__ y, int n, int k, int t_total, int splits) {
+  constexpr int NT = 32 * GW, XROWS = 3 * NT;
+  constexpr int W_BYTES = kTileRows * kRowBytes, STAGE = tiled_stage_bytes<GW>();
+  static_assert(NT * kTileRows * 4 <= tiled_smem_bytes<GW>(), "partial sums reuse the stages");
+  extern __shared__ __align__(128) uint8_t sm[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+  const int wr = warp & 1, wc = warp >> 1;
+  const int row0 = blockIdx.x * kTileRows, split = blockIdx.y, tok0 = blockIdx.z * NT;
+  const int kspan = k / splits, kbeg = split * kspan, nst = kspan / kKStage;
+  if (threadIdx.x < kTileRows)
+    prefetch_l2(w + static_cast<int64_t>(row0 + threadIdx.x) * k + kbeg, static_cast<uint32_t>(kspan * 2));
+  pdl_wait();  // the planes come from earlier kernels
+  pdl_launch_dependents();
+
+  auto load_stage = [&](int st) {
+    uint8_t* sw = sm + (st % kStages) * STAGE;
+    uint8_t* sx = sw + W_BYTES;
+    const int kk = kbeg + st * kKStage;
+    {  // weights: 64 rows x 4 pieces of 16 bytes, one per thread
+      const int r = threadIdx.x >> 2, c = threadIdx.x & 3;
+      cp_async16(sw + r * kRowBytes + 16 * c, w + static_cast<int64_t>(row0 + r) * k + kk + 8 * c);
+    }
+#pragma unroll
+    for (int i = threadIdx.x; i < XROWS * 4; i += kThreads) {  // planes: row q * NT + token
+      const int r = i >> 2, c = i & 3, q = r / NT, tok = min(tok0 + r - q * NT, t_total - 1);
+      cp_async16(sx + r * kRowBytes + 16 * c, xp + (static_cast<int64_t>(tok) * 3 + q) * k + kk + 8 * c);
+    }
+  };
+
+  float acc[2][GW][4] = {};
+#pragma unroll
+  for (int st = 0; st < kStages - 1; ++st) {
+    if (st < nst) load_stage(st);
+    cp_async_commit();  // (empty groups keep the count uniform)
+  }
+  for (int st = 0; st < nst; ++st) {
+    cp_async_wait<kStages - 2>();  // stage st has landed
+    __syncthreads();               // ... for every thread, and stage st - 1 is no longer read
+    if (st + kStages - 1 < nst) load_stage(st + kStages - 1);
+    cp_async_commit();
+    const uint8_t* sw = sm + (st % kStages) * STAGE;
+    const uint8_t* sx = sw + W_BYTES;
+    // B: per token group and plane, the 8 tokens' 32 columns (4 matrices of 8 columns)
+    uint32_t b[GW][3][4];
+#pragma unroll
+    for (int j = 0; j < GW; ++j)
+#pragma unroll
+      for (int q = 0; q < 3; ++q)
+        ldmatrix_x4(b[j][q], sx + (q * NT + (wc * GW + j) * 8 + (lane & 7)) * kRowBytes + 16 * (lane >> 3));
+#pragma unroll
+    for (int ks = 0; ks < 2; ++ks)
+#pragma unroll
+      for (int i = 0; i < 2; ++i) {
+        uint32_t a[4];  // rows (2 wr + i) * 16 + (lane & 15), columns 16 ks + 8 (lane >> 4)
+        ldmatrix_x4(a, sw + ((wr * 2 + i) * 16 + (lane & 15)) * kRowBytes + 16 * (2 * ks + (lane >> 4)));
+#pragma unroll
+        for (int j = 0; j < GW; ++j)
+#pragma unroll
+          for (int q = 0; q < 3; ++q) mma_bf16(acc[i][j], a[0], a[1], a[2], a[3], b[j][q][2 * ks], b[j][q][2 * ks + 1]);
+      }
+  }
+  cp_async_wait<0>();
+  __syncthreads();  // every stage consumed: the partial sums reuse the buffers
+  float* part = reinterpret_cast<float*>(sm);  // [token][row], NT x 64
+#pragma unroll
+  for (int i = 0; i < 2; ++i)
+#pragma unroll
+    for (int j = 0; j < GW; ++j)
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        const int row = (wr * 2 + i) * 16 + g + 8 * (c >> 1), tok = (wc * GW + j) * 8 + 2 * t + (c & 1);
+        part[tok * kTileRows + row] = acc[i][j][c];
+      }
+  cg::cluster_group cluster = cg::this_cluster();
+  cluster.sync();  // every split's partial sums are in place
+  // split r finishes outputs [r per, (r + 1) per), adding the splits in order
+  const int per = NT * kTileRows / splits;
+  for (int e = split * per + threadIdx.x; e < (split + 1) * per; e += kThreads) {
+    float s = 0.f;
+    for (int r = 0; r < splits; ++r) s += cluster.map_shared_rank(part, r)[e];
+    const int tok = tok0 + e / kTileRows;
+    if (tok < t_total) y[static_cast<int64_t>(tok) * n + row0 + e % kTileRows] = s;
+  }
+  cluster.sync();  // no CTA leaves while another still reads its shared memory
+}
+
 template <bool F32W, int TW>
 cudaError_t launch_np(cudaLaunchConfig_t& cfg, int np, const void* w, const __nv_bfloat16* xp, float* y, int n, int k,
                       int t) {
@@ -220,6 +362,43 @@ int linear_rows(const void* w, int w_dtype, const void* x_planes, float* y, int6
                 static_cast<long long>(n), static_cast<long long>(k));
   if ((reinterpret_cast<uintptr_t>(w) | reinterpret_cast<uintptr_t>(x_planes)) & 15)
     return fail(BT_ERR_INVALID, "linear_rows: w and the planes must be 16-byte aligned");
+  const auto* xp = static_cast<const __nv_bfloat16*>(x_planes);
+  if (w_dtype == BT_BF16 && t > 16 && n % kTileRows == 0) {
+    // tiled path: split K over a cluster until >= 2 blocks per SM
+    const int64_t blocks = n / kTileRows, chunks = (t + 63) / 64;
+    if (blocks > 2147483647LL || chunks > 65535)
+      return fail(BT_ERR_UNSUPPORTED, "linear_rows: too many rows or tokens");
+    int splits = 1;
+    while (splits < kMaxSplits && blocks * chunks * splits < 2 * sm_count() && k % (kKStage * splits * 2) == 0)
+      splits *= 2;
+    const bool wide = t > 32;  // 64 tokens per block, else 32
+    cudaLaunchAttribute attr[2];
+    cudaLaunchConfig_t cfg = pdl_config(
+        dim3(static_cast<unsigned>(blocks), static_cast<unsigned>(splits),
+             static_cast<unsigned>(wide ? chunks : (t + 31) / 32)),
+        stream, attr);
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = 1;
+    attr[1].val.clusterDim.y = static_cast<unsigned>(splits);
+    attr[1].val.clusterDim.z = 1;
+    cfg.numAttrs = 2;
+    const auto* wb = static_cast<const __nv_bfloat16*>(w);
+    const int nn = static_cast<int>(n), kk = static_cast<int>(k), tt = static_cast<int>(t);
+    cudaError_t e;
+    if (wide) {
+      cfg.dynamicSmemBytes = tiled_smem_bytes<2>();
+      e = cudaFuncSetAttribute(linear_rows_tiled_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               tiled_smem_bytes<2>());
+      if (e == cudaSuccess) e = cudaLaunchKernelEx(&cfg, linear_rows_tiled_kernel<2>, wb, xp, y, nn, kk, tt, splits);
+    } else {
+      cfg.dynamicSmemBytes = tiled_smem_bytes<1>();
+      e = cudaFuncSetAttribute(linear_rows_tiled_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               tiled_smem_bytes<1>());
+      if (e == cudaSuccess) e = cudaLaunchKernelEx(&cfg, linear_rows_tiled_kernel<1>, wb, xp, y, nn, kk, tt, splits);
+    }
+    if (e != cudaSuccess) return fail_cuda(e, "linear_rows (tiled) launch");
+    return BT_OK;
+  }
   // Two 16-row tiles per block when there are rows enough (each x plane load
   // then serves 32 rows); passes of 8 tokens per block: as many as keep
   // >= 2 blocks per SM busy (fewer weight re-reads), one when the matrix is
@@ -232,7 +411,6 @@ int linear_rows(const void* w, int w_dtype, const void* x_planes, float* y, int6
   cudaLaunchConfig_t cfg = pdl_config(
       dim3(static_cast<unsigned>(tiles / tw), static_cast<unsigned>((passes + np - 1) / np)), stream, attr);
   const int nn = static_cast<int>(n), kk = static_cast<int>(k), tt = static_cast<int>(t);
-  const auto* xp = static_cast<const __nv_bfloat16*>(x_planes);
   const cudaError_t e = w_dtype == BT_F32 ? launch_np<true, 1>(cfg, np, w, xp, y, nn, kk, tt)
                         : tw == 2         ? launch_np<false, 2>(cfg, np, w, xp, y, nn, kk, tt)
                                           : launch_np<false, 1>(cfg, np, w, xp, y, nn, kk, tt);

@@ -5,6 +5,7 @@
     python -m breezetoken_b200.kernel_bench attn --batch 64 --ctx 32768
     python -m breezetoken_b200.kernel_bench moe --tokens 8
     python -m breezetoken_b200.kernel_bench qwen36 --batch 64 --prompt 512 --steps 256
+    python -m breezetoken_b200.kernel_bench linear --tokens 64
     python -m breezetoken_b200.kernel_bench trace --gguf model.gguf
 
 Each prints one JSON line: average launch time and achieved HBM GB/s from
@@ -16,6 +17,10 @@ its bytes are the
 U * 1,351,680 of the U distinct experts the routing selects.
 ``qwen36`` is BASELINE config 5 on one GPU (Qwen3.6-35B-A3B shape, seeded
 random weights built on the device, 64 sequences in lockstep).
+``linear`` times ``bt_linear_rows`` (bf16 weight rows x three bf16 planes of
+x) at config 5's projection shapes (GDN qkv 8192 x 2048, z 4096 x 2048, out
+2048 x 4096, the 151936 x 2048 head) for T tokens, cycling over weight
+copies larger than L2 together.
 ``trace`` prints the device-side timeline of one Qwen3.5 decode step (per
 kernel kind: release gap, prologue, body) after a 16-token prefill.
 ``gdn`` and ``attn`` are the stand-alone decode ops of BASELINE configs 2
@@ -88,6 +93,32 @@ def bench_gemv(n: int, k: int, iters: int) -> dict:
     sec = _time(run, iters, s)
     nbytes = w.data.numel() + 4 * (k + n)
     return {"kernel": "gemv_q8", "n": n, "k": k, "us": sec * 1e6, "bytes": nbytes, "gbs": nbytes / sec / 1e9}
+
+
+def bench_linear(n: int, k: int, t: int, iters: int) -> dict:
+    g = torch.Generator(device="cuda").manual_seed(5)
+    nbytes_w = n * k * 2
+    copies = max(1, -(-(256 << 20) // nbytes_w))  # together larger than L2
+    ws = [(torch.randn(n, k, device="cuda", generator=g) * 0.02).to(torch.bfloat16) for _ in range(copies)]
+    x = torch.randn(t, k, device="cuda", generator=g)
+    planes = torch.empty(t, 3, k, dtype=torch.bfloat16, device="cuda")
+    y = torch.empty(t, n, device="cuda")
+    s = torch.cuda.Stream()
+    lib = N.load()
+    N.check(lib.bt_bf16_planes(x.data_ptr(), planes.data_ptr(), t, k, s.cuda_stream), "planes")
+    it = [0]
+
+    def run():
+        w = ws[it[0] % copies]
+        it[0] += 1
+        N.check(lib.bt_linear_rows(w.data_ptr(), N.BT_BF16, planes.data_ptr(), y.data_ptr(), n, k, t, s.cuda_stream),
+                "linear_rows")
+
+    sec = _time_graph(run, max(iters, copies), s)
+    nbytes = nbytes_w + t * 3 * k * 2 + t * n * 4
+    return {"kernel": "linear_rows", "n": n, "k": k, "tokens": t, "us": sec * 1e6, "bytes": nbytes,
+            "gbs": nbytes / sec / 1e9, "tflops": 2 * n * k * t / sec / 1e12,
+            "tflops_planes": 3 * 2 * n * k * t / sec / 1e12, "l2": f"{copies} weight copies cycled"}
 
 
 def bench_gdn(batch: int, steps: int, heads: int = 16, dim: int = 128) -> dict:
@@ -351,6 +382,11 @@ def main() -> None:
     mo.add_argument("--tokens", type=int, default=1)
     mo.add_argument("--iters", type=int, default=50)
     mo.add_argument("--no-shared", action="store_true", help="routed experts only")
+    li = sub.add_parser("linear")
+    li.add_argument("--tokens", type=int, default=64)
+    li.add_argument("--n", type=int, default=0, help="0: config 5's projection shapes")
+    li.add_argument("--k", type=int, default=2048)
+    li.add_argument("--iters", type=int, default=20)
     q6 = sub.add_parser("qwen36")
     q6.add_argument("--batch", type=int, default=64)
     q6.add_argument("--prompt", type=int, default=512)
@@ -363,6 +399,11 @@ def main() -> None:
     args = ap.parse_args()
     if args.cmd == "trace":
         print(trace_step(args.gguf, args.max_context, args.steps), flush=True)
+        return
+    if args.cmd == "linear":
+        shapes = [(args.n, args.k)] if args.n else [(8192, 2048), (4096, 2048), (2048, 4096), (151936, 2048)]
+        for n, k in shapes:
+            print(json.dumps(bench_linear(n, k, args.tokens, args.iters)), flush=True)
         return
     if args.cmd == "gemv":
         r = bench_gemv(args.n, args.k, args.iters)
