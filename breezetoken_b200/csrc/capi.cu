@@ -164,6 +164,8 @@ int bt_linear_rows(const void* w, int w_dtype, const void* x_planes, float* y, i
   return bt::linear_rows(w, w_dtype, x_planes, y, n, k, t, as_stream(stream));
 }
 
+int bt_linear_rows_timeouts(void) { return bt::linear_rows_timeouts(); }
+
 int bt_rms_norm(const float* x, const float* w, float* y, int64_t rows, int64_t n, float eps, void* stream) {
   return bt::rms_norm(x, nullptr, w, nullptr, y, rows, n, eps, as_stream(stream));
 }

@@ -27,8 +27,23 @@
 // split over the CTAs of a thread-block cluster (up to 8), whose partial
 // sums meet through distributed shared memory and are added in split order
 // (deterministic, no workspace).
+//
+// With N % 128 == 0 the tiled product runs on the 5th-generation tensor
+// cores instead: a CTA owns 128 weight rows (the MMA's M, one TMEM lane per
+// row) and up to 64 tokens, whose three planes are the MMA's N = 3 NT
+// columns (token-major: column 3 t + plane).  One thread streams 64-column
+// stages of both operands with TMA (one tensor copy per operand: rows of 128
+// bytes in the 128-byte-swizzled K-major layout the MMA descriptors name;
+// rows past T read as zeros), another issues tcgen05.mma
+// (kind::f16, bf16 x bf16 -> f32 accumulators in TMEM) as stages arrive and
+// releases each buffer with tcgen05.commit; full / empty mbarriers pace the
+// two.  The epilogue reads TMEM (tcgen05.ld), adds the planes and joins the
+// same split-order cluster reduction.  Every mbarrier wait gives up after
+// kWaitLimitNs (counted in g_umma_timeouts, read by bt_linear_rows_timeouts).
 #include <cooperative_groups.h>
+#include <cuda.h>  // CUtensorMap (the encoder comes through the runtime's driver entry point)
 #include <cuda_bf16.h>
+#include <cudaTypedefs.h>
 
 #include <algorithm>
 
@@ -209,6 +224,20 @@ __device__ __forceinline__ void ldmatrix_x4(uint32_t (&r)[4], const void* smem) 
                : "r"(a));
 }
 
+// Output e of a block's [token][row] partial sums: the splits' values,
+// loaded from every CTA of the cluster before any is added (one round trip),
+// added in split order.
+__device__ __forceinline__ float split_sum(cg::cluster_group& cluster, float* part, int e, int splits) {
+  float v[kMaxSplits];
+#pragma unroll
+  for (int r = 0; r < kMaxSplits; ++r) v[r] = r < splits ? cluster.map_shared_rank(part, r)[e] : 0.f;
+  float s = 0.f;
+#pragma unroll
+  for (int r = 0; r < kMaxSplits; ++r)
+    if (r < splits) s += v[r];
+  return s;
+}
+
 template <int GW>
 constexpr int tiled_stage_bytes() {
   return kTileRows * kRowBytes + 3 * 32 * GW * kRowBytes;
@@ -304,13 +333,261 @@ __global__ void __launch_bounds__(kThreads, 2)
   cluster.sync();  // every split's partial sums are in place
   // split r finishes outputs [r per, (r + 1) per), adding the splits in order
   const int per = NT * kTileRows / splits;
+#pragma unroll 2
   for (int e = split * per + threadIdx.x; e < (split + 1) * per; e += kThreads) {
-    float s = 0.f;
-    for (int r = 0; r < splits; ++r) s += cluster.map_shared_rank(part, r)[e];
+    const float s = split_sum(cluster, part, e, splits);
     const int tok = tok0 + e / kTileRows;
     if (tok < t_total) y[static_cast<int64_t>(tok) * n + row0 + e % kTileRows] = s;
   }
   cluster.sync();  // no CTA leaves while another still reads its shared memory
+}
+
+// ------------------------------------------------------------------ tcgen05 path
+constexpr int kUmmaRows = 128;  // weight rows per CTA: the MMA's M, one TMEM lane per row
+constexpr int kUmmaKStage = 64;  // K columns per stage (one 128-byte swizzle row): four MMAs of K 16
+constexpr int kUmmaStages = 5;
+__device__ int g_umma_timeouts;  // mbarrier waits that gave up
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint32_t addr, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(addr), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Waits until the phase of `parity` has completed.  Gives up after
+// kWaitLimitNs, counting the timeout; once a wait of this CTA gave up
+// (*abort), the others return at once, so a broken pipeline ends promptly.
+__device__ __forceinline__ void mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort) {
+  const uint32_t a = smem_u32(bar);
+  if (mbar_try_wait(a, parity)) return;
+  const uint64_t t0 = global_ns();
+  while (!mbar_try_wait(a, parity)) {
+    if (*abort) return;
+    if (global_ns() - t0 > kWaitLimitNs) {
+      *abort = 1;
+      atomicAdd(&g_umma_timeouts, 1);
+      return;
+    }
+  }
+}
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// K-major, 128-byte swizzle (layout type 2 at bits 61-63): rows of 128
+// bytes (64 bf16 columns) in 1024-byte atoms of 8 rows, the 16-byte pieces
+// of row r XOR-permuted by r % 8 -- what TMA writes with SWIZZLE_128B; 1024
+// bytes between 8-row groups (stride byte offset), the leading byte offset
+// unused within one atom's width (1); bits 46-48 hold the fixed 0b001.  The
+// MMA of K columns [16 s, 16 s + 16) starts 32 s bytes into the rows (the
+// swizzle is applied to the computed addresses, so the atom must sit at a
+// 1024-byte boundary).
+__device__ __forceinline__ uint64_t umma_desc(uint32_t saddr) {
+  return static_cast<uint64_t>((saddr & 0x3FFFFu) >> 4) | (1ull << 16) | (static_cast<uint64_t>(1024 >> 4) << 32) |
+         (1ull << 46) | (2ull << 61);
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
+}
+// 2-D tensor copy global -> this CTA's shared memory (no multicast), box at
+// (x = column, y = row), completion counted on `bar`.
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+          dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+      : "memory");
+}
+
+// Instruction descriptor, kind::f16: D f32 (bits 4-5 = 1), A and B bf16
+// (bits 7-9, 10-12 = 1), both K-major (bits 15, 16 = 0), N >> 3 at bit 17,
+// M >> 4 at bit 24.
+template <int N>
+constexpr uint32_t umma_idesc() {
+  return (1u << 4) | (1u << 7) | (1u << 10) | (static_cast<uint32_t>(N >> 3) << 17) |
+         (static_cast<uint32_t>(kUmmaRows >> 4) << 24);
+}
+
+__device__ __forceinline__ void umma_bf16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                          uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\ttcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}"
+      ::"r"(d_tmem), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+
+// Columns [c, c + 24) of this warp's 32 TMEM lanes (8 tokens x 3 planes),
+// loaded and waited for in one statement so no use of the registers can
+// move ahead of the wait.
+__device__ __forceinline__ void tmem_ld24(uint32_t taddr, uint32_t (&r)[24]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%24];\n\t"
+      "tcgen05.ld.sync.aligned.32x32b.x8.b32 {%8, %9, %10, %11, %12, %13, %14, %15}, [%25];\n\t"
+      "tcgen05.ld.sync.aligned.32x32b.x8.b32 {%16, %17, %18, %19, %20, %21, %22, %23}, [%26];\n\t"
+      "tcgen05.wait::ld.sync.aligned;"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23])
+      : "r"(taddr), "r"(taddr + 8), "r"(taddr + 16)
+      : "memory");
+}
+
+template <int NT>
+constexpr int umma_stage_bytes() {
+  return (kUmmaRows + 3 * NT) * kUmmaKStage * 2;
+}
+template <int NT>
+constexpr int umma_smem_bytes() {  // stages + alignment slack
+  return kUmmaStages * umma_stage_bytes<NT>() + 1024;
+}
+
+// Block (row block, split, token chunk): rows [128 x, 128 x + 128), K
+// columns [K/S split, K/S (split + 1)), tokens [NT z, NT z + NT).  `tmw`
+// maps W (N rows x K), `tmx` the planes ((3 T) rows x K, row 3 t + plane);
+// both with 64-column boxes, of 128 and 3 NT rows.
+template <int NT>
+__global__ void __launch_bounds__(kThreads, 1)
+    linear_rows_umma_kernel(const __grid_constant__ CUtensorMap tmw, const __grid_constant__ CUtensorMap tmx,
+                            const __nv_bfloat16* __restrict__ w, float* __restrict__ y, int n, int k, int t_total,
+                            int splits) {
+  constexpr int NB = 3 * NT;  // B rows (token-major: 3 t + plane) = the MMA's N
+  constexpr int A_BYTES = kUmmaRows * kUmmaKStage * 2, STAGE = umma_stage_bytes<NT>();
+  constexpr uint32_t COLS = NB <= 64 ? 64 : NB <= 128 ? 128 : 256;  // TMEM columns (power of 2 >= N)
+  constexpr uint32_t IDESC = umma_idesc<NB>();
+  static_assert(NB % 16 == 0 && NB <= 256, "M = 128 takes N = 16 .. 256 in steps of 16");
+  static_assert(NT * kUmmaRows * 4 <= kUmmaStages * STAGE, "partial sums reuse the stages");
+  static_assert(A_BYTES % 1024 == 0 && STAGE % 1024 == 0, "swizzle atoms at 1024-byte boundaries");
+  extern __shared__ uint8_t sm_raw[];
+  __shared__ __align__(8) uint64_t full[kUmmaStages], empty[kUmmaStages], done;
+  __shared__ uint32_t s_tmem;
+  __shared__ int s_abort;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int row0 = blockIdx.x * kUmmaRows, split = blockIdx.y, tok0 = blockIdx.z * NT;
+  const int kspan = k / splits, kbeg = split * kspan, nst = kspan / kUmmaKStage;
+  // stage buffers at a 1024-byte boundary (128-byte swizzle atoms)
+  uint8_t* sm = sm_raw + ((1024u - (smem_u32(sm_raw) & 1023u)) & 1023u);
+  const uint32_t sbase = smem_u32(sm);
+
+  if (warp == 0) {  // TMEM for the accumulators (the whole warp allocates)
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&s_tmem)),
+                 "r"(COLS)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  if (threadIdx.x == 32) {
+#pragma unroll
+    for (int b = 0; b < kUmmaStages; ++b) {
+      mbar_init(&full[b], 1);
+      mbar_init(&empty[b], 1);
+    }
+    mbar_init(&done, 1);
+    s_abort = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmw)) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmx)) : "memory");
+  }
+  if (threadIdx.x >= 64 && threadIdx.x < 64 + kUmmaRows)  // this block's weight slice into L2
+    prefetch_l2(w + static_cast<int64_t>(row0 + threadIdx.x - 64) * k + kbeg, static_cast<uint32_t>(kspan * 2));
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = s_tmem;
+  pdl_wait();  // the planes come from earlier kernels
+  pdl_launch_dependents();
+
+  if (threadIdx.x == 0) {
+    // producer: stage st into buffer st % S once the MMAs of stage st - S released it
+    for (int st = 0; st < nst; ++st) {
+      const int b = st % kUmmaStages;
+      if (st >= kUmmaStages) mbar_wait(&empty[b], ((st / kUmmaStages) - 1) & 1, &s_abort);
+      mbar_arrive_expect_tx(&full[b], STAGE);
+      const uint32_t sa = sbase + b * STAGE;
+      const int kk = kbeg + st * kUmmaKStage;
+      tma_load_2d(sa, &tmw, kk, row0, &full[b]);
+      tma_load_2d(sa + A_BYTES, &tmx, kk, 3 * tok0, &full[b]);
+    }
+  } else if (threadIdx.x == 32) {
+    // MMA issuer: four K-16 steps per stage, then the stage's buffer goes back
+    for (int st = 0; st < nst; ++st) {
+      const int b = st % kUmmaStages;
+      mbar_wait(&full[b], (st / kUmmaStages) & 1, &s_abort);
+      tc_fence_after();
+      const uint32_t a0 = sbase + b * STAGE, b0 = a0 + A_BYTES;
+#pragma unroll
+      for (int s4 = 0; s4 < kUmmaKStage / 16; ++s4)
+        umma_bf16(tmem, umma_desc(a0 + 32 * s4), umma_desc(b0 + 32 * s4), IDESC, (st > 0 || s4 > 0) ? 1u : 0u);
+      umma_commit(&empty[b]);
+    }
+    umma_commit(&done);  // every MMA of the CTA
+  }
+  mbar_wait(&done, 0, &s_abort);
+  tc_fence_after();
+
+  // TMEM lane r = weight row row0 + r, column 3 t + plane; warp w reads
+  // lanes 32 (w % 4) .. + 32 and tokens [NT/2 (w / 4), NT/2 (w / 4 + 1))
+  float* part = reinterpret_cast<float*>(sm);  // [token][row], NT x 128 (every TMA landed, every MMA done)
+  const int lq = warp & 3, half = warp >> 2;
+  const uint32_t tl = tmem + (static_cast<uint32_t>(32 * lq) << 16);
+#pragma unroll
+  for (int t8 = half * (NT / 2); t8 < (half + 1) * (NT / 2); t8 += 8) {
+    uint32_t r[24];
+    tmem_ld24(tl + 3 * t8, r);
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+      part[(t8 + i) * kUmmaRows + 32 * lq + lane] =
+          (__uint_as_float(r[3 * i]) + __uint_as_float(r[3 * i + 1])) + __uint_as_float(r[3 * i + 2]);
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(COLS) : "memory");
+  }
+  cg::cluster_group cluster = cg::this_cluster();
+  cluster.sync();  // every split's partial sums are in place
+  const int per = NT * kUmmaRows / splits;
+#pragma unroll 2
+  for (int e = split * per + threadIdx.x; e < (split + 1) * per; e += kThreads) {
+    const float s = split_sum(cluster, part, e, splits);
+    const int tok = tok0 + e / kUmmaRows;
+    if (tok < t_total) y[static_cast<int64_t>(tok) * n + row0 + e % kUmmaRows] = s;
+  }
+  cluster.sync();  // no CTA leaves while another still reads its shared memory
+}
+
+// 2-D tensor map over bf16 rows (rows x k, row stride k), 64-column boxes
+// of `box_rows` rows written 128-byte swizzled, zero fill past the rows.
+bool make_map(CUtensorMap* map, const void* base, int64_t rows, int64_t k, int box_rows) {
+  static PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
+  if (!encode) {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &fn, 12000, cudaEnableDefault, &q) !=
+            cudaSuccess ||
+        q != cudaDriverEntryPointSuccess || !fn)
+      return false;
+    encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+  }
+  const cuuint64_t dims[2] = {static_cast<cuuint64_t>(k), static_cast<cuuint64_t>(rows)};
+  const cuuint64_t strides[1] = {static_cast<cuuint64_t>(k) * 2};
+  const cuuint32_t box[2] = {static_cast<cuuint32_t>(kUmmaKStage), static_cast<cuuint32_t>(box_rows)};
+  const cuuint32_t estr[2] = {1, 1};
+  return encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
 template <bool F32W, int TW>
@@ -363,13 +640,56 @@ int linear_rows(const void* w, int w_dtype, const void* x_planes, float* y, int6
   if ((reinterpret_cast<uintptr_t>(w) | reinterpret_cast<uintptr_t>(x_planes)) & 15)
     return fail(BT_ERR_INVALID, "linear_rows: w and the planes must be 16-byte aligned");
   const auto* xp = static_cast<const __nv_bfloat16*>(x_planes);
+  if (w_dtype == BT_BF16 && t > 16 && n % kUmmaRows == 0) {
+    // tensor-core path: 64 tokens per CTA (32 for T <= 32); K split over a
+    // cluster as far as the CTAs still fit one wave of 1 per SM
+    const bool wide = t > 32;
+    const int nt = wide ? 64 : 32;
+    const int64_t blocks = n / kUmmaRows, chunks = (t + nt - 1) / nt;
+    if (blocks > 2147483647LL || chunks > 65535)
+      return fail(BT_ERR_UNSUPPORTED, "linear_rows: too many rows or tokens");
+    int splits = 1;
+    while (splits < kMaxSplits && blocks * chunks * splits * 2 <= sm_count() && k % (kUmmaKStage * splits * 2) == 0)
+      splits *= 2;
+    cudaLaunchAttribute attr[2];
+    cudaLaunchConfig_t cfg = pdl_config(
+        dim3(static_cast<unsigned>(blocks), static_cast<unsigned>(splits), static_cast<unsigned>(chunks)), stream, attr);
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = 1;
+    attr[1].val.clusterDim.y = static_cast<unsigned>(splits);
+    attr[1].val.clusterDim.z = 1;
+    cfg.numAttrs = 2;
+    const auto* wb = static_cast<const __nv_bfloat16*>(w);
+    const int nn = static_cast<int>(n), kk = static_cast<int>(k), tt = static_cast<int>(t);
+    CUtensorMap tmw, tmx;
+    if (!make_map(&tmw, w, n, k, kUmmaRows) || !make_map(&tmx, x_planes, 3 * t, k, 3 * nt))
+      return fail(BT_ERR_CUDA, "linear_rows: tensor maps could not be encoded");
+    cudaError_t e;
+    if (wide) {
+      cfg.dynamicSmemBytes = umma_smem_bytes<64>();
+      e = cudaFuncSetAttribute(linear_rows_umma_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               umma_smem_bytes<64>());
+      if (e == cudaSuccess)
+        e = cudaLaunchKernelEx(&cfg, linear_rows_umma_kernel<64>, tmw, tmx, wb, y, nn, kk, tt, splits);
+    } else {
+      cfg.dynamicSmemBytes = umma_smem_bytes<32>();
+      e = cudaFuncSetAttribute(linear_rows_umma_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               umma_smem_bytes<32>());
+      if (e == cudaSuccess)
+        e = cudaLaunchKernelEx(&cfg, linear_rows_umma_kernel<32>, tmw, tmx, wb, y, nn, kk, tt, splits);
+    }
+    if (e != cudaSuccess) return fail_cuda(e, "linear_rows (tcgen05) launch");
+    return BT_OK;
+  }
   if (w_dtype == BT_BF16 && t > 16 && n % kTileRows == 0) {
-    // tiled path: split K over a cluster until >= 2 blocks per SM
+    // tiled path: K split over a cluster as far as the blocks still fit one
+    // wave of 2 per SM
     const int64_t blocks = n / kTileRows, chunks = (t + 63) / 64;
     if (blocks > 2147483647LL || chunks > 65535)
       return fail(BT_ERR_UNSUPPORTED, "linear_rows: too many rows or tokens");
     int splits = 1;
-    while (splits < kMaxSplits && blocks * chunks * splits < 2 * sm_count() && k % (kKStage * splits * 2) == 0)
+    while (splits < kMaxSplits && blocks * chunks * splits * 2 <= 2 * sm_count() &&
+           k % (kKStage * splits * 2) == 0)
       splits *= 2;
     const bool wide = t > 32;  // 64 tokens per block, else 32
     cudaLaunchAttribute attr[2];
@@ -416,6 +736,15 @@ int linear_rows(const void* w, int w_dtype, const void* x_planes, float* y, int6
                                           : launch_np<false, 1>(cfg, np, w, xp, y, nn, kk, tt);
   if (e != cudaSuccess) return fail_cuda(e, "linear_rows launch");
   return BT_OK;
+}
+
+int linear_rows_timeouts() {
+  int v = 0;
+  const int zero = 0;
+  if (cudaMemcpyFromSymbol(&v, g_umma_timeouts, sizeof(int)) != cudaSuccess ||
+      cudaMemcpyToSymbol(g_umma_timeouts, &zero, sizeof(int)) != cudaSuccess)
+    return -1;
+  return v;
 }
 
 }  // namespace bt

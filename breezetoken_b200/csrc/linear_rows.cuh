@@ -10,4 +10,8 @@ int bf16_planes(const float* x, void* planes, int64_t t, int64_t k, cudaStream_t
 int linear_rows(const void* w, int w_dtype, const void* x_planes, float* y, int64_t n, int64_t k, int64_t t,
                 cudaStream_t stream);
 
+// Bounded waits of the tensor-core path that gave up since the last call
+// (synchronous; resets the count; -1 if the device could not be read).
+int linear_rows_timeouts();
+
 }  // namespace bt

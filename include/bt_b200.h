@@ -102,6 +102,12 @@ BT_API int bt_bf16_planes(const float* x, void* planes, int64_t t, int64_t k,
 BT_API int bt_linear_rows(const void* w, int w_dtype, const void* x_planes, float* y,
                    int64_t n, int64_t k, int64_t t, void* stream);
 
+/* Diagnostic without a reference counterpart: how many bounded mbarrier
+ * waits of bt_linear_rows' tensor-core path (tcgen05, > 16 tokens, N % 128
+ * == 0) gave up since the last call (0 unless the pipeline broke).
+ * Synchronises the device and resets the count; -1 if it cannot be read.  */
+BT_API int bt_linear_rows_timeouts(void);
+
 /* Backend.rms_norm (backends.py:119-123) over rows of length n.           */
 BT_API int bt_rms_norm(const float* x, const float* w, float* y, int64_t rows,
                 int64_t n, float eps, void* stream);

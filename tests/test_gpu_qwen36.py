@@ -103,12 +103,13 @@ def test_linear_rows_matches_f64(cuda, dtype, t) -> None:
 
 
 @pytest.mark.parametrize("t", [17, 32, 33, 64, 130])
-@pytest.mark.parametrize("n,k", [(64, 256), (192, 2048), (512, 4096)])
+@pytest.mark.parametrize("n,k", [(64, 256), (192, 2048), (128, 256), (256, 2048), (512, 4096)])
 def test_linear_rows_tiled_matches_f64(cuda, t, n, k) -> None:
-    """The tiled path (bf16 weights, > 16 tokens, N % 64 == 0; K split over
-    1 to 8 CTAs of a cluster): y = x W^T within 2e-6 of sum |x||w| per output,
-    ragged token counts included, and the same bits on a second call (the
-    splits are added in a fixed order)."""
+    """The tiled paths for bf16 weights and > 16 tokens (N % 128 == 0: tcgen05
+    MMAs with TMEM accumulators; else N % 64 == 0: ldmatrix-fed MMAs), K split
+    over 1 to 8 CTAs of a cluster: y = x W^T within 2e-6 of sum |x||w| per
+    output, ragged token counts included, the same bits on a second call (the
+    splits are added in a fixed order), and no bounded wait gave up."""
     rng = np.random.default_rng(13)
     w = torch.from_numpy(rng.standard_normal((n, k)).astype(np.float32) * 0.02).to(torch.bfloat16)
     x = torch.from_numpy(rng.standard_normal((t, k)).astype(np.float32))
@@ -123,6 +124,7 @@ def test_linear_rows_tiled_matches_f64(cuda, t, n, k) -> None:
     want = x.double().numpy() @ wf.T
     bound = np.abs(x.double().numpy()) @ np.abs(wf).T
     got = y.cpu().double().numpy()
+    assert N.load().bt_linear_rows_timeouts() == 0
     assert np.isfinite(got).all()
     assert (np.abs(got - want) <= 2e-6 * bound).all()
     assert torch.equal(y, y2)
