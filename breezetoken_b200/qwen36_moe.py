@@ -262,6 +262,9 @@ class Qwen36Moe:
         self._attn_ws = torch.zeros(max(nbytes, 256), dtype=torch.uint8, device=dev)
         self._moe_ws = torch.zeros(int(N.load().bt_moe_layer_workspace_bytes(
             b, cfg.hidden, cfg.expert_ffn, cfg.shared_ffn, cfg.n_experts, cfg.top_k)), dtype=torch.uint8, device=dev)
+        for i in self.conv_state:  # beta and alpha rows stacked: one projection launch for both
+            layer = self.layers[i]
+            layer["w_ba"] = torch.cat([layer["w_beta"], layer["w_alpha"]]).contiguous()
 
     def _splits(self) -> int:
         return max(1, min(16, self.cfg.max_context // 256))
@@ -335,8 +338,9 @@ class Qwen36Moe:
         q = mixed[:, : inner // 2].reshape(b, hk, dk).contiguous()
         k = mixed[:, inner // 2 : inner].reshape(b, hk, dk).contiguous()
         v = mixed[:, inner:].reshape(b, hv, dk).contiguous()
-        beta = self._lin(layer["w_beta"], xp)
-        g = layer["a_log"] * torch.nn.functional.softplus(self._lin(layer["w_alpha"], xp) + layer["dt_bias"])
+        ba = self._lin(layer["w_ba"], xp)  # [beta | alpha] (each row as its own projection)
+        beta = ba[:, :hv]
+        g = layer["a_log"] * torch.nn.functional.softplus(ba[:, hv:] + layer["dt_bias"])
         read = torch.empty(b, hv, cfg.gdn_value_dim, dtype=torch.float32, device=self.device)
         N.call("bt_gdn_decode", q.data_ptr(), k.data_ptr(), v.data_ptr(), N.BT_F32, g.contiguous().data_ptr(),
                beta.contiguous().data_ptr(), self.rec_state[i].data_ptr(), read.data_ptr(), b, hk, hv, dk,
