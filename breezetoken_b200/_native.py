@@ -132,6 +132,8 @@ _SIGS: dict[str, tuple[object, list]] = {
         [_P, _P, _P, C.c_int, _P, _P, _I64, _I64, _I64, _I64, _I64, C.c_float, C.c_int, _P],
     ),
     "bt_gdn_decode": (C.c_int, [_P, _P, _P, C.c_int, _P, _P, _P, _P, _I64, _I64, _I64, _I64, C.c_float, C.c_float, _P]),
+    "bt_gdn_decode_strided": (C.c_int, [_P, _P, _P, C.c_int, _I64, _I64, _I64, _P, _I64, _P, _I64, _P, _P, _I64, _I64,
+                                        _I64, _I64, _I64, C.c_float, C.c_float, _P]),
     "bt_argmax_workspace_bytes": (_I64, [_I64]),
     "bt_iq3s_row_bytes": (_I64, [_I64]),
     "bt_repack_iq3_s": (C.c_int, [_P, _P, _I64, _I64, _P]),

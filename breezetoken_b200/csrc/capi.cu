@@ -228,7 +228,18 @@ int bt_attention_decode(const float* q, const void* k, const void* v, int kv_dty
 int bt_gdn_decode(const void* q, const void* k, const void* v, int in_dtype, const float* g, const float* beta,
                   float* state, float* out, int64_t batch, int64_t heads_k, int64_t heads_v, int64_t dim, float scale,
                   float eps, void* stream) {
+  return bt_gdn_decode_strided(q, k, v, in_dtype, heads_k * dim, heads_k * dim, heads_v * dim, g, heads_v, beta,
+                               heads_v, state, out, heads_v * dim, batch, heads_k, heads_v, dim, scale, eps, stream);
+}
+
+int bt_gdn_decode_strided(const void* q, const void* k, const void* v, int in_dtype, int64_t q_bs, int64_t k_bs,
+                          int64_t v_bs, const float* g, int64_t g_bs, const float* beta, int64_t beta_bs, float* state,
+                          float* out, int64_t out_bs, int64_t batch, int64_t heads_k, int64_t heads_v, int64_t dim,
+                          float scale, float eps, void* stream) {
   if (!q || !k || !v || !g || !beta || !state || !out) return fail(BT_ERR_INVALID, "gdn_decode: null pointer");
+  if (q_bs < heads_k * dim || k_bs < heads_k * dim || v_bs < heads_v * dim || g_bs < heads_v ||
+      beta_bs < heads_v || out_bs < heads_v * dim)
+    return fail(BT_ERR_INVALID, "gdn_decode: a batch stride is shorter than its row");
   if (in_dtype != BT_F32 && in_dtype != BT_BF16) return fail(BT_ERR_UNSUPPORTED, "gdn_decode: dtype %d", in_dtype);
   if (batch * heads_v * (dim / 32) > 0x7fffffffLL) return fail(BT_ERR_UNSUPPORTED, "gdn_decode: grid too large");
   bt::GdnParams p{};
@@ -236,14 +247,16 @@ int bt_gdn_decode(const void* q, const void* k, const void* v, int in_dtype, con
   p.k = k;
   p.v = v;
   p.in_dtype = in_dtype;
-  p.q_bs = p.k_bs = heads_k * dim;
-  p.v_bs = heads_v * dim;
+  p.q_bs = q_bs;
+  p.k_bs = k_bs;
+  p.v_bs = v_bs;
   p.g = g;
   p.beta = beta;
-  p.g_bs = p.beta_bs = heads_v;
+  p.g_bs = g_bs;
+  p.beta_bs = beta_bs;
   p.state = state;
   p.out = out;
-  p.out_bs = heads_v * dim;
+  p.out_bs = out_bs;
   p.batch = static_cast<int32_t>(batch);
   p.heads_k = static_cast<int32_t>(heads_k);
   p.heads_v = static_cast<int32_t>(heads_v);

@@ -335,16 +335,15 @@ class Qwen36Moe:
         mixed = torch.empty_like(entry)
         N.call("bt_conv_silu", entry.data_ptr(), self.conv_state[i].data_ptr(), layer["conv"].data_ptr(),
                mixed.data_ptr(), b, cfg.conv_dim, cfg.gdn_conv, _stream())
-        q = mixed[:, : inner // 2].reshape(b, hk, dk).contiguous()
-        k = mixed[:, inner // 2 : inner].reshape(b, hk, dk).contiguous()
-        v = mixed[:, inner:].reshape(b, hv, dk).contiguous()
         ba = self._lin(layer["w_ba"], xp)  # [beta | alpha] (each row as its own projection)
-        beta = ba[:, :hv]
-        g = layer["a_log"] * torch.nn.functional.softplus(ba[:, hv:] + layer["dt_bias"])
+        g = (layer["a_log"] * torch.nn.functional.softplus(ba[:, hv:] + layer["dt_bias"])).contiguous()
         read = torch.empty(b, hv, cfg.gdn_value_dim, dtype=torch.float32, device=self.device)
-        N.call("bt_gdn_decode", q.data_ptr(), k.data_ptr(), v.data_ptr(), N.BT_F32, g.contiguous().data_ptr(),
-               beta.contiguous().data_ptr(), self.rec_state[i].data_ptr(), read.data_ptr(), b, hk, hv, dk,
-               float(dk ** -0.5), float(cfg.l2_eps), _stream())
+        # q | k | v are read in place from the conv output rows, beta from the projection rows
+        c = mixed.shape[1]
+        N.call("bt_gdn_decode_strided", mixed.data_ptr(), mixed[:, inner // 2 :].data_ptr(),
+               mixed[:, inner:].data_ptr(), N.BT_F32, c, c, c, g.data_ptr(), hv, ba.data_ptr(), 2 * hv,
+               self.rec_state[i].data_ptr(), read.data_ptr(), hv * dk, b, hk, hv, dk, float(dk ** -0.5),
+               float(cfg.l2_eps), _stream())
         z = self._lin(layer["z"], xp).view(b, hv, dk)
         gated = (self._rms(read, layer["ssm_norm"]) * torch.nn.functional.silu(z)).reshape(b, -1)
         return self._lin(layer["out"], self._planes(gated))
@@ -361,15 +360,18 @@ class Qwen36Moe:
         cfg = self.cfg
         h = self.embd[tokens.long()].float()
         attn = set(cfg.attn_layers)
+        xn = self._rms(h, self.layers[0]["norm_in"])
         for i in range(cfg.n_layers):
+            # each residual add runs fused with the norm that follows it
+            # (h = h + delta, then rms_norm(h): the same f32 operations)
             layer = self.layers[i]
-            xn = self._rms(h, layer["norm_in"])
-            h = h + (self._attn(i, xn, pos_t) if i in attn else self._gdn(i, xn))
-            xn = self._rms(h, layer["norm_post"])
-            h = h + self._moe(i, xn)
+            delta = self._attn(i, xn, pos_t) if i in attn else self._gdn(i, xn)
+            h, xn = self.backend.fused_add_rms_norm(h, delta, layer["norm_post"], cfg.eps)
+            nxt = self.layers[i + 1]["norm_in"] if i + 1 < cfg.n_layers else self.norm_f
+            h, xn = self.backend.fused_add_rms_norm(h, self._moe(i, xn), nxt, cfg.eps)
         if not logits:
             return None
-        return self._lin(self.head, self._planes(self._rms(h, self.norm_f)))
+        return self._lin(self.head, self._planes(xn))
 
     @torch.inference_mode()
     def _step(self, tokens: torch.Tensor, pos: int, logits: bool) -> torch.Tensor | None:

@@ -179,6 +179,18 @@ BT_API int bt_gdn_decode(const void* q, const void* k, const void* v, int in_dty
                   int64_t batch, int64_t heads_k, int64_t heads_v, int64_t dim,
                   float scale, float eps, void* stream);
 
+/* bt_gdn_decode on strided views, as the model layer hands them over
+ * (model/qwen36_moe.py:459-483 slices q, k and v out of the conv output and
+ * beta / alpha out of their projections): row b of q, k, v, g, beta and out
+ * starts b * q_bs, k_bs, v_bs, g_bs, beta_bs and out_bs elements after the
+ * first; inside a row the heads are contiguous as above.                  */
+BT_API int bt_gdn_decode_strided(const void* q, const void* k, const void* v, int in_dtype,
+                          int64_t q_bs, int64_t k_bs, int64_t v_bs, const float* g,
+                          int64_t g_bs, const float* beta, int64_t beta_bs, float* state,
+                          float* out, int64_t out_bs, int64_t batch, int64_t heads_k,
+                          int64_t heads_v, int64_t dim, float scale, float eps,
+                          void* stream);
+
 /* The GDN short conv (model/qwen36_moe.py:465-468) for `batch` sequences:
  * window = [state (taps-1 per channel) | entry], out = silu(sum_j window[j] *
  * w[c][j]) in tap order, state <- window[1:] (in place).  entry, out:

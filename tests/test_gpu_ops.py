@@ -168,6 +168,37 @@ def test_gdn_decode_config2_256_steps(be, batch) -> None:
     np.testing.assert_allclose(state.cpu().numpy(), ref_state, rtol=1e-4, atol=1e-4)
 
 
+def test_gdn_decode_strided_views_equal_contiguous(cuda) -> None:
+    """bt_gdn_decode_strided on views of one packed row per sequence (q | k |
+    v as the conv output holds them, beta | alpha as one projection, out with
+    padding) gives the same bits as bt_gdn_decode on contiguous copies, with
+    the GQA head mapping (32 value heads over 16 key heads)."""
+    rng = np.random.default_rng(31)
+    B, HK, HV, D = 5, 16, 32, 128
+    c = 2 * HK * D + HV * D
+    mixed = torch.from_numpy(rng.standard_normal((B, c), dtype=np.float32) * 0.3).cuda()
+    ba = torch.from_numpy(rng.standard_normal((B, 2 * HV), dtype=np.float32)).cuda()
+    g = -torch.nn.functional.softplus(torch.from_numpy(rng.standard_normal((B, HV), dtype=np.float32))).cuda()
+    q, k, v = mixed[:, : HK * D], mixed[:, HK * D : 2 * HK * D], mixed[:, 2 * HK * D :]
+    beta = ba[:, :HV]
+    s0 = torch.from_numpy(rng.standard_normal((B, HV, D, D), dtype=np.float32) * 0.1).cuda()
+    s1, s2 = s0.clone(), s0.clone()
+    o1 = torch.empty(B, HV, D, device="cuda")
+    o2 = torch.full((B, HV * D + 64), float("nan"), device="cuda")
+    qc, kc, vc, bc = q.contiguous(), k.contiguous(), v.contiguous(), beta.contiguous()
+    N.call("bt_gdn_decode", qc.data_ptr(), kc.data_ptr(), vc.data_ptr(), N.BT_F32, g.data_ptr(), bc.data_ptr(),
+           s1.data_ptr(), o1.data_ptr(), B, HK, HV, D, float(D ** -0.5), 1e-6, 0)
+    N.call("bt_gdn_decode_strided", q.data_ptr(), k.data_ptr(), v.data_ptr(), N.BT_F32, c, c, c, g.data_ptr(), HV,
+           beta.data_ptr(), 2 * HV, s2.data_ptr(), o2.data_ptr(), HV * D + 64, B, HK, HV, D, float(D ** -0.5), 1e-6,
+           0)
+    assert torch.equal(o2[:, : HV * D].reshape(B, HV, D), o1)
+    assert torch.isnan(o2[:, HV * D :]).all()  # the padding is not written
+    assert torch.equal(s2, s1)
+    assert N.load().bt_gdn_decode_strided(q.data_ptr(), k.data_ptr(), v.data_ptr(), N.BT_F32, HK * D - 1, c, c,
+                                          g.data_ptr(), HV, beta.data_ptr(), 2 * HV, s2.data_ptr(), o2.data_ptr(),
+                                          HV * D, B, HK, HV, D, 1.0, 1e-6, None) == N.BT_ERR_INVALID
+
+
 def test_attention_matches_reference(be) -> None:
     g, inp = golden("ops"), ops_inputs()
     for seq in (1, 17, 128):
