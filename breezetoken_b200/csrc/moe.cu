@@ -547,6 +547,30 @@ __device__ __forceinline__ int item_at(const int32_t* cum, int n_slots, int chun
   return lo * chunks + static_cast<int>((rem + pu - 1) / pu);
 }
 
+// Exclusive prefix sum of v over the threads of a kThreads block, in thread
+// order; *total gets the sum over all threads.  Every thread calls it.
+__device__ __forceinline__ int block_exscan(int v, int* wsum, int& total) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  int inc = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int y = __shfl_up_sync(0xffffffffu, inc, o);
+    if (lane >= o) inc += y;
+  }
+  if (lane == 31) wsum[warp] = inc;
+  __syncthreads();
+  int base = 0;
+  total = 0;
+#pragma unroll
+  for (int w = 0; w < kWarps; ++w) {
+    const int sw = wsum[w];
+    if (w < warp) base += sw;
+    total += sw;
+  }
+  __syncthreads();  // wsum free for the next scan
+  return base + inc - v;
+}
+
 // Block 0 (T > 1): counting sort of the P pairs by expert id (stable) into
 // slots, and each expert-kernel CTA's contiguous item range, balanced by
 // token passes.  The next T blocks: encode token (block - 1) (T == 1: block
@@ -585,7 +609,8 @@ __global__ void __launch_bounds__(kThreads) moe_prep_kernel(const int32_t* __res
   int32_t* off = sm + n_experts;   // [n_experts] exclusive prefix of counts
   int32_t* cum = off + n_experts;  // [n_experts + 1] prefix of the slots' passes
   int32_t* sid = cum + n_experts + 1;  // [p_total] the ids
-  __shared__ int32_t s_bad, s_slots;
+  __shared__ int32_t s_bad;
+  __shared__ int s_wsum[kWarps];
   for (int e = threadIdx.x; e < n_experts; e += blockDim.x) cnt[e] = 0;
   for (int q = threadIdx.x; q < p_total; q += blockDim.x) sid[q] = ids[q];
   if (threadIdx.x == 0) s_bad = 0;
@@ -598,26 +623,48 @@ __global__ void __launch_bounds__(kThreads) moe_prep_kernel(const int32_t* __res
       atomicAdd(&s_bad, 1);
   }
   __syncthreads();
-  if (threadIdx.x == 0) {
-    int o = 0, u = 0;
-    cum[0] = 0;
-    for (int e = 0; e < n_experts; ++e) {
+  // Slots = the experts with pairs, in id order.  Thread j owns a contiguous
+  // range of expert ids; three block scans give each range its first pair
+  // offset, first slot and first pass (the same values a serial walk over
+  // the ids would give).
+  int n_slots;
+  {
+    const int per = (n_experts + kThreads - 1) / kThreads;
+    const int e0 = min(n_experts, static_cast<int>(threadIdx.x) * per), e1 = min(n_experts, e0 + per);
+    int c_sum = 0, s_sum = 0, p_sum = 0;
+    for (int e = e0; e < e1; ++e) {
+      const int c = cnt[e];
+      c_sum += c;
+      s_sum += c > 0;
+      p_sum += (c + kTokensPerPass - 1) / kTokensPerPass;
+    }
+    int c_tot, s_tot, p_tot;
+    int o = block_exscan(c_sum, s_wsum, c_tot);
+    int u = block_exscan(s_sum, s_wsum, s_tot);
+    int pc = block_exscan(p_sum, s_wsum, p_tot);
+    (void)c_tot;
+    (void)p_tot;
+    n_slots = s_tot;
+    if (threadIdx.x == 0) {
+      cum[0] = 0;
+      ws.hdr[0] = s_tot;
+      ws.hdr[1] = s_bad;
+    }
+    for (int e = e0; e < e1; ++e) {
+      const int c = cnt[e];
       off[e] = o;
-      if (cnt[e]) {
+      if (c) {
         ws.slot_expert[u] = e;
         ws.slot_start[u] = o;
-        ws.slot_count[u] = cnt[e];
-        cum[u + 1] = cum[u] + (cnt[e] + kTokensPerPass - 1) / kTokensPerPass;
+        ws.slot_count[u] = c;
+        pc += (c + kTokensPerPass - 1) / kTokensPerPass;
+        cum[u + 1] = pc;
         ++u;
       }
-      o += cnt[e];
+      o += c;
     }
-    ws.hdr[0] = u;
-    ws.hdr[1] = s_bad;
-    s_slots = u;
   }
-  __syncthreads();
-  const int n_slots = s_slots;
+  __syncthreads();  // cum and off complete
   for (int b = threadIdx.x; b < gu_grid; b += blockDim.x) {
     const int64_t w = static_cast<int64_t>(cum[n_slots]) * gu_chunks;
     ws.ranges[2 * b] = item_at(cum, n_slots, gu_chunks, b * w / gu_grid);
