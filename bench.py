@@ -1,6 +1,6 @@
 """Benchmark: Qwen3.5-0.8B-shaped batch-1 greedy decode on B200 (tok/s).
 
-Workload: seeded random Qwen3.5-0.8B-shaped Q8_0 GGUF
+Workload (the batch-1 0.8B decode benchmark): seeded random Qwen3.5-0.8B-shaped Q8_0 GGUF
 (24 layers [GDN,GDN,GDN,GQA]x6, hidden 1024, FFN 3584, vocab 151936), a
 16-token uniform-random prompt, then 128 greedy decode steps.  One bench
 "step" is one decode step (one token per sequence).  The timed region runs

@@ -10,12 +10,12 @@
 
 Each prints one JSON line: average launch time and achieved HBM GB/s from
 the algorithmic bytes of one launch (weights / state / KV read once).
-``moe`` is BASELINE config 4: routed experts of one MoE layer (hidden 2048,
+``moe`` is the 35B-A3B MoE-layer benchmark: routed experts of one MoE layer (hidden 2048,
 256 IQ3_S experts of ffn 512, top-8 over N(0,1) router logits, seed 3),
 timed per call after reading a 256 MB buffer (the experts are not in L2);
 its bytes are the
 U * 1,351,680 of the U distinct experts the routing selects.
-``qwen36`` is BASELINE config 5 on one GPU (Qwen3.6-35B-A3B shape, seeded
+``qwen36`` is the 35B-A3B decode benchmark on one GPU (Qwen3.6-35B-A3B shape, seeded
 random weights built on the device, 64 sequences in lockstep).
 ``linear`` times ``bt_linear_rows`` (bf16 weight rows x three bf16 planes of
 x) at config 5's projection shapes (GDN qkv 8192 x 2048, z 4096 x 2048, out
@@ -23,8 +23,8 @@ x) at config 5's projection shapes (GDN qkv 8192 x 2048, z 4096 x 2048, out
 copies larger than L2 together.
 ``trace`` prints the device-side timeline of one Qwen3.5 decode step (per
 kernel kind: release gap, prologue, body) after a 16-token prefill.
-``gdn`` and ``attn`` are the stand-alone decode ops of BASELINE configs 2
-and 3 with their synthetic inputs (seeds 1 and 2).
+``gdn`` and ``attn`` are the stand-alone GDN-step and split-KV attention decode
+benchmarks with their synthetic inputs (seeds 1 and 2).
 """
 
 from __future__ import annotations
@@ -208,7 +208,7 @@ def bench_moe(tokens: int, iters: int, shared: bool = True) -> dict:
         flush.sum(dtype=torch.int32)  # read 256 MB: afterwards L2 holds only clean lines
 
     se = None
-    if shared:  # one bf16 shared expert of ffn 512
+    if shared:  # one bf16 shared expert of ffn 512 (the 35B-A3B layer)
         def w(*shape) -> torch.Tensor:
             return torch.from_numpy(rng.standard_normal(shape).astype(np.float32) * np.float32(0.02))
 
@@ -246,7 +246,7 @@ def bench_moe(tokens: int, iters: int, shared: bool = True) -> dict:
 
 
 def bench_qwen36(batch: int, prompt: int, steps: int, layers: int) -> dict | None:
-    """`batch` sequences of a `prompt`-token random prompt,
+    """The 35B-A3B decode benchmark: `batch` sequences of a `prompt`-token random prompt,
     fed in lockstep, then `steps` greedy steps timed with CUDA events; seeded
     random weights of the Qwen3.6-35B-A3B shape (with `layers` layers) built
     on the device.  Under torchrun the sequences are sharded: each of the N

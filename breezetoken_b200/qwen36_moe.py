@@ -8,7 +8,7 @@ experts + shared expert and argmax run on this library's kernels; the
 elementwise glue between them (conv window, output gates, residual adds, KV
 writes) runs as torch device ops, as in the reference's model layer.
 
-B sequences decode in lockstep at one position (how BASELINE config 5's 64
+B sequences decode in lockstep at one position (how the 35B-A3B benchmark's 64
 sequences per GPU run).  Prompts are fed token by token: the reference
 switches to a batched prefill with bf16 expert math for prompts of 8 or more
 tokens (_prefill_batch, :588-612), which this mirror does not reproduce.

@@ -55,7 +55,7 @@ class Qwen35Spec:
     context_length: int = 262144
 
 
-#: BASELINE config 1: the Qwen3.5-0.8B shape.
+#: The Qwen3.5-0.8B shape (the batch-1 decode benchmark).
 QWEN35_0_8B = Qwen35Spec()
 #: A small model with the same per-layer kernel shapes (GQA 8/2x256, GDN 16x128)
 #: and one full [GDN, GDN, GDN, GQA] period, for fast parity tests.
@@ -226,7 +226,7 @@ def make_moe_layer(spec: MoeSpec = MoeSpec(), seed: int = 3, n_experts: int | No
 # --------------------------------------------------------------------------
 @dataclass(frozen=True)
 class Qwen36Spec:
-    """Shape of a qwen35moe decoder (BASELINE config 5 with the defaults)."""
+    """Shape of a qwen35moe decoder (the 35B-A3B benchmark shape with the defaults)."""
 
     hidden: int = 2048
     n_layers: int = 40
@@ -257,7 +257,7 @@ class Qwen36Spec:
         return 2 * self.gdn_key_heads * self.gdn_dim + self.gdn_inner
 
 
-#: BASELINE config 5.
+#: The Qwen3.6-35B-A3B benchmark shape.
 QWEN36_35B = Qwen36Spec()
 #: The config-5 layer shapes (hidden 2048, GQA 16/2x256, GDN 16K/32V x128,
 #: experts of ffn 512 + a shared expert) with one [GDN, GDN, GDN, GQA]

@@ -11,13 +11,13 @@ records, on seeded inputs, what its torch f32 path computes:
   16/32 heads x 128, like tests/test_cuda.py:56-77,170-191),
   ``_torch_attention`` (seq 1, 17, 128; tests/test_cuda.py:195-211),
   ``_torch_rope``, rms_norm, fused_add_rms_norm, silu_mul;
-* ``moe.npz``       -- ``route`` on N(0,1) router logits (BASELINE config 4
+* ``moe.npz``       -- ``route`` on N(0,1) router logits (the 35B-A3B MoE layer
   shape) and one ``ExpertPool``-style expert evaluation from IQ3_S bytes;
 * ``moe_shared.npz`` -- ``Qwen36Moe._moe`` (routed output + gated bf16 shared
   expert) run on a stand-in object around moe.npz's routed output;
 * ``qwen36_tiny.npz`` -- greedy token ids, top-2 margins and the first
   logits of the reference's ``Qwen36Moe`` (CPU, f32) on the seeded tiny
-  qwen35moe checkpoint (BASELINE config 5 layer shapes);
+  qwen35moe checkpoint (35B-A3B layer shapes);
 * ``qwen35_tiny.npz`` / ``qwen35_0_8b.npz`` -- greedy token ids of
   ``Qwen35(backend="torch", device="cpu").generate`` on the seeded synthetic
   checkpoints of breezetoken_b200.synth, with per-step top-2 logit margins and
@@ -157,7 +157,7 @@ def gen_ops(out: Path) -> None:
 
 
 def moe_inputs():
-    """Seeded MoE-layer inputs (BASELINE config 4 shapes, 16 experts)."""
+    """Seeded MoE-layer inputs (35B-A3B layer shapes, 16 experts)."""
     rng = np.random.default_rng(3)
     hidden, ffn, n_exp = 2048, 512, 16
     logits = rng.standard_normal(256).astype(np.float32)
@@ -198,7 +198,7 @@ def gen_moe(out: Path) -> None:
 
 
 def moe_shared_inputs():
-    """Seeded bf16 shared expert for moe_inputs() (one
+    """Seeded bf16 shared expert for moe_inputs() (the 35B-A3B layer: one
     bf16 shared expert of ffn 512), as f32 arrays holding bf16 values."""
     rng = np.random.default_rng(4)
     m = moe_inputs()
@@ -242,7 +242,7 @@ def gen_moe_shared(out: Path) -> None:
 def gen_qwen36_tiny(out: Path, steps: int = 24) -> None:
     """Greedy decode of the reference's Qwen36Moe (model/qwen36_moe.py,
     device="cpu", dtype="f32") on the seeded tiny qwen35moe checkpoint of
-    breezetoken_b200.synth (BASELINE config 5 layer shapes, 4 layers, 16
+    breezetoken_b200.synth (35B-A3B layer shapes, 4 layers, 16
     experts).  The 7-token prompt stays below the reference's batched-prefill
     threshold (8 tokens), so every token takes its per-token f32 path."""
     from breezetoken.model.qwen36_moe import Qwen36Moe

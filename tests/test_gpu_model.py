@@ -91,7 +91,7 @@ def test_invalid_inputs_raise(tiny) -> None:
 
 
 def test_0_8b_greedy_128_steps_match_reference(cuda, gguf_0_8b) -> None:
-    """16-token prompt, 128 greedy steps, identical ids."""
+    """The 0.8B decode benchmark: 16-token prompt, 128 greedy steps, identical ids."""
     g = golden("qwen35_0_8b")
     m = Qwen35(gguf_0_8b, max_context=int(g["max_context"]))
     try:

@@ -1,5 +1,5 @@
 """GPU parity of the routed-expert (MoE) path against the oracle and the
-reference's golden output (BASELINE config 4 shapes: hidden 2048, ffn 512,
+reference's golden output (the 35B-A3B layer shapes: hidden 2048, ffn 512,
 IQ3_S experts, top-8 routing).
 
 f32 tolerance: outputs within 1e-5 of the output scale (max |ref|): the

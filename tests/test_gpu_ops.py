@@ -135,7 +135,7 @@ def test_gdn_decode_matches_reference(be) -> None:
 
 @pytest.mark.parametrize("batch", [1, 8, 64])
 def test_gdn_decode_config2_256_steps(be, batch) -> None:
-    """16 heads x 128, bf16 q/k/v, 256 steps, seed 1, vs the oracle."""
+    """The GDN op benchmark: 16 heads x 128, bf16 q/k/v, 256 steps, seed 1, vs the oracle."""
     steps = 256 if batch <= 8 else 32
     rng = np.random.default_rng(1)
     H, D = 16, 128
@@ -212,7 +212,7 @@ def test_attention_matches_reference(be) -> None:
     [(1, 1024, 8), (16, 1024, 4), (4, 8192, 16), (2, 32768, 64), (1, 8192, 40), (3, 777, 5)],
 )
 def test_attention_config3_bf16(be, batch, ctx, splits) -> None:
-    """BASELINE config 3 shapes: 8q/2kv x 256, bf16 KV N(0,1), scale 1/16, vs the f32 oracle."""
+    """The flash-decode benchmark shapes: 8q/2kv x 256, bf16 KV N(0,1), scale 1/16, vs the f32 oracle."""
     rng = np.random.default_rng(2)
     q = rng.standard_normal((batch, 8, 256), dtype=np.float32)
     k = torch.from_numpy(rng.standard_normal((batch, ctx, 2, 256), dtype=np.float32)).to(torch.bfloat16)
