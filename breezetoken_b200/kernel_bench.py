@@ -18,7 +18,7 @@ U * 1,351,680 of the U distinct experts the routing selects.
 ``qwen36`` is the 35B-A3B decode benchmark on one GPU (Qwen3.6-35B-A3B shape, seeded
 random weights built on the device, 64 sequences in lockstep).
 ``linear`` times ``bt_linear_rows`` (bf16 weight rows x three bf16 planes of
-x) at config 5's projection shapes (GDN qkv 8192 x 2048, z 4096 x 2048, out
+x) at the 35B-A3B decoder's projection shapes (GDN qkv 8192 x 2048, z 4096 x 2048, out
 2048 x 4096, the 151936 x 2048 head) for T tokens, cycling over weight
 copies larger than L2 together.
 ``trace`` prints the device-side timeline of one Qwen3.5 decode step (per
@@ -384,7 +384,7 @@ def main() -> None:
     mo.add_argument("--no-shared", action="store_true", help="routed experts only")
     li = sub.add_parser("linear")
     li.add_argument("--tokens", type=int, default=64)
-    li.add_argument("--n", type=int, default=0, help="0: config 5's projection shapes")
+    li.add_argument("--n", type=int, default=0, help="0: the 35B-A3B decoder's projection shapes")
     li.add_argument("--k", type=int, default=2048)
     li.add_argument("--iters", type=int, default=20)
     q6 = sub.add_parser("qwen36")
