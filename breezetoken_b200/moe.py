@@ -14,6 +14,7 @@ on an unsupported shape or a missing library; there is no CPU path.
 from __future__ import annotations
 
 import ctypes
+import warnings
 from dataclasses import dataclass
 
 import numpy as np
@@ -61,7 +62,13 @@ class IQ3SExperts:
 
     @staticmethod
     def _repack(raw, rows: int, k: int, device: str) -> torch.Tensor:
-        src = torch.as_tensor(np.ascontiguousarray(raw) if isinstance(raw, np.ndarray) else raw)
+        if isinstance(raw, np.ndarray):
+            with warnings.catch_warnings():
+                # GGUF bytes are a read-only memory map; the tensor is only read (the upload's source)
+                warnings.filterwarnings("ignore", message="The given NumPy array is not writable")
+                src = torch.as_tensor(np.ascontiguousarray(raw))
+        else:
+            src = torch.as_tensor(raw)
         src = src.reshape(-1).to(device)
         if src.numel() != rows * k // 256 * 110:
             raise ValueError(f"expected {rows * k // 256 * 110} IQ3_S bytes, got {src.numel()}")
