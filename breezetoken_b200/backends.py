@@ -16,6 +16,7 @@ in place) and error kinds (``ValueError`` for shape mismatches,
 from __future__ import annotations
 
 import ctypes as C
+import warnings
 from dataclasses import dataclass
 
 import numpy as np
@@ -79,7 +80,13 @@ class Q8Weight:
         """Upload GGUF Q8_0 rows and repack them into rows dst_row0 + i*step."""
         if rows == 0:
             return
-        src = torch.as_tensor(np.ascontiguousarray(raw) if isinstance(raw, np.ndarray) else raw)
+        if isinstance(raw, np.ndarray):
+            with warnings.catch_warnings():
+                # GGUF bytes are a read-only memory map; the tensor is only read (the upload's source)
+                warnings.filterwarnings("ignore", message="The given NumPy array is not writable")
+                src = torch.as_tensor(np.ascontiguousarray(raw))
+        else:
+            src = torch.as_tensor(raw)
         src = src.reshape(-1).to(self.device, non_blocking=False)
         if src.numel() != rows * self.k // 32 * 34:
             raise ValueError(f"expected {rows * self.k // 32 * 34} Q8_0 bytes, got {src.numel()}")
