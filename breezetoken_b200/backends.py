@@ -118,9 +118,20 @@ class B200Backend:
         self._ws: dict[tuple, torch.Tensor] = {}
 
     # ------------------------------------------------------------ helpers
+    def _check(self, *tensors) -> None:
+        """Every tensor argument must live on this backend's device before its
+        pointer reaches a kernel (a host pointer there would fault the GPU);
+        a mismatch raises like the reference's torch ops do."""
+        want = torch.device(self.device)
+        for t in tensors:
+            if t is None:
+                continue
+            d = t.device
+            if d.type != want.type or (want.index is not None and d.index is not None and d.index != want.index):
+                raise RuntimeError(f"tensor on {d}, backend on {self.device}")
+
     def _f32(self, t: torch.Tensor) -> torch.Tensor:
-        if t.device != torch.device(self.device) and not (t.is_cuda and torch.device(self.device).index is None):
-            raise ValueError(f"tensor on {t.device}, backend on {self.device}")
+        self._check(t)
         return t.float().contiguous() if t.dtype != torch.float32 or not t.is_contiguous() else t
 
     def _workspace(self, key: tuple, nbytes: int) -> torch.Tensor:
@@ -141,8 +152,10 @@ class B200Backend:
             raise ValueError(f"linear expects one vector of {K}, got {tuple(x.shape)}")
         y = torch.empty(Nn, dtype=torch.float32, device=self.device)
         if isinstance(w, Q8Weight):
+            self._check(w.data)
             N.call("bt_linear_q8", w.data.data_ptr(), xf.data_ptr(), y.data_ptr(), Nn, K, 1, _stream())
             return y
+        self._check(w)
         if w.dtype not in (torch.bfloat16, torch.float32):
             raise N.B200Error(N.BT_ERR_UNSUPPORTED, f"linear: weight dtype {w.dtype} not served")
         wc = w.contiguous()
@@ -159,6 +172,7 @@ class B200Backend:
         S = xf.shape[0]
         y = torch.empty(S, Nn, dtype=torch.float32, device=self.device)
         if isinstance(w, Q8Weight):
+            self._check(w.data)
             r = 0
             while r < S:
                 nv = 8 if S - r >= 8 else 4 if S - r >= 4 else 2 if S - r >= 2 else 1
@@ -195,7 +209,10 @@ class B200Backend:
             af.data_ptr(), bf.data_ptr(), wf.data_ptr(), h.data_ptr(), xn.data_ptr(),
             af.numel() // n, n, float(eps), _stream(),
         )
-        return h, xn
+        # h in the inputs' promoted dtype as the reference returns it (a + b);
+        # xn is normalised from the f32 sum
+        hd = torch.promote_types(a.dtype, b.dtype)
+        return (h if hd == torch.float32 else h.to(hd)), xn
 
     def silu_mul(self, gate: torch.Tensor, up: torch.Tensor) -> torch.Tensor:
         if gate.shape != up.shape:
@@ -226,6 +243,7 @@ class B200Backend:
         if kd != dim or v.shape != k.shape or heads % groups:
             raise ValueError(f"attention shape mismatch: q {tuple(q.shape)}, k {tuple(k.shape)}, v {tuple(v.shape)}")
         qf = self._f32(q)
+        self._check(k, v, lens)
         if k.dtype == torch.bfloat16 and v.dtype == torch.bfloat16:
             kk, vv, dt = k.contiguous(), v.contiguous(), N.BT_BF16
         else:
@@ -266,6 +284,7 @@ class B200Backend:
             raise ValueError(f"state shape {tuple(state.shape)} != {(heads_v, dim, dim)}")
         if state.dtype != torch.float32 or not state.is_contiguous():
             raise ValueError("gdn_decode state must be contiguous float32 (it is updated in place)")
+        self._check(q, k, v, g, beta, state)
         if q.dtype == k.dtype == v.dtype == torch.bfloat16:
             qq, kk, vv, dt = q.contiguous(), k.contiguous(), v.contiguous(), N.BT_BF16
         else:

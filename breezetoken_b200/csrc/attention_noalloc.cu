@@ -54,9 +54,14 @@ extern "C" int bt_attention_decode_noalloc(const float* q, const void* k, const 
                                            void* stream) {
   using bt::fail;
   if (!q || !k || !v || !lens || !out) return fail(BT_ERR_INVALID, "noalloc attention: null pointer");
-  if (batch < 1 || batch > 65535 || heads < 1 || kv_heads < 1 || kv_heads > 65535 || dim < 1 || cap < 1 ||
-      cap > (1LL << 30) || splits < 1)
+  // bounded before any size arithmetic, so the scratch size below cannot
+  // overflow and every field fits the kernel's 32-bit parameters
+  if (batch < 1 || batch > 65535 || heads < 1 || heads > 65535 || kv_heads < 1 || kv_heads > 65535 || dim < 1 ||
+      dim > 1024 || cap < 1 || cap > (1LL << 30) || splits < 1 || splits > 65535)
     return fail(BT_ERR_INVALID, "noalloc attention: shape out of range");
+  if (heads % kv_heads != 0)
+    return fail(BT_ERR_INVALID, "noalloc attention: heads (%lld) must be a multiple of kv_heads (%lld)",
+                static_cast<long long>(heads), static_cast<long long>(kv_heads));
   const int64_t part_bytes = (4 * bt::attn_part_floats(batch, kv_heads, heads, dim, splits) + 255) / 256 * 256;
   const int64_t counter_bytes = 4 * bt::attn_counters(batch, kv_heads, splits);
   if (part_bytes + counter_bytes > bt::kNoallocScratchBytes)

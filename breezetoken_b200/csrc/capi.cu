@@ -305,6 +305,12 @@ int bt_qwen35_graph_create(const BtQwen35Model* model, const BtQwen35Runtime* rt
   e = cudaGraphInstantiate(&exec, graph, 0);
   cudaGraphDestroy(graph);
   if (e != cudaSuccess) return bt::fail_cuda(e, "graph instantiate");
+  // upload now, so the first launch does not pay for it
+  e = cudaGraphUpload(exec, s);
+  if (e != cudaSuccess) {
+    cudaGraphExecDestroy(exec);
+    return bt::fail_cuda(e, "graph upload");
+  }
   *graph_out = exec;
   return BT_OK;
 }

@@ -2,7 +2,6 @@
 // epilogue) kinds.  The kernels are in gemv_q8_impl.cuh and are instantiated
 // per kind in the gemv_q8_k_*.cu files.  See gemv_q8.cuh for the design.
 #include <algorithm>
-#include <cstdlib>
 
 #include "errors.h"
 #include "gemv_q8_impl.cuh"
@@ -15,31 +14,13 @@ BT_GEMV_KINDS(BT_GEMV_EXTERN)
 
 namespace {
 
-struct GemvTuning {
-  // weight bytes per CTA prefetched into L2 before the dependency wait
-  // (BT_GEMV_PREFETCH_KB overrides it for tuning sweeps)
-  int64_t prefetch_bytes = 64 * 1024;
-  // CTAs per SM for long matrices (BT_GEMV_BIG_GRID: 1 or 2)
-  int big_grid = 2;
-  // row units (4 rows) per SM from which a matrix counts as long (BT_GEMV_BIG_UNITS)
-  int big_units = 8;
-};
-
-int env_int(const char* name, int dflt) {
-  const char* v = getenv(name);
-  return v && *v ? atoi(v) : dflt;
-}
-
-const GemvTuning& tuning() {
-  static const GemvTuning t = [] {
-    GemvTuning g;
-    g.prefetch_bytes = static_cast<int64_t>(std::min(1024, std::max(0, env_int("BT_GEMV_PREFETCH_KB", 64)))) * 1024;
-    g.big_grid = std::min(2, std::max(1, env_int("BT_GEMV_BIG_GRID", 2)));
-    g.big_units = std::max(1, env_int("BT_GEMV_BIG_UNITS", 8));
-    return g;
-  }();
-  return t;
-}
+// Weight bytes per CTA prefetched into L2 before the dependency wait.
+constexpr int64_t kPrefetchBytes = 64 * 1024;
+// Long matrices (at least kBigUnits row units of 4 rows per SM) run
+// kBigGrid CTAs per SM: twice the weight bytes in flight and half the rows
+// per CTA after the dependency wait.
+constexpr int kBigGrid = 2;
+constexpr int kBigUnits = 8;
 
 }  // namespace
 
@@ -68,10 +49,8 @@ int gemv_q8_plan(GemvQ8Params& p, int sm_count, GemvQ8Launch& L) {
   p.sb = static_cast<int32_t>(bt_q8_row_bytes(p.k) - p.k);
   p.row_bytes = static_cast<int32_t>(bt_q8_row_bytes(p.k));
   const int64_t n_units = (p.n_rows + 3) / 4;
-  // matrices of >= 8 row units per SM run two CTAs per SM: twice the weight
-  // bytes in flight and half the rows per CTA after the dependency wait
-  const int64_t ctas = n_units >= static_cast<int64_t>(tuning().big_units) * sm_count
-                           ? static_cast<int64_t>(tuning().big_grid) * sm_count
+  const int64_t ctas = n_units >= static_cast<int64_t>(kBigUnits) * sm_count
+                           ? static_cast<int64_t>(kBigGrid) * sm_count
                            : sm_count;
   const int grid = static_cast<int>(std::min<int64_t>(ctas, n_units));
   const int64_t rows_per_cta = ((n_units + grid - 1) / grid) * 4;
@@ -83,7 +62,7 @@ int gemv_q8_plan(GemvQ8Params& p, int sm_count, GemvQ8Launch& L) {
   if (p.epilogue == EPI_SILU_PAIR && !g4_ok)
     return fail(BT_ERR_UNSUPPORTED, "SiLU-pair epilogue serves at most 2 vectors and K <= 1024");
   p.group_rows = gr;
-  p.prefetch_bytes = tuning().prefetch_bytes;
+  p.prefetch_bytes = kPrefetchBytes;
   L.grid = grid;
   L.threads = kGemvThreads;
   L.smem = GemvSmem::kHeader + gemv_x_layout(p.k, p.n_vec).total;

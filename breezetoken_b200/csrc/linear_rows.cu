@@ -363,21 +363,37 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t addr, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
-// Waits until the phase of `parity` has completed.  Gives up after
-// kWaitLimitNs, counting the timeout; once a wait of this CTA gave up
-// (*abort), the others return at once, so a broken pipeline ends promptly.
-__device__ __forceinline__ void mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort) {
+// Waits until the phase of `parity` has completed; true once it has.  Gives
+// up after kWaitLimitNs, counting the timeout; once a wait of this CTA gave
+// up (*abort), the others return false at once, so a broken pipeline stops
+// issuing work promptly.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort) {
   const uint32_t a = smem_u32(bar);
-  if (mbar_try_wait(a, parity)) return;
+  if (mbar_try_wait(a, parity)) return true;
   const uint64_t t0 = global_ns();
   while (!mbar_try_wait(a, parity)) {
-    if (*abort) return;
+    if (*abort) return false;
     if (global_ns() - t0 > kWaitLimitNs) {
       *abort = 1;
       atomicAdd(&g_umma_timeouts, 1);
-      return;
+      return false;
     }
   }
+  return true;
+}
+// The same wait without the early return on *abort: used after an abort to
+// let copies and MMAs already issued complete before the CTA reuses its
+// shared memory or frees its TMEM.  Still bounded by kWaitLimitNs.
+__device__ __forceinline__ bool mbar_drain(uint64_t* bar, uint32_t parity) {
+  const uint32_t a = smem_u32(bar);
+  const uint64_t t0 = global_ns();
+  while (!mbar_try_wait(a, parity)) {
+    if (global_ns() - t0 > kWaitLimitNs) {
+      atomicAdd(&g_umma_timeouts, 1);
+      return false;
+    }
+  }
+  return true;
 }
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
@@ -509,21 +525,30 @@ __global__ void __launch_bounds__(kThreads, 1)
   pdl_launch_dependents();
 
   if (threadIdx.x == 0) {
-    // producer: stage st into buffer st % S once the MMAs of stage st - S released it
+    // producer: stage st into buffer st % S once the MMAs of stage st - S
+    // released it; after a wait gave up nothing new is issued
+    int issued = 0;
     for (int st = 0; st < nst; ++st) {
       const int b = st % kUmmaStages;
-      if (st >= kUmmaStages) mbar_wait(&empty[b], ((st / kUmmaStages) - 1) & 1, &s_abort);
+      if (st >= kUmmaStages && !mbar_wait(&empty[b], ((st / kUmmaStages) - 1) & 1, &s_abort)) break;
       mbar_arrive_expect_tx(&full[b], STAGE);
       const uint32_t sa = sbase + b * STAGE;
       const int kk = kbeg + st * kUmmaKStage;
       tma_load_2d(sa, &tmw, kk, row0, &full[b]);
       tma_load_2d(sa + A_BYTES, &tmx, kk, 3 * tok0, &full[b]);
+      issued = st + 1;
+    }
+    if (s_abort) {
+      // each buffer has at most one copy in flight (its last issued stage):
+      // let them land before the stages are overwritten below
+      for (int st = issued > kUmmaStages ? issued - kUmmaStages : 0; st < issued; ++st)
+        mbar_drain(&full[st % kUmmaStages], (st / kUmmaStages) & 1);
     }
   } else if (threadIdx.x == 32) {
     // MMA issuer: four K-16 steps per stage, then the stage's buffer goes back
     for (int st = 0; st < nst; ++st) {
       const int b = st % kUmmaStages;
-      mbar_wait(&full[b], (st / kUmmaStages) & 1, &s_abort);
+      if (!mbar_wait(&full[b], (st / kUmmaStages) & 1, &s_abort)) break;
       tc_fence_after();
       const uint32_t a0 = sbase + b * STAGE, b0 = a0 + A_BYTES;
 #pragma unroll
@@ -531,10 +556,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         umma_bf16(tmem, umma_desc(a0 + 32 * s4), umma_desc(b0 + 32 * s4), IDESC, (st > 0 || s4 > 0) ? 1u : 0u);
       umma_commit(&empty[b]);
     }
-    umma_commit(&done);  // every MMA of the CTA
+    umma_commit(&done);  // every MMA issued by this thread, also after an abort
   }
-  mbar_wait(&done, 0, &s_abort);
+  // every MMA completes before TMEM is read or freed, also after an abort
+  mbar_drain(&done, 0);
   tc_fence_after();
+  __syncthreads();  // the producer's drained copies have landed before the stages are reused
 
   // TMEM lane r = weight row row0 + r, column 3 t + plane; warp w reads
   // lanes 32 (w % 4) .. + 32 and tokens [NT/2 (w / 4), NT/2 (w / 4 + 1))

@@ -77,15 +77,9 @@ GemvQ8Params base_gemv(const BtQwen35Dims& d, const BtQwen35Runtime& rt) {
   return p;
 }
 
-// Programmatic dependent launch between the step's kernels (on by default;
-// BT_PDL=0 serialises them fully, for measurements).
-bool use_pdl() {
-  static const bool on = [] {
-    const char* v = getenv("BT_PDL");
-    return !(v && v[0] == '0');
-  }();
-  return on;
-}
+// Programmatic dependent launch between the step's kernels: each kernel's
+// weight prefetch and first row loads run while its predecessor finishes.
+constexpr bool kUsePdl = true;
 
 // The fused GDN layer kernel where it serves the shapes (on by default;
 // BT_GDN_FUSED=0 runs in-projection, recurrence and gated-norm out-projection
@@ -102,7 +96,7 @@ int run_gemv(GemvQ8Params& p, cudaStream_t s) {
   GemvQ8Launch L{};
   int rc = gemv_q8_plan(p, sm_count(), L);
   if (rc) return rc;
-  return gemv_q8_launch(p, L, s, use_pdl());
+  return gemv_q8_launch(p, L, s, kUsePdl);
 }
 
 }  // namespace
@@ -194,7 +188,7 @@ int qwen35_step(const BtQwen35Model& m, const BtQwen35Runtime& rt, int with_logi
       f.norm_eps = d.eps;
       f.out = rt.mix;
       f.out_bs = mix_stride;
-      if ((rc = gdn_fused_launch(f, s, use_pdl()))) return rc;
+      if ((rc = gdn_fused_launch(f, s, kUsePdl))) return rc;
     } else if ((rc = run_gemv(p1, s))) {
       return rc;
     }
@@ -223,7 +217,7 @@ int qwen35_step(const BtQwen35Model& m, const BtQwen35Runtime& rt, int with_logi
       g.eps = d.l2_eps;
       g.status = rt.status;
       g.trace = trace();
-      if ((rc = gdn_decode_launch(g, s, use_pdl()))) return rc;
+      if ((rc = gdn_decode_launch(g, s, kUsePdl))) return rc;
     } else {
       AttnParams a{};
       const int64_t qsz = 2LL * d.n_heads * d.head_dim;
@@ -260,7 +254,7 @@ int qwen35_step(const BtQwen35Model& m, const BtQwen35Runtime& rt, int with_logi
       a.counters = ws.attn_counters;
       a.status = rt.status;
       a.trace = trace();
-      if ((rc = attention_launch(a, s, use_pdl()))) return rc;
+      if ((rc = attention_launch(a, s, kUsePdl))) return rc;
     }
 
     // ---- 3: out-projection
@@ -333,7 +327,7 @@ int qwen35_step(const BtQwen35Model& m, const BtQwen35Runtime& rt, int with_logi
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = use_pdl() ? 1 : 0;
+    cfg.numAttrs = kUsePdl ? 1 : 0;
     cudaError_t e = cudaLaunchKernelEx(&cfg, advance_pos_kernel, rt.pos, static_cast<int>(d.batch));
     return e == cudaSuccess ? BT_OK : fail_cuda(e, "advance_pos");
   }

@@ -213,14 +213,27 @@ class GGUFWriter:
         else:
             raise TypeError(f"unsupported metadata value for {key}: {type(value)}")
 
-    def add_tensor(self, name: str, shape: tuple[int, ...], ggml_type: int, data: np.ndarray) -> None:
-        """``data``: the stored bytes (uint8) or a float32 array for F32."""
+    @staticmethod
+    def _blob(name: str, shape: tuple[int, ...], ggml_type: int, data: np.ndarray) -> np.ndarray:
         blob = np.ascontiguousarray(data).view(np.uint8).reshape(-1)
         rows = int(np.prod(shape[:-1])) if len(shape) > 1 else 1
         want = rows * row_bytes(ggml_type, shape[-1])
         if blob.nbytes != want:
             raise ValueError(f"{name}: {blob.nbytes} bytes, expected {want}")
-        self._tensors.append((name, tuple(int(s) for s in shape), ggml_type, blob))
+        return blob
+
+    def add_tensor(self, name: str, shape: tuple[int, ...], ggml_type: int, data) -> None:
+        """``data``: the stored bytes (uint8) or a float32 array for F32, or a
+        callable returning them, called once while the file is written (so a
+        large file never holds all its tensors in memory at once)."""
+        shape = tuple(int(s) for s in shape)
+        if not callable(data):
+            data = self._blob(name, shape, ggml_type, data)
+        self._tensors.append((name, shape, ggml_type, data))
+
+    def _nbytes(self, shape: tuple[int, ...], ggml_type: int) -> int:
+        rows = int(np.prod(shape[:-1])) if len(shape) > 1 else 1
+        return rows * row_bytes(ggml_type, shape[-1])
 
     @staticmethod
     def _str(s: str) -> bytes:
@@ -234,18 +247,18 @@ class GGUFWriter:
             head.append(self._str(key) + struct.pack("<I", vtype))
             head.append(self._str(value) if vtype == _STR else struct.pack(_SCALAR[vtype], value))
         offset = 0
-        offsets = []
-        for name, shape, ttype, blob in self._tensors:
-            offsets.append(offset)
+        for name, shape, ttype, _ in self._tensors:
             dims = tuple(reversed(shape))
             head.append(self._str(name) + struct.pack(f"<I{len(dims)}Q", len(dims), *dims))
             head.append(struct.pack("<IQ", ttype, offset))
-            offset += (blob.nbytes + self.ALIGN - 1) // self.ALIGN * self.ALIGN
+            offset += (self._nbytes(shape, ttype) + self.ALIGN - 1) // self.ALIGN * self.ALIGN
         header = b"".join(head)
         with open(path, "wb") as f:
             f.write(header)
             f.write(b"\0" * ((-len(header)) % self.ALIGN))
-            for (_, _, _, blob), off in zip(self._tensors, offsets, strict=True):
-                f.write(blob.tobytes())
+            for name, shape, ttype, data in self._tensors:
+                blob = self._blob(name, shape, ttype, data()) if callable(data) else data
+                f.write(memoryview(blob))
                 f.write(b"\0" * ((-blob.nbytes) % self.ALIGN))
+                del blob
         return path

@@ -149,17 +149,33 @@ def bench_gdn(batch: int, steps: int, heads: int = 16, dim: int = 128) -> dict:
             "note": "graph: the steps captured in one CUDA graph (device time; a B=1 state stays in L2)"}
 
 
-def bench_attn(batch: int, ctx: int, splits: int, iters: int) -> dict:
+def attn_inputs(batch: int, ctx: int, seed: int = 2):
+    """The flash-decode benchmark's inputs (8 q heads, 2 KV heads of 256, one
+    query per sequence, bf16 K/V N(0, 1), uniform length ctx), drawn on the
+    device from a seeded generator: q (B, 8, 256) f32, k and v (B, ctx, 2,
+    256) bf16, lens (B,) int32."""
     heads, kv_heads, dim = 8, 2, 256
-    gen = torch.Generator(device="cuda").manual_seed(2)
+    gen = torch.Generator(device="cuda").manual_seed(seed)
     q = torch.randn(batch, heads, dim, device="cuda", generator=gen)
     kc = torch.randn(batch, ctx, kv_heads, dim, device="cuda", generator=gen).to(torch.bfloat16)
     vc = torch.randn(batch, ctx, kv_heads, dim, device="cuda", generator=gen).to(torch.bfloat16)
     lens = torch.full((batch,), ctx, dtype=torch.int32, device="cuda")
+    return q, kc, vc, lens
+
+
+def attn_splits(batch: int, kv_heads: int, ctx: int) -> int:
+    """KV splits per (sequence, KV head): about two CTAs per SM in total, at
+    least 256 keys per split, at most 256 splits."""
+    return max(1, min(256, (2 * N.load().bt_sm_count() + batch * kv_heads - 1) // (batch * kv_heads), ctx // 256))
+
+
+def bench_attn(batch: int, ctx: int, splits: int, iters: int) -> dict:
+    heads, kv_heads, dim = 8, 2, 256
+    q, kc, vc, lens = attn_inputs(batch, ctx)
     out = torch.empty(batch, heads, dim, device="cuda")
     lib = N.load()
     if splits <= 0:
-        splits = max(1, min(256, (2 * N.load().bt_sm_count() + batch * kv_heads - 1) // (batch * kv_heads), ctx // 256))
+        splits = attn_splits(batch, kv_heads, ctx)
     ws = torch.zeros(int(lib.bt_attention_workspace_bytes(batch, kv_heads, heads, dim, splits)), dtype=torch.uint8,
                      device="cuda")
     s = torch.cuda.Stream()

@@ -266,6 +266,14 @@ class Qwen36Moe:
             layer = self.layers[i]
             layer["w_ba"] = torch.cat([layer["w_beta"], layer["w_alpha"]]).contiguous()
 
+    def check_pipeline(self) -> None:
+        """Raise if a bounded wait of the tensor-core projections gave up since
+        the last check (their outputs after such a timeout are invalid).
+        Synchronises the device."""
+        n = int(N.load().bt_linear_rows_timeouts())
+        if n != 0:
+            raise N.B200Error(N.BT_ERR_TIMEOUT, f"{n} bounded waits of bt_linear_rows gave up: outputs are invalid")
+
     def _splits(self) -> int:
         return max(1, min(16, self.cfg.max_context // 256))
 
@@ -414,7 +422,9 @@ class Qwen36Moe:
         self._n.zero_()
         for _ in range(steps):
             self._graph.replay()
-        return self._hist[:, :steps].clone()
+        out = self._hist[:, :steps].clone()
+        self.check_pipeline()
+        return out
 
     def forward_token(self, token: int, pos: int, *, logits: bool = True) -> torch.Tensor | None:
         """model/qwen36_moe.py:646-664 for sequence 0: (V,) f32 logits."""
@@ -444,6 +454,7 @@ class Qwen36Moe:
             out.append(nxt)
             if step + 1 < max_new:
                 logits = self.forward_token(nxt, len(ids) + step)
+        self.check_pipeline()
         return out
 
 

@@ -221,6 +221,19 @@ def make_moe_layer(spec: MoeSpec = MoeSpec(), seed: int = 3, n_experts: int | No
     return out
 
 
+def moe_layer_inputs(tokens: int, spec: MoeSpec = MoeSpec(), seed: int = 3) -> tuple[np.ndarray, np.ndarray]:
+    """The MoE-layer benchmark's per-step inputs for T tokens: activations
+    x (T, hidden) drawn N(0, 1) and rounded to bf16 (returned as f32), and
+    router logits (T, n_experts) drawn N(0, 1); one seeded stream per T."""
+    import torch  # noqa: PLC0415 - bf16 rounding only
+
+    rng = np.random.default_rng(np.random.SeedSequence(seed, spawn_key=(1000, tokens)))
+    x = rng.standard_normal((tokens, spec.hidden), dtype=np.float32)
+    x = torch.from_numpy(x).to(torch.bfloat16).float().numpy()
+    logits = rng.standard_normal((tokens, spec.n_experts), dtype=np.float32)
+    return x, logits
+
+
 # --------------------------------------------------------------------------
 # Qwen3.6-35B-A3B-shaped hybrid MoE decoder (qwen35moe GGUF)
 # --------------------------------------------------------------------------
@@ -313,12 +326,42 @@ def qwen36_tensors(spec: Qwen36Spec) -> list[tuple[str, tuple[int, ...], str]]:
     return t
 
 
-def write_qwen36_gguf(path: str | Path, spec: Qwen36Spec = QWEN36_TINY, seed: int = 4) -> Path:
-    """Write a seeded random qwen35moe GGUF: bf16 projections, IQ3_S experts
-    (N(0, 0.02) before quantisation), f32 router, gate vectors, norms and
-    SSM parameters (distributions as for the Qwen3.5 checkpoints)."""
+#: IQ3_S block scale d of the random-byte experts (fp16 2^-12, little-endian):
+#: with random scale nibbles, grid entries and signs the weights have the
+#: magnitude an N(0, 0.02) quantisation gives.
+IQ3S_RANDOM_D = (0x00, 0x0C)
+
+
+def iq3s_random_bytes(seed: int, tensor_id: int, rows: int, k: int, pool: cf.Executor) -> np.ndarray:
+    """Seeded uniform random IQ3_S blocks (rows, k/256 * 110) with the block
+    scale d fixed to IQ3S_RANDOM_D: every byte pattern is a valid IQ3_S block,
+    so this is a checkpoint of the format's full range without quantising."""
+    nb = rows * (k // 256)
+    out = np.empty((nb, 110), dtype=np.uint8)
+    per = max(1, CHUNK // 110)
+
+    def chunk(c: int) -> None:
+        rng = np.random.default_rng(np.random.SeedSequence(seed, spawn_key=(tensor_id, c)))
+        view = out[c * per : min(nb, (c + 1) * per)]
+        view[:] = rng.integers(0, 256, view.shape, dtype=np.uint8)
+        view[:, 0], view[:, 1] = IQ3S_RANDOM_D
+
+    list(pool.map(chunk, range((nb + per - 1) // per)))
+    return out.reshape(rows, -1)
+
+
+def write_qwen36_gguf(path: str | Path, spec: Qwen36Spec = QWEN36_TINY, seed: int = 4,
+                      experts: str = "quantized") -> Path:
+    """Write a seeded random qwen35moe GGUF: bf16 projections, IQ3_S experts,
+    f32 router, gate vectors, norms and SSM parameters (distributions as for
+    the Qwen3.5 checkpoints).  ``experts="quantized"`` quantises N(0, 0.02)
+    weights to IQ3_S; ``experts="random"`` writes seeded random IQ3_S blocks
+    (iq3s_random_bytes), minutes faster for the full 35B-A3B shape.  Tensors
+    are generated while the file is written, one at a time."""
     import torch  # noqa: PLC0415 - bf16 rounding
 
+    if experts not in ("quantized", "random"):
+        raise ValueError(f"experts must be 'quantized' or 'random', got {experts!r}")
     s = spec
     w = GGUFWriter()
     w.add("general.architecture", "qwen35moe")
@@ -336,38 +379,42 @@ def write_qwen36_gguf(path: str | Path, spec: Qwen36Spec = QWEN36_TINY, seed: in
         ("ssm.conv_kernel", s.conv_k), ("full_attention_interval", s.attn_interval), ("nextn_predict_layers", 0),
     ):
         w.add(a + key, val)
+    def tensor(tid: int, shape: tuple[int, ...], role: str, pool: cf.Executor) -> np.ndarray:
+        n = int(np.prod(shape))
+        if role == "bf16":
+            vals = _fill(seed, tid, n, "normal", pool) * np.float32(0.02)
+            return torch.from_numpy(vals).to(torch.bfloat16).view(torch.int16).numpy().view(np.uint16)
+        if role == "iq3s":
+            k = shape[-1]
+            rows = n // k
+            if experts == "random":
+                return iq3s_random_bytes(seed, tid, rows, k, pool)
+            vals = (_fill(seed, tid, n, "normal", pool) * np.float32(0.02)).reshape(rows, k)
+            step = max(1, CHUNK // k)
+            parts = list(pool.map(lambda r, v=vals: quantize_iq3_s(v[r : r + step]), range(0, rows, step)))
+            return np.concatenate(parts, axis=0)
+        if role == "gamma":
+            vals = np.float32(1.0) + _fill(seed, tid, n, "normal", pool) * np.float32(0.02)
+        elif role == "f32w":
+            vals = _fill(seed, tid, n, "normal", pool) * np.float32(0.02)
+        elif role == "conv":
+            vals = _fill(seed, tid, n, "normal", pool) * np.float32(0.25)
+        elif role == "ssm_a":
+            vals = -np.exp(_fill(seed, tid, n, "uniform", pool) * np.float32(np.log(16.0)))
+        elif role == "dt_bias":
+            u = _fill(seed, tid, n, "uniform", pool)
+            dt = np.exp(np.log(1e-3) + u * (np.log(1e-1) - np.log(1e-3)))
+            vals = np.log(np.expm1(dt))
+        else:
+            raise AssertionError(role)
+        return np.asarray(vals, dtype=np.float32)
+
+    kinds = {"bf16": GGML_BF16, "iq3s": GGML_IQ3_S}
     with cf.ThreadPoolExecutor(_threads()) as pool:
         for tid, (name, shape, role) in enumerate(qwen36_tensors(s)):
-            n = int(np.prod(shape))
-            if role == "bf16":
-                vals = _fill(seed, tid, n, "normal", pool) * np.float32(0.02)
-                bf = torch.from_numpy(vals).to(torch.bfloat16).view(torch.int16).numpy().view(np.uint16)
-                w.add_tensor(name, shape, GGML_BF16, bf.reshape(shape))
-                continue
-            if role == "iq3s":
-                k = shape[-1]
-                rows = n // k
-                vals = (_fill(seed, tid, n, "normal", pool) * np.float32(0.02)).reshape(rows, k)
-                step = max(1, CHUNK // k)
-                parts = list(pool.map(lambda r, v=vals: quantize_iq3_s(v[r : r + step]), range(0, rows, step)))
-                w.add_tensor(name, shape, GGML_IQ3_S, np.concatenate(parts, axis=0))
-                continue
-            if role == "gamma":
-                vals = np.float32(1.0) + _fill(seed, tid, n, "normal", pool) * np.float32(0.02)
-            elif role == "f32w":
-                vals = _fill(seed, tid, n, "normal", pool) * np.float32(0.02)
-            elif role == "conv":
-                vals = _fill(seed, tid, n, "normal", pool) * np.float32(0.25)
-            elif role == "ssm_a":
-                vals = -np.exp(_fill(seed, tid, n, "uniform", pool) * np.float32(np.log(16.0)))
-            elif role == "dt_bias":
-                u = _fill(seed, tid, n, "uniform", pool)
-                dt = np.exp(np.log(1e-3) + u * (np.log(1e-1) - np.log(1e-3)))
-                vals = np.log(np.expm1(dt))
-            else:
-                raise AssertionError(role)
-            w.add_tensor(name, shape, GGML_F32, np.asarray(vals, dtype=np.float32).reshape(shape))
-    return w.write(path)
+            w.add_tensor(name, shape, kinds.get(role, GGML_F32),
+                         lambda tid=tid, shape=shape, role=role: tensor(tid, shape, role, pool))
+        return w.write(path)
 
 
 __all__ = [
@@ -383,6 +430,7 @@ __all__ = [
     "Qwen35Spec",
     "SPECS",
     "make_moe_layer",
+    "moe_layer_inputs",
     "qwen35_tensors",
     "write_qwen35_gguf",
 ]

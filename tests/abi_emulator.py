@@ -60,6 +60,8 @@ class Emulator:
             bt_argmax_workspace_bytes = staticmethod(lambda *a: 256)
             bt_iq3s_row_bytes = staticmethod(lambda k: int(real.bt_iq3s_row_bytes(k)))
             bt_q8_row_bytes = staticmethod(lambda k: int(real.bt_q8_row_bytes(k)))
+            # host emulation has no bounded device waits to give up
+            bt_linear_rows_timeouts = staticmethod(lambda: 0)
 
         return Lib()
 

@@ -136,7 +136,7 @@ def test_gdn_decode_matches_reference(be) -> None:
 @pytest.mark.parametrize("batch", [1, 8, 64])
 def test_gdn_decode_config2_256_steps(be, batch) -> None:
     """The GDN op benchmark: 16 heads x 128, bf16 q/k/v, 256 steps, seed 1, vs the oracle."""
-    steps = 256 if batch <= 8 else 32
+    steps = 256
     rng = np.random.default_rng(1)
     H, D = 16, 128
     state = torch.zeros(batch, H, D, D, device="cuda")
@@ -236,6 +236,30 @@ def test_attention_config3_bf16(be, batch, ctx, splits) -> None:
     groups = -(-splits // 16) if splits > 16 else 0
     part_bytes = (4 * batch * 2 * (splits + groups) * 4 * (256 + 2) + 255) // 256 * 256
     assert int(ws[part_bytes:].sum().item()) == 0  # split and group counters re-armed
+
+
+@pytest.mark.parametrize("batch", [1, 16, 64])
+@pytest.mark.parametrize("ctx", [1024, 8192, 32768])
+def test_attention_config3_benchmark_inputs(be, batch, ctx) -> None:
+    """The flash-decode benchmark exactly as measured (kernel_bench attn: its
+    device-drawn inputs, seed 2, and its split count), every (batch, context)
+    of the benchmark, up to four sequences per case (first, last, two drawn)
+    against the f32 oracle, on two calls in a row."""
+    from breezetoken_b200.kernel_bench import attn_inputs, attn_splits
+
+    q, kc, vc, lens = attn_inputs(batch, ctx)
+    splits = attn_splits(batch, 2, ctx)
+    out = torch.empty(batch, 8, 256, device="cuda")
+    ws = torch.zeros(int(N.load().bt_attention_workspace_bytes(batch, 2, 8, 256, splits)), dtype=torch.uint8,
+                     device="cuda")
+    picks = sorted({0, batch - 1, *np.random.default_rng(batch * 7 + ctx).integers(0, batch, 2).tolist()})
+    for _ in range(2):
+        N.call("bt_attention_decode", q.data_ptr(), kc.data_ptr(), vc.data_ptr(), N.BT_BF16, lens.data_ptr(),
+               out.data_ptr(), batch, 8, 2, 256, ctx, 1.0 / 16, splits, ws.data_ptr(), 0)
+        for b in picks:
+            ref = ops.attention(q[b].cpu().numpy(), kc[b].float().cpu().numpy(), vc[b].float().cpu().numpy(),
+                                1.0 / 16)
+            np.testing.assert_allclose(out[b].cpu().numpy(), ref, rtol=1e-4, atol=1e-5)
 
 
 def test_argmax_first_index(be) -> None:
