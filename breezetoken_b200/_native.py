@@ -118,6 +118,7 @@ _SIGS: dict[str, tuple[object, list]] = {
     "bt_conv_silu": (C.c_int, [_P, _P, _P, _P, _I64, _I64, _I64, _P]),
     "bt_linear_rows": (C.c_int, [_P, C.c_int, _P, _P, _I64, _I64, _I64, _P]),
     "bt_linear_rows_timeouts": (C.c_int, []),
+    "bt_launch_count": (C.c_longlong, []),
     "bt_rms_norm": (C.c_int, [_P, _P, _P, _I64, _I64, C.c_float, _P]),
     "bt_fused_add_rms_norm": (C.c_int, [_P, _P, _P, _P, _P, _I64, _I64, C.c_float, _P]),
     "bt_silu_mul": (C.c_int, [_P, _P, _P, _I64, _P]),

@@ -633,13 +633,13 @@ int launch_t(const AttnParams& p, cudaStream_t stream, bool pdl) {
         configured_device = dev;
       }
       cfg.dynamicSmemBytes = stage_bytes;
-      e = cudaLaunchKernelEx(&cfg, kern, p);
+      e = ::bt::launch_ex(&cfg, kern, p);
     } else {
-      e = cudaLaunchKernelEx(&cfg, attn_decode_kernel<float, DPL, GS, false, true>, p);
+      e = ::bt::launch_ex(&cfg, attn_decode_kernel<float, DPL, GS, false, true>, p);
     }
   } else {
-    e = cl ? cudaLaunchKernelEx(&cfg, attn_decode_kernel<KV, DPL, GS, (GS == 4), false>, p)
-           : cudaLaunchKernelEx(&cfg, attn_decode_kernel<KV, DPL, GS, false, false>, p);
+    e = cl ? ::bt::launch_ex(&cfg, attn_decode_kernel<KV, DPL, GS, (GS == 4), false>, p)
+           : ::bt::launch_ex(&cfg, attn_decode_kernel<KV, DPL, GS, false, false>, p);
   }
   if (e != cudaSuccess) return fail_cuda(e, "attention launch");
   return BT_OK;

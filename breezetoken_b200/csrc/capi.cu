@@ -166,6 +166,8 @@ int bt_linear_rows(const void* w, int w_dtype, const void* x_planes, float* y, i
 
 int bt_linear_rows_timeouts(void) { return bt::linear_rows_timeouts(); }
 
+long long bt_launch_count(void) { return bt::g_launch_count.load(std::memory_order_relaxed); }
+
 int bt_rms_norm(const float* x, const float* w, float* y, int64_t rows, int64_t n, float eps, void* stream) {
   return bt::rms_norm(x, nullptr, w, nullptr, y, rows, n, eps, as_stream(stream));
 }

@@ -126,9 +126,9 @@ __global__ void __launch_bounds__(kThreads) gdn_decode_kernel(const __grid_const
 template <typename T>
 cudaError_t launch_dim(const GdnParams& p, cudaLaunchConfig_t& cfg) {
   switch (p.dim) {
-    case 64: return cudaLaunchKernelEx(&cfg, gdn_decode_kernel<T, 4>, p);
-    case 128: return cudaLaunchKernelEx(&cfg, gdn_decode_kernel<T, 8>, p);
-    default: return cudaLaunchKernelEx(&cfg, gdn_decode_kernel<T, 16>, p);
+    case 64: return ::bt::launch_ex(&cfg, gdn_decode_kernel<T, 4>, p);
+    case 128: return ::bt::launch_ex(&cfg, gdn_decode_kernel<T, 8>, p);
+    default: return ::bt::launch_ex(&cfg, gdn_decode_kernel<T, 16>, p);
   }
 }
 

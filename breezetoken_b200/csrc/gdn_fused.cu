@@ -378,7 +378,7 @@ int launch_fused(const GdnFusedParams& P, cudaStream_t stream, bool pdl) {
   }
   cfg.attrs = attr;
   cfg.numAttrs = n;
-  const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, P);
+  const cudaError_t e = ::bt::launch_ex(&cfg, kern, P);
   if (e != cudaSuccess) return fail_cuda(e, "gdn_fused launch");
   return BT_OK;
 }

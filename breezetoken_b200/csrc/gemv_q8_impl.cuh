@@ -583,7 +583,7 @@ int launch_impl(const GemvQ8Params& p, const GemvQ8Launch& L, cudaStream_t strea
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 1 : 0;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, p);
+  cudaError_t e = ::bt::launch_ex(&cfg, kern, p);
   if (e != cudaSuccess) return fail_cuda(e, "gemv_q8 launch");
   return BT_OK;
 }

@@ -621,11 +621,11 @@ template <bool F32W, int TW>
 cudaError_t launch_np(cudaLaunchConfig_t& cfg, int np, const void* w, const __nv_bfloat16* xp, float* y, int n, int k,
                       int t) {
   switch (np) {
-    case 1: return cudaLaunchKernelEx(&cfg, linear_rows_kernel<F32W, 1, TW>, w, xp, y, n, k, t);
-    case 2: return cudaLaunchKernelEx(&cfg, linear_rows_kernel<F32W, 2, TW>, w, xp, y, n, k, t);
-    case 4: return cudaLaunchKernelEx(&cfg, linear_rows_kernel<F32W, 4, TW>, w, xp, y, n, k, t);
+    case 1: return ::bt::launch_ex(&cfg, linear_rows_kernel<F32W, 1, TW>, w, xp, y, n, k, t);
+    case 2: return ::bt::launch_ex(&cfg, linear_rows_kernel<F32W, 2, TW>, w, xp, y, n, k, t);
+    case 4: return ::bt::launch_ex(&cfg, linear_rows_kernel<F32W, 4, TW>, w, xp, y, n, k, t);
     default:  // two tiles per warp stop at 4 passes (the reduction's shared memory)
-      return cudaLaunchKernelEx(&cfg, linear_rows_kernel<F32W, (TW == 2 ? 4 : 8), TW>, w, xp, y, n, k, t);
+      return ::bt::launch_ex(&cfg, linear_rows_kernel<F32W, (TW == 2 ? 4 : 8), TW>, w, xp, y, n, k, t);
   }
 }
 
@@ -651,7 +651,7 @@ int bf16_planes(const float* x, void* planes, int64_t t, int64_t k, cudaStream_t
   cudaLaunchAttribute attr[1];
   cudaLaunchConfig_t cfg =
       pdl_config(dim3(static_cast<unsigned>(std::min<int64_t>((chunks + kThreads - 1) / kThreads, 4096))), stream, attr);
-  const cudaError_t e = cudaLaunchKernelEx(&cfg, bf16_planes_kernel, x, static_cast<__nv_bfloat16*>(planes), t,
+  const cudaError_t e = ::bt::launch_ex(&cfg, bf16_planes_kernel, x, static_cast<__nv_bfloat16*>(planes), t,
                                            static_cast<int>(k));
   if (e != cudaSuccess) return fail_cuda(e, "bf16_planes launch");
   return BT_OK;
@@ -697,13 +697,13 @@ int linear_rows(const void* w, int w_dtype, const void* x_planes, float* y, int6
       e = cudaFuncSetAttribute(linear_rows_umma_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                umma_smem_bytes<64>());
       if (e == cudaSuccess)
-        e = cudaLaunchKernelEx(&cfg, linear_rows_umma_kernel<64>, tmw, tmx, wb, y, nn, kk, tt, splits);
+        e = ::bt::launch_ex(&cfg, linear_rows_umma_kernel<64>, tmw, tmx, wb, y, nn, kk, tt, splits);
     } else {
       cfg.dynamicSmemBytes = umma_smem_bytes<32>();
       e = cudaFuncSetAttribute(linear_rows_umma_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                umma_smem_bytes<32>());
       if (e == cudaSuccess)
-        e = cudaLaunchKernelEx(&cfg, linear_rows_umma_kernel<32>, tmw, tmx, wb, y, nn, kk, tt, splits);
+        e = ::bt::launch_ex(&cfg, linear_rows_umma_kernel<32>, tmw, tmx, wb, y, nn, kk, tt, splits);
     }
     if (e != cudaSuccess) return fail_cuda(e, "linear_rows (tcgen05) launch");
     return BT_OK;
@@ -736,12 +736,12 @@ int linear_rows(const void* w, int w_dtype, const void* x_planes, float* y, int6
       cfg.dynamicSmemBytes = tiled_smem_bytes<2>();
       e = cudaFuncSetAttribute(linear_rows_tiled_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                tiled_smem_bytes<2>());
-      if (e == cudaSuccess) e = cudaLaunchKernelEx(&cfg, linear_rows_tiled_kernel<2>, wb, xp, y, nn, kk, tt, splits);
+      if (e == cudaSuccess) e = ::bt::launch_ex(&cfg, linear_rows_tiled_kernel<2>, wb, xp, y, nn, kk, tt, splits);
     } else {
       cfg.dynamicSmemBytes = tiled_smem_bytes<1>();
       e = cudaFuncSetAttribute(linear_rows_tiled_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                tiled_smem_bytes<1>());
-      if (e == cudaSuccess) e = cudaLaunchKernelEx(&cfg, linear_rows_tiled_kernel<1>, wb, xp, y, nn, kk, tt, splits);
+      if (e == cudaSuccess) e = ::bt::launch_ex(&cfg, linear_rows_tiled_kernel<1>, wb, xp, y, nn, kk, tt, splits);
     }
     if (e != cudaSuccess) return fail_cuda(e, "linear_rows (tiled) launch");
     return BT_OK;

@@ -1201,7 +1201,7 @@ cudaError_t launch_pdl(Kern kern, dim3 grid, size_t smem, cudaStream_t stream, A
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, kern, args...);
+  return ::bt::launch_ex(&cfg, kern, args...);
 }
 
 template <int KBG, int KBD>
@@ -1270,6 +1270,7 @@ int repack_iq3_s(const void* src, void* dst, int64_t rows, int64_t k, cudaStream
   const int64_t chunks = rows / 16 * (k / 256);
   if (chunks == 0) return BT_OK;
   const int blocks = static_cast<int>(std::min<int64_t>((chunks * 32 + 255) / 256, 65535));
+  ::bt::note_launch();
   repack_iq3s_kernel<<<blocks, 256, 0, stream>>>(static_cast<const uint8_t*>(src), static_cast<uint8_t*>(dst), chunks,
                                                  static_cast<int>(k / 256));
   const cudaError_t e = cudaGetLastError();
@@ -1285,6 +1286,7 @@ int moe_route(const float* logits, int64_t t, int64_t n_experts, int top_k, int3
                 static_cast<long long>(n_experts), top_k);
   if (t == 0) return BT_OK;
   const int blocks = static_cast<int>((t + 7) / 8);
+  ::bt::note_launch();
   moe_route_kernel<<<blocks, 256, 0, stream>>>(logits, t, static_cast<int>(n_experts), top_k, ids, weights);
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return fail_cuda(e, "moe_route launch");

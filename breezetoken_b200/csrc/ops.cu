@@ -251,6 +251,7 @@ int repack_q8_0(const void* src, void* dst, int64_t rows, int64_t k, int64_t dst
     return fail(BT_ERR_INVALID, "repack_q8_0: dst must be 16-byte and src 2-byte aligned");
   if (rows == 0) return BT_OK;
   const int64_t row_bytes = bt_q8_row_bytes(k);
+  ::bt::note_launch();
   repack_q8_0_kernel<<<grid_for(rows * (k / 32), 256), 256, 0, stream>>>(
       static_cast<const uint8_t*>(src), static_cast<uint8_t*>(dst), rows, k, dst_row0, dst_row_step, row_bytes,
       row_bytes - k);
@@ -261,6 +262,7 @@ int dequant_q8_rows(const void* w, float* out, int64_t rows, int64_t k, cudaStre
   if (!w || !out || rows < 0 || k < 32 || k % 32) return fail(BT_ERR_INVALID, "dequant_q8_rows: bad arguments");
   if (rows == 0) return BT_OK;
   const int64_t row_bytes = bt_q8_row_bytes(k);
+  ::bt::note_launch();
   dequant_q8_rows_kernel<<<grid_for(rows * k, 256), 256, 0, stream>>>(static_cast<const uint8_t*>(w), out, rows, k,
                                                                      row_bytes, row_bytes - k);
   return check_launch("dequant_q8_rows");
@@ -271,6 +273,7 @@ int dequant_iq3_s(const void* raw, float* out, int64_t rows, int64_t cols, cudaS
   if (reinterpret_cast<uintptr_t>(out) & 15) return fail(BT_ERR_INVALID, "dequant_iq3_s: out must be 16-byte aligned");
   const int64_t n_blocks = rows * (cols / 256);
   if (n_blocks == 0) return BT_OK;
+  ::bt::note_launch();
   dequant_iq3_s_kernel<<<grid_for(n_blocks * 32, 256), 256, 0, stream>>>(static_cast<const uint8_t*>(raw), out,
                                                                         n_blocks);
   return check_launch("dequant_iq3_s");
@@ -280,12 +283,12 @@ int linear_kn(const void* w, int w_dtype, const float* x, float* y, int64_t k, i
   if (!w || !x || !y || k < 1 || n < 1) return fail(BT_ERR_INVALID, "linear_kn: bad arguments");
   const int threads = 128;
   const int blocks = static_cast<int>((n + 8 * threads - 1) / (8 * threads));
+  if (w_dtype != BT_BF16 && w_dtype != BT_F32) return fail(BT_ERR_UNSUPPORTED, "linear_kn: weight dtype %d", w_dtype);
+  ::bt::note_launch();
   if (w_dtype == BT_BF16)
     linear_kn_kernel<__nv_bfloat16><<<blocks, threads, 0, stream>>>(static_cast<const __nv_bfloat16*>(w), x, y, k, n);
-  else if (w_dtype == BT_F32)
-    linear_kn_kernel<float><<<blocks, threads, 0, stream>>>(static_cast<const float*>(w), x, y, k, n);
   else
-    return fail(BT_ERR_UNSUPPORTED, "linear_kn: weight dtype %d", w_dtype);
+    linear_kn_kernel<float><<<blocks, threads, 0, stream>>>(static_cast<const float*>(w), x, y, k, n);
   return check_launch("linear_kn");
 }
 
@@ -294,6 +297,7 @@ int rms_norm(const float* a, const float* b, const float* w, float* h, float* y,
   if (!a || !w || !y || rows < 0 || n < 1 || (b && !h)) return fail(BT_ERR_INVALID, "rms_norm: bad arguments");
   if (rows == 0) return BT_OK;
   if (rows > 2147483647LL) return fail(BT_ERR_UNSUPPORTED, "rms_norm: too many rows");
+  ::bt::note_launch();
   rms_norm_kernel<<<static_cast<unsigned>(rows), 256, 0, stream>>>(a, b, w, h, y, n, eps);
   return check_launch("rms_norm");
 }
@@ -301,6 +305,7 @@ int rms_norm(const float* a, const float* b, const float* w, float* h, float* y,
 int silu_mul(const float* g, const float* u, float* y, int64_t n, cudaStream_t stream) {
   if (!g || !u || !y || n < 0) return fail(BT_ERR_INVALID, "silu_mul: bad arguments");
   if (n == 0) return BT_OK;
+  ::bt::note_launch();
   silu_mul_kernel<<<grid_for(n, 256), 256, 0, stream>>>(g, u, y, n);
   return check_launch("silu_mul");
 }
@@ -310,6 +315,7 @@ int rope(const float* x, const float* cos_t, const float* sin_t, const int32_t* 
   if (!x || !cos_t || !sin_t || !pos || !y || rows < 0 || rope_dim < 0 || rope_dim > dim || rope_dim % 2 || cap < 1)
     return fail(BT_ERR_INVALID, "rope: bad arguments");
   if (rows == 0) return BT_OK;
+  ::bt::note_launch();
   rope_kernel<<<static_cast<unsigned>(rows), 128, 0, stream>>>(x, cos_t, sin_t, pos, y, dim, rope_dim, cap, nullptr);
   return check_launch("rope");
 }
@@ -318,6 +324,7 @@ int conv_silu(const float* entry, float* state, const float* w, float* out, int6
               int64_t taps, cudaStream_t stream) {
   if (!entry || !state || !w || !out || batch < 1 || channels < 1 || taps < 2 || taps > 8)
     return fail(BT_ERR_INVALID, "conv_silu: bad arguments (taps in [2, 8])");
+  ::bt::note_launch();
   conv_silu_kernel<<<grid_for(batch * channels, 256), 256, 0, stream>>>(entry, state, w, out, batch, channels,
                                                                           static_cast<int>(taps));
   return check_launch("conv_silu");
@@ -329,6 +336,7 @@ int argmax(const float* x, int64_t rows, int64_t n, int32_t* out, void* workspac
   auto* best = static_cast<unsigned long long*>(workspace);
   auto* counters = reinterpret_cast<uint32_t*>(best + rows);
   const int64_t blocks = std::min<int64_t>((n + 255) / 256, static_cast<int64_t>(sm_count()) * 4);
+  ::bt::note_launch();
   argmax_kernel<<<dim3(static_cast<unsigned>(blocks), static_cast<unsigned>(rows)), 256, 0, stream>>>(x, n, out, best,
                                                                                                      counters);
   return check_launch("argmax");

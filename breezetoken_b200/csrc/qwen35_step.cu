@@ -328,7 +328,7 @@ int qwen35_step(const BtQwen35Model& m, const BtQwen35Runtime& rt, int with_logi
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = kUsePdl ? 1 : 0;
-    cudaError_t e = cudaLaunchKernelEx(&cfg, advance_pos_kernel, rt.pos, static_cast<int>(d.batch));
+    cudaError_t e = ::bt::launch_ex(&cfg, advance_pos_kernel, rt.pos, static_cast<int>(d.batch));
     return e == cudaSuccess ? BT_OK : fail_cuda(e, "advance_pos");
   }
 

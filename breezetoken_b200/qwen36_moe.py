@@ -359,6 +359,9 @@ class Qwen36Moe:
     def _moe(self, i: int, xn: torch.Tensor) -> torch.Tensor:
         layer = self.layers[i]
         r = route_logits(self._lin(layer["router"], self._planes(xn)), self.cfg.top_k)
+        rec = getattr(self, "_route_record", None)
+        if rec is not None:  # measurement: each layer's input and routing of this (eager) step
+            rec.append((xn.clone(), r.expert_ids.clone(), r.weights.clone()))
         return moe_forward(layer["experts"], layer["shared"], xn, r.expert_ids, r.weights, self._moe_ws)
 
     # ------------------------------------------------------------------ step
@@ -390,6 +393,51 @@ class Qwen36Moe:
             raise ValueError("token id outside the vocabulary")
         return self._step_t(tokens, torch.full((1,), pos, dtype=torch.int32, device=self.device), logits)
 
+    # ------------------------------------------------------------ graphs
+    @torch.inference_mode()
+    def capture(self, history: int = 256) -> int:
+        """Capture one decode step of the B sequences as a CUDA graph (once):
+        it consumes the device token at the device position, writes the
+        argmax token back, records it in a history ring of `history` steps and
+        advances the position, with no host synchronisation.  Call an eager
+        step first so that every lazily configured kernel is set up.  Returns
+        the number of this library's kernels one replay launches."""
+        if getattr(self, "_graph", None) is not None and self._hist.shape[1] >= history:
+            return self.kernels_per_step
+        b = self.batch
+        self._tok = torch.zeros(b, dtype=torch.int64, device=self.device)
+        self._pos = torch.zeros(1, dtype=torch.int32, device=self.device)
+        self._n = torch.zeros(1, dtype=torch.int64, device=self.device)
+        self._hist = torch.zeros(b, max(history, 1), dtype=torch.int64, device=self.device)
+        self.backend._workspace(("argmax", b), int(N.load().bt_argmax_workspace_bytes(b)))
+        lib = N.load()
+        stream = torch.cuda.Stream(device=self.device)
+        stream.wait_stream(torch.cuda.current_stream())
+        self._graph = torch.cuda.CUDAGraph()
+        before = int(lib.bt_launch_count())
+        with torch.cuda.graph(self._graph, stream=stream):
+            nxt = self.backend.argmax(self._step_t(self._tok, self._pos, True)).long()
+            self._hist.index_copy_(1, self._n, nxt.unsqueeze(1))
+            self._tok.copy_(nxt)
+            self._pos.add_(1)
+            self._n.add_(1).remainder_(self._hist.shape[1])
+        self.kernels_per_step = int(lib.bt_launch_count()) - before
+        return self.kernels_per_step
+
+    def set_decode(self, tokens: torch.Tensor, pos: int) -> None:
+        """The next replay consumes `tokens` (B,) at position `pos` (copies on
+        the current stream; `tokens` may be pinned host memory)."""
+        if tokens.numel() != self.batch:
+            raise ValueError(f"expected {self.batch} tokens, got {tokens.numel()}")
+        self._tok.copy_(tokens.reshape(-1), non_blocking=True)
+        self._pos.fill_(pos)
+        self._n.zero_()
+
+    def replay(self, steps: int = 1) -> None:
+        """`steps` graph replays on the current stream (no host sync)."""
+        for _ in range(steps):
+            self._graph.replay()
+
     @torch.inference_mode()
     def graph_decode(self, tokens: torch.Tensor, pos: int, steps: int) -> torch.Tensor:
         """`steps` greedy steps of the B sequences, the first feeding `tokens`
@@ -397,34 +445,58 @@ class Qwen36Moe:
         position and the generated ids stay on the device; no host sync
         between steps).  Returns the generated ids (B, steps).  Call an eager
         step first so that every lazily configured kernel is set up."""
-        cfg, b = self.cfg, self.batch
-        if tokens.numel() != b:
-            raise ValueError(f"expected {b} tokens, got {tokens.numel()}")
+        cfg = self.cfg
+        if tokens.numel() != self.batch:
+            raise ValueError(f"expected {self.batch} tokens, got {tokens.numel()}")
         if not 0 <= pos or pos + steps > cfg.max_context:
             raise ValueError(f"positions {pos}..{pos + steps - 1} outside [0, {cfg.max_context})")
-        if getattr(self, "_graph", None) is None or self._hist.shape[1] < steps:
-            self._tok = torch.zeros(b, dtype=torch.int64, device=self.device)
-            self._pos = torch.zeros(1, dtype=torch.int32, device=self.device)
-            self._n = torch.zeros(1, dtype=torch.int64, device=self.device)
-            self._hist = torch.zeros(b, max(steps, 1), dtype=torch.int64, device=self.device)
-            self.backend._workspace(("argmax", b), int(N.load().bt_argmax_workspace_bytes(b)))
-            stream = torch.cuda.Stream(device=self.device)
-            stream.wait_stream(torch.cuda.current_stream())
-            self._graph = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(self._graph, stream=stream):
-                nxt = self.backend.argmax(self._step_t(self._tok, self._pos, True)).long()
-                self._hist.index_copy_(1, self._n, nxt.unsqueeze(1))
-                self._tok.copy_(nxt)
-                self._pos.add_(1)
-                self._n.add_(1)
-        self._tok.copy_(tokens.reshape(-1))
-        self._pos.fill_(pos)
-        self._n.zero_()
-        for _ in range(steps):
-            self._graph.replay()
+        self.capture(history=max(steps, 256))
+        self.set_decode(tokens, pos)
+        self.replay(steps)
         out = self._hist[:, :steps].clone()
         self.check_pipeline()
         return out
+
+    # ----------------------------------------------------------- prefill
+    @torch.inference_mode()
+    def prefill(self, prompts: torch.Tensor) -> None:
+        """Consume prompts (B, L) at positions 0 .. L-1 in lockstep (no logits):
+        the next step feeds each sequence's next token at position L."""
+        if prompts.dim() != 2 or prompts.shape[0] != self.batch:
+            raise ValueError(f"prompts must be ({self.batch}, L), got {tuple(prompts.shape)}")
+        if prompts.shape[1] > self.cfg.max_context:
+            raise ValueError("prompt longer than max_context")
+        toks = prompts.to(self.device)
+        for i in range(prompts.shape[1]):
+            self._step(toks[:, i], i, logits=False)
+
+    def snapshot(self) -> dict:
+        """Device copies of every per-sequence state (KV caches, conv windows,
+        recurrent states), for restore()."""
+        return {"kv": {i: (k.clone(), v.clone()) for i, (k, v) in self.kv.items()},
+                "conv": {i: t.clone() for i, t in self.conv_state.items()},
+                "rec": {i: t.clone() for i, t in self.rec_state.items()}}
+
+    def restore(self, snap: dict) -> None:
+        """Put back a snapshot (device copies on the current stream)."""
+        for i, (k, v) in snap["kv"].items():
+            self.kv[i][0].copy_(k)
+            self.kv[i][1].copy_(v)
+        for i, t in snap["conv"].items():
+            self.conv_state[i].copy_(t)
+        for i, t in snap["rec"].items():
+            self.rec_state[i].copy_(t)
+
+    @torch.inference_mode()
+    def record_routing(self, tokens: torch.Tensor, pos: int) -> list:
+        """One eager step (the state advances as usual) that records each
+        layer's MoE input and routing: [(xn (B, H), ids (B, k), weights (B, k))]."""
+        self._route_record = []
+        try:
+            self._step(tokens.reshape(-1).to(self.device), pos, True)
+            return self._route_record
+        finally:
+            self._route_record = None
 
     def forward_token(self, token: int, pos: int, *, logits: bool = True) -> torch.Tensor | None:
         """model/qwen36_moe.py:646-664 for sequence 0: (V,) f32 logits."""

@@ -108,6 +108,13 @@ BT_API int bt_linear_rows(const void* w, int w_dtype, const void* x_planes, floa
  * Synchronises the device and resets the count; -1 if it cannot be read.  */
 BT_API int bt_linear_rows_timeouts(void);
 
+/* Diagnostic without a reference counterpart: kernels this library has
+ * launched in this process, each launch recorded into a CUDA graph under
+ * stream capture counted once (replays launch it again and are not
+ * counted).  The difference across one captured step is that step's kernel
+ * count.                                                                  */
+BT_API long long bt_launch_count(void);
+
 /* Backend.rms_norm (backends.py:119-123) over rows of length n.           */
 BT_API int bt_rms_norm(const float* x, const float* w, float* y, int64_t rows,
                 int64_t n, float eps, void* stream);

@@ -272,6 +272,61 @@ def gen_qwen36_tiny(out: Path, steps: int = 24) -> None:
         )
 
 
+#: The config-5 full-shape parity case: two 7-token prompts (below the
+#: reference's 8-token batched-prefill threshold, so every token takes its
+#: per-token f32 path), 8 greedy steps each.
+QWEN36_FULL_PROMPTS, QWEN36_FULL_PROMPT_LEN, QWEN36_FULL_STEPS = 2, 7, 8
+
+
+def qwen36_full_prompts() -> np.ndarray:
+    from breezetoken_b200.synth import QWEN36_35B
+
+    return np.random.default_rng(5).integers(0, QWEN36_35B.vocab, (QWEN36_FULL_PROMPTS, QWEN36_FULL_PROMPT_LEN))
+
+
+def gen_qwen36_full(out: Path, gguf: Path | None = None) -> None:
+    """Greedy decode of the reference's Qwen36Moe (device="cpu", dtype="f32")
+    on the full Qwen3.6-35B-A3B-shaped checkpoint (40 layers, 256 IQ3_S
+    experts, vocab 151936; seed 4, random-byte experts: synth.write_qwen36_gguf
+    experts="random"), for the two prompts of qwen36_full_prompts()."""
+    from breezetoken.model.qwen36_moe import Qwen36Moe
+
+    from breezetoken_b200.synth import QWEN36_35B, write_qwen36_gguf
+
+    with tempfile.TemporaryDirectory() as d:
+        path = gguf or write_qwen36_gguf(Path(d) / "q36_full.gguf", QWEN36_35B, seed=4, experts="random")
+        m = Qwen36Moe(str(path), device="cpu", dtype="f32", max_context=64)
+        prompts = qwen36_full_prompts()
+        t0 = time.time()
+        tokens, margins, top_idx, top_val, first = [], [], [], [], None
+        with torch.inference_mode():
+            for b, prompt in enumerate(prompts.tolist()):
+                m.reset()
+                for i, tok in enumerate(prompt):
+                    logits = m.forward_token(tok, i, logits=(i == len(prompt) - 1))
+                if b == 0:
+                    first = logits.numpy().copy()
+                seq_t, seq_m, seq_i, seq_v = [], [], [], []
+                for step in range(QWEN36_FULL_STEPS):
+                    top = torch.topk(logits, 16)
+                    seq_m.append(float(top.values[0] - top.values[1]))
+                    seq_i.append(top.indices.numpy())
+                    seq_v.append(top.values.numpy())
+                    tok = int(logits.argmax())
+                    seq_t.append(tok)
+                    if step + 1 < QWEN36_FULL_STEPS:
+                        logits = m.forward_token(tok, len(prompt) + step, logits=True)
+                tokens.append(seq_t)
+                margins.append(seq_m)
+                top_idx.append(np.stack(seq_i))
+                top_val.append(np.stack(seq_v))
+        np.savez_compressed(
+            out, prompts=prompts, tokens=np.array(tokens), margins=np.array(margins, dtype=np.float32),
+            top_idx=np.stack(top_idx), top_val=np.stack(top_val), logits=first[None], max_context=np.array(64),
+            seconds=np.array(time.time() - t0), threads=np.array(torch.get_num_threads()),
+        )
+
+
 def gen_model(out: Path, spec, steps: int, max_context: int, keep_logits: int) -> None:
     from breezetoken.gguf import GGUFFile
     from breezetoken.model.qwen35 import Qwen35
@@ -311,6 +366,7 @@ def main() -> None:
     ap.add_argument("--reference", required=True)
     ap.add_argument("--skip-0_8b", action="store_true")
     ap.add_argument("--only", help="regenerate one fixture (e.g. moe_shared)")
+    ap.add_argument("--gguf", help="qwen36_full: an already written full-shape checkpoint (seed 4, random experts)")
     args = ap.parse_args()
     sys.path.insert(0, args.reference)
     if args.only == "moe_shared":
@@ -319,11 +375,15 @@ def main() -> None:
     if args.only == "qwen36_tiny":
         gen_qwen36_tiny(HERE / "qwen36_tiny.npz")
         return
+    if args.only == "qwen36_full":
+        gen_qwen36_full(HERE / "qwen36_full.npz", Path(args.gguf) if args.gguf else None)
+        return
     gen_dequant(HERE / "dequant.npz")
     gen_ops(HERE / "ops.npz")
     gen_moe(HERE / "moe.npz")
     gen_moe_shared(HERE / "moe_shared.npz")
     gen_qwen36_tiny(HERE / "qwen36_tiny.npz")
+    gen_qwen36_full(HERE / "qwen36_full.npz")
     gen_model(HERE / "qwen35_tiny.npz", QWEN35_TINY, steps=32, max_context=512, keep_logits=4)
     if not args.skip_0_8b:
         gen_model(HERE / "qwen35_0_8b.npz", QWEN35_0_8B, steps=128, max_context=1024, keep_logits=1)
