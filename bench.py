@@ -1,21 +1,29 @@
-"""Benchmark: Qwen3.5-0.8B-shaped batch-1 greedy decode on B200 (tok/s).
+"""Benchmark: batched greedy decode of the Qwen3.6-35B-A3B-shaped decoder on B200s (tok/s).
 
-Workload (the batch-1 0.8B decode benchmark): seeded random Qwen3.5-0.8B-shaped Q8_0 GGUF
-(24 layers [GDN,GDN,GDN,GQA]x6, hidden 1024, FFN 3584, vocab 151936), a
-16-token uniform-random prompt, then 128 greedy decode steps.  One bench
-"step" is one decode step (one token per sequence).  The timed region runs
-K steps as repeated 128-step decodes from the post-prefill state (a device
-snapshot is restored every 128 tokens, ~0.05% of the time), replaying
-natively captured CUDA graphs with no host synchronisation.  The weights
-(694 MB) are larger than L2 (126 MB), so every step streams them from HBM.
+Workload (the north star's scaled decode): a Qwen3.6-35B-A3B-shaped model --
+40 layers [GDN, GDN, GDN, GQA] x 10, hidden 2048, GQA 16q/2kv x 256, GDN
+16 key / 32 value heads of 128, 256 IQ3_S experts (top-8, ffn 512) plus a
+bf16 shared expert per layer, bf16 projections, vocab 151936 -- decoding 64
+independent sequences, each a 512-token uniform random prompt followed by 256
+greedy steps.  Weights are seeded random-init built on the device (seed 4).
+One bench "step" is one decode step of every sequence.  The timed region
+replays a natively captured CUDA graph of one step K times with no host
+synchronisation (after the first 256 steps the post-prefill state is put back
+by device copies).  The weights (17.4 GB) are far larger than L2 (126 MB), so
+every step streams them from HBM.
 
-Multi-GPU (torchrun): one process per GPU, each decoding its own
-independent sequence (prompt seeded by rank) on a full replica of the
-weights -- sequence sharding with no collective; ``value`` is the tokens of
-all ranks divided by the slowest rank's time.
+Multi-GPU (torchrun): the 64 sequences are sharded 64/N per GPU, one process
+per GPU, each with a full replica of the weights and its own graph; there is
+no data-path collective (NCCL carries only the barriers and the max of the
+ranks' times).  ``value`` is the tokens of all ranks over the slowest rank's
+time.  At N = 1 the line also carries ``config1``: the batch-1 Qwen3.5-0.8B
+Q8_0 decode (16-token prompt + 128 steps) with its own roofline and CPU
+baseline.
 
-``--impl reference`` times the reference's CPU algorithm (the oracle port of
-its torch f32 path) on the host cores instead.
+``--impl reference`` times the reference's own CPU implementation of the same
+decode (its ``Qwen36Moe(device="cpu", dtype="f32")`` from baseline/_ref, see
+baseline/install_reference.py) on the host cores, on a bounded sample of the
+workload (one sequence, a few decode steps).
 """
 
 from __future__ import annotations
@@ -38,9 +46,13 @@ import torch  # noqa: E402
 
 METRIC = "decode tok/s"
 UNIT = "tok/s"
-PROMPT_LEN = 16
-DECODE_STEPS = 128
-WORKLOAD = "qwen35-0.8b-q8_0 batch-1 greedy decode (16-token prompt + 128 steps), seed 0"
+C5_BATCH, C5_PROMPT, C5_DECODE = 64, 512, 256
+WORKLOAD = ("qwen36-35b-a3b-shaped batched greedy decode: 64 sequences (64/N per GPU), 512-token prompts + "
+            "256 greedy steps, 40 layers, 256 IQ3_S experts top-8 + bf16 shared expert, seed 4")
+C1_PROMPT, C1_DECODE = 16, 128
+C1_WORKLOAD = "qwen35-0.8b-q8_0 batch-1 greedy decode (16-token prompt + 128 steps), seed 0"
+REF = ROOT / "baseline" / "_ref"
+IQ3S_EXPERT_BYTES = 1_351_680  # gate + up + down of one expert (hidden 2048, ffn 512)
 
 
 def _peaks() -> dict:
@@ -51,21 +63,54 @@ def _peaks() -> dict:
     return {"hbm_gbs": 6650.0, "source": "fallback"}
 
 
-def _gguf_path(rank: int, world: int) -> Path:
-    from breezetoken_b200.synth import QWEN35_0_8B, write_qwen35_gguf
-
+def _bench_dir() -> Path:
     d = Path(os.environ.get("BT_BENCH_DIR", Path(tempfile.gettempdir()) / "bt_bench"))
     d.mkdir(parents=True, exist_ok=True)
-    path = d / "qwen35-0.8b-seed0.gguf"
-    done = d / "qwen35-0.8b-seed0.ok"
-    if rank == 0 and not done.exists():
+    return d
+
+
+def _c1_gguf() -> Path:
+    from breezetoken_b200.synth import QWEN35_0_8B, write_qwen35_gguf
+
+    d = _bench_dir()
+    path, done = d / "qwen35-0.8b-seed0.gguf", d / "qwen35-0.8b-seed0.ok"
+    if not done.exists():
         write_qwen35_gguf(path, QWEN35_0_8B, seed=0)
         done.write_text("ok")
-    if world > 1:
-        import torch.distributed as dist
-
-        dist.barrier()
     return path
+
+
+def _c5_gguf() -> Path:
+    """The full-shape checkpoint the CPU arm loads (seed 4, random-byte IQ3_S
+    experts; ~18 GB, written once per box)."""
+    from breezetoken_b200.synth import cached_qwen36_full
+
+    return cached_qwen36_full(_bench_dir())
+
+
+def _all_host_threads() -> int:
+    """Use every host core for a CPU arm, whatever the launcher set (torchrun
+    exports OMP_NUM_THREADS=1): numpy's BLAS pool and torch's."""
+    cores = os.cpu_count() or 1
+    try:
+        from threadpoolctl import threadpool_limits
+
+        threadpool_limits(limits=cores)
+    except ImportError:
+        pass
+    torch.set_num_threads(cores)
+    return cores
+
+
+def _reference():
+    """The installed reference package, or None (baseline/install_reference.py)."""
+    if not (REF / "breezetoken" / "model" / "qwen36_moe.py").is_file():
+        return None
+    if str(REF) not in sys.path:
+        sys.path.insert(0, str(REF))
+    import breezetoken
+
+    return breezetoken
 
 
 class ClockSampler:
@@ -127,72 +172,269 @@ class ClockSampler:
         return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons), "samples": len(sm)}
 
 
-def cpu_baseline(steps: int, warmup: int, path: Path) -> dict:
-    """The reference's torch-f32 CPU decode restated (oracle port), all host cores."""
-    from oracle.qwen35 import Qwen35Oracle
+# ----------------------------------------------------------------- CPU arms
+def c5_reference_cpu(steps: int, warmup: int) -> dict:
+    """The reference's own Qwen36Moe torch f32 CPU decode (model/qwen36_moe.py
+    forward_token) of one sequence on the full-shape checkpoint, all host
+    cores: a 1-token prompt, `warmup` untimed and `steps` timed decode steps
+    (context < 16: attention over the context is a negligible part of a CPU
+    step, the projections and the per-token expert dequantisation dominate)."""
+    if _reference() is None:
+        raise RuntimeError("reference not installed: python baseline/install_reference.py <breezetoken checkout>")
+    cores = _all_host_threads()
+    path = _c5_gguf()
+    from breezetoken.model.qwen36_moe import Qwen36Moe as RefQwen36Moe
 
-    cores = os.cpu_count() or 1
-    o = Qwen35Oracle(path, max_context=1024)
-    prompt = np.random.default_rng(0).integers(0, o.vocab, PROMPT_LEN).tolist()
-    o.reset()
-    for i, t in enumerate(prompt):
-        logits = o.forward_token(t, i, logits=(i == PROMPT_LEN - 1))
-    pos = PROMPT_LEN
-    tok = int(np.argmax(logits))
-    for _ in range(warmup):
-        logits = o.forward_token(tok, pos)
-        tok, pos = int(np.argmax(logits)), pos + 1
-    t0 = time.perf_counter()
-    for _ in range(steps):
-        logits = o.forward_token(tok, pos)
-        tok, pos = int(np.argmax(logits)), pos + 1
-    dt = time.perf_counter() - t0
+    m = RefQwen36Moe(str(path), device="cpu", dtype="f32", max_context=64)
+    with torch.inference_mode():
+        m.reset()
+        logits = m.forward_token(1, 0, logits=True)
+        pos = 1
+        for _ in range(warmup):
+            logits = m.forward_token(int(logits.argmax()), pos, logits=True)
+            pos += 1
+        t0 = time.perf_counter()
+        for _ in range(steps):
+            logits = m.forward_token(int(logits.argmax()), pos, logits=True)
+            pos += 1
+        dt = time.perf_counter() - t0
     return {
-        "value": steps / dt,
-        "unit": UNIT,
-        "cores": cores,
-        "kind": "port",
-        "sample": f"{steps} decode steps of the same workload after a {PROMPT_LEN}-token prefill "
-        f"(numpy f32 oracle of the reference torch path, {cores} host threads)",
+        "value": steps / dt, "unit": UNIT, "cores": cores, "kind": "reference",
+        "sample": f"{steps} timed decode steps (after {warmup} untimed) of one sequence of the same model shape, "
+        f"reference Qwen36Moe(device='cpu', dtype='f32') from baseline/_ref, {cores} host threads",
     }
 
 
-def _all_host_threads() -> int:
-    """Use every host core for the CPU arm, whatever the launcher set
-    (torchrun exports OMP_NUM_THREADS=1): numpy's BLAS and torch's pool."""
-    cores = os.cpu_count() or 1
-    try:
-        from threadpoolctl import threadpool_limits
+def c1_cpu_baseline(steps: int, warmup: int) -> dict:
+    """Config 1 on the host cores: the reference's own Qwen35 torch f32 CPU path
+    when installed (model/qwen35.py), else the numpy oracle port of it."""
+    cores = _all_host_threads()
+    path = _c1_gguf()
+    prompt = np.random.default_rng(0).integers(0, 151936, C1_PROMPT).tolist()
+    ref = _reference()
+    if ref is not None:
+        from breezetoken.gguf import GGUFFile
+        from breezetoken.model.qwen35 import Qwen35 as RefQwen35
 
-        threadpool_limits(limits=cores)
-    except ImportError:
-        pass
-    torch.set_num_threads(cores)
-    return cores
+        with GGUFFile(str(path)) as g:
+            m = RefQwen35(g, backend="torch", device="cpu", max_context=1024)
+        kind, what = "reference", "reference Qwen35(backend='torch', device='cpu') from baseline/_ref"
+
+        def fwd(tok: int, pos: int):
+            return m.forward_token(tok, pos, logits=True)
+
+        with torch.inference_mode():
+            m.reset()
+            logits = m._prefill_batch(prompt)
+        argmax = lambda lg: int(lg.argmax())  # noqa: E731
+    else:
+        from oracle.qwen35 import Qwen35Oracle
+
+        o = Qwen35Oracle(path, max_context=1024)
+        kind, what = "port", "numpy f32 oracle of the reference torch path"
+        o.reset()
+        for i, t in enumerate(prompt):
+            logits = o.forward_token(t, i, logits=(i == C1_PROMPT - 1))
+        fwd = o.forward_token
+        argmax = lambda lg: int(np.argmax(lg))  # noqa: E731
+    pos, tok = C1_PROMPT, argmax(logits)
+    with torch.inference_mode():
+        for _ in range(warmup):
+            tok, pos = argmax(fwd(tok, pos)), pos + 1
+        t0 = time.perf_counter()
+        for _ in range(steps):
+            tok, pos = argmax(fwd(tok, pos)), pos + 1
+        dt = time.perf_counter() - t0
+    return {"value": steps / dt, "unit": UNIT, "cores": cores, "kind": kind,
+            "sample": f"{steps} decode steps after a {C1_PROMPT}-token prefill ({what}, {cores} host threads)"}
 
 
 def run_reference(args) -> None:
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    _all_host_threads()
-    path = _gguf_path(0, 1)
-    steps, warm = min(args.steps, 256), max(args.warmup, 3)
-    cb = cpu_baseline(steps, warm, path)
+    steps, warm = min(args.steps, 3), min(args.warmup, 1)
+    try:
+        cb = c5_reference_cpu(steps, warm)
+    except RuntimeError as exc:
+        print(json.dumps({"impl": "reference", "unavailable": str(exc)}), flush=True)
+        return
     line = {
         "impl": "reference", "metric": METRIC, "value": cb["value"], "unit": UNIT, "n_gpus": args.gpus,
         "steps": steps, "warmup": warm, "ms_per_step": 1000.0 / cb["value"], "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded random-init GGUF)",
-        "config": {"workload": WORKLOAD, "batch_per_gpu": 1, "sample": cb["sample"]},
+        "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded random-init GGUF)",
+        "config": {"workload": WORKLOAD, "sample": cb["sample"]},
         "cpu_baseline": cb,
         "e2e": {"value": cb["value"], "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
 
 
+# ------------------------------------------------------------------ config 5
+def moe_layer_roofline(m, record, peak: float, launches: int = 10) -> dict:
+    """The step's dominant kernels -- one MoE layer call (bt_moe_layer_iq3s:
+    routing prep, routed IQ3_S gate/up and down, bf16 shared expert) -- timed
+    alone with CUDA events on the launching stream, on layer 0's input and
+    routing of a real decode step, L2 flushed (256 MB read) before each call."""
+    from breezetoken_b200.moe import moe_forward
+
+    xn, ids, w = record[0]
+    layer = m.layers[0]
+    t = xn.shape[0]
+    u = int(torch.unique(ids).numel())
+    flush = torch.ones(256 << 20, dtype=torch.uint8, device=xn.device)
+    s = torch.cuda.current_stream()
+    total = 0.0
+    for i in range(launches + 3):
+        flush.sum(dtype=torch.int32)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(s)
+        moe_forward(layer["experts"], layer["shared"], xn, ids, w, m._moe_ws)
+        e1.record(s)
+        e1.synchronize()
+        if i >= 3:
+            total += e0.elapsed_time(e1) / 1e3
+    sec = total / launches
+    nbytes = u * IQ3S_EXPERT_BYTES + 6_291_456 + t * 2048 * 8
+    traffic = None
+    tf = ROOT / "profiles" / "ncu_traffic.json"
+    if tf.is_file():
+        per_expert = json.loads(tf.read_text()).get("moe_layer_bytes_per_expert")
+        if per_expert:  # DRAM bytes of one call per distinct expert, from an ncu capture
+            traffic = per_expert * u + 6_291_456
+    return {"kernel": f"MoE layer (bt_moe_layer_iq3s, {t} tokens, {u} distinct experts, timed alone)",
+            "bound": "hbm", "achieved": nbytes / sec / 1e9, "peak": peak, "unit": "GB/s",
+            "frac": nbytes / sec / 1e9 / peak, "traffic": traffic, "bytes_per_launch": nbytes,
+            "us_per_launch": sec * 1e6}
+
+
+def c5_step_bytes(m, u_mean: float, context: float) -> float:
+    """Algorithmic bytes of one decode step on one GPU: the bf16 / f32
+    non-expert weights once (the embedding is a gather), the selected experts
+    of every layer, the GDN states read and written, the f32 KV read."""
+    cfg = m.cfg
+    dense = m.head.numel() * 2
+    for layer in m.layers:
+        for k, v in layer.items():
+            if isinstance(v, torch.Tensor) and k != "w_ba":
+                dense += v.numel() * v.element_size()
+        sh = layer["shared"]
+        dense += sum(x.numel() * x.element_size() for x in (sh.gate, sh.up, sh.down, sh.gate_inp))
+    b = m.batch
+    n_gdn = cfg.n_layers - len(cfg.attn_layers)
+    state = b * n_gdn * cfg.gdn_value_heads * cfg.gdn_k_dim * cfg.gdn_value_dim * 4 * 2
+    kv = b * context * len(cfg.attn_layers) * 2 * cfg.n_kv * cfg.head_dim * 4
+    return float(dense + cfg.n_layers * u_mean * IQ3S_EXPERT_BYTES + state + kv)
+
+
+def run_config5(args, world: int, rank: int, local: int, peaks: dict) -> dict | None:
+    import torch.distributed as dist
+
+    from breezetoken_b200.qwen36_moe import Qwen36Moe
+    from breezetoken_b200.shard import aggregate_rate, max_over_ranks, rank_prompts
+    from breezetoken_b200.synth import QWEN36_35B
+
+    if args.batch % world:
+        raise ValueError(f"{args.batch} sequences do not split over {world} GPUs")
+    S = args.batch // world
+    m = Qwen36Moe.random(QWEN36_35B, batch=S, max_context=C5_PROMPT + C5_DECODE + 1, seed=4)
+    prompts = torch.tensor(rank_prompts(rank, S, QWEN36_35B.vocab, C5_PROMPT), dtype=torch.int64)
+    t0 = time.perf_counter()
+    m.prefill(prompts[:, :-1])
+    torch.cuda.synchronize()
+    prefill_s = time.perf_counter() - t0
+    pos0 = C5_PROMPT - 1
+    last = prompts[:, -1].to(m.device)
+    snap = m.snapshot()
+    m._step(last, pos0, logits=True)  # first use of the head path outside capture
+    m.restore(snap)
+    kps = m.capture(history=C5_DECODE)
+    span = {"used": C5_DECODE}
+
+    def decode(n: int) -> None:
+        """n decode steps; every 256 steps the post-prefill state is put back."""
+        while n > 0:
+            if span["used"] == C5_DECODE:
+                m.restore(snap)
+                m.set_decode(last, pos0)
+                span["used"] = 0
+            k = min(n, C5_DECODE - span["used"])
+            m.replay(k)
+            span["used"] += k
+            n -= k
+
+    warm = max(args.warmup, 3)
+    decode(warm)
+    torch.cuda.synchronize()
+    m.check_pipeline()
+
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    s = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        e0.record(s)
+        decode(args.steps)
+        e1.record(s)
+        e1.synchronize()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    sec = e0.elapsed_time(e1) / 1e3
+    m.check_pipeline()
+
+    # end to end through the public API: pinned host tokens in, one graph
+    # step (Qwen36Moe.graph_decode), the step's tokens back to the host
+    e2e_steps = min(args.steps, 64)
+    tok_host = torch.empty(S, dtype=torch.int64, pin_memory=True)
+    m.restore(snap)
+    tok_host.copy_(prompts[:, -1])
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    pos = pos0
+    for _ in range(e2e_steps):
+        out = m.graph_decode(tok_host, pos, 1)
+        tok_host.copy_(out.reshape(-1))
+        pos += 1
+    e2e_sec = time.perf_counter() - t0
+
+    # routing of one real decode step: distinct experts per layer (U) and the
+    # MoE layer's inputs for its roofline
+    m.restore(snap)
+    record = m.record_routing(last, pos0)
+    u_layers = [int(torch.unique(ids).numel()) for _, ids, _ in record]
+    u_mean = float(np.mean(u_layers))
+    roof = moe_layer_roofline(m, record, peaks["hbm_gbs"]) if rank == 0 else None
+
+    sec, e2e_sec, prefill_s = max_over_ranks([sec, e2e_sec, prefill_s], m.device)
+    value = aggregate_rate(args.steps * S, world, sec)
+    mean_ctx = C5_PROMPT + C5_DECODE / 2.0
+    step_bytes = c5_step_bytes(m, u_mean, mean_ctx)
+    achieved = step_bytes * (args.steps / sec) / 1e9
+    m.close()
+    if rank != 0:
+        return None
+    return {
+        "value": value, "sec": sec, "warm": warm, "S": S, "kps": kps, "clocks": clk.summary(),
+        "prefill_s": prefill_s, "roofline": roof,
+        "step_roofline": {
+            "bound": "hbm", "bytes_per_step_per_gpu": step_bytes, "mean_context": mean_ctx,
+            "distinct_experts_per_layer": u_mean, "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+            "frac": achieved / peaks["hbm_gbs"], "peak_source": peaks["source"],
+            "per_gpu_tok_s": args.steps * S / sec,
+        },
+        "e2e": {"value": aggregate_rate(e2e_steps * S, world, e2e_sec), "unit": UNIT, "h2d_bytes_per_step": 8 * S,
+                "d2h_bytes_per_step": 8 * S, "steps": e2e_steps,
+                "note": "public API per step: pinned host tokens in, Qwen36Moe.graph_decode(tokens, pos, 1), "
+                        "tokens out, sync"},
+    }
+
+
+# ------------------------------------------------------------------ config 1
 def head_gemv_roofline(model, peak: float, launches: int = 20) -> dict:
     """Average duration of the head GEMV (151936 x 1024 q8 rows, the largest
-    single launch of the step) timed alone with CUDA events on its stream."""
+    single launch of the 0.8B step) timed alone with CUDA events on its stream."""
     from breezetoken_b200 import _native as N
 
     cfg = model.cfg
@@ -225,11 +467,90 @@ def head_gemv_roofline(model, peak: float, launches: int = 20) -> dict:
     }
 
 
+def run_config1(steps: int, warmup: int, peaks: dict, cpu: bool) -> dict:
+    """Config 1: Qwen3.5-0.8B-shaped batch-1 Q8_0 decode (16-token prompt, then
+    repeated 128-step decodes from the post-prefill state, restored by device
+    copies every 128 tokens), native CUDA graphs of 16 steps."""
+    from breezetoken_b200.model import Qwen35
+
+    model = Qwen35(_c1_gguf(), device="cuda", max_context=1024, batch=1)
+    s = model.stream
+    chunk = 16
+    model.prefill([np.random.default_rng(0).integers(0, 151936, C1_PROMPT).tolist()])
+    s.synchronize()
+    snap = model.snapshot()
+
+    def decode(n: int) -> None:
+        done = 0
+        with torch.cuda.stream(s):
+            while done < n:
+                model.restore(snap)
+                run = min(C1_DECODE, n - done)
+                for _ in range(run // chunk):
+                    model.replay(chunk)
+                for _ in range(run % chunk):
+                    model.replay(1)
+                done += run
+
+    model._graph(chunk)
+    model._graph(1)
+    with torch.cuda.stream(s):
+        model.restore(snap)
+        model.replay(chunk)
+        model.replay(1)
+    decode(max(warmup, 3))
+    s.synchronize()
+    model._check_status()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(s)
+    decode(steps)
+    e1.record(s)
+    e1.synchronize()
+    sec = e0.elapsed_time(e1) / 1e3
+    model._check_status()
+
+    e2e_steps = min(steps, 512)
+    tok_host = torch.zeros(1, dtype=torch.int32, pin_memory=True)
+    out_host = torch.zeros(1, dtype=torch.int32, pin_memory=True)
+    snap_tok = snap["token"].cpu()
+    s.synchronize()
+    t0 = time.perf_counter()
+    for done in range(e2e_steps):
+        with torch.cuda.stream(s):
+            if done % C1_DECODE == 0:
+                model.restore(snap)
+                tok_host.copy_(snap_tok)
+            model.token.copy_(tok_host, non_blocking=True)
+            model.replay(1)
+            out_host.copy_(model.token, non_blocking=True)
+        s.synchronize()
+        tok_host.copy_(out_host)
+    e2e_sec = time.perf_counter() - t0
+
+    mean_ctx = C1_PROMPT + (C1_DECODE + 1) / 2.0
+    step_bytes = model.step_bytes(mean_ctx)
+    achieved = step_bytes * (steps / sec) / 1e9
+    roof = head_gemv_roofline(model, peaks["hbm_gbs"])
+    kps = model.kernels_per_step()
+    model.close()
+    return {
+        "workload": C1_WORKLOAD, "metric": METRIC, "value": steps / sec, "unit": UNIT, "steps": steps,
+        "warmup": max(warmup, 3), "ms_per_step": 1000.0 * sec / steps, "dtype": "f32 activations, q8_0 weights",
+        "roofline": roof,
+        "step_roofline": {"bound": "hbm", "bytes_per_step": step_bytes, "mean_context": mean_ctx,
+                          "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                          "frac": achieved / peaks["hbm_gbs"], "peak_source": peaks["source"]},
+        "e2e": {"value": e2e_steps / e2e_sec, "unit": UNIT, "h2d_bytes_per_step": 4, "d2h_bytes_per_step": 4,
+                "note": "public API: host token in, graph step, host token out, sync"},
+        "gpu_launches": steps * kps,
+        "cpu_baseline": c1_cpu_baseline(8, 2) if cpu else None,
+        "graph": f"native CUDA graphs of {chunk} steps, PDL between kernels",
+    }
+
+
 def run_b200(args) -> None:
     import torch.distributed as dist
-
-    from breezetoken_b200.model import Qwen35
-    from breezetoken_b200.shard import aggregate_rate, max_over_ranks, rank_prompts
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -238,118 +559,40 @@ def run_b200(args) -> None:
     if world > 1:
         from datetime import timedelta
 
-        dist.init_process_group("nccl", timeout=timedelta(seconds=600), device_id=torch.device("cuda", local))
-    path = _gguf_path(rank, world)
-    B = args.batch
-    model = Qwen35(path, device=f"cuda:{local}", max_context=1024, batch=B)
-    prompts = rank_prompts(rank, B, model.cfg.vocab, PROMPT_LEN)
-    s = model.stream
-    chunk = 16
-    model.prefill(prompts)
-    s.synchronize()
-    snap = model.snapshot()
-
-    def decode(n: int) -> None:
-        """n decode steps as repeated 128-step runs from the post-prefill state."""
-        done = 0
-        with torch.cuda.stream(s):
-            while done < n:
-                model.restore(snap)
-                run = min(DECODE_STEPS, n - done)
-                for _ in range(run // chunk):
-                    model.replay(chunk)
-                for _ in range(run % chunk):
-                    model.replay(1)
-                done += run
-
-    # warm-up: capture (and upload) both graphs, launch each at least once,
-    # then W decode steps, so nothing is first used inside the timed region
-    model._graph(chunk)
-    model._graph(1)
-    with torch.cuda.stream(s):
-        model.restore(snap)
-        model.replay(chunk)
-        model.replay(1)
-    decode(max(args.warmup, 3))
-    s.synchronize()
-    model._check_status()
-
+        dist.init_process_group("nccl", timeout=timedelta(seconds=900), device_id=torch.device("cuda", local))
     peaks = _peaks()
-    if world > 1:
-        dist.barrier()
-    torch.cuda.synchronize()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(local) as clk:
-        e0.record(s)
-        decode(args.steps)
-        e1.record(s)
-        e1.synchronize()
-    torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
-    sec = e0.elapsed_time(e1) / 1e3
-    model._check_status()
-
-    # end to end through the public API: host token in, host token out, every step
-    e2e_steps = min(args.steps, 512)
-    tok_host = torch.zeros(B, dtype=torch.int32, pin_memory=True)
-    out_host = torch.zeros(B, dtype=torch.int32, pin_memory=True)
-    snap_tok = snap["token"].cpu()
-    s.synchronize()
-    t0 = time.perf_counter()
-    done = 0
-    while done < e2e_steps:
-        with torch.cuda.stream(s):
-            if done % DECODE_STEPS == 0:
-                model.restore(snap)
-                tok_host.copy_(snap_tok)
-            model.token.copy_(tok_host, non_blocking=True)
-            model.replay(1)
-            out_host.copy_(model.token, non_blocking=True)
-        s.synchronize()
-        tok_host.copy_(out_host)
-        done += 1
-    e2e_sec = time.perf_counter() - t0
-
-    sec, e2e_sec = max_over_ranks([sec, e2e_sec], model.device)
-    value = aggregate_rate(args.steps * B, world, sec)
-
-    # step roofline: algorithmic bytes per token vs measured per-GPU token time
-    mean_ctx = PROMPT_LEN + (DECODE_STEPS + 1) / 2.0
-    per_gpu_tok_s = args.steps * B / sec
-    step_bytes = model.step_bytes(mean_ctx)
-    weight_bytes_shared = model.weight_bytes  # read once per step for all B sequences
-    bytes_per_step = step_bytes + (B - 1) * (step_bytes - weight_bytes_shared)
-    achieved_step = bytes_per_step * (args.steps / sec) / 1e9
-
+    r = run_config5(args, world, rank, local, peaks)
     line = None
     if rank == 0:
-        cb = cpu_baseline(24, 2, path) if world == 1 and not args.no_cpu_baseline else None
-        roof = head_gemv_roofline(model, peaks["hbm_gbs"])
+        c1 = run_config1(1024, 64, peaks, not args.no_cpu_baseline) if world == 1 and not args.no_config1 else None
+        cb = None
+        if world == 1 and not args.no_cpu_baseline:
+            try:
+                cb = c5_reference_cpu(2, 1)
+            except RuntimeError as exc:
+                cb = {"unavailable": str(exc)}
         line = {
-            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
-            "warmup": max(args.warmup, 3), "ms_per_step": 1000.0 * sec / args.steps, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "f32 activations, q8_0 weights",
-            "data": "synthetic (seeded random-init GGUF, N(0,0.02) weights quantised to Q8_0)",
+            "metric": METRIC, "value": r["value"], "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": r["warm"], "ms_per_step": 1000.0 * r["sec"] / args.steps, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None,
+            "dtype": "f32 accumulation: bf16 projections, IQ3_S experts, f32 state",
+            "data": "synthetic (seeded random-init weights built on the device: bf16 N(0,0.02), IQ3_S experts "
+                    "random blocks with d=2^-12; uniform random prompts)",
             "config": {
-                "workload": WORKLOAD, "batch_per_gpu": B, "parallelism": f"sequence-sharded x{world} (replicated weights)",
-                "l2": "weights 694 MB > 126 MB L2 streamed every step (no flush needed)",
-                "graph": f"native CUDA graphs of {chunk} steps, PDL between kernels",
+                "workload": WORKLOAD, "batch_total": args.batch, "batch_per_gpu": r["S"],
+                "parallelism": f"sequence-sharded x{world} (replicated weights, no data-path collective)",
+                "l2": "weights 17.4 GB > 126 MB L2, streamed every step (no flush needed)",
+                "graph": "one native CUDA graph per decode step", "prefill_s": r["prefill_s"],
             },
-            "roofline": roof,
-            "step_roofline": {
-                "bound": "hbm", "bytes_per_step": bytes_per_step, "mean_context": mean_ctx,
-                "achieved": achieved_step, "peak": peaks["hbm_gbs"], "unit": "GB/s",
-                "frac": achieved_step / peaks["hbm_gbs"], "peak_source": peaks["source"],
-                "per_gpu_tok_s": per_gpu_tok_s,
-            },
+            "roofline": r["roofline"],
+            "step_roofline": r["step_roofline"],
             "cpu_baseline": cb,
-            "e2e": {"value": aggregate_rate(e2e_steps * B, world, e2e_sec), "unit": UNIT, "h2d_bytes_per_step": 4 * B,
-                    "d2h_bytes_per_step": 4 * B, "note": "public API: host token in, graph step, host token out, sync"},
-            "gpu_launches": args.steps * model.kernels_per_step(),
-            "clocks": clk.summary(),
+            "e2e": r["e2e"],
+            "gpu_launches": args.steps * r["kps"],
+            "kernels_per_step": r["kps"],
+            "clocks": r["clocks"],
+            "config1": c1,
         }
-    model.close()
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
@@ -358,13 +601,14 @@ def run_b200(args) -> None:
 
 
 def main() -> None:
-    ap = argparse.ArgumentParser(description=__doc__)
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=4096)
-    ap.add_argument("--warmup", type=int, default=256)
-    ap.add_argument("--batch", type=int, default=1, choices=(1, 2, 4, 8))
+    ap.add_argument("--steps", type=int, default=128)
+    ap.add_argument("--warmup", type=int, default=8)
+    ap.add_argument("--batch", type=int, default=C5_BATCH, help="sequences over all GPUs")
     ap.add_argument("--impl", default="b200", choices=("b200", "reference"))
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-config1", action="store_true")
     args = ap.parse_args()
     if args.impl == "reference":
         run_reference(args)

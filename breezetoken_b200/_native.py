@@ -128,6 +128,11 @@ _SIGS: dict[str, tuple[object, list]] = {
         C.c_int,
         [_P, _P, _P, C.c_int, _P, _P, _I64, _I64, _I64, _I64, _I64, C.c_float, C.c_int, _P, _P],
     ),
+    "bt_attention_layer": (
+        C.c_int,
+        [_P, _I64, _P, _P, _P, _P, _I64, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, C.c_float, C.c_float,
+         C.c_int, _P, _P, _P],
+    ),
     "bt_attention_decode_noalloc": (
         C.c_int,
         [_P, _P, _P, C.c_int, _P, _P, _I64, _I64, _I64, _I64, _I64, C.c_float, C.c_int, _P],
@@ -135,6 +140,9 @@ _SIGS: dict[str, tuple[object, list]] = {
     "bt_gdn_decode": (C.c_int, [_P, _P, _P, C.c_int, _P, _P, _P, _P, _I64, _I64, _I64, _I64, C.c_float, C.c_float, _P]),
     "bt_gdn_decode_strided": (C.c_int, [_P, _P, _P, C.c_int, _I64, _I64, _I64, _P, _I64, _P, _I64, _P, _P, _I64, _I64,
                                         _I64, _I64, _I64, C.c_float, C.c_float, _P]),
+    "bt_gdn_gated_step": (C.c_int, [_P, _I64, _P, _I64, _P, _P, _P, _P, _I64, _P, _P, _I64, _I64, _I64, _I64,
+                                    C.c_float, C.c_float, C.c_float, _P]),
+    "bt_add_rms_norm_planes": (C.c_int, [_P, _P, _P, _P, _P, _P, _I64, _I64, C.c_float, _P]),
     "bt_argmax_workspace_bytes": (_I64, [_I64]),
     "bt_iq3s_row_bytes": (_I64, [_I64]),
     "bt_repack_iq3_s": (C.c_int, [_P, _P, _I64, _I64, _P]),

@@ -6,6 +6,7 @@
 #include <vector>
 
 #include "attention.cuh"
+#include "qwen36_layer.cuh"
 #include "errors.h"
 #include "gdn.cuh"
 #include "gemv_q8.cuh"
@@ -225,6 +226,92 @@ int bt_attention_decode(const float* q, const void* k, const void* v, int kv_dty
     p.counters = reinterpret_cast<uint32_t*>(static_cast<uint8_t*>(workspace) + part_bytes);
   }
   return bt::attention_launch(p, as_stream(stream), false);
+}
+
+int bt_attention_layer(const float* proj, int64_t proj_bs, const float* q_norm, const float* k_norm,
+                       const float* rope_cos, const float* rope_sin, int64_t rope_dim, const int32_t* pos,
+                       float* k_cache, float* v_cache, float* out, int64_t batch, int64_t heads, int64_t kv_heads,
+                       int64_t dim, int64_t cap, float scale, float eps, int splits, void* workspace,
+                       int32_t* status, void* stream) {
+  if (!proj || !q_norm || !k_norm || !rope_cos || !rope_sin || !pos || !k_cache || !v_cache || !out)
+    return fail(BT_ERR_INVALID, "attention layer: null pointer");
+  if (splits > 1 && !workspace) return fail(BT_ERR_INVALID, "attention layer: splits > 1 needs a workspace");
+  if (batch < 1 || batch > 65535 || heads < 1 || heads > 65535 || kv_heads < 1 || kv_heads > 65535 || dim < 1 ||
+      dim > 1024 || cap < 1 || cap > (1LL << 30) || rope_dim < 2 || rope_dim > dim)
+    return fail(BT_ERR_INVALID, "attention layer: shape out of range");
+  const int64_t need = (2 * heads + 2 * kv_heads) * dim;
+  if (proj_bs < need) return fail(BT_ERR_INVALID, "attention layer: projection rows of %lld < %lld elements",
+                                  static_cast<long long>(proj_bs), static_cast<long long>(need));
+  bt::AttnParams p{};
+  p.q = proj;
+  p.q_bs = proj_bs;
+  p.q_hs = static_cast<int32_t>(2 * dim);
+  p.gate = proj + dim;
+  p.k_new = proj + 2 * heads * dim;
+  p.v_new = proj + (2 * heads + kv_heads) * dim;
+  p.k = k_cache;
+  p.v = v_cache;
+  p.kv_dtype = BT_F32;
+  p.kv_ts = static_cast<int32_t>(kv_heads * dim);
+  p.kv_bs = cap * kv_heads * dim;
+  p.out = out;
+  p.out_bs = heads * dim;
+  p.batch = static_cast<int32_t>(batch);
+  p.heads = static_cast<int32_t>(heads);
+  p.kv_heads = static_cast<int32_t>(kv_heads);
+  p.dim = static_cast<int32_t>(dim);
+  p.cap = static_cast<int32_t>(cap);
+  p.splits = splits;
+  p.cluster = (heads == 4 * kv_heads && splits <= 8) ? 1 : 0;
+  p.scale = scale;
+  p.model = 1;
+  p.pos = pos;
+  p.q_norm = q_norm;
+  p.k_norm = k_norm;
+  p.rope_cos = rope_cos;
+  p.rope_sin = rope_sin;
+  p.rope_dim = static_cast<int32_t>(rope_dim);
+  p.eps = eps;
+  p.status = status;
+  if (splits > 1) {
+    p.part = static_cast<float*>(workspace);
+    const int64_t part_bytes = (4 * bt::attn_part_floats(batch, kv_heads, heads, dim, splits) + 255) / 256 * 256;
+    p.counters = reinterpret_cast<uint32_t*>(static_cast<uint8_t*>(workspace) + part_bytes);
+  }
+  return bt::attention_launch(p, as_stream(stream), false);
+}
+
+int bt_gdn_gated_step(const float* mixed, int64_t mixed_bs, const float* ba, int64_t ba_bs, const float* a_log,
+                      const float* dt_bias, float* state, const float* z, int64_t z_bs, const float* norm_w,
+                      void* planes, int64_t batch, int64_t heads_k, int64_t heads_v, int64_t dim, float scale,
+                      float l2_eps, float norm_eps, void* stream) {
+  if (batch < 1 || batch > (1LL << 24) || heads_k < 1 || heads_k > 65535 || heads_v < 1 || heads_v > 65535)
+    return fail(BT_ERR_INVALID, "gdn gated step: shape out of range");
+  bt::GdnStepParams p{};
+  p.mixed = mixed;
+  p.mixed_bs = mixed_bs;
+  p.ba = ba;
+  p.ba_bs = ba_bs;
+  p.a_log = a_log;
+  p.dt_bias = dt_bias;
+  p.state = state;
+  p.z = z;
+  p.z_bs = z_bs;
+  p.norm_w = norm_w;
+  p.planes = planes;
+  p.batch = static_cast<int32_t>(batch);
+  p.heads_k = static_cast<int32_t>(heads_k);
+  p.heads_v = static_cast<int32_t>(heads_v);
+  p.dim = static_cast<int32_t>(dim);
+  p.scale = scale;
+  p.l2_eps = l2_eps;
+  p.norm_eps = norm_eps;
+  return bt::gdn_gated_step_launch(p, as_stream(stream));
+}
+
+int bt_add_rms_norm_planes(const float* a, const float* b, const float* w, float* h, float* y, void* planes,
+                           int64_t rows, int64_t n, float eps, void* stream) {
+  return bt::add_rms_norm_planes(a, b, w, h, y, planes, rows, n, eps, as_stream(stream));
 }
 
 int bt_gdn_decode(const void* q, const void* k, const void* v, int in_dtype, const float* g, const float* beta,

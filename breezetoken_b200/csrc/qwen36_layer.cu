@@ -1,0 +1,223 @@
+// Fused per-layer pieces of the Qwen3.6-MoE (qwen35moe) decode step.
+//
+// gdn_gated_step_kernel: the GDN mixer of model/qwen36_moe.py:459-483 from
+// the conv output on, for B sequences: the decay g = a * softplus(alpha +
+// dt_bias) from the alpha logits, the gated delta rule of
+// _torch_gdn_decode (backends.py:241-271) with the state updated in place,
+// then the output gate rms_norm(o, ssm_norm) * silu(z), written as the three
+// bf16 planes the out-projection (bt_linear_rows) reads.  One CTA of 256
+// threads per (sequence, value head): thread t owns column t % 128 of the
+// head's 128 x 128 state, rows [64 (t / 128), 64 (t / 128) + 64), held in
+// registers, so the state is read and written once per step in 512-byte
+// rows; the column sums S^T k and S^T q add the two row halves in shared
+// memory, and the gated norm's sum of squares is one block reduction.  It
+// replaces the separate decay arithmetic, recurrence, norm, SiLU, product and
+// plane-split launches of the unfused layer.
+//
+// add_rms_norm_planes_kernel: h = a + b; y = rms_norm(h) * w
+// (backends.py:229-238) and y's three bf16 planes (y = hi + mid + lo) in the
+// same pass, so the projections that read y need no separate split.
+#include "errors.h"
+#include "qwen36_layer.cuh"
+
+namespace bt {
+namespace {
+
+__device__ __forceinline__ uint32_t bf16_pair_rn(float lo, float hi) {
+  const uint32_t a = __bfloat16_as_ushort(__float2bfloat16_rn(lo));
+  const uint32_t b = __bfloat16_as_ushort(__float2bfloat16_rn(hi));
+  return a | (b << 16);
+}
+
+// v = hi + mid + lo with each remainder exact in f32 (bf16 keeps 8 bits).
+__device__ __forceinline__ void split3(float v, float& hi, float& mid, float& lo) {
+  hi = __bfloat162float(__float2bfloat16_rn(v));
+  const float r1 = v - hi;
+  mid = __bfloat162float(__float2bfloat16_rn(r1));
+  lo = r1 - mid;
+}
+
+template <int DIM>
+__device__ __forceinline__ float block_total(float v, float* scratch) {
+  v = warp_sum(v);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  __syncthreads();
+  if (lane == 0) scratch[warp] = v;
+  __syncthreads();
+  float t = 0.f;
+#pragma unroll
+  for (int i = 0; i < kGdnStepThreads / 32; ++i) t += scratch[i];
+  return t;
+}
+
+template <int DIM>
+__global__ void __launch_bounds__(kGdnStepThreads) gdn_gated_step_kernel(const __grid_constant__ GdnStepParams p) {
+  constexpr int HALF = kGdnStepThreads / DIM;  // row groups
+  constexpr int R = DIM / HALF;                 // rows per thread
+  static_assert(DIM * HALF == kGdnStepThreads, "one thread per (column, row group)");
+  __shared__ float sq[DIM], sk[DIM], red[HALF][DIM];
+  __shared__ float s_decay, s_bsig, scratch[kGdnStepThreads / 32];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int c = tid % DIM, half = tid / DIM, r0 = half * R;
+  const int hv = blockIdx.x % p.heads_v, b = blockIdx.x / p.heads_v;
+  const int hk = hv % p.heads_k;
+  float* S = p.state + (static_cast<int64_t>(b) * p.heads_v + hv) * DIM * DIM;
+
+  float s[R];
+#pragma unroll
+  for (int i = 0; i < R; ++i) s[i] = S[static_cast<int64_t>(r0 + i) * DIM + c];
+
+  const float* row = p.mixed + static_cast<int64_t>(b) * p.mixed_bs;
+  if (warp < 2) {  // L2-normalised q (x scale) and k of key head hk
+    const float* src = row + (warp == 0 ? 0 : static_cast<int64_t>(p.heads_k) * DIM) + static_cast<int64_t>(hk) * DIM;
+    float vals[DIM / 32];
+    float ss = 0.f;
+#pragma unroll
+    for (int i = 0; i < DIM / 32; ++i) {
+      vals[i] = src[lane + 32 * i];
+      ss = fmaf(vals[i], vals[i], ss);
+    }
+    ss = warp_sum(ss);
+    const float r = 1.0f / sqrtf(ss + p.l2_eps);
+    float* dst = warp == 0 ? sq : sk;
+#pragma unroll
+    for (int i = 0; i < DIM / 32; ++i)
+      dst[lane + 32 * i] = warp == 0 ? __fmul_rn(__fmul_rn(vals[i], r), p.scale) : __fmul_rn(vals[i], r);
+  } else if (tid == 64) {
+    // decay: a * softplus(alpha + dt_bias) (model/qwen36_moe.py:474-476)
+    const float* ba = p.ba + static_cast<int64_t>(b) * p.ba_bs;
+    const float g = __fmul_rn(p.a_log[hv], softplus_f(__fadd_rn(ba[p.heads_v + hv], p.dt_bias[hv])));
+    s_decay = expf(g);
+    s_bsig = sigmoid_f(ba[hv]);
+  }
+  __syncthreads();
+  const float decay = s_decay, bsig = s_bsig;
+  float rec = 0.f;
+#pragma unroll
+  for (int i = 0; i < R; ++i) {
+    s[i] = __fmul_rn(s[i], decay);
+    rec = fmaf(s[i], sk[r0 + i], rec);
+  }
+  red[half][c] = rec;
+  __syncthreads();
+  float recalled = 0.f;
+#pragma unroll
+  for (int h = 0; h < HALF; ++h) recalled += red[h][c];
+  const float vv = row[static_cast<int64_t>(2 * p.heads_k) * DIM + static_cast<int64_t>(hv) * DIM + c];
+  const float delta = __fmul_rn(vv - recalled, bsig);
+  float o = 0.f;
+#pragma unroll
+  for (int i = 0; i < R; ++i) {
+    s[i] = __fadd_rn(s[i], __fmul_rn(sk[r0 + i], delta));
+    S[static_cast<int64_t>(r0 + i) * DIM + c] = s[i];
+    o = fmaf(s[i], sq[r0 + i], o);
+  }
+  __syncthreads();  // every thread has read red[][] above
+  red[half][c] = o;
+  __syncthreads();
+  float out = 0.f;
+#pragma unroll
+  for (int h = 0; h < HALF; ++h) out += red[h][c];
+  // gated norm: rms_norm(o) * w * silu(z) over the head's DIM outputs
+  // (threads of row group 0 hold one output each; the others add zero)
+  const float total = block_total<DIM>(half == 0 ? out * out : 0.f, scratch);
+  if (half == 0) {
+    const float r = 1.0f / sqrtf(total / static_cast<float>(DIM) + p.norm_eps);
+    const float zz = p.z[static_cast<int64_t>(b) * p.z_bs + static_cast<int64_t>(hv) * DIM + c];
+    const float y = __fmul_rn(__fmul_rn(__fmul_rn(out, r), p.norm_w[c]), silu_f(zz));
+    float hi, mid, lo;
+    split3(y, hi, mid, lo);
+    const int64_t width = static_cast<int64_t>(p.heads_v) * DIM;
+    __nv_bfloat16* dst = static_cast<__nv_bfloat16*>(p.planes) + static_cast<int64_t>(b) * 3 * width +
+                         static_cast<int64_t>(hv) * DIM + c;
+    dst[0] = __float2bfloat16_rn(hi);
+    dst[width] = __float2bfloat16_rn(mid);
+    dst[2 * width] = __float2bfloat16_rn(lo);
+  }
+}
+
+// One block per row; n % 8 == 0.
+__global__ void __launch_bounds__(256) add_rms_norm_planes_kernel(const float* __restrict__ a,
+                                                                   const float* __restrict__ b,
+                                                                   const float* __restrict__ w, float* __restrict__ h,
+                                                                   float* __restrict__ y, __nv_bfloat16* planes,
+                                                                   int n, float eps) {
+  __shared__ float scratch[8];
+  const int64_t row = blockIdx.x;
+  const float* ar = a + row * n;
+  const float* br = b ? b + row * n : nullptr;
+  float ss = 0.f;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    float v = ar[i];
+    if (br) {
+      v = v + br[i];
+      if (h) h[row * n + i] = v;
+    }
+    ss = fmaf(v, v, ss);
+  }
+  ss = warp_sum(ss);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane == 0) scratch[warp] = ss;
+  __syncthreads();
+  float total = 0.f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) total += scratch[i];
+  const float r = 1.0f / sqrtf(total / static_cast<float>(n) + eps);
+  for (int i0 = 8 * threadIdx.x; i0 < n; i0 += 8 * blockDim.x) {
+    float v[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const float x = br ? ar[i0 + j] + br[i0 + j] : ar[i0 + j];
+      v[j] = __fmul_rn(__fmul_rn(x, r), w[i0 + j]);
+      y[row * n + i0 + j] = v[j];
+    }
+    uint32_t pk[3][4];
+#pragma unroll
+    for (int j = 0; j < 8; j += 2) {
+      float h0, m0, l0, h1, m1, l1;
+      split3(v[j], h0, m0, l0);
+      split3(v[j + 1], h1, m1, l1);
+      pk[0][j / 2] = bf16_pair_rn(h0, h1);
+      pk[1][j / 2] = bf16_pair_rn(m0, m1);
+      pk[2][j / 2] = bf16_pair_rn(l0, l1);
+    }
+#pragma unroll
+    for (int q = 0; q < 3; ++q)
+      *reinterpret_cast<uint4*>(planes + (row * 3 + q) * n + i0) = make_uint4(pk[q][0], pk[q][1], pk[q][2], pk[q][3]);
+  }
+}
+
+}  // namespace
+
+int gdn_gated_step_launch(const GdnStepParams& p, cudaStream_t stream) {
+  if (!p.mixed || !p.ba || !p.a_log || !p.dt_bias || !p.state || !p.z || !p.norm_w || !p.planes)
+    return fail(BT_ERR_INVALID, "gdn gated step: null pointer");
+  if (p.batch < 1 || p.heads_k < 1 || p.heads_v < 1 || p.heads_v % p.heads_k)
+    return fail(BT_ERR_INVALID, "gdn gated step: value heads must be a positive multiple of key heads");
+  if (p.dim != 128) return fail(BT_ERR_UNSUPPORTED, "gdn gated step serves head dim 128, got %d", p.dim);
+  if (static_cast<int64_t>(p.batch) * p.heads_v > (1LL << 31) - 1)
+    return fail(BT_ERR_UNSUPPORTED, "gdn gated step: too many heads");
+  const int64_t mixed_need = static_cast<int64_t>(2 * p.heads_k + p.heads_v) * p.dim;
+  if (p.mixed_bs < mixed_need || p.ba_bs < 2 * p.heads_v || p.z_bs < static_cast<int64_t>(p.heads_v) * p.dim)
+    return fail(BT_ERR_INVALID, "gdn gated step: row strides shorter than the rows");
+  note_launch();
+  gdn_gated_step_kernel<128><<<static_cast<unsigned>(p.batch * p.heads_v), kGdnStepThreads, 0, stream>>>(p);
+  const cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? BT_OK : fail_cuda(e, "gdn gated step launch");
+}
+
+int add_rms_norm_planes(const float* a, const float* b, const float* w, float* h, float* y, void* planes,
+                        int64_t rows, int64_t n, float eps, cudaStream_t stream) {
+  if (!a || !w || !y || !planes || (b && !h) || rows < 0 || n < 8 || n % 8)
+    return fail(BT_ERR_INVALID, "add_rms_norm_planes: bad arguments (n %% 8 == 0)");
+  if ((reinterpret_cast<uintptr_t>(planes) & 15) || rows > 2147483647LL || n > 2147483647LL)
+    return fail(BT_ERR_INVALID, "add_rms_norm_planes: planes must be 16-byte aligned");
+  if (rows == 0) return BT_OK;
+  note_launch();
+  add_rms_norm_planes_kernel<<<static_cast<unsigned>(rows), 256, 0, stream>>>(
+      a, b, w, h, y, static_cast<__nv_bfloat16*>(planes), static_cast<int>(n), eps);
+  const cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? BT_OK : fail_cuda(e, "add_rms_norm_planes launch");
+}
+
+}  // namespace bt

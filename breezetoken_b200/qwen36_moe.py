@@ -2,11 +2,16 @@
 
 Mirrors breezetoken/model/qwen36_moe.py: the same config keys, weight names
 and orientation, and per-token math -- forward_token (:646-664), _attn
-(:432-457), _gdn (:459-483), _moe (:634-642).  The projections (bf16 / f32
-weight rows), RMSNorms, RoPE, attention, gated-delta step, routing, IQ3_S
-experts + shared expert and argmax run on this library's kernels; the
-elementwise glue between them (conv window, output gates, residual adds, KV
-writes) runs as torch device ops, as in the reference's model layer.
+(:432-457), _gdn (:459-483), _moe (:634-642).  Every operation of the step
+runs on this library's kernels, fused where one follows another: the
+residual add, RMSNorm and bf16 plane split of each activation
+(bt_add_rms_norm_planes); the projections (bf16 / f32 weight rows,
+bt_linear_rows); the attention layer after its one stacked [q | gate, k, v]
+projection (q/k norms, RoPE, KV writes, split-KV attention, sigmoid gate:
+bt_attention_layer); the GDN mixer after its projections and short conv
+(decay, gated delta rule, output norm and SiLU gate: bt_gdn_gated_step);
+routing, IQ3_S experts + shared expert and argmax.  Only the embedding row
+gather and the graph's token/position bookkeeping are torch device ops.
 
 B sequences decode in lockstep at one position (how the 35B-A3B benchmark's 64
 sequences per GPU run).  Prompts are fed token by token: the reference
@@ -264,7 +269,10 @@ class Qwen36Moe:
             b, cfg.hidden, cfg.expert_ffn, cfg.shared_ffn, cfg.n_experts, cfg.top_k)), dtype=torch.uint8, device=dev)
         for i in self.conv_state:  # beta and alpha rows stacked: one projection launch for both
             layer = self.layers[i]
-            layer["w_ba"] = torch.cat([layer["w_beta"], layer["w_alpha"]]).contiguous()
+            layer["w_ba"] = torch.cat([layer.pop("w_beta"), layer.pop("w_alpha")]).contiguous()
+        for i in self.kv:  # [q | gate per head, k, v] rows stacked: one projection, the attention layer's input
+            layer = self.layers[i]
+            layer["qkv_all"] = torch.cat([layer.pop("q"), layer.pop("k"), layer.pop("v")]).contiguous()
 
     def check_pipeline(self) -> None:
         """Raise if a bounded wait of the tensor-core projections gave up since
@@ -306,59 +314,57 @@ class Qwen36Moe:
         N.call("bt_linear_rows", w.data_ptr(), dt, xp.data_ptr(), y.data_ptr(), n, k, xp.shape[0], _stream())
         return y
 
-    def _rms(self, x: torch.Tensor, gamma: torch.Tensor) -> torch.Tensor:
-        return self.backend.rms_norm(x, gamma, self.cfg.eps)
+    def _norm_planes(self, a: torch.Tensor, b: torch.Tensor | None, gamma: torch.Tensor):
+        """h = a + b (a alone when b is None), y = rms_norm(h) * gamma and y's
+        bf16 planes, in one pass: (h, y, planes)."""
+        rows, n = a.shape
+        y = torch.empty(rows, n, dtype=torch.float32, device=self.device)
+        planes = torch.empty(rows, 3, n, dtype=torch.bfloat16, device=self.device)
+        h = torch.empty_like(y) if b is not None else a
+        N.call("bt_add_rms_norm_planes", a.data_ptr(), None if b is None else b.data_ptr(), gamma.data_ptr(),
+               None if b is None else h.data_ptr(), y.data_ptr(), planes.data_ptr(), rows, n,
+               float(self.cfg.eps), _stream())
+        return h, y, planes
 
-    def _rope(self, x: torch.Tensor, pos_t: torch.Tensor) -> torch.Tensor:
-        return self.backend.rope(x, self.rope_cos, self.rope_sin, pos_t, self.cfg.rope_dim)
-
-    def _attn(self, i: int, xn: torch.Tensor, pos_t: torch.Tensor) -> torch.Tensor:
+    def _attn(self, i: int, xp: torch.Tensor, pos_t: torch.Tensor) -> torch.Tensor:
+        """model/qwen36_moe.py:432-457: one projection of [q | gate, k, v], then
+        q/k norms, RoPE at the device positions, the KV writes, attention and
+        the sigmoid gate in one launch (bt_attention_layer)."""
         cfg, layer = self.cfg, self.layers[i]
-        b, H, D = xn.shape[0], cfg.n_heads, cfg.head_dim
-        xp = self._planes(xn)
-        q_full = self._lin(layer["q"], xp).view(b, H, 2 * D)
-        q, gate = q_full[..., :D].contiguous(), q_full[..., D:]
-        k = self._lin(layer["k"], xp).view(b, cfg.n_kv, D)
-        v = self._lin(layer["v"], xp).view(b, cfg.n_kv, D)
-        q = self._rope(self._rms(q, layer["q_norm"]), pos_t)
-        k = self._rope(self._rms(k, layer["k_norm"]), pos_t)
+        b, H, D = xp.shape[0], cfg.n_heads, cfg.head_dim
+        proj = self._lin(layer["qkv_all"], xp)
         k_cache, v_cache = self.kv[i]
-        idx = pos_t.long()  # the KV write and the attended length follow the device position
-        k_cache.index_copy_(1, idx, k.unsqueeze(1))
-        v_cache.index_copy_(1, idx, v.unsqueeze(1))
-        lens = (pos_t + 1).expand(b).contiguous()
         out = torch.empty(b, H, D, dtype=torch.float32, device=self.device)
-        N.call("bt_attention_decode", q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), N.BT_F32,
-               lens.data_ptr(), out.data_ptr(), b, H, cfg.n_kv, D, cfg.max_context, float(D ** -0.5),
-               self._splits(), self._attn_ws.data_ptr(), _stream())
-        out = out * torch.sigmoid(gate)
+        N.call("bt_attention_layer", proj.data_ptr(), proj.shape[1], layer["q_norm"].data_ptr(),
+               layer["k_norm"].data_ptr(), self.rope_cos.data_ptr(), self.rope_sin.data_ptr(), cfg.rope_dim,
+               pos_t.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), out.data_ptr(), b, H, cfg.n_kv, D,
+               cfg.max_context, float(D ** -0.5), float(cfg.eps), self._splits(), self._attn_ws.data_ptr(), None,
+               _stream())
         return self._lin(layer["o"], self._planes(out.reshape(b, -1)))
 
-    def _gdn(self, i: int, xn: torch.Tensor) -> torch.Tensor:
+    def _gdn(self, i: int, xp: torch.Tensor) -> torch.Tensor:
+        """model/qwen36_moe.py:459-483: the qkv projection and the short conv,
+        the [beta | alpha] and z projections, then the decay, gated delta
+        rule, output norm and SiLU gate in one launch (bt_gdn_gated_step)."""
         cfg, layer = self.cfg, self.layers[i]
-        b, hk, hv, dk = xn.shape[0], cfg.gdn_key_heads, cfg.gdn_value_heads, cfg.gdn_k_dim
+        b, hk, hv, dk = xp.shape[0], cfg.gdn_key_heads, cfg.gdn_value_heads, cfg.gdn_k_dim
         inner = cfg.gdn_inner
-        xp = self._planes(xn)
         entry = self._lin(layer["qkv"], xp)  # (B, C)
         mixed = torch.empty_like(entry)
         N.call("bt_conv_silu", entry.data_ptr(), self.conv_state[i].data_ptr(), layer["conv"].data_ptr(),
                mixed.data_ptr(), b, cfg.conv_dim, cfg.gdn_conv, _stream())
-        ba = self._lin(layer["w_ba"], xp)  # [beta | alpha] (each row as its own projection)
-        g = (layer["a_log"] * torch.nn.functional.softplus(ba[:, hv:] + layer["dt_bias"])).contiguous()
-        read = torch.empty(b, hv, cfg.gdn_value_dim, dtype=torch.float32, device=self.device)
-        # q | k | v are read in place from the conv output rows, beta from the projection rows
-        c = mixed.shape[1]
-        N.call("bt_gdn_decode_strided", mixed.data_ptr(), mixed[:, inner // 2 :].data_ptr(),
-               mixed[:, inner:].data_ptr(), N.BT_F32, c, c, c, g.data_ptr(), hv, ba.data_ptr(), 2 * hv,
-               self.rec_state[i].data_ptr(), read.data_ptr(), hv * dk, b, hk, hv, dk, float(dk ** -0.5),
-               float(cfg.l2_eps), _stream())
-        z = self._lin(layer["z"], xp).view(b, hv, dk)
-        gated = (self._rms(read, layer["ssm_norm"]) * torch.nn.functional.silu(z)).reshape(b, -1)
-        return self._lin(layer["out"], self._planes(gated))
+        ba = self._lin(layer["w_ba"], xp)  # [beta | alpha]
+        z = self._lin(layer["z"], xp)
+        gated = torch.empty(b, 3, inner, dtype=torch.bfloat16, device=self.device)
+        N.call("bt_gdn_gated_step", mixed.data_ptr(), mixed.shape[1], ba.data_ptr(), 2 * hv,
+               layer["a_log"].data_ptr(), layer["dt_bias"].data_ptr(), self.rec_state[i].data_ptr(), z.data_ptr(),
+               inner, layer["ssm_norm"].data_ptr(), gated.data_ptr(), b, hk, hv, dk, float(dk ** -0.5),
+               float(cfg.l2_eps), float(cfg.eps), _stream())
+        return self._lin(layer["out"], gated)
 
-    def _moe(self, i: int, xn: torch.Tensor) -> torch.Tensor:
+    def _moe(self, i: int, xn: torch.Tensor, xp: torch.Tensor) -> torch.Tensor:
         layer = self.layers[i]
-        r = route_logits(self._lin(layer["router"], self._planes(xn)), self.cfg.top_k)
+        r = route_logits(self._lin(layer["router"], xp), self.cfg.top_k)
         rec = getattr(self, "_route_record", None)
         if rec is not None:  # measurement: each layer's input and routing of this (eager) step
             rec.append((xn.clone(), r.expert_ids.clone(), r.weights.clone()))
@@ -366,23 +372,23 @@ class Qwen36Moe:
 
     # ------------------------------------------------------------------ step
     def _step_t(self, tokens: torch.Tensor, pos_t: torch.Tensor, logits: bool) -> torch.Tensor | None:
-        """One step with the position as a device tensor (int32 (1,)): no
+        """One step with the positions as a device tensor (int32 (B,)): no
         host synchronisation, so it can be captured in a CUDA graph."""
         cfg = self.cfg
         h = self.embd[tokens.long()].float()
         attn = set(cfg.attn_layers)
-        xn = self._rms(h, self.layers[0]["norm_in"])
+        _, xn, xp = self._norm_planes(h, None, self.layers[0]["norm_in"])
         for i in range(cfg.n_layers):
             # each residual add runs fused with the norm that follows it
             # (h = h + delta, then rms_norm(h): the same f32 operations)
             layer = self.layers[i]
-            delta = self._attn(i, xn, pos_t) if i in attn else self._gdn(i, xn)
-            h, xn = self.backend.fused_add_rms_norm(h, delta, layer["norm_post"], cfg.eps)
+            delta = self._attn(i, xp, pos_t) if i in attn else self._gdn(i, xp)
+            h, xn, xp = self._norm_planes(h, delta, layer["norm_post"])
             nxt = self.layers[i + 1]["norm_in"] if i + 1 < cfg.n_layers else self.norm_f
-            h, xn = self.backend.fused_add_rms_norm(h, self._moe(i, xn), nxt, cfg.eps)
+            h, xn, xp = self._norm_planes(h, self._moe(i, xn, xp), nxt)
         if not logits:
             return None
-        return self._lin(self.head, self._planes(xn))
+        return self._lin(self.head, xp)
 
     @torch.inference_mode()
     def _step(self, tokens: torch.Tensor, pos: int, logits: bool) -> torch.Tensor | None:
@@ -391,7 +397,7 @@ class Qwen36Moe:
             raise ValueError(f"position {pos} outside [0, {cfg.max_context})")
         if int(tokens.min()) < 0 or int(tokens.max()) >= cfg.vocab:
             raise ValueError("token id outside the vocabulary")
-        return self._step_t(tokens, torch.full((1,), pos, dtype=torch.int32, device=self.device), logits)
+        return self._step_t(tokens, torch.full((self.batch,), pos, dtype=torch.int32, device=self.device), logits)
 
     # ------------------------------------------------------------ graphs
     @torch.inference_mode()
@@ -406,7 +412,7 @@ class Qwen36Moe:
             return self.kernels_per_step
         b = self.batch
         self._tok = torch.zeros(b, dtype=torch.int64, device=self.device)
-        self._pos = torch.zeros(1, dtype=torch.int32, device=self.device)
+        self._pos = torch.zeros(b, dtype=torch.int32, device=self.device)
         self._n = torch.zeros(1, dtype=torch.int64, device=self.device)
         self._hist = torch.zeros(b, max(history, 1), dtype=torch.int64, device=self.device)
         self.backend._workspace(("argmax", b), int(N.load().bt_argmax_workspace_bytes(b)))

@@ -417,7 +417,24 @@ def write_qwen36_gguf(path: str | Path, spec: Qwen36Spec = QWEN36_TINY, seed: in
         return w.write(path)
 
 
+def cached_qwen36_full(directory: str | Path | None = None) -> Path:
+    """The full Qwen3.6-35B-A3B-shaped checkpoint (seed 4, random-byte
+    experts, ~18 GB), written once into `directory` (default: $BT_BENCH_DIR,
+    else <tmp>/bt_bench) and reused by later calls on the same machine."""
+    import os
+    import tempfile
+
+    d = Path(directory or os.environ.get("BT_BENCH_DIR", Path(tempfile.gettempdir()) / "bt_bench"))
+    d.mkdir(parents=True, exist_ok=True)
+    path, done = d / "qwen36-35b-seed4.gguf", d / "qwen36-35b-seed4.ok"
+    if not done.exists():
+        write_qwen36_gguf(path, QWEN36_35B, seed=4, experts="random")
+        done.write_text("ok")
+    return path
+
+
 __all__ = [
+    "cached_qwen36_full",
     "GGML_IQ3_S",
     "QWEN36_35B",
     "QWEN36_TINY",

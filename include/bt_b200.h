@@ -152,6 +152,27 @@ BT_API int bt_attention_decode(const float* q, const void* k, const void* v,
                         int64_t dim, int64_t cap, float scale, int splits,
                         void* workspace, void* stream);
 
+/* The attention layer after its in-projection, for `batch` sequences each at
+ * its own position: Qwen36Moe._attn (model/qwen36_moe.py:432-457) and the
+ * Qwen3.5 layer (model/layers.py:55-82) from the projection output on.
+ *   proj: row b (stride proj_bs elements) = [q_h | gate_h for each head h
+ *         (2*dim each)] [k (kv_heads*dim)] [v (kv_heads*dim)], f32
+ * Per head RMSNorm of q and k (q_norm, k_norm: (dim,), eps), partial
+ * rotate-half RoPE of the first rope_dim dims at pos[b] (rope_cos/sin:
+ * (cap, rope_dim) f32, the cos|cos and sin|sin halves), k and v written to
+ * the f32 caches (batch, cap, kv_heads, dim) at pos[b], attention over
+ * positions [0, pos[b]] (value head h uses KV head h / (heads/kv_heads)),
+ * out = attention * sigmoid(gate): (batch, heads, dim) f32.  workspace:
+ * bt_attention_workspace_bytes(batch, kv_heads, heads, dim, splits), zeroed
+ * once.  status: NULL or BT_STATUS_WORDS device int32 zeroed by the caller;
+ * a position outside [0, cap) is recorded there ([0] = BT_ERR_INVALID).   */
+BT_API int bt_attention_layer(const float* proj, int64_t proj_bs, const float* q_norm,
+                              const float* k_norm, const float* rope_cos, const float* rope_sin,
+                              int64_t rope_dim, const int32_t* pos, float* k_cache, float* v_cache,
+                              float* out, int64_t batch, int64_t heads, int64_t kv_heads,
+                              int64_t dim, int64_t cap, float scale, float eps, int splits,
+                              void* workspace, int32_t* status, void* stream);
+
 /* bt_attention_decode without a caller workspace, for callers that cannot
  * allocate device memory at call time (a pre-sized arena or memory pool that
  * owns every allocation, or a binding that only holds the buffers it was
@@ -197,6 +218,31 @@ BT_API int bt_gdn_decode_strided(const void* q, const void* k, const void* v, in
                           float* out, int64_t out_bs, int64_t batch, int64_t heads_k,
                           int64_t heads_v, int64_t dim, float scale, float eps,
                           void* stream);
+
+/* The GDN mixer of Qwen36Moe._gdn (model/qwen36_moe.py:459-483) from the
+ * conv output on, for `batch` sequences, with dim == 128:
+ *   mixed: row b (stride mixed_bs) = q (heads_k*dim) | k (heads_k*dim) |
+ *          v (heads_v*dim), the SiLU conv output
+ *   ba:    row b (stride ba_bs) = beta logits (heads_v) | alpha logits (heads_v)
+ *   g = a_log * softplus(alpha + dt_bias); the gated delta rule of
+ *   bt_gdn_decode on L2-normalised q (times scale) and k, state (batch,
+ *   heads_v, dim, dim) f32 updated in place; then per value head
+ *   y = rms_norm(o, norm_w, norm_eps) * silu(z) with z row b (stride z_bs),
+ *   written as three bf16 planes (batch, 3, heads_v*dim), the input form of
+ *   bt_linear_rows for the out-projection.                                 */
+BT_API int bt_gdn_gated_step(const float* mixed, int64_t mixed_bs, const float* ba, int64_t ba_bs,
+                             const float* a_log, const float* dt_bias, float* state, const float* z,
+                             int64_t z_bs, const float* norm_w, void* planes, int64_t batch,
+                             int64_t heads_k, int64_t heads_v, int64_t dim, float scale, float l2_eps,
+                             float norm_eps, void* stream);
+
+/* bt_fused_add_rms_norm that also writes y's three bf16 planes (rows, 3, n)
+ * (the form of bt_bf16_planes) in the same pass: h = a + b (b may be NULL:
+ * then y = rms_norm(a) and h is not written), y = rms_norm(h, w, eps).
+ * n % 8 == 0; planes 16-byte aligned.                                     */
+BT_API int bt_add_rms_norm_planes(const float* a, const float* b, const float* w, float* h,
+                                  float* y, void* planes, int64_t rows, int64_t n, float eps,
+                                  void* stream);
 
 /* The GDN short conv (model/qwen36_moe.py:465-468) for `batch` sequences:
  * window = [state (taps-1 per channel) | entry], out = silu(sum_j window[j] *

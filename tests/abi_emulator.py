@@ -79,6 +79,64 @@ class Emulator:
         out = _view(planes, np.uint16, t * 3 * k).reshape(t, 3, k)
         out[:, 0], out[:, 1], out[:, 2] = hi, mid, lo
 
+    def _planes_of(self, v: np.ndarray, planes: int) -> None:
+        t, k = v.shape
+        hi = _bf16_rn(v)
+        r1 = v - _bf16_to_f32(hi)
+        mid = _bf16_rn(r1)
+        lo = _bf16_rn(r1 - _bf16_to_f32(mid))
+        out = _view(planes, np.uint16, t * 3 * k).reshape(t, 3, k)
+        out[:, 0], out[:, 1], out[:, 2] = hi, mid, lo
+
+    def bt_add_rms_norm_planes(self, a, b, w, h, y, planes, rows, n, eps, stream) -> None:
+        av, wv = _view(a, F32, rows * n).reshape(rows, n), _view(w, F32, n)
+        if b:
+            hv, yv = ops.fused_add_rms_norm(av, _view(b, F32, rows * n).reshape(rows, n), wv, eps)
+            _view(h, F32, rows * n)[:] = hv.reshape(-1)
+        else:
+            yv = ops.rms_norm(av, wv, eps)
+        _view(y, F32, rows * n)[:] = yv.reshape(-1)
+        self._planes_of(yv.astype(F32), planes)
+
+    def bt_attention_layer(self, proj, proj_bs, q_norm, k_norm, cos, sin, rope_dim, pos, k_cache, v_cache, out,
+                           batch, heads, kv_heads, dim, cap, scale, eps, splits, ws, status, stream) -> None:
+        qn, kn = _view(q_norm, F32, dim), _view(k_norm, F32, dim)
+        cv = _view(cos, F32, cap * rope_dim).reshape(cap, rope_dim)
+        sv = _view(sin, F32, cap * rope_dim).reshape(cap, rope_dim)
+        kc = _view(k_cache, F32, batch * cap * kv_heads * dim).reshape(batch, cap, kv_heads, dim)
+        vc = _view(v_cache, F32, batch * cap * kv_heads * dim).reshape(batch, cap, kv_heads, dim)
+        o = _view(out, F32, batch * heads * dim).reshape(batch, heads, dim)
+        pv = _view(pos, np.int32, batch)
+        for b in range(batch):
+            row = _view(proj + 4 * b * proj_bs, F32, (2 * heads + 2 * kv_heads) * dim)
+            qg = row[: 2 * heads * dim].reshape(heads, 2 * dim)
+            q, gate = qg[:, :dim], qg[:, dim:]
+            k = row[2 * heads * dim : (2 * heads + kv_heads) * dim].reshape(kv_heads, dim)
+            v = row[(2 * heads + kv_heads) * dim :].reshape(kv_heads, dim)
+            p = int(pv[b])
+            assert 0 <= p < cap
+            q = ops.rope(ops.rms_norm(q, qn, eps), cv, sv, p, rope_dim)
+            k = ops.rope(ops.rms_norm(k, kn, eps), cv, sv, p, rope_dim)
+            kc[b, p], vc[b, p] = k, v
+            o[b] = ops.attention(q, kc[b, : p + 1], vc[b, : p + 1], scale) * ops.sigmoid(gate)
+
+    def bt_gdn_gated_step(self, mixed, mixed_bs, ba, ba_bs, a_log, dt_bias, state, z, z_bs, norm_w, planes, batch,
+                          heads_k, heads_v, dim, scale, l2_eps, norm_eps, stream) -> None:
+        sv = _view(state, F32, batch * heads_v * dim * dim).reshape(batch, heads_v, dim, dim)
+        al, dt, nw = _view(a_log, F32, heads_v), _view(dt_bias, F32, heads_v), _view(norm_w, F32, dim)
+        y = np.empty((batch, heads_v * dim), F32)
+        for b in range(batch):
+            row = _view(mixed + 4 * b * mixed_bs, F32, (2 * heads_k + heads_v) * dim)
+            q = row[: heads_k * dim].reshape(heads_k, dim)
+            k = row[heads_k * dim : 2 * heads_k * dim].reshape(heads_k, dim)
+            v = row[2 * heads_k * dim :].reshape(heads_v, dim)
+            bav = _view(ba + 4 * b * ba_bs, F32, 2 * heads_v)
+            g = al * ops.softplus(bav[heads_v:] + dt)
+            o = ops.gdn_decode(q, k, v, g, bav[:heads_v], sv[b], scale, l2_eps)
+            zv = _view(z + 4 * b * z_bs, F32, heads_v * dim).reshape(heads_v, dim)
+            y[b] = (ops.rms_norm(o, nw, norm_eps) * ops.silu(zv)).reshape(-1)
+        self._planes_of(y, planes)
+
     def bt_linear_rows(self, w, w_dtype, xp, y, n, k, t, stream) -> None:
         p = _bf16_to_f32(_view(xp, np.uint16, t * 3 * k).reshape(t, 3, k)).astype(np.float64).sum(1)
         wm = _bf16_to_f32(_view(w, np.uint16, n * k)) if w_dtype == N.BT_BF16 else _view(w, F32, n * k)

@@ -81,6 +81,54 @@ def test_qwen36_graph_decode_matches_reference(model) -> None:
     assert got[0].tolist() == g["tokens"].tolist()
 
 
+@pytest.fixture(scope="module")
+def full_gguf(cuda):
+    """The full Qwen3.6-35B-A3B-shaped checkpoint of the golden (40 layers,
+    256 IQ3_S experts, vocab 151936, seed 4, random-byte experts), ~18 GB,
+    written once per machine (the benchmark's CPU arm loads the same file)."""
+    from breezetoken_b200.synth import cached_qwen36_full
+
+    return cached_qwen36_full()
+
+
+def test_qwen36_full_shape_64_sequences_match_reference(full_gguf) -> None:
+    """The 35B-A3B decode benchmark's shape and batch: 64 sequences in
+    lockstep through the CUDA-graph decode (tcgen05 projections at 64 tokens,
+    the 256-expert MoE layers, 40 layers).  Sequences 0 and 1 carry the
+    golden prompts: their first logits are within 1e-4 of the logit scale of
+    the reference's Qwen36Moe (CPU, f32) and all 8 greedy tokens are
+    identical; the other 62 sequences are random prompts."""
+    from tests.golden.make_golden import qwen36_full_prompts
+
+    g = golden("qwen36_full")
+    prompts = g["prompts"]
+    assert (prompts == qwen36_full_prompts()).all()
+    B, L = 64, prompts.shape[1]
+    steps = g["tokens"].shape[1]
+    rng = np.random.default_rng(12)
+    allp = np.concatenate([prompts, rng.integers(0, 151936, (B - len(prompts), L))])
+    m = Qwen36Moe(full_gguf, max_context=int(g["max_context"]), batch=B)
+    try:
+        toks = torch.from_numpy(allp).cuda()
+        m.reset()
+        m.prefill(toks[:, : L - 1])
+        logits = m._step(toks[:, L - 1], L - 1, logits=True)
+        for b in range(len(prompts)):
+            got = logits[b].cpu().numpy()
+            want = g["top_val"][b, 0]
+            assert (np.argsort(-got, kind="stable")[:4] == g["top_idx"][b, 0, :4]).all()
+            assert np.abs(got[g["top_idx"][b, 0]] - want).max() <= 1e-4 * np.abs(want).max()
+        want0 = g["logits"][0]
+        assert np.abs(logits[0].cpu().numpy() - want0).max() <= 1e-4 * np.abs(want0).max()
+        first = m.backend.argmax(logits).long()
+        rest = m.graph_decode(first, L, steps - 1)
+        out = torch.cat([first[:, None], rest], 1).cpu().numpy()
+    finally:
+        m.close()
+    for b in range(len(prompts)):
+        assert out[b].tolist() == g["tokens"][b].tolist(), f"sequence {b} (margins {g['margins'][b]})"
+
+
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
 @pytest.mark.parametrize("t", [1, 5, 20, 70])
 def test_linear_rows_matches_f64(cuda, dtype, t) -> None:

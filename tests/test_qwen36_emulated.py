@@ -41,6 +41,6 @@ def test_qwen36_host_composition_reproduces_reference(emulated, qwen36_tiny_gguf
     toks = m.generate(prompt, steps)
     assert toks == g["tokens"][:steps].tolist(), f"margins {g['margins'][:steps]}"
     # every entry point the mirror's decode path uses was exercised
-    assert {"bt_linear_rows", "bt_gdn_decode_strided", "bt_fused_add_rms_norm", "bt_attention_decode",
-            "bt_moe_layer_iq3s", "bt_moe_route", "bt_conv_silu", "bt_rope", "bt_argmax"} <= emulated.names
+    assert {"bt_linear_rows", "bt_gdn_gated_step", "bt_add_rms_norm_planes", "bt_attention_layer",
+            "bt_moe_layer_iq3s", "bt_moe_route", "bt_conv_silu", "bt_bf16_planes", "bt_argmax"} <= emulated.names
     m.close()
