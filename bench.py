@@ -327,6 +327,7 @@ def c5_step_bytes(m, u_mean: float, context: float) -> float:
     return float(dense + cfg.n_layers * u_mean * IQ3S_EXPERT_BYTES + state + kv)
 
 
+@torch.inference_mode()
 def run_config5(args, world: int, rank: int, local: int, peaks: dict) -> dict | None:
     import torch.distributed as dist
 
@@ -467,6 +468,7 @@ def head_gemv_roofline(model, peak: float, launches: int = 20) -> dict:
     }
 
 
+@torch.inference_mode()
 def run_config1(steps: int, warmup: int, peaks: dict, cpu: bool) -> dict:
     """Config 1: Qwen3.5-0.8B-shaped batch-1 Q8_0 decode (16-token prompt, then
     repeated 128-step decodes from the post-prefill state, restored by device

@@ -430,6 +430,7 @@ class Qwen36Moe:
         self.kernels_per_step = int(lib.bt_launch_count()) - before
         return self.kernels_per_step
 
+    @torch.inference_mode()
     def set_decode(self, tokens: torch.Tensor, pos: int) -> None:
         """The next replay consumes `tokens` (B,) at position `pos` (copies on
         the current stream; `tokens` may be pinned host memory)."""
@@ -476,6 +477,7 @@ class Qwen36Moe:
         for i in range(prompts.shape[1]):
             self._step(toks[:, i], i, logits=False)
 
+    @torch.inference_mode()
     def snapshot(self) -> dict:
         """Device copies of every per-sequence state (KV caches, conv windows,
         recurrent states), for restore()."""
@@ -483,6 +485,7 @@ class Qwen36Moe:
                 "conv": {i: t.clone() for i, t in self.conv_state.items()},
                 "rec": {i: t.clone() for i, t in self.rec_state.items()}}
 
+    @torch.inference_mode()
     def restore(self, snap: dict) -> None:
         """Put back a snapshot (device copies on the current stream)."""
         for i, (k, v) in snap["kv"].items():
