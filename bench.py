@@ -308,38 +308,22 @@ def moe_layer_roofline(m, record, peak: float, launches: int = 10) -> dict:
             "us_per_launch": sec * 1e6}
 
 
-def c5_step_bytes(m, u_mean: float, context: float) -> float:
-    """Algorithmic bytes of one decode step on one GPU: the bf16 / f32
-    non-expert weights once (the embedding is a gather), the selected experts
-    of every layer, the GDN states read and written, the f32 KV read."""
-    cfg = m.cfg
-    dense = m.head.numel() * 2
-    for layer in m.layers:
-        for k, v in layer.items():
-            if isinstance(v, torch.Tensor) and k != "w_ba":
-                dense += v.numel() * v.element_size()
-        sh = layer["shared"]
-        dense += sum(x.numel() * x.element_size() for x in (sh.gate, sh.up, sh.down, sh.gate_inp))
-    b = m.batch
-    n_gdn = cfg.n_layers - len(cfg.attn_layers)
-    state = b * n_gdn * cfg.gdn_value_heads * cfg.gdn_k_dim * cfg.gdn_value_dim * 4 * 2
-    kv = b * context * len(cfg.attn_layers) * 2 * cfg.n_kv * cfg.head_dim * 4
-    return float(dense + cfg.n_layers * u_mean * IQ3S_EXPERT_BYTES + state + kv)
-
-
 @torch.inference_mode()
 def run_config5(args, world: int, rank: int, local: int, peaks: dict) -> dict | None:
     import torch.distributed as dist
 
-    from breezetoken_b200.qwen36_moe import Qwen36Moe
-    from breezetoken_b200.shard import aggregate_rate, max_over_ranks, rank_prompts
+    from breezetoken_b200.planner import plan, step_bytes
+    from breezetoken_b200.qwen36_moe import Qwen36Config, Qwen36Moe
+    from breezetoken_b200.shard import aggregate_rate, max_over_ranks
     from breezetoken_b200.synth import QWEN36_35B
 
-    if args.batch % world:
-        raise ValueError(f"{args.batch} sequences do not split over {world} GPUs")
-    S = args.batch // world
-    m = Qwen36Moe.random(QWEN36_35B, batch=S, max_context=C5_PROMPT + C5_DECODE + 1, seed=4)
-    prompts = torch.tensor(rank_prompts(rank, S, QWEN36_35B.vocab, C5_PROMPT), dtype=torch.int64)
+    cap = C5_PROMPT + C5_DECODE + 1
+    placement = plan(Qwen36Config.from_spec(QWEN36_35B, cap), max_context=cap, batch=args.batch, n_gpus=world)
+    seqs = placement.sequences(rank)  # global sequence ids of this GPU
+    S = len(seqs)
+    m = Qwen36Moe.random(QWEN36_35B, batch=S, max_context=cap, seed=4)
+    prompts = torch.tensor(np.stack([np.random.default_rng(g).integers(0, QWEN36_35B.vocab, C5_PROMPT) for g in seqs]),
+                           dtype=torch.int64)
     t0 = time.perf_counter()
     m.prefill(prompts[:, :-1])
     torch.cuda.synchronize()
@@ -411,16 +395,18 @@ def run_config5(args, world: int, rank: int, local: int, peaks: dict) -> dict | 
     sec, e2e_sec, prefill_s = max_over_ranks([sec, e2e_sec, prefill_s], m.device)
     value = aggregate_rate(args.steps * S, world, sec)
     mean_ctx = C5_PROMPT + C5_DECODE / 2.0
-    step_bytes = c5_step_bytes(m, u_mean, mean_ctx)
-    achieved = step_bytes * (args.steps / sec) / 1e9
+    nbytes = step_bytes(m.cfg, S, mean_ctx, u_mean)
+    achieved = nbytes * (args.steps / sec) / 1e9
     m.close()
     if rank != 0:
         return None
     return {
         "value": value, "sec": sec, "warm": warm, "S": S, "kps": kps, "clocks": clk.summary(),
+        "placement": {"summary": placement.summary(m.cfg.n_layers), "gpu_bytes": placement.gpu_bytes,
+                      "weight_bytes": placement.weight_bytes},
         "prefill_s": prefill_s, "roofline": roof,
         "step_roofline": {
-            "bound": "hbm", "bytes_per_step_per_gpu": step_bytes, "mean_context": mean_ctx,
+            "bound": "hbm", "bytes_per_step_per_gpu": nbytes, "mean_context": mean_ctx,
             "distinct_experts_per_layer": u_mean, "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
             "frac": achieved / peaks["hbm_gbs"], "peak_source": peaks["source"],
             "per_gpu_tok_s": args.steps * S / sec,
@@ -585,6 +571,7 @@ def run_b200(args) -> None:
                 "parallelism": f"sequence-sharded x{world} (replicated weights, no data-path collective)",
                 "l2": "weights 17.4 GB > 126 MB L2, streamed every step (no flush needed)",
                 "graph": "one native CUDA graph per decode step", "prefill_s": r["prefill_s"],
+                "placement": r["placement"],
             },
             "roofline": r["roofline"],
             "step_roofline": r["step_roofline"],

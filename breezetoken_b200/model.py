@@ -31,6 +31,7 @@ import torch
 from breezetoken_b200 import _native as N
 from breezetoken_b200.backends import Q8Weight, resolve_device
 from breezetoken_b200.gguf import GGML_F32, GGML_Q8_0, GGUFFile
+from breezetoken_b200.planner import Placement, plan
 
 _DEFAULT_CONTEXT = 8192
 
@@ -111,21 +112,6 @@ class Qwen35Config:
             raise ValueError("ssm group_count * state_size must equal ssm.inner_size")
 
 
-@dataclass(frozen=True)
-class Placement:
-    """planner.py:30-47: everything on one GPU (no CPU suffix on B200)."""
-
-    max_context: int
-    gpu_layers: int
-    head_on_gpu: bool
-    gpu_bytes: int
-    cpu_bytes: int
-    reason: str
-
-    def summary(self, n_layers: int) -> str:
-        return f"gpu_layers={self.gpu_layers}/{n_layers}, head=gpu, {self.reason}"
-
-
 def rope_tables(cfg: Qwen35Config, cap: int) -> tuple[torch.Tensor, torch.Tensor]:
     """model/layers.py:26-32, computed with the same torch f32 CPU ops."""
     half = cfg.rope_dim // 2
@@ -175,7 +161,7 @@ class Qwen35:
             if own:
                 g.close()
         cfg = self.cfg
-        self.placement = Placement(cfg.max_context, cfg.n_layers, True, self.weight_bytes, 0, "b200 all-GPU")
+        self.placement = plan(cfg, max_context=cfg.max_context, batch=batch, n_gpus=1)
         self._graphs: dict[int, int] = {}
         self._lock = threading.Lock()
 

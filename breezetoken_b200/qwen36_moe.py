@@ -72,6 +72,17 @@ class Qwen36Config:
         return self.gdn_inner // self.gdn_value_heads
 
     @classmethod
+    def from_spec(cls, spec, max_context: int) -> Qwen36Config:
+        """The configuration of a breezetoken_b200.synth.Qwen36Spec shape."""
+        return cls(
+            hidden=spec.hidden, n_layers=spec.n_layers, n_heads=spec.n_heads, n_kv=spec.n_kv,
+            head_dim=spec.head_dim, rope_dim=spec.rope_dim, rope_theta=spec.rope_theta, max_context=max_context,
+            n_experts=spec.n_experts, top_k=spec.top_k, expert_ffn=spec.expert_ffn, shared_ffn=spec.shared_ffn,
+            gdn_key_heads=spec.gdn_key_heads, gdn_value_heads=spec.gdn_value_heads, gdn_k_dim=spec.gdn_dim,
+            gdn_inner=spec.gdn_inner, gdn_conv=spec.conv_k, vocab=spec.vocab, eps=spec.eps,
+        )
+
+    @classmethod
     def from_gguf(cls, gguf: GGUFFile, max_context: int | None = None) -> Qwen36Config:
         md = gguf.metadata
         a = "qwen35moe."
@@ -198,13 +209,7 @@ class Qwen36Moe:
         import math
 
         self = cls.__new__(cls)
-        self.cfg = Qwen36Config(
-            hidden=spec.hidden, n_layers=spec.n_layers, n_heads=spec.n_heads, n_kv=spec.n_kv,
-            head_dim=spec.head_dim, rope_dim=spec.rope_dim, rope_theta=spec.rope_theta, max_context=max_context,
-            n_experts=spec.n_experts, top_k=spec.top_k, expert_ffn=spec.expert_ffn, shared_ffn=spec.shared_ffn,
-            gdn_key_heads=spec.gdn_key_heads, gdn_value_heads=spec.gdn_value_heads, gdn_k_dim=spec.gdn_dim,
-            gdn_inner=spec.gdn_inner, gdn_conv=spec.conv_k, vocab=spec.vocab, eps=spec.eps,
-        )
+        self.cfg = Qwen36Config.from_spec(spec, max_context)
         self.device, self.batch = resolve_device(device), int(batch)
         cfg, dev = self.cfg, self.device
         gen = torch.Generator(device=dev)
@@ -273,6 +278,14 @@ class Qwen36Moe:
         for i in self.kv:  # [q | gate per head, k, v] rows stacked: one projection, the attention layer's input
             layer = self.layers[i]
             layer["qkv_all"] = torch.cat([layer.pop("q"), layer.pop("k"), layer.pop("v")]).contiguous()
+
+    @property
+    def placement(self):
+        """planner.plan for this model on one GPU: context and device bytes
+        (raises RuntimeError if the weights and B sequences' state do not fit)."""
+        from breezetoken_b200.planner import plan
+
+        return plan(self.cfg, max_context=self.cfg.max_context, batch=self.batch, n_gpus=1)
 
     def check_pipeline(self) -> None:
         """Raise if a bounded wait of the tensor-core projections gave up since
