@@ -101,6 +101,11 @@ constexpr float kWeightSumMin = 6.103515625e-5f;  // moe.py:24
 // Workspace header words [kTicketBase, kTicketBase + hidden / rows per item):
 // the one-token combine's arrival counters (zero between calls).
 constexpr int kTicketBase = 16;
+// Header words 2 and 3: the next gate/up and down item of the pulled-item
+// kernels (T > 1), reset by the prep kernel of every call.
+constexpr int kWorkGateUp = 2, kWorkDown = 3;
+// Header word 4: the number of passes (T > 1).
+constexpr int kPassCount = 4;
 constexpr int kHeaderBytes = 512;
 // Item ranges of the expert kernels' CTAs (T > 1): gate/up at [0, 2G), down
 // at [kRangeDown, kRangeDown + 2G), G <= kMaxGrid.
@@ -249,6 +254,11 @@ struct MoeWs {
   int32_t* slot_start;
   int32_t* slot_count;
   int32_t* pairs;
+  // passes (T > 1): the slots' pair ranges cut into runs of kTokensPerPass,
+  // in slot order; header word kPassCount holds their number
+  int32_t* pass_expert;
+  int32_t* pass_start;
+  int32_t* pass_count;
   uint8_t* xenc;  // (T, 4 * hidden): hi plane, lo plane
   float* xscale;  // (T): x = (hi + lo) * xscale
   float* act;     // (P, ffn)
@@ -278,6 +288,12 @@ __host__ __device__ inline MoeWs moe_ws(void* base, int64_t t, int64_t p, int64_
   o += align256(4 * p);
   w.pairs = reinterpret_cast<int32_t*>(b + o);
   o += align256(4 * p);
+  w.pass_expert = reinterpret_cast<int32_t*>(b + o);
+  o += align256(4 * p);
+  w.pass_start = reinterpret_cast<int32_t*>(b + o);
+  o += align256(4 * p);
+  w.pass_count = reinterpret_cast<int32_t*>(b + o);
+  o += align256(4 * p);
   w.xenc = b + o;
   o += align256(4 * t * hidden);
   w.xscale = reinterpret_cast<float*>(b + o);
@@ -296,7 +312,7 @@ __host__ __device__ inline MoeWs moe_ws(void* base, int64_t t, int64_t p, int64_
 
 inline int64_t moe_ws_bytes(int64_t t, int64_t p, int64_t hidden, int64_t ffn, int64_t sffn) {
   const int64_t shared = sffn > 0 ? align256(6 * t * sffn) + align256(4 * t) + align256(4 * t * hidden) : 0;
-  return kHeaderBytes + kRangeBytes + 4 * align256(4 * p) + align256(4 * t * hidden) + align256(4 * t) +
+  return kHeaderBytes + kRangeBytes + 7 * align256(4 * p) + align256(4 * t * hidden) + align256(4 * t) +
          align256(4 * p * ffn) + align256(4 * p * hidden) + shared;
 }
 
@@ -643,12 +659,14 @@ __global__ void __launch_bounds__(kThreads) moe_prep_kernel(const int32_t* __res
     int u = block_exscan(s_sum, s_wsum, s_tot);
     int pc = block_exscan(p_sum, s_wsum, p_tot);
     (void)c_tot;
-    (void)p_tot;
     n_slots = s_tot;
     if (threadIdx.x == 0) {
       cum[0] = 0;
       ws.hdr[0] = s_tot;
       ws.hdr[1] = s_bad;
+      ws.hdr[kWorkGateUp] = 0;
+      ws.hdr[kWorkDown] = 0;
+      ws.hdr[kPassCount] = p_tot;
     }
     for (int e = e0; e < e1; ++e) {
       const int c = cnt[e];
@@ -657,7 +675,11 @@ __global__ void __launch_bounds__(kThreads) moe_prep_kernel(const int32_t* __res
         ws.slot_expert[u] = e;
         ws.slot_start[u] = o;
         ws.slot_count[u] = c;
-        pc += (c + kTokensPerPass - 1) / kTokensPerPass;
+        for (int c0 = 0; c0 < c; c0 += kTokensPerPass, ++pc) {
+          ws.pass_expert[pc] = e;
+          ws.pass_start[pc] = o + c0;
+          ws.pass_count[pc] = min(kTokensPerPass, c - c0);
+        }
         cum[u + 1] = pc;
         ++u;
       }
@@ -1169,6 +1191,256 @@ __global__ void __launch_bounds__(kThreads, 2)
   }
 }
 
+// ------------------------------------------------- pulled items (T > 1)
+// The batched form of the two expert kernels.  An item is (slot u, row
+// chunk c) of a whole CTA: each warp owns its own 16-row tile pair (gate/up)
+// or two 16-row tiles (down) over ALL K-blocks, accumulating in registers,
+// so no partial sums meet across warps and the only barriers are the
+// restaging of the item's token planes; CTAs pull items from a counter
+// (header word kWorkGateUp / kWorkDown, reset by the prep kernel), so the
+// ones that finish early take the remaining work.  The next K-block's tiles
+// (and at an item's last K-block the next item's first ones) load while the
+// current block computes.
+
+// K splits of a pulled gate/up item: 64-row items (4 tile pairs x 2 K
+// halves) give ~6 items per CTA at 64 tokens, so the last round's tail stays small.
+constexpr int kGuSplits = 2;
+// Batches of up to this many tokens keep the static, K-split items (few
+// selected experts: finer items fill the GPU better).
+constexpr int64_t kStaticMaxTokens = 8;
+
+// Items are published two ahead: at the start of iteration i thread 0 pulls
+// the item of iteration i + 2 into s_next[(i + 2) % 3], so the item of
+// iteration i + 1 (published before the previous closing barrier) can be
+// read during iteration i, to load its first tiles early; the slot a pull
+// overwrites was last read before the previous closing barrier.
+__device__ __forceinline__ int pull_item(int32_t* counter) { return atomicAdd(counter, 1); }
+
+// Gate/up: item = (slot u, chunk c) of OUT = 16 TP rows, TP = 8 / KS tile
+// pairs; warp w owns tile pair w % TP over the KB / KS K-blocks of split
+// w / TP.  KS > 1 adds the splits' partial sums through shared memory.
+template <int KB, int KS>
+__global__ void __launch_bounds__(kThreads, 2)
+    moe_gate_up_pulled_kernel(const uint8_t* __restrict__ gate, const uint8_t* __restrict__ up, int top_k,
+                              int ffn, MoeWs ws, MoeShared sh, int s_blocks, int t_total, int hidden) {
+  constexpr int K = KB * 256, TP = kWarps / KS, OUT = 16 * TP, KPW = KB / KS;
+  static_assert(kWarps % KS == 0 && KB % KS == 0, "K splits");
+  extern __shared__ __align__(16) uint8_t smem[];
+  uint8_t* lut = smem;
+  float* red = reinterpret_cast<float*>(smem + kLutBytes);
+  float* xsc = reinterpret_cast<float*>(smem + kLutBytes + kRedBytes);
+  int* spair = reinterpret_cast<int*>(xsc) + kMiscPair;
+  uint8_t* xs = smem + kLutBytes + kRedBytes + kMiscBytes;
+  __shared__ int s_next[3];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+  if (static_cast<int>(blockIdx.x) < s_blocks) {  // the shared expert's down rows
+    shared_down_block(blockIdx.x, sh, t_total, hidden, ws);
+    return;
+  }
+  stage_lut(lut);
+  pdl_wait();
+  pdl_launch_dependents();
+  const int chunks = ffn / OUT;
+  const int n_items = __ldcg(ws.hdr + kPassCount) * chunks;
+  const int tp = warp % TP, kb0 = (warp / TP) * KPW;
+  const uint32_t lane_off = static_cast<uint32_t>(lane & 15) * 8u;
+  const uint8_t* xl = xs + (g >> 1) * token_stride(K) + (g & 1) * plane_stride(K) + 16 * t;
+  auto tile_of = [&](int item, int kb) -> int64_t {
+    const int q = item / chunks, c = item - q * chunks;
+    const int e = __ldcg(ws.pass_expert + q);
+    return ((static_cast<int64_t>(e) * (ffn / 16) + c * TP + tp) * KB + kb) * kChunkBytes;
+  };
+  if (threadIdx.x == 0) {
+    s_next[0] = pull_item(ws.hdr + kWorkGateUp);
+    s_next[1] = pull_item(ws.hdr + kWorkGateUp);
+  }
+  cp_async_wait_all();
+  __syncthreads();
+  int it = s_next[0];
+  Tile tg{}, tu{};
+  if (it < n_items) {
+    const int64_t off = tile_of(it, kb0);
+    load_tile(gate + off, lane, tg);
+    load_tile(up + off, lane, tu);
+  }
+  int staged = -1;
+  int npass = 0;  // the reduction buffer of a pass is npass & 1
+  for (int iter = 0; it < n_items; ++iter) {
+    if (threadIdx.x == 0) s_next[(iter + 2) % 3] = pull_item(ws.hdr + kWorkGateUp);
+    const int next = s_next[(iter + 1) % 3];
+    const int q = it / chunks, c = it - q * chunks;  // one pass of <= kTokensPerPass tokens
+    const int start = __ldcg(ws.pass_start + q), mc = __ldcg(ws.pass_count + q);
+    if (q != staged) {
+      for (int i = threadIdx.x; i < mc * (K / 4); i += kThreads) {  // 16-byte pieces, K/8 per plane
+        const int v = i / (K / 4), j = i - v * (K / 4), plane = j / (K / 8), piece = j - plane * (K / 8);
+        const int tok = __ldcg(ws.pairs + start + v) / top_k;
+        cp_async16(xs + v * token_stride(K) + plane * plane_stride(K) + 16 * piece,
+                   ws.xenc + static_cast<int64_t>(tok) * 4 * K + plane * 2 * K + 16 * piece);
+      }
+      cp_async_commit();
+      if (threadIdx.x < mc) {
+        const int pair = __ldcg(ws.pairs + start + threadIdx.x);
+        spair[threadIdx.x] = pair;
+        xsc[threadIdx.x] = __ldcg(ws.xscale + pair / top_k);
+      }
+      cp_async_wait_all();
+      __syncthreads();
+      staged = q;
+    }
+    float acc[2][2] = {};
+#pragma unroll 1
+    for (int kb = kb0; kb < kb0 + KPW; ++kb) {
+      Tile ng{}, nu{};
+      if (kb + 1 < kb0 + KPW) {
+        const int64_t off = tile_of(it, kb + 1);
+        load_tile(gate + off, lane, ng);
+        load_tile(up + off, lane, nu);
+      } else if (next < n_items) {  // the next item's first tiles
+        const int64_t off = tile_of(next, kb0);
+        load_tile(gate + off, lane, ng);
+        load_tile(up + off, lane, nu);
+      }
+      block_steps(tg, tu, lut, lane_off, xl, kb, acc);
+      tg = ng;
+      tu = nu;
+    }
+    if constexpr (KS == 1) {
+      // lane (g, t): gate and up rows g, g+8 of this warp's tile pair, token t
+      if (t < mc) {
+        const float sc = xsc[t];
+        float* dst = ws.act + static_cast<int64_t>(spair[t]) * ffn + c * OUT + warp * 16 + g;
+        dst[0] = silu_f(acc[0][0] * sc) * (acc[1][0] * sc);
+        dst[8] = silu_f(acc[0][1] * sc) * (acc[1][1] * sc);
+      }
+    } else {
+      float* rb = red + (npass++ & 1) * kRedFloats;
+      reinterpret_cast<float4*>(rb)[warp * 32 + lane] = make_float4(acc[0][0], acc[0][1], acc[1][0], acc[1][1]);
+      __syncthreads();
+      for (int i = threadIdx.x; i < OUT * mc; i += kThreads) {
+        const int v = i / OUT, o = i - v * OUT;
+        const int otp = o >> 4, r = o & 15, src = (r & 7) * 4 + v, reg = r >> 3;
+        float gs = 0.f, us = 0.f;
+#pragma unroll
+        for (int k = 0; k < KS; ++k) {
+          const float* rr = rb + ((k * TP + otp) * 32 + src) * 4;
+          gs += rr[reg];
+          us += rr[2 + reg];
+        }
+        gs *= xsc[v];
+        us *= xsc[v];
+        ws.act[static_cast<int64_t>(spair[v]) * ffn + c * OUT + o] = silu_f(gs) * us;
+      }
+    }
+    __syncthreads();  // every warp is done with this item's planes and sums (a restaging follows)
+    it = next;
+  }
+}
+
+template <int KB>
+__global__ void __launch_bounds__(kThreads, 2)
+    moe_down_pulled_kernel(const uint8_t* __restrict__ down, int top_k, int hidden, MoeWs ws) {
+  constexpr int K = KB * 256, ROWS = 32 * kWarps;
+  extern __shared__ __align__(16) uint8_t smem[];
+  uint8_t* lut = smem;
+  float* xsc = reinterpret_cast<float*>(smem + kLutBytes + kRedBytes);
+  float* wmax = xsc + 16;
+  int* spair = reinterpret_cast<int*>(xsc) + kMiscPair;
+  uint8_t* xs = smem + kLutBytes + kRedBytes + kMiscBytes;
+  __shared__ int s_next[3];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+  stage_lut(lut);
+  pdl_launch_dependents();
+  pdl_wait();
+  const int chunks = hidden / ROWS;
+  const int n_items = __ldcg(ws.hdr + kPassCount) * chunks;
+  const uint32_t lane_off = static_cast<uint32_t>(lane & 15) * 8u;
+  const uint8_t* xl = xs + (g >> 1) * token_stride(K) + (g & 1) * plane_stride(K) + 16 * t;
+  auto tile_of = [&](int item, int half, int kb) -> int64_t {
+    const int q = item / chunks, c = item - q * chunks;
+    const int e = __ldcg(ws.pass_expert + q);
+    const int64_t tile = static_cast<int64_t>(e) * (hidden / 16) + c * 2 * kWarps + 2 * warp + half;
+    return (tile * KB + kb) * kChunkBytes;
+  };
+  if (threadIdx.x == 0) {
+    s_next[0] = pull_item(ws.hdr + kWorkDown);
+    s_next[1] = pull_item(ws.hdr + kWorkDown);
+  }
+  cp_async_wait_all();
+  __syncthreads();
+  int it = s_next[0];
+  Tile ta{}, tb{};
+  if (it < n_items) {
+    load_tile(down + tile_of(it, 0, 0), lane, ta);
+    load_tile(down + tile_of(it, 1, 0), lane, tb);
+  }
+  int staged = -1;
+  for (int iter = 0; it < n_items; ++iter) {
+    if (threadIdx.x == 0) s_next[(iter + 2) % 3] = pull_item(ws.hdr + kWorkDown);
+    const int next = s_next[(iter + 1) % 3];
+    const int q = it / chunks, c = it - q * chunks;  // one pass of <= kTokensPerPass tokens
+    const int start = __ldcg(ws.pass_start + q), mc = __ldcg(ws.pass_count + q);
+    if (q != staged) {
+      // act of pair slot v: threads [64 v, 64 v + 64) (warps 2v, 2v+1) -> fp16 planes
+      const int v = threadIdx.x >> 6, j = threadIdx.x & 63;
+      constexpr int F4 = K / 4 / 64;  // float4 per thread
+      float4 h[F4];
+      float m = 0.f;
+      const float4* src = nullptr;
+      const int pair = v < mc ? __ldcg(ws.pairs + start + v) : 0;
+      if (v < mc) src = reinterpret_cast<const float4*>(ws.act + static_cast<int64_t>(pair) * K);
+#pragma unroll
+      for (int i = 0; i < F4; ++i) {
+        h[i] = v < mc ? __ldcg(src + j + 64 * i) : make_float4(0.f, 0.f, 0.f, 0.f);
+        m = fmaxf(m, fmaxf(fmaxf(fabsf(h[i].x), fabsf(h[i].y)), fmaxf(fabsf(h[i].z), fabsf(h[i].w))));
+      }
+      m = warp_max(m);
+      if (lane == 0) wmax[warp] = m;  // (the previous item's readers passed its closing barrier)
+      __syncthreads();
+      m = fmaxf(wmax[2 * v], wmax[2 * v + 1]);
+      float inv, sx;
+      vector_scale(m, inv, sx);
+      if (v < mc) {
+        uint8_t* dst = xs + v * token_stride(K);
+#pragma unroll
+        for (int i = 0; i < F4; ++i)
+          store_planes(h[i], inv, dst + 8 * (j + 64 * i), dst + plane_stride(K) + 8 * (j + 64 * i));
+        if (j == 0) {
+          xsc[v] = sx;
+          spair[v] = pair;
+        }
+      }
+      __syncthreads();
+      staged = q;
+    }
+    float acc[2][2] = {};
+#pragma unroll 1
+    for (int kb = 0; kb < KB; ++kb) {
+      Tile na{}, nb{};
+      if (kb + 1 < KB) {
+        load_tile(down + tile_of(it, 0, kb + 1), lane, na);
+        load_tile(down + tile_of(it, 1, kb + 1), lane, nb);
+      } else if (next < n_items) {  // the next item's first tiles
+        load_tile(down + tile_of(next, 0, 0), lane, na);
+        load_tile(down + tile_of(next, 1, 0), lane, nb);
+      }
+      block_steps(ta, tb, lut, lane_off, xl, kb, acc);
+      ta = na;
+      tb = nb;
+    }
+    // lane (g, t): rows g, g+8 of the warp's tiles 2w (acc[0]) and 2w+1 (acc[1]), token t
+    if (t < mc) {
+      const float sc = xsc[t];
+      float* dst = ws.dn + static_cast<int64_t>(spair[t]) * hidden + c * ROWS + warp * 32 + g;
+      dst[0] = acc[0][0] * sc;
+      dst[8] = acc[0][1] * sc;
+      dst[16] = acc[1][0] * sc;
+      dst[24] = acc[1][1] * sc;
+    }
+    __syncthreads();  // every warp is done with this item's planes
+    it = next;
+  }
+}
+
 // ------------------------------------------------------------------ combine
 // out[t] = sum_k w[t, k] * down_k(act) in routing order, each product rounded
 // before the add like the reference's (out * w).sum(0) in f32.
@@ -1225,6 +1497,12 @@ int launch_all(const uint8_t* gate, const uint8_t* up, const uint8_t* down, cons
     if (e == cudaSuccess)
       e = cudaFuncSetAttribute(moe_down_kernel<KBD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                static_cast<int>(d_smem));
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(moe_gate_up_pulled_kernel<KBG, kGuSplits>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               static_cast<int>(gu_smem));
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(moe_down_pulled_kernel<KBD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               static_cast<int>(d_smem));
     if (e != cudaSuccess) return fail_cuda(e, "moe set smem");
     configured_device = dev;
   }
@@ -1244,12 +1522,23 @@ int launch_all(const uint8_t* gate, const uint8_t* up, const uint8_t* down, cons
   const int prep_blocks = (direct ? 1 : 1 + static_cast<int>(t)) + sgu_blocks;
   cudaError_t e = launch_pdl(moe_prep_kernel, dim3(prep_blocks), prep_smem, stream, ids, p, n_experts, direct, x,
                              static_cast<int>(t), hidden, ws, gu_grid, gu_chunks, d_grid, d_chunks, shv);
-  if (e == cudaSuccess)
-    e = launch_pdl(moe_gate_up_kernel<KBG>, dim3(sd_blocks + gu_grid), gu_smem, stream, gate, up, ids, n_experts,
-                   direct, top_k, ffn, ws, gu_grid, shv, sd_blocks, static_cast<int>(t), hidden);
-  if (e == cudaSuccess)
-    e = launch_pdl(moe_down_kernel<KBD>, dim3(d_grid), d_smem, stream, down, ids, weights, out, n_experts, direct,
-                   top_k, hidden, ws, shared);
+  // up to kStaticMaxTokens tokens: static item ranges of K-split items (one
+  // token: the last of a row chunk's CTAs combines); more: whole-pass items
+  // pulled from a counter, then the combine kernel
+  if (t <= kStaticMaxTokens) {
+    if (e == cudaSuccess)
+      e = launch_pdl(moe_gate_up_kernel<KBG>, dim3(sd_blocks + gu_grid), gu_smem, stream, gate, up, ids, n_experts,
+                     direct, top_k, ffn, ws, gu_grid, shv, sd_blocks, static_cast<int>(t), hidden);
+    if (e == cudaSuccess)
+      e = launch_pdl(moe_down_kernel<KBD>, dim3(d_grid), d_smem, stream, down, ids, weights, out, n_experts, direct,
+                     top_k, hidden, ws, shared);
+  } else {
+    if (e == cudaSuccess)
+      e = launch_pdl(moe_gate_up_pulled_kernel<KBG, kGuSplits>, dim3(sd_blocks + gu_grid), gu_smem, stream, gate, up, top_k,
+                     ffn, ws, shv, sd_blocks, static_cast<int>(t), hidden);
+    if (e == cudaSuccess)
+      e = launch_pdl(moe_down_pulled_kernel<KBD>, dim3(d_grid), d_smem, stream, down, top_k, hidden, ws);
+  }
   const int64_t total = t * hidden;
   const int blocks = static_cast<int>(std::min<int64_t>((total + kThreads - 1) / kThreads, 4096));
   if (e == cudaSuccess && !direct)

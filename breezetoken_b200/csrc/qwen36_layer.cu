@@ -136,7 +136,9 @@ __global__ void __launch_bounds__(kGdnStepThreads) gdn_gated_step_kernel(const _
   }
 }
 
-// One block per row; n % 8 == 0.
+// One block per row, n % 8 == 0.  Rows of up to 8 * 256 elements are read
+// once: each thread keeps its 8 consecutive elements in registers through
+// the block reduction; longer rows take a second pass.
 __global__ void __launch_bounds__(256) add_rms_norm_planes_kernel(const float* __restrict__ a,
                                                                    const float* __restrict__ b,
                                                                    const float* __restrict__ w, float* __restrict__ h,
@@ -146,14 +148,27 @@ __global__ void __launch_bounds__(256) add_rms_norm_planes_kernel(const float* _
   const int64_t row = blockIdx.x;
   const float* ar = a + row * n;
   const float* br = b ? b + row * n : nullptr;
+  const bool one_pass = n <= 8 * static_cast<int>(blockDim.x);
+  float v[8];
   float ss = 0.f;
-  for (int i = threadIdx.x; i < n; i += blockDim.x) {
-    float v = ar[i];
+  for (int i0 = 8 * threadIdx.x; i0 < n; i0 += 8 * blockDim.x) {
+    const float4 a0 = *reinterpret_cast<const float4*>(ar + i0), a1 = *reinterpret_cast<const float4*>(ar + i0 + 4);
+    float x[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
     if (br) {
-      v = v + br[i];
-      if (h) h[row * n + i] = v;
+      const float4 b0 = *reinterpret_cast<const float4*>(br + i0), b1 = *reinterpret_cast<const float4*>(br + i0 + 4);
+      const float bb[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+#pragma unroll
+      for (int j = 0; j < 8; ++j) x[j] = x[j] + bb[j];
+      if (h) {
+        *reinterpret_cast<float4*>(h + row * n + i0) = make_float4(x[0], x[1], x[2], x[3]);
+        *reinterpret_cast<float4*>(h + row * n + i0 + 4) = make_float4(x[4], x[5], x[6], x[7]);
+      }
     }
-    ss = fmaf(v, v, ss);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      ss = fmaf(x[j], x[j], ss);
+      v[j] = x[j];
+    }
   }
   ss = warp_sum(ss);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -164,19 +179,23 @@ __global__ void __launch_bounds__(256) add_rms_norm_planes_kernel(const float* _
   for (int i = 0; i < 8; ++i) total += scratch[i];
   const float r = 1.0f / sqrtf(total / static_cast<float>(n) + eps);
   for (int i0 = 8 * threadIdx.x; i0 < n; i0 += 8 * blockDim.x) {
-    float v[8];
+    if (!one_pass) {
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      const float x = br ? ar[i0 + j] + br[i0 + j] : ar[i0 + j];
-      v[j] = __fmul_rn(__fmul_rn(x, r), w[i0 + j]);
-      y[row * n + i0 + j] = v[j];
+      for (int j = 0; j < 8; ++j) v[j] = br ? ar[i0 + j] + br[i0 + j] : ar[i0 + j];
     }
+    const float4 w0 = *reinterpret_cast<const float4*>(w + i0), w1 = *reinterpret_cast<const float4*>(w + i0 + 4);
+    const float ww[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+    float o[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) o[j] = __fmul_rn(__fmul_rn(v[j], r), ww[j]);
+    *reinterpret_cast<float4*>(y + row * n + i0) = make_float4(o[0], o[1], o[2], o[3]);
+    *reinterpret_cast<float4*>(y + row * n + i0 + 4) = make_float4(o[4], o[5], o[6], o[7]);
     uint32_t pk[3][4];
 #pragma unroll
     for (int j = 0; j < 8; j += 2) {
       float h0, m0, l0, h1, m1, l1;
-      split3(v[j], h0, m0, l0);
-      split3(v[j + 1], h1, m1, l1);
+      split3(o[j], h0, m0, l0);
+      split3(o[j + 1], h1, m1, l1);
       pk[0][j / 2] = bf16_pair_rn(h0, h1);
       pk[1][j / 2] = bf16_pair_rn(m0, m1);
       pk[2][j / 2] = bf16_pair_rn(l0, l1);
@@ -210,8 +229,10 @@ int add_rms_norm_planes(const float* a, const float* b, const float* w, float* h
                         int64_t rows, int64_t n, float eps, cudaStream_t stream) {
   if (!a || !w || !y || !planes || (b && !h) || rows < 0 || n < 8 || n % 8)
     return fail(BT_ERR_INVALID, "add_rms_norm_planes: bad arguments (n %% 8 == 0)");
-  if ((reinterpret_cast<uintptr_t>(planes) & 15) || rows > 2147483647LL || n > 2147483647LL)
-    return fail(BT_ERR_INVALID, "add_rms_norm_planes: planes must be 16-byte aligned");
+  if ((reinterpret_cast<uintptr_t>(a) | reinterpret_cast<uintptr_t>(b) | reinterpret_cast<uintptr_t>(w) |
+       reinterpret_cast<uintptr_t>(h) | reinterpret_cast<uintptr_t>(y) | reinterpret_cast<uintptr_t>(planes)) & 15 ||
+      rows > 2147483647LL || n > 2147483647LL)
+    return fail(BT_ERR_INVALID, "add_rms_norm_planes: every buffer must be 16-byte aligned");
   if (rows == 0) return BT_OK;
   note_launch();
   add_rms_norm_planes_kernel<<<static_cast<unsigned>(rows), 256, 0, stream>>>(

@@ -10,11 +10,12 @@
 
 Each prints one JSON line: average launch time and achieved HBM GB/s from
 the algorithmic bytes of one launch (weights / state / KV read once).
-``moe`` is the 35B-A3B MoE-layer benchmark: routed experts of one MoE layer (hidden 2048,
-256 IQ3_S experts of ffn 512, top-8 over N(0,1) router logits, seed 3),
-timed per call after reading a 256 MB buffer (the experts are not in L2);
-its bytes are the
-U * 1,351,680 of the U distinct experts the routing selects.
+``moe`` is the 35B-A3B MoE-layer benchmark: one MoE layer (hidden 2048, 256
+IQ3_S experts of ffn 512 quantised from N(0, 0.02), top-8 over N(0,1) router
+logits, the bf16 shared expert, seed 3), its output checked once against a
+dequantise-then-matmul, then timed per call after reading a 256 MB buffer
+(the experts are not in L2); its bytes are the U * 1,351,680 of the U
+distinct experts the routing selects, the shared expert and x in and out.
 ``qwen36`` is the 35B-A3B decode benchmark on one GPU (Qwen3.6-35B-A3B shape, seeded
 random weights built on the device, 64 sequences in lockstep).
 ``linear`` times ``bt_linear_rows`` (bf16 weight rows x three bf16 planes of
@@ -197,43 +198,59 @@ def bench_attn(batch: int, ctx: int, splits: int, iters: int) -> dict:
 
 def bench_moe(tokens: int, iters: int, shared: bool = True) -> dict:
     from breezetoken_b200.moe import IQ3SExperts, SharedExpert, moe_forward, route_logits
-    from breezetoken_b200.quant import quantize_iq3_s
+    from breezetoken_b200.synth import MoeSpec, make_moe_layer, moe_layer_inputs
 
     hidden, ffn, n_exp, top_k = 2048, 512, 256, 8
-    rng = np.random.default_rng(3)
-    # 4 distinct quantised experts tiled to 256: timing needs valid IQ3_S
-    # bytes, not 256 distinct ones
-    base = 4
-
-    def tensor(rows: int, k: int) -> np.ndarray:
-        q = quantize_iq3_s(rng.standard_normal((base * rows, k)).astype(np.float32) * np.float32(0.02))
-        return np.tile(q.reshape(base, -1), (n_exp // base, 1)).reshape(-1)
-
-    ex = IQ3SExperts.from_gguf_bytes(tensor(ffn, hidden), tensor(ffn, hidden), tensor(hidden, ffn), n_exp, hidden,
-                                     ffn, "cuda")
-    x = torch.from_numpy(rng.standard_normal((tokens, hidden)).astype(np.float32)).cuda().bfloat16().float()
-    logits = torch.from_numpy(rng.standard_normal((tokens, n_exp)).astype(np.float32)).cuda()
+    # the MoE-layer benchmark's layer: 256 distinct IQ3_S experts quantised
+    # from N(0, 0.02) and the bf16 shared expert, seed 3
+    m = make_moe_layer(MoeSpec(), seed=3)
+    ex = IQ3SExperts.from_gguf_bytes(m["gate"], m["up"], m["down"], n_exp, hidden, ffn, "cuda")
+    xh, lh = moe_layer_inputs(tokens)
+    x, logits = torch.from_numpy(xh).cuda(), torch.from_numpy(lh).cuda()
     r = route_logits(logits, top_k)
     u = int(torch.unique(r.expert_ids).numel())
-    ws = torch.zeros(int(N.load().bt_moe_workspace_bytes(tokens, hidden, ffn, n_exp, top_k)), dtype=torch.uint8,
-                     device="cuda")
+    se = None
+    if shared:
+        se = SharedExpert.from_tensors(torch.from_numpy(m["sh_gate"]), torch.from_numpy(m["sh_up"]),
+                                       torch.from_numpy(m["sh_down"]), torch.from_numpy(m["sh_gate_inp"]), "cuda")
+        ws = torch.zeros(int(N.load().bt_moe_layer_workspace_bytes(tokens, hidden, ffn, ffn, n_exp, top_k)),
+                         dtype=torch.uint8, device="cuda")
+    else:
+        ws = torch.zeros(int(N.load().bt_moe_workspace_bytes(tokens, hidden, ffn, n_exp, top_k)), dtype=torch.uint8,
+                         device="cuda")
     flush = torch.ones(256 << 20, dtype=torch.uint8, device="cuda")
     s = torch.cuda.Stream()
 
     def flush_l2() -> None:
         flush.sum(dtype=torch.int32)  # read 256 MB: afterwards L2 holds only clean lines
 
-    se = None
-    if shared:  # one bf16 shared expert of ffn 512 (the 35B-A3B layer)
-        def w(*shape) -> torch.Tensor:
-            return torch.from_numpy(rng.standard_normal(shape).astype(np.float32) * np.float32(0.02))
+    def call() -> torch.Tensor:
+        return moe_forward(ex, se, x, r.expert_ids, r.weights, ws)
 
-        se = SharedExpert.from_tensors(w(ffn, hidden), w(ffn, hidden), w(hidden, ffn), w(hidden), "cuda")
-        ws = torch.zeros(int(N.load().bt_moe_layer_workspace_bytes(tokens, hidden, ffn, ffn, n_exp, top_k)),
-                         dtype=torch.uint8, device="cuda")
-
-    def call() -> None:
-        moe_forward(ex, se, x, r.expert_ids, r.weights, ws)
+    # self-check of up to 4 tokens against a dequantise-then-matmul in f64 on
+    # the bit-exact device dequantisation (bt_dequant_iq3_s)
+    got = call()
+    worst = 0.0
+    for t in range(min(tokens, 4)):
+        ref = torch.zeros(hidden, dtype=torch.float64, device="cuda")
+        xt = x[t].double()
+        for e, w in zip(r.expert_ids[t].tolist(), r.weights[t].tolist(), strict=True):
+            deq = []
+            for name, rows, k in (("gate", ffn, hidden), ("up", ffn, hidden), ("down", hidden, ffn)):
+                raw = torch.from_numpy(m[name][e * rows:(e + 1) * rows].reshape(-1).copy()).cuda()
+                out = torch.empty(rows, k, device="cuda")
+                N.call("bt_dequant_iq3_s", raw.data_ptr(), out.data_ptr(), rows, k, 0)
+                torch.cuda.synchronize()
+                deq.append(out.double())
+            act = torch.nn.functional.silu(deq[0] @ xt) * (deq[1] @ xt)
+            ref += w * (deq[2] @ act)
+        if se is not None:
+            g = torch.sigmoid(se.gate_inp.double() @ xt)
+            act = torch.nn.functional.silu(se.gate.double() @ xt) * (se.up.double() @ xt)
+            ref += g * (se.down.double() @ act)
+        worst = max(worst, float((got[t].double() - ref).abs().max() / ref.abs().max()))
+    if worst > 1e-5:
+        raise AssertionError(f"MoE layer output off by {worst:.2e} of scale")
 
     # launch-timed: events around each call, L2 flushed before it
     total = 0.0
@@ -256,8 +273,8 @@ def bench_moe(tokens: int, iters: int, shared: bool = True) -> dict:
     # algorithmic bytes: the selected experts, the bf16 shared expert, x in and out
     nbytes = u * 1_351_680 + (6_291_456 if shared else 0) + tokens * hidden * 8
     return {"kernel": "moe_layer_iq3s", "tokens": tokens, "unique_experts": u, "shared_expert": shared,
-            "us": sec * 1e6,
-            "us_graph": gsec * 1e6, "bytes": nbytes, "gbs": nbytes / sec / 1e9, "gbs_graph": nbytes / gsec / 1e9,
+            "us": sec * 1e6, "us_graph": gsec * 1e6, "bytes": nbytes, "gbs": nbytes / sec / 1e9,
+            "gbs_graph": nbytes / gsec / 1e9, "check_rel_err": worst,
             "l2": "flushed before each call (256 MB read)"}
 
 

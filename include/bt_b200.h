@@ -239,7 +239,7 @@ BT_API int bt_gdn_gated_step(const float* mixed, int64_t mixed_bs, const float* 
 /* bt_fused_add_rms_norm that also writes y's three bf16 planes (rows, 3, n)
  * (the form of bt_bf16_planes) in the same pass: h = a + b (b may be NULL:
  * then y = rms_norm(a) and h is not written), y = rms_norm(h, w, eps).
- * n % 8 == 0; planes 16-byte aligned.                                     */
+ * n % 8 == 0; every buffer 16-byte aligned.                              */
 BT_API int bt_add_rms_norm_planes(const float* a, const float* b, const float* w, float* h,
                                   float* y, void* planes, int64_t rows, int64_t n, float eps,
                                   void* stream);
