@@ -123,6 +123,91 @@ __global__ void __launch_bounds__(kThreads) gdn_decode_kernel(const __grid_const
   }
 }
 
+// One CTA of 256 threads per (sequence, value head) of dim 128, for batches
+// with enough heads to fill the GPU: thread t owns column t % 128 of the
+// head's state, rows [64 (t / 128), +64), in registers, so every warp reads
+// and writes whole 512-byte rows and the step needs four barriers instead of
+// the column-tiled kernel's per-tile reductions.  Same arithmetic per
+// element as gdn_decode_kernel (only the row-group partition of the column
+// sums differs: two halves of 64 rows instead of 16 groups of 8).
+constexpr int kHeadDim = 128;
+constexpr int kHeadHalves = kThreads / kHeadDim;
+constexpr int kHeadRows = kHeadDim / kHeadHalves;
+
+template <typename T>
+__global__ void __launch_bounds__(kThreads) gdn_head_kernel(const __grid_constant__ GdnParams p) {
+  __shared__ float sq[kHeadDim], sk[kHeadDim], red[kHeadHalves][kHeadDim];
+  __shared__ float s_decay, s_bsig;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int c = tid % kHeadDim, half = tid / kHeadDim, r0 = half * kHeadRows;
+  const int hv = blockIdx.x % p.heads_v, b = blockIdx.x / p.heads_v;
+  const int hk = hv % p.heads_k;
+  trace_entry(p.trace);
+  float* S = p.state + (static_cast<int64_t>(b) * p.heads_v + hv) * kHeadDim * kHeadDim;
+  pdl_launch_dependents();
+  pdl_wait();
+  trace_waited(p.trace);
+  float s[kHeadRows];
+#pragma unroll
+  for (int i = 0; i < kHeadRows; ++i) s[i] = S[static_cast<int64_t>(r0 + i) * kHeadDim + c];
+  if (warp < 2) {  // normalised q (x scale) and k of key head hk
+    const void* src = warp == 0 ? p.q : p.k;
+    const int64_t off = static_cast<int64_t>(b) * (warp == 0 ? p.q_bs : p.k_bs) + static_cast<int64_t>(hk) * kHeadDim;
+    float vals[kHeadDim / 32];
+    float ss = 0.f;
+#pragma unroll
+    for (int i = 0; i < kHeadDim / 32; ++i) {
+      vals[i] = load_elem<T>(src, off + lane + 32 * i);
+      ss = fmaf(vals[i], vals[i], ss);
+    }
+    ss = warp_sum(ss);
+    const float r = 1.0f / sqrtf(ss + p.eps);
+    float* dst = warp == 0 ? sq : sk;
+#pragma unroll
+    for (int i = 0; i < kHeadDim / 32; ++i)
+      dst[lane + 32 * i] = warp == 0 ? __fmul_rn(__fmul_rn(vals[i], r), p.scale) : __fmul_rn(vals[i], r);
+  } else if (tid == 64) {
+    s_decay = expf(p.g[static_cast<int64_t>(b) * p.g_bs + hv]);
+    s_bsig = sigmoid_f(p.beta[static_cast<int64_t>(b) * p.beta_bs + hv]);
+  }
+  __syncthreads();
+  trace_ready(p.trace);
+  const float decay = s_decay, bsig = s_bsig;
+  float rec = 0.f;
+#pragma unroll
+  for (int i = 0; i < kHeadRows; ++i) {
+    s[i] = __fmul_rn(s[i], decay);
+    rec = fmaf(s[i], sk[r0 + i], rec);
+  }
+  red[half][c] = rec;
+  __syncthreads();
+  float recalled = 0.f;
+#pragma unroll
+  for (int h = 0; h < kHeadHalves; ++h) recalled += red[h][c];
+  const float vv = load_elem<T>(p.v, static_cast<int64_t>(b) * p.v_bs + static_cast<int64_t>(hv) * kHeadDim + c);
+  const float delta = __fmul_rn(vv - recalled, bsig);
+  float o = 0.f;
+#pragma unroll
+  for (int i = 0; i < kHeadRows; ++i) {
+    s[i] = __fadd_rn(s[i], __fmul_rn(sk[r0 + i], delta));
+    S[static_cast<int64_t>(r0 + i) * kHeadDim + c] = s[i];
+    o = fmaf(s[i], sq[r0 + i], o);
+  }
+  __syncthreads();  // every thread has read red[][] above
+  red[half][c] = o;
+  __syncthreads();
+  if (half == 0) {
+    float t = 0.f;
+#pragma unroll
+    for (int h = 0; h < kHeadHalves; ++h) t += red[h][c];
+    p.out[static_cast<int64_t>(b) * p.out_bs + static_cast<int64_t>(hv) * kHeadDim + c] = t;
+  }
+  if (p.trace) {
+    __syncthreads();
+    trace_exit(p.trace);
+  }
+}
+
 template <typename T>
 cudaError_t launch_dim(const GdnParams& p, cudaLaunchConfig_t& cfg) {
   switch (p.dim) {
@@ -151,7 +236,15 @@ int gdn_decode_launch(const GdnParams& p, cudaStream_t stream, bool pdl) {
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 1 : 0;
-  const cudaError_t e = p.in_dtype == BT_BF16 ? launch_dim<__nv_bfloat16>(p, cfg) : launch_dim<float>(p, cfg);
+  cudaError_t e;
+  if (p.dim == kHeadDim && static_cast<int64_t>(p.batch) * p.heads_v >= 4LL * sm_count()) {
+    // enough heads for every SM: one CTA per head
+    cfg.gridDim = dim3(static_cast<unsigned>(p.batch) * p.heads_v);
+    e = p.in_dtype == BT_BF16 ? ::bt::launch_ex(&cfg, gdn_head_kernel<__nv_bfloat16>, p)
+                              : ::bt::launch_ex(&cfg, gdn_head_kernel<float>, p);
+  } else {
+    e = p.in_dtype == BT_BF16 ? launch_dim<__nv_bfloat16>(p, cfg) : launch_dim<float>(p, cfg);
+  }
   if (e != cudaSuccess) return fail_cuda(e, "gdn_decode launch");
   return BT_OK;
 }

@@ -594,7 +594,8 @@ __device__ __forceinline__ int block_exscan(int v, int* wsum, int& total) {
 __global__ void __launch_bounds__(kThreads) moe_prep_kernel(const int32_t* __restrict__ ids, int p_total,
                                                             int n_experts, int direct, const float* __restrict__ x,
                                                             int t_total, int hidden, MoeWs ws, int gu_grid,
-                                                            int gu_chunks, int d_grid, int d_chunks, MoeShared sh) {
+                                                            int gu_chunks, int d_grid, int d_chunks, MoeShared sh,
+                                                            int pulled) {
   pdl_launch_dependents();
   const int enc0 = direct ? 0 : 1;
   if (static_cast<int>(blockIdx.x) >= enc0 + t_total) {
@@ -687,6 +688,18 @@ __global__ void __launch_bounds__(kThreads) moe_prep_kernel(const int32_t* __res
     }
   }
   __syncthreads();  // cum and off complete
+  if (pulled) {
+    // pulled items need no static ranges, and a token's expert output does
+    // not depend on its place in the expert's pair list: place the pairs
+    // with a per-expert cursor (one atomic each) instead of ranking them
+    for (int e = threadIdx.x; e < n_experts; e += blockDim.x) cnt[e] = 0;
+    __syncthreads();
+    for (int q = threadIdx.x; q < p_total; q += blockDim.x) {
+      const int e = sid[q];
+      if (e >= 0 && e < n_experts) ws.pairs[off[e] + atomicAdd(&cnt[e], 1)] = q;
+    }
+    return;
+  }
   for (int b = threadIdx.x; b < gu_grid; b += blockDim.x) {
     const int64_t w = static_cast<int64_t>(cum[n_slots]) * gu_chunks;
     ws.ranges[2 * b] = item_at(cum, n_slots, gu_chunks, b * w / gu_grid);
@@ -1520,12 +1533,13 @@ int launch_all(const uint8_t* gate, const uint8_t* up, const uint8_t* down, cons
   const int sgu_blocks = shared ? (static_cast<int>(shv.ffn) / 16 + 1) * passes : 0;
   const int sd_blocks = shared ? hidden / 64 * passes : 0;
   const int prep_blocks = (direct ? 1 : 1 + static_cast<int>(t)) + sgu_blocks;
+  const int pulled = t > kStaticMaxTokens ? 1 : 0;
   cudaError_t e = launch_pdl(moe_prep_kernel, dim3(prep_blocks), prep_smem, stream, ids, p, n_experts, direct, x,
-                             static_cast<int>(t), hidden, ws, gu_grid, gu_chunks, d_grid, d_chunks, shv);
+                             static_cast<int>(t), hidden, ws, gu_grid, gu_chunks, d_grid, d_chunks, shv, pulled);
   // up to kStaticMaxTokens tokens: static item ranges of K-split items (one
   // token: the last of a row chunk's CTAs combines); more: whole-pass items
   // pulled from a counter, then the combine kernel
-  if (t <= kStaticMaxTokens) {
+  if (!pulled) {
     if (e == cudaSuccess)
       e = launch_pdl(moe_gate_up_kernel<KBG>, dim3(sd_blocks + gu_grid), gu_smem, stream, gate, up, ids, n_experts,
                      direct, top_k, ffn, ws, gu_grid, shv, sd_blocks, static_cast<int>(t), hidden);

@@ -143,11 +143,20 @@ def bench_gdn(batch: int, steps: int, heads: int = 16, dim: int = 128) -> dict:
 
     sec = _time(run, steps, s)
     gsec = _time_graph(run, steps, s)
+    # the same steps with a 256 MB read before each (L2 holds none of the
+    # state when a step starts): device time of (flush + step) minus flush
+    flush = torch.ones(256 << 20, dtype=torch.uint8, device="cuda")
+
+    def flush_l2() -> None:
+        flush.sum(dtype=torch.int32)
+
+    fsec = _time_graph(lambda: (flush_l2(), run()), steps, s) - _time_graph(flush_l2, steps, s)
     nbytes = batch * (2 * heads * dim * dim * 4 + 3 * heads * dim * 2 + 2 * heads * 4 + heads * dim * 4)
     return {"kernel": "gdn_decode", "batch": batch, "steps": steps, "us_per_step": sec * 1e6,
-            "us_per_step_graph": gsec * 1e6, "bytes": nbytes, "gbs": nbytes / sec / 1e9,
-            "gbs_graph": nbytes / gsec / 1e9,
-            "note": "graph: the steps captured in one CUDA graph (device time; a B=1 state stays in L2)"}
+            "us_per_step_graph": gsec * 1e6, "us_per_step_l2_flushed": fsec * 1e6, "bytes": nbytes,
+            "gbs": nbytes / sec / 1e9, "gbs_graph": nbytes / gsec / 1e9, "gbs_l2_flushed": nbytes / fsec / 1e9,
+            "note": "graph: the steps captured in one CUDA graph, back to back (a state of up to ~126 MB partly "
+                    "stays in L2 between steps); l2_flushed: a 256 MB read before every step"}
 
 
 def attn_inputs(batch: int, ctx: int, seed: int = 2):

@@ -168,13 +168,15 @@ def test_gdn_decode_config2_256_steps(be, batch) -> None:
     np.testing.assert_allclose(state.cpu().numpy(), ref_state, rtol=1e-4, atol=1e-4)
 
 
-def test_gdn_decode_strided_views_equal_contiguous(cuda) -> None:
+@pytest.mark.parametrize("B", [5, 40])
+def test_gdn_decode_strided_views_equal_contiguous(cuda, B) -> None:
     """bt_gdn_decode_strided on views of one packed row per sequence (q | k |
     v as the conv output holds them, beta | alpha as one projection, out with
     padding) gives the same bits as bt_gdn_decode on contiguous copies, with
-    the GQA head mapping (32 value heads over 16 key heads)."""
+    the GQA head mapping (32 value heads over 16 key heads); 40 sequences
+    take the one-CTA-per-head kernel, checked against the oracle as well."""
     rng = np.random.default_rng(31)
-    B, HK, HV, D = 5, 16, 32, 128
+    HK, HV, D = 16, 32, 128
     c = 2 * HK * D + HV * D
     mixed = torch.from_numpy(rng.standard_normal((B, c), dtype=np.float32) * 0.3).cuda()
     ba = torch.from_numpy(rng.standard_normal((B, 2 * HV), dtype=np.float32)).cuda()
@@ -194,6 +196,13 @@ def test_gdn_decode_strided_views_equal_contiguous(cuda) -> None:
     assert torch.equal(o2[:, : HV * D].reshape(B, HV, D), o1)
     assert torch.isnan(o2[:, HV * D :]).all()  # the padding is not written
     assert torch.equal(s2, s1)
+    ref_state = s0.cpu().numpy().copy()
+    for b in range(B):
+        ro = ops.gdn_decode(q[b].reshape(HK, D).cpu().numpy(), k[b].reshape(HK, D).cpu().numpy(),
+                            v[b].reshape(HV, D).cpu().numpy(), g[b].cpu().numpy(), beta[b].cpu().numpy(),
+                            ref_state[b], float(D ** -0.5), 1e-6)
+        np.testing.assert_allclose(o1[b].cpu().numpy(), ro, rtol=1e-4, atol=1e-5)
+    np.testing.assert_allclose(s1.cpu().numpy(), ref_state, rtol=1e-4, atol=1e-5)
     assert N.load().bt_gdn_decode_strided(q.data_ptr(), k.data_ptr(), v.data_ptr(), N.BT_F32, HK * D - 1, c, c,
                                           g.data_ptr(), HV, beta.data_ptr(), 2 * HV, s2.data_ptr(), o2.data_ptr(),
                                           HV * D, B, HK, HV, D, 1.0, 1e-6, None) == N.BT_ERR_INVALID
