@@ -129,17 +129,22 @@ __device__ __forceinline__ void prefetch_l2(const void* p, uint32_t bytes) {
   asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
 }
 
-template <bool F32W, int NP, int TW>
+// KS > 1: the K range is split over the KS CTAs of a cluster (grid z); each
+// CTA reduces its warps' sums, then cluster rank 0 adds the CTAs' sums in
+// rank order through distributed shared memory (deterministic, no workspace).
+template <bool F32W, int NP, int TW, int KS>
 __global__ void __launch_bounds__(kThreads) linear_rows_kernel(const void* __restrict__ w,
                                                                const __nv_bfloat16* __restrict__ xp,
                                                                float* __restrict__ y, int n, int k, int t_total) {
   using Elem = typename std::conditional<F32W, float, __nv_bfloat16>::type;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
-  const int tile0 = blockIdx.x * TW, c0 = blockIdx.y * kPass * NP, span = k / kWarps;
+  const int tile0 = blockIdx.x * TW, c0 = blockIdx.y * kPass * NP, span = k / (kWarps * KS);
+  const int kbase = static_cast<int>(blockIdx.z % KS) * (k / KS);
   if (lane < 16)
 #pragma unroll
     for (int j = 0; j < TW; ++j)
-      prefetch_l2(static_cast<const Elem*>(w) + static_cast<int64_t>(16 * (tile0 + j) + lane) * k + warp * span,
+      prefetch_l2(static_cast<const Elem*>(w) + static_cast<int64_t>(16 * (tile0 + j) + lane) * k + kbase +
+                      warp * span,
                   static_cast<uint32_t>(span * sizeof(Elem)));
   pdl_wait();  // the planes come from earlier kernels
   pdl_launch_dependents();
@@ -153,7 +158,7 @@ __global__ void __launch_bounds__(kThreads) linear_rows_kernel(const void* __res
   }
   float c[TW][NP][4] = {};
 #pragma unroll(NP * TW < 4 ? 2 : 1)  // the passes of a step already give the loads to overlap
-  for (int k0 = warp * span; k0 < (warp + 1) * span; k0 += 32) {
+  for (int k0 = kbase + warp * span; k0 < kbase + (warp + 1) * span; k0 += 32) {
     const int col = k0 + 8 * t;
     constexpr int NA = F32W ? 3 : 1;
     uint4 ra[TW][NA], rb[TW][NA];
@@ -189,14 +194,36 @@ __global__ void __launch_bounds__(kThreads) linear_rows_kernel(const void* __res
     for (int p = 0; p < NP; ++p)
       red[warp][j * NP + p][lane] = make_float4(c[j][p][0], c[j][p][1], c[j][p][2], c[j][p][3]);
   __syncthreads();
-  for (int i = threadIdx.x; i < TW * 16 * kPass * NP; i += kThreads) {  // (tile j, row r, token v), K slices in order
+  constexpr int OUTS = TW * 16 * kPass * NP;
+  __shared__ float part[KS > 1 ? OUTS : 1];
+  for (int i = threadIdx.x; i < OUTS; i += kThreads) {  // (tile j, row r, token v), K slices in order
     const int r = i & 15, v = (i >> 4) % (kPass * NP), j = (i >> 4) / (kPass * NP);
     const int p = v / kPass, vv = v % kPass;
     const int src = (r & 7) * 4 + (vv >> 1), reg = (r >> 3) * 2 + (vv & 1);
     float s = 0.f;
 #pragma unroll
     for (int q = 0; q < kWarps; ++q) s += reinterpret_cast<const float*>(&red[q][j * NP + p][src])[reg];
-    if (c0 + v < t_total) y[static_cast<int64_t>(c0 + v) * n + 16 * (tile0 + j) + r] = s;
+    if constexpr (KS > 1)
+      part[i] = s;
+    else if (c0 + v < t_total)
+      y[static_cast<int64_t>(c0 + v) * n + 16 * (tile0 + j) + r] = s;
+  }
+  if constexpr (KS > 1) {
+    cg::cluster_group cluster = cg::this_cluster();
+    cluster.sync();  // every CTA's sums are in place
+    if (cluster.block_rank() == 0) {
+      for (int i = threadIdx.x; i < OUTS; i += kThreads) {
+        const int r = i & 15, v = (i >> 4) % (kPass * NP), j = (i >> 4) / (kPass * NP);
+        float vals[KS];
+#pragma unroll
+        for (int q = 0; q < KS; ++q) vals[q] = cluster.map_shared_rank(part, q)[i];
+        float s = vals[0];
+#pragma unroll
+        for (int q = 1; q < KS; ++q) s += vals[q];
+        if (c0 + v < t_total) y[static_cast<int64_t>(c0 + v) * n + 16 * (tile0 + j) + r] = s;
+      }
+    }
+    cluster.sync();  // no CTA leaves while rank 0 still reads its shared memory
   }
 }
 
@@ -206,6 +233,7 @@ constexpr int kKStage = 32;                  // K columns per pipeline stage
 constexpr int kStages = 4;
 constexpr int kRowBytes = 2 * kKStage + 16;  // padded shared-memory row: 8 rows of a ldmatrix hit distinct banks
 constexpr int kMaxSplits = 8;                // cluster size (portable limit)
+constexpr int kF32Splits = 4;                // K splits of the per-tile kernel for small f32 matrices
 
 __device__ __forceinline__ void cp_async16(void* smem_dst, const void* gsrc) {
   const uint32_t d = static_cast<uint32_t>(__cvta_generic_to_shared(smem_dst));
@@ -617,15 +645,15 @@ bool make_map(CUtensorMap* map, const void* base, int64_t rows, int64_t k, int b
                 CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-template <bool F32W, int TW>
+template <bool F32W, int TW, int KS = 1>
 cudaError_t launch_np(cudaLaunchConfig_t& cfg, int np, const void* w, const __nv_bfloat16* xp, float* y, int n, int k,
                       int t) {
   switch (np) {
-    case 1: return ::bt::launch_ex(&cfg, linear_rows_kernel<F32W, 1, TW>, w, xp, y, n, k, t);
-    case 2: return ::bt::launch_ex(&cfg, linear_rows_kernel<F32W, 2, TW>, w, xp, y, n, k, t);
-    case 4: return ::bt::launch_ex(&cfg, linear_rows_kernel<F32W, 4, TW>, w, xp, y, n, k, t);
+    case 1: return ::bt::launch_ex(&cfg, linear_rows_kernel<F32W, 1, TW, KS>, w, xp, y, n, k, t);
+    case 2: return ::bt::launch_ex(&cfg, linear_rows_kernel<F32W, 2, TW, KS>, w, xp, y, n, k, t);
+    case 4: return ::bt::launch_ex(&cfg, linear_rows_kernel<F32W, 4, TW, KS>, w, xp, y, n, k, t);
     default:  // two tiles per warp stop at 4 passes (the reduction's shared memory)
-      return ::bt::launch_ex(&cfg, linear_rows_kernel<F32W, (TW == 2 ? 4 : 8), TW>, w, xp, y, n, k, t);
+      return ::bt::launch_ex(&cfg, linear_rows_kernel<F32W, (TW == 2 ? 4 : 8), TW, KS>, w, xp, y, n, k, t);
   }
 }
 
@@ -754,13 +782,27 @@ int linear_rows(const void* w, int w_dtype, const void* x_planes, float* y, int6
   const int tw = (w_dtype == BT_BF16 && tiles % 2 == 0 && tiles / 2 >= want / 2 && passes > 1) ? 2 : 1;
   int np = tw == 2 ? 4 : 8;
   while (np > 1 && (np > passes || tiles / tw * ((passes + np - 1) / np) < want)) np >>= 1;
-  cudaLaunchAttribute attr[1];
+  // f32 weights that leave most SMs idle (the router and GDN beta/alpha rows
+  // of a batch): K split over a cluster of kF32Splits CTAs, so each CTA's
+  // serial K loop is that much shorter
+  const int64_t blocks = tiles / tw * ((passes + np - 1) / np);
+  const bool ksplit = w_dtype == BT_F32 && blocks < want && k % (kF32Splits * kWarps * 32) == 0;
+  cudaLaunchAttribute attr[2];
   cudaLaunchConfig_t cfg = pdl_config(
-      dim3(static_cast<unsigned>(tiles / tw), static_cast<unsigned>((passes + np - 1) / np)), stream, attr);
+      dim3(static_cast<unsigned>(tiles / tw), static_cast<unsigned>((passes + np - 1) / np), ksplit ? kF32Splits : 1),
+      stream, attr);
+  if (ksplit) {
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = 1;
+    attr[1].val.clusterDim.y = 1;
+    attr[1].val.clusterDim.z = kF32Splits;
+    cfg.numAttrs = 2;
+  }
   const int nn = static_cast<int>(n), kk = static_cast<int>(k), tt = static_cast<int>(t);
-  const cudaError_t e = w_dtype == BT_F32 ? launch_np<true, 1>(cfg, np, w, xp, y, nn, kk, tt)
-                        : tw == 2         ? launch_np<false, 2>(cfg, np, w, xp, y, nn, kk, tt)
-                                          : launch_np<false, 1>(cfg, np, w, xp, y, nn, kk, tt);
+  const cudaError_t e = ksplit                 ? launch_np<true, 1, kF32Splits>(cfg, np, w, xp, y, nn, kk, tt)
+                        : w_dtype == BT_F32    ? launch_np<true, 1>(cfg, np, w, xp, y, nn, kk, tt)
+                        : tw == 2              ? launch_np<false, 2>(cfg, np, w, xp, y, nn, kk, tt)
+                                               : launch_np<false, 1>(cfg, np, w, xp, y, nn, kk, tt);
   if (e != cudaSuccess) return fail_cuda(e, "linear_rows launch");
   return BT_OK;
 }

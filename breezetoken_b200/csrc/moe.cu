@@ -192,19 +192,32 @@ __global__ void repack_iq3s_kernel(const uint8_t* __restrict__ src, uint8_t* __r
 // ------------------------------------------------------------------ route
 // One warp per token: softmax over the expert logits (f32), top-k by
 // repeated warp argmax (ties -> lower id), renormalised weights.
+// One warp per token; lane l holds the logits of experts l, l + 32, ... in
+// registers (PL of them), so the max, the softmax sum and the top-k rounds
+// read global memory once.
+template <int PL>
 __global__ void moe_route_kernel(const float* __restrict__ logits, int64_t t, int n_experts, int top_k,
                                  int32_t* __restrict__ ids, float* __restrict__ weights) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t tok = blockIdx.x * static_cast<int64_t>(blockDim.x >> 5) + warp;
   if (tok >= t) return;
   const float* lg = logits + tok * n_experts;
+  float v[PL];
+#pragma unroll
+  for (int i = 0; i < PL; ++i) {
+    const int e = lane + 32 * i;
+    v[i] = e < n_experts ? lg[e] : -INFINITY;
+  }
   float m = -INFINITY;
-  for (int e = lane; e < n_experts; e += 32) m = fmaxf(m, lg[e]);
+#pragma unroll
+  for (int i = 0; i < PL; ++i) m = fmaxf(m, v[i]);
   m = warp_max(m);
   float s = 0.f;
-  for (int e = lane; e < n_experts; e += 32) s += expf(lg[e] - m);
+#pragma unroll
+  for (int i = 0; i < PL; ++i)
+    if (lane + 32 * i < n_experts) s += expf(v[i] - m);
   s = warp_sum(s);
-  // selection state: bit set = taken (n_experts <= 32 * 32)
+  // selection state: bit i set = expert lane + 32 i taken
   uint32_t taken = 0;
   float sel[16];
   int sid[16];
@@ -212,11 +225,12 @@ __global__ void moe_route_kernel(const float* __restrict__ logits, int64_t t, in
   for (int k = 0; k < top_k && k < 16; ++k) {
     float best = -INFINITY;
     int bid = 0x7fffffff;
-    for (int e = lane, i = 0; e < n_experts; e += 32, ++i) {
-      if ((taken >> i) & 1u) continue;
-      const float v = lg[e];
-      if (v > best || (v == best && e < bid)) {
-        best = v;
+#pragma unroll
+    for (int i = 0; i < PL; ++i) {
+      const int e = lane + 32 * i;
+      if (e >= n_experts || ((taken >> i) & 1u)) continue;
+      if (v[i] > best || (v[i] == best && e < bid)) {
+        best = v[i];
         bid = e;
       }
     }
@@ -1589,8 +1603,14 @@ int moe_route(const float* logits, int64_t t, int64_t n_experts, int top_k, int3
                 static_cast<long long>(n_experts), top_k);
   if (t == 0) return BT_OK;
   const int blocks = static_cast<int>((t + 7) / 8);
+  const int ne = static_cast<int>(n_experts);
   ::bt::note_launch();
-  moe_route_kernel<<<blocks, 256, 0, stream>>>(logits, t, static_cast<int>(n_experts), top_k, ids, weights);
+  if (ne <= 64)
+    moe_route_kernel<2><<<blocks, 256, 0, stream>>>(logits, t, ne, top_k, ids, weights);
+  else if (ne <= 256)
+    moe_route_kernel<8><<<blocks, 256, 0, stream>>>(logits, t, ne, top_k, ids, weights);
+  else
+    moe_route_kernel<32><<<blocks, 256, 0, stream>>>(logits, t, ne, top_k, ids, weights);
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return fail_cuda(e, "moe_route launch");
   return BT_OK;

@@ -150,6 +150,32 @@ def test_linear_rows_matches_f64(cuda, dtype, t) -> None:
     assert (np.abs(y.cpu().double().numpy() - want) <= 2e-6 * bound).all()
 
 
+@pytest.mark.parametrize("n,t", [(256, 64), (64, 64), (64, 9), (256, 130)])
+def test_linear_rows_f32_cluster_split_matches_f64(cuda, n, t) -> None:
+    """f32 weight rows of the router / GDN beta-alpha shapes (K = 2048) for a
+    batch: the K range split over a cluster of CTAs whose sums are added in
+    rank order: within 2e-6 of sum |x||w| of an f64 product and the same bits
+    on a second call."""
+    rng = np.random.default_rng(14)
+    k = 2048
+    w = torch.from_numpy(rng.standard_normal((n, k)).astype(np.float32) * 0.02)
+    x = torch.from_numpy(rng.standard_normal((t, k)).astype(np.float32))
+    wd, xd = w.cuda().contiguous(), x.cuda().contiguous()
+    planes = torch.empty(t, 3, k, dtype=torch.bfloat16, device="cuda")
+    N.call("bt_bf16_planes", xd.data_ptr(), planes.data_ptr(), t, k, 0)
+    ys = []
+    for _ in range(2):
+        y = torch.full((t, n), float("nan"), device="cuda")
+        N.call("bt_linear_rows", wd.data_ptr(), N.BT_F32, planes.data_ptr(), y.data_ptr(), n, k, t, 0)
+        ys.append(y)
+    want = x.double().numpy() @ w.double().numpy().T
+    bound = np.abs(x.double().numpy()) @ np.abs(w.double().numpy()).T
+    got = ys[0].cpu().double().numpy()
+    assert np.isfinite(got).all()
+    assert (np.abs(got - want) <= 2e-6 * bound).all()
+    assert torch.equal(ys[0], ys[1])
+
+
 @pytest.mark.parametrize("t", [17, 32, 33, 64, 130])
 @pytest.mark.parametrize("n,k", [(64, 256), (192, 2048), (128, 256), (256, 2048), (512, 4096)])
 def test_linear_rows_tiled_matches_f64(cuda, t, n, k) -> None:
