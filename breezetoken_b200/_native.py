@@ -116,6 +116,7 @@ _SIGS: dict[str, tuple[object, list]] = {
     "bt_linear_kn": (C.c_int, [_P, C.c_int, _P, _P, _I64, _I64, _P]),
     "bt_bf16_planes": (C.c_int, [_P, _P, _I64, _I64, _P]),
     "bt_conv_silu": (C.c_int, [_P, _P, _P, _P, _I64, _I64, _I64, _P]),
+    "bt_conv_silu_scan": (C.c_int, [_P, _P, _P, _P, _I64, _I64, _I64, _I64, _P]),
     "bt_linear_rows": (C.c_int, [_P, C.c_int, _P, _P, _I64, _I64, _I64, _P]),
     "bt_linear_rows_timeouts": (C.c_int, []),
     "bt_launch_count": (C.c_longlong, []),
@@ -142,6 +143,10 @@ _SIGS: dict[str, tuple[object, list]] = {
                                         _I64, _I64, _I64, C.c_float, C.c_float, _P]),
     "bt_gdn_gated_step": (C.c_int, [_P, _I64, _P, _I64, _P, _P, _P, _P, _I64, _P, _P, _I64, _I64, _I64, _I64,
                                     C.c_float, C.c_float, C.c_float, _P]),
+    "bt_gdn_gated_scan": (C.c_int, [_P, _I64, _P, _I64, _P, _P, _P, _P, _I64, _P, _P, _I64, _I64, _I64, _I64, _I64,
+                                    C.c_float, C.c_float, C.c_float, _P]),
+    "bt_gdn_prefill": (C.c_int, [_P, _P, _P, C.c_int, _I64, _I64, _I64, _I64, _I64, _I64, _P, _I64, _I64, _P, _I64,
+                                 _I64, _P, _P, _I64, _I64, _I64, _I64, _I64, _I64, _I64, C.c_float, C.c_float, _P]),
     "bt_add_rms_norm_planes": (C.c_int, [_P, _P, _P, _P, _P, _P, _I64, _I64, C.c_float, _P]),
     "bt_argmax_workspace_bytes": (_I64, [_I64]),
     "bt_iq3s_row_bytes": (_I64, [_I64]),

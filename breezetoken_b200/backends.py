@@ -297,6 +297,40 @@ class B200Backend:
         )
         return out
 
+    def gdn_prefill(self, q, k, v, g, beta, state, scale, eps=1e-6):
+        """The prompt loop of model/prefill.py:106-110 in one launch:
+        ``gdn_decode(q[t], k[t], v[t], g[t], beta[t], state, ...)`` for t = 0 ..
+        S-1 in order, with the state kept on chip between tokens.  q/k:
+        (S, key_heads, dim), v: (S, value_heads, dim), g/beta: (S,
+        value_heads); ``state`` (value_heads, dim, dim) f32 is updated in
+        place; returns o (S, value_heads, dim) f32.  dim must be 128."""
+        if q.shape != k.shape or q.ndim != 3 or v.ndim != 3 or v.shape[0] != q.shape[0]:
+            raise ValueError("q/k must be (steps, key_heads, dim); v must be (steps, value_heads, dim)")
+        steps, heads_k, dim = q.shape
+        heads_v = v.shape[1]
+        if heads_v % heads_k or v.shape[2] != dim:
+            raise ValueError("value_heads must be a multiple of key_heads, with the same dim")
+        if g.shape != (steps, heads_v) or beta.shape != (steps, heads_v):
+            raise ValueError(f"g and beta must be {(steps, heads_v)}")
+        if state.shape != (heads_v, dim, dim):
+            raise ValueError(f"state shape {tuple(state.shape)} != {(heads_v, dim, dim)}")
+        if state.dtype != torch.float32 or not state.is_contiguous():
+            raise ValueError("gdn_prefill state must be contiguous float32 (it is updated in place)")
+        self._check(q, k, v, g, beta, state)
+        if q.dtype == k.dtype == v.dtype == torch.bfloat16:
+            qq, kk, vv, dt = q.contiguous(), k.contiguous(), v.contiguous(), N.BT_BF16
+        else:
+            qq, kk, vv, dt = self._f32(q), self._f32(k), self._f32(v), N.BT_F32
+        gg, bb = self._f32(g).contiguous(), self._f32(beta).contiguous()
+        out = torch.empty(steps, heads_v, dim, dtype=torch.float32, device=self.device)
+        nk, nv = heads_k * dim, heads_v * dim
+        N.call(
+            "bt_gdn_prefill", qq.data_ptr(), kk.data_ptr(), vv.data_ptr(), dt, 0, 0, 0, nk, nk, nv,
+            gg.data_ptr(), 0, heads_v, bb.data_ptr(), 0, heads_v, state.data_ptr(), out.data_ptr(), 0, nv,
+            steps, 1, heads_k, heads_v, dim, float(scale), float(eps), _stream(),
+        )
+        return out
+
     def argmax(self, x: torch.Tensor) -> torch.Tensor:
         """First-index argmax of each row (graph.py:88-91) as int32."""
         xf = self._f32(x)

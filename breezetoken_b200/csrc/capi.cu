@@ -153,7 +153,12 @@ int bt_linear_kn(const void* w, int w_dtype, const float* x, float* y, int64_t k
 
 int bt_conv_silu(const float* entry, float* state, const float* w, float* out, int64_t batch, int64_t channels,
                  int64_t taps, void* stream) {
-  return bt::conv_silu(entry, state, w, out, batch, channels, taps, as_stream(stream));
+  return bt::conv_silu(entry, state, w, out, 1, batch, channels, taps, as_stream(stream));
+}
+
+int bt_conv_silu_scan(const float* entry, float* state, const float* w, float* out, int64_t steps, int64_t batch,
+                      int64_t channels, int64_t taps, void* stream) {
+  return bt::conv_silu(entry, state, w, out, steps, batch, channels, taps, as_stream(stream));
 }
 
 int bt_bf16_planes(const float* x, void* planes, int64_t t, int64_t k, void* stream) {
@@ -285,9 +290,19 @@ int bt_gdn_gated_step(const float* mixed, int64_t mixed_bs, const float* ba, int
                       const float* dt_bias, float* state, const float* z, int64_t z_bs, const float* norm_w,
                       void* planes, int64_t batch, int64_t heads_k, int64_t heads_v, int64_t dim, float scale,
                       float l2_eps, float norm_eps, void* stream) {
-  if (batch < 1 || batch > (1LL << 24) || heads_k < 1 || heads_k > 65535 || heads_v < 1 || heads_v > 65535)
+  return bt_gdn_gated_scan(mixed, mixed_bs, ba, ba_bs, a_log, dt_bias, state, z, z_bs, norm_w, planes, 1, batch,
+                           heads_k, heads_v, dim, scale, l2_eps, norm_eps, stream);
+}
+
+int bt_gdn_gated_scan(const float* mixed, int64_t mixed_bs, const float* ba, int64_t ba_bs, const float* a_log,
+                      const float* dt_bias, float* state, const float* z, int64_t z_bs, const float* norm_w,
+                      void* planes, int64_t steps, int64_t batch, int64_t heads_k, int64_t heads_v, int64_t dim,
+                      float scale, float l2_eps, float norm_eps, void* stream) {
+  if (batch < 1 || batch > (1LL << 24) || heads_k < 1 || heads_k > 65535 || heads_v < 1 || heads_v > 65535 ||
+      steps < 1 || steps * batch > 0x7fffffffLL)
     return fail(BT_ERR_INVALID, "gdn gated step: shape out of range");
   bt::GdnStepParams p{};
+  p.steps = static_cast<int32_t>(steps);
   p.mixed = mixed;
   p.mixed_bs = mixed_bs;
   p.ba = ba;
@@ -319,6 +334,50 @@ int bt_gdn_decode(const void* q, const void* k, const void* v, int in_dtype, con
                   float eps, void* stream) {
   return bt_gdn_decode_strided(q, k, v, in_dtype, heads_k * dim, heads_k * dim, heads_v * dim, g, heads_v, beta,
                                heads_v, state, out, heads_v * dim, batch, heads_k, heads_v, dim, scale, eps, stream);
+}
+
+int bt_gdn_prefill(const void* q, const void* k, const void* v, int in_dtype, int64_t q_bs, int64_t k_bs,
+                   int64_t v_bs, int64_t q_ts, int64_t k_ts, int64_t v_ts, const float* g, int64_t g_bs, int64_t g_ts,
+                   const float* beta, int64_t beta_bs, int64_t beta_ts, float* state, float* out, int64_t out_bs,
+                   int64_t out_ts, int64_t steps, int64_t batch, int64_t heads_k, int64_t heads_v, int64_t dim,
+                   float scale, float eps, void* stream) {
+  if (!q || !k || !v || !g || !beta || !state || !out) return fail(BT_ERR_INVALID, "gdn_prefill: null pointer");
+  if (steps < 0 || steps > 0x7fffffffLL || batch < 1 || heads_k < 1 || heads_v < 1 || dim < 1)
+    return fail(BT_ERR_INVALID, "gdn_prefill: bad shape");
+  if (q_bs < 0 || k_bs < 0 || v_bs < 0 || g_bs < 0 || beta_bs < 0 || out_bs < 0 || q_ts < 0 || k_ts < 0 ||
+      v_ts < 0 || g_ts < 0 || beta_ts < 0 || out_ts < 0)
+    return fail(BT_ERR_INVALID, "gdn_prefill: negative stride");
+  if (in_dtype != BT_F32 && in_dtype != BT_BF16) return fail(BT_ERR_UNSUPPORTED, "gdn_prefill: dtype %d", in_dtype);
+  bt::GdnParams p{};
+  p.q = q;
+  p.k = k;
+  p.v = v;
+  p.in_dtype = in_dtype;
+  p.q_bs = q_bs;
+  p.k_bs = k_bs;
+  p.v_bs = v_bs;
+  p.g = g;
+  p.beta = beta;
+  p.g_bs = g_bs;
+  p.beta_bs = beta_bs;
+  p.state = state;
+  p.out = out;
+  p.out_bs = out_bs;
+  p.batch = static_cast<int32_t>(std::min<int64_t>(batch, 0x7fffffffLL));
+  p.heads_k = static_cast<int32_t>(std::min<int64_t>(heads_k, 0x7fffffffLL));
+  p.heads_v = static_cast<int32_t>(std::min<int64_t>(heads_v, 0x7fffffffLL));
+  p.dim = static_cast<int32_t>(std::min<int64_t>(dim, 0x7fffffffLL));
+  p.scale = scale;
+  p.eps = eps;
+  bt::GdnScan sc{};
+  sc.len = static_cast<int32_t>(steps);
+  sc.tok_q = q_ts;
+  sc.tok_k = k_ts;
+  sc.tok_v = v_ts;
+  sc.tok_g = g_ts;
+  sc.tok_beta = beta_ts;
+  sc.tok_out = out_ts;
+  return bt::gdn_prefill_launch(p, sc, as_stream(stream));
 }
 
 int bt_gdn_decode_strided(const void* q, const void* k, const void* v, int in_dtype, int64_t q_bs, int64_t k_bs,

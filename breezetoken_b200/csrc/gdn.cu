@@ -208,6 +208,104 @@ __global__ void __launch_bounds__(kThreads) gdn_head_kernel(const __grid_constan
   }
 }
 
+// Prefill scan: the gated delta rule over `len` consecutive tokens of every
+// (sequence, value head), one CTA each, with the 128 x 128 state held in the
+// registers of its 256 threads for the whole scan (read once, written once)
+// instead of going through HBM once per token.  Token i's q / k / v / g /
+// beta sit `tok_*` elements after token i - 1's (the batch strides still
+// apply), its output o_i tok_out after o_{i-1}.  Per token the arithmetic is
+// gdn_head_kernel's, in the same order, so L scanned tokens give the same
+// bits as L steps of the one-CTA-per-head decode.  The next token's inputs
+// are loaded while the current one computes.
+template <typename T>
+__global__ void __launch_bounds__(kThreads) gdn_prefill_kernel(const __grid_constant__ GdnParams p,
+                                                               const __grid_constant__ GdnScan sc) {
+  __shared__ float sq[kHeadDim], sk[kHeadDim], red[kHeadHalves][kHeadDim];
+  __shared__ float s_decay, s_bsig;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int c = tid % kHeadDim, half = tid / kHeadDim, r0 = half * kHeadRows;
+  const int hv = blockIdx.x % p.heads_v, b = blockIdx.x / p.heads_v;
+  const int hk = hv % p.heads_k;
+  float* S = p.state + (static_cast<int64_t>(b) * p.heads_v + hv) * kHeadDim * kHeadDim;
+  float s[kHeadRows];
+#pragma unroll
+  for (int i = 0; i < kHeadRows; ++i) s[i] = S[static_cast<int64_t>(r0 + i) * kHeadDim + c];
+  // the next token's inputs: warps 0 / 1 hold its q / k, thread 64 its g and
+  // beta logit, every thread its v column
+  float vals[kHeadDim / 32];
+  float gv = 0.f, bv = 0.f, vv = 0.f;
+  auto load_token = [&](int i) {
+    if (warp < 2) {
+      const void* src = warp == 0 ? p.q : p.k;
+      const int64_t off = static_cast<int64_t>(b) * (warp == 0 ? p.q_bs : p.k_bs) +
+                          static_cast<int64_t>(i) * (warp == 0 ? sc.tok_q : sc.tok_k) +
+                          static_cast<int64_t>(hk) * kHeadDim;
+#pragma unroll
+      for (int j = 0; j < kHeadDim / 32; ++j) vals[j] = load_elem<T>(src, off + lane + 32 * j);
+    } else if (tid == 64) {
+      gv = p.g[static_cast<int64_t>(b) * p.g_bs + static_cast<int64_t>(i) * sc.tok_g + hv];
+      bv = p.beta[static_cast<int64_t>(b) * p.beta_bs + static_cast<int64_t>(i) * sc.tok_beta + hv];
+    }
+    vv = load_elem<T>(p.v, static_cast<int64_t>(b) * p.v_bs + static_cast<int64_t>(i) * sc.tok_v +
+                               static_cast<int64_t>(hv) * kHeadDim + c);
+  };
+  if (sc.len > 0) load_token(0);
+  for (int i = 0; i < sc.len; ++i) {
+    // every thread has passed the previous token's third barrier, after its
+    // last reads of sq / sk / s_decay / s_bsig, so they are free to overwrite
+    if (warp < 2) {  // normalised q (x scale) and k
+      float ss = 0.f;
+#pragma unroll
+      for (int j = 0; j < kHeadDim / 32; ++j) ss = fmaf(vals[j], vals[j], ss);
+      ss = warp_sum(ss);
+      const float r = 1.0f / sqrtf(ss + p.eps);
+      float* dst = warp == 0 ? sq : sk;
+#pragma unroll
+      for (int j = 0; j < kHeadDim / 32; ++j)
+        dst[lane + 32 * j] = warp == 0 ? __fmul_rn(__fmul_rn(vals[j], r), p.scale) : __fmul_rn(vals[j], r);
+    } else if (tid == 64) {
+      s_decay = expf(gv);
+      s_bsig = sigmoid_f(bv);
+    }
+    const float v_now = vv;
+    __syncthreads();
+    if (i + 1 < sc.len) load_token(i + 1);  // in flight while this token computes
+    const float decay = s_decay, bsig = s_bsig;
+    float rec = 0.f;
+#pragma unroll
+    for (int j = 0; j < kHeadRows; ++j) {
+      s[j] = __fmul_rn(s[j], decay);
+      rec = fmaf(s[j], sk[r0 + j], rec);
+    }
+    red[half][c] = rec;
+    __syncthreads();
+    float recalled = 0.f;
+#pragma unroll
+    for (int h = 0; h < kHeadHalves; ++h) recalled += red[h][c];
+    const float delta = __fmul_rn(v_now - recalled, bsig);
+    float o = 0.f;
+#pragma unroll
+    for (int j = 0; j < kHeadRows; ++j) {
+      s[j] = __fadd_rn(s[j], __fmul_rn(sk[r0 + j], delta));
+      o = fmaf(s[j], sq[r0 + j], o);
+    }
+    __syncthreads();  // every thread has read red[][], sq and sk above
+    red[half][c] = o;
+    __syncthreads();
+    if (half == 0) {
+      float t = 0.f;
+#pragma unroll
+      for (int h = 0; h < kHeadHalves; ++h) t += red[h][c];
+      p.out[static_cast<int64_t>(b) * p.out_bs + static_cast<int64_t>(i) * sc.tok_out +
+            static_cast<int64_t>(hv) * kHeadDim + c] = t;
+    }
+    // red[][] is next written after the next token's first barrier, which
+    // every thread reaches only after its reads above
+  }
+#pragma unroll
+  for (int j = 0; j < kHeadRows; ++j) S[static_cast<int64_t>(r0 + j) * kHeadDim + c] = s[j];
+}
+
 template <typename T>
 cudaError_t launch_dim(const GdnParams& p, cudaLaunchConfig_t& cfg) {
   switch (p.dim) {
@@ -218,6 +316,24 @@ cudaError_t launch_dim(const GdnParams& p, cudaLaunchConfig_t& cfg) {
 }
 
 }  // namespace
+
+int gdn_prefill_launch(const GdnParams& p, const GdnScan& sc, cudaStream_t stream) {
+  if (p.dim != kHeadDim) return fail(BT_ERR_UNSUPPORTED, "gdn_prefill serves head dim %d, got %d", kHeadDim, p.dim);
+  if (p.heads_k <= 0 || p.heads_v <= 0 || p.heads_v % p.heads_k != 0)
+    return fail(BT_ERR_INVALID, "gdn_prefill: value heads (%d) must be a positive multiple of key heads (%d)",
+                p.heads_v, p.heads_k);
+  if (p.batch <= 0 || sc.len < 0) return fail(BT_ERR_INVALID, "gdn_prefill: batch must be positive, steps >= 0");
+  if (static_cast<int64_t>(p.batch) * p.heads_v > (1LL << 31) - 1)
+    return fail(BT_ERR_UNSUPPORTED, "gdn_prefill: too many heads");
+  if (sc.len == 0) return BT_OK;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(p.batch) * p.heads_v);
+  cfg.blockDim = dim3(kThreads);
+  cfg.stream = stream;
+  const cudaError_t e = p.in_dtype == BT_BF16 ? ::bt::launch_ex(&cfg, gdn_prefill_kernel<__nv_bfloat16>, p, sc)
+                                              : ::bt::launch_ex(&cfg, gdn_prefill_kernel<float>, p, sc);
+  return e == cudaSuccess ? BT_OK : fail_cuda(e, "gdn_prefill launch");
+}
 
 int gdn_decode_launch(const GdnParams& p, cudaStream_t stream, bool pdl) {
   if (p.dim != 64 && p.dim != 128 && p.dim != 256)

@@ -25,4 +25,11 @@ struct GdnParams {
 
 int gdn_decode_launch(const GdnParams& p, cudaStream_t stream, bool pdl);
 
+// Token strides (elements) of the multi-token prefill scan over `len` tokens.
+struct GdnScan {
+  int32_t len;
+  int64_t tok_q, tok_k, tok_v, tok_g, tok_beta, tok_out;
+};
+int gdn_prefill_launch(const GdnParams& p, const GdnScan& sc, cudaStream_t stream);
+
 }  // namespace bt

@@ -697,14 +697,17 @@ int linear_rows(const void* w, int w_dtype, const void* x_planes, float* y, int6
   const auto* xp = static_cast<const __nv_bfloat16*>(x_planes);
   if (w_dtype == BT_BF16 && t > 16 && n % kUmmaRows == 0) {
     // tensor-core path: 64 tokens per CTA (32 for T <= 32); K split over a
-    // cluster as far as the CTAs still fit one wave of 1 per SM
+    // cluster as far as one token chunk's CTAs still fit one wave of 1 per
+    // SM.  The split depends on the rows and K only, not on T, so a token's
+    // outputs are the same bits whichever tokens share the call (a prefill
+    // chunk of many tokens per sequence gets the decode step's sums).
     const bool wide = t > 32;
     const int nt = wide ? 64 : 32;
     const int64_t blocks = n / kUmmaRows, chunks = (t + nt - 1) / nt;
     if (blocks > 2147483647LL || chunks > 65535)
       return fail(BT_ERR_UNSUPPORTED, "linear_rows: too many rows or tokens");
     int splits = 1;
-    while (splits < kMaxSplits && blocks * chunks * splits * 2 <= sm_count() && k % (kUmmaKStage * splits * 2) == 0)
+    while (splits < kMaxSplits && blocks * splits * 2 <= sm_count() && k % (kUmmaKStage * splits * 2) == 0)
       splits *= 2;
     cudaLaunchAttribute attr[2];
     cudaLaunchConfig_t cfg = pdl_config(
@@ -737,14 +740,13 @@ int linear_rows(const void* w, int w_dtype, const void* x_planes, float* y, int6
     return BT_OK;
   }
   if (w_dtype == BT_BF16 && t > 16 && n % kTileRows == 0) {
-    // tiled path: K split over a cluster as far as the blocks still fit one
-    // wave of 2 per SM
+    // tiled path: K split over a cluster as far as one token chunk's blocks
+    // still fit one wave of 2 per SM (rows and K decide it, not T)
     const int64_t blocks = n / kTileRows, chunks = (t + 63) / 64;
     if (blocks > 2147483647LL || chunks > 65535)
       return fail(BT_ERR_UNSUPPORTED, "linear_rows: too many rows or tokens");
     int splits = 1;
-    while (splits < kMaxSplits && blocks * chunks * splits * 2 <= 2 * sm_count() &&
-           k % (kKStage * splits * 2) == 0)
+    while (splits < kMaxSplits && blocks * splits * 2 <= 2 * sm_count() && k % (kKStage * splits * 2) == 0)
       splits *= 2;
     const bool wide = t > 32;  // 64 tokens per block, else 32
     cudaLaunchAttribute attr[2];
@@ -782,11 +784,11 @@ int linear_rows(const void* w, int w_dtype, const void* x_planes, float* y, int6
   const int tw = (w_dtype == BT_BF16 && tiles % 2 == 0 && tiles / 2 >= want / 2 && passes > 1) ? 2 : 1;
   int np = tw == 2 ? 4 : 8;
   while (np > 1 && (np > passes || tiles / tw * ((passes + np - 1) / np) < want)) np >>= 1;
-  // f32 weights that leave most SMs idle (the router and GDN beta/alpha rows
-  // of a batch): K split over a cluster of kF32Splits CTAs, so each CTA's
-  // serial K loop is that much shorter
-  const int64_t blocks = tiles / tw * ((passes + np - 1) / np);
-  const bool ksplit = w_dtype == BT_F32 && blocks < want && k % (kF32Splits * kWarps * 32) == 0;
+  // f32 weights of fewer tiles than a wave of blocks (the router and GDN
+  // beta/alpha rows): K split over a cluster of kF32Splits CTAs, so each
+  // CTA's serial K loop is that much shorter.  Decided by the rows alone, so
+  // a token's sums do not depend on T (as on the tensor-core path).
+  const bool ksplit = w_dtype == BT_F32 && tiles < want && k % (kF32Splits * kWarps * 32) == 0;
   cudaLaunchAttribute attr[2];
   cudaLaunchConfig_t cfg = pdl_config(
       dim3(static_cast<unsigned>(tiles / tw), static_cast<unsigned>((passes + np - 1) / np), ksplit ? kF32Splits : 1),

@@ -176,10 +176,11 @@ __global__ void rope_kernel(const float* __restrict__ x, const float* __restrict
 // Short causal conv of the GDN projection (model/qwen36_moe.py:465-468):
 // window = [state (K-1 taps) | entry], out = silu(sum_j window[j] * w[j])
 // (products rounded, summed in tap order), state <- window[1:].  One thread
-// per (sequence, channel).
+// per (sequence, channel), scanning `steps` tokens (token-major rows:
+// token s of sequence b at row s * batch + b) with the window in registers.
 __global__ void conv_silu_kernel(const float* __restrict__ entry, float* __restrict__ state,
-                                 const float* __restrict__ w, float* __restrict__ out, int64_t batch,
-                                 int64_t channels, int taps) {
+                                 const float* __restrict__ w, float* __restrict__ out, int64_t steps,
+                                 int64_t batch, int64_t channels, int taps) {
   const int64_t total = batch * channels;
   for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
        i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
@@ -187,11 +188,14 @@ __global__ void conv_silu_kernel(const float* __restrict__ entry, float* __restr
     float* st = state + i * (taps - 1);
     float win[8];
     for (int j = 0; j < taps - 1; ++j) win[j] = st[j];
-    win[taps - 1] = entry[i];
-    float acc = __fmul_rn(win[0], w[c * taps]);
-    for (int j = 1; j < taps; ++j) acc = __fadd_rn(acc, __fmul_rn(win[j], w[c * taps + j]));
-    out[i] = silu_f(acc);
-    for (int j = 0; j < taps - 1; ++j) st[j] = win[j + 1];
+    for (int64_t s = 0; s < steps; ++s) {
+      win[taps - 1] = entry[s * total + i];
+      float acc = __fmul_rn(win[0], w[c * taps]);
+      for (int j = 1; j < taps; ++j) acc = __fadd_rn(acc, __fmul_rn(win[j], w[c * taps + j]));
+      out[s * total + i] = silu_f(acc);
+      for (int j = 0; j < taps - 1; ++j) win[j] = win[j + 1];
+    }
+    for (int j = 0; j < taps - 1; ++j) st[j] = win[j];
   }
 }
 
@@ -320,12 +324,12 @@ int rope(const float* x, const float* cos_t, const float* sin_t, const int32_t* 
   return check_launch("rope");
 }
 
-int conv_silu(const float* entry, float* state, const float* w, float* out, int64_t batch, int64_t channels,
-              int64_t taps, cudaStream_t stream) {
-  if (!entry || !state || !w || !out || batch < 1 || channels < 1 || taps < 2 || taps > 8)
-    return fail(BT_ERR_INVALID, "conv_silu: bad arguments (taps in [2, 8])");
+int conv_silu(const float* entry, float* state, const float* w, float* out, int64_t steps, int64_t batch,
+              int64_t channels, int64_t taps, cudaStream_t stream) {
+  if (!entry || !state || !w || !out || steps < 1 || batch < 1 || channels < 1 || taps < 2 || taps > 8)
+    return fail(BT_ERR_INVALID, "conv_silu: bad arguments (steps >= 1, taps in [2, 8])");
   ::bt::note_launch();
-  conv_silu_kernel<<<grid_for(batch * channels, 256), 256, 0, stream>>>(entry, state, w, out, batch, channels,
+  conv_silu_kernel<<<grid_for(batch * channels, 256), 256, 0, stream>>>(entry, state, w, out, steps, batch, channels,
                                                                           static_cast<int>(taps));
   return check_launch("conv_silu");
 }

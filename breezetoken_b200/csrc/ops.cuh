@@ -19,7 +19,7 @@ int silu_mul(const float* g, const float* u, float* y, int64_t n, cudaStream_t s
 int rope(const float* x, const float* cos_t, const float* sin_t, const int32_t* pos, float* y, int64_t rows,
          int64_t dim, int64_t rope_dim, int64_t cap, cudaStream_t stream);
 int argmax(const float* x, int64_t rows, int64_t n, int32_t* out, void* workspace, cudaStream_t stream);
-int conv_silu(const float* entry, float* state, const float* w, float* out, int64_t batch, int64_t channels,
-              int64_t taps, cudaStream_t stream);
+int conv_silu(const float* entry, float* state, const float* w, float* out, int64_t steps, int64_t batch,
+              int64_t channels, int64_t taps, cudaStream_t stream);
 
 }  // namespace bt

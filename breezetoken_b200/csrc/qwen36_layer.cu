@@ -12,7 +12,10 @@
 // rows; the column sums S^T k and S^T q add the two row halves in shared
 // memory, and the gated norm's sum of squares is one block reduction.  It
 // replaces the separate decay arithmetic, recurrence, norm, SiLU, product and
-// plane-split launches of the unfused layer.
+// plane-split launches of the unfused layer.  With steps > 1 the same CTA
+// scans `steps` consecutive tokens of its sequence (a prefill chunk, token
+// major) with the state kept in registers throughout: the per-token
+// arithmetic is the decode step's, the state is read and written once.
 //
 // add_rms_norm_planes_kernel: h = a + b; y = rms_norm(h) * w
 // (backends.py:229-238) and y's three bf16 planes (y = hi + mid + lo) in the
@@ -67,73 +70,95 @@ __global__ void __launch_bounds__(kGdnStepThreads) gdn_gated_step_kernel(const _
 #pragma unroll
   for (int i = 0; i < R; ++i) s[i] = S[static_cast<int64_t>(r0 + i) * DIM + c];
 
-  const float* row = p.mixed + static_cast<int64_t>(b) * p.mixed_bs;
-  if (warp < 2) {  // L2-normalised q (x scale) and k of key head hk
-    const float* src = row + (warp == 0 ? 0 : static_cast<int64_t>(p.heads_k) * DIM) + static_cast<int64_t>(hk) * DIM;
-    float vals[DIM / 32];
-    float ss = 0.f;
+  // The inputs of token j of sequence b sit in row j * batch + b of mixed,
+  // ba and z; they are loaded one token ahead: warps 0 / 1 hold q / k, thread
+  // 64 the beta and alpha logits, every thread its v column, the threads of
+  // row group 0 their z column.
+  float vals[DIM / 32];
+  float beta_l = 0.f, alpha_l = 0.f, vv = 0.f, zz = 0.f;
+  auto load_token = [&](int j) {
+    const int64_t r = static_cast<int64_t>(j) * p.batch + b;
+    const float* row = p.mixed + r * p.mixed_bs;
+    if (warp < 2) {
+      const float* src = row + (warp == 0 ? 0 : static_cast<int64_t>(p.heads_k) * DIM) + static_cast<int64_t>(hk) * DIM;
 #pragma unroll
-    for (int i = 0; i < DIM / 32; ++i) {
-      vals[i] = src[lane + 32 * i];
-      ss = fmaf(vals[i], vals[i], ss);
+      for (int i = 0; i < DIM / 32; ++i) vals[i] = src[lane + 32 * i];
+    } else if (tid == 64) {
+      const float* ba = p.ba + r * p.ba_bs;
+      beta_l = ba[hv];
+      alpha_l = ba[p.heads_v + hv];
     }
-    ss = warp_sum(ss);
-    const float r = 1.0f / sqrtf(ss + p.l2_eps);
-    float* dst = warp == 0 ? sq : sk;
+    vv = row[static_cast<int64_t>(2 * p.heads_k) * DIM + static_cast<int64_t>(hv) * DIM + c];
+    if (half == 0) zz = p.z[r * p.z_bs + static_cast<int64_t>(hv) * DIM + c];
+  };
+  load_token(0);
+  for (int j = 0; j < p.steps; ++j) {
+    // every thread has passed this token's predecessor's block_total, after
+    // its last reads of sq / sk / s_decay / s_bsig, so they are free to overwrite
+    if (warp < 2) {  // L2-normalised q (x scale) and k of key head hk
+      float ss = 0.f;
 #pragma unroll
-    for (int i = 0; i < DIM / 32; ++i)
-      dst[lane + 32 * i] = warp == 0 ? __fmul_rn(__fmul_rn(vals[i], r), p.scale) : __fmul_rn(vals[i], r);
-  } else if (tid == 64) {
-    // decay: a * softplus(alpha + dt_bias) (model/qwen36_moe.py:474-476)
-    const float* ba = p.ba + static_cast<int64_t>(b) * p.ba_bs;
-    const float g = __fmul_rn(p.a_log[hv], softplus_f(__fadd_rn(ba[p.heads_v + hv], p.dt_bias[hv])));
-    s_decay = expf(g);
-    s_bsig = sigmoid_f(ba[hv]);
+      for (int i = 0; i < DIM / 32; ++i) ss = fmaf(vals[i], vals[i], ss);
+      ss = warp_sum(ss);
+      const float r = 1.0f / sqrtf(ss + p.l2_eps);
+      float* dst = warp == 0 ? sq : sk;
+#pragma unroll
+      for (int i = 0; i < DIM / 32; ++i)
+        dst[lane + 32 * i] = warp == 0 ? __fmul_rn(__fmul_rn(vals[i], r), p.scale) : __fmul_rn(vals[i], r);
+    } else if (tid == 64) {
+      // decay: a * softplus(alpha + dt_bias) (model/qwen36_moe.py:474-476)
+      const float g = __fmul_rn(p.a_log[hv], softplus_f(__fadd_rn(alpha_l, p.dt_bias[hv])));
+      s_decay = expf(g);
+      s_bsig = sigmoid_f(beta_l);
+    }
+    const float v_now = vv, z_now = zz;
+    __syncthreads();
+    if (j + 1 < p.steps) load_token(j + 1);  // in flight while this token computes
+    const float decay = s_decay, bsig = s_bsig;
+    float rec = 0.f;
+#pragma unroll
+    for (int i = 0; i < R; ++i) {
+      s[i] = __fmul_rn(s[i], decay);
+      rec = fmaf(s[i], sk[r0 + i], rec);
+    }
+    red[half][c] = rec;
+    __syncthreads();
+    float recalled = 0.f;
+#pragma unroll
+    for (int h = 0; h < HALF; ++h) recalled += red[h][c];
+    const float delta = __fmul_rn(v_now - recalled, bsig);
+    float o = 0.f;
+#pragma unroll
+    for (int i = 0; i < R; ++i) {
+      s[i] = __fadd_rn(s[i], __fmul_rn(sk[r0 + i], delta));
+      o = fmaf(s[i], sq[r0 + i], o);
+    }
+    __syncthreads();  // every thread has read red[][] above
+    red[half][c] = o;
+    __syncthreads();
+    float out = 0.f;
+#pragma unroll
+    for (int h = 0; h < HALF; ++h) out += red[h][c];
+    // gated norm: rms_norm(o) * w * silu(z) over the head's DIM outputs
+    // (threads of row group 0 hold one output each; the others add zero);
+    // block_total's first barrier also orders the reads of red[][] above
+    // before the next token's writes
+    const float total = block_total<DIM>(half == 0 ? out * out : 0.f, scratch);
+    if (half == 0) {
+      const float r = 1.0f / sqrtf(total / static_cast<float>(DIM) + p.norm_eps);
+      const float y = __fmul_rn(__fmul_rn(__fmul_rn(out, r), p.norm_w[c]), silu_f(z_now));
+      float hi, mid, lo;
+      split3(y, hi, mid, lo);
+      const int64_t width = static_cast<int64_t>(p.heads_v) * DIM;
+      __nv_bfloat16* dst = static_cast<__nv_bfloat16*>(p.planes) +
+                           (static_cast<int64_t>(j) * p.batch + b) * 3 * width + static_cast<int64_t>(hv) * DIM + c;
+      dst[0] = __float2bfloat16_rn(hi);
+      dst[width] = __float2bfloat16_rn(mid);
+      dst[2 * width] = __float2bfloat16_rn(lo);
+    }
   }
-  __syncthreads();
-  const float decay = s_decay, bsig = s_bsig;
-  float rec = 0.f;
 #pragma unroll
-  for (int i = 0; i < R; ++i) {
-    s[i] = __fmul_rn(s[i], decay);
-    rec = fmaf(s[i], sk[r0 + i], rec);
-  }
-  red[half][c] = rec;
-  __syncthreads();
-  float recalled = 0.f;
-#pragma unroll
-  for (int h = 0; h < HALF; ++h) recalled += red[h][c];
-  const float vv = row[static_cast<int64_t>(2 * p.heads_k) * DIM + static_cast<int64_t>(hv) * DIM + c];
-  const float delta = __fmul_rn(vv - recalled, bsig);
-  float o = 0.f;
-#pragma unroll
-  for (int i = 0; i < R; ++i) {
-    s[i] = __fadd_rn(s[i], __fmul_rn(sk[r0 + i], delta));
-    S[static_cast<int64_t>(r0 + i) * DIM + c] = s[i];
-    o = fmaf(s[i], sq[r0 + i], o);
-  }
-  __syncthreads();  // every thread has read red[][] above
-  red[half][c] = o;
-  __syncthreads();
-  float out = 0.f;
-#pragma unroll
-  for (int h = 0; h < HALF; ++h) out += red[h][c];
-  // gated norm: rms_norm(o) * w * silu(z) over the head's DIM outputs
-  // (threads of row group 0 hold one output each; the others add zero)
-  const float total = block_total<DIM>(half == 0 ? out * out : 0.f, scratch);
-  if (half == 0) {
-    const float r = 1.0f / sqrtf(total / static_cast<float>(DIM) + p.norm_eps);
-    const float zz = p.z[static_cast<int64_t>(b) * p.z_bs + static_cast<int64_t>(hv) * DIM + c];
-    const float y = __fmul_rn(__fmul_rn(__fmul_rn(out, r), p.norm_w[c]), silu_f(zz));
-    float hi, mid, lo;
-    split3(y, hi, mid, lo);
-    const int64_t width = static_cast<int64_t>(p.heads_v) * DIM;
-    __nv_bfloat16* dst = static_cast<__nv_bfloat16*>(p.planes) + static_cast<int64_t>(b) * 3 * width +
-                         static_cast<int64_t>(hv) * DIM + c;
-    dst[0] = __float2bfloat16_rn(hi);
-    dst[width] = __float2bfloat16_rn(mid);
-    dst[2 * width] = __float2bfloat16_rn(lo);
-  }
+  for (int i = 0; i < R; ++i) S[static_cast<int64_t>(r0 + i) * DIM + c] = s[i];
 }
 
 // One block per row, n % 8 == 0.  Rows of up to 8 * 256 elements are read
@@ -211,6 +236,7 @@ __global__ void __launch_bounds__(256) add_rms_norm_planes_kernel(const float* _
 int gdn_gated_step_launch(const GdnStepParams& p, cudaStream_t stream) {
   if (!p.mixed || !p.ba || !p.a_log || !p.dt_bias || !p.state || !p.z || !p.norm_w || !p.planes)
     return fail(BT_ERR_INVALID, "gdn gated step: null pointer");
+  if (p.steps < 1) return fail(BT_ERR_INVALID, "gdn gated step: steps must be >= 1");
   if (p.batch < 1 || p.heads_k < 1 || p.heads_v < 1 || p.heads_v % p.heads_k)
     return fail(BT_ERR_INVALID, "gdn gated step: value heads must be a positive multiple of key heads");
   if (p.dim != 128) return fail(BT_ERR_UNSUPPORTED, "gdn gated step serves head dim 128, got %d", p.dim);

@@ -9,15 +9,21 @@ residual add, RMSNorm and bf16 plane split of each activation
 bt_linear_rows); the attention layer after its one stacked [q | gate, k, v]
 projection (q/k norms, RoPE, KV writes, split-KV attention, sigmoid gate:
 bt_attention_layer); the GDN mixer after its projections and short conv
-(decay, gated delta rule, output norm and SiLU gate: bt_gdn_gated_step);
+(decay, gated delta rule, output norm and SiLU gate: bt_gdn_gated_scan);
 routing, IQ3_S experts + shared expert and argmax.  Only the embedding row
 gather and the graph's token/position bookkeeping are torch device ops.
 
 B sequences decode in lockstep at one position (how the 35B-A3B benchmark's 64
-sequences per GPU run).  Prompts are fed token by token: the reference
-switches to a batched prefill with bf16 expert math for prompts of 8 or more
-tokens (_prefill_batch, :588-612), which this mirror does not reproduce.
-Everything raises on an unsupported shape or a missing library.
+sequences per GPU run).  prefill() consumes the B prompts in chunks of
+several tokens per sequence (the batched prefill of _prefill_batch,
+:588-612): projections, norms and MoE layers run once per chunk, the conv,
+the GDN recurrence (bt_gdn_gated_scan, state on chip across the chunk) and
+attention go through the chunk's tokens in order.  Its arithmetic is the
+per-token path's f32 (the reference's batched prefill rounds the expert
+inputs and weights to bf16, _moe_batch :536-586; this one does not), so a
+chunked prefill and a token-by-token one agree to f32 rounding.  generate()
+feeds its prompt token by token like forward_token.  Everything raises on an
+unsupported shape or a missing library.
 """
 
 from __future__ import annotations
@@ -339,54 +345,72 @@ class Qwen36Moe:
                float(self.cfg.eps), _stream())
         return h, y, planes
 
-    def _attn(self, i: int, xp: torch.Tensor, pos_t: torch.Tensor) -> torch.Tensor:
+    def _attn(self, i: int, xp: torch.Tensor, pos_t: torch.Tensor, steps: int = 1) -> torch.Tensor:
         """model/qwen36_moe.py:432-457: one projection of [q | gate, k, v], then
         q/k norms, RoPE at the device positions, the KV writes, attention and
-        the sigmoid gate in one launch (bt_attention_layer)."""
+        the sigmoid gate in one launch (bt_attention_layer) per token.
+
+        With steps > 1 (a prefill chunk, model/qwen36_moe.py:394-430) xp holds
+        steps * B token-major rows and pos_t (steps, B) their positions: the
+        projections run once over the chunk, then one launch per token in
+        order, each writing its K/V before the next token attends, which is
+        the causal attention over the chunk and the cached prefix."""
         cfg, layer = self.cfg, self.layers[i]
-        b, H, D = xp.shape[0], cfg.n_heads, cfg.head_dim
+        t, H, D = xp.shape[0], cfg.n_heads, cfg.head_dim
+        b = t // steps
         proj = self._lin(layer["qkv_all"], xp)
         k_cache, v_cache = self.kv[i]
-        out = torch.empty(b, H, D, dtype=torch.float32, device=self.device)
-        N.call("bt_attention_layer", proj.data_ptr(), proj.shape[1], layer["q_norm"].data_ptr(),
-               layer["k_norm"].data_ptr(), self.rope_cos.data_ptr(), self.rope_sin.data_ptr(), cfg.rope_dim,
-               pos_t.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), out.data_ptr(), b, H, cfg.n_kv, D,
-               cfg.max_context, float(D ** -0.5), float(cfg.eps), self._splits(), self._attn_ws.data_ptr(), None,
-               _stream())
-        return self._lin(layer["o"], self._planes(out.reshape(b, -1)))
+        out = torch.empty(t, H, D, dtype=torch.float32, device=self.device)
+        pos_t = pos_t.reshape(steps, b)
+        for j in range(steps):
+            N.call("bt_attention_layer", proj[j * b:].data_ptr(), proj.shape[1], layer["q_norm"].data_ptr(),
+                   layer["k_norm"].data_ptr(), self.rope_cos.data_ptr(), self.rope_sin.data_ptr(), cfg.rope_dim,
+                   pos_t[j].data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), out[j * b:].data_ptr(), b, H,
+                   cfg.n_kv, D, cfg.max_context, float(D ** -0.5), float(cfg.eps), self._splits(),
+                   self._attn_ws.data_ptr(), None, _stream())
+        return self._lin(layer["o"], self._planes(out.reshape(t, -1)))
 
-    def _gdn(self, i: int, xp: torch.Tensor) -> torch.Tensor:
+    def _gdn(self, i: int, xp: torch.Tensor, steps: int = 1) -> torch.Tensor:
         """model/qwen36_moe.py:459-483: the qkv projection and the short conv,
         the [beta | alpha] and z projections, then the decay, gated delta
-        rule, output norm and SiLU gate in one launch (bt_gdn_gated_step)."""
+        rule, output norm and SiLU gate in one launch (bt_gdn_gated_scan).
+
+        With steps > 1 (a prefill chunk, model/qwen36_moe.py:485-534) xp holds
+        steps * B token-major rows: the projections run once over the chunk,
+        the conv and the recurrence scan each sequence's tokens in order
+        (bt_conv_silu_scan, bt_gdn_gated_scan) with their state on chip."""
         cfg, layer = self.cfg, self.layers[i]
-        b, hk, hv, dk = xp.shape[0], cfg.gdn_key_heads, cfg.gdn_value_heads, cfg.gdn_k_dim
-        inner = cfg.gdn_inner
-        entry = self._lin(layer["qkv"], xp)  # (B, C)
+        t, hk, hv, dk = xp.shape[0], cfg.gdn_key_heads, cfg.gdn_value_heads, cfg.gdn_k_dim
+        b, inner = t // steps, cfg.gdn_inner
+        entry = self._lin(layer["qkv"], xp)  # (T, C)
         mixed = torch.empty_like(entry)
-        N.call("bt_conv_silu", entry.data_ptr(), self.conv_state[i].data_ptr(), layer["conv"].data_ptr(),
-               mixed.data_ptr(), b, cfg.conv_dim, cfg.gdn_conv, _stream())
+        N.call("bt_conv_silu_scan", entry.data_ptr(), self.conv_state[i].data_ptr(), layer["conv"].data_ptr(),
+               mixed.data_ptr(), steps, b, cfg.conv_dim, cfg.gdn_conv, _stream())
         ba = self._lin(layer["w_ba"], xp)  # [beta | alpha]
         z = self._lin(layer["z"], xp)
-        gated = torch.empty(b, 3, inner, dtype=torch.bfloat16, device=self.device)
-        N.call("bt_gdn_gated_step", mixed.data_ptr(), mixed.shape[1], ba.data_ptr(), 2 * hv,
+        gated = torch.empty(t, 3, inner, dtype=torch.bfloat16, device=self.device)
+        N.call("bt_gdn_gated_scan", mixed.data_ptr(), mixed.shape[1], ba.data_ptr(), 2 * hv,
                layer["a_log"].data_ptr(), layer["dt_bias"].data_ptr(), self.rec_state[i].data_ptr(), z.data_ptr(),
-               inner, layer["ssm_norm"].data_ptr(), gated.data_ptr(), b, hk, hv, dk, float(dk ** -0.5),
+               inner, layer["ssm_norm"].data_ptr(), gated.data_ptr(), steps, b, hk, hv, dk, float(dk ** -0.5),
                float(cfg.l2_eps), float(cfg.eps), _stream())
         return self._lin(layer["out"], gated)
 
-    def _moe(self, i: int, xn: torch.Tensor, xp: torch.Tensor) -> torch.Tensor:
+    def _moe(self, i: int, xn: torch.Tensor, xp: torch.Tensor, ws: torch.Tensor | None = None) -> torch.Tensor:
         layer = self.layers[i]
         r = route_logits(self._lin(layer["router"], xp), self.cfg.top_k)
         rec = getattr(self, "_route_record", None)
         if rec is not None:  # measurement: each layer's input and routing of this (eager) step
             rec.append((xn.clone(), r.expert_ids.clone(), r.weights.clone()))
-        return moe_forward(layer["experts"], layer["shared"], xn, r.expert_ids, r.weights, self._moe_ws)
+        return moe_forward(layer["experts"], layer["shared"], xn, r.expert_ids, r.weights,
+                           self._moe_ws if ws is None else ws)
 
     # ------------------------------------------------------------------ step
-    def _step_t(self, tokens: torch.Tensor, pos_t: torch.Tensor, logits: bool) -> torch.Tensor | None:
+    def _step_t(self, tokens: torch.Tensor, pos_t: torch.Tensor, logits: bool, steps: int = 1,
+                moe_ws: torch.Tensor | None = None) -> torch.Tensor | None:
         """One step with the positions as a device tensor (int32 (B,)): no
-        host synchronisation, so it can be captured in a CUDA graph."""
+        host synchronisation, so it can be captured in a CUDA graph.  With
+        steps > 1, `steps` tokens of each sequence at once (token-major
+        tokens and positions, steps * B rows): a prefill chunk."""
         cfg = self.cfg
         h = self.embd[tokens.long()].float()
         attn = set(cfg.attn_layers)
@@ -395,10 +419,10 @@ class Qwen36Moe:
             # each residual add runs fused with the norm that follows it
             # (h = h + delta, then rms_norm(h): the same f32 operations)
             layer = self.layers[i]
-            delta = self._attn(i, xp, pos_t) if i in attn else self._gdn(i, xp)
+            delta = self._attn(i, xp, pos_t, steps) if i in attn else self._gdn(i, xp, steps)
             h, xn, xp = self._norm_planes(h, delta, layer["norm_post"])
             nxt = self.layers[i + 1]["norm_in"] if i + 1 < cfg.n_layers else self.norm_f
-            h, xn, xp = self._norm_planes(h, self._moe(i, xn, xp), nxt)
+            h, xn, xp = self._norm_planes(h, self._moe(i, xn, xp, moe_ws), nxt)
         if not logits:
             return None
         return self._lin(self.head, xp)
@@ -479,16 +503,45 @@ class Qwen36Moe:
 
     # ----------------------------------------------------------- prefill
     @torch.inference_mode()
-    def prefill(self, prompts: torch.Tensor) -> None:
+    def prefill_chunk(self) -> int:
+        """Tokens per sequence that one prefill chunk carries: as many as keep
+        the chunk's expert pairs within one MoE launch (T * top_k <= 4096)."""
+        return max(1, 4096 // (self.cfg.top_k * self.batch))
+
+    @torch.inference_mode()
+    def prefill(self, prompts: torch.Tensor, chunk: int | None = None) -> None:
         """Consume prompts (B, L) at positions 0 .. L-1 in lockstep (no logits):
-        the next step feeds each sequence's next token at position L."""
+        the next step feeds each sequence's next token at position L.
+
+        The batched prefill of model/qwen36_moe.py:588-612, in chunks of
+        `chunk` tokens per sequence (default prefill_chunk()): each chunk runs
+        every projection, norm and MoE layer once over its chunk * B tokens,
+        and the conv, the GDN recurrence and attention scan the chunk's
+        tokens in order (bt_conv_silu_scan, bt_gdn_gated_scan, one
+        bt_attention_layer per token)."""
         if prompts.dim() != 2 or prompts.shape[0] != self.batch:
             raise ValueError(f"prompts must be ({self.batch}, L), got {tuple(prompts.shape)}")
-        if prompts.shape[1] > self.cfg.max_context:
+        n = prompts.shape[1]
+        if n > self.cfg.max_context:
             raise ValueError("prompt longer than max_context")
+        if n and (int(prompts.min()) < 0 or int(prompts.max()) >= self.cfg.vocab):
+            raise ValueError("token id outside the vocabulary")
+        c = self.prefill_chunk() if chunk is None else int(chunk)
+        if c < 1 or c * self.batch * self.cfg.top_k > 4096:
+            raise ValueError(f"chunk must be in [1, {self.prefill_chunk()}] tokens per sequence")
         toks = prompts.to(self.device)
-        for i in range(prompts.shape[1]):
-            self._step(toks[:, i], i, logits=False)
+        ws = None
+        if c > 1:
+            need = int(N.load().bt_moe_layer_workspace_bytes(c * self.batch, self.cfg.hidden, self.cfg.expert_ffn,
+                                                             self.cfg.shared_ffn, self.cfg.n_experts, self.cfg.top_k))
+            ws = getattr(self, "_moe_ws_prefill", None)
+            if ws is None or ws.numel() < need:
+                ws = self._moe_ws_prefill = torch.zeros(need, dtype=torch.uint8, device=self.device)
+        for j0 in range(0, n, c):
+            s = min(c, n - j0)
+            pos = torch.arange(j0, j0 + s, dtype=torch.int32, device=self.device)
+            pos_t = pos[:, None].expand(s, self.batch).contiguous()
+            self._step_t(toks[:, j0:j0 + s].t().reshape(-1), pos_t, False, s, ws)
 
     @torch.inference_mode()
     def snapshot(self) -> dict:

@@ -219,6 +219,23 @@ BT_API int bt_gdn_decode_strided(const void* q, const void* k, const void* v, in
                           int64_t heads_v, int64_t dim, float scale, float eps,
                           void* stream);
 
+/* The prefill loop of model/prefill.py:106-110 and
+ * model/qwen36_moe.py:520-530 (a gdn_decode step once per prompt token) as
+ * one launch: `steps` consecutive gated-delta-rule steps of each of `batch`
+ * sequences, with the state kept on chip between tokens (read and written
+ * once).  Element (token s, sequence b, head h, i) of q sits at
+ * s * q_ts + b * q_bs + h * dim + i, likewise k, v (k_ts, k_bs, v_ts,
+ * v_bs) and out (out_ts, out_bs); g and beta at s * g_ts + b * g_bs + h
+ * (beta_ts, beta_bs).  Each token's step is bt_gdn_decode's arithmetic.
+ * dim == 128 (the reference models' head size); steps == 0 is a no-op.  */
+BT_API int bt_gdn_prefill(const void* q, const void* k, const void* v, int in_dtype,
+                          int64_t q_bs, int64_t k_bs, int64_t v_bs, int64_t q_ts,
+                          int64_t k_ts, int64_t v_ts, const float* g, int64_t g_bs,
+                          int64_t g_ts, const float* beta, int64_t beta_bs, int64_t beta_ts,
+                          float* state, float* out, int64_t out_bs, int64_t out_ts,
+                          int64_t steps, int64_t batch, int64_t heads_k, int64_t heads_v,
+                          int64_t dim, float scale, float eps, void* stream);
+
 /* The GDN mixer of Qwen36Moe._gdn (model/qwen36_moe.py:459-483) from the
  * conv output on, for `batch` sequences, with dim == 128:
  *   mixed: row b (stride mixed_bs) = q (heads_k*dim) | k (heads_k*dim) |
@@ -236,6 +253,18 @@ BT_API int bt_gdn_gated_step(const float* mixed, int64_t mixed_bs, const float* 
                              int64_t heads_k, int64_t heads_v, int64_t dim, float scale, float l2_eps,
                              float norm_eps, void* stream);
 
+/* bt_gdn_gated_step over a prompt chunk of `steps` tokens per sequence
+ * (the GDN mixer of Qwen36Moe._gdn_batch, model/qwen36_moe.py:485-534,
+ * whose recurrence runs token by token): mixed, ba, z and planes hold
+ * steps * batch rows, token s of sequence b in row s * batch + b; each
+ * (sequence, head) scans its tokens in order with the state on chip, and
+ * each token's arithmetic is bt_gdn_gated_step's.                         */
+BT_API int bt_gdn_gated_scan(const float* mixed, int64_t mixed_bs, const float* ba, int64_t ba_bs,
+                             const float* a_log, const float* dt_bias, float* state, const float* z,
+                             int64_t z_bs, const float* norm_w, void* planes, int64_t steps,
+                             int64_t batch, int64_t heads_k, int64_t heads_v, int64_t dim,
+                             float scale, float l2_eps, float norm_eps, void* stream);
+
 /* bt_fused_add_rms_norm that also writes y's three bf16 planes (rows, 3, n)
  * (the form of bt_bf16_planes) in the same pass: h = a + b (b may be NULL:
  * then y = rms_norm(a) and h is not written), y = rms_norm(h, w, eps).
@@ -251,6 +280,16 @@ BT_API int bt_add_rms_norm_planes(const float* a, const float* b, const float* w
  * taps in [2, 8].                                                         */
 BT_API int bt_conv_silu(const float* entry, float* state, const float* w, float* out,
                  int64_t batch, int64_t channels, int64_t taps, void* stream);
+
+/* bt_conv_silu over `steps` consecutive tokens of every sequence, the
+ * prompt-chunk form of the batched prefill's conv1d over [state | entries]
+ * (model/qwen36_moe.py:493-501, model/prefill.py:90-93): entry and out are
+ * (steps, batch, channels), token s of sequence b in row s * batch + b;
+ * the state ends as the window after the last token.  Per token the same
+ * arithmetic as bt_conv_silu.                                             */
+BT_API int bt_conv_silu_scan(const float* entry, float* state, const float* w, float* out,
+                             int64_t steps, int64_t batch, int64_t channels, int64_t taps,
+                             void* stream);
 
 /* argmax with torch.argmax's first-index tie rule over rows of length n.
  * workspace: bt_argmax_workspace_bytes(rows) bytes, zeroed before first use. */

@@ -137,6 +137,14 @@ class Emulator:
             y[b] = (ops.rms_norm(o, nw, norm_eps) * ops.silu(zv)).reshape(-1)
         self._planes_of(y, planes)
 
+    def bt_gdn_gated_scan(self, mixed, mixed_bs, ba, ba_bs, a_log, dt_bias, state, z, z_bs, norm_w, planes, steps,
+                          batch, heads_k, heads_v, dim, scale, l2_eps, norm_eps, stream) -> None:
+        for s in range(steps):  # token s of every sequence: rows s * batch .. s * batch + batch - 1
+            r = s * batch
+            self.bt_gdn_gated_step(mixed + 4 * r * mixed_bs, mixed_bs, ba + 4 * r * ba_bs, ba_bs, a_log, dt_bias,
+                                   state, z + 4 * r * z_bs, z_bs, norm_w, planes + 2 * r * 3 * heads_v * dim,
+                                   batch, heads_k, heads_v, dim, scale, l2_eps, norm_eps, stream)
+
     def bt_linear_rows(self, w, w_dtype, xp, y, n, k, t, stream) -> None:
         p = _bf16_to_f32(_view(xp, np.uint16, t * 3 * k).reshape(t, 3, k)).astype(np.float64).sum(1)
         wm = _bf16_to_f32(_view(w, np.uint16, n * k)) if w_dtype == N.BT_BF16 else _view(w, F32, n * k)
@@ -240,6 +248,11 @@ class Emulator:
             acc = (acc + win[..., j] * wv[:, j]).astype(F32)
         _view(out, F32, batch * channels)[:] = ops.silu(acc.astype(F32)).reshape(-1)
         st[...] = win[..., 1:]
+
+    def bt_conv_silu_scan(self, entry, state, w, out, steps, batch, channels, taps, stream) -> None:
+        for s in range(steps):
+            off = 4 * s * batch * channels
+            self.bt_conv_silu(entry + off, state, w, out + off, batch, channels, taps, stream)
 
     def bt_gdn_decode_strided(self, q, k, v, in_dtype, q_bs, k_bs, v_bs, g, g_bs, beta, beta_bs, state, out, out_bs,
                               batch, heads_k, heads_v, dim, scale, eps, stream) -> None:

@@ -110,9 +110,16 @@ def test_qwen36_full_shape_64_sequences_match_reference(full_gguf) -> None:
     m = Qwen36Moe(full_gguf, max_context=int(g["max_context"]), batch=B)
     try:
         toks = torch.from_numpy(allp).cuda()
+        # the prompts' first L - 1 tokens token by token, then as one chunk
+        # (the default prefill): the same bits, since no projection's sums
+        # depend on how many tokens share the call
+        m.reset()
+        m.prefill(toks[:, : L - 1], chunk=1)
+        by_token = m._step(toks[:, L - 1], L - 1, logits=True)
         m.reset()
         m.prefill(toks[:, : L - 1])
         logits = m._step(toks[:, L - 1], L - 1, logits=True)
+        assert torch.equal(logits, by_token)
         for b in range(len(prompts)):
             got = logits[b].cpu().numpy()
             want = g["top_val"][b, 0]
@@ -127,6 +134,31 @@ def test_qwen36_full_shape_64_sequences_match_reference(full_gguf) -> None:
         m.close()
     for b in range(len(prompts)):
         assert out[b].tolist() == g["tokens"][b].tolist(), f"sequence {b} (margins {g['margins'][b]})"
+
+
+@pytest.mark.parametrize("n,k,dtype", [(8192, 2048, torch.bfloat16), (2048, 4096, torch.bfloat16),
+                                       (256, 2048, torch.float32), (64, 2048, torch.float32)])
+def test_linear_rows_sums_do_not_depend_on_token_count(cuda, n, k, dtype) -> None:
+    """A token's outputs are the same bits whether it is projected alone with
+    16+ others (bf16, the tensor-core path) or with any number of others
+    (f32): the chunked prefill relies on it to reproduce the decode step."""
+    rng = np.random.default_rng(19)
+    w = torch.from_numpy(rng.standard_normal((n, k), dtype=np.float32) * 0.02).to(dtype).cuda()
+    x = torch.from_numpy(rng.standard_normal((448, k), dtype=np.float32)).cuda()
+    dt = N.BT_BF16 if dtype == torch.bfloat16 else N.BT_F32
+
+    def lin(xs):
+        t = xs.shape[0]
+        p = torch.empty(t, 3, k, dtype=torch.bfloat16, device="cuda")
+        N.call("bt_bf16_planes", xs.data_ptr(), p.data_ptr(), t, k, 0)
+        y = torch.empty(t, n, device="cuda")
+        N.call("bt_linear_rows", w.data_ptr(), dt, p.data_ptr(), y.data_ptr(), n, k, t, 0)
+        return y
+
+    full = lin(x)
+    spans = [(64, 128), (0, 32), (0, 17), (100, 292)] + ([(5, 6), (0, 9)] if dtype == torch.float32 else [])
+    for a, b in spans:
+        assert torch.equal(lin(x[a:b].contiguous()), full[a:b]), (a, b)
 
 
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])

@@ -18,6 +18,7 @@ from __future__ import annotations
 
 import numpy as np
 import pytest
+import torch
 
 from breezetoken_b200 import qwen36_moe
 from tests.abi_emulator import install
@@ -41,6 +42,22 @@ def test_qwen36_host_composition_reproduces_reference(emulated, qwen36_tiny_gguf
     toks = m.generate(prompt, steps)
     assert toks == g["tokens"][:steps].tolist(), f"margins {g['margins'][:steps]}"
     # every entry point the mirror's decode path uses was exercised
-    assert {"bt_linear_rows", "bt_gdn_gated_step", "bt_add_rms_norm_planes", "bt_attention_layer",
-            "bt_moe_layer_iq3s", "bt_moe_route", "bt_conv_silu", "bt_bf16_planes", "bt_argmax"} <= emulated.names
+    assert {"bt_linear_rows", "bt_gdn_gated_scan", "bt_add_rms_norm_planes", "bt_attention_layer",
+            "bt_moe_layer_iq3s", "bt_moe_route", "bt_conv_silu_scan", "bt_bf16_planes", "bt_argmax"} <= emulated.names
+    m.close()
+
+
+@pytest.mark.parametrize("chunk", [4, 6])
+def test_qwen36_chunked_prefill_host_composition(emulated, qwen36_tiny_gguf, chunk) -> None:
+    """prefill() in chunks (4 + 2 tokens, or all 6 at once) hands every
+    entry point token-major rows, per-token positions and the chunk's row
+    offsets such that the last prompt token's logits are the reference's."""
+    g = golden("qwen36_tiny")
+    m = qwen36_moe.Qwen36Moe(qwen36_tiny_gguf, device="cpu", max_context=int(g["max_context"]))
+    prompt = g["prompt"].tolist()
+    m.reset()
+    m.prefill(torch.tensor([prompt[:-1]]), chunk=chunk)
+    logits = m.forward_token(prompt[-1], len(prompt) - 1)
+    got, want = logits.numpy(), g["logits"][0]
+    assert np.abs(got - want).max() <= 1e-4 * np.abs(want).max()
     m.close()
