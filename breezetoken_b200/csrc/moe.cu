@@ -17,16 +17,21 @@
 // tiles of one 256-weight column block per item and loads the next item's
 // tiles while it computes.
 //
-// Weights: `bt_repack_iq3_s` stores each 16-row x 256-weight tile (16 GGUF
-// blocks) as one 1792-byte chunk laid out for the m16n8k16 MMA: lane (g, t)
-// loads, with three 16-byte and a few small coalesced loads, the quant bytes
-// of rows g and g+8 for groups 2t and 2t+1 (weights 8t..8t+7) of all 8
-// sub-blocks, so each decoded 4-weight group is two of the MMA's A-fragment
-// registers (the k order inside a sub-block is permuted identically on both
-// operands).  A group is one 8-byte load from the codebook in shared memory,
-// stored as fp16 (exact: |value| <= 15) in 16 bank-interleaved copies so a
-// warp's lookups never conflict, and its 4 sign bits XORed into the fp16
-// sign bits.
+// Weights: every IQ3_S weight is d * (1 + 2 * scale nibble) * v with v a
+// signed codebook value, odd and in [-15, 15] (quant/dequant.py:164-185), so
+// v = 2c - 15 for a 4-bit code c.  `bt_repack_iq3_s` re-encodes the GGUF
+// blocks losslessly as these codes (the codebook index, its high bit and the
+// signs become one nibble per weight) and stores each 16-row x 256-weight
+// tile (16 GGUF blocks) as one 2176-byte chunk laid out for the m16n8k16
+// MMA: lane (g, t) loads, with four 16-byte and two 8-byte coalesced loads,
+// the codes of rows g and g+8 for weights 8t..8t+7 of all 8 sub-blocks, one
+// 32-bit word per (row, sub-block), so a word is four of the MMA's
+// A-fragment registers (the k order inside a sub-block is permuted
+// identically on both operands).  A register is two fp16 weights made with
+// one mask-and-or (the codes land in an fp16 mantissa under the exponent of
+// 1024) and one f16x2 add or fma (exact: the results are small integers):
+// no codebook lookups and no sign arithmetic.  The layout costs 136 bytes
+// per 256 weights against the format's 110.
 //
 // Activations: each vector x is scaled by a power of two (max |x| in
 // [2^13, 2^14)) and split into fp16 hi + lo planes (hi = fp16(x), lo =
@@ -60,40 +65,18 @@ constexpr bool grid_values_small() {
 }
 static_assert(grid_values_small(), "IQ3_S codebook values must be <= 15 (exact fp16 operands)");
 
-// fp16 bit pattern of a non-negative integer n < 2048 (exact).
-constexpr uint32_t half_bits(uint32_t n) {
-  if (n == 0) return 0;
-  int e = 0;
-  while ((n >> (e + 1)) != 0) ++e;
-  return (static_cast<uint32_t>(e + 15) << 10) | ((n << (10 - e)) & 0x3FFu);
+constexpr bool grid_values_odd() {
+  for (int i = 0; i < 512; ++i)
+    for (int j = 0; j < 4; ++j)
+      if ((((kGrid[i] >> (8 * j)) & 255u) & 1u) == 0u) return false;
+  return true;
 }
+static_assert(grid_values_odd(), "IQ3_S codebook values must be odd: v = 2c - 15 for a 4-bit code c");
 
-// Codebook in its shared-memory layout: row (b, qh) at byte b * 256 + qh *
-// 128 holds 16 copies of the 4 fp16 weights of entry qh * 256 + b (8 bytes
-// each).  Lane L reads copy L % 16: a half warp touches each bank once.
-struct alignas(8) Half4 {
-  uint32_t lo, hi;  // (w0, w1), (w2, w3)
+// The codebook for the repack kernel.
+__device__ const uint32_t g_grid[512] = {
+#include "iq3s_grid.inc"
 };
-struct __align__(16) HalfGrid {
-  Half4 v[512 * 16];
-};
-constexpr HalfGrid make_half_grid() {
-  HalfGrid t{};
-  for (int b = 0; b < 256; ++b)
-    for (int qh = 0; qh < 2; ++qh) {
-      const uint32_t e = kGrid[qh * 256 + b];
-      const uint32_t lo = half_bits(e & 255u) | (half_bits((e >> 8) & 255u) << 16);
-      const uint32_t hi = half_bits((e >> 16) & 255u) | (half_bits(e >> 24) << 16);
-      for (int c = 0; c < 16; ++c) {
-        t.v[(b * 2 + qh) * 16 + c].lo = lo;
-        t.v[(b * 2 + qh) * 16 + c].hi = hi;
-      }
-    }
-  return t;
-}
-__device__ const HalfGrid g_half_grid = make_half_grid();
-constexpr int kLutBytes = static_cast<int>(sizeof(HalfGrid));
-static_assert(kLutBytes == 64 * 1024, "codebook layout");
 
 constexpr int kThreads = 256;  // 8 warps; the expert kernels run two CTAs per SM
 constexpr int kWarps = kThreads / 32;
@@ -113,22 +96,22 @@ constexpr int kMaxGrid = 512;
 constexpr int kRangeDown = 2 * kMaxGrid;
 constexpr int kRangeBytes = 4 * 2 * kRangeDown;
 
-// Tile chunk: 16 rows x 256 weights.  Sections (lane L = 4 g + t, group
-// q = 2 s + h of the lane's 16 per row: sub-block s, weights 8t + 4h ..):
-//   [0, 512)     qs of row g:   16 B per lane, byte 4 (q % 4) + q / 4 =
-//                qs[8s + 2t + h] (word j = q % 4 holds the four sub-block
-//                pairs' bytes of that group position, so the kernels pick
-//                pair p's byte with a prmt selector instead of rotating
-//                registers)
-//   [512, 1024)  qs of row g+8: same
-//   [1024, 1536) signs: per lane (row g: S0, S1; row g+8: S0, S1); S0 bit
-//                15 - q / 31 - q = sign of weight 0 / 1 of group q, S1 the
-//                same for weights 2 / 3
-//   [1536, 1664) qh: per lane one word, bit 16r + q = qh[s] bit 2t + h
-//   [1664, 1792) per row: scales[4], d (fp16), 2 pad bytes
+// Tile chunk: 16 rows x 256 weights.  Sections (lane L = 4 g + t):
+//   [0, 2048)     codes: part j (sub-blocks 2j, 2j+1) at 512 j, lane L's 16
+//                 bytes at 512 j + 16 L = the words of (row g, sub-block 2j),
+//                 (row g+8, 2j), (row g, 2j+1), (row g+8, 2j+1); a word holds
+//                 the codes c_i of weights 8t + i (i = 0..7) of its
+//                 sub-block, code c_i at bits (kCodeBit[i] + b) mod 32, b =
+//                 0..3 (see decode_word)
+//   [2048, 2176)  per row: scales[4], d (fp16), 2 zero bytes
 constexpr int kChunkBytes = 16 * kIq3sBlockBytes;
-constexpr int kQsA = 0, kQsB = 512, kSigns = 1024, kQh = 1536, kScales = 1664;
-static_assert(kChunkBytes == 1792, "tile chunk");
+constexpr int kCodes = 0, kScales = 2048;
+static_assert(kChunkBytes == 2176, "tile chunk");
+__host__ __device__ constexpr int code_bit(int i) {
+  // codes 0, 2, 4, 6 (the low halves' weights) at bits 1, 5, 9, 13; codes 1,
+  // 3, 5, 7 at bits 17, 21, 25, 29 (code 7's top bit wraps to bit 0)
+  return (i & 1) * 16 + 1 + 4 * (i >> 1);
+}
 
 constexpr int kTokensPerPass = 4;              // 8 MMA columns: hi and lo per token
 // 4 partial sums per lane; two buffers, so that a pass may write its sums
@@ -148,7 +131,9 @@ __host__ __device__ constexpr int token_stride(int k) { return 2 * plane_stride(
 
 // ------------------------------------------------------------------ repack
 // GGUF IQ3_S rows (110-byte blocks: d[2] qs[64] qh[8] signs[32] scales[4])
-// -> tile chunks.  One thread per (chunk, lane).
+// -> tile chunks.  One thread per (chunk, lane): weight 8t + i of sub-block s
+// is weight j = i % 4 of group q = 8s + 2t + i / 4, whose codebook entry is
+// qs[q] | qh bit q << 8 and whose sign is bit 8t + i of signs[4s .. 4s+3].
 __global__ void repack_iq3s_kernel(const uint8_t* __restrict__ src, uint8_t* __restrict__ dst, int64_t n_chunks,
                                    int kb_per_row) {
   for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n_chunks * 32;
@@ -158,25 +143,22 @@ __global__ void repack_iq3s_kernel(const uint8_t* __restrict__ src, uint8_t* __r
     const int64_t tile = chunk / kb_per_row;
     const int kb = static_cast<int>(chunk % kb_per_row);
     uint8_t* d = dst + chunk * kChunkBytes;
-    uint32_t qh = 0;
     for (int r = 0; r < 2; ++r) {
       const uint8_t* blk = src + ((tile * 16 + g + 8 * r) * kb_per_row + kb) * 110;
-      uint8_t* q = d + (r ? kQsB : kQsA) + 16 * lane;
-      uint32_t s01 = 0, s23 = 0;
-      for (int s = 0; s < 8; ++s)
-        for (int h = 0; h < 2; ++h) {
-          const int grp = 2 * s + h;
-          q[4 * (grp & 3) + (grp >> 2)] = blk[2 + 8 * s + 2 * t + h];
-          const uint32_t nib = (blk[74 + 4 * s + t] >> (4 * h)) & 15u;
-          s01 |= ((nib & 1u) << (15 - grp)) | (((nib >> 1) & 1u) << (31 - grp));
-          s23 |= (((nib >> 2) & 1u) << (15 - grp)) | (((nib >> 3) & 1u) << (31 - grp));
-          qh |= ((static_cast<uint32_t>(blk[66 + s]) >> (2 * t + h)) & 1u) << (16 * r + grp);
+      for (int sb = 0; sb < 8; ++sb) {
+        const uint32_t signs = blk[74 + 4 * sb + t];
+        uint32_t word = 0;
+        for (int w = 0; w < 8; ++w) {
+          const int q = 8 * sb + 2 * t + (w >> 2);
+          const uint32_t idx = blk[2 + q] | (((static_cast<uint32_t>(blk[66 + sb]) >> (2 * t + (w >> 2))) & 1u) << 8);
+          const int mag = static_cast<int>((g_grid[idx] >> (8 * (w & 3))) & 255u);
+          const int v = ((signs >> w) & 1u) ? -mag : mag;
+          const uint32_t code = static_cast<uint32_t>((v + 15) >> 1);
+          for (int b = 0; b < 4; ++b) word |= ((code >> b) & 1u) << ((code_bit(w) + b) & 31);
         }
-      uint32_t* sw = reinterpret_cast<uint32_t*>(d + kSigns + 16 * lane + 8 * r);
-      sw[0] = s01;
-      sw[1] = s23;
+        *reinterpret_cast<uint32_t*>(d + kCodes + 512 * (sb >> 1) + 16 * lane + 4 * (2 * (sb & 1) + r)) = word;
+      }
     }
-    *reinterpret_cast<uint32_t*>(d + kQh + 4 * lane) = qh;
     if (lane < 16) {
       const uint8_t* blk = src + ((tile * 16 + lane) * kb_per_row + kb) * 110;
       uint8_t* rec = d + kScales + 8 * lane;
@@ -753,88 +735,56 @@ __device__ __forceinline__ uint32_t ld_stream4(const uint8_t* p) {
   return v;
 }
 
-// A lane's share of one tile chunk (rows g and g+8).
+// A lane's share of one tile chunk (rows g and g+8): the code words of all
+// 8 sub-blocks (part[j] = sub-blocks 2j, 2j+1) and the two rows' scale
+// records.
 struct Tile {
-  uint4 qa, qb, sg;
-  uint32_t qh;
-  uint2 ra, rb;  // scale records of rows g, g+8
+  uint4 part[4];
+  uint2 ra, rb;
 };
 
 __device__ __forceinline__ void load_tile(const uint8_t* chunk, int lane, Tile& T) {
-  T.qa = ld_stream16(chunk + kQsA + 16 * lane);
-  T.qb = ld_stream16(chunk + kQsB + 16 * lane);
-  T.sg = ld_stream16(chunk + kSigns + 16 * lane);
-  T.qh = ld_stream4(chunk + kQh + 4 * lane);
+#pragma unroll
+  for (int j = 0; j < 4; ++j) T.part[j] = ld_stream16(chunk + kCodes + 512 * j + 16 * lane);
   const int g = lane >> 2;
   T.ra = __ldg(reinterpret_cast<const uint2*>(chunk + kScales) + g);
   T.rb = __ldg(reinterpret_cast<const uint2*>(chunk + kScales) + g + 8);
 }
 
-// A tile's sign, qh and scale words for the current pair of sub-blocks;
-// block_steps advances it by two sub-blocks per step of a rolled loop, so the
-// code of one step is all that is live beside the tiles.  (The qs words stay
-// in the tile: a step picks its pair's bytes with a prmt selector.)
-struct Cursor {
-  uint32_t s0a, s1a, s0b, s1b;  // sign words of rows g, g+8, shifted to the pair
-  uint32_t qh;                  // bits 2s+h (row g), 16+2s+h (row g+8)
-  uint32_t sca, scb;            // scale nibbles of rows g, g+8 (nibble s)
-  float da, db;                 // d of rows g, g+8
-  float dna, dnb;               // -2^23 d (exact: a power-of-two multiple)
-};
-
-__device__ __forceinline__ Cursor cursor_of(const Tile& T) {
-  Cursor c;
-  c.s0a = T.sg.x;
-  c.s1a = T.sg.y;
-  c.s0b = T.sg.z;
-  c.s1b = T.sg.w;
-  c.qh = T.qh;
-  c.sca = T.ra.x;
-  c.scb = T.rb.x;
-  c.da = __half2float(__ushort_as_half(static_cast<unsigned short>(T.ra.y & 0xFFFFu)));
-  c.db = __half2float(__ushort_as_half(static_cast<unsigned short>(T.rb.y & 0xFFFFu)));
-  c.dna = -8388608.0f * c.da;
-  c.dnb = -8388608.0f * c.db;
-  return c;
+__device__ __forceinline__ uint32_t f16x2_add(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("add.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+__device__ __forceinline__ uint32_t f16x2_fma(uint32_t a, uint32_t b, uint32_t c) {
+  uint32_t d;
+  asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+  return d;
 }
 
-__device__ __forceinline__ void cursor_next(Cursor& c) {
-  c.s0a <<= 4;
-  c.s1a <<= 4;
-  c.s0b <<= 4;
-  c.s1b <<= 4;
-  c.qh >>= 4;
-  c.sca >>= 8;
-  c.scb >>= 8;
+// The fp16 pairs (w0, w1), (w2, w3), (w4, w5), (w6, w7) of a code word.  A
+// code c at mantissa bits [k, k+4) of an fp16 with the exponent of 1024 (bit
+// pattern 0x6400) makes 1024 + 2^k c; then v = 2c - 15 is one exact f16x2
+// add (k = 1: minus 1039) or fma (k = 5: times 1/16, minus 79).  Codes 4/5
+// reach bits 1-4 of each half by a shift of 8, codes 6/7 by a rotation by 12.
+__device__ __forceinline__ void decode_word(uint32_t w, uint32_t& p01, uint32_t& p23, uint32_t& p45,
+                                            uint32_t& p67) {
+  constexpr uint32_t kMagic = 0x64006400u;       // fp16 1024 | 1024
+  constexpr uint32_t kMinus1039 = 0xE40FE40Fu;   // fp16 -1039 | -1039
+  constexpr uint32_t kSixteenth = 0x2C002C00u;   // fp16 1/16 | 1/16
+  constexpr uint32_t kMinus79 = 0xD4F0D4F0u;     // fp16 -79 | -79
+  p01 = f16x2_add((w & 0x001E001Eu) | kMagic, kMinus1039);
+  p23 = f16x2_fma((w & 0x01E001E0u) | kMagic, kSixteenth, kMinus79);
+  p45 = f16x2_add(((w >> 8) & 0x001E001Eu) | kMagic, kMinus1039);
+  p67 = f16x2_add((__funnelshift_r(w, w, 12) & 0x001E001Eu) | kMagic, kMinus1039);
 }
 
-// fp16 weights (w0, w1), (w2, w3) of group 2t+H of sub-block S (0/1 within
-// the current pair), row g (R = 0) or g+8.  `lut` is the codebook's shared
-// memory, `lane_off` this lane's copy offset (byte 0 of the word), `sel` the
-// prmt selector of the current pair p: (qs byte p of word 2S+H << 8) |
-// lane_off.
-template <int S, int R, int H>
-__device__ __forceinline__ uint2 tile_word(const Tile& T, const Cursor& c, const uint8_t* lut, uint32_t lane_off,
-                                           uint32_t sel) {
-  constexpr int J = 2 * S + H;
-  const uint4& q = R ? T.qb : T.qa;
-  const uint32_t qw = J == 0 ? q.x : J == 1 ? q.y : J == 2 ? q.z : q.w;
-  constexpr int QB = 16 * R + J;
-  const uint32_t hb = QB >= 7 ? (c.qh >> (QB - 7)) : (c.qh << (7 - QB));
-  const uint32_t off = prmt(qw, lane_off, sel) | (hb & 0x80u);
-  uint2 w = *reinterpret_cast<const uint2*>(lut + off);
-  w.x ^= ((R ? c.s0b : c.s0a) << J) & 0x80008000u;
-  w.y ^= ((R ? c.s1b : c.s1a) << J) & 0x80008000u;
-  return w;
-}
-
-// d * (1 + 2 * nibble s) (quant/dequant.py:164-185), as one fma: the float
-// with bits 0x4B000000 | (2n + 1) is 2^23 + 2n + 1, so m * d - 2^23 d is
-// (2n + 1) d exactly (an 11-bit by 5-bit product), rounded once: the same
-// value as the f32 product.
-template <int S>
-__device__ __forceinline__ float row_scale(uint32_t nibbles, float d, float dneg) {
-  const uint32_t two_n = (S == 0 ? (nibbles << 1) : (nibbles >> 3)) & 0x1Eu;
+// d * (1 + 2 * nibble of sub-block sb) (quant/dequant.py:164-185), as one
+// fma: the float with bits 0x4B000000 | (2n + 1) is 2^23 + 2n + 1, so m * d -
+// 2^23 d is (2n + 1) d exactly (an 11-bit by 5-bit product), rounded once:
+// the same value as the f32 product.
+__device__ __forceinline__ float sub_scale(uint32_t nibbles, int sb, float d, float dneg) {
+  const uint32_t two_n = (sb == 0 ? (nibbles << 1) : (nibbles >> (4 * sb - 1))) & 0x1Eu;
   return fmaf(__uint_as_float(0x4B000001u | two_n), d, dneg);
 }
 
@@ -846,41 +796,70 @@ __device__ __forceinline__ void mma_f16(float (&c)[4], uint32_t a0, uint32_t a1,
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
-// acc[r] += db(row) * (hi + lo sums of sub-block S) for rows g (r = 0) and
-// g+8, token column pair t.  `b`: elements 8t..8t+7 of the sub-block of
-// this lane's B column (token g/2, plane g%2).
-template <int S>
-__device__ __forceinline__ void tile_step(const Tile& T, const Cursor& c, const uint8_t* lut, uint32_t lane_off,
-                                          uint32_t sel, const uint4& b, float (&acc)[2]) {
-  const uint2 w00 = tile_word<S, 0, 0>(T, c, lut, lane_off, sel), w10 = tile_word<S, 1, 0>(T, c, lut, lane_off, sel);
-  const uint2 w01 = tile_word<S, 0, 1>(T, c, lut, lane_off, sel), w11 = tile_word<S, 1, 1>(T, c, lut, lane_off, sel);
+// acc[r] += scale(row) * (hi + lo sums of one sub-block) for rows g (r = 0)
+// and g+8, token column pair t.  wg / wg8: the sub-block's code words of
+// rows g and g+8; `b`: elements 8t..8t+7 of the sub-block of this lane's B
+// column (token g/2, plane g%2).
+__device__ __forceinline__ void tile_step(uint32_t wg, uint32_t wg8, float sg, float sg8, const uint4& b,
+                                          float (&acc)[2]) {
+  uint32_t a01, a23, a45, a67, c01, c23, c45, c67;
+  decode_word(wg, a01, a23, a45, a67);
+  decode_word(wg8, c01, c23, c45, c67);
   float cc[4] = {0.f, 0.f, 0.f, 0.f};
-  mma_f16(cc, w00.x, w10.x, w00.y, w10.y, b.x, b.y);  // groups 2t: weights 8t .. 8t+3
-  mma_f16(cc, w01.x, w11.x, w01.y, w11.y, b.z, b.w);  // groups 2t+1: weights 8t+4 .. 8t+7
-  acc[0] = fmaf(row_scale<S>(c.sca, c.da, c.dna), cc[0] + cc[1], acc[0]);
-  acc[1] = fmaf(row_scale<S>(c.scb, c.db, c.dnb), cc[2] + cc[3], acc[1]);
+  mma_f16(cc, a01, c01, a23, c23, b.x, b.y);  // weights 8t .. 8t+3
+  mma_f16(cc, a45, c45, a67, c67, b.z, b.w);  // weights 8t+4 .. 8t+7
+  acc[0] = fmaf(sg, cc[0] + cc[1], acc[0]);
+  acc[1] = fmaf(sg8, cc[2] + cc[3], acc[1]);
+}
+
+__device__ __forceinline__ float half_lo(uint32_t v) {
+  return __half2float(__ushort_as_half(static_cast<unsigned short>(v & 0xFFFFu)));
 }
 
 // All 8 sub-blocks of K-block `kb` for two tiles sharing the B operands,
-// two sub-blocks per step of a rolled loop.  `xl`: this lane's B column
-// base (token g/2, plane g%2, element 8t).
-__device__ __forceinline__ void block_steps(const Tile& ta, const Tile& tb, const uint8_t* lut, uint32_t lane_off,
+// in sub-block order.  Each part of a tile's registers is refilled with the
+// same part of the next chunk (na / nb; null: none) as soon as it has been
+// read, so one tile's registers carry the current block and the next one's
+// loads in flight.  `xl`: this lane's B column base (token g/2, plane g%2,
+// element 8t).
+__device__ __forceinline__ void block_steps(Tile& ta, Tile& tb, const uint8_t* na, const uint8_t* nb, int lane,
                                             const uint8_t* xl, int kb, float (&acc)[2][2]) {
-  Cursor ca = cursor_of(ta), cb = cursor_of(tb);
+  // the 4 lanes of a quad share rows g and g+8: lane t computes the scales of
+  // sub-blocks 2t and 2t+1, the others read them with a shuffle
+  const int g = lane >> 2, tq = lane & 3, q0 = lane & ~3;
+  float s_a0e, s_a0o, s_a1e, s_a1o, s_b0e, s_b0o, s_b1e, s_b1o;
+  {
+    const float da0 = half_lo(ta.ra.y), da1 = half_lo(ta.rb.y), db0 = half_lo(tb.ra.y), db1 = half_lo(tb.rb.y);
+    s_a0e = sub_scale(ta.ra.x, 2 * tq, da0, -8388608.0f * da0);
+    s_a0o = sub_scale(ta.ra.x, 2 * tq + 1, da0, -8388608.0f * da0);
+    s_a1e = sub_scale(ta.rb.x, 2 * tq, da1, -8388608.0f * da1);
+    s_a1o = sub_scale(ta.rb.x, 2 * tq + 1, da1, -8388608.0f * da1);
+    s_b0e = sub_scale(tb.ra.x, 2 * tq, db0, -8388608.0f * db0);
+    s_b0o = sub_scale(tb.ra.x, 2 * tq + 1, db0, -8388608.0f * db0);
+    s_b1e = sub_scale(tb.rb.x, 2 * tq, db1, -8388608.0f * db1);
+    s_b1o = sub_scale(tb.rb.x, 2 * tq + 1, db1, -8388608.0f * db1);
+  }
+  if (na) {
+    ta.ra = __ldg(reinterpret_cast<const uint2*>(na + kScales) + g);
+    ta.rb = __ldg(reinterpret_cast<const uint2*>(na + kScales) + g + 8);
+  }
+  if (nb) {
+    tb.ra = __ldg(reinterpret_cast<const uint2*>(nb + kScales) + g);
+    tb.rb = __ldg(reinterpret_cast<const uint2*>(nb + kScales) + g + 8);
+  }
   const uint8_t* xq = xl + kb * 512;  // 8 sub-blocks x 32 fp16
-  // prmt selector: byte 0 <- lane_off byte 0, byte 1 <- qs word byte p,
-  // bytes 2, 3 <- lane_off byte 1 (zero)
-  uint32_t sel = 0x5504u;
-#pragma unroll 1
-  for (int p = 0; p < 4; ++p, sel += 0x10u) {
+#pragma unroll
+  for (int p = 0; p < 4; ++p) {
     const uint4 b0 = *reinterpret_cast<const uint4*>(xq + 128 * p);
     const uint4 b1 = *reinterpret_cast<const uint4*>(xq + 128 * p + 64);
-    tile_step<0>(ta, ca, lut, lane_off, sel, b0, acc[0]);
-    tile_step<0>(tb, cb, lut, lane_off, sel, b0, acc[1]);
-    tile_step<1>(ta, ca, lut, lane_off, sel, b1, acc[0]);
-    tile_step<1>(tb, cb, lut, lane_off, sel, b1, acc[1]);
-    cursor_next(ca);
-    cursor_next(cb);
+    const uint4 &pa = ta.part[p], &pb = tb.part[p];
+    const int src = q0 | p;
+    tile_step(pa.x, pa.y, __shfl_sync(0xffffffffu, s_a0e, src), __shfl_sync(0xffffffffu, s_a1e, src), b0, acc[0]);
+    tile_step(pb.x, pb.y, __shfl_sync(0xffffffffu, s_b0e, src), __shfl_sync(0xffffffffu, s_b1e, src), b0, acc[1]);
+    tile_step(pa.z, pa.w, __shfl_sync(0xffffffffu, s_a0o, src), __shfl_sync(0xffffffffu, s_a1o, src), b1, acc[0]);
+    tile_step(pb.z, pb.w, __shfl_sync(0xffffffffu, s_b0o, src), __shfl_sync(0xffffffffu, s_b1o, src), b1, acc[1]);
+    if (na) ta.part[p] = ld_stream16(na + kCodes + 512 * p + 16 * lane);
+    if (nb) tb.part[p] = ld_stream16(nb + kCodes + 512 * p + 16 * lane);
   }
 }
 
@@ -891,12 +870,6 @@ __device__ __forceinline__ void cp_async16(void* smem_dst, const void* gsrc) {
 }
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
-
-__device__ __forceinline__ void stage_lut(uint8_t* lut) {
-  const uint8_t* src = reinterpret_cast<const uint8_t*>(g_half_grid.v);
-  for (int i = threadIdx.x; i < kLutBytes / 16; i += kThreads) cp_async16(lut + 16 * i, src + 16 * i);
-  cp_async_commit();
-}
 
 // The expert slot an item serves: from the prep kernel's sort, or (one
 // token, whose top-k experts are distinct) straight from the routing ids.
@@ -996,18 +969,16 @@ __global__ void __launch_bounds__(kThreads, 2)
   constexpr int K = KB * 256, TP = kWarps / KB, OUT = 16 * TP;
   static_assert(kWarps % KB == 0, "K blocks per item");
   extern __shared__ __align__(16) uint8_t smem[];
-  uint8_t* lut = smem;
-  float* red = reinterpret_cast<float*>(smem + kLutBytes);
-  float* xsc = reinterpret_cast<float*>(smem + kLutBytes + kRedBytes);
+  float* red = reinterpret_cast<float*>(smem);
+  float* xsc = reinterpret_cast<float*>(smem + kRedBytes);
   int* spair = reinterpret_cast<int*>(xsc) + kMiscPair;
-  uint8_t* xs = smem + kLutBytes + kRedBytes + kMiscBytes;
+  uint8_t* xs = smem + kRedBytes + kMiscBytes;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
   if (static_cast<int>(blockIdx.x) < s_blocks) {  // the shared expert's down rows
     shared_down_block(blockIdx.x, sh, t_total, hidden, ws);
     return;
   }
   const int rb = blockIdx.x - s_blocks;  // routed CTA
-  stage_lut(lut);
   // The op's inputs (ids, x) come from whatever ran before: read them only
   // after the wait, and let the down kernel start only then, so that it may
   // read the slots before its own wait.
@@ -1017,30 +988,38 @@ __global__ void __launch_bounds__(kThreads, 2)
   const int i0 = direct ? rb * top_k * chunks / gu_grid : ws.ranges[2 * rb];
   const int i1 = direct ? (rb + 1) * top_k * chunks / gu_grid : ws.ranges[2 * rb + 1];
   const int tp = warp % TP, kb = warp / TP;
-  const uint32_t lane_off = static_cast<uint32_t>(lane & 15) * 8u;
   const uint8_t* xl = xs + (g >> 1) * token_stride(K) + (g & 1) * plane_stride(K) + 16 * t;
   __shared__ SlotCache sc;
   fill_slots(sc, i0, i1, chunks, direct != 0, ids, n_experts, ws);
-  auto load_item = [&](int it, Tile& tg, Tile& tu) {
+  // this warp's chunk offset of item `it` (-1: a slot with an invalid expert)
+  auto item_off = [&](int it) -> int64_t {
     const int u = it / chunks, c = it - u * chunks;
     Slot s;
-    if (!cached_slot(sc, u, direct != 0, ids, n_experts, ws, s)) return;
-    const int64_t off = ((static_cast<int64_t>(s.expert) * (ffn / 16) + c * TP + tp) * KB + kb) * kChunkBytes;
-    load_tile(gate + off, lane, tg);
-    load_tile(up + off, lane, tu);
+    if (!cached_slot(sc, u, direct != 0, ids, n_experts, ws, s)) return -1;
+    return ((static_cast<int64_t>(s.expert) * (ffn / 16) + c * TP + tp) * KB + kb) * kChunkBytes;
   };
-  Tile tg{}, tu{}, ng{}, nu{};
-  if (i0 < i1) load_item(i0, tg, tu);
+  Tile tg{}, tu{};
+  int64_t cur = i0 < i1 ? item_off(i0) : -1;
+  if (cur >= 0) {
+    load_tile(gate + cur, lane, tg);
+    load_tile(up + cur, lane, tu);
+  }
   int staged = -1;  // (slot, first pair) whose tokens are in xs
   int npass = 0;    // passes so far: the reduction buffer of a pass is npass & 1
   for (int it = i0; it < i1; ++it) {
     const int u = it / chunks, c = it - u * chunks;
     Slot s;
     const bool live = cached_slot(sc, u, direct != 0, ids, n_experts, ws, s);
-    if (it + 1 < i1) load_item(it + 1, ng, nu);
+    const int64_t nxt = it + 1 < i1 ? item_off(it + 1) : -1;
+    if (!live && nxt >= 0) {  // nothing computed here: load the next item's tiles now
+      load_tile(gate + nxt, lane, tg);
+      load_tile(up + nxt, lane, tu);
+    }
     for (int c0 = 0; live && c0 < s.count; c0 += kTokensPerPass) {
       const int mc = min(kTokensPerPass, s.count - c0);
-      if (c0 > 0) load_item(it, tg, tu);  // a later pass re-reads the tiles
+      // the tiles to load during this pass: this item's again for a later
+      // pass, else the next item's
+      const int64_t load = c0 + kTokensPerPass < s.count ? cur : nxt;
       if (u * 4096 + c0 != staged) {
         __syncthreads();  // readers of xs are done
         for (int i = threadIdx.x; i < mc * (K / 4); i += kThreads) {  // 16-byte pieces, K/8 per plane
@@ -1060,7 +1039,7 @@ __global__ void __launch_bounds__(kThreads, 2)
         staged = u * 4096 + c0;
       }
       float acc[2][2] = {};
-      block_steps(tg, tu, lut, lane_off, xl, kb, acc);
+      block_steps(tg, tu, load >= 0 ? gate + load : nullptr, load >= 0 ? up + load : nullptr, lane, xl, kb, acc);
       float* rb = red + (npass++ & 1) * kRedFloats;
       reinterpret_cast<float4*>(rb)[warp * 32 + lane] = make_float4(acc[0][0], acc[0][1], acc[1][0], acc[1][1]);
       __syncthreads();
@@ -1081,8 +1060,7 @@ __global__ void __launch_bounds__(kThreads, 2)
         ws.act[static_cast<int64_t>(spair[v]) * ffn + c * OUT + o] = silu_f(gs) * us;
       }
     }
-    tg = ng;
-    tu = nu;
+    cur = nxt;
   }
 }
 
@@ -1101,32 +1079,35 @@ __global__ void __launch_bounds__(kThreads, 2)
   constexpr int K = KB * 256, TP = kWarps / KB, ROWS = 32 * TP;
   static_assert(kWarps % KB == 0, "K blocks per item");
   extern __shared__ __align__(16) uint8_t smem[];
-  uint8_t* lut = smem;
-  float* red = reinterpret_cast<float*>(smem + kLutBytes);
-  float* xsc = reinterpret_cast<float*>(smem + kLutBytes + kRedBytes);
+  float* red = reinterpret_cast<float*>(smem);
+  float* xsc = reinterpret_cast<float*>(smem + kRedBytes);
   float* wmax = xsc + 16;
   int* spair = reinterpret_cast<int*>(xsc) + kMiscPair;
-  uint8_t* xs = smem + kLutBytes + kRedBytes + kMiscBytes;
+  uint8_t* xs = smem + kRedBytes + kMiscBytes;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
-  stage_lut(lut);
   const int chunks = hidden / ROWS;
   const int i0 = direct ? blockIdx.x * top_k * chunks / gridDim.x : ws.ranges[kRangeDown + 2 * blockIdx.x];
   const int i1 = direct ? (blockIdx.x + 1) * top_k * chunks / gridDim.x : ws.ranges[kRangeDown + 2 * blockIdx.x + 1];
   const int tp = warp % TP, kb = warp / TP;
-  const uint32_t lane_off = static_cast<uint32_t>(lane & 15) * 8u;
   const uint8_t* xl = xs + (g >> 1) * token_stride(K) + (g & 1) * plane_stride(K) + 16 * t;
   __shared__ SlotCache sc;
   fill_slots(sc, i0, i1, chunks, direct != 0, ids, n_experts, ws);
-  auto load_item = [&](int it, Tile& ta, Tile& tb) {
+  // the offset of this warp's first chunk of item `it` (the second follows
+  // KB chunks later; -1: a slot with an invalid expert)
+  auto item_off = [&](int it) -> int64_t {
     const int u = it / chunks, c = it - u * chunks;
     Slot s;
-    if (!cached_slot(sc, u, direct != 0, ids, n_experts, ws, s)) return;
+    if (!cached_slot(sc, u, direct != 0, ids, n_experts, ws, s)) return -1;
     const int64_t tile = static_cast<int64_t>(s.expert) * (hidden / 16) + c * 2 * TP + 2 * tp;
-    load_tile(down + (tile * KB + kb) * kChunkBytes, lane, ta);
-    load_tile(down + ((tile + 1) * KB + kb) * kChunkBytes, lane, tb);
+    return (tile * KB + kb) * kChunkBytes;
   };
-  Tile ta{}, tb{}, na{}, nb{};
-  if (i0 < i1) load_item(i0, ta, tb);
+  constexpr int64_t kNextTile = static_cast<int64_t>(KB) * kChunkBytes;
+  Tile ta{}, tb{};
+  int64_t cur = i0 < i1 ? item_off(i0) : -1;
+  if (cur >= 0) {
+    load_tile(down + cur, lane, ta);
+    load_tile(down + cur + kNextTile, lane, tb);
+  }
   pdl_launch_dependents();
   pdl_wait();
   __shared__ int s_last;
@@ -1136,10 +1117,14 @@ __global__ void __launch_bounds__(kThreads, 2)
     const int u = it / chunks, c = it - u * chunks;
     Slot s;
     const bool live = cached_slot(sc, u, direct != 0, ids, n_experts, ws, s);
-    if (it + 1 < i1) load_item(it + 1, na, nb);
+    const int64_t nxt = it + 1 < i1 ? item_off(it + 1) : -1;
+    if (!live && nxt >= 0) {  // nothing computed here: load the next item's tiles now
+      load_tile(down + nxt, lane, ta);
+      load_tile(down + nxt + kNextTile, lane, tb);
+    }
     for (int c0 = 0; live && c0 < s.count; c0 += kTokensPerPass) {
       const int mc = min(kTokensPerPass, s.count - c0);
-      if (c0 > 0) load_item(it, ta, tb);
+      const int64_t load = c0 + kTokensPerPass < s.count ? cur : nxt;  // as in the gate/up kernel
       if (u * 4096 + c0 != staged) {
         // act of pair slot v: threads [64 v, 64 v + 64) (warps 2v, 2v+1) -> fp16 planes
         const int v = threadIdx.x >> 6, j = threadIdx.x & 63;
@@ -1175,7 +1160,8 @@ __global__ void __launch_bounds__(kThreads, 2)
         staged = u * 4096 + c0;
       }
       float acc[2][2] = {};
-      block_steps(ta, tb, lut, lane_off, xl, kb, acc);
+      block_steps(ta, tb, load >= 0 ? down + load : nullptr, load >= 0 ? down + load + kNextTile : nullptr, lane,
+                  xl, kb, acc);
       float* rb = red + (npass++ & 1) * kRedFloats;
       reinterpret_cast<float4*>(rb)[warp * 32 + lane] = make_float4(acc[0][0], acc[0][1], acc[1][0], acc[1][1]);
       __syncthreads();
@@ -1213,8 +1199,7 @@ __global__ void __launch_bounds__(kThreads, 2)
       }
       __syncthreads();  // s_last readers done
     }
-    ta = na;
-    tb = nb;
+    cur = nxt;
   }
 }
 
@@ -1253,24 +1238,21 @@ __global__ void __launch_bounds__(kThreads, 2)
   constexpr int K = KB * 256, TP = kWarps / KS, OUT = 16 * TP, KPW = KB / KS;
   static_assert(kWarps % KS == 0 && KB % KS == 0, "K splits");
   extern __shared__ __align__(16) uint8_t smem[];
-  uint8_t* lut = smem;
-  float* red = reinterpret_cast<float*>(smem + kLutBytes);
-  float* xsc = reinterpret_cast<float*>(smem + kLutBytes + kRedBytes);
+  float* red = reinterpret_cast<float*>(smem);
+  float* xsc = reinterpret_cast<float*>(smem + kRedBytes);
   int* spair = reinterpret_cast<int*>(xsc) + kMiscPair;
-  uint8_t* xs = smem + kLutBytes + kRedBytes + kMiscBytes;
+  uint8_t* xs = smem + kRedBytes + kMiscBytes;
   __shared__ int s_next[3];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
   if (static_cast<int>(blockIdx.x) < s_blocks) {  // the shared expert's down rows
     shared_down_block(blockIdx.x, sh, t_total, hidden, ws);
     return;
   }
-  stage_lut(lut);
   pdl_wait();
   pdl_launch_dependents();
   const int chunks = ffn / OUT;
   const int n_items = __ldcg(ws.hdr + kPassCount) * chunks;
   const int tp = warp % TP, kb0 = (warp / TP) * KPW;
-  const uint32_t lane_off = static_cast<uint32_t>(lane & 15) * 8u;
   const uint8_t* xl = xs + (g >> 1) * token_stride(K) + (g & 1) * plane_stride(K) + 16 * t;
   auto tile_of = [&](int item, int kb) -> int64_t {
     const int q = item / chunks, c = item - q * chunks;
@@ -1281,7 +1263,6 @@ __global__ void __launch_bounds__(kThreads, 2)
     s_next[0] = pull_item(ws.hdr + kWorkGateUp);
     s_next[1] = pull_item(ws.hdr + kWorkGateUp);
   }
-  cp_async_wait_all();
   __syncthreads();
   int it = s_next[0];
   Tile tg{}, tu{};
@@ -1317,19 +1298,10 @@ __global__ void __launch_bounds__(kThreads, 2)
     float acc[2][2] = {};
 #pragma unroll 1
     for (int kb = kb0; kb < kb0 + KPW; ++kb) {
-      Tile ng{}, nu{};
-      if (kb + 1 < kb0 + KPW) {
-        const int64_t off = tile_of(it, kb + 1);
-        load_tile(gate + off, lane, ng);
-        load_tile(up + off, lane, nu);
-      } else if (next < n_items) {  // the next item's first tiles
-        const int64_t off = tile_of(next, kb0);
-        load_tile(gate + off, lane, ng);
-        load_tile(up + off, lane, nu);
-      }
-      block_steps(tg, tu, lut, lane_off, xl, kb, acc);
-      tg = ng;
-      tu = nu;
+      // the tiles to load meanwhile: the next K-block's, or at the last one
+      // the next item's first
+      const int64_t off = kb + 1 < kb0 + KPW ? tile_of(it, kb + 1) : next < n_items ? tile_of(next, kb0) : -1;
+      block_steps(tg, tu, off >= 0 ? gate + off : nullptr, off >= 0 ? up + off : nullptr, lane, xl, kb, acc);
     }
     if constexpr (KS == 1) {
       // lane (g, t): gate and up rows g, g+8 of this warp's tile pair, token t
@@ -1368,19 +1340,16 @@ __global__ void __launch_bounds__(kThreads, 2)
     moe_down_pulled_kernel(const uint8_t* __restrict__ down, int top_k, int hidden, MoeWs ws) {
   constexpr int K = KB * 256, ROWS = 32 * kWarps;
   extern __shared__ __align__(16) uint8_t smem[];
-  uint8_t* lut = smem;
-  float* xsc = reinterpret_cast<float*>(smem + kLutBytes + kRedBytes);
+  float* xsc = reinterpret_cast<float*>(smem + kRedBytes);
   float* wmax = xsc + 16;
   int* spair = reinterpret_cast<int*>(xsc) + kMiscPair;
-  uint8_t* xs = smem + kLutBytes + kRedBytes + kMiscBytes;
+  uint8_t* xs = smem + kRedBytes + kMiscBytes;
   __shared__ int s_next[3];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
-  stage_lut(lut);
   pdl_launch_dependents();
   pdl_wait();
   const int chunks = hidden / ROWS;
   const int n_items = __ldcg(ws.hdr + kPassCount) * chunks;
-  const uint32_t lane_off = static_cast<uint32_t>(lane & 15) * 8u;
   const uint8_t* xl = xs + (g >> 1) * token_stride(K) + (g & 1) * plane_stride(K) + 16 * t;
   auto tile_of = [&](int item, int half, int kb) -> int64_t {
     const int q = item / chunks, c = item - q * chunks;
@@ -1392,7 +1361,6 @@ __global__ void __launch_bounds__(kThreads, 2)
     s_next[0] = pull_item(ws.hdr + kWorkDown);
     s_next[1] = pull_item(ws.hdr + kWorkDown);
   }
-  cp_async_wait_all();
   __syncthreads();
   int it = s_next[0];
   Tile ta{}, tb{};
@@ -1442,17 +1410,12 @@ __global__ void __launch_bounds__(kThreads, 2)
     float acc[2][2] = {};
 #pragma unroll 1
     for (int kb = 0; kb < KB; ++kb) {
-      Tile na{}, nb{};
-      if (kb + 1 < KB) {
-        load_tile(down + tile_of(it, 0, kb + 1), lane, na);
-        load_tile(down + tile_of(it, 1, kb + 1), lane, nb);
-      } else if (next < n_items) {  // the next item's first tiles
-        load_tile(down + tile_of(next, 0, 0), lane, na);
-        load_tile(down + tile_of(next, 1, 0), lane, nb);
-      }
-      block_steps(ta, tb, lut, lane_off, xl, kb, acc);
-      ta = na;
-      tb = nb;
+      // the tiles to load meanwhile: the next K-block's, or at the last one
+      // the next item's first
+      const bool more = kb + 1 < KB, other = !more && next < n_items;
+      const uint8_t* na = more ? down + tile_of(it, 0, kb + 1) : other ? down + tile_of(next, 0, 0) : nullptr;
+      const uint8_t* nb = more ? down + tile_of(it, 1, kb + 1) : other ? down + tile_of(next, 1, 0) : nullptr;
+      block_steps(ta, tb, na, nb, lane, xl, kb, acc);
     }
     // lane (g, t): rows g, g+8 of the warp's tiles 2w (acc[0]) and 2w+1 (acc[1]), token t
     if (t < mc) {
@@ -1513,8 +1476,8 @@ int launch_all(const uint8_t* gate, const uint8_t* up, const uint8_t* down, cons
   const int direct = t == 1 ? 1 : 0;
   constexpr int kGuOut = 16 * (kWarps / KBG), kDnRows = 32 * (kWarps / KBD);
   static_assert(kWarps % KBG == 0 && kWarps % KBD == 0, "K blocks per item");
-  constexpr size_t gu_smem = kLutBytes + kRedBytes + kMiscBytes + kTokensPerPass * token_stride(KBG * 256);
-  constexpr size_t d_smem = kLutBytes + kRedBytes + kMiscBytes + kTokensPerPass * token_stride(KBD * 256);
+  constexpr size_t gu_smem = kRedBytes + kMiscBytes + kTokensPerPass * token_stride(KBG * 256);
+  constexpr size_t d_smem = kRedBytes + kMiscBytes + kTokensPerPass * token_stride(KBD * 256);
   static int configured_device = -1;
   int dev = 0;
   cudaGetDevice(&dev);

@@ -6,9 +6,10 @@
 namespace bt {
 
 // Device IQ3_S layout: rows in tiles of 16; each 16-row x 256-weight tile
-// (16 GGUF blocks of 110 bytes) is a 1792-byte chunk arranged for the
-// m16n8k32 int8 MMA's A fragments (moe.cu), i.e. 112 bytes per row and block.
-constexpr int kIq3sBlockBytes = 112;
+// (16 GGUF blocks of 110 bytes) is a 2176-byte chunk of 4-bit signed weight
+// codes and per-row scale records arranged for the m16n8k16 MMA's A
+// fragments (moe.cu), i.e. 136 bytes per row and block.
+constexpr int kIq3sBlockBytes = 136;
 
 inline int64_t iq3s_row_bytes(int64_t k) { return k / 256 * kIq3sBlockBytes; }
 

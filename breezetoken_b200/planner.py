@@ -13,7 +13,7 @@ one box: each GPU holds a full replica of the weights and the KV / GDN state
 of its own sequences, with no collective on the data path.
 
 The byte model counts the library's device layout: Q8_0 "q8 rows" for the
-Qwen3.5 checkpoints, bf16 / f32 rows and IQ3_S tile chunks (112 bytes per
+Qwen3.5 checkpoints, bf16 / f32 rows and IQ3_S tile chunks (136 bytes per
 256 weights) for the Qwen3.6-MoE ones, plus per sequence the GDN conv
 window and recurrent state and the f32 KV cache at the planned context.
 ``step_bytes`` is the matching per-step traffic of one decode step on one
@@ -34,7 +34,7 @@ _GIB = 1 << 30
 AUTO_CONTEXT = 8192
 #: Per-GPU reserve for the CUDA context, graphs, workspaces and activations.
 RESERVE_BYTES = 2 * _GIB
-IQ3S_DEVICE_BYTES_PER_256 = 112  # bt_iq3s_row_bytes: the GGUF's 110 + 2 pad
+IQ3S_DEVICE_BYTES_PER_256 = 136  # bt_iq3s_row_bytes: 4-bit codes (128) + scales and d (8)
 IQ3S_BYTES_PER_256 = 110  # the format's own bytes: what a step must read
 
 

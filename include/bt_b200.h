@@ -299,9 +299,13 @@ BT_API int bt_argmax(const float* x, int64_t rows, int64_t n, int32_t* out,
 
 /* ------------------------------------------------------- MoE experts */
 /* Bytes per IQ3_S row of K weights in the device layout (K % 256 == 0):
- * K / 256 * 112.  Rows are stored in tiles of 16; a tile's 16 GGUF blocks of
- * one 256-weight column block form one 1792-byte chunk ordered for the
- * integer tensor-core MMA (chunks of a tile contiguous, tiles in row order). */
+ * K / 256 * 136.  Every weight d * (1 + 2 * scale nibble) * v, v an odd
+ * codebook value in [-15, 15], is stored as the 4-bit code (v + 15) / 2 (a
+ * lossless re-encoding of the GGUF block's codebook index, high bit and
+ * sign); rows in tiles of 16; a tile's 16 GGUF blocks of one 256-weight
+ * column block form one 2176-byte chunk (codes ordered for the fp16
+ * tensor-core MMA's operand fragments, then each row's scales and d),
+ * chunks of a tile contiguous, tiles in row order.                        */
 BT_API int64_t bt_iq3s_row_bytes(int64_t k);
 
 /* GGUF IQ3_S rows (110-byte blocks, quant/dequant.py:164-185) -> the device

@@ -275,7 +275,7 @@ class Emulator:
 
     def bt_repack_iq3_s(self, src, dst, rows, k, stream) -> None:
         raw = _view(src, np.uint8, rows * (k // 256) * 110).copy()
-        _view(dst, np.uint8, rows * (k // 256) * 112)[:] = pack_iq3s_tiles(raw, rows, k)
+        _view(dst, np.uint8, rows * (k // 256) * 136)[:] = pack_iq3s_tiles(raw, rows, k)
         self.packed[dst] = (raw.reshape(rows, -1), rows, k)
 
     def _expert(self, buf: int, e: int, rows: int) -> np.ndarray:

@@ -40,42 +40,51 @@ def layer(cuda):
     return m, ex
 
 
+#: Bit of a code word where code i (weight 8t + i of a lane's sub-block
+#: slice) starts; its 4 bits are at (CODE_BIT[i] + b) % 32 (moe.cu code_bit).
+CODE_BIT = (1, 17, 5, 21, 9, 25, 13, 29)
+
+
+def iq3s_signed_values(raw: np.ndarray, rows: int, k: int) -> np.ndarray:
+    """The signed codebook value v (odd, -15..15) of every weight, (rows, k)
+    int8: weight = d * (1 + 2 * scale nibble) * v (quant/dequant.py:164-185)."""
+    from oracle.dequant import iq3s_grid
+
+    b = np.ascontiguousarray(raw).reshape(rows, k // 256, 110)
+    qs = b[..., 2:66].astype(np.int64)  # (rows, blocks, 64 groups)
+    qh = b[..., 66:74].astype(np.int64)
+    hb = (qh[..., np.arange(64) // 8] >> (np.arange(64) % 8)) & 1
+    grid = iq3s_grid().astype(np.int64) & 255  # (512, 4)
+    mag = grid[qs | (hb << 8)]  # (rows, blocks, 64, 4)
+    signs = b[..., 74:106].astype(np.int64)  # (rows, blocks, 32): byte j = weights 8j .. 8j+7
+    neg = (signs[..., np.arange(256) // 8] >> (np.arange(256) % 8)) & 1
+    v = mag.reshape(rows, k // 256, 256) * (1 - 2 * neg)
+    return v.reshape(rows, k).astype(np.int8)
+
+
 def pack_iq3s_tiles(raw: np.ndarray, rows: int, k: int) -> np.ndarray:
     """The device layout of bt_repack_iq3_s, restated in numpy: per 16-row
-    tile and 256-weight block, a 1792-byte chunk of [qs of rows g (512 B),
-    qs of rows g+8 (512 B), sign words (512 B), qh words (128 B), per-row
-    scales + d (128 B)], lane L = 4g + t holding groups 2t, 2t+1 of every
-    sub-block (quant/dequant.py:164-185 field meanings); group q = 2s + h of
-    a lane's row has its qs byte at byte 4 (q % 4) + q // 4 of the lane's 16,
-    its weight-0/1 signs at bits 15 - q / 31 - q of sign word S0 and its
-    weight-2/3 signs at the same bits of S1."""
+    tile and 256-weight block, a 2176-byte chunk of [4-bit codes (2048 B),
+    per-row scales + d (128 B)].  Code c = (v + 15) / 2 of each weight's
+    signed codebook value v; part j (sub-blocks 2j, 2j+1) at 512 j, lane
+    L = 4g + t's 16 bytes at 512 j + 16 L = the words of (row g, sub-block
+    2j), (row g+8, 2j), (row g, 2j+1), (row g+8, 2j+1); a word holds the
+    codes of weights 8t .. 8t+7 of its sub-block at CODE_BIT."""
     kb = k // 256
-    b = np.ascontiguousarray(raw).reshape(rows // 16, 2, 8, kb, 110)  # (tile, half r, g, block, byte)
-    qs = b[..., 2:66].reshape(rows // 16, 2, 8, kb, 8, 4, 2)  # (.., s, t, h)
-    qs = qs.reshape(rows // 16, 2, 8, kb, 4, 2, 4, 2)  # (.., pair p, S, t, h): s = 2p + S
-    qs = qs.transpose(0, 3, 1, 2, 6, 5, 7, 4).reshape(rows // 16, kb, 2, 512)  # (tile, block, r, g t S h p)
-    sg = b[..., 74:106].reshape(rows // 16, 2, 8, kb, 8, 4).astype(np.uint32)  # (.., s, t)
-    words = np.zeros((rows // 16, 2, 8, kb, 4, 2), np.uint32)  # (.., t, word S0 / S1)
-    for s in range(8):
-        for h in range(2):
-            nib = (sg[..., s, :] >> (4 * h)) & 15
-            q = 2 * s + h
-            for i in range(4):  # weight i of the group: word i // 2, bit 15 - q (+ 16 for odd i)
-                words[..., i >> 1] |= ((nib >> i) & 1) << (16 * (i & 1) + 15 - q)
-    signs = words.transpose(0, 3, 2, 4, 1, 5).reshape(rows // 16, kb, 32 * 4)  # (tile, block, g t r w)
-    qhb = b[..., 66:74].astype(np.uint32)  # (tile, r, g, block, s)
-    qh = np.zeros((rows // 16, kb, 8, 4), np.uint32)  # (tile, block, g, t)
-    for r in range(2):
-        for s in range(8):
-            for h in range(2):
-                for t in range(4):
-                    bit = (qhb[:, r, :, :, s] >> (2 * t + h)) & 1  # (tile, g, block)
-                    qh[:, :, :, t] |= bit.transpose(0, 2, 1) << (16 * r + 2 * s + h)
+    codes = ((iq3s_signed_values(raw, rows, k).astype(np.int64) + 15) >> 1).astype(np.uint64)
+    c = codes.reshape(rows // 16, 2, 8, kb, 8, 4, 8)  # (tile, r, g, block, sub-block, t, i)
+    word = np.zeros(c.shape[:-1], np.uint64)
+    for i in range(8):
+        for bit in range(4):
+            word |= ((c[..., i] >> np.uint64(bit)) & np.uint64(1)) << np.uint64((CODE_BIT[i] + bit) % 32)
+    word = word.astype(np.uint32)  # (tile, r, g, block, sb, t)
+    w = word.reshape(rows // 16, 2, 8, kb, 4, 2, 4)  # (.., part j, S, t)
+    w = w.transpose(0, 3, 4, 2, 6, 5, 1)  # (tile, block, j, g, t, S, r): 16 bytes per lane = (S, r) words
+    codes_b = w.reshape(rows // 16, kb, 2048 // 4).view(np.uint8).reshape(rows // 16, kb, 2048)
+    b = np.ascontiguousarray(raw).reshape(rows // 16, 16, kb, 110)
     rec = np.concatenate([b[..., 106:110], b[..., 0:2], np.zeros(b.shape[:-1] + (2,), np.uint8)], -1)
-    rec = rec.transpose(0, 3, 1, 2, 4).reshape(rows // 16, kb, 128)  # (tile, block, row 0..15, 8 B)
-    chunk = np.concatenate([qs.reshape(rows // 16, kb, 1024), signs.view(np.uint8).reshape(rows // 16, kb, 512),
-                            qh.view(np.uint8).reshape(rows // 16, kb, 128), rec], -1)
-    return chunk.reshape(-1)
+    rec = rec.transpose(0, 2, 1, 3).reshape(rows // 16, kb, 128)  # (tile, block, row 0..15, 8 B)
+    return np.concatenate([codes_b, rec], -1).reshape(-1)
 
 
 def test_iq3s_repack_matches_layout(layer) -> None:
