@@ -373,7 +373,6 @@ __global__ void __launch_bounds__(kThreads, 2)
 // ------------------------------------------------------------------ tcgen05 path
 constexpr int kUmmaRows = 128;  // weight rows per CTA: the MMA's M, one TMEM lane per row
 constexpr int kUmmaKStage = 64;  // K columns per stage (one 128-byte swizzle row): four MMAs of K 16
-constexpr int kUmmaStages = 5;
 __device__ int g_umma_timeouts;  // mbarrier waits that gave up
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -489,37 +488,49 @@ __device__ __forceinline__ void tmem_ld24(uint32_t taddr, uint32_t (&r)[24]) {
       : "memory");
 }
 
-template <int NT>
-constexpr int umma_stage_bytes() {
-  return (kUmmaRows + 3 * NT) * kUmmaKStage * 2;
+// RB row blocks of 128 per CTA share each stage's token planes (the B
+// operand): with RB = 2 a stage carries 32 KB of weights per 24 KB of planes
+// instead of 16 per 24.  Each row's accumulation (its K split and the K
+// order inside it) is the same for RB = 1 and 2.
+template <int RB>
+constexpr int umma_stages() {
+  return RB == 1 ? 5 : 4;
 }
-template <int NT>
+template <int NT, int RB>
+constexpr int umma_stage_bytes() {
+  return (RB * kUmmaRows + 3 * NT) * kUmmaKStage * 2;
+}
+template <int NT, int RB>
 constexpr int umma_smem_bytes() {  // stages + alignment slack
-  return kUmmaStages * umma_stage_bytes<NT>() + 1024;
+  return umma_stages<RB>() * umma_stage_bytes<NT, RB>() + 1024;
 }
 
-// Block (row block, split, token chunk): rows [128 x, 128 x + 128), K
+// Block (row block, split, token chunk): rows [128 RB x, 128 RB (x + 1)), K
 // columns [K/S split, K/S (split + 1)), tokens [NT z, NT z + NT).  `tmw`
 // maps W (N rows x K), `tmx` the planes ((3 T) rows x K, row 3 t + plane);
-// both with 64-column boxes, of 128 and 3 NT rows.
-template <int NT>
+// both with 64-column boxes, of 128 and 3 NT rows.  Row blocks past N load
+// zeros (TMA fill) and store nothing.
+template <int NT, int RB>
 __global__ void __launch_bounds__(kThreads, 1)
     linear_rows_umma_kernel(const __grid_constant__ CUtensorMap tmw, const __grid_constant__ CUtensorMap tmx,
                             const __nv_bfloat16* __restrict__ w, float* __restrict__ y, int n, int k, int t_total,
                             int splits) {
   constexpr int NB = 3 * NT;  // B rows (token-major: 3 t + plane) = the MMA's N
-  constexpr int A_BYTES = kUmmaRows * kUmmaKStage * 2, STAGE = umma_stage_bytes<NT>();
-  constexpr uint32_t COLS = NB <= 64 ? 64 : NB <= 128 ? 128 : 256;  // TMEM columns (power of 2 >= N)
+  constexpr int S = umma_stages<RB>(), ROWS = RB * kUmmaRows;
+  constexpr int W_BYTES = kUmmaRows * kUmmaKStage * 2, A_BYTES = RB * W_BYTES, STAGE = umma_stage_bytes<NT, RB>();
+  constexpr uint32_t ACC = NB <= 64 ? 64 : NB <= 128 ? 128 : 256;  // TMEM columns of one accumulator
+  constexpr uint32_t COLS = RB * ACC;                             // a power of 2 (RB = 1, 2)
   constexpr uint32_t IDESC = umma_idesc<NB>();
   static_assert(NB % 16 == 0 && NB <= 256, "M = 128 takes N = 16 .. 256 in steps of 16");
-  static_assert(NT * kUmmaRows * 4 <= kUmmaStages * STAGE, "partial sums reuse the stages");
-  static_assert(A_BYTES % 1024 == 0 && STAGE % 1024 == 0, "swizzle atoms at 1024-byte boundaries");
+  static_assert(RB == 1 || RB == 2, "one or two row blocks per CTA");
+  static_assert(NT * ROWS * 4 <= S * STAGE, "partial sums reuse the stages");
+  static_assert(W_BYTES % 1024 == 0 && STAGE % 1024 == 0, "swizzle atoms at 1024-byte boundaries");
   extern __shared__ uint8_t sm_raw[];
-  __shared__ __align__(8) uint64_t full[kUmmaStages], empty[kUmmaStages], done;
+  __shared__ __align__(8) uint64_t full[S], empty[S], done;
   __shared__ uint32_t s_tmem;
   __shared__ int s_abort;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int row0 = blockIdx.x * kUmmaRows, split = blockIdx.y, tok0 = blockIdx.z * NT;
+  const int row0 = blockIdx.x * ROWS, split = blockIdx.y, tok0 = blockIdx.z * NT;
   const int kspan = k / splits, kbeg = split * kspan, nst = kspan / kUmmaKStage;
   // stage buffers at a 1024-byte boundary (128-byte swizzle atoms)
   uint8_t* sm = sm_raw + ((1024u - (smem_u32(sm_raw) & 1023u)) & 1023u);
@@ -533,7 +544,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
   if (threadIdx.x == 32) {
 #pragma unroll
-    for (int b = 0; b < kUmmaStages; ++b) {
+    for (int b = 0; b < S; ++b) {
       mbar_init(&full[b], 1);
       mbar_init(&empty[b], 1);
     }
@@ -543,8 +554,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmw)) : "memory");
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmx)) : "memory");
   }
-  if (threadIdx.x >= 64 && threadIdx.x < 64 + kUmmaRows)  // this block's weight slice into L2
-    prefetch_l2(w + static_cast<int64_t>(row0 + threadIdx.x - 64) * k + kbeg, static_cast<uint32_t>(kspan * 2));
+  for (int r = static_cast<int>(threadIdx.x) - 64; r >= 0 && r < ROWS; r += kThreads - 64)  // weight slice into L2
+    if (row0 + r < n) prefetch_l2(w + static_cast<int64_t>(row0 + r) * k + kbeg, static_cast<uint32_t>(kspan * 2));
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -557,31 +568,34 @@ __global__ void __launch_bounds__(kThreads, 1)
     // released it; after a wait gave up nothing new is issued
     int issued = 0;
     for (int st = 0; st < nst; ++st) {
-      const int b = st % kUmmaStages;
-      if (st >= kUmmaStages && !mbar_wait(&empty[b], ((st / kUmmaStages) - 1) & 1, &s_abort)) break;
+      const int b = st % S;
+      if (st >= S && !mbar_wait(&empty[b], ((st / S) - 1) & 1, &s_abort)) break;
       mbar_arrive_expect_tx(&full[b], STAGE);
       const uint32_t sa = sbase + b * STAGE;
       const int kk = kbeg + st * kUmmaKStage;
-      tma_load_2d(sa, &tmw, kk, row0, &full[b]);
+#pragma unroll
+      for (int j = 0; j < RB; ++j) tma_load_2d(sa + j * W_BYTES, &tmw, kk, row0 + j * kUmmaRows, &full[b]);
       tma_load_2d(sa + A_BYTES, &tmx, kk, 3 * tok0, &full[b]);
       issued = st + 1;
     }
     if (s_abort) {
       // each buffer has at most one copy in flight (its last issued stage):
       // let them land before the stages are overwritten below
-      for (int st = issued > kUmmaStages ? issued - kUmmaStages : 0; st < issued; ++st)
-        mbar_drain(&full[st % kUmmaStages], (st / kUmmaStages) & 1);
+      for (int st = issued > S ? issued - S : 0; st < issued; ++st) mbar_drain(&full[st % S], (st / S) & 1);
     }
   } else if (threadIdx.x == 32) {
     // MMA issuer: four K-16 steps per stage, then the stage's buffer goes back
     for (int st = 0; st < nst; ++st) {
-      const int b = st % kUmmaStages;
-      if (!mbar_wait(&full[b], (st / kUmmaStages) & 1, &s_abort)) break;
+      const int b = st % S;
+      if (!mbar_wait(&full[b], (st / S) & 1, &s_abort)) break;
       tc_fence_after();
       const uint32_t a0 = sbase + b * STAGE, b0 = a0 + A_BYTES;
 #pragma unroll
       for (int s4 = 0; s4 < kUmmaKStage / 16; ++s4)
-        umma_bf16(tmem, umma_desc(a0 + 32 * s4), umma_desc(b0 + 32 * s4), IDESC, (st > 0 || s4 > 0) ? 1u : 0u);
+#pragma unroll
+        for (int j = 0; j < RB; ++j)
+          umma_bf16(tmem + j * ACC, umma_desc(a0 + j * W_BYTES + 32 * s4), umma_desc(b0 + 32 * s4), IDESC,
+                    (st > 0 || s4 > 0) ? 1u : 0u);
       umma_commit(&empty[b]);
     }
     umma_commit(&done);  // every MMA issued by this thread, also after an abort
@@ -591,20 +605,23 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   __syncthreads();  // the producer's drained copies have landed before the stages are reused
 
-  // TMEM lane r = weight row row0 + r, column 3 t + plane; warp w reads
-  // lanes 32 (w % 4) .. + 32 and tokens [NT/2 (w / 4), NT/2 (w / 4 + 1))
-  float* part = reinterpret_cast<float*>(sm);  // [token][row], NT x 128 (every TMA landed, every MMA done)
+  // TMEM lane r, accumulator j = weight row row0 + 128 j + r, column
+  // 128 j... + 3 t + plane; warp w reads lanes 32 (w % 4) .. + 32 and
+  // tokens [NT/2 (w / 4), NT/2 (w / 4 + 1))
+  float* part = reinterpret_cast<float*>(sm);  // [token][row], NT x ROWS (every TMA landed, every MMA done)
   const int lq = warp & 3, half = warp >> 2;
   const uint32_t tl = tmem + (static_cast<uint32_t>(32 * lq) << 16);
 #pragma unroll
-  for (int t8 = half * (NT / 2); t8 < (half + 1) * (NT / 2); t8 += 8) {
-    uint32_t r[24];
-    tmem_ld24(tl + 3 * t8, r);
+  for (int j = 0; j < RB; ++j)
 #pragma unroll
-    for (int i = 0; i < 8; ++i)
-      part[(t8 + i) * kUmmaRows + 32 * lq + lane] =
-          (__uint_as_float(r[3 * i]) + __uint_as_float(r[3 * i + 1])) + __uint_as_float(r[3 * i + 2]);
-  }
+    for (int t8 = half * (NT / 2); t8 < (half + 1) * (NT / 2); t8 += 8) {
+      uint32_t r[24];
+      tmem_ld24(tl + j * ACC + 3 * t8, r);
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+        part[(t8 + i) * ROWS + j * kUmmaRows + 32 * lq + lane] =
+            (__uint_as_float(r[3 * i]) + __uint_as_float(r[3 * i + 1])) + __uint_as_float(r[3 * i + 2]);
+    }
   tc_fence_before();
   __syncthreads();
   if (warp == 0) {
@@ -613,12 +630,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
   cg::cluster_group cluster = cg::this_cluster();
   cluster.sync();  // every split's partial sums are in place
-  const int per = NT * kUmmaRows / splits;
+  const int per = NT * ROWS / splits;
 #pragma unroll 2
   for (int e = split * per + threadIdx.x; e < (split + 1) * per; e += kThreads) {
     const float s = split_sum(cluster, part, e, splits);
-    const int tok = tok0 + e / kUmmaRows;
-    if (tok < t_total) y[static_cast<int64_t>(tok) * n + row0 + e % kUmmaRows] = s;
+    const int tok = tok0 + e / ROWS, row = row0 + e % ROWS;
+    if (tok < t_total && row < n) y[static_cast<int64_t>(tok) * n + row] = s;
   }
   cluster.sync();  // no CTA leaves while another still reads its shared memory
 }
@@ -697,10 +714,17 @@ int linear_rows(const void* w, int w_dtype, const void* x_planes, float* y, int6
   const auto* xp = static_cast<const __nv_bfloat16*>(x_planes);
   if (w_dtype == BT_BF16 && t > 16 && n % kUmmaRows == 0) {
     // tensor-core path: 64 tokens per CTA (32 for T <= 32); K split over a
-    // cluster as far as one token chunk's CTAs still fit one wave of 1 per
-    // SM.  The split depends on the rows and K only, not on T, so a token's
-    // outputs are the same bits whichever tokens share the call (a prefill
-    // chunk of many tokens per sequence gets the decode step's sums).
+    // cluster as far as one token chunk's 128-row blocks still fit one wave
+    // of 1 per SM.  The split depends on the rows and K only, not on T, so a
+    // token's outputs are the same bits whichever tokens share the call (a
+    // prefill chunk of many tokens per sequence gets the decode step's sums).
+    // Two 128-row blocks per CTA (sharing each stage's planes) when one
+    // block per CTA would take more than one wave (the head, prefill
+    // chunks) or the K split is 4 or more; measured on B200 at the 35B
+    // shapes: head 231 -> 201 us at 64 tokens, the 2048 x 4096 out-projection
+    // 23 -> 18 us, the 8192 x 2048 one 104 -> 90 us at 512 tokens, while the
+    // decode step's 2048-K projections (<= 128 CTAs, split 2) are faster with
+    // one block per CTA.  Same bits either way.
     const bool wide = t > 32;
     const int nt = wide ? 64 : 32;
     const int64_t blocks = n / kUmmaRows, chunks = (t + nt - 1) / nt;
@@ -709,9 +733,11 @@ int linear_rows(const void* w, int w_dtype, const void* x_planes, float* y, int6
     int splits = 1;
     while (splits < kMaxSplits && blocks * splits * 2 <= sm_count() && k % (kUmmaKStage * splits * 2) == 0)
       splits *= 2;
+    const int rb = (blocks * splits * chunks > sm_count() || splits >= 4) ? 2 : 1;
     cudaLaunchAttribute attr[2];
-    cudaLaunchConfig_t cfg = pdl_config(
-        dim3(static_cast<unsigned>(blocks), static_cast<unsigned>(splits), static_cast<unsigned>(chunks)), stream, attr);
+    cudaLaunchConfig_t cfg = pdl_config(dim3(static_cast<unsigned>((blocks + rb - 1) / rb),
+                                             static_cast<unsigned>(splits), static_cast<unsigned>(chunks)),
+                                        stream, attr);
     attr[1].id = cudaLaunchAttributeClusterDimension;
     attr[1].val.clusterDim.x = 1;
     attr[1].val.clusterDim.y = static_cast<unsigned>(splits);
@@ -722,20 +748,15 @@ int linear_rows(const void* w, int w_dtype, const void* x_planes, float* y, int6
     CUtensorMap tmw, tmx;
     if (!make_map(&tmw, w, n, k, kUmmaRows) || !make_map(&tmx, x_planes, 3 * t, k, 3 * nt))
       return fail(BT_ERR_CUDA, "linear_rows: tensor maps could not be encoded");
-    cudaError_t e;
-    if (wide) {
-      cfg.dynamicSmemBytes = umma_smem_bytes<64>();
-      e = cudaFuncSetAttribute(linear_rows_umma_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               umma_smem_bytes<64>());
-      if (e == cudaSuccess)
-        e = ::bt::launch_ex(&cfg, linear_rows_umma_kernel<64>, tmw, tmx, wb, y, nn, kk, tt, splits);
-    } else {
-      cfg.dynamicSmemBytes = umma_smem_bytes<32>();
-      e = cudaFuncSetAttribute(linear_rows_umma_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               umma_smem_bytes<32>());
-      if (e == cudaSuccess)
-        e = ::bt::launch_ex(&cfg, linear_rows_umma_kernel<32>, tmw, tmx, wb, y, nn, kk, tt, splits);
-    }
+    auto go = [&](auto kernel, int smem) {
+      cfg.dynamicSmemBytes = smem;
+      cudaError_t err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+      return err == cudaSuccess ? ::bt::launch_ex(&cfg, kernel, tmw, tmx, wb, y, nn, kk, tt, splits) : err;
+    };
+    const cudaError_t e = wide ? (rb == 2 ? go(linear_rows_umma_kernel<64, 2>, umma_smem_bytes<64, 2>())
+                                          : go(linear_rows_umma_kernel<64, 1>, umma_smem_bytes<64, 1>()))
+                               : (rb == 2 ? go(linear_rows_umma_kernel<32, 2>, umma_smem_bytes<32, 2>())
+                                          : go(linear_rows_umma_kernel<32, 1>, umma_smem_bytes<32, 1>()));
     if (e != cudaSuccess) return fail_cuda(e, "linear_rows (tcgen05) launch");
     return BT_OK;
   }
