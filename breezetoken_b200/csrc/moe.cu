@@ -46,6 +46,8 @@
 
 #include "errors.h"
 #include "moe.cuh"
+#include "norm_planes.cuh"
+#include "qwen36_layer.cuh"
 
 namespace bt {
 
@@ -716,22 +718,11 @@ __global__ void __launch_bounds__(kThreads) moe_prep_kernel(const int32_t* __res
 }
 
 // ------------------------------------------------------------------ MMA core
-__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
-  uint32_t d;
-  asm("prmt.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(sel));
-  return d;
-}
-
 __device__ __forceinline__ uint4 ld_stream16(const uint8_t* p) {
   uint4 v;
   asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0, %1, %2, %3}, [%4];"
                : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
                : "l"(p));
-  return v;
-}
-__device__ __forceinline__ uint32_t ld_stream4(const uint8_t* p) {
-  uint32_t v;
-  asm volatile("ld.global.nc.L1::no_allocate.u32 %0, [%1];" : "=r"(v) : "l"(p));
   return v;
 }
 
@@ -1451,6 +1442,55 @@ __global__ void moe_combine_kernel(const float* __restrict__ weights, const int3
   }
 }
 
+// moe_combine_kernel's sums for 8 consecutive outputs (dn: element i0 of the
+// token's first pair row), each in routing order with the same roundings,
+// the rows read with 16-byte loads.
+__device__ __forceinline__ void routed_sum8(const int32_t* ids, const float* w, const float* dn, int64_t stride,
+                                            int top_k, int n_experts, float (&a)[8]) {
+#pragma unroll
+  for (int j = 0; j < 8; ++j) a[j] = 0.f;
+  for (int k = 0; k < top_k; ++k) {
+    const int e = ids[k];
+    if (e < 0 || e >= n_experts) continue;
+    const float wk = w[k];
+    const float4 v0 = __ldcg(reinterpret_cast<const float4*>(dn + k * stride));
+    const float4 v1 = __ldcg(reinterpret_cast<const float4*>(dn + k * stride) + 1);
+    const float v[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+#pragma unroll
+    for (int j = 0; j < 8; ++j) a[j] = __fadd_rn(a[j], __fmul_rn(v[j], wk));
+  }
+}
+
+// The combine of moe_combine_kernel followed by the decoder's residual add +
+// RMSNorm + planes (add_rms_norm_planes_row, the same bits as the separate
+// kernels), one 256-thread block per token: the layer's output never goes
+// through memory.  hidden <= 2048.
+__global__ void __launch_bounds__(kThreads) moe_combine_norm_kernel(const float* __restrict__ weights,
+                                                                    const int32_t* __restrict__ ids, int top_k,
+                                                                    int hidden, int n_experts, MoeWs ws, int shared,
+                                                                    MoeNorm nm) {
+  __shared__ float scratch[8];
+  pdl_launch_dependents();
+  pdl_wait();
+  const int64_t tok = blockIdx.x;
+  const int32_t* id = ids + tok * top_k;
+  const float* wt = weights + tok * top_k;
+  const float* dn = ws.dn + tok * top_k * hidden;
+  const float sg = shared ? __ldcg(ws.sgate + tok) : 0.f;
+  auto b_of = [&](int i0, float (&bb)[8]) {
+    routed_sum8(id, wt, dn + i0, hidden, top_k, n_experts, bb);
+    if (shared) {
+      const float4 s0 = __ldcg(reinterpret_cast<const float4*>(ws.sout + tok * hidden + i0));
+      const float4 s1 = __ldcg(reinterpret_cast<const float4*>(ws.sout + tok * hidden + i0) + 1);
+      const float sv[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+#pragma unroll
+      for (int j = 0; j < 8; ++j) bb[j] = __fadd_rn(bb[j], __fmul_rn(sg, sv[j]));  // routed + gate * shared
+    }
+  };
+  add_rms_norm_planes_row(nm.h + tok * hidden, true, b_of, nm.w, nm.h_out + tok * hidden, nm.y + tok * hidden,
+                          static_cast<__nv_bfloat16*>(nm.planes) + tok * 3 * hidden, hidden, nm.eps, scratch);
+}
+
 template <typename Kern, typename... Args>
 cudaError_t launch_pdl(Kern kern, dim3 grid, size_t smem, cudaStream_t stream, Args... args) {
   cudaLaunchConfig_t cfg = {};
@@ -1469,7 +1509,7 @@ cudaError_t launch_pdl(Kern kern, dim3 grid, size_t smem, cudaStream_t stream, A
 template <int KBG, int KBD>
 int launch_all(const uint8_t* gate, const uint8_t* up, const uint8_t* down, const MoeShared* sh, const float* x,
                int64_t t, int hidden, int ffn, int n_experts, const int32_t* ids, const float* weights, int top_k,
-               float* out, MoeWs ws, cudaStream_t stream) {
+               float* out, MoeWs ws, cudaStream_t stream, const MoeNorm* norm) {
   const int shared = sh ? 1 : 0;
   const int p = static_cast<int>(t * top_k);
   // one token selects top_k distinct experts: no grouping needed
@@ -1532,11 +1572,18 @@ int launch_all(const uint8_t* gate, const uint8_t* up, const uint8_t* down, cons
   }
   const int64_t total = t * hidden;
   const int blocks = static_cast<int>(std::min<int64_t>((total + kThreads - 1) / kThreads, 4096));
-  if (e == cudaSuccess && !direct)
+  const bool fused = norm && !direct && hidden <= 8 * kThreads;
+  if (e == cudaSuccess && fused)
+    e = launch_pdl(moe_combine_norm_kernel, dim3(static_cast<unsigned>(t)), 0, stream, weights, ids, top_k, hidden,
+                   n_experts, ws, shared, *norm);
+  else if (e == cudaSuccess && !direct)
     e = launch_pdl(moe_combine_kernel, dim3(blocks), 0, stream, weights, ids, t, top_k, hidden, n_experts, ws, shared,
                    out);
   if (e == cudaSuccess) e = cudaGetLastError();
   if (e != cudaSuccess) return fail_cuda(e, "moe experts launch");
+  if (norm && !fused)
+    return add_rms_norm_planes(norm->h, out, norm->w, norm->h_out, norm->y, norm->planes, t, hidden, norm->eps,
+                               stream);
   return BT_OK;
 }
 
@@ -1587,9 +1634,14 @@ int64_t moe_workspace_bytes(int64_t t, int64_t hidden, int64_t ffn, int64_t shar
 
 int moe_layer_iq3s(const void* gate, const void* up, const void* down, const MoeShared* shared, const float* x,
                    int64_t t, int64_t hidden, int64_t ffn, int64_t n_experts, const int32_t* ids, const float* weights,
-                   int top_k, float* out, void* workspace, cudaStream_t stream) {
+                   int top_k, float* out, void* workspace, cudaStream_t stream, const MoeNorm* norm) {
   if (!gate || !up || !down || !x || !ids || !weights || !out || !workspace)
     return fail(BT_ERR_INVALID, "moe_experts_iq3s: null pointer");
+  if (norm && (!norm->h || !norm->w || !norm->h_out || !norm->y || !norm->planes || hidden % 8 ||
+               ((reinterpret_cast<uintptr_t>(norm->h) | reinterpret_cast<uintptr_t>(norm->w) |
+                 reinterpret_cast<uintptr_t>(norm->h_out) | reinterpret_cast<uintptr_t>(norm->y) |
+                 reinterpret_cast<uintptr_t>(norm->planes) | reinterpret_cast<uintptr_t>(out)) & 15)))
+    return fail(BT_ERR_INVALID, "moe layer + norm: null or misaligned norm buffers");
   if (t < 1 || t * top_k > 4096 || top_k < 1 || top_k > 64 || n_experts < 1 || n_experts > 4096)
     return fail(BT_ERR_UNSUPPORTED, "moe_experts_iq3s serves T * top_k <= 4096 pairs over <= 4096 experts");
   if ((reinterpret_cast<uintptr_t>(gate) | reinterpret_cast<uintptr_t>(up) | reinterpret_cast<uintptr_t>(down) |
@@ -1611,11 +1663,11 @@ int moe_layer_iq3s(const void* gate, const void* up, const void* down, const Moe
   const int h = static_cast<int>(hidden), f = static_cast<int>(ffn), ne = static_cast<int>(n_experts);
   const int k = top_k;
   if (hidden == 2048 && ffn == 512)
-    return launch_all<8, 2>(g, u, d, shared, x, t, h, f, ne, ids, weights, k, out, ws, stream);
+    return launch_all<8, 2>(g, u, d, shared, x, t, h, f, ne, ids, weights, k, out, ws, stream, norm);
   if (hidden == 1024 && ffn == 512)
-    return launch_all<4, 2>(g, u, d, shared, x, t, h, f, ne, ids, weights, k, out, ws, stream);
+    return launch_all<4, 2>(g, u, d, shared, x, t, h, f, ne, ids, weights, k, out, ws, stream, norm);
   if (hidden == 2048 && ffn == 1024)
-    return launch_all<8, 4>(g, u, d, shared, x, t, h, f, ne, ids, weights, k, out, ws, stream);
+    return launch_all<8, 4>(g, u, d, shared, x, t, h, f, ne, ids, weights, k, out, ws, stream, norm);
   return fail(BT_ERR_UNSUPPORTED, "moe_experts_iq3s serves (hidden, ffn) in {(1024,512), (2048,512), (2048,1024)}");
 }
 

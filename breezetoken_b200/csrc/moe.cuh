@@ -29,9 +29,22 @@ struct MoeShared {
 
 int64_t moe_workspace_bytes(int64_t t, int64_t hidden, int64_t ffn, int64_t shared_ffn, int64_t n_experts, int top_k);
 
-// shared may be null (routed experts only).
+// The residual add + RMSNorm + bf16 planes that follow a MoE layer in the
+// decoder: h_out = h + out, y = rms_norm(h_out) * w, planes of y
+// (add_rms_norm_planes); fused into the combine for batches (out is then
+// not written).
+struct MoeNorm {
+  const float* h;
+  const float* w;
+  float* h_out;
+  float* y;
+  void* planes;
+  float eps;
+};
+
+// shared may be null (routed experts only); norm may be null (out only).
 int moe_layer_iq3s(const void* gate, const void* up, const void* down, const MoeShared* shared, const float* x,
                    int64_t t, int64_t hidden, int64_t ffn, int64_t n_experts, const int32_t* ids, const float* weights,
-                   int top_k, float* out, void* workspace, cudaStream_t stream);
+                   int top_k, float* out, void* workspace, cudaStream_t stream, const MoeNorm* norm = nullptr);
 
 }  // namespace bt

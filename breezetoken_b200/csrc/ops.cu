@@ -339,7 +339,9 @@ int argmax(const float* x, int64_t rows, int64_t n, int32_t* out, void* workspac
     return fail(BT_ERR_INVALID, "argmax: bad arguments");
   auto* best = static_cast<unsigned long long*>(workspace);
   auto* counters = reinterpret_cast<uint32_t*>(best + rows);
-  const int64_t blocks = std::min<int64_t>((n + 255) / 256, static_cast<int64_t>(sm_count()) * 4);
+  // about four blocks per SM over all rows (a batch's rows share the grid)
+  const int64_t per_row = std::max<int64_t>(1, (static_cast<int64_t>(sm_count()) * 4 + rows - 1) / rows);
+  const int64_t blocks = std::min<int64_t>((n + 255) / 256, per_row);
   ::bt::note_launch();
   argmax_kernel<<<dim3(static_cast<unsigned>(blocks), static_cast<unsigned>(rows)), 256, 0, stream>>>(x, n, out, best,
                                                                                                      counters);

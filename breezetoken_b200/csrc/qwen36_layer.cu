@@ -21,24 +21,11 @@
 // (backends.py:229-238) and y's three bf16 planes (y = hi + mid + lo) in the
 // same pass, so the projections that read y need no separate split.
 #include "errors.h"
+#include "norm_planes.cuh"
 #include "qwen36_layer.cuh"
 
 namespace bt {
 namespace {
-
-__device__ __forceinline__ uint32_t bf16_pair_rn(float lo, float hi) {
-  const uint32_t a = __bfloat16_as_ushort(__float2bfloat16_rn(lo));
-  const uint32_t b = __bfloat16_as_ushort(__float2bfloat16_rn(hi));
-  return a | (b << 16);
-}
-
-// v = hi + mid + lo with each remainder exact in f32 (bf16 keeps 8 bits).
-__device__ __forceinline__ void split3(float v, float& hi, float& mid, float& lo) {
-  hi = __bfloat162float(__float2bfloat16_rn(v));
-  const float r1 = v - hi;
-  mid = __bfloat162float(__float2bfloat16_rn(r1));
-  lo = r1 - mid;
-}
 
 template <int DIM>
 __device__ __forceinline__ float block_total(float v, float* scratch) {
@@ -161,9 +148,7 @@ __global__ void __launch_bounds__(kGdnStepThreads) gdn_gated_step_kernel(const _
   for (int i = 0; i < R; ++i) S[static_cast<int64_t>(r0 + i) * DIM + c] = s[i];
 }
 
-// One block per row, n % 8 == 0.  Rows of up to 8 * 256 elements are read
-// once: each thread keeps its 8 consecutive elements in registers through
-// the block reduction; longer rows take a second pass.
+// One block of 256 threads per row, n % 8 == 0 (add_rms_norm_planes_row).
 __global__ void __launch_bounds__(256) add_rms_norm_planes_kernel(const float* __restrict__ a,
                                                                    const float* __restrict__ b,
                                                                    const float* __restrict__ w, float* __restrict__ h,
@@ -171,64 +156,13 @@ __global__ void __launch_bounds__(256) add_rms_norm_planes_kernel(const float* _
                                                                    int n, float eps) {
   __shared__ float scratch[8];
   const int64_t row = blockIdx.x;
-  const float* ar = a + row * n;
   const float* br = b ? b + row * n : nullptr;
-  const bool one_pass = n <= 8 * static_cast<int>(blockDim.x);
-  float v[8];
-  float ss = 0.f;
-  for (int i0 = 8 * threadIdx.x; i0 < n; i0 += 8 * blockDim.x) {
-    const float4 a0 = *reinterpret_cast<const float4*>(ar + i0), a1 = *reinterpret_cast<const float4*>(ar + i0 + 4);
-    float x[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
-    if (br) {
-      const float4 b0 = *reinterpret_cast<const float4*>(br + i0), b1 = *reinterpret_cast<const float4*>(br + i0 + 4);
-      const float bb[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
-#pragma unroll
-      for (int j = 0; j < 8; ++j) x[j] = x[j] + bb[j];
-      if (h) {
-        *reinterpret_cast<float4*>(h + row * n + i0) = make_float4(x[0], x[1], x[2], x[3]);
-        *reinterpret_cast<float4*>(h + row * n + i0 + 4) = make_float4(x[4], x[5], x[6], x[7]);
-      }
-    }
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      ss = fmaf(x[j], x[j], ss);
-      v[j] = x[j];
-    }
-  }
-  ss = warp_sum(ss);
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  if (lane == 0) scratch[warp] = ss;
-  __syncthreads();
-  float total = 0.f;
-#pragma unroll
-  for (int i = 0; i < 8; ++i) total += scratch[i];
-  const float r = 1.0f / sqrtf(total / static_cast<float>(n) + eps);
-  for (int i0 = 8 * threadIdx.x; i0 < n; i0 += 8 * blockDim.x) {
-    if (!one_pass) {
-#pragma unroll
-      for (int j = 0; j < 8; ++j) v[j] = br ? ar[i0 + j] + br[i0 + j] : ar[i0 + j];
-    }
-    const float4 w0 = *reinterpret_cast<const float4*>(w + i0), w1 = *reinterpret_cast<const float4*>(w + i0 + 4);
-    const float ww[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
-    float o[8];
-#pragma unroll
-    for (int j = 0; j < 8; ++j) o[j] = __fmul_rn(__fmul_rn(v[j], r), ww[j]);
-    *reinterpret_cast<float4*>(y + row * n + i0) = make_float4(o[0], o[1], o[2], o[3]);
-    *reinterpret_cast<float4*>(y + row * n + i0 + 4) = make_float4(o[4], o[5], o[6], o[7]);
-    uint32_t pk[3][4];
-#pragma unroll
-    for (int j = 0; j < 8; j += 2) {
-      float h0, m0, l0, h1, m1, l1;
-      split3(o[j], h0, m0, l0);
-      split3(o[j + 1], h1, m1, l1);
-      pk[0][j / 2] = bf16_pair_rn(h0, h1);
-      pk[1][j / 2] = bf16_pair_rn(m0, m1);
-      pk[2][j / 2] = bf16_pair_rn(l0, l1);
-    }
-#pragma unroll
-    for (int q = 0; q < 3; ++q)
-      *reinterpret_cast<uint4*>(planes + (row * 3 + q) * n + i0) = make_uint4(pk[q][0], pk[q][1], pk[q][2], pk[q][3]);
-  }
+  auto b_of = [&](int i0, float (&bb)[8]) {
+    const float4 b0 = *reinterpret_cast<const float4*>(br + i0), b1 = *reinterpret_cast<const float4*>(br + i0 + 4);
+    bb[0] = b0.x, bb[1] = b0.y, bb[2] = b0.z, bb[3] = b0.w, bb[4] = b1.x, bb[5] = b1.y, bb[6] = b1.z, bb[7] = b1.w;
+  };
+  add_rms_norm_planes_row(a + row * n, br != nullptr, b_of, w, h ? h + row * n : nullptr, y + row * n,
+                          planes + row * 3 * n, n, eps, scratch);
 }
 
 }  // namespace

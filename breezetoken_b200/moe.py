@@ -136,10 +136,15 @@ class SharedExpert:
 
 
 def moe_forward(ex: IQ3SExperts, shared: SharedExpert | None, x: torch.Tensor, ids: torch.Tensor,
-                weights: torch.Tensor, workspace: torch.Tensor | None = None) -> torch.Tensor:
+                weights: torch.Tensor, workspace: torch.Tensor | None = None, norm: tuple | None = None):
     """Qwen36Moe._moe after routing (model/qwen36_moe.py:634-642) for x (T,
     hidden) f32: the routed experts plus, when given, the shared expert gated
-    by sigmoid(x . gate_inp)."""
+    by sigmoid(x . gate_inp).
+
+    With norm = (h, gamma, eps) the layer's output goes straight into the
+    decoder's residual add and the next RMSNorm (bt_moe_layer_iq3s_add_norm,
+    the same bits as the separate ops) and (h + out, rms_norm(h + out) *
+    gamma, its bf16 planes (T, 3, hidden)) is returned instead of out."""
     x2 = x.float().reshape(-1, ex.hidden).contiguous()
     t = x2.shape[0]
     ids2 = ids.to(torch.int32).reshape(t, -1).contiguous()
@@ -157,10 +162,21 @@ def moe_forward(ex: IQ3SExperts, shared: SharedExpert | None, x: torch.Tensor, i
             raise ValueError(f"shared expert hidden {shared.gate.shape[1]} != {ex.hidden}")
         sh = N.BtMoeShared(shared.gate.data_ptr(), shared.up.data_ptr(), shared.down.data_ptr(),
                            shared.gate_inp.data_ptr(), sffn)
-    N.call("bt_moe_layer_iq3s", ex.gate.data_ptr(), ex.up.data_ptr(), ex.down.data_ptr(),
+    if norm is None:
+        N.call("bt_moe_layer_iq3s", ex.gate.data_ptr(), ex.up.data_ptr(), ex.down.data_ptr(),
+               None if sh is None else ctypes.byref(sh), x2.data_ptr(), t, ex.hidden, ex.ffn, ex.n_experts,
+               ids2.data_ptr(), w2.data_ptr(), top_k, out.data_ptr(), workspace.data_ptr(), _stream())
+        return out
+    h, gamma, eps = norm
+    if h.shape != (t, ex.hidden) or h.dtype != torch.float32 or not h.is_contiguous():
+        raise ValueError(f"residual must be contiguous f32 {(t, ex.hidden)}")
+    h_out, y = torch.empty_like(h), torch.empty_like(h)
+    planes = torch.empty(t, 3, ex.hidden, dtype=torch.bfloat16, device=x2.device)
+    N.call("bt_moe_layer_iq3s_add_norm", ex.gate.data_ptr(), ex.up.data_ptr(), ex.down.data_ptr(),
            None if sh is None else ctypes.byref(sh), x2.data_ptr(), t, ex.hidden, ex.ffn, ex.n_experts,
-           ids2.data_ptr(), w2.data_ptr(), top_k, out.data_ptr(), workspace.data_ptr(), _stream())
-    return out
+           ids2.data_ptr(), w2.data_ptr(), top_k, h.data_ptr(), gamma.data_ptr(), float(eps), h_out.data_ptr(),
+           y.data_ptr(), planes.data_ptr(), out.data_ptr(), workspace.data_ptr(), _stream())
+    return h_out, y, planes
 
 
 class ExpertPool:

@@ -395,14 +395,19 @@ class Qwen36Moe:
                float(cfg.l2_eps), float(cfg.eps), _stream())
         return self._lin(layer["out"], gated)
 
-    def _moe(self, i: int, xn: torch.Tensor, xp: torch.Tensor, ws: torch.Tensor | None = None) -> torch.Tensor:
+    def _moe(self, i: int, xn: torch.Tensor, xp: torch.Tensor, ws: torch.Tensor | None = None,
+             norm: tuple | None = None):
+        """model/qwen36_moe.py:634-642: routing, the IQ3_S experts and the
+        shared expert; with norm = (h, gamma) fused with the residual add and
+        the next RMSNorm + planes: (h, y, planes)."""
         layer = self.layers[i]
         r = route_logits(self._lin(layer["router"], xp), self.cfg.top_k)
         rec = getattr(self, "_route_record", None)
         if rec is not None:  # measurement: each layer's input and routing of this (eager) step
             rec.append((xn.clone(), r.expert_ids.clone(), r.weights.clone()))
         return moe_forward(layer["experts"], layer["shared"], xn, r.expert_ids, r.weights,
-                           self._moe_ws if ws is None else ws)
+                           self._moe_ws if ws is None else ws,
+                           None if norm is None else (norm[0], norm[1], float(self.cfg.eps)))
 
     # ------------------------------------------------------------------ step
     def _step_t(self, tokens: torch.Tensor, pos_t: torch.Tensor, logits: bool, steps: int = 1,
@@ -422,7 +427,7 @@ class Qwen36Moe:
             delta = self._attn(i, xp, pos_t, steps) if i in attn else self._gdn(i, xp, steps)
             h, xn, xp = self._norm_planes(h, delta, layer["norm_post"])
             nxt = self.layers[i + 1]["norm_in"] if i + 1 < cfg.n_layers else self.norm_f
-            h, xn, xp = self._norm_planes(h, self._moe(i, xn, xp, moe_ws), nxt)
+            h, xn, xp = self._moe(i, xn, xp, moe_ws, norm=(h, nxt))
         if not logits:
             return None
         return self._lin(self.head, xp)

@@ -360,6 +360,20 @@ BT_API int bt_moe_layer_iq3s(const void* gate, const void* up, const void* down,
                       const int32_t* ids, const float* weights, int top_k,
                       float* out, void* workspace, void* stream);
 
+/* bt_moe_layer_iq3s followed by the decoder's residual add + RMSNorm + bf16
+ * planes (bt_add_rms_norm_planes(h, out, w, eps, h_out, y, planes):
+ * model/qwen36_moe.py:658-662 with the next layer's input norm), the same
+ * bits as the two calls.  For T > 1 the combine and the norm run as one
+ * kernel and `out` (T x hidden f32) is not written; for T == 1 it is the
+ * layer's output.  All buffers 16-byte aligned.                          */
+BT_API int bt_moe_layer_iq3s_add_norm(const void* gate, const void* up, const void* down,
+                                      const BtMoeShared* shared, const float* x, int64_t t,
+                                      int64_t hidden, int64_t ffn, int64_t n_experts,
+                                      const int32_t* ids, const float* weights, int top_k,
+                                      const float* h, const float* w, float eps, float* h_out,
+                                      float* y, void* planes, float* out, void* workspace,
+                                      void* stream);
+
 /* ------------------------------------------------- Qwen3.5 decode step */
 typedef struct BtQwen35Dims {
   int32_t hidden, n_layers, n_heads, n_kv, head_dim, rope_dim, ffn, vocab;

@@ -285,6 +285,12 @@ class Emulator:
             self.dense[key] = dequant_iq3_s(raw[e * rows : (e + 1) * rows], rows, k)
         return self.dense[key]
 
+    def bt_moe_layer_iq3s_add_norm(self, gate, up, down, shared, x, t, hidden, ffn, n_experts, ids, weights, top_k,
+                                   h, w, eps, h_out, y, planes, out, ws, stream) -> None:
+        self.bt_moe_layer_iq3s(gate, up, down, shared, x, t, hidden, ffn, n_experts, ids, weights, top_k, out, ws,
+                               stream)
+        self.bt_add_rms_norm_planes(h, out, w, h_out, y, planes, t, hidden, eps, stream)
+
     def bt_moe_layer_iq3s(self, gate, up, down, shared, x, t, hidden, ffn, n_experts, ids, weights, top_k, out, ws,
                           stream) -> None:
         xv = _view(x, F32, t * hidden).reshape(t, hidden)

@@ -302,3 +302,30 @@ def test_moe_layer_config4_full_shape(layer256, t) -> None:
                                                                  m["sh_gate_inp"])
         for got in outs:
             _close(got[i], want)
+
+
+@pytest.mark.parametrize("t", [1, 8, 9, 64])
+def test_moe_layer_add_norm_equals_layer_then_norm(layer256, t) -> None:
+    """bt_moe_layer_iq3s_add_norm (the combine fused with the residual add,
+    RMSNorm and bf16 planes for T > 1) gives the bits of bt_moe_layer_iq3s
+    followed by bt_add_rms_norm_planes, on the static (T <= 8), pulled (T > 8)
+    and one-token paths."""
+    from breezetoken_b200.moe import moe_forward, route_logits
+    from breezetoken_b200.synth import moe_layer_inputs
+
+    m, ex, se = layer256
+    xh, lh = moe_layer_inputs(t)
+    x, logits = torch.from_numpy(xh).cuda(), torch.from_numpy(lh).cuda()
+    r = route_logits(logits, 8)
+    rng = np.random.default_rng(57)
+    h = torch.from_numpy(rng.standard_normal((t, 2048), dtype=np.float32)).cuda()
+    gamma = torch.from_numpy(1 + 0.02 * rng.standard_normal(2048, dtype=np.float32)).cuda()
+    out = moe_forward(ex, se, x, r.expert_ids, r.weights)
+    h1, y1 = torch.empty_like(h), torch.empty_like(h)
+    p1 = torch.empty(t, 3, 2048, dtype=torch.bfloat16, device="cuda")
+    N.call("bt_add_rms_norm_planes", h.data_ptr(), out.data_ptr(), gamma.data_ptr(), h1.data_ptr(), y1.data_ptr(),
+           p1.data_ptr(), t, 2048, 1e-6, 0)
+    h2, y2, p2 = moe_forward(ex, se, x, r.expert_ids, r.weights, norm=(h, gamma, 1e-6))
+    assert torch.equal(h2, h1)
+    assert torch.equal(y2, y1)
+    assert torch.equal(p2, p1)

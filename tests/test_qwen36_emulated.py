@@ -43,7 +43,8 @@ def test_qwen36_host_composition_reproduces_reference(emulated, qwen36_tiny_gguf
     assert toks == g["tokens"][:steps].tolist(), f"margins {g['margins'][:steps]}"
     # every entry point the mirror's decode path uses was exercised
     assert {"bt_linear_rows", "bt_gdn_gated_scan", "bt_add_rms_norm_planes", "bt_attention_layer",
-            "bt_moe_layer_iq3s", "bt_moe_route", "bt_conv_silu_scan", "bt_bf16_planes", "bt_argmax"} <= emulated.names
+            "bt_moe_layer_iq3s_add_norm", "bt_moe_route", "bt_conv_silu_scan", "bt_bf16_planes",
+            "bt_argmax"} <= emulated.names
     m.close()
 
 
