@@ -720,11 +720,11 @@ int linear_rows(const void* w, int w_dtype, const void* x_planes, float* y, int6
     // prefill chunk of many tokens per sequence gets the decode step's sums).
     // Two 128-row blocks per CTA (sharing each stage's planes) when one
     // block per CTA would take more than one wave (the head, prefill
-    // chunks) or the K split is 4 or more; measured on B200 at the 35B
-    // shapes: head 231 -> 201 us at 64 tokens, the 2048 x 4096 out-projection
+    // chunks) or the K split is 8; measured on B200 at the 35B shapes: head
+    // 231 -> 201 us at 64 tokens, the 2048 x 4096 out-projection (split 8)
     // 23 -> 18 us, the 8192 x 2048 one 104 -> 90 us at 512 tokens, while the
-    // decode step's 2048-K projections (<= 128 CTAs, split 2) are faster with
-    // one block per CTA.  Same bits either way.
+    // decode step's 4096 x 2048 (split 4) and 8192 x 2048 (split 2)
+    // projections are faster with one block per CTA.  Same bits either way.
     const bool wide = t > 32;
     const int nt = wide ? 64 : 32;
     const int64_t blocks = n / kUmmaRows, chunks = (t + nt - 1) / nt;
@@ -733,7 +733,7 @@ int linear_rows(const void* w, int w_dtype, const void* x_planes, float* y, int6
     int splits = 1;
     while (splits < kMaxSplits && blocks * splits * 2 <= sm_count() && k % (kUmmaKStage * splits * 2) == 0)
       splits *= 2;
-    const int rb = (blocks * splits * chunks > sm_count() || splits >= 4) ? 2 : 1;
+    const int rb = (blocks * splits * chunks > sm_count() || splits >= 8) ? 2 : 1;
     cudaLaunchAttribute attr[2];
     cudaLaunchConfig_t cfg = pdl_config(dim3(static_cast<unsigned>((blocks + rb - 1) / rb),
                                              static_cast<unsigned>(splits), static_cast<unsigned>(chunks)),

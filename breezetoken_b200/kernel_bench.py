@@ -159,6 +159,59 @@ def bench_gdn(batch: int, steps: int, heads: int = 16, dim: int = 128) -> dict:
                     "stays in L2 between steps); l2_flushed: a 256 MB read before every step"}
 
 
+def bench_gdn_scan(batch: int, steps: int, iters: int = 5, heads: int = 16, dim: int = 128) -> dict:
+    """The config-2 op's `steps` tokens as one prefill scan (bt_gdn_prefill):
+    q/k/v (steps, B, 16, 128) bf16, g/beta (steps, B, 16) f32, state read and
+    written once; L2 flushed before each launch.  Compared with `steps`
+    launches of the decode step on the same inputs."""
+    gen = torch.Generator(device="cuda").manual_seed(1)
+    q = torch.nn.functional.normalize(torch.randn(steps, batch, heads, dim, device="cuda", generator=gen), dim=-1)
+    k = torch.nn.functional.normalize(torch.randn(steps, batch, heads, dim, device="cuda", generator=gen), dim=-1)
+    q, k = q.to(torch.bfloat16), k.to(torch.bfloat16)
+    v = torch.randn(steps, batch, heads, dim, device="cuda", generator=gen).to(torch.bfloat16)
+    g = -torch.nn.functional.softplus(torch.randn(steps, batch, heads, device="cuda", generator=gen))
+    beta = torch.randn(steps, batch, heads, device="cuda", generator=gen)
+    state = torch.zeros(batch, heads, dim, dim, device="cuda")
+    out = torch.empty(steps, batch, heads, dim, device="cuda")
+    flush = torch.ones(256 << 20, dtype=torch.uint8, device="cuda")
+    s = torch.cuda.Stream()
+    lib = N.load()
+    nk = heads * dim
+
+    def scan():
+        N.check(lib.bt_gdn_prefill(q.data_ptr(), k.data_ptr(), v.data_ptr(), N.BT_BF16, nk, nk, nk, batch * nk,
+                                   batch * nk, batch * nk, g.data_ptr(), heads, batch * heads, beta.data_ptr(), heads,
+                                   batch * heads, state.data_ptr(), out.data_ptr(), nk, batch * nk, steps, batch,
+                                   heads, heads, dim, 1.0, 1e-6, s.cuda_stream), "gdn_prefill")
+
+    def steps_loop():
+        for t in range(steps):
+            N.check(lib.bt_gdn_decode(q[t].data_ptr(), k[t].data_ptr(), v[t].data_ptr(), N.BT_BF16, g[t].data_ptr(),
+                                      beta[t].data_ptr(), state.data_ptr(), out[t].data_ptr(), batch, heads, heads,
+                                      dim, 1.0, 1e-6, s.cuda_stream), "gdn_decode")
+
+    def timed(fn) -> float:
+        tot = 0.0
+        with torch.cuda.stream(s):
+            for i in range(iters + 1):
+                flush.sum(dtype=torch.int32)
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record(s)
+                fn()
+                e1.record(s)
+                e1.synchronize()
+                if i:
+                    tot += e0.elapsed_time(e1) / 1e3
+        return tot / iters
+
+    scan_s, loop_s = timed(scan), timed(steps_loop)
+    nbytes = batch * heads * dim * dim * 4 * 2 + steps * batch * heads * (3 * dim * 2 + 2 * 4 + dim * 4)
+    return {"kernel": "gdn_prefill", "batch": batch, "steps": steps, "us": scan_s * 1e6,
+            "us_per_token": scan_s * 1e6 / steps, "decode_steps_us": loop_s * 1e6, "speedup": loop_s / scan_s,
+            "bytes": nbytes, "gbs": nbytes / scan_s / 1e9,
+            "note": "one launch over all steps (state on chip) vs one decode launch per step; L2 flushed before each"}
+
+
 def attn_inputs(batch: int, ctx: int, seed: int = 2):
     """The flash-decode benchmark's inputs (8 q heads, 2 KV heads of 256, one
     query per sequence, bf16 K/V N(0, 1), uniform length ctx), drawn on the
@@ -415,6 +468,7 @@ def main() -> None:
     b = sub.add_parser("gdn")
     b.add_argument("--batch", type=int, default=1)
     b.add_argument("--steps", type=int, default=256)
+    b.add_argument("--scan", action="store_true", help="all steps as one prefill scan (bt_gdn_prefill)")
     c = sub.add_parser("attn")
     c.add_argument("--batch", type=int, default=1)
     c.add_argument("--ctx", type=int, default=8192)
@@ -454,7 +508,7 @@ def main() -> None:
     elif args.cmd == "moe":
         r = bench_moe(args.tokens, args.iters, shared=not args.no_shared)
     elif args.cmd == "gdn":
-        r = bench_gdn(args.batch, args.steps)
+        r = bench_gdn_scan(args.batch, args.steps) if args.scan else bench_gdn(args.batch, args.steps)
     else:
         r = bench_attn(args.batch, args.ctx, args.splits, args.iters)
     if r is not None:
