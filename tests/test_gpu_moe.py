@@ -276,7 +276,7 @@ class _DequantCache:
         return out
 
 
-@pytest.mark.parametrize("t", [1, 8, 64])
+@pytest.mark.parametrize("t", [1, 8, 16, 64])
 def test_moe_layer_config4_full_shape(layer256, t) -> None:
     """The MoE-layer benchmark exactly as measured: 256 experts, top-8 over
     N(0, 1) router logits, T tokens of bf16 N(0, 1) activations, seed 3:
@@ -304,11 +304,11 @@ def test_moe_layer_config4_full_shape(layer256, t) -> None:
             _close(got[i], want)
 
 
-@pytest.mark.parametrize("t", [1, 8, 9, 64])
+@pytest.mark.parametrize("t", [1, 8, 16, 17, 64])
 def test_moe_layer_add_norm_equals_layer_then_norm(layer256, t) -> None:
     """bt_moe_layer_iq3s_add_norm (the combine fused with the residual add,
     RMSNorm and bf16 planes for T > 1) gives the bits of bt_moe_layer_iq3s
-    followed by bt_add_rms_norm_planes, on the static (T <= 8), pulled (T > 8)
+    followed by bt_add_rms_norm_planes, on the static (T <= 16), pulled (T > 16)
     and one-token paths."""
     from breezetoken_b200.moe import moe_forward, route_logits
     from breezetoken_b200.synth import moe_layer_inputs
