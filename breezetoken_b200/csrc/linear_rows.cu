@@ -17,7 +17,7 @@
 // MMAs).  Before the dependency wait each warp bulk-prefetches its weight
 // slices into L2: the weights never depend on earlier kernels.
 //
-// More than 16 tokens with bf16 weights (the batched decode of many
+// More than 8 tokens with bf16 weights (the batched decode of many
 // sequences) run as a tiled product instead, where the x planes would
 // otherwise be re-read from L2 by every 16-row block: a block owns 64 rows
 // and up to 64 tokens, and stages 32-column slices of its weight rows and of
@@ -371,6 +371,11 @@ __global__ void __launch_bounds__(kThreads, 2)
 }
 
 // ------------------------------------------------------------------ tcgen05 path
+// bf16 projections of more than this many tokens take a tensor-core path
+// (measured at the 35B shapes: 16 tokens on tcgen05 with a 32-token tile
+// 8192 x 2048 12.7 us and the head 164 us, against 19.5 and 210 us on the
+// per-tile path, which stays ahead at 8 tokens: 9.6 and 137 us).
+constexpr int64_t kTensorMinTokens = 8;
 constexpr int kUmmaRows = 128;  // weight rows per CTA: the MMA's M, one TMEM lane per row
 constexpr int kUmmaKStage = 64;  // K columns per stage (one 128-byte swizzle row): four MMAs of K 16
 __device__ int g_umma_timeouts;  // mbarrier waits that gave up
@@ -712,7 +717,7 @@ int linear_rows(const void* w, int w_dtype, const void* x_planes, float* y, int6
   if ((reinterpret_cast<uintptr_t>(w) | reinterpret_cast<uintptr_t>(x_planes)) & 15)
     return fail(BT_ERR_INVALID, "linear_rows: w and the planes must be 16-byte aligned");
   const auto* xp = static_cast<const __nv_bfloat16*>(x_planes);
-  if (w_dtype == BT_BF16 && t > 16 && n % kUmmaRows == 0) {
+  if (w_dtype == BT_BF16 && t > kTensorMinTokens && n % kUmmaRows == 0) {
     // tensor-core path: 64 tokens per CTA (32 for T <= 32); K split over a
     // cluster as far as one token chunk's 128-row blocks still fit one wave
     // of 1 per SM.  The split depends on the rows and K only, not on T, so a
@@ -760,7 +765,7 @@ int linear_rows(const void* w, int w_dtype, const void* x_planes, float* y, int6
     if (e != cudaSuccess) return fail_cuda(e, "linear_rows (tcgen05) launch");
     return BT_OK;
   }
-  if (w_dtype == BT_BF16 && t > 16 && n % kTileRows == 0) {
+  if (w_dtype == BT_BF16 && t > kTensorMinTokens && n % kTileRows == 0) {
     // tiled path: K split over a cluster as far as one token chunk's blocks
     // still fit one wave of 2 per SM (rows and K decide it, not T)
     const int64_t blocks = n / kTileRows, chunks = (t + 63) / 64;

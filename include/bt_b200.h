@@ -103,7 +103,7 @@ BT_API int bt_linear_rows(const void* w, int w_dtype, const void* x_planes, floa
                    int64_t n, int64_t k, int64_t t, void* stream);
 
 /* Diagnostic without a reference counterpart: how many bounded mbarrier
- * waits of bt_linear_rows' tensor-core path (tcgen05, > 16 tokens, N % 128
+ * waits of bt_linear_rows' tensor-core path (tcgen05, > 8 tokens, N % 128
  * == 0) gave up since the last call (0 unless the pipeline broke).
  * Synchronises the device and resets the count; -1 if it cannot be read.  */
 BT_API int bt_linear_rows_timeouts(void);

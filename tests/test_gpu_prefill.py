@@ -15,7 +15,7 @@ same per-token arithmetic with the state on chip between tokens, so:
 * a chunked prefill of the 4-layer config-5-shaped model reaches the same
   greedy tokens as a token-by-token one, with logits within 1e-4 of scale
   (4 sequences: the token-by-token steps project 4 tokens on the CUDA cores,
-  the chunks 80 on the tensor cores; with more than 16 sequences both take
+  the chunks 80 on the tensor cores; with more than 8 sequences both take
   the tensor cores and the full-shape test in test_gpu_qwen36.py finds the
   same bits).
 """
