@@ -340,7 +340,35 @@ def bench_moe(tokens: int, iters: int, shared: bool = True) -> dict:
             "l2": "flushed before each call (256 MB read)"}
 
 
-def bench_qwen36(batch: int, prompt: int, steps: int, layers: int) -> dict | None:
+def _kernel_timeline(run, n_steps: int) -> dict:
+    """Device timeline of `run()` (n_steps decode steps) under the CUDA
+    profiling interface (torch.profiler): per kernel name the launches and the
+    summed device time per step, and the span from the first kernel's start
+    to the last one's end per step.  Kernels launched early with programmatic
+    dependent launch count their wait for the predecessor, so the per-kernel
+    sums exceed the span."""
+    import collections
+
+    from torch.profiler import ProfilerActivity, profile
+
+    torch.cuda.synchronize()
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        run()
+        torch.cuda.synchronize()
+    evs = [e for e in prof.events() if e.device_type == torch.autograd.DeviceType.CUDA and e.time_range.elapsed_us() > 0
+           and "Memcpy" not in e.name and "Memset" not in e.name]
+    span = max(e.time_range.end for e in evs) - min(e.time_range.start for e in evs)
+    agg = collections.defaultdict(lambda: [0, 0.0])
+    for e in evs:
+        name = e.name.replace("(anonymous namespace)::", "").split("(")[0].replace("void ", "").replace("bt::", "")
+        agg[name][0] += 1
+        agg[name][1] += e.time_range.elapsed_us()
+    rows = sorted(agg.items(), key=lambda kv: -kv[1][1])
+    return {"span_us_per_step": span / n_steps, "kernels_per_step": len(evs) / n_steps,
+            "kernels": [{"kernel": k, "launches_per_step": c / n_steps, "us_per_step": t / n_steps} for k, (c, t) in rows]}
+
+
+def bench_qwen36(batch: int, prompt: int, steps: int, layers: int, timeline: bool = False) -> dict | None:
     """The 35B-A3B decode benchmark: `batch` sequences of a `prompt`-token random prompt,
     fed in lockstep, then `steps` greedy steps timed with CUDA events; seeded
     random weights of the Qwen3.6-35B-A3B shape (with `layers` layers) built
@@ -372,8 +400,7 @@ def bench_qwen36(batch: int, prompt: int, steps: int, layers: int) -> dict | Non
     rng = np.random.default_rng(4 + rank)
     toks = torch.from_numpy(rng.integers(0, spec.vocab, (prompt, local))).cuda()
     t0 = time.time()
-    for i in range(prompt - 1):
-        m._step(toks[i], i, logits=False)
+    m.prefill(toks[: prompt - 1].t().contiguous())  # the chunked batched prefill
     nxt = m.decode_batch(toks[prompt - 1], prompt - 1)
     torch.cuda.synchronize()
     prefill_s = time.time() - t0
@@ -391,6 +418,11 @@ def bench_qwen36(batch: int, prompt: int, steps: int, layers: int) -> dict | Non
     sec, prefill_s = max_over_ranks([e0.elapsed_time(e1) / 1e3, prefill_s], "cuda")
     if world > 1:
         dist.barrier()
+    tl = None
+    if timeline and rank == 0:
+        n_tl = min(steps, 4)
+        m.set_decode(nxt, prompt)
+        tl = _kernel_timeline(lambda: m.replay(n_tl), n_tl)
     cfg = m.cfg
     # per-step algorithmic bytes (bf16 non-expert weights without the
     # embedding gather, selected experts at the expected number of distinct
@@ -414,7 +446,7 @@ def bench_qwen36(batch: int, prompt: int, steps: int, layers: int) -> dict | Non
             "scaling": "strong (64 sequences split over the GPUs)", "ms_per_step": sec / steps * 1e3,
             "host_enqueue_ms_per_step": host / steps * 1e3, "prefill_s": prefill_s,
             "expected_unique_experts": u, "step_bytes_per_gpu": step_bytes,
-            "gbs_per_gpu": step_bytes * steps / sec / 1e9}
+            "gbs_per_gpu": step_bytes * steps / sec / 1e9, **({"timeline": tl} if tl else {})}
 
 
 def trace_step(gguf: str, max_context: int, steps: int) -> str:
@@ -488,6 +520,7 @@ def main() -> None:
     q6.add_argument("--prompt", type=int, default=512)
     q6.add_argument("--steps", type=int, default=256)
     q6.add_argument("--layers", type=int, default=40)
+    q6.add_argument("--timeline", action="store_true", help="per-kernel device times of a few graph replays")
     t = sub.add_parser("trace")
     t.add_argument("--gguf", required=True)
     t.add_argument("--max-context", type=int, default=1024)
@@ -504,7 +537,7 @@ def main() -> None:
     if args.cmd == "gemv":
         r = bench_gemv(args.n, args.k, args.iters)
     elif args.cmd == "qwen36":
-        r = bench_qwen36(args.batch, args.prompt, args.steps, args.layers)
+        r = bench_qwen36(args.batch, args.prompt, args.steps, args.layers, args.timeline)
     elif args.cmd == "moe":
         r = bench_moe(args.tokens, args.iters, shared=not args.no_shared)
     elif args.cmd == "gdn":
