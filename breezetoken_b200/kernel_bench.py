@@ -7,6 +7,8 @@
     python -m breezetoken_b200.kernel_bench qwen36 --batch 64 --prompt 512 --steps 256
     python -m breezetoken_b200.kernel_bench linear --tokens 64
     python -m breezetoken_b200.kernel_bench trace --gguf model.gguf
+    python -m breezetoken_b200.kernel_bench load
+    torchrun --nproc-per-node 2 -m breezetoken_b200.kernel_bench moe-ep --tokens 8
 
 Each prints one JSON line: average launch time and achieved HBM GB/s from
 the algorithmic bytes of one launch (weights / state / KV read once).
@@ -24,6 +26,9 @@ x) at the 35B-A3B decoder's projection shapes (GDN qkv 8192 x 2048, z 4096 x 204
 copies larger than L2 together.
 ``trace`` prints the device-side timeline of one Qwen3.5 decode step (per
 kernel kind: release gap, prologue, body) after a 16-token prefill.
+``load`` times loading the full-shape checkpoint (parse, upload, repack).
+``moe-ep`` times the ``moe`` layer expert-parallel over the torchrun ranks
+against the replicated layer.
 ``gdn`` and ``attn`` are the stand-alone GDN-step and split-KV attention decode
 benchmarks with their synthetic inputs (seeds 1 and 2).
 """
@@ -33,6 +38,7 @@ from __future__ import annotations
 import argparse
 import json
 import time
+from pathlib import Path
 
 import numpy as np
 import torch
@@ -449,6 +455,137 @@ def bench_qwen36(batch: int, prompt: int, steps: int, layers: int, timeline: boo
             "gbs_per_gpu": step_bytes * steps / sec / 1e9, **({"timeline": tl} if tl else {})}
 
 
+def bench_moe_ep(tokens: int, iters: int) -> dict | None:
+    """The MoE-layer benchmark's layer placed expert-parallel over the N
+    ranks of torchrun (breezetoken_b200.expert_parallel): each rank holds 256 / N
+    experts and T tokens of its own (seed 3 + rank), and one layer call is
+    dispatch all-to-all -> local experts over N T tokens -> combine all-to-all
+    + shared expert.  Timed per call with CUDA events after a 256 MB read and a
+    barrier, slowest rank; beside it the same rank's tokens through the
+    replicated layer (all 256 experts on the GPU, no collective) and the parts
+    of the EP call.  Rank 0 returns the result."""
+    import datetime
+    import os
+
+    import torch.distributed as dist
+
+    from breezetoken_b200.expert_parallel import ExpertParallelMoE
+    from breezetoken_b200.moe import IQ3SExperts, SharedExpert, moe_forward, route_logits
+    from breezetoken_b200.synth import MoeSpec, make_moe_layer, moe_layer_inputs
+
+    rank, world = int(os.environ.get("RANK", "0")), int(os.environ.get("WORLD_SIZE", "1"))
+    torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", "0")))
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300))
+    spec = MoeSpec()
+    m = make_moe_layer(spec, seed=3)
+    ex = IQ3SExperts.from_gguf_bytes(m["gate"], m["up"], m["down"], spec.n_experts, spec.hidden, spec.ffn, "cuda")
+    se = SharedExpert.from_tensors(torch.from_numpy(m["sh_gate"]), torch.from_numpy(m["sh_up"]),
+                                   torch.from_numpy(m["sh_down"]), torch.from_numpy(m["sh_gate_inp"]), "cuda")
+    xh, lh = moe_layer_inputs(tokens, spec, seed=3 + rank)
+    x = torch.from_numpy(xh).cuda()
+    r = route_logits(torch.from_numpy(lh).cuda(), spec.top_k)
+    ep = ExpertParallelMoE(ex, se)
+    ws = torch.zeros(int(N.load().bt_moe_layer_workspace_bytes(tokens, spec.hidden, spec.ffn, spec.ffn,
+                                                               spec.n_experts, spec.top_k)),
+                     dtype=torch.uint8, device="cuda")
+    want = moe_forward(ex, se, x, r.expert_ids, r.weights, ws)
+    got = ep(x, r.expert_ids, r.weights)
+    err = float((got - want).abs().max() / want.abs().max())
+    rows_in, r_ids, r_w = ep.dispatch(x, r.expert_ids, r.weights)
+    part = ep.local_experts(rows_in, r_ids, r_w)
+    local_u = int(torch.unique(r_ids[r_ids >= 0]).numel())
+    flush = torch.ones(256 << 20, dtype=torch.uint8, device="cuda")
+
+    def timed(fn) -> float:
+        total = 0.0
+        for i in range(iters + 3):
+            flush.sum(dtype=torch.int32)  # the experts are not in L2
+            dist.barrier()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            fn()
+            b.record()
+            b.synchronize()
+            if i >= 3:
+                total += a.elapsed_time(b) * 1e3
+        t = torch.tensor([total / iters], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def captured(fn):
+        """fn captured in a CUDA graph (its collectives included), after a
+        warm-up call on a side stream; every rank captures the same calls."""
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            fn()
+        torch.cuda.current_stream().wait_stream(side)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            fn()
+        graphs.append(g)
+        return g.replay
+
+    graphs: list = []
+    res = {
+        "ep_graph_us": timed(captured(lambda: ep(x, r.expert_ids, r.weights))),
+        "replicated_graph_us": timed(captured(lambda: moe_forward(ex, se, x, r.expert_ids, r.weights, ws))),
+        "ep_us": timed(lambda: ep(x, r.expert_ids, r.weights)),
+        "ep_dispatch_us": timed(lambda: ep.dispatch(x, r.expert_ids, r.weights)),
+        "ep_local_experts_us": timed(lambda: ep.local_experts(rows_in, r_ids, r_w)),
+        "ep_combine_us": timed(lambda: ep.combine(part, x)),
+        "replicated_us": timed(lambda: moe_forward(ex, se, x, r.expert_ids, r.weights, ws)),
+    }
+    errs = torch.tensor([err, float(local_u)], device="cuda")
+    dist.all_reduce(errs, op=dist.ReduceOp.MAX)
+    dist.barrier()
+    torch.cuda.synchronize()
+    graphs.clear()  # graphs holding NCCL calls go before the process group
+    dist.destroy_process_group()
+    if rank != 0:
+        return None
+    return {"kernel": "moe_expert_parallel", "ranks": world, "tokens_per_rank": tokens,
+            "experts_per_rank": ep.per_rank, "max_local_unique_experts": int(errs[1].item()),
+            "exchange_bytes_per_rank": (world * tokens * spec.hidden * 4 * 2 + world * tokens * spec.top_k * 8),
+            **res, "check_rel_err_vs_replicated": float(errs[0].item()),
+            "l2": "256 MB read before each call",
+            "timing": "CUDA events per call (eager: host launches included; graph: one replay) after a barrier, "
+                      "max over ranks"}
+
+
+def bench_load(path: str | None) -> dict:
+    """Load time of the full 35B-A3B-shaped checkpoint (written once per
+    machine by synth.cached_qwen36_full when no path is given): the GGUF
+    bytes read and uploaded, against the time the repack kernels take on the
+    device (CUDA events around the whole load)."""
+    from breezetoken_b200.gguf import GGUFFile
+    from breezetoken_b200.qwen36_moe import Qwen36Moe
+    from breezetoken_b200.synth import cached_qwen36_full
+
+    path = path or str(cached_qwen36_full())
+    nbytes = Path(path).stat().st_size
+    t0 = time.perf_counter()
+    with open(path, "rb") as f:  # the file into the page cache, timed on its own
+        while f.read(1 << 28):
+            pass
+    read_s = time.perf_counter() - t0
+    lib = N.load()
+    before = int(lib.bt_launch_count())
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    g = GGUFFile(path)
+    m = Qwen36Moe(g, max_context=64, batch=1)
+    torch.cuda.synchronize()
+    load_s = time.perf_counter() - t0
+    launches = int(lib.bt_launch_count()) - before
+    g.close()
+    m.close()
+    return {"kernel": "qwen36_load", "gguf_bytes": nbytes, "file_read_s": read_s,
+            "file_read_gbs": nbytes / read_s / 1e9, "load_s": load_s, "load_gbs": nbytes / load_s / 1e9,
+            "library_launches": launches,
+            "note": "load = open + parse + host->device upload + repack kernels, the file already in the page cache"}
+
+
 def trace_step(gguf: str, max_context: int, steps: int) -> str:
     """Per-kernel-kind device timeline of a decode step (model.Qwen35.trace_step):
     entered = previous kernel's last CTA exit -> this kernel's last CTA entry
@@ -521,6 +658,11 @@ def main() -> None:
     q6.add_argument("--steps", type=int, default=256)
     q6.add_argument("--layers", type=int, default=40)
     q6.add_argument("--timeline", action="store_true", help="per-kernel device times of a few graph replays")
+    ep = sub.add_parser("moe-ep", help="under torchrun: the MoE layer expert-parallel over the ranks")
+    ep.add_argument("--tokens", type=int, default=8, help="tokens per rank")
+    ep.add_argument("--iters", type=int, default=30)
+    ld = sub.add_parser("load")
+    ld.add_argument("--gguf", default=None, help="default: the cached full-shape checkpoint")
     t = sub.add_parser("trace")
     t.add_argument("--gguf", required=True)
     t.add_argument("--max-context", type=int, default=1024)
@@ -536,6 +678,10 @@ def main() -> None:
         return
     if args.cmd == "gemv":
         r = bench_gemv(args.n, args.k, args.iters)
+    elif args.cmd == "moe-ep":
+        r = bench_moe_ep(args.tokens, args.iters)
+    elif args.cmd == "load":
+        r = bench_load(args.gguf)
     elif args.cmd == "qwen36":
         r = bench_qwen36(args.batch, args.prompt, args.steps, args.layers, args.timeline)
     elif args.cmd == "moe":

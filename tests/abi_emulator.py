@@ -279,10 +279,18 @@ class Emulator:
         self.packed[dst] = (raw.reshape(rows, -1), rows, k)
 
     def _expert(self, buf: int, e: int, rows: int) -> np.ndarray:
+        """Expert e of the expert tensor at `buf`: a repacked buffer or a
+        view that starts at one of its experts (moe.expert_slice)."""
         key = (buf, e, rows)
         if key not in self.dense:
-            raw, _, k = self.packed[buf]
-            self.dense[key] = dequant_iq3_s(raw[e * rows : (e + 1) * rows], rows, k)
+            for base, (raw, n_rows, k) in self.packed.items():
+                expert_bytes = rows * (k // 256) * 136
+                if base <= buf < base + n_rows * (k // 256) * 136 and (buf - base) % expert_bytes == 0:
+                    first = (buf - base) // expert_bytes + e
+                    self.dense[key] = dequant_iq3_s(raw[first * rows : (first + 1) * rows], rows, k)
+                    break
+            else:
+                raise KeyError(f"no repacked expert tensor holds address {buf:#x}")
         return self.dense[key]
 
     def bt_moe_layer_iq3s_add_norm(self, gate, up, down, shared, x, t, hidden, ffn, n_experts, ids, weights, top_k,
@@ -290,6 +298,11 @@ class Emulator:
         self.bt_moe_layer_iq3s(gate, up, down, shared, x, t, hidden, ffn, n_experts, ids, weights, top_k, out, ws,
                                stream)
         self.bt_add_rms_norm_planes(h, out, w, h_out, y, planes, t, hidden, eps, stream)
+
+    def bt_moe_experts_iq3s(self, gate, up, down, x, t, hidden, ffn, n_experts, ids, weights, top_k, out, ws,
+                            stream) -> None:
+        self.bt_moe_layer_iq3s(gate, up, down, None, x, t, hidden, ffn, n_experts, ids, weights, top_k, out, ws,
+                               stream)
 
     def bt_moe_layer_iq3s(self, gate, up, down, shared, x, t, hidden, ffn, n_experts, ids, weights, top_k, out, ws,
                           stream) -> None:
@@ -300,6 +313,8 @@ class Emulator:
         for r in range(t):
             y = np.zeros(hidden, F32)  # oracle.moe.experts, with each dequantised expert kept
             for e, w in zip(iv[r], wv[r], strict=True):
+                if not 0 <= e < n_experts:  # invalid ids contribute nothing
+                    continue
                 act = ops.silu(self._expert(gate, e, ffn) @ xv[r]) * (self._expert(up, e, ffn) @ xv[r])
                 y += (self._expert(down, e, hidden) @ act) * F32(w)
             if sh is not None:
