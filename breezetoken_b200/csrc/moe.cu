@@ -1448,20 +1448,33 @@ __global__ void moe_combine_kernel(const float* __restrict__ weights, const int3
 
 // moe_combine_kernel's sums for 8 consecutive outputs (dn: element i0 of the
 // token's first pair row), each in routing order with the same roundings,
-// the rows read with 16-byte loads.
+// the rows read with 16-byte loads.  Eight pairs' rows are loaded at once and
+// without waiting for their ids (every pair has a workspace row; the rows of
+// invalid ids are read but not added), so a token costs one round trip.
 __device__ __forceinline__ void routed_sum8(const int32_t* ids, const float* w, const float* dn, int64_t stride,
                                             int top_k, int n_experts, float (&a)[8]) {
 #pragma unroll
   for (int j = 0; j < 8; ++j) a[j] = 0.f;
-  for (int k = 0; k < top_k; ++k) {
-    const int e = ids[k];
-    if (e < 0 || e >= n_experts) continue;
-    const float wk = w[k];
-    const float4 v0 = __ldcg(reinterpret_cast<const float4*>(dn + k * stride));
-    const float4 v1 = __ldcg(reinterpret_cast<const float4*>(dn + k * stride) + 1);
-    const float v[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+  for (int k0 = 0; k0 < top_k; k0 += 8) {
+    float4 v[8][2];
+    float wk[8];
+    int e[8];
 #pragma unroll
-    for (int j = 0; j < 8; ++j) a[j] = __fadd_rn(a[j], __fmul_rn(v[j], wk));
+    for (int j = 0; j < 8; ++j) {
+      const int k = k0 + j;
+      e[j] = k < top_k ? ids[k] : -1;
+      wk[j] = k < top_k ? w[k] : 0.f;
+      const float4* row = reinterpret_cast<const float4*>(dn + static_cast<int64_t>(min(k, top_k - 1)) * stride);
+      v[j][0] = __ldcg(row);
+      v[j][1] = __ldcg(row + 1);
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      if (e[j] < 0 || e[j] >= n_experts) continue;
+      const float vv[8] = {v[j][0].x, v[j][0].y, v[j][0].z, v[j][0].w, v[j][1].x, v[j][1].y, v[j][1].z, v[j][1].w};
+#pragma unroll
+      for (int i = 0; i < 8; ++i) a[i] = __fadd_rn(a[i], __fmul_rn(vv[i], wk[j]));
+    }
   }
 }
 

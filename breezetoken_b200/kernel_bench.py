@@ -352,7 +352,9 @@ def _kernel_timeline(run, n_steps: int) -> dict:
     summed device time per step, and the span from the first kernel's start
     to the last one's end per step.  Kernels launched early with programmatic
     dependent launch count their wait for the predecessor, so the per-kernel
-    sums exceed the span."""
+    sums exceed the span; `excl_us_per_step` charges each launch only the time
+    from the previous kernel's end (or its own start, if later) to its own end,
+    which sums to the span less the idle gaps."""
     import collections
 
     from torch.profiler import ProfilerActivity, profile
@@ -364,14 +366,19 @@ def _kernel_timeline(run, n_steps: int) -> dict:
     evs = [e for e in prof.events() if e.device_type == torch.autograd.DeviceType.CUDA and e.time_range.elapsed_us() > 0
            and "Memcpy" not in e.name and "Memset" not in e.name]
     span = max(e.time_range.end for e in evs) - min(e.time_range.start for e in evs)
-    agg = collections.defaultdict(lambda: [0, 0.0])
-    for e in evs:
+    agg = collections.defaultdict(lambda: [0, 0.0, 0.0])
+    prev_end = None
+    for e in sorted(evs, key=lambda e: e.time_range.start):
         name = e.name.replace("(anonymous namespace)::", "").split("(")[0].replace("void ", "").replace("bt::", "")
         agg[name][0] += 1
         agg[name][1] += e.time_range.elapsed_us()
-    rows = sorted(agg.items(), key=lambda kv: -kv[1][1])
+        start = e.time_range.start if prev_end is None else max(prev_end, e.time_range.start)
+        agg[name][2] += max(0.0, e.time_range.end - start)
+        prev_end = e.time_range.end if prev_end is None else max(prev_end, e.time_range.end)
+    rows = sorted(agg.items(), key=lambda kv: -kv[1][2])
     return {"span_us_per_step": span / n_steps, "kernels_per_step": len(evs) / n_steps,
-            "kernels": [{"kernel": k, "launches_per_step": c / n_steps, "us_per_step": t / n_steps} for k, (c, t) in rows]}
+            "kernels": [{"kernel": k, "launches_per_step": c / n_steps, "us_per_step": t / n_steps,
+                         "excl_us_per_step": x / n_steps} for k, (c, t, x) in rows]}
 
 
 def bench_qwen36(batch: int, prompt: int, steps: int, layers: int, timeline: bool = False) -> dict | None:

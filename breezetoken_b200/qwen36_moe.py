@@ -278,6 +278,9 @@ class Qwen36Moe:
         self._attn_ws = torch.zeros(max(nbytes, 256), dtype=torch.uint8, device=dev)
         self._moe_ws = torch.zeros(int(N.load().bt_moe_layer_workspace_bytes(
             b, cfg.hidden, cfg.expert_ffn, cfg.shared_ffn, cfg.n_experts, cfg.top_k)), dtype=torch.uint8, device=dev)
+        # the GDN layers' small projections run beside the qkv projection on
+        # this stream (a parallel branch of the step's graph)
+        self._side = torch.cuda.Stream(device=dev) if torch.device(dev).type == "cuda" else None
         for i in self.conv_state:  # beta and alpha rows stacked: one projection launch for both
             layer = self.layers[i]
             layer["w_ba"] = torch.cat([layer.pop("w_beta"), layer.pop("w_alpha")]).contiguous()
@@ -332,12 +335,14 @@ class Qwen36Moe:
         N.call("bt_bf16_planes", x2.data_ptr(), p.data_ptr(), x2.shape[0], x2.shape[1], _stream())
         return p
 
-    def _lin(self, w: torch.Tensor, xp: torch.Tensor) -> torch.Tensor:
-        """Planes xp (T, 3, K) -> (T, N) f32 through weight rows w (N, K)."""
+    def _lin(self, w: torch.Tensor, xp: torch.Tensor, y: torch.Tensor | None = None) -> torch.Tensor:
+        """Planes xp (T, 3, K) -> (T, N) f32 through weight rows w (N, K)
+        (into y when given)."""
         n, k = w.shape
         if xp.shape[-1] != k:
             raise ValueError(f"projection of {xp.shape[-1]} columns through a ({n}, {k}) weight")
-        y = torch.empty(xp.shape[0], n, dtype=torch.float32, device=self.device)
+        if y is None:
+            y = torch.empty(xp.shape[0], n, dtype=torch.float32, device=self.device)
         dt = N.BT_BF16 if w.dtype == torch.bfloat16 else N.BT_F32
         N.call("bt_linear_rows", w.data_ptr(), dt, xp.data_ptr(), y.data_ptr(), n, k, xp.shape[0], _stream())
         return y
@@ -391,12 +396,25 @@ class Qwen36Moe:
         cfg, layer = self.cfg, self.layers[i]
         t, hk, hv, dk = xp.shape[0], cfg.gdn_key_heads, cfg.gdn_value_heads, cfg.gdn_k_dim
         b, inner = t // steps, cfg.gdn_inner
+        # [beta | alpha] and z on the side stream while the qkv projection and
+        # the conv run (their outputs allocated here, on the main stream)
+        ba = torch.empty(t, layer["w_ba"].shape[0], dtype=torch.float32, device=self.device)
+        z = torch.empty(t, layer["z"].shape[0], dtype=torch.float32, device=self.device)
+        side = self._side
+        if side is not None:
+            side.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.stream(side):
+                self._lin(layer["w_ba"], xp, ba)
+                self._lin(layer["z"], xp, z)
         entry = self._lin(layer["qkv"], xp)  # (T, C)
         mixed = torch.empty_like(entry)
         N.call("bt_conv_silu_scan", entry.data_ptr(), self.conv_state[i].data_ptr(), layer["conv"].data_ptr(),
                mixed.data_ptr(), steps, b, cfg.conv_dim, cfg.gdn_conv, _stream())
-        ba = self._lin(layer["w_ba"], xp)  # [beta | alpha]
-        z = self._lin(layer["z"], xp)
+        if side is None:
+            self._lin(layer["w_ba"], xp, ba)
+            self._lin(layer["z"], xp, z)
+        else:
+            torch.cuda.current_stream().wait_stream(side)
         gated = torch.empty(t, 3, inner, dtype=torch.bfloat16, device=self.device)
         N.call("bt_gdn_gated_scan", mixed.data_ptr(), mixed.shape[1], ba.data_ptr(), 2 * hv,
                layer["a_log"].data_ptr(), layer["dt_bias"].data_ptr(), self.rec_state[i].data_ptr(), z.data_ptr(),
