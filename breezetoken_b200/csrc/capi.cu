@@ -126,18 +126,44 @@ int bt_moe_layer_iq3s(const void* gate, const void* up, const void* down, const 
                             as_stream(stream));
 }
 
+namespace {
+int moe_add_norm(const void* gate, const void* up, const void* down, const BtMoeShared* shared, const float* x,
+                 int64_t t, int64_t hidden, int64_t ffn, int64_t n_experts, const int32_t* ids, const float* weights,
+                 int top_k, const float* h, const float* w, float eps, float* h_out, float* y, void* planes,
+                 float* out, void* workspace, void* stream, int prep_part) {
+  const bt::MoeNorm nm{h, w, h_out, y, planes, eps};
+  if (!shared)
+    return bt::moe_layer_iq3s(gate, up, down, nullptr, x, t, hidden, ffn, n_experts, ids, weights, top_k, out,
+                              workspace, as_stream(stream), &nm, prep_part);
+  const bt::MoeShared sh{shared->gate, shared->up, shared->down, shared->gate_inp, shared->ffn};
+  return bt::moe_layer_iq3s(gate, up, down, &sh, x, t, hidden, ffn, n_experts, ids, weights, top_k, out, workspace,
+                            as_stream(stream), &nm, prep_part);
+}
+}  // namespace
+
 int bt_moe_layer_iq3s_add_norm(const void* gate, const void* up, const void* down, const BtMoeShared* shared,
                                const float* x, int64_t t, int64_t hidden, int64_t ffn, int64_t n_experts,
                                const int32_t* ids, const float* weights, int top_k, const float* h, const float* w,
                                float eps, float* h_out, float* y, void* planes, float* out, void* workspace,
                                void* stream) {
-  const bt::MoeNorm nm{h, w, h_out, y, planes, eps};
-  if (!shared)
-    return bt::moe_layer_iq3s(gate, up, down, nullptr, x, t, hidden, ffn, n_experts, ids, weights, top_k, out,
-                              workspace, as_stream(stream), &nm);
+  return moe_add_norm(gate, up, down, shared, x, t, hidden, ffn, n_experts, ids, weights, top_k, h, w, eps, h_out, y,
+                      planes, out, workspace, stream, bt::kPrepAll);
+}
+
+int bt_moe_prepare_iq3s(const BtMoeShared* shared, const float* x, int64_t t, int64_t hidden, int64_t ffn,
+                        int64_t n_experts, int top_k, void* workspace, void* stream) {
+  if (!shared) return bt::moe_prepare_iq3s(nullptr, x, t, hidden, ffn, n_experts, top_k, workspace, as_stream(stream));
   const bt::MoeShared sh{shared->gate, shared->up, shared->down, shared->gate_inp, shared->ffn};
-  return bt::moe_layer_iq3s(gate, up, down, &sh, x, t, hidden, ffn, n_experts, ids, weights, top_k, out, workspace,
-                            as_stream(stream), &nm);
+  return bt::moe_prepare_iq3s(&sh, x, t, hidden, ffn, n_experts, top_k, workspace, as_stream(stream));
+}
+
+int bt_moe_layer_iq3s_add_norm_prepared(const void* gate, const void* up, const void* down,
+                                        const BtMoeShared* shared, const float* x, int64_t t, int64_t hidden,
+                                        int64_t ffn, int64_t n_experts, const int32_t* ids, const float* weights,
+                                        int top_k, const float* h, const float* w, float eps, float* h_out, float* y,
+                                        void* planes, float* out, void* workspace, void* stream) {
+  return moe_add_norm(gate, up, down, shared, x, t, hidden, ffn, n_experts, ids, weights, top_k, h, w, eps, h_out, y,
+                      planes, out, workspace, stream, bt::kPrepSort);
 }
 
 int bt_linear_q8(const void* w, const float* x, float* y, int64_t n, int64_t k, int n_vec, void* stream) {

@@ -589,21 +589,26 @@ __device__ __forceinline__ int block_exscan(int v, int* wsum, int& total) {
 // slots, and each expert-kernel CTA's contiguous item range, balanced by
 // token passes.  The next T blocks: encode token (block - 1) (T == 1: block
 // 0, token 0).  The rest: the shared expert's gate/up blocks.
+// part (moe.cuh): kPrepAll runs every block; kPrepX only the blocks that
+// read x alone (encode + shared gate/up, launched ahead of the routing);
+// kPrepSort only the sort block (after kPrepX ran on the same workspace).
 __global__ void __launch_bounds__(kThreads) moe_prep_kernel(const int32_t* __restrict__ ids, int p_total,
                                                             int n_experts, int direct, const float* __restrict__ x,
                                                             int t_total, int hidden, MoeWs ws, int gu_grid,
                                                             int gu_chunks, int d_grid, int d_chunks, MoeShared sh,
-                                                            int pulled) {
+                                                            int pulled, int part) {
   pdl_launch_dependents();
   const int enc0 = direct ? 0 : 1;
-  if (static_cast<int>(blockIdx.x) >= enc0 + t_total) {
-    shared_gu_block(blockIdx.x - enc0 - t_total, sh, x, t_total, hidden, ws);  // waits after its L2 prefetch
+  // the block's role in the full layout
+  const int bx = static_cast<int>(blockIdx.x) + (part == kPrepX ? enc0 : 0);
+  if (bx >= enc0 + t_total) {
+    shared_gu_block(bx - enc0 - t_total, sh, x, t_total, hidden, ws);  // waits after its L2 prefetch
     return;
   }
   pdl_wait();
-  if (direct || blockIdx.x > 0) {
+  if (direct || bx > 0) {
     __shared__ float red[kWarps];
-    const int tok = blockIdx.x - (direct ? 0 : 1);
+    const int tok = bx - (direct ? 0 : 1);
     const float4* src = reinterpret_cast<const float4*>(x + static_cast<int64_t>(tok) * hidden);
     float m = 0.f;
     for (int f = threadIdx.x; f < hidden / 4; f += kThreads) {
@@ -1526,7 +1531,7 @@ cudaError_t launch_pdl(Kern kern, dim3 grid, size_t smem, cudaStream_t stream, A
 template <int KBG, int KBD>
 int launch_all(const uint8_t* gate, const uint8_t* up, const uint8_t* down, const MoeShared* sh, const float* x,
                int64_t t, int hidden, int ffn, int n_experts, const int32_t* ids, const float* weights, int top_k,
-               float* out, MoeWs ws, cudaStream_t stream, const MoeNorm* norm) {
+               float* out, MoeWs ws, cudaStream_t stream, const MoeNorm* norm, int prep_part) {
   const int shared = sh ? 1 : 0;
   const int p = static_cast<int>(t * top_k);
   // one token selects top_k distinct experts: no grouping needed
@@ -1568,8 +1573,17 @@ int launch_all(const uint8_t* gate, const uint8_t* up, const uint8_t* down, cons
   const int sd_blocks = shared ? hidden / 64 * passes : 0;
   const int prep_blocks = (direct ? 1 : 1 + static_cast<int>(t)) + sgu_blocks;
   const int pulled = t > kStaticMaxTokens ? 1 : 0;
-  cudaError_t e = launch_pdl(moe_prep_kernel, dim3(prep_blocks), prep_smem, stream, ids, p, n_experts, direct, x,
-                             static_cast<int>(t), hidden, ws, gu_grid, gu_chunks, d_grid, d_chunks, shv, pulled);
+  // kPrepX: the x blocks only (moe_prepare_iq3s); kPrepSort: the layer after
+  // moe_prepare_iq3s, the sort block only (none for one token)
+  const int grid = prep_part == kPrepX ? prep_blocks - (direct ? 0 : 1) : prep_part == kPrepSort ? 1 : prep_blocks;
+  cudaError_t e = cudaSuccess;
+  if (!(prep_part == kPrepSort && direct))
+    e = launch_pdl(moe_prep_kernel, dim3(grid), prep_part == kPrepX ? 0 : prep_smem, stream, ids, p, n_experts, direct,
+                   x, static_cast<int>(t), hidden, ws, gu_grid, gu_chunks, d_grid, d_chunks, shv, pulled, prep_part);
+  if (prep_part == kPrepX) {
+    if (e == cudaSuccess) e = cudaGetLastError();
+    return e == cudaSuccess ? BT_OK : fail_cuda(e, "moe prepare launch");
+  }
   // up to kStaticMaxTokens tokens: static item ranges of K-split items (one
   // token: the last of a row chunk's CTAs combines); more: whole-pass items
   // pulled from a counter, then the combine kernel
@@ -1649,9 +1663,20 @@ int64_t moe_workspace_bytes(int64_t t, int64_t hidden, int64_t ffn, int64_t shar
   return moe_ws_bytes(t, t * top_k, hidden, ffn, shared_ffn);
 }
 
+int moe_prepare_iq3s(const MoeShared* shared, const float* x, int64_t t, int64_t hidden, int64_t ffn,
+                     int64_t n_experts, int top_k, void* workspace, cudaStream_t stream) {
+  if (!x || !workspace) return fail(BT_ERR_INVALID, "moe prepare: null pointer");
+  // the layer's checks and launch geometry; the x part reads neither the
+  // weights nor the routing, so the workspace stands in for those pointers
+  void* w = workspace;
+  return moe_layer_iq3s(w, w, w, shared, x, t, hidden, ffn, n_experts, static_cast<const int32_t*>(w),
+                        static_cast<const float*>(w), top_k, static_cast<float*>(w), workspace, stream, nullptr,
+                        kPrepX);
+}
+
 int moe_layer_iq3s(const void* gate, const void* up, const void* down, const MoeShared* shared, const float* x,
                    int64_t t, int64_t hidden, int64_t ffn, int64_t n_experts, const int32_t* ids, const float* weights,
-                   int top_k, float* out, void* workspace, cudaStream_t stream, const MoeNorm* norm) {
+                   int top_k, float* out, void* workspace, cudaStream_t stream, const MoeNorm* norm, int prep_part) {
   if (!gate || !up || !down || !x || !ids || !weights || !out || !workspace)
     return fail(BT_ERR_INVALID, "moe_experts_iq3s: null pointer");
   if (norm && (!norm->h || !norm->w || !norm->h_out || !norm->y || !norm->planes || hidden % 8 ||
@@ -1680,11 +1705,11 @@ int moe_layer_iq3s(const void* gate, const void* up, const void* down, const Moe
   const int h = static_cast<int>(hidden), f = static_cast<int>(ffn), ne = static_cast<int>(n_experts);
   const int k = top_k;
   if (hidden == 2048 && ffn == 512)
-    return launch_all<8, 2>(g, u, d, shared, x, t, h, f, ne, ids, weights, k, out, ws, stream, norm);
+    return launch_all<8, 2>(g, u, d, shared, x, t, h, f, ne, ids, weights, k, out, ws, stream, norm, prep_part);
   if (hidden == 1024 && ffn == 512)
-    return launch_all<4, 2>(g, u, d, shared, x, t, h, f, ne, ids, weights, k, out, ws, stream, norm);
+    return launch_all<4, 2>(g, u, d, shared, x, t, h, f, ne, ids, weights, k, out, ws, stream, norm, prep_part);
   if (hidden == 2048 && ffn == 1024)
-    return launch_all<8, 4>(g, u, d, shared, x, t, h, f, ne, ids, weights, k, out, ws, stream, norm);
+    return launch_all<8, 4>(g, u, d, shared, x, t, h, f, ne, ids, weights, k, out, ws, stream, norm, prep_part);
   return fail(BT_ERR_UNSUPPORTED, "moe_experts_iq3s serves (hidden, ffn) in {(1024,512), (2048,512), (2048,1024)}");
 }
 

@@ -7,6 +7,7 @@
     python -m breezetoken_b200.kernel_bench qwen36 --batch 64 --prompt 512 --steps 256
     python -m breezetoken_b200.kernel_bench linear --tokens 64
     python -m breezetoken_b200.kernel_bench trace --gguf model.gguf
+    python -m breezetoken_b200.kernel_bench attn-layer --batch 64 --pos 648 --splits 2
     python -m breezetoken_b200.kernel_bench load
     torchrun --nproc-per-node 2 -m breezetoken_b200.kernel_bench moe-ep --tokens 8
 
@@ -262,6 +263,65 @@ def bench_attn(batch: int, ctx: int, splits: int, iters: int) -> dict:
     nbytes = batch * ctx * kv_heads * dim * 2 * 2 + 2 * batch * heads * dim * 4
     return {"kernel": "attn_decode", "batch": batch, "ctx": ctx, "splits": splits, "us": sec * 1e6,
             "us_graph": gsec * 1e6, "bytes": nbytes, "gbs": nbytes / sec / 1e9, "gbs_graph": nbytes / gsec / 1e9}
+
+
+def bench_attn_layer(batch: int, pos: int, splits: int, iters: int) -> dict:
+    """bt_attention_layer (the fused Qwen3.6 attention layer: q/k norms, RoPE,
+    KV write, attention, gate) at the 35B-A3B shape (16 q / 2 KV heads x 256,
+    f32 cache of 769 positions), every sequence at position `pos` - 7 b, seed
+    3; timed per call in a CUDA graph of `iters` calls (no host launch time),
+    L2 flushed by a 256 MB read between calls outside the events.  Bytes: the
+    K and V rows attended (f32)."""
+    from breezetoken_b200.qwen36_moe import Qwen36Config, rope_tables
+    from breezetoken_b200.synth import QWEN36_35B
+
+    heads, kv, dim, cap = 16, 2, 256, 769
+    cfg = Qwen36Config.from_spec(QWEN36_35B, cap)
+    cos, sin = (t.cuda() for t in rope_tables(cfg))
+    g = torch.Generator(device="cuda").manual_seed(3)
+    proj = torch.randn(batch, (2 * heads + 2 * kv) * dim, device="cuda", generator=g)
+    qn = 1 + 0.02 * torch.randn(dim, device="cuda", generator=g)
+    kn = 1 + 0.02 * torch.randn(dim, device="cuda", generator=g)
+    kc = torch.randn(batch, cap, kv, dim, device="cuda", generator=g)
+    vc = torch.randn(batch, cap, kv, dim, device="cuda", generator=g)
+    pos_t = torch.tensor([max(0, pos - 7 * b) for b in range(batch)], dtype=torch.int32, device="cuda")
+    lib = N.load()
+    ws = torch.zeros(max(256, int(lib.bt_attention_workspace_bytes(batch, kv, heads, dim, splits))),
+                     dtype=torch.uint8, device="cuda")
+    out = torch.empty(batch, heads, dim, device="cuda")
+    flush = torch.ones(256 << 20, dtype=torch.uint8, device="cuda")
+    s = torch.cuda.Stream()
+
+    def call() -> None:
+        N.call("bt_attention_layer", proj.data_ptr(), proj.shape[1], qn.data_ptr(), kn.data_ptr(), cos.data_ptr(),
+               sin.data_ptr(), cfg.rope_dim, pos_t.data_ptr(), kc.data_ptr(), vc.data_ptr(), out.data_ptr(), batch,
+               heads, kv, dim, cap, float(dim ** -0.5), float(cfg.eps), splits, ws.data_ptr(), None,
+               torch.cuda.current_stream().cuda_stream)
+
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        for _ in range(3):
+            call()
+    torch.cuda.current_stream().wait_stream(s)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=s):
+        call()
+    total = 0.0
+    with torch.cuda.stream(s):
+        for i in range(iters + 3):
+            flush.sum(dtype=torch.int32)
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(s)
+            graph.replay()
+            b.record(s)
+            b.synchronize()
+            if i >= 3:
+                total += a.elapsed_time(b) * 1e3
+    us = total / iters
+    nbytes = int(sum(int(p) + 1 for p in pos_t.tolist())) * kv * dim * 4 * 2
+    return {"kernel": "attention_layer", "batch": batch, "pos": pos, "splits": splits, "us": us,
+            "bytes": nbytes, "gbs": nbytes / us / 1e3, "l2": "flushed before each call (256 MB read)",
+            "timing": "one graph replay of one call between CUDA events"}
 
 
 def bench_moe(tokens: int, iters: int, shared: bool = True) -> dict:
@@ -650,6 +710,11 @@ def main() -> None:
     c.add_argument("--ctx", type=int, default=8192)
     c.add_argument("--splits", type=int, default=0)
     c.add_argument("--iters", type=int, default=20)
+    al = sub.add_parser("attn-layer", help="the fused Qwen3.6 attention layer at the 35B shape")
+    al.add_argument("--batch", type=int, default=64)
+    al.add_argument("--pos", type=int, default=648)
+    al.add_argument("--splits", type=int, default=2)
+    al.add_argument("--iters", type=int, default=20)
     mo = sub.add_parser("moe")
     mo.add_argument("--tokens", type=int, default=1)
     mo.add_argument("--iters", type=int, default=50)
@@ -685,6 +750,8 @@ def main() -> None:
         return
     if args.cmd == "gemv":
         r = bench_gemv(args.n, args.k, args.iters)
+    elif args.cmd == "attn-layer":
+        r = bench_attn_layer(args.batch, args.pos, args.splits, args.iters)
     elif args.cmd == "moe-ep":
         r = bench_moe_ep(args.tokens, args.iters)
     elif args.cmd == "load":

@@ -135,8 +135,37 @@ class SharedExpert:
         return cls(g, u, d, gi)
 
 
+def _shared_arg(shared: SharedExpert | None, hidden: int):
+    if shared is None:
+        return None
+    if shared.gate.shape[1] != hidden:
+        raise ValueError(f"shared expert hidden {shared.gate.shape[1]} != {hidden}")
+    return N.BtMoeShared(shared.gate.data_ptr(), shared.up.data_ptr(), shared.down.data_ptr(),
+                         shared.gate_inp.data_ptr(), shared.ffn)
+
+
+def moe_prepare(ex: IQ3SExperts, shared: SharedExpert | None, x: torch.Tensor, top_k: int,
+                workspace: torch.Tensor) -> None:
+    """The part of a MoE layer call that reads x alone (the tokens' encoding
+    and the shared expert's gate/up, bt_moe_prepare_iq3s) into `workspace`,
+    before the routing is known; the layer call follows with
+    moe_forward(..., prepared=True) on the same x and workspace."""
+    x2 = x.float().reshape(-1, ex.hidden)
+    if not x2.is_contiguous():
+        raise ValueError("moe_prepare needs contiguous x (the layer call must read the same buffer)")
+    t = x2.shape[0]
+    sffn = shared.ffn if shared is not None else 0
+    need = int(N.load().bt_moe_layer_workspace_bytes(t, ex.hidden, ex.ffn, sffn, ex.n_experts, top_k))
+    if workspace.numel() < need:
+        raise ValueError(f"MoE workspace of {workspace.numel()} bytes < {need}")
+    sh = _shared_arg(shared, ex.hidden)
+    N.call("bt_moe_prepare_iq3s", None if sh is None else ctypes.byref(sh), x2.data_ptr(), t, ex.hidden, ex.ffn,
+           ex.n_experts, top_k, workspace.data_ptr(), _stream())
+
+
 def moe_forward(ex: IQ3SExperts, shared: SharedExpert | None, x: torch.Tensor, ids: torch.Tensor,
-                weights: torch.Tensor, workspace: torch.Tensor | None = None, norm: tuple | None = None):
+                weights: torch.Tensor, workspace: torch.Tensor | None = None, norm: tuple | None = None,
+                prepared: bool = False):
     """Qwen36Moe._moe after routing (model/qwen36_moe.py:634-642) for x (T,
     hidden) f32: the routed experts plus, when given, the shared expert gated
     by sigmoid(x . gate_inp).
@@ -144,7 +173,8 @@ def moe_forward(ex: IQ3SExperts, shared: SharedExpert | None, x: torch.Tensor, i
     With norm = (h, gamma, eps) the layer's output goes straight into the
     decoder's residual add and the next RMSNorm (bt_moe_layer_iq3s_add_norm,
     the same bits as the separate ops) and (h + out, rms_norm(h + out) *
-    gamma, its bf16 planes (T, 3, hidden)) is returned instead of out."""
+    gamma, its bf16 planes (T, 3, hidden)) is returned instead of out.
+    prepared (with norm): moe_prepare already ran on this x and workspace."""
     x2 = x.float().reshape(-1, ex.hidden).contiguous()
     t = x2.shape[0]
     ids2 = ids.to(torch.int32).reshape(t, -1).contiguous()
@@ -153,15 +183,12 @@ def moe_forward(ex: IQ3SExperts, shared: SharedExpert | None, x: torch.Tensor, i
     sffn = shared.ffn if shared is not None else 0
     lib = N.load()
     need = int(lib.bt_moe_layer_workspace_bytes(t, ex.hidden, ex.ffn, sffn, ex.n_experts, top_k))
+    if prepared and (norm is None or workspace is None or workspace.numel() < need):
+        raise ValueError("a prepared MoE layer call takes the norm and the workspace moe_prepare filled")
     if workspace is None or workspace.numel() < need:
         workspace = torch.zeros(need, dtype=torch.uint8, device=x2.device)
     out = torch.empty(t, ex.hidden, dtype=torch.float32, device=x2.device)
-    sh = None
-    if shared is not None:
-        if shared.gate.shape[1] != ex.hidden:
-            raise ValueError(f"shared expert hidden {shared.gate.shape[1]} != {ex.hidden}")
-        sh = N.BtMoeShared(shared.gate.data_ptr(), shared.up.data_ptr(), shared.down.data_ptr(),
-                           shared.gate_inp.data_ptr(), sffn)
+    sh = _shared_arg(shared, ex.hidden)
     if norm is None:
         N.call("bt_moe_layer_iq3s", ex.gate.data_ptr(), ex.up.data_ptr(), ex.down.data_ptr(),
                None if sh is None else ctypes.byref(sh), x2.data_ptr(), t, ex.hidden, ex.ffn, ex.n_experts,
@@ -172,7 +199,8 @@ def moe_forward(ex: IQ3SExperts, shared: SharedExpert | None, x: torch.Tensor, i
         raise ValueError(f"residual must be contiguous f32 {(t, ex.hidden)}")
     h_out, y = torch.empty_like(h), torch.empty_like(h)
     planes = torch.empty(t, 3, ex.hidden, dtype=torch.bfloat16, device=x2.device)
-    N.call("bt_moe_layer_iq3s_add_norm", ex.gate.data_ptr(), ex.up.data_ptr(), ex.down.data_ptr(),
+    N.call("bt_moe_layer_iq3s_add_norm_prepared" if prepared else "bt_moe_layer_iq3s_add_norm",
+           ex.gate.data_ptr(), ex.up.data_ptr(), ex.down.data_ptr(),
            None if sh is None else ctypes.byref(sh), x2.data_ptr(), t, ex.hidden, ex.ffn, ex.n_experts,
            ids2.data_ptr(), w2.data_ptr(), top_k, h.data_ptr(), gamma.data_ptr(), float(eps), h_out.data_ptr(),
            y.data_ptr(), planes.data_ptr(), out.data_ptr(), workspace.data_ptr(), _stream())

@@ -374,6 +374,27 @@ BT_API int bt_moe_layer_iq3s_add_norm(const void* gate, const void* up, const vo
                                       float* y, void* planes, float* out, void* workspace,
                                       void* stream);
 
+/* bt_moe_layer_iq3s_add_norm in two calls, so that the work which reads x
+ * alone can run before the routing is known (for instance while the router
+ * projection and bt_moe_route run on another stream of the same graph):
+ * bt_moe_prepare_iq3s encodes the T tokens and runs the shared expert's
+ * gate/up into `workspace`; bt_moe_layer_iq3s_add_norm_prepared then does
+ * the rest with the same x, shapes, shared expert and workspace, ordered
+ * after the prepare call (same stream, or joined).  Together they give the
+ * bits of bt_moe_layer_iq3s_add_norm.  No reference counterpart: a split of
+ * the layer above (model/qwen36_moe.py:634-642).                          */
+BT_API int bt_moe_prepare_iq3s(const BtMoeShared* shared, const float* x, int64_t t,
+                               int64_t hidden, int64_t ffn, int64_t n_experts, int top_k,
+                               void* workspace, void* stream);
+BT_API int bt_moe_layer_iq3s_add_norm_prepared(const void* gate, const void* up,
+                                               const void* down, const BtMoeShared* shared,
+                                               const float* x, int64_t t, int64_t hidden,
+                                               int64_t ffn, int64_t n_experts,
+                                               const int32_t* ids, const float* weights,
+                                               int top_k, const float* h, const float* w,
+                                               float eps, float* h_out, float* y, void* planes,
+                                               float* out, void* workspace, void* stream);
+
 /* ------------------------------------------------- Qwen3.5 decode step */
 typedef struct BtQwen35Dims {
   int32_t hidden, n_layers, n_heads, n_kv, head_dim, rope_dim, ffn, vocab;

@@ -329,3 +329,35 @@ def test_moe_layer_add_norm_equals_layer_then_norm(layer256, t) -> None:
     assert torch.equal(h2, h1)
     assert torch.equal(y2, y1)
     assert torch.equal(p2, p1)
+
+
+@pytest.mark.parametrize("t", [1, 8, 16, 17, 64])
+def test_moe_prepared_layer_equals_layer(layer256, t) -> None:
+    """bt_moe_prepare_iq3s on one stream, the routing on another, then
+    bt_moe_layer_iq3s_add_norm_prepared: the bits of the one-call layer, on the
+    static, pulled and one-token paths, from a workspace left dirty by another
+    layer call."""
+    from breezetoken_b200.moe import moe_forward, moe_prepare, route_logits
+    from breezetoken_b200.synth import moe_layer_inputs
+
+    m, ex, se = layer256
+    xh, lh = moe_layer_inputs(t)
+    x, logits = torch.from_numpy(xh).cuda(), torch.from_numpy(lh).cuda()
+    rng = np.random.default_rng(58)
+    h = torch.from_numpy(rng.standard_normal((t, 2048), dtype=np.float32)).cuda()
+    gamma = torch.from_numpy(1 + 0.02 * rng.standard_normal(2048, dtype=np.float32)).cuda()
+    r = route_logits(logits, 8)
+    want = moe_forward(ex, se, x, r.expert_ids, r.weights, norm=(h, gamma, 1e-6))
+    ws = torch.zeros(int(N.load().bt_moe_layer_workspace_bytes(t, 2048, 512, 512, 256, 8)), dtype=torch.uint8,
+                     device="cuda")
+    other = torch.from_numpy(moe_layer_inputs(t, seed=9)[0]).cuda()
+    moe_forward(ex, se, other, r.expert_ids, r.weights, ws, norm=(h, gamma, 1e-6))  # dirty workspace
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        r2 = route_logits(logits, 8)
+    moe_prepare(ex, se, x, 8, ws)
+    torch.cuda.current_stream().wait_stream(side)
+    got = moe_forward(ex, se, x, r2.expert_ids, r2.weights, ws, norm=(h, gamma, 1e-6), prepared=True)
+    for a, b in zip(got, want, strict=True):
+        assert torch.equal(a, b)
