@@ -184,6 +184,8 @@ __global__ void moe_route_kernel(const float* __restrict__ logits, int64_t t, in
                                  int32_t* __restrict__ ids, float* __restrict__ weights) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t tok = blockIdx.x * static_cast<int64_t>(blockDim.x >> 5) + warp;
+  pdl_launch_dependents();
+  pdl_wait();  // the logits come from the previous kernel
   if (tok >= t) return;
   const float* lg = logits + tok * n_experts;
   float v[PL];
@@ -201,10 +203,11 @@ __global__ void moe_route_kernel(const float* __restrict__ logits, int64_t t, in
   for (int i = 0; i < PL; ++i)
     if (lane + 32 * i < n_experts) s += expf(v[i] - m);
   s = warp_sum(s);
-  // selection state: bit i set = expert lane + 32 i taken
+  // selection state: bit i set = expert lane + 32 i taken; pick k is kept
+  // by lane k
   uint32_t taken = 0;
-  float sel[16];
-  int sid[16];
+  float my_p = 0.f;
+  int my_id = 0;
   float wsum = 0.f;
   for (int k = 0; k < top_k && k < 16; ++k) {
     float best = -INFINITY;
@@ -229,16 +232,17 @@ __global__ void moe_route_kernel(const float* __restrict__ logits, int64_t t, in
     }
     if ((bid & 31) == lane) taken |= 1u << (bid >> 5);
     const float p = expf(best - m) / s;  // softmax probability of the pick
-    sel[k] = p;
-    sid[k] = bid;
+    if (lane == k) {
+      my_p = p;
+      my_id = bid;
+    }
     wsum += p;
   }
   const float denom = fmaxf(wsum, kWeightSumMin);
-  if (lane == 0)
-    for (int k = 0; k < top_k && k < 16; ++k) {
-      ids[tok * top_k + k] = sid[k];
-      weights[tok * top_k + k] = sel[k] / denom;
-    }
+  if (lane < top_k && lane < 16) {
+    ids[tok * top_k + lane] = my_id;
+    weights[tok * top_k + lane] = my_p / denom;
+  }
 }
 
 // ------------------------------------------------------------------ workspace
@@ -1645,14 +1649,14 @@ int moe_route(const float* logits, int64_t t, int64_t n_experts, int top_k, int3
   if (t == 0) return BT_OK;
   const int blocks = static_cast<int>((t + 7) / 8);
   const int ne = static_cast<int>(n_experts);
-  ::bt::note_launch();
+  cudaError_t e;
   if (ne <= 64)
-    moe_route_kernel<2><<<blocks, 256, 0, stream>>>(logits, t, ne, top_k, ids, weights);
+    e = launch_pdl(moe_route_kernel<2>, dim3(blocks), 0, stream, logits, t, ne, top_k, ids, weights);
   else if (ne <= 256)
-    moe_route_kernel<8><<<blocks, 256, 0, stream>>>(logits, t, ne, top_k, ids, weights);
+    e = launch_pdl(moe_route_kernel<8>, dim3(blocks), 0, stream, logits, t, ne, top_k, ids, weights);
   else
-    moe_route_kernel<32><<<blocks, 256, 0, stream>>>(logits, t, ne, top_k, ids, weights);
-  const cudaError_t e = cudaGetLastError();
+    e = launch_pdl(moe_route_kernel<32>, dim3(blocks), 0, stream, logits, t, ne, top_k, ids, weights);
+  if (e == cudaSuccess) e = cudaGetLastError();
   if (e != cudaSuccess) return fail_cuda(e, "moe_route launch");
   return BT_OK;
 }
