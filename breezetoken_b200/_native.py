@@ -166,7 +166,7 @@ _SIGS: dict[str, tuple[object, list]] = {
     "bt_moe_layer_iq3s_add_norm": (C.c_int, [_P, _P, _P, C.POINTER(BtMoeShared), _P, _I64, _I64, _I64, _I64, _P, _P,
                                              C.c_int, _P, _P,
                                              C.c_float, _P, _P, _P, _P, _P, _P]),
-    "bt_moe_prepare_iq3s": (C.c_int, [C.POINTER(BtMoeShared), _P, _I64, _I64, _I64, _I64, C.c_int, _P, _P]),
+    "bt_moe_route_sort_iq3s": (C.c_int, [_P, _P, _I64, _I64, _I64, _I64, C.c_int, _I64, _P, _P, _P, _P]),
     "bt_moe_layer_iq3s_add_norm_prepared": (C.c_int, [_P, _P, _P, C.POINTER(BtMoeShared), _P, _I64, _I64, _I64, _I64,
                                                       _P, _P, C.c_int, _P, _P, C.c_float, _P, _P, _P, _P, _P, _P]),
     "bt_qwen35_kernels_per_step": (C.c_int, [C.POINTER(BtQwen35Model)]),

@@ -150,20 +150,20 @@ int bt_moe_layer_iq3s_add_norm(const void* gate, const void* up, const void* dow
                       planes, out, workspace, stream, bt::kPrepAll);
 }
 
-int bt_moe_prepare_iq3s(const BtMoeShared* shared, const float* x, int64_t t, int64_t hidden, int64_t ffn,
-                        int64_t n_experts, int top_k, void* workspace, void* stream) {
-  if (!shared) return bt::moe_prepare_iq3s(nullptr, x, t, hidden, ffn, n_experts, top_k, workspace, as_stream(stream));
-  const bt::MoeShared sh{shared->gate, shared->up, shared->down, shared->gate_inp, shared->ffn};
-  return bt::moe_prepare_iq3s(&sh, x, t, hidden, ffn, n_experts, top_k, workspace, as_stream(stream));
-}
-
 int bt_moe_layer_iq3s_add_norm_prepared(const void* gate, const void* up, const void* down,
                                         const BtMoeShared* shared, const float* x, int64_t t, int64_t hidden,
                                         int64_t ffn, int64_t n_experts, const int32_t* ids, const float* weights,
                                         int top_k, const float* h, const float* w, float eps, float* h_out, float* y,
                                         void* planes, float* out, void* workspace, void* stream) {
   return moe_add_norm(gate, up, down, shared, x, t, hidden, ffn, n_experts, ids, weights, top_k, h, w, eps, h_out, y,
-                      planes, out, workspace, stream, bt::kPrepSort);
+                      planes, out, workspace, stream, bt::kPrepNone);
+}
+
+int bt_moe_route_sort_iq3s(const float* logits, const float* x, int64_t t, int64_t hidden, int64_t ffn,
+                           int64_t n_experts, int top_k, int64_t shared_ffn, int32_t* ids, float* weights,
+                           void* workspace, void* stream) {
+  return bt::moe_route_sort_iq3s(logits, x, t, hidden, ffn, n_experts, top_k, shared_ffn, ids, weights, workspace,
+                                 as_stream(stream));
 }
 
 int bt_linear_q8(const void* w, const float* x, float* y, int64_t n, int64_t k, int n_vec, void* stream) {

@@ -91,6 +91,9 @@ constexpr int kTicketBase = 16;
 constexpr int kWorkGateUp = 2, kWorkDown = 3;
 // Header word 4: the number of passes (T > 1).
 constexpr int kPassCount = 4;
+// Header word 5: arrivals of the routing blocks of moe_route_sort_kernel
+// (zero between calls).
+constexpr int kRouteTicket = 5;
 constexpr int kHeaderBytes = 512;
 // Item ranges of the expert kernels' CTAs (T > 1): gate/up at [0, 2G), down
 // at [kRangeDown, kRangeDown + 2G), G <= kMaxGrid.
@@ -180,13 +183,9 @@ __global__ void repack_iq3s_kernel(const uint8_t* __restrict__ src, uint8_t* __r
 // registers (PL of them), so the max, the softmax sum and the top-k rounds
 // read global memory once.
 template <int PL>
-__global__ void moe_route_kernel(const float* __restrict__ logits, int64_t t, int n_experts, int top_k,
-                                 int32_t* __restrict__ ids, float* __restrict__ weights) {
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int64_t tok = blockIdx.x * static_cast<int64_t>(blockDim.x >> 5) + warp;
-  pdl_launch_dependents();
-  pdl_wait();  // the logits come from the previous kernel
-  if (tok >= t) return;
+__device__ __forceinline__ void route_token(const float* __restrict__ logits, int64_t tok, int n_experts, int top_k,
+                                            int32_t* ids, float* weights) {
+  const int lane = threadIdx.x & 31;
   const float* lg = logits + tok * n_experts;
   float v[PL];
 #pragma unroll
@@ -243,6 +242,15 @@ __global__ void moe_route_kernel(const float* __restrict__ logits, int64_t t, in
     ids[tok * top_k + lane] = my_id;
     weights[tok * top_k + lane] = my_p / denom;
   }
+}
+
+template <int PL>
+__global__ void moe_route_kernel(const float* __restrict__ logits, int64_t t, int n_experts, int top_k,
+                                 int32_t* __restrict__ ids, float* __restrict__ weights) {
+  const int64_t tok = blockIdx.x * static_cast<int64_t>(blockDim.x >> 5) + (threadIdx.x >> 5);
+  pdl_launch_dependents();
+  pdl_wait();  // the logits come from the previous kernel
+  if (tok < t) route_token<PL>(logits, tok, n_experts, top_k, ids, weights);
 }
 
 // ------------------------------------------------------------------ workspace
@@ -553,90 +561,93 @@ __device__ void shared_down_block(int b, const MoeShared& sh, int t_total, int h
 // The first item of a CTA whose share of the work starts at cost w: items
 // (u, c) of slot u cost passes(u) = cum[u + 1] - cum[u] each and are
 // ordered by (u, c); an item belongs to the CTA its start cost falls in.
-__device__ __forceinline__ int item_at(const int32_t* cum, int n_slots, int chunks, int64_t w) {
-  if (w >= static_cast<int64_t>(cum[n_slots]) * chunks) return n_slots * chunks;
-  int lo = 0, hi = n_slots - 1;  // last slot with cum[u] * chunks <= w
-  while (lo < hi) {
-    const int mid = (lo + hi + 1) >> 1;
-    if (static_cast<int64_t>(cum[mid]) * chunks <= w) lo = mid; else hi = mid - 1;
+// CTA b of a static grid of G takes items [item_at(w_b), item_at(w_b+1)) with
+// w_b = b W / G over the W = cum[n_slots] * chunks units of work (a pass's
+// chunk is one unit; a slot's items are its chunks), where item_at(w) for w
+// in slot u's units [cum[u] chunks, cum[u+1] chunks) is
+// u chunks + ceil((w - cum[u] chunks) / (cum[u+1] - cum[u])).  Each slot's
+// thread writes the boundaries that fall in its units (the first b there is
+// ceil(cum[u] chunks G / W)), so no boundary needs a search.  32-bit: W <=
+// 4096 passes x 64 chunks, G <= kMaxGrid.
+__device__ __forceinline__ void static_ranges(const int32_t* cum, int n_slots, int chunks, int grid,
+                                              int32_t* ranges) {
+  const int w_total = cum[n_slots] * chunks;
+  auto put = [&](int b, int item) {  // boundary b: the end of CTA b - 1 and the start of CTA b
+    if (b > 0) ranges[2 * b - 1] = item;
+    if (b < grid) ranges[2 * b] = item;
+  };
+  if (w_total == 0) {
+    for (int b = threadIdx.x; b <= grid; b += blockDim.x) put(b, 0);
+    return;
   }
-  const int64_t rem = w - static_cast<int64_t>(cum[lo]) * chunks;
-  const int pu = cum[lo + 1] - cum[lo];
-  return lo * chunks + static_cast<int>((rem + pu - 1) / pu);
+  if (threadIdx.x == 0) put(grid, n_slots * chunks);
+  for (int u = threadIdx.x; u < n_slots; u += blockDim.x) {
+    const int w0 = cum[u] * chunks, w1 = cum[u + 1] * chunks, pu = cum[u + 1] - cum[u];
+    for (int b = static_cast<int>((static_cast<int64_t>(w0) * grid + w_total - 1) / w_total); b < grid; ++b) {
+      const int w = static_cast<int>(static_cast<int64_t>(b) * w_total / grid);
+      if (w >= w1) break;
+      put(b, u * chunks + (w - w0 + pu - 1) / pu);
+    }
+  }
 }
 
 // Exclusive prefix sum of v over the threads of a kThreads block, in thread
 // order; *total gets the sum over all threads.  Every thread calls it.
-__device__ __forceinline__ int block_exscan(int v, int* wsum, int& total) {
+// (v: packed fields whose sums do not carry)
+__device__ __forceinline__ uint64_t block_exscan64(uint64_t v, uint64_t* wsum, uint64_t& total) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  int inc = v;
+  uint64_t inc = v;
 #pragma unroll
   for (int o = 1; o < 32; o <<= 1) {
-    const int y = __shfl_up_sync(0xffffffffu, inc, o);
+    const uint64_t y = __shfl_up_sync(0xffffffffu, inc, o);
     if (lane >= o) inc += y;
   }
   if (lane == 31) wsum[warp] = inc;
   __syncthreads();
-  int base = 0;
+  uint64_t base = 0;
   total = 0;
 #pragma unroll
   for (int w = 0; w < kWarps; ++w) {
-    const int sw = wsum[w];
+    const uint64_t sw = wsum[w];
     if (w < warp) base += sw;
     total += sw;
   }
-  __syncthreads();  // wsum free for the next scan
+  __syncthreads();
   return base + inc - v;
 }
 
-// Block 0 (T > 1): counting sort of the P pairs by expert id (stable) into
-// slots, and each expert-kernel CTA's contiguous item range, balanced by
-// token passes.  The next T blocks: encode token (block - 1) (T == 1: block
-// 0, token 0).  The rest: the shared expert's gate/up blocks.
-// part (moe.cuh): kPrepAll runs every block; kPrepX only the blocks that
-// read x alone (encode + shared gate/up, launched ahead of the routing);
-// kPrepSort only the sort block (after kPrepX ran on the same workspace).
-__global__ void __launch_bounds__(kThreads) moe_prep_kernel(const int32_t* __restrict__ ids, int p_total,
-                                                            int n_experts, int direct, const float* __restrict__ x,
-                                                            int t_total, int hidden, MoeWs ws, int gu_grid,
-                                                            int gu_chunks, int d_grid, int d_chunks, MoeShared sh,
-                                                            int pulled, int part) {
-  pdl_launch_dependents();
-  const int enc0 = direct ? 0 : 1;
-  // the block's role in the full layout
-  const int bx = static_cast<int>(blockIdx.x) + (part == kPrepX ? enc0 : 0);
-  if (bx >= enc0 + t_total) {
-    shared_gu_block(bx - enc0 - t_total, sh, x, t_total, hidden, ws);  // waits after its L2 prefetch
-    return;
+// Token `tok`'s fp16 hi / lo planes and scale for the expert kernels.
+__device__ void encode_token(int tok, const float* __restrict__ x, int hidden, const MoeWs& ws) {
+  __shared__ float red[kWarps];
+  const float4* src = reinterpret_cast<const float4*>(x + static_cast<int64_t>(tok) * hidden);
+  float m = 0.f;
+  for (int f = threadIdx.x; f < hidden / 4; f += kThreads) {
+    const float4 h = src[f];
+    m = fmaxf(m, fmaxf(fmaxf(fabsf(h.x), fabsf(h.y)), fmaxf(fabsf(h.z), fabsf(h.w))));
   }
-  pdl_wait();
-  if (direct || bx > 0) {
-    __shared__ float red[kWarps];
-    const int tok = bx - (direct ? 0 : 1);
-    const float4* src = reinterpret_cast<const float4*>(x + static_cast<int64_t>(tok) * hidden);
-    float m = 0.f;
-    for (int f = threadIdx.x; f < hidden / 4; f += kThreads) {
-      const float4 h = src[f];
-      m = fmaxf(m, fmaxf(fmaxf(fabsf(h.x), fabsf(h.y)), fmaxf(fabsf(h.z), fabsf(h.w))));
-    }
-    m = cta_max(m, red);
-    float inv, sx;
-    vector_scale(m, inv, sx);
-    uint8_t* dst = ws.xenc + static_cast<int64_t>(tok) * 4 * hidden;
-    for (int f = threadIdx.x; f < hidden / 4; f += kThreads)
-      store_planes(src[f], inv, dst + 8 * f, dst + 2 * hidden + 8 * f);
-    if (threadIdx.x == 0) ws.xscale[tok] = sx;
-    return;
-  }
+  m = cta_max(m, red);
+  float inv, sx;
+  vector_scale(m, inv, sx);
+  uint8_t* dst = ws.xenc + static_cast<int64_t>(tok) * 4 * hidden;
+  for (int f = threadIdx.x; f < hidden / 4; f += kThreads)
+    store_planes(src[f], inv, dst + 8 * f, dst + 2 * hidden + 8 * f);
+  if (threadIdx.x == 0) ws.xscale[tok] = sx;
+}
+
+// The pairs' sort: block 0 of the prep kernel, or the last block of the
+// routing kernel (moe_route_sort_kernel), whose other blocks wrote the ids
+// (read through L2).  Dynamic shared memory: (3 n_experts + 1 + P) int32.
+__device__ void prep_sort(const int32_t* ids, int p_total, int n_experts, const MoeWs& ws, int gu_grid, int gu_chunks,
+                          int d_grid, int d_chunks, int pulled) {
   extern __shared__ int32_t sm[];
   int32_t* cnt = sm;               // [n_experts]
   int32_t* off = sm + n_experts;   // [n_experts] exclusive prefix of counts
   int32_t* cum = off + n_experts;  // [n_experts + 1] prefix of the slots' passes
   int32_t* sid = cum + n_experts + 1;  // [p_total] the ids
   __shared__ int32_t s_bad;
-  __shared__ int s_wsum[kWarps];
+  __shared__ uint64_t s_wsum64[kWarps];
   for (int e = threadIdx.x; e < n_experts; e += blockDim.x) cnt[e] = 0;
-  for (int q = threadIdx.x; q < p_total; q += blockDim.x) sid[q] = ids[q];
+  for (int q = threadIdx.x; q < p_total; q += blockDim.x) sid[q] = __ldcg(ids + q);
   if (threadIdx.x == 0) s_bad = 0;
   __syncthreads();
   for (int q = threadIdx.x; q < p_total; q += blockDim.x) {
@@ -648,9 +659,10 @@ __global__ void __launch_bounds__(kThreads) moe_prep_kernel(const int32_t* __res
   }
   __syncthreads();
   // Slots = the experts with pairs, in id order.  Thread j owns a contiguous
-  // range of expert ids; three block scans give each range its first pair
-  // offset, first slot and first pass (the same values a serial walk over
-  // the ids would give).
+  // range of expert ids; one block scan of the three counts packed into 21-bit
+  // fields (each total <= 4096) gives each range its first pair offset,
+  // first slot and first pass (the same values a serial walk over the ids
+  // would give).
   int n_slots;
   {
     const int per = (n_experts + kThreads - 1) / kThreads;
@@ -662,11 +674,14 @@ __global__ void __launch_bounds__(kThreads) moe_prep_kernel(const int32_t* __res
       s_sum += c > 0;
       p_sum += (c + kTokensPerPass - 1) / kTokensPerPass;
     }
-    int c_tot, s_tot, p_tot;
-    int o = block_exscan(c_sum, s_wsum, c_tot);
-    int u = block_exscan(s_sum, s_wsum, s_tot);
-    int pc = block_exscan(p_sum, s_wsum, p_tot);
-    (void)c_tot;
+    constexpr uint64_t kField = (1ull << 21) - 1;
+    uint64_t tot;
+    const uint64_t ex = block_exscan64(static_cast<uint64_t>(c_sum) | (static_cast<uint64_t>(s_sum) << 21) |
+                                           (static_cast<uint64_t>(p_sum) << 42),
+                                       s_wsum64, tot);
+    int o = static_cast<int>(ex & kField), u = static_cast<int>((ex >> 21) & kField);
+    int pc = static_cast<int>(ex >> 42);
+    const int s_tot = static_cast<int>((tot >> 21) & kField), p_tot = static_cast<int>(tot >> 42);
     n_slots = s_tot;
     if (threadIdx.x == 0) {
       cum[0] = 0;
@@ -695,35 +710,80 @@ __global__ void __launch_bounds__(kThreads) moe_prep_kernel(const int32_t* __res
     }
   }
   __syncthreads();  // cum and off complete
-  if (pulled) {
-    // pulled items need no static ranges, and a token's expert output does
-    // not depend on its place in the expert's pair list: place the pairs
-    // with a per-expert cursor (one atomic each) instead of ranking them
-    for (int e = threadIdx.x; e < n_experts; e += blockDim.x) cnt[e] = 0;
-    __syncthreads();
-    for (int q = threadIdx.x; q < p_total; q += blockDim.x) {
-      const int e = sid[q];
-      if (e >= 0 && e < n_experts) ws.pairs[off[e] + atomicAdd(&cnt[e], 1)] = q;
-    }
-    return;
-  }
-  for (int b = threadIdx.x; b < gu_grid; b += blockDim.x) {
-    const int64_t w = static_cast<int64_t>(cum[n_slots]) * gu_chunks;
-    ws.ranges[2 * b] = item_at(cum, n_slots, gu_chunks, b * w / gu_grid);
-    ws.ranges[2 * b + 1] = item_at(cum, n_slots, gu_chunks, (b + 1) * w / gu_grid);
-  }
-  for (int b = threadIdx.x; b < d_grid; b += blockDim.x) {
-    const int64_t w = static_cast<int64_t>(cum[n_slots]) * d_chunks;
-    ws.ranges[kRangeDown + 2 * b] = item_at(cum, n_slots, d_chunks, b * w / d_grid);
-    ws.ranges[kRangeDown + 2 * b + 1] = item_at(cum, n_slots, d_chunks, (b + 1) * w / d_grid);
-  }
+  // A token's expert output does not depend on its place in the expert's
+  // pair list (each pass column is one token's own): place the pairs with a
+  // per-expert cursor (one shared-memory atomic each).
+  for (int e = threadIdx.x; e < n_experts; e += blockDim.x) cnt[e] = 0;
+  __syncthreads();
   for (int q = threadIdx.x; q < p_total; q += blockDim.x) {
     const int e = sid[q];
-    if (e < 0 || e >= n_experts) continue;
-    int rank = 0;
-    for (int q2 = 0; q2 < q; ++q2) rank += sid[q2] == e;
-    ws.pairs[off[e] + rank] = q;
+    if (e >= 0 && e < n_experts) ws.pairs[off[e] + atomicAdd(&cnt[e], 1)] = q;
   }
+  if (pulled) return;  // pulled items need no static ranges
+  static_ranges(cum, n_slots, gu_chunks, gu_grid, ws.ranges);
+  static_ranges(cum, n_slots, d_chunks, d_grid, ws.ranges + kRangeDown);
+}
+
+// Block 0 (T > 1): counting sort of the P pairs by expert id (stable) into
+// slots, and each expert-kernel CTA's contiguous item range, balanced by
+// token passes.  The next T blocks: encode token (block - 1) (T == 1: block
+// 0, token 0).  The rest: the shared expert's gate/up blocks.
+// part (moe.cuh): kPrepAll runs every block; kPrepX only the blocks that
+// read x alone (encode + shared gate/up, launched ahead of the routing).
+__global__ void __launch_bounds__(kThreads) moe_prep_kernel(const int32_t* __restrict__ ids, int p_total,
+                                                            int n_experts, int direct, const float* __restrict__ x,
+                                                            int t_total, int hidden, MoeWs ws, int gu_grid,
+                                                            int gu_chunks, int d_grid, int d_chunks, MoeShared sh,
+                                                            int pulled, int part) {
+  pdl_launch_dependents();
+  const int enc0 = direct ? 0 : 1;
+  // the block's role in the full layout
+  const int bx = static_cast<int>(blockIdx.x) + (part == kPrepX ? enc0 : 0);
+  if (bx >= enc0 + t_total) {
+    shared_gu_block(bx - enc0 - t_total, sh, x, t_total, hidden, ws);  // waits after its L2 prefetch
+    return;
+  }
+  pdl_wait();
+  if (direct || bx > 0) {
+    encode_token(bx - (direct ? 0 : 1), x, hidden, ws);
+    return;
+  }
+  prep_sort(ids, p_total, n_experts, ws, gu_grid, gu_chunks, d_grid, d_chunks, pulled);
+}
+
+
+// bt_moe_route_sort_iq3s, the prep kernel's work folded into the routing
+// launch: blocks [0, n_route) route (moe_route_kernel's warps), and the last
+// of them to finish (an arrival ticket in header word kRouteTicket, re-armed
+// by that block) sorts the pairs; blocks [n_route, n_route + T) encode the
+// tokens (n_enc = T, or 0 for one token, whose layer call encodes).
+template <int PL>
+__global__ void __launch_bounds__(kThreads) moe_route_sort_kernel(const float* __restrict__ logits, int64_t t,
+                                                                  int n_experts, int top_k, int32_t* ids,
+                                                                  float* weights, MoeWs ws, int gu_grid,
+                                                                  int gu_chunks, int d_grid, int d_chunks,
+                                                                  int pulled, const float* __restrict__ x,
+                                                                  int hidden, int n_route) {
+  pdl_launch_dependents();
+  pdl_wait();  // the logits and x come from earlier kernels
+  if (static_cast<int>(blockIdx.x) >= n_route) {
+    encode_token(blockIdx.x - n_route, x, hidden, ws);
+    return;
+  }
+  const int64_t tok = blockIdx.x * static_cast<int64_t>(kWarps) + (threadIdx.x >> 5);
+  if (tok < t) route_token<PL>(logits, tok, n_experts, top_k, ids, weights);
+  if (t == 1) return;
+  __shared__ int s_last;
+  __threadfence();  // this block's ids before its arrival
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    s_last = atomicAdd(ws.hdr + kRouteTicket, 1) == n_route - 1;
+    if (s_last) atomicExch(ws.hdr + kRouteTicket, 0);
+  }
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();  // every block's ids are visible past its arrival
+  prep_sort(ids, static_cast<int>(t * top_k), n_experts, ws, gu_grid, gu_chunks, d_grid, d_chunks, pulled);
 }
 
 // ------------------------------------------------------------------ MMA core
@@ -965,7 +1025,7 @@ template <int KB>
 __global__ void __launch_bounds__(kThreads, 2)
     moe_gate_up_kernel(const uint8_t* __restrict__ gate, const uint8_t* __restrict__ up, const int32_t* ids,
                        int n_experts, int direct, int top_k, int ffn, MoeWs ws, int gu_grid, MoeShared sh,
-                       int s_blocks, int t_total, int hidden) {
+                       int s_blocks, int t_total, int hidden, const float* __restrict__ x, int sgu_blocks) {
   constexpr int K = KB * 256, TP = kWarps / KB, OUT = 16 * TP;
   static_assert(kWarps % KB == 0, "K blocks per item");
   extern __shared__ __align__(16) uint8_t smem[];
@@ -978,7 +1038,11 @@ __global__ void __launch_bounds__(kThreads, 2)
     shared_down_block(blockIdx.x, sh, t_total, hidden, ws);
     return;
   }
-  const int rb = blockIdx.x - s_blocks;  // routed CTA
+  if (static_cast<int>(blockIdx.x) < s_blocks + sgu_blocks) {  // or its gate/up rows
+    shared_gu_block(blockIdx.x - s_blocks, sh, x, t_total, hidden, ws);
+    return;
+  }
+  const int rb = blockIdx.x - s_blocks - sgu_blocks;  // routed CTA
   // The op's inputs (ids, x) come from whatever ran before: read them only
   // after the wait, and let the down kernel start only then, so that it may
   // read the slots before its own wait.
@@ -1075,7 +1139,8 @@ __global__ void __launch_bounds__(kThreads, 2)
 template <int KB>
 __global__ void __launch_bounds__(kThreads, 2)
     moe_down_kernel(const uint8_t* __restrict__ down, const int32_t* ids, const float* __restrict__ weights,
-                    float* out, int n_experts, int direct, int top_k, int hidden, MoeWs ws, int shared) {
+                    float* out, int n_experts, int direct, int top_k, int hidden, MoeWs ws, int shared, MoeShared sh,
+                    int sd_blocks, int t_total) {
   constexpr int K = KB * 256, TP = kWarps / KB, ROWS = 32 * TP;
   static_assert(kWarps % KB == 0, "K blocks per item");
   extern __shared__ __align__(16) uint8_t smem[];
@@ -1085,9 +1150,14 @@ __global__ void __launch_bounds__(kThreads, 2)
   int* spair = reinterpret_cast<int*>(xsc) + kMiscPair;
   uint8_t* xs = smem + kRedBytes + kMiscBytes;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+  if (static_cast<int>(blockIdx.x) < sd_blocks) {  // the shared expert's down rows (T > 1)
+    shared_down_block(blockIdx.x, sh, t_total, hidden, ws);
+    return;
+  }
+  const int rb = blockIdx.x - sd_blocks, nrb = gridDim.x - sd_blocks;  // routed CTA
   const int chunks = hidden / ROWS;
-  const int i0 = direct ? blockIdx.x * top_k * chunks / gridDim.x : ws.ranges[kRangeDown + 2 * blockIdx.x];
-  const int i1 = direct ? (blockIdx.x + 1) * top_k * chunks / gridDim.x : ws.ranges[kRangeDown + 2 * blockIdx.x + 1];
+  const int i0 = direct ? rb * top_k * chunks / nrb : ws.ranges[kRangeDown + 2 * rb];
+  const int i1 = direct ? (rb + 1) * top_k * chunks / nrb : ws.ranges[kRangeDown + 2 * rb + 1];
   const int tp = warp % TP, kb = warp / TP;
   const uint8_t* xl = xs + (g >> 1) * token_stride(K) + (g & 1) * plane_stride(K) + 16 * t;
   __shared__ SlotCache sc;
@@ -1238,7 +1308,8 @@ __device__ __forceinline__ int pull_item(int32_t* counter) { return atomicAdd(co
 template <int KB, int KS>
 __global__ void __launch_bounds__(kThreads, 2)
     moe_gate_up_pulled_kernel(const uint8_t* __restrict__ gate, const uint8_t* __restrict__ up, int top_k,
-                              int ffn, MoeWs ws, MoeShared sh, int s_blocks, int t_total, int hidden) {
+                              int ffn, MoeWs ws, MoeShared sh, int s_blocks, int t_total, int hidden,
+                              const float* __restrict__ x, int sgu_blocks) {
   constexpr int K = KB * 256, TP = kWarps / KS, OUT = 16 * TP, KPW = KB / KS;
   static_assert(kWarps % KS == 0 && KB % KS == 0, "K splits");
   extern __shared__ __align__(16) uint8_t smem[];
@@ -1250,6 +1321,10 @@ __global__ void __launch_bounds__(kThreads, 2)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
   if (static_cast<int>(blockIdx.x) < s_blocks) {  // the shared expert's down rows
     shared_down_block(blockIdx.x, sh, t_total, hidden, ws);
+    return;
+  }
+  if (static_cast<int>(blockIdx.x) < s_blocks + sgu_blocks) {  // or its gate/up rows
+    shared_gu_block(blockIdx.x - s_blocks, sh, x, t_total, hidden, ws);
     return;
   }
   pdl_wait();
@@ -1341,7 +1416,8 @@ __global__ void __launch_bounds__(kThreads, 2)
 
 template <int KB>
 __global__ void __launch_bounds__(kThreads, 2)
-    moe_down_pulled_kernel(const uint8_t* __restrict__ down, int top_k, int hidden, MoeWs ws) {
+    moe_down_pulled_kernel(const uint8_t* __restrict__ down, int top_k, int hidden, MoeWs ws, MoeShared sh,
+                           int sd_blocks, int t_total) {
   constexpr int K = KB * 256, ROWS = 32 * kWarps;
   extern __shared__ __align__(16) uint8_t smem[];
   float* xsc = reinterpret_cast<float*>(smem + kRedBytes);
@@ -1350,6 +1426,10 @@ __global__ void __launch_bounds__(kThreads, 2)
   uint8_t* xs = smem + kRedBytes + kMiscBytes;
   __shared__ int s_next[3];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+  if (static_cast<int>(blockIdx.x) < sd_blocks) {  // the shared expert's down rows
+    shared_down_block(blockIdx.x, sh, t_total, hidden, ws);
+    return;
+  }
   pdl_launch_dependents();
   pdl_wait();
   const int chunks = hidden / ROWS;
@@ -1532,6 +1612,42 @@ cudaError_t launch_pdl(Kern kern, dim3 grid, size_t smem, cudaStream_t stream, A
   return ::bt::launch_ex(&cfg, kern, args...);
 }
 
+// Launch geometry of a layer call: the expert kernels' persistent grids and
+// item sizes, shared by the layer and bt_moe_route_sort_iq3s.  `chain`: the
+// shared expert's gate/up blocks ride ahead of the routed gate/up CTAs and
+// its down blocks ahead of the routed down CTAs (kPrepNone, T > 1);
+// otherwise its down blocks ride ahead of the routed gate/up CTAs.  Static
+// grids leave those blocks their slots, so that every routed CTA starts in
+// the first wave.
+struct Geometry {
+  int direct, pulled, gu_grid, gu_chunks, d_grid, d_chunks, sgu_blocks, sd_blocks;
+  size_t prep_smem;
+};
+template <int KBG, int KBD>
+Geometry geometry(int64_t t, int hidden, int ffn, int n_experts, int top_k, int64_t shared_ffn, bool chain) {
+  constexpr int kGuOut = 16 * (kWarps / KBG), kDnRows = 32 * (kWarps / KBD);
+  Geometry g;
+  g.direct = t == 1 ? 1 : 0;  // one token selects top_k distinct experts: no grouping needed
+  g.pulled = t > kStaticMaxTokens ? 1 : 0;
+  const int passes = shared_ffn > 0 ? shared_passes(t) : 0;
+  g.sgu_blocks = shared_ffn > 0 ? (static_cast<int>(shared_ffn) / 16 + 1) * passes : 0;
+  g.sd_blocks = shared_ffn > 0 ? hidden / 64 * passes : 0;
+  // persistent grids: two CTAs per SM, or one per item when there are fewer
+  const int slots_max = std::min(2 * sm_count(), kMaxGrid);
+  const bool in_chain = chain && !g.direct;
+  const int gu_extra = in_chain ? g.sgu_blocks : g.sd_blocks, d_extra = in_chain ? g.sd_blocks : 0;
+  g.gu_chunks = ffn / kGuOut;
+  g.d_chunks = hidden / kDnRows;
+  g.gu_grid = g.direct   ? std::min(top_k * g.gu_chunks, slots_max)
+              : g.pulled ? slots_max
+                         : std::max(1, slots_max - gu_extra);
+  g.d_grid = g.direct   ? std::min(top_k * g.d_chunks, slots_max)
+             : g.pulled ? slots_max
+                        : std::max(1, slots_max - d_extra);
+  g.prep_smem = g.direct ? 0 : (3 * n_experts + 1 + static_cast<size_t>(t * top_k)) * sizeof(int32_t);
+  return g;
+}
+
 template <int KBG, int KBD>
 int launch_all(const uint8_t* gate, const uint8_t* up, const uint8_t* down, const MoeShared* sh, const float* x,
                int64_t t, int hidden, int ffn, int n_experts, const int32_t* ids, const float* weights, int top_k,
@@ -1562,48 +1678,50 @@ int launch_all(const uint8_t* gate, const uint8_t* up, const uint8_t* down, cons
     if (e != cudaSuccess) return fail_cuda(e, "moe set smem");
     configured_device = dev;
   }
-  // persistent grids: two CTAs per SM, or one per item when there are fewer
-  const int slots_max = std::min(2 * sm_count(), kMaxGrid);
-  const int gu_chunks = ffn / kGuOut, d_chunks = hidden / kDnRows;
-  const int gu_grid = direct ? std::min(top_k * gu_chunks, slots_max) : slots_max;
-  const int d_grid = direct ? std::min(top_k * d_chunks, slots_max) : slots_max;
-  const size_t prep_smem = direct ? 0 : (3 * n_experts + 1 + p) * sizeof(int32_t);
+  const Geometry geo = geometry<KBG, KBD>(t, hidden, ffn, n_experts, top_k, sh ? sh->ffn : 0, prep_part == kPrepNone);
+  const int gu_chunks = geo.gu_chunks, d_chunks = geo.d_chunks, gu_grid = geo.gu_grid, d_grid = geo.d_grid;
+  const size_t prep_smem = geo.prep_smem;
+  static_assert(kGuOut > 0 && kDnRows > 0, "item rows");
   if (prep_smem > 48 * 1024) return fail(BT_ERR_UNSUPPORTED, "moe_experts_iq3s: too many experts + pairs");
   // the shared expert rides along: its gate/up blocks after the prep
   // kernel's, its down blocks ahead of the routed gate/up CTAs
   const MoeShared shv = sh ? *sh : MoeShared{};
-  const int passes = shared ? shared_passes(t) : 0;
-  const int sgu_blocks = shared ? (static_cast<int>(shv.ffn) / 16 + 1) * passes : 0;
-  const int sd_blocks = shared ? hidden / 64 * passes : 0;
+  const int sgu_blocks = geo.sgu_blocks, sd_blocks = geo.sd_blocks;
   const int prep_blocks = (direct ? 1 : 1 + static_cast<int>(t)) + sgu_blocks;
   const int pulled = t > kStaticMaxTokens ? 1 : 0;
-  // kPrepX: the x blocks only (moe_prepare_iq3s); kPrepSort: the layer after
-  // moe_prepare_iq3s, the sort block only (none for one token)
-  const int grid = prep_part == kPrepX ? prep_blocks - (direct ? 0 : 1) : prep_part == kPrepSort ? 1 : prep_blocks;
+  // kPrepNone (after moe_route_sort_iq3s routed, sorted and encoded), T > 1:
+  // no prep launch; the shared expert's gate/up blocks run ahead of the
+  // routed gate/up CTAs and its down blocks ahead of the routed down CTAs,
+  // so the whole layer is one chain of early-launched kernels.  Otherwise
+  // (and for one token, whose down kernel adds the shared output in place)
+  // the prep kernel encodes and runs the shared gate/up (kPrepX: without the
+  // sort, which moe_route_sort_iq3s did), and the shared down blocks run
+  // ahead of the routed gate/up CTAs.
+  const bool chain = prep_part == kPrepNone && !direct;
+  const int part = prep_part == kPrepNone ? kPrepX : prep_part;
+  const int gu_sd = chain ? 0 : sd_blocks, gu_sgu = chain ? sgu_blocks : 0, dn_sd = chain ? sd_blocks : 0;
   cudaError_t e = cudaSuccess;
-  if (!(prep_part == kPrepSort && direct))
-    e = launch_pdl(moe_prep_kernel, dim3(grid), prep_part == kPrepX ? 0 : prep_smem, stream, ids, p, n_experts, direct,
-                   x, static_cast<int>(t), hidden, ws, gu_grid, gu_chunks, d_grid, d_chunks, shv, pulled, prep_part);
-  if (prep_part == kPrepX) {
-    if (e == cudaSuccess) e = cudaGetLastError();
-    return e == cudaSuccess ? BT_OK : fail_cuda(e, "moe prepare launch");
-  }
+  if (!chain)
+    e = launch_pdl(moe_prep_kernel, dim3(part == kPrepX ? prep_blocks - (direct ? 0 : 1) : prep_blocks),
+                   part == kPrepX ? 0 : prep_smem, stream, ids, p, n_experts, direct, x, static_cast<int>(t), hidden,
+                   ws, gu_grid, gu_chunks, d_grid, d_chunks, shv, pulled, part);
   // up to kStaticMaxTokens tokens: static item ranges of K-split items (one
   // token: the last of a row chunk's CTAs combines); more: whole-pass items
   // pulled from a counter, then the combine kernel
   if (!pulled) {
     if (e == cudaSuccess)
-      e = launch_pdl(moe_gate_up_kernel<KBG>, dim3(sd_blocks + gu_grid), gu_smem, stream, gate, up, ids, n_experts,
-                     direct, top_k, ffn, ws, gu_grid, shv, sd_blocks, static_cast<int>(t), hidden);
+      e = launch_pdl(moe_gate_up_kernel<KBG>, dim3(gu_sd + gu_sgu + gu_grid), gu_smem, stream, gate, up, ids,
+                     n_experts, direct, top_k, ffn, ws, gu_grid, shv, gu_sd, static_cast<int>(t), hidden, x, gu_sgu);
     if (e == cudaSuccess)
-      e = launch_pdl(moe_down_kernel<KBD>, dim3(d_grid), d_smem, stream, down, ids, weights, out, n_experts, direct,
-                     top_k, hidden, ws, shared);
+      e = launch_pdl(moe_down_kernel<KBD>, dim3(dn_sd + d_grid), d_smem, stream, down, ids, weights, out, n_experts,
+                     direct, top_k, hidden, ws, shared, shv, dn_sd, static_cast<int>(t));
   } else {
     if (e == cudaSuccess)
-      e = launch_pdl(moe_gate_up_pulled_kernel<KBG, kGuSplits>, dim3(sd_blocks + gu_grid), gu_smem, stream, gate, up, top_k,
-                     ffn, ws, shv, sd_blocks, static_cast<int>(t), hidden);
+      e = launch_pdl(moe_gate_up_pulled_kernel<KBG, kGuSplits>, dim3(gu_sd + gu_sgu + gu_grid), gu_smem, stream, gate,
+                     up, top_k, ffn, ws, shv, gu_sd, static_cast<int>(t), hidden, x, gu_sgu);
     if (e == cudaSuccess)
-      e = launch_pdl(moe_down_pulled_kernel<KBD>, dim3(d_grid), d_smem, stream, down, top_k, hidden, ws);
+      e = launch_pdl(moe_down_pulled_kernel<KBD>, dim3(dn_sd + d_grid), d_smem, stream, down, top_k, hidden, ws, shv,
+                     dn_sd, static_cast<int>(t));
   }
   const int64_t total = t * hidden;
   const int blocks = static_cast<int>(std::min<int64_t>((total + kThreads - 1) / kThreads, 4096));
@@ -1620,6 +1738,27 @@ int launch_all(const uint8_t* gate, const uint8_t* up, const uint8_t* down, cons
     return add_rms_norm_planes(norm->h, out, norm->w, norm->h_out, norm->y, norm->planes, t, hidden, norm->eps,
                                stream);
   return BT_OK;
+}
+
+template <int KBG, int KBD>
+int route_sort_launch(const float* logits, const float* x, int64_t t, int hidden, int ffn, int n_experts, int top_k,
+                      int64_t shared_ffn, int32_t* ids, float* weights, MoeWs ws, cudaStream_t stream) {
+  const Geometry geo = geometry<KBG, KBD>(t, hidden, ffn, n_experts, top_k, shared_ffn, true);
+  if (geo.prep_smem > 48 * 1024) return fail(BT_ERR_UNSUPPORTED, "moe route + sort: too many experts + pairs");
+  const int n_route = static_cast<int>((t + kWarps - 1) / kWarps);
+  const dim3 grid(static_cast<unsigned>(n_route + (geo.direct ? 0 : t)));  // one token: the layer encodes
+  cudaError_t e;
+  if (n_experts <= 64)
+    e = launch_pdl(moe_route_sort_kernel<2>, grid, geo.prep_smem, stream, logits, t, n_experts, top_k, ids, weights, ws,
+                   geo.gu_grid, geo.gu_chunks, geo.d_grid, geo.d_chunks, geo.pulled, x, hidden, n_route);
+  else if (n_experts <= 256)
+    e = launch_pdl(moe_route_sort_kernel<8>, grid, geo.prep_smem, stream, logits, t, n_experts, top_k, ids, weights,
+                   ws, geo.gu_grid, geo.gu_chunks, geo.d_grid, geo.d_chunks, geo.pulled, x, hidden, n_route);
+  else
+    e = launch_pdl(moe_route_sort_kernel<32>, grid, geo.prep_smem, stream, logits, t, n_experts, top_k, ids, weights,
+                   ws, geo.gu_grid, geo.gu_chunks, geo.d_grid, geo.d_chunks, geo.pulled, x, hidden, n_route);
+  if (e == cudaSuccess) e = cudaGetLastError();
+  return e == cudaSuccess ? BT_OK : fail_cuda(e, "moe route + sort launch");
 }
 
 }  // namespace
@@ -1667,15 +1806,22 @@ int64_t moe_workspace_bytes(int64_t t, int64_t hidden, int64_t ffn, int64_t shar
   return moe_ws_bytes(t, t * top_k, hidden, ffn, shared_ffn);
 }
 
-int moe_prepare_iq3s(const MoeShared* shared, const float* x, int64_t t, int64_t hidden, int64_t ffn,
-                     int64_t n_experts, int top_k, void* workspace, cudaStream_t stream) {
-  if (!x || !workspace) return fail(BT_ERR_INVALID, "moe prepare: null pointer");
-  // the layer's checks and launch geometry; the x part reads neither the
-  // weights nor the routing, so the workspace stands in for those pointers
-  void* w = workspace;
-  return moe_layer_iq3s(w, w, w, shared, x, t, hidden, ffn, n_experts, static_cast<const int32_t*>(w),
-                        static_cast<const float*>(w), top_k, static_cast<float*>(w), workspace, stream, nullptr,
-                        kPrepX);
+int moe_route_sort_iq3s(const float* logits, const float* x, int64_t t, int64_t hidden, int64_t ffn,
+                        int64_t n_experts, int top_k, int64_t shared_ffn, int32_t* ids, float* weights,
+                        void* workspace, cudaStream_t stream) {
+  if (!logits || !x || !ids || !weights || !workspace) return fail(BT_ERR_INVALID, "moe route + sort: null pointer");
+  if (t < 1 || t * top_k > 4096 || top_k < 1 || top_k > 16 || n_experts < 1 || n_experts > 1024 ||
+      top_k > n_experts)
+    return fail(BT_ERR_UNSUPPORTED, "moe route + sort serves T * top_k <= 4096 pairs, <= 1024 experts, top-k <= 16");
+  if ((reinterpret_cast<uintptr_t>(workspace) | reinterpret_cast<uintptr_t>(x)) & 15 || hidden % 8)
+    return fail(BT_ERR_INVALID, "moe route + sort: workspace and x must be 16-byte aligned, hidden a multiple of 8");
+  if (shared_ffn < 0) return fail(BT_ERR_INVALID, "moe route + sort: negative shared ffn");
+  const MoeWs ws = moe_ws(workspace, t, t * top_k, hidden, ffn, shared_ffn);
+  const int h = static_cast<int>(hidden), f = static_cast<int>(ffn), ne = static_cast<int>(n_experts);
+  if (hidden == 2048 && ffn == 512) return route_sort_launch<8, 2>(logits, x, t, h, f, ne, top_k, shared_ffn, ids, weights, ws, stream);
+  if (hidden == 1024 && ffn == 512) return route_sort_launch<4, 2>(logits, x, t, h, f, ne, top_k, shared_ffn, ids, weights, ws, stream);
+  if (hidden == 2048 && ffn == 1024) return route_sort_launch<8, 4>(logits, x, t, h, f, ne, top_k, shared_ffn, ids, weights, ws, stream);
+  return fail(BT_ERR_UNSUPPORTED, "moe route + sort serves (hidden, ffn) in {(1024,512), (2048,512), (2048,1024)}");
 }
 
 int moe_layer_iq3s(const void* gate, const void* up, const void* down, const MoeShared* shared, const float* x,

@@ -42,12 +42,11 @@ struct MoeNorm {
   float eps;
 };
 
-// The layer's prep kernel in parts: kPrepAll everything (the layer alone);
-// kPrepX the work that reads x alone (the tokens' fp16 planes and the shared
-// expert's gate/up), which moe_prepare_iq3s launches before the routing is
-// known; kPrepSort the rest (the pairs' sort), for a layer call whose
-// workspace moe_prepare_iq3s filled earlier on the same stream.
-constexpr int kPrepAll = 0, kPrepX = 1, kPrepSort = 2;
+// The layer's prep kernel in parts: kPrepAll everything (the layer alone:
+// the pairs' sort, the tokens' fp16 planes, the shared expert's gate/up);
+// kPrepX all but the sort; kPrepNone: a layer call after
+// moe_route_sort_iq3s, which routed, sorted and encoded into its workspace.
+constexpr int kPrepAll = 0, kPrepX = 1, kPrepNone = 2;
 
 // shared may be null (routed experts only); norm may be null (out only).
 int moe_layer_iq3s(const void* gate, const void* up, const void* down, const MoeShared* shared, const float* x,
@@ -55,9 +54,11 @@ int moe_layer_iq3s(const void* gate, const void* up, const void* down, const Moe
                    int top_k, float* out, void* workspace, cudaStream_t stream, const MoeNorm* norm = nullptr,
                    int prep_part = kPrepAll);
 
-// The x part of a layer call (kPrepX) into `workspace`, for a following
-// moe_layer_iq3s(..., kPrepSort) with the same x, shapes and workspace.
-int moe_prepare_iq3s(const MoeShared* shared, const float* x, int64_t t, int64_t hidden, int64_t ffn,
-                     int64_t n_experts, int top_k, void* workspace, cudaStream_t stream);
+// moe_route (the same ids and weights) plus the prep kernel's pair sort and
+// token encoding of a layer call into `workspace` (the last routing block
+// sorts), for a following moe_layer_iq3s(..., kPrepNone) with the same x.
+int moe_route_sort_iq3s(const float* logits, const float* x, int64_t t, int64_t hidden, int64_t ffn,
+                        int64_t n_experts, int top_k, int64_t shared_ffn, int32_t* ids, float* weights,
+                        void* workspace, cudaStream_t stream);
 
 }  // namespace bt

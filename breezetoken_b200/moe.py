@@ -144,23 +144,25 @@ def _shared_arg(shared: SharedExpert | None, hidden: int):
                          shared.gate_inp.data_ptr(), shared.ffn)
 
 
-def moe_prepare(ex: IQ3SExperts, shared: SharedExpert | None, x: torch.Tensor, top_k: int,
-                workspace: torch.Tensor) -> None:
-    """The part of a MoE layer call that reads x alone (the tokens' encoding
-    and the shared expert's gate/up, bt_moe_prepare_iq3s) into `workspace`,
-    before the routing is known; the layer call follows with
-    moe_forward(..., prepared=True) on the same x and workspace."""
+def route_sort(logits: torch.Tensor, x: torch.Tensor, top_k: int, ex: IQ3SExperts, shared: SharedExpert | None,
+               workspace: torch.Tensor) -> RouterOutput:
+    """route_logits (the same ids and weights) plus the layer's pair sort and
+    the encoding of x (T, hidden) f32 into `workspace`, in one launch
+    (bt_moe_route_sort_iq3s), for moe_forward(x, ..., prepared=True) next."""
+    lg = logits.float().reshape(-1, ex.n_experts).contiguous()
+    t = lg.shape[0]
     x2 = x.float().reshape(-1, ex.hidden)
-    if not x2.is_contiguous():
-        raise ValueError("moe_prepare needs contiguous x (the layer call must read the same buffer)")
-    t = x2.shape[0]
+    if x2.shape[0] != t or not x2.is_contiguous():
+        raise ValueError(f"route_sort needs contiguous f32 x of {t} rows (the layer call reads the same buffer)")
     sffn = shared.ffn if shared is not None else 0
     need = int(N.load().bt_moe_layer_workspace_bytes(t, ex.hidden, ex.ffn, sffn, ex.n_experts, top_k))
     if workspace.numel() < need:
         raise ValueError(f"MoE workspace of {workspace.numel()} bytes < {need}")
-    sh = _shared_arg(shared, ex.hidden)
-    N.call("bt_moe_prepare_iq3s", None if sh is None else ctypes.byref(sh), x2.data_ptr(), t, ex.hidden, ex.ffn,
-           ex.n_experts, top_k, workspace.data_ptr(), _stream())
+    ids = torch.empty(t, top_k, dtype=torch.int32, device=lg.device)
+    w = torch.empty(t, top_k, dtype=torch.float32, device=lg.device)
+    N.call("bt_moe_route_sort_iq3s", lg.data_ptr(), x2.data_ptr(), t, ex.hidden, ex.ffn, ex.n_experts, top_k, sffn,
+           ids.data_ptr(), w.data_ptr(), workspace.data_ptr(), _stream())
+    return RouterOutput(w, ids)
 
 
 def moe_forward(ex: IQ3SExperts, shared: SharedExpert | None, x: torch.Tensor, ids: torch.Tensor,
@@ -174,7 +176,8 @@ def moe_forward(ex: IQ3SExperts, shared: SharedExpert | None, x: torch.Tensor, i
     decoder's residual add and the next RMSNorm (bt_moe_layer_iq3s_add_norm,
     the same bits as the separate ops) and (h + out, rms_norm(h + out) *
     gamma, its bf16 planes (T, 3, hidden)) is returned instead of out.
-    prepared (with norm): moe_prepare already ran on this x and workspace."""
+    prepared (with norm): route_sort (whose ids and weights these are)
+    already ran on this x and workspace."""
     x2 = x.float().reshape(-1, ex.hidden).contiguous()
     t = x2.shape[0]
     ids2 = ids.to(torch.int32).reshape(t, -1).contiguous()
@@ -184,7 +187,7 @@ def moe_forward(ex: IQ3SExperts, shared: SharedExpert | None, x: torch.Tensor, i
     lib = N.load()
     need = int(lib.bt_moe_layer_workspace_bytes(t, ex.hidden, ex.ffn, sffn, ex.n_experts, top_k))
     if prepared and (norm is None or workspace is None or workspace.numel() < need):
-        raise ValueError("a prepared MoE layer call takes the norm and the workspace moe_prepare filled")
+        raise ValueError("a prepared MoE layer call takes the norm and the workspace route_sort filled")
     if workspace is None or workspace.numel() < need:
         workspace = torch.zeros(need, dtype=torch.uint8, device=x2.device)
     out = torch.empty(t, ex.hidden, dtype=torch.float32, device=x2.device)

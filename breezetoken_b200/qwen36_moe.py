@@ -37,7 +37,7 @@ import torch
 from breezetoken_b200 import _native as N
 from breezetoken_b200.backends import B200Backend, _stream, resolve_device
 from breezetoken_b200.gguf import GGML_BF16, GGML_F32, GGUFFile
-from breezetoken_b200.moe import IQ3SExperts, SharedExpert, moe_forward, moe_prepare, route_logits
+from breezetoken_b200.moe import IQ3SExperts, SharedExpert, moe_forward, route_logits, route_sort
 
 
 @dataclass(frozen=True)
@@ -429,15 +429,11 @@ class Qwen36Moe:
         the next RMSNorm + planes: (h, y, planes)."""
         layer = self.layers[i]
         ws = self._moe_ws if ws is None else ws
-        side = self._side if norm is not None else None
-        if side is not None:
-            # the router projection and the routing on the side stream while
-            # the layer's x-only work (token encoding, shared gate/up) runs
-            side.wait_stream(torch.cuda.current_stream())
-            with torch.cuda.stream(side):
-                r = route_logits(self._lin(layer["router"], xp), self.cfg.top_k)
-            moe_prepare(layer["experts"], layer["shared"], xn, self.cfg.top_k, ws)
-            torch.cuda.current_stream().wait_stream(side)
+        chained = norm is not None and self._side is not None
+        if chained:
+            # routing, the pairs' sort and the token encoding in one launch;
+            # the layer's kernels follow it (and each other) with early launch
+            r = route_sort(self._lin(layer["router"], xp), xn, self.cfg.top_k, layer["experts"], layer["shared"], ws)
         else:
             r = route_logits(self._lin(layer["router"], xp), self.cfg.top_k)
         rec = getattr(self, "_route_record", None)
@@ -445,7 +441,7 @@ class Qwen36Moe:
             rec.append((xn.clone(), r.expert_ids.clone(), r.weights.clone()))
         return moe_forward(layer["experts"], layer["shared"], xn, r.expert_ids, r.weights, ws,
                            None if norm is None else (norm[0], norm[1], float(self.cfg.eps)),
-                           prepared=side is not None)
+                           prepared=chained)
 
     # ------------------------------------------------------------------ step
     def _step_t(self, tokens: torch.Tensor, pos_t: torch.Tensor, logits: bool, steps: int = 1,

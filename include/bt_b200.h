@@ -374,18 +374,22 @@ BT_API int bt_moe_layer_iq3s_add_norm(const void* gate, const void* up, const vo
                                       float* y, void* planes, float* out, void* workspace,
                                       void* stream);
 
-/* bt_moe_layer_iq3s_add_norm in two calls, so that the work which reads x
- * alone can run before the routing is known (for instance while the router
- * projection and bt_moe_route run on another stream of the same graph):
- * bt_moe_prepare_iq3s encodes the T tokens and runs the shared expert's
- * gate/up into `workspace`; bt_moe_layer_iq3s_add_norm_prepared then does
- * the rest with the same x, shapes, shared expert and workspace, ordered
- * after the prepare call (same stream, or joined).  Together they give the
- * bits of bt_moe_layer_iq3s_add_norm.  No reference counterpart: a split of
- * the layer above (model/qwen36_moe.py:634-642).                          */
-BT_API int bt_moe_prepare_iq3s(const BtMoeShared* shared, const float* x, int64_t t,
-                               int64_t hidden, int64_t ffn, int64_t n_experts, int top_k,
-                               void* workspace, void* stream);
+/* bt_moe_route + bt_moe_layer_iq3s_add_norm as two calls on one workspace
+ * that chain without a gap: bt_moe_route_sort_iq3s routes the router
+ * logits (T x n_experts f32) into ids / weights exactly like bt_moe_route
+ * and, in the same launch, sorts the pairs and encodes the T tokens of x
+ * into the workspace (the last routing block sorts; shared_ffn: the layer's
+ * shared expert's ffn, 0 for none, as the layer call will get it);
+ * bt_moe_layer_iq3s_add_norm_prepared, ordered after it, does the rest with
+ * the same x, ids, weights, shapes, shared expert and workspace (for T > 1
+ * the shared expert's blocks ride in the expert kernels, no prep launch).
+ * Together they give the bits of bt_moe_route followed by
+ * bt_moe_layer_iq3s_add_norm.  No reference counterpart: a regrouping of
+ * model/moe.py:33-39 and model/qwen36_moe.py:634-642.                      */
+BT_API int bt_moe_route_sort_iq3s(const float* logits, const float* x, int64_t t,
+                                  int64_t hidden, int64_t ffn, int64_t n_experts, int top_k,
+                                  int64_t shared_ffn, int32_t* ids, float* weights,
+                                  void* workspace, void* stream);
 BT_API int bt_moe_layer_iq3s_add_norm_prepared(const void* gate, const void* up,
                                                const void* down, const BtMoeShared* shared,
                                                const float* x, int64_t t, int64_t hidden,

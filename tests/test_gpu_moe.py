@@ -333,11 +333,11 @@ def test_moe_layer_add_norm_equals_layer_then_norm(layer256, t) -> None:
 
 @pytest.mark.parametrize("t", [1, 8, 16, 17, 64])
 def test_moe_prepared_layer_equals_layer(layer256, t) -> None:
-    """bt_moe_prepare_iq3s on one stream, the routing on another, then
-    bt_moe_layer_iq3s_add_norm_prepared: the bits of the one-call layer, on the
-    static, pulled and one-token paths, from a workspace left dirty by another
-    layer call."""
-    from breezetoken_b200.moe import moe_forward, moe_prepare, route_logits
+    """bt_moe_route_sort_iq3s then bt_moe_layer_iq3s_add_norm_prepared: the
+    routing and the bits of bt_moe_route + the one-call layer, on the static,
+    pulled and one-token paths, from a workspace left dirty by another layer
+    call, twice (the routing ticket re-armed)."""
+    from breezetoken_b200.moe import moe_forward, route_logits, route_sort
     from breezetoken_b200.synth import moe_layer_inputs
 
     m, ex, se = layer256
@@ -352,12 +352,9 @@ def test_moe_prepared_layer_equals_layer(layer256, t) -> None:
                      device="cuda")
     other = torch.from_numpy(moe_layer_inputs(t, seed=9)[0]).cuda()
     moe_forward(ex, se, other, r.expert_ids, r.weights, ws, norm=(h, gamma, 1e-6))  # dirty workspace
-    side = torch.cuda.Stream()
-    side.wait_stream(torch.cuda.current_stream())
-    with torch.cuda.stream(side):
-        r2 = route_logits(logits, 8)
-    moe_prepare(ex, se, x, 8, ws)
-    torch.cuda.current_stream().wait_stream(side)
-    got = moe_forward(ex, se, x, r2.expert_ids, r2.weights, ws, norm=(h, gamma, 1e-6), prepared=True)
-    for a, b in zip(got, want, strict=True):
-        assert torch.equal(a, b)
+    for _ in range(2):
+        r2 = route_sort(logits, x, 8, ex, se, ws)
+        assert torch.equal(r2.expert_ids, r.expert_ids) and torch.equal(r2.weights, r.weights)
+        got = moe_forward(ex, se, x, r2.expert_ids, r2.weights, ws, norm=(h, gamma, 1e-6), prepared=True)
+        for a, b in zip(got, want, strict=True):
+            assert torch.equal(a, b)
