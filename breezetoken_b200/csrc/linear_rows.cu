@@ -233,7 +233,7 @@ constexpr int kKStage = 32;                  // K columns per pipeline stage
 constexpr int kStages = 4;
 constexpr int kRowBytes = 2 * kKStage + 16;  // padded shared-memory row: 8 rows of a ldmatrix hit distinct banks
 constexpr int kMaxSplits = 8;                // cluster size (portable limit)
-constexpr int kF32Splits = 4;                // K splits of the per-tile kernel for small f32 matrices
+constexpr int kF32Splits = 4;                // K splits of the per-tile kernel for matrices under a wave
 
 __device__ __forceinline__ void cp_async16(void* smem_dst, const void* gsrc) {
   const uint32_t d = static_cast<uint32_t>(__cvta_generic_to_shared(smem_dst));
@@ -810,11 +810,14 @@ int linear_rows(const void* w, int w_dtype, const void* x_planes, float* y, int6
   const int tw = (w_dtype == BT_BF16 && tiles % 2 == 0 && tiles / 2 >= want / 2 && passes > 1) ? 2 : 1;
   int np = tw == 2 ? 4 : 8;
   while (np > 1 && (np > passes || tiles / tw * ((passes + np - 1) / np) < want)) np >>= 1;
-  // f32 weights of fewer tiles than a wave of blocks (the router and GDN
-  // beta/alpha rows): K split over a cluster of kF32Splits CTAs, so each
-  // CTA's serial K loop is that much shorter.  Decided by the rows alone, so
-  // a token's sums do not depend on T (as on the tensor-core path).
-  const bool ksplit = w_dtype == BT_F32 && tiles < want && k % (kF32Splits * kWarps * 32) == 0;
+  // Matrices whose row tiles, split kF32Splits ways, still fit two waves of
+  // blocks (the router, the GDN beta/alpha rows; for <= 8 tokens also the
+  // 2048-row bf16 out-projections, 10.3 -> 6.9 us at K = 4096 on B200, but
+  // not the 4096-row ones, 6.7 -> 9.9 us at 3.5 waves): K split over a
+  // cluster of kF32Splits CTAs, so each CTA's serial K loop is that much
+  // shorter.  Decided by the rows and K alone, so a token's sums do not
+  // depend on T (as on the tensor-core path).
+  const bool ksplit = tiles * kF32Splits <= 2 * want && k % (kF32Splits * kWarps * 32) == 0;
   cudaLaunchAttribute attr[2];
   cudaLaunchConfig_t cfg = pdl_config(
       dim3(static_cast<unsigned>(tiles / tw), static_cast<unsigned>((passes + np - 1) / np), ksplit ? kF32Splits : 1),
@@ -827,7 +830,8 @@ int linear_rows(const void* w, int w_dtype, const void* x_planes, float* y, int6
     cfg.numAttrs = 2;
   }
   const int nn = static_cast<int>(n), kk = static_cast<int>(k), tt = static_cast<int>(t);
-  const cudaError_t e = ksplit                 ? launch_np<true, 1, kF32Splits>(cfg, np, w, xp, y, nn, kk, tt)
+  const cudaError_t e = ksplit && w_dtype == BT_F32 ? launch_np<true, 1, kF32Splits>(cfg, np, w, xp, y, nn, kk, tt)
+                        : ksplit               ? launch_np<false, 1, kF32Splits>(cfg, np, w, xp, y, nn, kk, tt)
                         : w_dtype == BT_F32    ? launch_np<true, 1>(cfg, np, w, xp, y, nn, kk, tt)
                         : tw == 2              ? launch_np<false, 2>(cfg, np, w, xp, y, nn, kk, tt)
                                                : launch_np<false, 1>(cfg, np, w, xp, y, nn, kk, tt);

@@ -182,6 +182,34 @@ def test_linear_rows_matches_f64(cuda, dtype, t) -> None:
     assert (np.abs(y.cpu().double().numpy() - want) <= 2e-6 * bound).all()
 
 
+@pytest.mark.parametrize("n,k", [(2048, 4096), (4096, 2048)])
+def test_linear_rows_small_batch_bf16_split_matches_f64(cuda, n, k) -> None:
+    """The 35B out- and z-projections' bf16 rows for <= 8 tokens (the first
+    with its K split over a 4-CTA cluster, the second not): within 2e-6 of
+    sum |x||w| of an f64 product, and a token's sums the same bits for any
+    T <= 8 (the split is chosen from N and K)."""
+    rng = np.random.default_rng(21)
+    w = torch.from_numpy(rng.standard_normal((n, k)).astype(np.float32) * 0.02).to(torch.bfloat16)
+    x = torch.from_numpy(rng.standard_normal((8, k)).astype(np.float32))
+    wd, xd = w.cuda().contiguous(), x.cuda().contiguous()
+
+    def lin(xs):
+        t = xs.shape[0]
+        planes = torch.empty(t, 3, k, dtype=torch.bfloat16, device="cuda")
+        N.call("bt_bf16_planes", xs.data_ptr(), planes.data_ptr(), t, k, 0)
+        y = torch.empty(t, n, device="cuda")
+        N.call("bt_linear_rows", wd.data_ptr(), N.BT_BF16, planes.data_ptr(), y.data_ptr(), n, k, t, 0)
+        return y
+
+    full = lin(xd)
+    wf = w.double().numpy()
+    want = x.double().numpy() @ wf.T
+    bound = np.abs(x.double().numpy()) @ np.abs(wf).T
+    assert (np.abs(full.cpu().double().numpy() - want) <= 2e-6 * bound).all()
+    for a, b in [(0, 1), (0, 5), (3, 8), (7, 8)]:
+        assert torch.equal(lin(xd[a:b].contiguous()), full[a:b]), (a, b)
+
+
 @pytest.mark.parametrize("n,t", [(256, 64), (64, 64), (64, 9), (256, 130)])
 def test_linear_rows_f32_cluster_split_matches_f64(cuda, n, t) -> None:
     """f32 weight rows of the router / GDN beta-alpha shapes (K = 2048) for a
