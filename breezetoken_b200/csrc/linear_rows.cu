@@ -803,11 +803,16 @@ int linear_rows(const void* w, int w_dtype, const void* x_planes, float* y, int6
     return BT_OK;
   }
   // Two 16-row tiles per block when there are rows enough (each x plane load
-  // then serves 32 rows); passes of 8 tokens per block: as many as keep
-  // >= 2 blocks per SM busy (fewer weight re-reads), one when the matrix is
-  // small.  bf16 weights only: f32 ones are the small matrices.
+  // then serves 32 rows): with several passes when they fill half a wave;
+  // with one pass (<= 8 tokens) only when they still take several waves
+  // (the head, 137 -> 123 us at 8 tokens on B200; the 8192-row qkv
+  // projection, one wave either way, is faster with one tile: 9.5 vs 11.7
+  // us).  Passes of 8 tokens per block: as many as keep >= 2 blocks per SM
+  // busy (fewer weight re-reads), one when the matrix is small.  bf16
+  // weights only: f32 ones are the small matrices.  (Per output the same
+  // sums in the same order either way.)
   const int64_t tiles = n / 16, passes = (t + kPass - 1) / kPass, want = 2 * sm_count();
-  const int tw = (w_dtype == BT_BF16 && tiles % 2 == 0 && tiles / 2 >= want / 2 && passes > 1) ? 2 : 1;
+  const int tw = (w_dtype == BT_BF16 && tiles % 2 == 0 && tiles / 2 >= (passes > 1 ? want / 2 : 2 * want)) ? 2 : 1;
   int np = tw == 2 ? 4 : 8;
   while (np > 1 && (np > passes || tiles / tw * ((passes + np - 1) / np) < want)) np >>= 1;
   // Matrices whose row tiles, split kF32Splits ways, still fit two waves of
