@@ -119,12 +119,20 @@ __host__ __device__ constexpr int code_bit(int i) {
 }
 
 constexpr int kTokensPerPass = 4;              // 8 MMA columns: hi and lo per token
+// Wide passes (prefill-sized batches, >= kWideMinPairs pairs per expert on
+// average): up to kWideGroups groups of kTokensPerPass tokens share each
+// decoded weight tile.  The `pulled` word of the prep: 0 static items, 1
+// pulled passes of kTokensPerPass tokens, kPulledWide pulled wide passes.
+constexpr int kWideGroups = 4;
+constexpr int kWideTokensPerPass = kWideGroups * kTokensPerPass;
+constexpr int kWideMinPairs = 8;
+constexpr int kPulledWide = 2;
 // 4 partial sums per lane; two buffers, so that a pass may write its sums
 // while the previous pass's epilogue still reads the other buffer
 constexpr int kRedFloats = kWarps * 32 * 4;
 constexpr int kRedBytes = 2 * kRedFloats * 4;
-// token scales [0, 16), block maxima [16, 24), the staged tokens' pair ids
-// (ints) [32, 32 + kTokensPerPass)
+// token scales [0, 16), block maxima [16, 32) (two buffers of 8), the staged
+// tokens' pair ids (ints) [32, 32 + kWideTokensPerPass)
 constexpr int kMiscBytes = 256;
 constexpr int kMiscPair = 32;
 
@@ -646,6 +654,7 @@ __device__ void prep_sort(const int32_t* ids, int p_total, int n_experts, const 
   int32_t* sid = cum + n_experts + 1;  // [p_total] the ids
   __shared__ int32_t s_bad;
   __shared__ uint64_t s_wsum64[kWarps];
+  const int tpp = pulled == kPulledWide ? kWideTokensPerPass : kTokensPerPass;  // tokens per pass
   for (int e = threadIdx.x; e < n_experts; e += blockDim.x) cnt[e] = 0;
   for (int q = threadIdx.x; q < p_total; q += blockDim.x) sid[q] = __ldcg(ids + q);
   if (threadIdx.x == 0) s_bad = 0;
@@ -672,7 +681,7 @@ __device__ void prep_sort(const int32_t* ids, int p_total, int n_experts, const 
       const int c = cnt[e];
       c_sum += c;
       s_sum += c > 0;
-      p_sum += (c + kTokensPerPass - 1) / kTokensPerPass;
+      p_sum += (c + tpp - 1) / tpp;
     }
     constexpr uint64_t kField = (1ull << 21) - 1;
     uint64_t tot;
@@ -698,10 +707,10 @@ __device__ void prep_sort(const int32_t* ids, int p_total, int n_experts, const 
         ws.slot_expert[u] = e;
         ws.slot_start[u] = o;
         ws.slot_count[u] = c;
-        for (int c0 = 0; c0 < c; c0 += kTokensPerPass, ++pc) {
+        for (int c0 = 0; c0 < c; c0 += tpp, ++pc) {
           ws.pass_expert[pc] = e;
           ws.pass_start[pc] = o + c0;
-          ws.pass_count[pc] = min(kTokensPerPass, c - c0);
+          ws.pass_count[pc] = min(tpp, c - c0);
         }
         cum[u + 1] = pc;
         ++u;
@@ -773,6 +782,11 @@ __global__ void __launch_bounds__(kThreads) moe_route_sort_kernel(const float* _
   const int64_t tok = blockIdx.x * static_cast<int64_t>(kWarps) + (threadIdx.x >> 5);
   if (tok < t) route_token<PL>(logits, tok, n_experts, top_k, ids, weights);
   if (t == 1) return;
+  if (n_route == 1) {  // one routing block: its own ids, visible after a block barrier
+    __syncthreads();
+    prep_sort(ids, static_cast<int>(t * top_k), n_experts, ws, gu_grid, gu_chunks, d_grid, d_chunks, pulled);
+    return;
+  }
   __shared__ int s_last;
   __threadfence();  // this block's ids before its arrival
   __syncthreads();
@@ -918,6 +932,72 @@ __device__ __forceinline__ void block_steps(Tile& ta, Tile& tb, const uint8_t* n
     tile_step(pb.x, pb.y, __shfl_sync(0xffffffffu, s_b0e, src), __shfl_sync(0xffffffffu, s_b1e, src), b0, acc[1]);
     tile_step(pa.z, pa.w, __shfl_sync(0xffffffffu, s_a0o, src), __shfl_sync(0xffffffffu, s_a1o, src), b1, acc[0]);
     tile_step(pb.z, pb.w, __shfl_sync(0xffffffffu, s_b0o, src), __shfl_sync(0xffffffffu, s_b1o, src), b1, acc[1]);
+    if (na) ta.part[p] = ld_stream16(na + kCodes + 512 * p + 16 * lane);
+    if (nb) tb.part[p] = ld_stream16(nb + kCodes + 512 * p + 16 * lane);
+  }
+}
+
+// tile_step on code words decoded beforehand: a[0..3] row g, a[4..7] row g+8.
+__device__ __forceinline__ void mma_sub(const uint32_t (&a)[8], float sg, float sg8, const uint4& b,
+                                        float (&acc)[2]) {
+  float cc[4] = {0.f, 0.f, 0.f, 0.f};
+  mma_f16(cc, a[0], a[4], a[1], a[5], b.x, b.y);
+  mma_f16(cc, a[2], a[6], a[3], a[7], b.z, b.w);
+  acc[0] = fmaf(sg, cc[0] + cc[1], acc[0]);
+  acc[1] = fmaf(sg8, cc[2] + cc[3], acc[1]);
+}
+
+// block_steps for a wide pass: each code word is decoded once and multiplied
+// with the planes of every 4-token group s < ng (group s's planes `gstride`
+// bytes after group 0's) into acc[s].  Per token the MMAs, the sub-block
+// order and the f32 adds are block_steps', so the sums are the same bits.
+template <int NG>
+__device__ __forceinline__ void block_steps_wide(Tile& ta, Tile& tb, const uint8_t* na, const uint8_t* nb, int lane,
+                                                 const uint8_t* xl, int gstride, int kb, int ng,
+                                                 float (&acc)[NG][2][2]) {
+  const int g = lane >> 2, tq = lane & 3, q0 = lane & ~3;
+  float s_a0[2], s_a1[2], s_b0[2], s_b1[2];  // [even, odd] sub-block of the lane's pair
+  {
+    const float da0 = half_lo(ta.ra.y), da1 = half_lo(ta.rb.y), db0 = half_lo(tb.ra.y), db1 = half_lo(tb.rb.y);
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      s_a0[h] = sub_scale(ta.ra.x, 2 * tq + h, da0, -8388608.0f * da0);
+      s_a1[h] = sub_scale(ta.rb.x, 2 * tq + h, da1, -8388608.0f * da1);
+      s_b0[h] = sub_scale(tb.ra.x, 2 * tq + h, db0, -8388608.0f * db0);
+      s_b1[h] = sub_scale(tb.rb.x, 2 * tq + h, db1, -8388608.0f * db1);
+    }
+  }
+  if (na) {
+    ta.ra = __ldg(reinterpret_cast<const uint2*>(na + kScales) + g);
+    ta.rb = __ldg(reinterpret_cast<const uint2*>(na + kScales) + g + 8);
+  }
+  if (nb) {
+    tb.ra = __ldg(reinterpret_cast<const uint2*>(nb + kScales) + g);
+    tb.rb = __ldg(reinterpret_cast<const uint2*>(nb + kScales) + g + 8);
+  }
+  const uint8_t* xq = xl + kb * 512;
+#pragma unroll
+  for (int p = 0; p < 4; ++p) {
+    const uint4 &pa = ta.part[p], &pb = tb.part[p];
+    const int src = q0 | p;
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      uint32_t da[8], db[8];
+      decode_word(h ? pa.z : pa.x, da[0], da[1], da[2], da[3]);
+      decode_word(h ? pa.w : pa.y, da[4], da[5], da[6], da[7]);
+      decode_word(h ? pb.z : pb.x, db[0], db[1], db[2], db[3]);
+      decode_word(h ? pb.w : pb.y, db[4], db[5], db[6], db[7]);
+      const float sa0 = __shfl_sync(0xffffffffu, s_a0[h], src), sa1 = __shfl_sync(0xffffffffu, s_a1[h], src);
+      const float sb0 = __shfl_sync(0xffffffffu, s_b0[h], src), sb1 = __shfl_sync(0xffffffffu, s_b1[h], src);
+#pragma unroll
+      for (int s = 0; s < NG; ++s) {
+        if (s < ng) {
+          const uint4 b = *reinterpret_cast<const uint4*>(xq + s * gstride + 128 * p + 64 * h);
+          mma_sub(da, sa0, sa1, b, acc[s][0]);
+          mma_sub(db, sb0, sb1, b, acc[s][1]);
+        }
+      }
+    }
     if (na) ta.part[p] = ld_stream16(na + kCodes + 512 * p + 16 * lane);
     if (nb) tb.part[p] = ld_stream16(nb + kCodes + 512 * p + 16 * lane);
   }
@@ -1305,13 +1385,16 @@ __device__ __forceinline__ int pull_item(int32_t* counter) { return atomicAdd(co
 // Gate/up: item = (slot u, chunk c) of OUT = 16 TP rows, TP = 8 / KS tile
 // pairs; warp w owns tile pair w % TP over the KB / KS K-blocks of split
 // w / TP.  KS > 1 adds the splits' partial sums through shared memory.
-template <int KB, int KS>
-__global__ void __launch_bounds__(kThreads, 2)
+// NG > 1: wide passes of up to 4 NG tokens (one CTA per SM: their planes
+// take 8 KB of shared memory per token at hidden 2048).
+template <int KB, int KS, int NG>
+__global__ void __launch_bounds__(kThreads, NG == 1 ? 2 : 1)
     moe_gate_up_pulled_kernel(const uint8_t* __restrict__ gate, const uint8_t* __restrict__ up, int top_k,
                               int ffn, MoeWs ws, MoeShared sh, int s_blocks, int t_total, int hidden,
                               const float* __restrict__ x, int sgu_blocks) {
   constexpr int K = KB * 256, TP = kWarps / KS, OUT = 16 * TP, KPW = KB / KS;
   static_assert(kWarps % KS == 0 && KB % KS == 0, "K splits");
+  static_assert(NG == 1 || KS == 1, "wide passes keep the undivided K");
   extern __shared__ __align__(16) uint8_t smem[];
   float* red = reinterpret_cast<float*>(smem);
   float* xsc = reinterpret_cast<float*>(smem + kRedBytes);
@@ -1374,6 +1457,29 @@ __global__ void __launch_bounds__(kThreads, 2)
       __syncthreads();
       staged = q;
     }
+    if constexpr (NG > 1) {
+      const int ng = (mc + kTokensPerPass - 1) / kTokensPerPass;
+      float acc[NG][2][2] = {};
+#pragma unroll 1
+      for (int kb = kb0; kb < kb0 + KPW; ++kb) {
+        const int64_t off = kb + 1 < kb0 + KPW ? tile_of(it, kb + 1) : next < n_items ? tile_of(next, kb0) : -1;
+        block_steps_wide<NG>(tg, tu, off >= 0 ? gate + off : nullptr, off >= 0 ? up + off : nullptr, lane, xl,
+                             kTokensPerPass * token_stride(K), kb, ng, acc);
+      }
+#pragma unroll
+      for (int s = 0; s < NG; ++s) {  // lane (g, t): token 4 s + t of the pass
+        const int v = kTokensPerPass * s + t;
+        if (s < ng && v < mc) {
+          const float sc = xsc[v];
+          float* dst = ws.act + static_cast<int64_t>(spair[v]) * ffn + c * OUT + warp * 16 + g;
+          dst[0] = silu_f(acc[s][0][0] * sc) * (acc[s][1][0] * sc);
+          dst[8] = silu_f(acc[s][0][1] * sc) * (acc[s][1][1] * sc);
+        }
+      }
+      __syncthreads();  // every warp is done with this item's planes
+      it = next;
+      continue;
+    }
     float acc[2][2] = {};
 #pragma unroll 1
     for (int kb = kb0; kb < kb0 + KPW; ++kb) {
@@ -1414,7 +1520,7 @@ __global__ void __launch_bounds__(kThreads, 2)
   }
 }
 
-template <int KB>
+template <int KB, int NG>
 __global__ void __launch_bounds__(kThreads, 2)
     moe_down_pulled_kernel(const uint8_t* __restrict__ down, int top_k, int hidden, MoeWs ws, MoeShared sh,
                            int sd_blocks, int t_total) {
@@ -1459,37 +1565,71 @@ __global__ void __launch_bounds__(kThreads, 2)
     const int q = it / chunks, c = it - q * chunks;  // one pass of <= kTokensPerPass tokens
     const int start = __ldcg(ws.pass_start + q), mc = __ldcg(ws.pass_count + q);
     if (q != staged) {
-      // act of pair slot v: threads [64 v, 64 v + 64) (warps 2v, 2v+1) -> fp16 planes
-      const int v = threadIdx.x >> 6, j = threadIdx.x & 63;
-      constexpr int F4 = K / 4 / 64;  // float4 per thread
-      float4 h[F4];
-      float m = 0.f;
-      const float4* src = nullptr;
-      const int pair = v < mc ? __ldcg(ws.pairs + start + v) : 0;
-      if (v < mc) src = reinterpret_cast<const float4*>(ws.act + static_cast<int64_t>(pair) * K);
+      // act of pair slot v = 4 s + i of group s: threads [64 i, 64 i + 64)
+      // (warps 2i, 2i+1) -> fp16 planes; the groups' block maxima alternate
+      // between two buffers, so one barrier per group suffices
+      const int ng = NG == 1 ? 1 : (mc + kTokensPerPass - 1) / kTokensPerPass;
+#pragma unroll 1
+      for (int s = 0; s < ng; ++s) {
+        const int v = kTokensPerPass * s + (threadIdx.x >> 6), j = threadIdx.x & 63;
+        float* wm = wmax + 8 * (s & 1);
+        constexpr int F4 = K / 4 / 64;  // float4 per thread
+        float4 h[F4];
+        float m = 0.f;
+        const float4* src = nullptr;
+        const int pair = v < mc ? __ldcg(ws.pairs + start + v) : 0;
+        if (v < mc) src = reinterpret_cast<const float4*>(ws.act + static_cast<int64_t>(pair) * K);
 #pragma unroll
-      for (int i = 0; i < F4; ++i) {
-        h[i] = v < mc ? __ldcg(src + j + 64 * i) : make_float4(0.f, 0.f, 0.f, 0.f);
-        m = fmaxf(m, fmaxf(fmaxf(fabsf(h[i].x), fabsf(h[i].y)), fmaxf(fabsf(h[i].z), fabsf(h[i].w))));
-      }
-      m = warp_max(m);
-      if (lane == 0) wmax[warp] = m;  // (the previous item's readers passed its closing barrier)
-      __syncthreads();
-      m = fmaxf(wmax[2 * v], wmax[2 * v + 1]);
-      float inv, sx;
-      vector_scale(m, inv, sx);
-      if (v < mc) {
-        uint8_t* dst = xs + v * token_stride(K);
+        for (int i = 0; i < F4; ++i) {
+          h[i] = v < mc ? __ldcg(src + j + 64 * i) : make_float4(0.f, 0.f, 0.f, 0.f);
+          m = fmaxf(m, fmaxf(fmaxf(fabsf(h[i].x), fabsf(h[i].y)), fmaxf(fabsf(h[i].z), fabsf(h[i].w))));
+        }
+        m = warp_max(m);
+        if (lane == 0) wm[warp] = m;  // (this buffer's last readers passed a later barrier)
+        __syncthreads();
+        const int w2 = 2 * (threadIdx.x >> 6);
+        m = fmaxf(wm[w2], wm[w2 + 1]);
+        float inv, sx;
+        vector_scale(m, inv, sx);
+        if (v < mc) {
+          uint8_t* dst = xs + v * token_stride(K);
 #pragma unroll
-        for (int i = 0; i < F4; ++i)
-          store_planes(h[i], inv, dst + 8 * (j + 64 * i), dst + plane_stride(K) + 8 * (j + 64 * i));
-        if (j == 0) {
-          xsc[v] = sx;
-          spair[v] = pair;
+          for (int i = 0; i < F4; ++i)
+            store_planes(h[i], inv, dst + 8 * (j + 64 * i), dst + plane_stride(K) + 8 * (j + 64 * i));
+          if (j == 0) {
+            xsc[v] = sx;
+            spair[v] = pair;
+          }
         }
       }
       __syncthreads();
       staged = q;
+    }
+    if constexpr (NG > 1) {
+      const int ng = (mc + kTokensPerPass - 1) / kTokensPerPass;
+      float acc[NG][2][2] = {};
+#pragma unroll 1
+      for (int kb = 0; kb < KB; ++kb) {
+        const bool more = kb + 1 < KB, other = !more && next < n_items;
+        const uint8_t* na = more ? down + tile_of(it, 0, kb + 1) : other ? down + tile_of(next, 0, 0) : nullptr;
+        const uint8_t* nb = more ? down + tile_of(it, 1, kb + 1) : other ? down + tile_of(next, 1, 0) : nullptr;
+        block_steps_wide<NG>(ta, tb, na, nb, lane, xl, kTokensPerPass * token_stride(K), kb, ng, acc);
+      }
+#pragma unroll
+      for (int s = 0; s < NG; ++s) {  // lane (g, t): token 4 s + t of the pass
+        const int v = kTokensPerPass * s + t;
+        if (s < ng && v < mc) {
+          const float sc = xsc[v];
+          float* dst = ws.dn + static_cast<int64_t>(spair[v]) * hidden + c * ROWS + warp * 32 + g;
+          dst[0] = acc[s][0][0] * sc;
+          dst[8] = acc[s][0][1] * sc;
+          dst[16] = acc[s][1][0] * sc;
+          dst[24] = acc[s][1][1] * sc;
+        }
+      }
+      __syncthreads();  // every warp is done with this item's planes
+      it = next;
+      continue;
     }
     float acc[2][2] = {};
 #pragma unroll 1
@@ -1620,6 +1760,7 @@ cudaError_t launch_pdl(Kern kern, dim3 grid, size_t smem, cudaStream_t stream, A
 // grids leave those blocks their slots, so that every routed CTA starts in
 // the first wave.
 struct Geometry {
+  // pulled: 0 static items, 1 pulled passes, kPulledWide pulled wide passes
   int direct, pulled, gu_grid, gu_chunks, d_grid, d_chunks, sgu_blocks, sd_blocks;
   size_t prep_smem;
 };
@@ -1628,7 +1769,9 @@ Geometry geometry(int64_t t, int hidden, int ffn, int n_experts, int top_k, int6
   constexpr int kGuOut = 16 * (kWarps / KBG), kDnRows = 32 * (kWarps / KBD);
   Geometry g;
   g.direct = t == 1 ? 1 : 0;  // one token selects top_k distinct experts: no grouping needed
-  g.pulled = t > kStaticMaxTokens ? 1 : 0;
+  g.pulled = t <= kStaticMaxTokens                                   ? 0
+             : t * top_k >= static_cast<int64_t>(kWideMinPairs) * n_experts ? kPulledWide
+                                                                            : 1;
   const int passes = shared_ffn > 0 ? shared_passes(t) : 0;
   g.sgu_blocks = shared_ffn > 0 ? (static_cast<int>(shared_ffn) / 16 + 1) * passes : 0;
   g.sd_blocks = shared_ffn > 0 ? hidden / 64 * passes : 0;
@@ -1638,9 +1781,10 @@ Geometry geometry(int64_t t, int hidden, int ffn, int n_experts, int top_k, int6
   const int gu_extra = in_chain ? g.sgu_blocks : g.sd_blocks, d_extra = in_chain ? g.sd_blocks : 0;
   g.gu_chunks = ffn / kGuOut;
   g.d_chunks = hidden / kDnRows;
-  g.gu_grid = g.direct   ? std::min(top_k * g.gu_chunks, slots_max)
-              : g.pulled ? slots_max
-                         : std::max(1, slots_max - gu_extra);
+  g.gu_grid = g.direct                   ? std::min(top_k * g.gu_chunks, slots_max)
+              : g.pulled == kPulledWide ? std::min(sm_count(), kMaxGrid)  // one CTA per SM
+              : g.pulled                ? slots_max
+                                        : std::max(1, slots_max - gu_extra);
   g.d_grid = g.direct   ? std::min(top_k * g.d_chunks, slots_max)
              : g.pulled ? slots_max
                         : std::max(1, slots_max - d_extra);
@@ -1660,6 +1804,9 @@ int launch_all(const uint8_t* gate, const uint8_t* up, const uint8_t* down, cons
   static_assert(kWarps % KBG == 0 && kWarps % KBD == 0, "K blocks per item");
   constexpr size_t gu_smem = kRedBytes + kMiscBytes + kTokensPerPass * token_stride(KBG * 256);
   constexpr size_t d_smem = kRedBytes + kMiscBytes + kTokensPerPass * token_stride(KBD * 256);
+  constexpr size_t gu_smem_w = kRedBytes + kMiscBytes + kWideTokensPerPass * token_stride(KBG * 256);
+  constexpr size_t d_smem_w = kRedBytes + kMiscBytes + kWideTokensPerPass * token_stride(KBD * 256);
+  static_assert(gu_smem_w <= 227 * 1024 && d_smem_w <= 227 * 1024, "wide pass planes");
   static int configured_device = -1;
   int dev = 0;
   cudaGetDevice(&dev);
@@ -1670,11 +1817,17 @@ int launch_all(const uint8_t* gate, const uint8_t* up, const uint8_t* down, cons
       e = cudaFuncSetAttribute(moe_down_kernel<KBD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                static_cast<int>(d_smem));
     if (e == cudaSuccess)
-      e = cudaFuncSetAttribute(moe_gate_up_pulled_kernel<KBG, kGuSplits>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               static_cast<int>(gu_smem));
+      e = cudaFuncSetAttribute(moe_gate_up_pulled_kernel<KBG, kGuSplits, 1>,
+                               cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(gu_smem));
     if (e == cudaSuccess)
-      e = cudaFuncSetAttribute(moe_down_pulled_kernel<KBD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+      e = cudaFuncSetAttribute(moe_down_pulled_kernel<KBD, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                static_cast<int>(d_smem));
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(moe_gate_up_pulled_kernel<KBG, 1, kWideGroups>,
+                               cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(gu_smem_w));
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(moe_down_pulled_kernel<KBD, kWideGroups>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               static_cast<int>(d_smem_w));
     if (e != cudaSuccess) return fail_cuda(e, "moe set smem");
     configured_device = dev;
   }
@@ -1688,7 +1841,7 @@ int launch_all(const uint8_t* gate, const uint8_t* up, const uint8_t* down, cons
   const MoeShared shv = sh ? *sh : MoeShared{};
   const int sgu_blocks = geo.sgu_blocks, sd_blocks = geo.sd_blocks;
   const int prep_blocks = (direct ? 1 : 1 + static_cast<int>(t)) + sgu_blocks;
-  const int pulled = t > kStaticMaxTokens ? 1 : 0;
+  const int pulled = geo.pulled;
   // kPrepNone (after moe_route_sort_iq3s routed, sorted and encoded), T > 1:
   // no prep launch; the shared expert's gate/up blocks run ahead of the
   // routed gate/up CTAs and its down blocks ahead of the routed down CTAs,
@@ -1715,13 +1868,20 @@ int launch_all(const uint8_t* gate, const uint8_t* up, const uint8_t* down, cons
     if (e == cudaSuccess)
       e = launch_pdl(moe_down_kernel<KBD>, dim3(dn_sd + d_grid), d_smem, stream, down, ids, weights, out, n_experts,
                      direct, top_k, hidden, ws, shared, shv, dn_sd, static_cast<int>(t));
-  } else {
+  } else if (pulled != kPulledWide) {
     if (e == cudaSuccess)
-      e = launch_pdl(moe_gate_up_pulled_kernel<KBG, kGuSplits>, dim3(gu_sd + gu_sgu + gu_grid), gu_smem, stream, gate,
-                     up, top_k, ffn, ws, shv, gu_sd, static_cast<int>(t), hidden, x, gu_sgu);
+      e = launch_pdl(moe_gate_up_pulled_kernel<KBG, kGuSplits, 1>, dim3(gu_sd + gu_sgu + gu_grid), gu_smem, stream,
+                     gate, up, top_k, ffn, ws, shv, gu_sd, static_cast<int>(t), hidden, x, gu_sgu);
     if (e == cudaSuccess)
-      e = launch_pdl(moe_down_pulled_kernel<KBD>, dim3(dn_sd + d_grid), d_smem, stream, down, top_k, hidden, ws, shv,
-                     dn_sd, static_cast<int>(t));
+      e = launch_pdl(moe_down_pulled_kernel<KBD, 1>, dim3(dn_sd + d_grid), d_smem, stream, down, top_k, hidden, ws,
+                     shv, dn_sd, static_cast<int>(t));
+  } else {  // prefill-sized batches: wide passes, each decoded tile shared by up to 16 tokens
+    if (e == cudaSuccess)
+      e = launch_pdl(moe_gate_up_pulled_kernel<KBG, 1, kWideGroups>, dim3(gu_sd + gu_sgu + gu_grid), gu_smem_w,
+                     stream, gate, up, top_k, ffn, ws, shv, gu_sd, static_cast<int>(t), hidden, x, gu_sgu);
+    if (e == cudaSuccess)
+      e = launch_pdl(moe_down_pulled_kernel<KBD, kWideGroups>, dim3(dn_sd + d_grid), d_smem_w, stream, down, top_k,
+                     hidden, ws, shv, dn_sd, static_cast<int>(t));
   }
   const int64_t total = t * hidden;
   const int blocks = static_cast<int>(std::min<int64_t>((total + kThreads - 1) / kThreads, 4096));

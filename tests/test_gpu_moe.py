@@ -358,3 +358,48 @@ def test_moe_prepared_layer_equals_layer(layer256, t) -> None:
         got = moe_forward(ex, se, x, r2.expert_ids, r2.weights, ws, norm=(h, gamma, 1e-6), prepared=True)
         for a, b in zip(got, want, strict=True):
             assert torch.equal(a, b)
+
+
+def test_moe_wide_passes_equal_narrow_batches(layer256) -> None:
+    """512 tokens over 256 experts (a prefill chunk: 16 pairs per expert on
+    average) run on wide passes, where each decoded weight tile serves up to
+    16 tokens; every token's output has the bits of the same token in 64-token
+    calls (4-token passes), through the one-call layer, the fused add + norm
+    and the prepared (route + sort) call, and a sample of tokens is within
+    1e-5 of the output scale of the oracle's dequantise-then-matmul."""
+    from breezetoken_b200.moe import route_sort
+    from breezetoken_b200.synth import moe_layer_inputs
+
+    m, ex, se = layer256
+    t, step = 512, 64
+    xh, lh = moe_layer_inputs(t)
+    x, logits = torch.from_numpy(xh).cuda(), torch.from_numpy(lh).cuda()
+    r = route_logits(logits, 8)
+    counts = np.bincount(r.expert_ids.cpu().numpy().reshape(-1), minlength=256)
+    assert counts.max() > 16 and (counts % 4).any()  # several and ragged wide passes
+    got = moe_forward(ex, se, x, r.expert_ids, r.weights)
+    want = torch.cat([moe_forward(ex, se, x[i:i + step], r.expert_ids[i:i + step], r.weights[i:i + step])
+                      for i in range(0, t, step)])
+    assert torch.equal(got, want)
+    rng = np.random.default_rng(59)
+    h = torch.from_numpy(rng.standard_normal((t, 2048), dtype=np.float32)).cuda()
+    gamma = torch.from_numpy(1 + 0.02 * rng.standard_normal(2048, dtype=np.float32)).cuda()
+    fused = moe_forward(ex, se, x, r.expert_ids, r.weights, norm=(h, gamma, 1e-6))
+    parts = [moe_forward(ex, se, x[i:i + step], r.expert_ids[i:i + step], r.weights[i:i + step],
+                         norm=(h[i:i + step], gamma, 1e-6)) for i in range(0, t, step)]
+    for j, a in enumerate(fused):
+        assert torch.equal(a, torch.cat([p[j] for p in parts]))
+    ws = torch.zeros(int(N.load().bt_moe_layer_workspace_bytes(t, 2048, 512, 512, 256, 8)), dtype=torch.uint8,
+                     device="cuda")
+    for _ in range(2):
+        r2 = route_sort(logits, x, 8, ex, se, ws)
+        assert torch.equal(r2.expert_ids, r.expert_ids) and torch.equal(r2.weights, r.weights)
+        prep = moe_forward(ex, se, x, r2.expert_ids, r2.weights, ws, norm=(h, gamma, 1e-6), prepared=True)
+        for a, b in zip(prep, fused, strict=True):
+            assert torch.equal(a, b)
+    cache = _DequantCache(m)
+    ids, w, out = r.expert_ids.cpu().numpy(), r.weights.cpu().numpy(), got.cpu().numpy()
+    for i in (0, 1, 255, 511):
+        ref = cache.routed(xh[i], ids[i], w[i]) + oracle_shared(xh[i], m["sh_gate"], m["sh_up"], m["sh_down"],
+                                                                m["sh_gate_inp"])
+        _close(out[i], ref)
