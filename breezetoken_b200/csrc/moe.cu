@@ -1385,16 +1385,13 @@ __device__ __forceinline__ int pull_item(int32_t* counter) { return atomicAdd(co
 // Gate/up: item = (slot u, chunk c) of OUT = 16 TP rows, TP = 8 / KS tile
 // pairs; warp w owns tile pair w % TP over the KB / KS K-blocks of split
 // w / TP.  KS > 1 adds the splits' partial sums through shared memory.
-// NG > 1: wide passes of up to 4 NG tokens (one CTA per SM: their planes
-// take 8 KB of shared memory per token at hidden 2048).
-template <int KB, int KS, int NG>
-__global__ void __launch_bounds__(kThreads, NG == 1 ? 2 : 1)
+template <int KB, int KS>
+__global__ void __launch_bounds__(kThreads, 2)
     moe_gate_up_pulled_kernel(const uint8_t* __restrict__ gate, const uint8_t* __restrict__ up, int top_k,
                               int ffn, MoeWs ws, MoeShared sh, int s_blocks, int t_total, int hidden,
                               const float* __restrict__ x, int sgu_blocks) {
   constexpr int K = KB * 256, TP = kWarps / KS, OUT = 16 * TP, KPW = KB / KS;
   static_assert(kWarps % KS == 0 && KB % KS == 0, "K splits");
-  static_assert(NG == 1 || KS == 1, "wide passes keep the undivided K");
   extern __shared__ __align__(16) uint8_t smem[];
   float* red = reinterpret_cast<float*>(smem);
   float* xsc = reinterpret_cast<float*>(smem + kRedBytes);
@@ -1456,29 +1453,6 @@ __global__ void __launch_bounds__(kThreads, NG == 1 ? 2 : 1)
       cp_async_wait_all();
       __syncthreads();
       staged = q;
-    }
-    if constexpr (NG > 1) {
-      const int ng = (mc + kTokensPerPass - 1) / kTokensPerPass;
-      float acc[NG][2][2] = {};
-#pragma unroll 1
-      for (int kb = kb0; kb < kb0 + KPW; ++kb) {
-        const int64_t off = kb + 1 < kb0 + KPW ? tile_of(it, kb + 1) : next < n_items ? tile_of(next, kb0) : -1;
-        block_steps_wide<NG>(tg, tu, off >= 0 ? gate + off : nullptr, off >= 0 ? up + off : nullptr, lane, xl,
-                             kTokensPerPass * token_stride(K), kb, ng, acc);
-      }
-#pragma unroll
-      for (int s = 0; s < NG; ++s) {  // lane (g, t): token 4 s + t of the pass
-        const int v = kTokensPerPass * s + t;
-        if (s < ng && v < mc) {
-          const float sc = xsc[v];
-          float* dst = ws.act + static_cast<int64_t>(spair[v]) * ffn + c * OUT + warp * 16 + g;
-          dst[0] = silu_f(acc[s][0][0] * sc) * (acc[s][1][0] * sc);
-          dst[8] = silu_f(acc[s][0][1] * sc) * (acc[s][1][1] * sc);
-        }
-      }
-      __syncthreads();  // every warp is done with this item's planes
-      it = next;
-      continue;
     }
     float acc[2][2] = {};
 #pragma unroll 1
@@ -1655,6 +1629,151 @@ __global__ void __launch_bounds__(kThreads, 2)
   }
 }
 
+// ------------------------------------------------- wide gate/up, 16 warps
+// Gate/up over wide passes with one warp per 16-row tile: warp w decodes tile
+// w % 8 of the item's 128 gate rows (w < 8) or up rows (w >= 8) over the full
+// K, each code word once for the pass's <= 16 tokens, and the up warps hand
+// their sums to the gate warps through shared memory.  Half the registers of
+// a tile pair per warp, so 16 warps share the SM (one CTA per SM: the planes
+// of 16 tokens take 8 KB each at hidden 2048).  The shared expert's blocks
+// run in their own launch ahead of it.
+constexpr int kWideThreads = 512;
+
+// block_steps_wide for one tile.
+template <int NG>
+__device__ __forceinline__ void block_steps_one(Tile& ta, const uint8_t* na, int lane, const uint8_t* xl, int gstride,
+                                                int kb, int ng, float (&acc)[NG][2]) {
+  const int g = lane >> 2, tq = lane & 3, q0 = lane & ~3;
+  float s0[2], s1[2];
+  {
+    const float d0 = half_lo(ta.ra.y), d1 = half_lo(ta.rb.y);
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      s0[h] = sub_scale(ta.ra.x, 2 * tq + h, d0, -8388608.0f * d0);
+      s1[h] = sub_scale(ta.rb.x, 2 * tq + h, d1, -8388608.0f * d1);
+    }
+  }
+  if (na) {
+    ta.ra = __ldg(reinterpret_cast<const uint2*>(na + kScales) + g);
+    ta.rb = __ldg(reinterpret_cast<const uint2*>(na + kScales) + g + 8);
+  }
+  const uint8_t* xq = xl + kb * 512;
+#pragma unroll
+  for (int p = 0; p < 4; ++p) {
+    const uint4& pa = ta.part[p];
+    const int src = q0 | p;
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      uint32_t da[8];
+      decode_word(h ? pa.z : pa.x, da[0], da[1], da[2], da[3]);
+      decode_word(h ? pa.w : pa.y, da[4], da[5], da[6], da[7]);
+      const float sa0 = __shfl_sync(0xffffffffu, s0[h], src), sa1 = __shfl_sync(0xffffffffu, s1[h], src);
+#pragma unroll
+      for (int s = 0; s < NG; ++s)
+        if (s < ng) mma_sub(da, sa0, sa1, *reinterpret_cast<const uint4*>(xq + s * gstride + 128 * p + 64 * h), acc[s]);
+    }
+    if (na) ta.part[p] = ld_stream16(na + kCodes + 512 * p + 16 * lane);
+  }
+}
+
+template <int KB>
+__global__ void __launch_bounds__(kWideThreads, 1)
+    moe_gate_up_wide_kernel(const uint8_t* __restrict__ gate, const uint8_t* __restrict__ up, int top_k, int ffn,
+                            MoeWs ws) {
+  constexpr int K = KB * 256, NG = kWideGroups, OUT = 16 * kWarps;
+  extern __shared__ __align__(16) uint8_t smem[];
+  float* red = reinterpret_cast<float*>(smem);  // [tile][lane][NG][2]: the up warps' sums
+  float* xsc = reinterpret_cast<float*>(smem + kRedBytes);
+  int* spair = reinterpret_cast<int*>(xsc) + kMiscPair;
+  uint8_t* xs = smem + kRedBytes + kMiscBytes;
+  static_assert(kWarps * 32 * NG * 2 * 4 <= kRedBytes, "up sums");
+  __shared__ int s_next[3];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+  const int tile = warp % kWarps;
+  const bool is_up = warp >= kWarps;
+  const uint8_t* wm = is_up ? up : gate;
+  pdl_wait();
+  pdl_launch_dependents();
+  const int chunks = ffn / OUT;
+  const int n_items = __ldcg(ws.hdr + kPassCount) * chunks;
+  const uint8_t* xl = xs + (g >> 1) * token_stride(K) + (g & 1) * plane_stride(K) + 16 * t;
+  auto tile_of = [&](int item, int kb) -> int64_t {
+    const int q = item / chunks, c = item - q * chunks;
+    const int e = __ldcg(ws.pass_expert + q);
+    return ((static_cast<int64_t>(e) * (ffn / 16) + c * kWarps + tile) * KB + kb) * kChunkBytes;
+  };
+  if (threadIdx.x == 0) {
+    s_next[0] = pull_item(ws.hdr + kWorkGateUp);
+    s_next[1] = pull_item(ws.hdr + kWorkGateUp);
+  }
+  __syncthreads();
+  int it = s_next[0];
+  Tile tw{};
+  if (it < n_items) load_tile(wm + tile_of(it, 0), lane, tw);
+  int staged = -1;
+  for (int iter = 0; it < n_items; ++iter) {
+    if (threadIdx.x == 0) s_next[(iter + 2) % 3] = pull_item(ws.hdr + kWorkGateUp);
+    const int next = s_next[(iter + 1) % 3];
+    const int q = it / chunks, c = it - q * chunks;
+    const int start = __ldcg(ws.pass_start + q), mc = __ldcg(ws.pass_count + q);
+    if (q != staged) {
+      for (int i = threadIdx.x; i < mc * (K / 4); i += kWideThreads) {  // 16-byte pieces, K/8 per plane
+        const int v = i / (K / 4), j = i - v * (K / 4), plane = j / (K / 8), piece = j - plane * (K / 8);
+        const int tok = __ldcg(ws.pairs + start + v) / top_k;
+        cp_async16(xs + v * token_stride(K) + plane * plane_stride(K) + 16 * piece,
+                   ws.xenc + static_cast<int64_t>(tok) * 4 * K + plane * 2 * K + 16 * piece);
+      }
+      cp_async_commit();
+      if (threadIdx.x < mc) {
+        const int pair = __ldcg(ws.pairs + start + threadIdx.x);
+        spair[threadIdx.x] = pair;
+        xsc[threadIdx.x] = __ldcg(ws.xscale + pair / top_k);
+      }
+      cp_async_wait_all();
+      __syncthreads();
+      staged = q;
+    }
+    const int ng = (mc + kTokensPerPass - 1) / kTokensPerPass;
+    float acc[NG][2] = {};
+#pragma unroll 1
+    for (int kb = 0; kb < KB; ++kb) {
+      // the next K-block's tile, or at the last one the next item's first
+      const int64_t off = kb + 1 < KB ? tile_of(it, kb + 1) : next < n_items ? tile_of(next, 0) : -1;
+      block_steps_one<NG>(tw, off >= 0 ? wm + off : nullptr, lane, xl, kTokensPerPass * token_stride(K), kb, ng, acc);
+    }
+    float* ru = red + (tile * 32 + lane) * (NG * 2);
+    if (is_up) {
+#pragma unroll
+      for (int s = 0; s < NG; ++s) {
+        ru[2 * s] = acc[s][0];
+        ru[2 * s + 1] = acc[s][1];
+      }
+    }
+    __syncthreads();  // the up sums are in shared memory
+    if (!is_up) {
+#pragma unroll
+      for (int s = 0; s < NG; ++s) {  // lane (g, t): rows g, g+8 of this tile, token 4 s + t of the pass
+        const int v = kTokensPerPass * s + t;
+        if (s < ng && v < mc) {
+          const float sc = xsc[v];
+          float* dst = ws.act + static_cast<int64_t>(spair[v]) * ffn + c * OUT + tile * 16 + g;
+          dst[0] = silu_f(acc[s][0] * sc) * (ru[2 * s] * sc);
+          dst[8] = silu_f(acc[s][1] * sc) * (ru[2 * s + 1] * sc);
+        }
+      }
+    }
+    __syncthreads();  // every warp is done with this item's planes and sums
+    it = next;
+  }
+}
+
+// The shared expert's gate/up blocks alone (ahead of moe_gate_up_wide_kernel).
+__global__ void __launch_bounds__(kThreads) moe_shared_gu_kernel(MoeShared sh, const float* __restrict__ x,
+                                                                 int t_total, int hidden, MoeWs ws) {
+  pdl_launch_dependents();
+  shared_gu_block(blockIdx.x, sh, x, t_total, hidden, ws);
+}
+
 // ------------------------------------------------------------------ combine
 // out[t] = sum_k w[t, k] * down_k(act) in routing order, each product rounded
 // before the add like the reference's (out * w).sum(0) in f32.
@@ -1738,10 +1857,10 @@ __global__ void __launch_bounds__(kThreads) moe_combine_norm_kernel(const float*
 }
 
 template <typename Kern, typename... Args>
-cudaError_t launch_pdl(Kern kern, dim3 grid, size_t smem, cudaStream_t stream, Args... args) {
+cudaError_t launch_pdl_n(Kern kern, dim3 grid, int threads, size_t smem, cudaStream_t stream, Args... args) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
-  cfg.blockDim = dim3(kThreads);
+  cfg.blockDim = dim3(threads);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
@@ -1750,6 +1869,10 @@ cudaError_t launch_pdl(Kern kern, dim3 grid, size_t smem, cudaStream_t stream, A
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   return ::bt::launch_ex(&cfg, kern, args...);
+}
+template <typename Kern, typename... Args>
+cudaError_t launch_pdl(Kern kern, dim3 grid, size_t smem, cudaStream_t stream, Args... args) {
+  return launch_pdl_n(kern, grid, kThreads, smem, stream, args...);
 }
 
 // Launch geometry of a layer call: the expert kernels' persistent grids and
@@ -1817,14 +1940,14 @@ int launch_all(const uint8_t* gate, const uint8_t* up, const uint8_t* down, cons
       e = cudaFuncSetAttribute(moe_down_kernel<KBD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                static_cast<int>(d_smem));
     if (e == cudaSuccess)
-      e = cudaFuncSetAttribute(moe_gate_up_pulled_kernel<KBG, kGuSplits, 1>,
+      e = cudaFuncSetAttribute(moe_gate_up_pulled_kernel<KBG, kGuSplits>,
                                cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(gu_smem));
     if (e == cudaSuccess)
       e = cudaFuncSetAttribute(moe_down_pulled_kernel<KBD, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                static_cast<int>(d_smem));
     if (e == cudaSuccess)
-      e = cudaFuncSetAttribute(moe_gate_up_pulled_kernel<KBG, 1, kWideGroups>,
-                               cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(gu_smem_w));
+      e = cudaFuncSetAttribute(moe_gate_up_wide_kernel<KBG>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               static_cast<int>(gu_smem_w));
     if (e == cudaSuccess)
       e = cudaFuncSetAttribute(moe_down_pulled_kernel<KBD, kWideGroups>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                static_cast<int>(d_smem_w));
@@ -1870,18 +1993,24 @@ int launch_all(const uint8_t* gate, const uint8_t* up, const uint8_t* down, cons
                      direct, top_k, hidden, ws, shared, shv, dn_sd, static_cast<int>(t));
   } else if (pulled != kPulledWide) {
     if (e == cudaSuccess)
-      e = launch_pdl(moe_gate_up_pulled_kernel<KBG, kGuSplits, 1>, dim3(gu_sd + gu_sgu + gu_grid), gu_smem, stream,
+      e = launch_pdl(moe_gate_up_pulled_kernel<KBG, kGuSplits>, dim3(gu_sd + gu_sgu + gu_grid), gu_smem, stream,
                      gate, up, top_k, ffn, ws, shv, gu_sd, static_cast<int>(t), hidden, x, gu_sgu);
     if (e == cudaSuccess)
       e = launch_pdl(moe_down_pulled_kernel<KBD, 1>, dim3(dn_sd + d_grid), d_smem, stream, down, top_k, hidden, ws,
                      shv, dn_sd, static_cast<int>(t));
-  } else {  // prefill-sized batches: wide passes, each decoded tile shared by up to 16 tokens
+  } else {
+    // prefill-sized batches: wide passes, each decoded tile shared by up to
+    // 16 tokens; the shared expert's gate/up blocks (when the prep kernel
+    // did not run them) in a launch of their own, its down blocks ahead of
+    // the routed down CTAs
+    if (e == cudaSuccess && gu_sgu)
+      e = launch_pdl(moe_shared_gu_kernel, dim3(gu_sgu), 0, stream, shv, x, static_cast<int>(t), hidden, ws);
     if (e == cudaSuccess)
-      e = launch_pdl(moe_gate_up_pulled_kernel<KBG, 1, kWideGroups>, dim3(gu_sd + gu_sgu + gu_grid), gu_smem_w,
-                     stream, gate, up, top_k, ffn, ws, shv, gu_sd, static_cast<int>(t), hidden, x, gu_sgu);
+      e = launch_pdl_n(moe_gate_up_wide_kernel<KBG>, dim3(gu_grid), kWideThreads, gu_smem_w, stream, gate, up, top_k,
+                       ffn, ws);
     if (e == cudaSuccess)
-      e = launch_pdl(moe_down_pulled_kernel<KBD, kWideGroups>, dim3(dn_sd + d_grid), d_smem_w, stream, down, top_k,
-                     hidden, ws, shv, dn_sd, static_cast<int>(t));
+      e = launch_pdl(moe_down_pulled_kernel<KBD, kWideGroups>, dim3(sd_blocks + d_grid), d_smem_w, stream, down,
+                     top_k, hidden, ws, shv, sd_blocks, static_cast<int>(t));
   }
   const int64_t total = t * hidden;
   const int blocks = static_cast<int>(std::min<int64_t>((total + kThreads - 1) / kThreads, 4096));
