@@ -1413,10 +1413,12 @@ __global__ void __launch_bounds__(kThreads, 2)
   const int n_items = __ldcg(ws.hdr + kPassCount) * chunks;
   const int tp = warp % TP, kb0 = (warp / TP) * KPW;
   const uint8_t* xl = xs + (g >> 1) * token_stride(K) + (g & 1) * plane_stride(K) + 16 * t;
-  auto tile_of = [&](int item, int kb) -> int64_t {
+  // offset of K-block 0 of this warp's tile pair in item `item` (-1: none)
+  auto item_base = [&](int item) -> int64_t {
+    if (item >= n_items) return -1;
     const int q = item / chunks, c = item - q * chunks;
     const int e = __ldcg(ws.pass_expert + q);
-    return ((static_cast<int64_t>(e) * (ffn / 16) + c * TP + tp) * KB + kb) * kChunkBytes;
+    return (static_cast<int64_t>(e) * (ffn / 16) + c * TP + tp) * KB * kChunkBytes;
   };
   if (threadIdx.x == 0) {
     s_next[0] = pull_item(ws.hdr + kWorkGateUp);
@@ -1425,16 +1427,18 @@ __global__ void __launch_bounds__(kThreads, 2)
   __syncthreads();
   int it = s_next[0];
   Tile tg{}, tu{};
-  if (it < n_items) {
-    const int64_t off = tile_of(it, kb0);
-    load_tile(gate + off, lane, tg);
-    load_tile(up + off, lane, tu);
+  int64_t base = item_base(it);
+  if (base >= 0) {
+    load_tile(gate + base + kb0 * kChunkBytes, lane, tg);
+    load_tile(up + base + kb0 * kChunkBytes, lane, tu);
   }
   int staged = -1;
   int npass = 0;  // the reduction buffer of a pass is npass & 1
   for (int iter = 0; it < n_items; ++iter) {
     if (threadIdx.x == 0) s_next[(iter + 2) % 3] = pull_item(ws.hdr + kWorkGateUp);
     const int next = s_next[(iter + 1) % 3];
+    // the next item's tiles: its expert read now, long before they load
+    const int64_t nbase = item_base(next);
     const int q = it / chunks, c = it - q * chunks;  // one pass of <= kTokensPerPass tokens
     const int start = __ldcg(ws.pass_start + q), mc = __ldcg(ws.pass_count + q);
     if (q != staged) {
@@ -1459,7 +1463,9 @@ __global__ void __launch_bounds__(kThreads, 2)
     for (int kb = kb0; kb < kb0 + KPW; ++kb) {
       // the tiles to load meanwhile: the next K-block's, or at the last one
       // the next item's first
-      const int64_t off = kb + 1 < kb0 + KPW ? tile_of(it, kb + 1) : next < n_items ? tile_of(next, kb0) : -1;
+      const int64_t off = kb + 1 < kb0 + KPW ? base + (kb + 1) * kChunkBytes
+                          : nbase >= 0         ? nbase + kb0 * kChunkBytes
+                                               : -1;
       block_steps(tg, tu, off >= 0 ? gate + off : nullptr, off >= 0 ? up + off : nullptr, lane, xl, kb, acc);
     }
     if constexpr (KS == 1) {
@@ -1491,6 +1497,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     }
     __syncthreads();  // every warp is done with this item's planes and sums (a restaging follows)
     it = next;
+    base = nbase;
   }
 }
 
@@ -1515,12 +1522,15 @@ __global__ void __launch_bounds__(kThreads, 2)
   const int chunks = hidden / ROWS;
   const int n_items = __ldcg(ws.hdr + kPassCount) * chunks;
   const uint8_t* xl = xs + (g >> 1) * token_stride(K) + (g & 1) * plane_stride(K) + 16 * t;
-  auto tile_of = [&](int item, int half, int kb) -> int64_t {
+  // offset of K-block 0 of this warp's first tile in item `item` (-1: none);
+  // the second tile follows KB chunks later
+  auto item_base = [&](int item) -> int64_t {
+    if (item >= n_items) return -1;
     const int q = item / chunks, c = item - q * chunks;
     const int e = __ldcg(ws.pass_expert + q);
-    const int64_t tile = static_cast<int64_t>(e) * (hidden / 16) + c * 2 * kWarps + 2 * warp + half;
-    return (tile * KB + kb) * kChunkBytes;
+    return (static_cast<int64_t>(e) * (hidden / 16) + c * 2 * kWarps + 2 * warp) * KB * kChunkBytes;
   };
+  constexpr int64_t kHalf = static_cast<int64_t>(KB) * kChunkBytes;
   if (threadIdx.x == 0) {
     s_next[0] = pull_item(ws.hdr + kWorkDown);
     s_next[1] = pull_item(ws.hdr + kWorkDown);
@@ -1528,14 +1538,16 @@ __global__ void __launch_bounds__(kThreads, 2)
   __syncthreads();
   int it = s_next[0];
   Tile ta{}, tb{};
-  if (it < n_items) {
-    load_tile(down + tile_of(it, 0, 0), lane, ta);
-    load_tile(down + tile_of(it, 1, 0), lane, tb);
+  int64_t base = item_base(it);
+  if (base >= 0) {
+    load_tile(down + base, lane, ta);
+    load_tile(down + base + kHalf, lane, tb);
   }
   int staged = -1;
   for (int iter = 0; it < n_items; ++iter) {
     if (threadIdx.x == 0) s_next[(iter + 2) % 3] = pull_item(ws.hdr + kWorkDown);
     const int next = s_next[(iter + 1) % 3];
+    const int64_t nbase = item_base(next);  // read now, long before the next item's tiles load
     const int q = it / chunks, c = it - q * chunks;  // one pass of <= kTokensPerPass tokens
     const int start = __ldcg(ws.pass_start + q), mc = __ldcg(ws.pass_count + q);
     if (q != staged) {
@@ -1584,9 +1596,9 @@ __global__ void __launch_bounds__(kThreads, 2)
       float acc[NG][2][2] = {};
 #pragma unroll 1
       for (int kb = 0; kb < KB; ++kb) {
-        const bool more = kb + 1 < KB, other = !more && next < n_items;
-        const uint8_t* na = more ? down + tile_of(it, 0, kb + 1) : other ? down + tile_of(next, 0, 0) : nullptr;
-        const uint8_t* nb = more ? down + tile_of(it, 1, kb + 1) : other ? down + tile_of(next, 1, 0) : nullptr;
+        const int64_t off = kb + 1 < KB ? base + (kb + 1) * kChunkBytes : nbase;
+        const uint8_t* na = off >= 0 ? down + off : nullptr;
+        const uint8_t* nb = off >= 0 ? down + off + kHalf : nullptr;
         block_steps_wide<NG>(ta, tb, na, nb, lane, xl, kTokensPerPass * token_stride(K), kb, ng, acc);
       }
 #pragma unroll
@@ -1603,6 +1615,7 @@ __global__ void __launch_bounds__(kThreads, 2)
       }
       __syncthreads();  // every warp is done with this item's planes
       it = next;
+      base = nbase;
       continue;
     }
     float acc[2][2] = {};
@@ -1610,9 +1623,9 @@ __global__ void __launch_bounds__(kThreads, 2)
     for (int kb = 0; kb < KB; ++kb) {
       // the tiles to load meanwhile: the next K-block's, or at the last one
       // the next item's first
-      const bool more = kb + 1 < KB, other = !more && next < n_items;
-      const uint8_t* na = more ? down + tile_of(it, 0, kb + 1) : other ? down + tile_of(next, 0, 0) : nullptr;
-      const uint8_t* nb = more ? down + tile_of(it, 1, kb + 1) : other ? down + tile_of(next, 1, 0) : nullptr;
+      const int64_t off = kb + 1 < KB ? base + (kb + 1) * kChunkBytes : nbase;
+      const uint8_t* na = off >= 0 ? down + off : nullptr;
+      const uint8_t* nb = off >= 0 ? down + off + kHalf : nullptr;
       block_steps(ta, tb, na, nb, lane, xl, kb, acc);
     }
     // lane (g, t): rows g, g+8 of the warp's tiles 2w (acc[0]) and 2w+1 (acc[1]), token t
@@ -1626,6 +1639,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     }
     __syncthreads();  // every warp is done with this item's planes
     it = next;
+    base = nbase;
   }
 }
 
@@ -1697,10 +1711,12 @@ __global__ void __launch_bounds__(kWideThreads, 1)
   const int chunks = ffn / OUT;
   const int n_items = __ldcg(ws.hdr + kPassCount) * chunks;
   const uint8_t* xl = xs + (g >> 1) * token_stride(K) + (g & 1) * plane_stride(K) + 16 * t;
-  auto tile_of = [&](int item, int kb) -> int64_t {
+  // offset of K-block 0 of this warp's tile in item `item` (-1: none)
+  auto item_base = [&](int item) -> int64_t {
+    if (item >= n_items) return -1;
     const int q = item / chunks, c = item - q * chunks;
     const int e = __ldcg(ws.pass_expert + q);
-    return ((static_cast<int64_t>(e) * (ffn / 16) + c * kWarps + tile) * KB + kb) * kChunkBytes;
+    return (static_cast<int64_t>(e) * (ffn / 16) + c * kWarps + tile) * KB * kChunkBytes;
   };
   if (threadIdx.x == 0) {
     s_next[0] = pull_item(ws.hdr + kWorkGateUp);
@@ -1709,11 +1725,13 @@ __global__ void __launch_bounds__(kWideThreads, 1)
   __syncthreads();
   int it = s_next[0];
   Tile tw{};
-  if (it < n_items) load_tile(wm + tile_of(it, 0), lane, tw);
+  int64_t base = item_base(it);
+  if (base >= 0) load_tile(wm + base, lane, tw);
   int staged = -1;
   for (int iter = 0; it < n_items; ++iter) {
     if (threadIdx.x == 0) s_next[(iter + 2) % 3] = pull_item(ws.hdr + kWorkGateUp);
     const int next = s_next[(iter + 1) % 3];
+    const int64_t nbase = item_base(next);  // read now, long before the next item's tiles load
     const int q = it / chunks, c = it - q * chunks;
     const int start = __ldcg(ws.pass_start + q), mc = __ldcg(ws.pass_count + q);
     if (q != staged) {
@@ -1738,7 +1756,7 @@ __global__ void __launch_bounds__(kWideThreads, 1)
 #pragma unroll 1
     for (int kb = 0; kb < KB; ++kb) {
       // the next K-block's tile, or at the last one the next item's first
-      const int64_t off = kb + 1 < KB ? tile_of(it, kb + 1) : next < n_items ? tile_of(next, 0) : -1;
+      const int64_t off = kb + 1 < KB ? base + (kb + 1) * kChunkBytes : nbase;
       block_steps_one<NG>(tw, off >= 0 ? wm + off : nullptr, lane, xl, kTokensPerPass * token_stride(K), kb, ng, acc);
     }
     float* ru = red + (tile * 32 + lane) * (NG * 2);
@@ -1764,6 +1782,7 @@ __global__ void __launch_bounds__(kWideThreads, 1)
     }
     __syncthreads();  // every warp is done with this item's planes and sums
     it = next;
+    base = nbase;
   }
 }
 

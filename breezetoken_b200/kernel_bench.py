@@ -9,6 +9,7 @@
     python -m breezetoken_b200.kernel_bench trace --gguf model.gguf
     python -m breezetoken_b200.kernel_bench attn-layer --batch 64 --pos 648 --splits 2
     python -m breezetoken_b200.kernel_bench load
+    python -m breezetoken_b200.kernel_bench precision
     torchrun --nproc-per-node 2 -m breezetoken_b200.kernel_bench moe-ep --tokens 8
 
 Each prints one JSON line: average launch time and achieved HBM GB/s from
@@ -30,6 +31,8 @@ kernel kind: release gap, prologue, body) after a 16-token prefill.
 ``load`` times loading the full-shape checkpoint (parse, upload, repack).
 ``moe-ep`` times the ``moe`` layer expert-parallel over the torchrun ranks
 against the replicated layer.
+``precision`` prints, per projection path at the decoders' shapes, the worst
+error against an f64 product (of the output scale, and per element).
 ``gdn`` and ``attn`` are the stand-alone GDN-step and split-KV attention decode
 benchmarks with their synthetic inputs (seeds 1 and 2).
 """
@@ -127,6 +130,64 @@ def bench_linear(n: int, k: int, t: int, iters: int) -> dict:
     return {"kernel": "linear_rows", "n": n, "k": k, "tokens": t, "us": sec * 1e6, "bytes": nbytes,
             "gbs": nbytes / sec / 1e9, "tflops": 2 * n * k * t / sec / 1e12,
             "tflops_planes": 3 * 2 * n * k * t / sec / 1e12, "l2": f"{copies} weight copies cycled"}
+
+
+def _errors(y: np.ndarray, want: np.ndarray, host_f32: np.ndarray) -> dict:
+    """Errors of f32 outputs `y` against an f64 product `want`: relative to the
+    output scale (max |want|), and per element over the elements of at least
+    1e-3 of the scale (smaller ones are cancellations, whose relative error
+    says nothing about the kernel); `host_f32` (the same product in f32 by
+    the host's BLAS, as a torch f32 CPU path computes it) measured the same
+    way for comparison."""
+    scale = float(np.abs(want).max())
+    big = np.abs(want) >= 1e-3 * scale
+
+    def measure(v: np.ndarray) -> tuple[float, float, float]:
+        err = np.abs(v.astype(np.float64) - want)
+        rel = err[big] / np.abs(want[big])
+        return float(err.max() / scale), float(rel.max()), float(np.quantile(rel, 0.999))
+
+    a, b, c = measure(y)
+    ha, hb, _ = measure(host_f32)
+    return {"rel_of_scale": a, "rel_elem_max": b, "rel_elem_p999": c, "host_f32_rel_of_scale": ha,
+            "host_f32_rel_elem_max": hb, "elements": int(y.size)}
+
+
+def bench_precision() -> list[dict]:
+    """Worst errors of each projection path on seeded N(0, 0.02) weights and
+    N(0, 1) activations, against f64 products of the same (device-dequantised)
+    weights: the Q8_0 GEMV of a batch-1 step (its activations carried to 2^-22
+    of each 32-element block's maximum), bf16 rows for 8 tokens (CUDA cores)
+    and 64 tokens (tcgen05), f32 rows (the router) for 64 tokens."""
+    rng = np.random.default_rng(21)
+    out = []
+    lib = N.load()
+    for n, k in ((3584, 1024), (1024, 3584), (8224, 1024)):  # 0.8B gate/up, down, GDN in-projection
+        w = Q8Weight.from_gguf(quantize_q8_0(rng.standard_normal((n, k)).astype(np.float32) * 0.02), n, k, "cuda")
+        deq32 = w.dequantize().cpu().numpy()
+        deq = deq32.astype(np.float64)
+        x = rng.standard_normal(k).astype(np.float32)
+        y = torch.empty(n, device="cuda")
+        xd = torch.from_numpy(x).cuda()
+        N.check(lib.bt_linear_q8(w.data.data_ptr(), xd.data_ptr(), y.data_ptr(), n, k, 1, 0), "gemv")
+        out.append({"path": "q8_0 gemv", "n": n, "k": k, "tokens": 1,
+                    **_errors(y.cpu().numpy(), deq @ x.astype(np.float64), deq32 @ x)})
+    for n, k, t, dt in ((2048, 4096, 8, N.BT_BF16), (8192, 2048, 8, N.BT_BF16), (8192, 2048, 64, N.BT_BF16),
+                        (2048, 4096, 64, N.BT_BF16), (256, 2048, 64, N.BT_F32)):
+        wf = rng.standard_normal((n, k)).astype(np.float32) * 0.02
+        w = torch.from_numpy(wf).to(torch.bfloat16 if dt == N.BT_BF16 else torch.float32).cuda().contiguous()
+        x = rng.standard_normal((t, k)).astype(np.float32)
+        xd = torch.from_numpy(x).cuda()
+        planes = torch.empty(t, 3, k, dtype=torch.bfloat16, device="cuda")
+        y = torch.empty(t, n, device="cuda")
+        N.check(lib.bt_bf16_planes(xd.data_ptr(), planes.data_ptr(), t, k, 0), "planes")
+        N.check(lib.bt_linear_rows(w.data_ptr(), dt, planes.data_ptr(), y.data_ptr(), n, k, t, 0), "linear_rows")
+        w32 = w.float().cpu().numpy()
+        want = x.astype(np.float64) @ w32.astype(np.float64).T
+        out.append({"path": ("bf16" if dt == N.BT_BF16 else "f32") + " rows", "n": n, "k": k, "tokens": t,
+                    **_errors(y.cpu().numpy(), want, x @ w32.T)})
+    torch.cuda.synchronize()
+    return out
 
 
 def bench_gdn(batch: int, steps: int, heads: int = 16, dim: int = 128) -> dict:
@@ -715,6 +776,7 @@ def main() -> None:
     al.add_argument("--pos", type=int, default=648)
     al.add_argument("--splits", type=int, default=2)
     al.add_argument("--iters", type=int, default=20)
+    sub.add_parser("precision")
     mo = sub.add_parser("moe")
     mo.add_argument("--tokens", type=int, default=1)
     mo.add_argument("--iters", type=int, default=50)
@@ -760,6 +822,10 @@ def main() -> None:
         r = bench_qwen36(args.batch, args.prompt, args.steps, args.layers, args.timeline)
     elif args.cmd == "moe":
         r = bench_moe(args.tokens, args.iters, shared=not args.no_shared)
+    elif args.cmd == "precision":
+        for line in bench_precision():
+            print(json.dumps(line), flush=True)
+        r = None
     elif args.cmd == "gdn":
         r = bench_gdn_scan(args.batch, args.steps) if args.scan else bench_gdn(args.batch, args.steps)
     else:
