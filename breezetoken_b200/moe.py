@@ -61,15 +61,17 @@ class IQ3SExperts:
     ffn: int
 
     @staticmethod
-    def _repack(raw, rows: int, k: int, device: str) -> torch.Tensor:
-        if isinstance(raw, np.ndarray):
+    def _repack(raw, rows: int, k: int, device: str, uploader=None) -> torch.Tensor:
+        if isinstance(raw, np.ndarray) and uploader is not None:
+            src = uploader.to_device(raw)
+        elif isinstance(raw, np.ndarray):
             with warnings.catch_warnings():
                 # GGUF bytes are a read-only memory map; the tensor is only read (the upload's source)
                 warnings.filterwarnings("ignore", message="The given NumPy array is not writable")
                 src = torch.as_tensor(np.ascontiguousarray(raw))
         else:
             src = torch.as_tensor(raw)
-        src = src.reshape(-1).to(device)
+        src = src.reshape(-1).to(device)  # (a no-op for the uploader's device bytes)
         if src.numel() != rows * k // 256 * 110:
             raise ValueError(f"expected {rows * k // 256 * 110} IQ3_S bytes, got {src.numel()}")
         out = torch.empty(rows * int(N.load().bt_iq3s_row_bytes(k)), dtype=torch.uint8, device=device)
@@ -77,12 +79,15 @@ class IQ3SExperts:
         return out
 
     @classmethod
-    def from_gguf_bytes(cls, gate, up, down, n_experts: int, hidden: int, ffn: int, device: str) -> IQ3SExperts:
-        """GGUF-stored expert tensors (ffn_{gate,up,down}_exps) as raw bytes."""
+    def from_gguf_bytes(cls, gate, up, down, n_experts: int, hidden: int, ffn: int, device: str,
+                        uploader=None) -> IQ3SExperts:
+        """GGUF-stored expert tensors (ffn_{gate,up,down}_exps) as raw bytes;
+        `uploader` (breezetoken_b200.upload.Uploader): stage host bytes
+        through its pinned buffers."""
         return cls(
-            cls._repack(gate, n_experts * ffn, hidden, device),
-            cls._repack(up, n_experts * ffn, hidden, device),
-            cls._repack(down, n_experts * hidden, ffn, device),
+            cls._repack(gate, n_experts * ffn, hidden, device, uploader),
+            cls._repack(up, n_experts * ffn, hidden, device, uploader),
+            cls._repack(down, n_experts * hidden, ffn, device, uploader),
             n_experts, hidden, ffn,
         )
 

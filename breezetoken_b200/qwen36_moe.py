@@ -38,6 +38,7 @@ from breezetoken_b200 import _native as N
 from breezetoken_b200.backends import B200Backend, _stream, resolve_device
 from breezetoken_b200.gguf import GGML_BF16, GGML_F32, GGUFFile
 from breezetoken_b200.moe import IQ3SExperts, SharedExpert, moe_forward, route_logits, route_sort
+from breezetoken_b200.upload import Uploader
 
 
 @dataclass(frozen=True)
@@ -152,19 +153,23 @@ class Qwen36Moe:
     def _rows(self, g: GGUFFile, name: str) -> torch.Tensor:
         """A 2-D bf16 or f32 weight in its (out, in) orientation."""
         shape, ttype, _ = g.tensor_layout(name)
-        raw = torch.from_numpy(np.array(g.raw(name)))  # a writable copy of the mapped bytes
-        if ttype == GGML_BF16:
-            t = raw.view(torch.int16).view(torch.bfloat16)
-        elif ttype == GGML_F32:
-            t = raw.view(torch.float32)
-        else:
+        if ttype not in (GGML_BF16, GGML_F32):
             raise ValueError(f"{name}: dense weights must be bf16 or f32")
-        return t.reshape(shape).to(self.device).contiguous()
+        raw = self._up.to_device(g.raw(name))  # the mapped bytes, staged through pinned buffers
+        return raw.view(torch.bfloat16 if ttype == GGML_BF16 else torch.float32).reshape(shape)
 
     def _vec(self, g: GGUFFile, name: str) -> torch.Tensor:
         return torch.from_numpy(np.array(g.f32(name))).to(self.device).contiguous()
 
     def _load(self, g: GGUFFile) -> None:
+        self._up = Uploader(self.device)
+        try:
+            self._load_tensors(g)
+        finally:
+            self._up.close()
+            del self._up
+
+    def _load_tensors(self, g: GGUFFile) -> None:
         cfg = self.cfg
         self.embd = self._rows(g, "token_embd.weight")
         self.head = self._rows(g, "output.weight")
@@ -179,7 +184,8 @@ class Qwen36Moe:
                 "router": self._rows(g, p + "ffn_gate_inp.weight").float().contiguous(),
                 "experts": IQ3SExperts.from_gguf_bytes(
                     g.raw(p + "ffn_gate_exps.weight"), g.raw(p + "ffn_up_exps.weight"),
-                    g.raw(p + "ffn_down_exps.weight"), cfg.n_experts, cfg.hidden, cfg.expert_ffn, self.device),
+                    g.raw(p + "ffn_down_exps.weight"), cfg.n_experts, cfg.hidden, cfg.expert_ffn, self.device,
+                    uploader=self._up),
                 "shared": SharedExpert.from_tensors(
                     self._rows(g, p + "ffn_gate_shexp.weight"), self._rows(g, p + "ffn_up_shexp.weight"),
                     self._rows(g, p + "ffn_down_shexp.weight"), self._vec(g, p + "ffn_gate_inp_shexp.weight"),

@@ -306,3 +306,29 @@ def test_sequence_shards_decode_the_same_bits(cuda) -> None:
         l_s, t_s = run(rows)
         assert torch.equal(l_s, l_all[rows])
         assert torch.equal(t_s, t_all[rows])
+
+
+def test_uploader_moves_the_bytes_unchanged(cuda, tmp_path) -> None:
+    """The checkpoint uploader (pinned double buffering, host copies split over
+    threads) delivers every byte: empty, small and multi-chunk arrays, a
+    read-only memory map and a non-byte dtype, with chunks smaller than the
+    arrays so both buffers are reused several times."""
+    from breezetoken_b200.upload import Uploader
+
+    rng = np.random.default_rng(61)
+    up = Uploader("cuda", chunk_bytes=8 << 20, threads=4)
+    try:
+        for n in (0, 1000, (8 << 20) + 3, (20 << 20) + 7):
+            src = rng.integers(0, 256, n, dtype=np.uint8)
+            got = up.to_device(src)
+            assert got.dtype == torch.uint8 and got.numel() == n
+            assert torch.equal(got.cpu(), torch.from_numpy(src))
+        path = tmp_path / "blob.bin"
+        blob = rng.integers(0, 256, (17 << 20) + 11, dtype=np.uint8)
+        blob.tofile(path)
+        mm = np.memmap(path, dtype=np.uint8, mode="r")
+        assert torch.equal(up.to_device(mm[5:]).cpu(), torch.from_numpy(blob[5:]))
+        f = rng.standard_normal(3 << 20).astype(np.float32)
+        assert torch.equal(up.to_device(f).view(torch.float32).cpu(), torch.from_numpy(f))
+    finally:
+        up.close()
