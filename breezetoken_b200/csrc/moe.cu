@@ -15,7 +15,10 @@
 // (two 8-warp CTAs per SM, each taking a contiguous range of (expert, row
 // chunk) items, balanced by token passes); every warp decodes two 16-row
 // tiles of one 256-weight column block per item and loads the next item's
-// tiles while it computes.
+// tiles while it computes.  Above 16 tokens the items are whole passes of up
+// to 4 tokens pulled from a counter; at prefill sizes (>= 8 pairs per expert)
+// wide passes of up to 16 tokens let each decoded tile serve four 4-token
+// groups (moe_gate_up_wide_kernel, moe_down_pulled_kernel<KB, 4>).
 //
 // Weights: every IQ3_S weight is d * (1 + 2 * scale nibble) * v with v a
 // signed codebook value, odd and in [-15, 15] (quant/dequant.py:164-185), so
