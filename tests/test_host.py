@@ -146,3 +146,26 @@ def test_make_backend_errors() -> None:
     if not torch.cuda.is_available():
         with pytest.raises(RuntimeError):
             make_backend("b200", "cuda")
+
+
+def test_uploader_cpu_copy_and_precision_measure(tmp_path) -> None:
+    """The checkpoint uploader on a CPU device returns a copy of the bytes (a
+    read-only memory map included); the precision report measures a planted
+    error against the output scale and per element."""
+    from breezetoken_b200.kernel_bench import _errors
+    from breezetoken_b200.upload import Uploader
+
+    rng = np.random.default_rng(62)
+    blob = rng.integers(0, 256, 100_003, dtype=np.uint8)
+    blob.tofile(tmp_path / "b.bin")
+    mm = np.memmap(tmp_path / "b.bin", dtype=np.uint8, mode="r")
+    up = Uploader("cpu")
+    got = up.to_device(mm[3:])
+    up.close()
+    assert got.dtype == torch.uint8 and torch.equal(got, torch.from_numpy(blob[3:]))
+    y = np.array([4.0, -2.0, 1.0, 1e-6], dtype=np.float32)
+    want = y.astype(np.float64) - np.array([4e-6, 0.0, -1e-6, 5e-7])  # planted errors
+    e = _errors(y, want, want.astype(np.float32))
+    assert abs(e["rel_of_scale"] - 1e-6) < 1e-8  # 4e-6 of a scale of 4
+    assert abs(e["rel_elem_max"] - 1e-6) < 1e-8  # the 1e-6 element is below 1e-3 of the scale
+    assert e["host_f32_rel_of_scale"] < 1e-7 and e["elements"] == 4
